@@ -1,0 +1,155 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference implementation.
+
+Run in a container where the reference source tree is available (read-only is fine):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference <path-to-reference>
+
+It imports the reference's own ``src.infer`` / ``src.model`` (CPU, fp32, no CUDA
+extension), loads the deterministic synthetic weights of ``pulsar_b200.weights`` into
+``PulsarForCausalLM``, runs the reference inference engine (prefill, decode_pulse_pass,
+decode_step, stream_generate, self_speculative_stream_generate) and writes compact
+summaries to ``tests/golden/*.pt``. The reference is never needed at test time.
+
+Cases:
+  tiny_*  - the reference test-suite's tiny config (tests/conftest.py:30-51): full logits.
+  full_*  - the production Pulsar-283M config, recipes A and B: top-k + sampled logits.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "pulsar-300m_b200"))
+
+from pulsar_b200.weights import make_state_dict, random_prompts  # noqa: E402
+
+N_PROBE = 256          # fixed probe indices per logits vector (full-size cases)
+TOPK = 32
+
+
+class MockTokenizer:
+    """Duck-typed tokenizer for the reference loops (modelled on tests/test_model.py:518-526)."""
+
+    unk_token_id = None
+
+    def __init__(self, ids):
+        self.ids = list(ids)
+
+    def encode(self, prompt, return_tensors="pt"):
+        return torch.tensor([self.ids], dtype=torch.long)
+
+    def decode(self, ids, skip_special_tokens=False):
+        return "".join(f"{int(i)}," for i in ids)
+
+    def convert_tokens_to_ids(self, s):
+        return None
+
+
+def summarise(logits: torch.Tensor, full: bool, probe_idx: torch.Tensor):
+    lg = logits.detach().float().reshape(-1)
+    d = {"lse": torch.logsumexp(lg, 0).item(), "argmax": int(lg.argmax())}
+    v, i = torch.topk(lg, min(TOPK, lg.numel()))
+    d["top_val"], d["top_idx"] = v.clone(), i.clone()
+    if full:
+        d["full"] = lg.clone()
+    else:
+        d["probe"] = lg[probe_idx].clone()
+    return d
+
+
+def tiny_cfg_dict():
+    return dict(vocab_size=256, d_model=64, n_heads=4, n_kv_heads=2, head_dim=16, d_expert=32,
+                d_shared=64, n_core=2, n_routed_experts=4, top_k=2, max_pulses=4, default_pulses=3,
+                base_seq_len=32, max_seq_len=128, sliding_window=16, ce_chunk_size=64, eos_token_id=-1)
+
+
+def run_case(name, cfg_dict, recipe, seed, prompt_len, n_new, n_pulse_steps, out_dir, full_logits, b_std=0.09):
+    from src.infer import PulsarInferenceEngine, UnifiedKVCache
+    from src.model import PulsarConfig, PulsarForCausalLM
+    from pulsar_b200.config import PulsarConfig as MyCfg
+
+    cfg = PulsarConfig(**cfg_dict)
+    my_cfg = MyCfg(**cfg_dict)
+    sd = make_state_dict(my_cfg, recipe=recipe, seed=seed, b_std=b_std)
+    torch.manual_seed(1234)
+    model = PulsarForCausalLM(cfg)
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected, unexpected
+    assert all(k.startswith("rope_") for k in missing) or not missing, missing
+    eng = PulsarInferenceEngine(model, device="cpu", dtype=torch.float32)
+    ids = random_prompts(1, prompt_len, cfg.vocab_size, seed=seed)[0].tolist()
+    probe_idx = torch.randperm(cfg.vocab_size, generator=torch.Generator().manual_seed(7))[:N_PROBE]
+    rec = {"name": name, "cfg": cfg_dict, "recipe": recipe, "seed": seed, "b_std": b_std, "prompt": ids,
+           "n_new": n_new, "probe_idx": probe_idx}
+
+    # Per-pulse logits of the prefill and the first decode steps (src/infer.py:353-549).
+    kv = UnifiedKVCache(cfg, 1, "cpu", torch.float32)
+    with torch.inference_mode():
+        lg = eng.prefill(torch.tensor([ids]), kv)[0, -1]
+    rec["prefill"] = summarise(lg, full_logits, probe_idx)
+    steps = []
+    tok = int(lg.argmax())
+    pos = len(ids)
+    for _ in range(n_pulse_steps):
+        h = h0n = None
+        pulses = []
+        with torch.inference_mode():
+            for p in range(cfg.default_pulses):
+                lg, h, h0n = eng.decode_pulse_pass(tok, pos, kv, p, h, h0n)
+                pulses.append(summarise(lg[0], full_logits, probe_idx))
+        kv.seq_len = pos + 1
+        steps.append({"token": tok, "pos": pos, "pulses": pulses, "kv_lengths": kv.checkpoint_state()})
+        tok = pulses[-1]["argmax"]
+        pos += 1
+    rec["steps"] = steps
+
+    # Token streams of the two reference generate loops (greedy, no repetition penalty).
+    def run(spec):
+        tk = MockTokenizer(ids)
+        txt = eng.generate(tk, "", max_new_tokens=n_new, temperature=0.0, top_p=1.0,
+                           repetition_penalty=1.0, stream=False, speculative=spec)
+        return [int(s) for s in txt.split(",") if s != ""]
+
+    rec["greedy_ids"] = run(False)
+    rec["spec_ids"] = run(True)
+    # With the reference's default repetition penalty 1.15 (src/infer.py:559).
+    tk = MockTokenizer(ids)
+    txt = eng.generate(tk, "", max_new_tokens=min(n_new, 16), temperature=0.0, top_p=1.0,
+                       repetition_penalty=1.15, stream=False, speculative=False)
+    rec["greedy_rep115_ids"] = [int(s) for s in txt.split(",") if s != ""]
+    path = os.path.join(out_dir, f"{name}.pt")
+    torch.save(rec, path)
+    print(f"wrote {path}: greedy={rec['greedy_ids'][:12]}... spec={rec['spec_ids'][:12]}...", flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("PULSAR_REFERENCE", "/root/reference"))
+    ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", default=None)
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    torch.set_num_threads(os.cpu_count() or 1)
+    full = dict(eos_token_id=-1)
+    cases = [
+        ("tiny_A", tiny_cfg_dict(), "A", 0, 12, 16, 3, True),
+        ("tiny_B", tiny_cfg_dict(), "B", 0, 12, 24, 3, True, 0.35),
+        ("tiny_B_long", tiny_cfg_dict(), "B", 3, 40, 24, 3, True, 0.35),  # T > window and > base_seq_len
+        ("full_A_c1", full, "A", 0, 128, 64, 2, False),                  # BASELINE config 1 shape
+        ("full_B_c1", full, "B", 0, 128, 32, 2, False),
+        ("full_B_long", full, "B", 5, 1100, 6, 2, False),                # T > 1024: local quirk + YaRN
+    ]
+    for c in cases:
+        if args.only and c[0] != args.only:
+            continue
+        run_case(c[0], c[1], c[2], c[3], c[4], c[5], c[6], args.out, c[7], *c[8:])
+
+
+if __name__ == "__main__":
+    main()
