@@ -1,0 +1,180 @@
+/*
+ * pulsar_b200 - C ABI of the B200-native (sm_100a) Pulsar-283M KV-cache decode engine.
+ *
+ * Conventions
+ *   - Every entry point returns an int status: PULSAR_OK (0) or a negative PULSAR_ERR_*;
+ *     pulsar_last_error() returns a message for the calling thread's last failure.
+ *   - Pointers named *_dev are device pointers; *_host are host pointers. `stream` is a
+ *     cudaStream_t passed as void* (NULL = the legacy default stream). Every kernel is
+ *     launched on that stream and every launch is checked.
+ *   - No torch types cross this boundary: plain pointers, sizes and strides.
+ *   - Ops (pulsar_op_*) are functional: the caller owns and sizes every output buffer.
+ *     Engine calls (pulsar_engine_*) use memory the engine allocated at create time; the
+ *     token path allocates nothing.
+ *   - An engine handle is not thread-safe: one host thread drives one engine.
+ */
+#ifndef PULSAR_B200_H
+#define PULSAR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PULSAR_OK 0
+#define PULSAR_ERR_INVALID (-1)     /* bad argument, shape or dtype */
+#define PULSAR_ERR_CUDA (-2)        /* CUDA runtime / launch error */
+#define PULSAR_ERR_OOM (-3)         /* device allocation failed */
+#define PULSAR_ERR_STATE (-4)       /* call not valid in the engine's current state */
+#define PULSAR_ERR_UNSUPPORTED (-5) /* configuration the compiled kernels do not cover */
+#define PULSAR_ERR_CAPACITY (-6)    /* KV / row capacity exceeded */
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* pulsar_last_error(void);
+/* ABI version (major * 10000 + minor * 100 + patch). */
+int pulsar_abi_version(void);
+
+/* ==================================================================================
+ * pulsar_cuda forward ops. Each replaces one binding of the reference extension
+ * (csrc/pulsar_cuda.cpp:199-279) and keeps its argument meaning; the reference checks
+ * (TORCH_CHECK) become PULSAR_ERR_INVALID with the same message text.
+ * ================================================================================== */
+
+/* csrc/kernels.cu:224-266 rmsnorm_forward_cuda (binding csrc/pulsar_cuda.cpp:200).
+ * x [rows, D] bf16, weight [D] f32 -> y [rows, D] bf16, rsqrt [rows] f32. */
+int pulsar_op_rmsnorm(const void* x_dev, const float* weight_dev, int64_t rows, int64_t D, float eps,
+                      void* y_dev, float* rsqrt_dev, void* stream);
+
+/* csrc/kernels.cu:908-965 rope_forward_cuda (binding :206). qk [rows, Dh] bf16 where the
+ * position of row r is r % T; cos/sin [T, Dh/2] f32 -> y [rows, Dh] bf16. */
+int pulsar_op_rope(const void* qk_dev, const float* cos_dev, const float* sin_dev, int64_t rows, int64_t T,
+                   int64_t Dh, void* y_dev, void* stream);
+
+/* csrc/kernels.cu:825-863 fused_swiglu_forward_cuda (binding :204). gu [rows, 2*d_ff] bf16
+ * -> out [rows, d_ff] bf16, out = silu(gate) * up computed in fp32. */
+int pulsar_op_swiglu(const void* gu_dev, int64_t rows, int64_t d_ff, void* out_dev, void* stream);
+
+/* csrc/kernels.cu:2417-2491 moe_router_topk_forward_cuda (binding :244-255).
+ * logits [N, E] (f32, or bf16 when logits_bf16 != 0), expert_bias [E] f32; E <= 32,
+ * 1 <= K <= min(8, E). Outputs: topk_idx [N, K] i64, topk_weights [N, K] bf16,
+ * z_loss [1] f32 (z_loss_weight * mean_t lse_t^2 over centred logits; 0 when
+ * z_loss_weight <= 0), probs_mean [E] f32 (mean sigmoid score).
+ * workspace_dev: N * (E + 1) floats of caller scratch (deterministic two-pass means). */
+int pulsar_op_moe_router_topk(const void* logits_dev, int logits_bf16, const float* expert_bias_dev,
+                              int64_t N, int64_t E, int64_t K, float z_loss_weight, int64_t* topk_idx_dev,
+                              void* topk_weights_dev, float* z_loss_dev, float* probs_mean_dev,
+                              float* workspace_dev, void* stream);
+
+/* csrc/kernels.cu:2716-2765 qk_rmsnorm_rope_forward_cuda (binding :229-230).
+ * x: n_vec vectors of 64 bf16 with element strides (sB, sH, sT) over the logical
+ * [B, n_heads, T, 64] index, vector v = ((b * n_heads) + h) * T + t; weight [n_heads, 64]
+ * f32; cos/sin [T, 32] f32. Outputs y [n_vec, 64] bf16 contiguous, rsqrt [n_vec] f32. */
+int pulsar_op_qk_rmsnorm_rope(const void* x_dev, int64_t sB, int64_t sH, int64_t sT, int64_t n_vec,
+                              int64_t n_heads, int64_t T, const float* weight_dev, const float* cos_dev,
+                              const float* sin_dev, float eps, void* y_dev, float* rsqrt_dev, void* stream);
+
+/* csrc/kernels.cu:2844-2877, 2930-2958 fused_attn_gate_forward_cuda (binding :233-234).
+ * attn [B, H, T, 64] bf16 contiguous, gate_logits [B, T, H] f32 -> out [B, T, H*64] bf16. */
+int pulsar_op_attn_gate(const void* attn_dev, const float* gate_logits_dev, int64_t B, int64_t H, int64_t T,
+                        void* out_dev, void* stream);
+
+/* csrc/kernels.cu:3653-3691 causal_depthwise_conv1d_k4_forward_cuda (binding :271-273).
+ * x [B, T, D] bf16, weight [D, 4] f32 -> y[b,t,d] = x + sum_k w[d,k] * x[b,t-k,d]. */
+int pulsar_op_conv1d_k4(const void* x_dev, const float* weight_dev, int64_t B, int64_t T, int64_t D,
+                        void* y_dev, void* stream);
+
+/* csrc/kernels.cu:1633-1664 moe_combine_forward_cuda (binding :214-216).
+ * expert_outputs [E, C, D] bf16, topk_idx [N, K] i64, topk_weights [N, K] bf16,
+ * token_to_slot [N, K] i32 (-1 dropped), shared_out [N, D] bf16 or NULL -> out [N, D] bf16. */
+int pulsar_op_moe_combine(const void* expert_outputs_dev, const int64_t* topk_idx_dev,
+                          const void* topk_weights_dev, const int32_t* token_to_slot_dev,
+                          const void* shared_out_dev, int64_t N, int64_t K, int64_t E, int64_t C, int64_t D,
+                          void* out_dev, void* stream);
+
+/* csrc/kernels.cu:1548-1605 moe_dispatch_forward_cuda (binding :209-211).
+ * x [N, D] bf16 -> expert_inputs [E, C, D] bf16; unused slots are zeroed (all of them, or
+ * only the tail past expert_counts[e] when expert_counts_dev [E] i64 is given). */
+int pulsar_op_moe_dispatch(const void* x_dev, const int64_t* topk_idx_dev, const int32_t* token_to_slot_dev,
+                           const int64_t* expert_counts_dev, int64_t N, int64_t K, int64_t E, int64_t C,
+                           int64_t D, void* expert_inputs_dev, void* stream);
+
+/* ==================================================================================
+ * Engine: the KV-cache decode path of src/infer.py on the device.
+ * ================================================================================== */
+
+typedef struct pulsar_engine pulsar_engine;
+
+typedef struct {
+    int32_t vocab_size;        /* multiple of 256 */
+    int32_t max_pulses;        /* leading dim of per-pulse parameters (reference: 8) */
+    int32_t loop_lora_rank;    /* 0 = no loop adapters */
+    float loop_lora_alpha;
+    float rms_eps;
+    float logit_softcap;       /* <= 0: no softcap */
+    int32_t base_seq_len;      /* YaRN base (1024) */
+    int32_t use_canon_conv;
+    int32_t per_pulse_bias;
+    int32_t max_batch;         /* sequence slots */
+    int32_t max_seq_len;       /* KV positions per slot (prompt + generated + slack) */
+    int32_t max_prefill;       /* longest prompt one prefill call accepts */
+    int32_t kv_fp32;           /* 0: bf16 KV cache (default); 1: fp32 KV cache (parity mode) */
+    int32_t device;            /* CUDA device ordinal */
+} pulsar_engine_config;
+
+/* Replaces PulsarInferenceEngine.__init__ + load_inference_model (src/infer.py:184-209,
+ * 785-817): allocates the weight arena, the per-slot KV cache and the workspaces. */
+int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engine** out);
+int pulsar_engine_destroy(pulsar_engine* eng);
+
+/* Upload one reference state_dict tensor (name as in PulsarForCausalLM.state_dict(),
+ * fp32 host data, row-major, numel checked). rope inv_freq tables are passed as
+ * "rope_local.inv_freq" / "rope_global.inv_freq" [32]. */
+int pulsar_engine_set_tensor(pulsar_engine* eng, const char* name, const float* data_host, int64_t numel);
+
+/* Build the per-pulse bf16 arena: loop-adapter merges (src/model.py:716-727), expert
+ * transposes, rope tables. Required once after all set_tensor calls. */
+int pulsar_engine_finalize(pulsar_engine* eng);
+
+/* Bytes of the device weight arena / KV cache / workspaces. */
+int pulsar_engine_memory(const pulsar_engine* eng, int64_t* arena_bytes, int64_t* kv_bytes, int64_t* work_bytes);
+
+/* PulsarInferenceEngine.prefill (src/infer.py:353-461) for one sequence slot.
+ * ids_dev [T] i32. Writes last-position logits [V] f32 (no softcap, as the reference)
+ * and sets the slot length to T. */
+int pulsar_engine_prefill(pulsar_engine* eng, int32_t slot, const int32_t* ids_dev, int32_t T, float* logits_dev,
+                          void* stream);
+
+/* decode_pulse_pass (src/infer.py:463-524) over R rows (1 <= R <= 32).
+ * rows_dev [R] x int4 {slot, pos, token, 0}. Rows of the same slot must have
+ * consecutive positions (block-verify: a row sees in-block predecessors' K/V of this
+ * pulse). h_prev_dev / h0n_dev [R, 1024] f32 (ignored for pulse 0). Outputs h_out,
+ * h0n_out [R, 1024] f32; logits [R, V] f32 (softcapped) unless logits_dev is NULL. */
+int pulsar_engine_pulse(pulsar_engine* eng, int32_t pulse, int32_t R, const int32_t* rows_dev,
+                        const float* h_prev_dev, const float* h0n_dev, float* h_out_dev, float* h0n_out_dev,
+                        float* logits_dev, void* stream);
+
+/* Sequence-slot KV length (UnifiedKVCache.seq_len / checkpoint_state / restore_state,
+ * src/infer.py:99, 159-168). Restoring a shorter length is the rollback. */
+int pulsar_engine_get_length(pulsar_engine* eng, int32_t slot, int32_t* length);
+int pulsar_engine_set_length(pulsar_engine* eng, int32_t slot, int32_t length);
+
+/* Greedy decode loop, reference semantics (stream_generate with temperature 0 and
+ * repetition_penalty 1, src/infer.py:551-621): starting from the prefill logits already
+ * in the slot's state, emit n_new tokens. gamma == 0: exact sequential decode (3 pulses
+ * per token). gamma >= 1: draft gamma tokens from the pulse-1 exit, verify the gamma+1
+ * block with pulses 2-3 in one batched pass, accept while argmax agrees, roll back.
+ * Runs device-resident (CUDA graphs, no per-token host sync).
+ * first_logits_dev [n_seq, V] f32: logits that choose each sequence's first token.
+ * slots_host [n_seq]; out_tokens_dev [n_seq, n_new] i32; stats_host (may be NULL)
+ * receives {rounds, drafted, accepted} summed over sequences. */
+int pulsar_engine_generate_greedy(pulsar_engine* eng, int32_t n_seq, const int32_t* slots_host,
+                                  const float* first_logits_dev, int32_t n_new, int32_t gamma,
+                                  int32_t* out_tokens_dev, int64_t* stats_host, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PULSAR_B200_H */

@@ -1,0 +1,874 @@
+// Host side of the Pulsar decode engine: weight staging and repack, the per-slot KV cache,
+// workspaces, the pulse-pass / prefill drivers, the graph-captured decode loops and the
+// pulsar_engine_* C ABI (include/pulsar_b200.h).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "capi_util.h"
+#include "engine_kernels.cuh"
+#include "prefill_kernels.cuh"
+
+using namespace pulsar;
+
+namespace {
+
+// ------------------------------------------------------------------ repack kernels
+__global__ void k_f32_to_bf16(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16(src[i]);
+}
+
+// dst[b][c][r] = bf16(src[b][r][c]) for a batch of [rows][cols] matrices (32x32 tiles).
+__global__ void k_transpose_bf16(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int rows, int cols) {
+    __shared__ float tile[32][33];
+    const int b = blockIdx.z;
+    const float* s = src + (int64_t)b * rows * cols;
+    __nv_bfloat16* d = dst + (int64_t)b * rows * cols;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        tile[i][threadIdx.x] = (r < rows && c < cols) ? s[(int64_t)r * cols + c] : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) d[(int64_t)c * rows + r] = __float2bfloat16(tile[threadIdx.x][i]);
+    }
+}
+
+// Loop-adapter up factor for pulse p: dst[o][j*q + r] = lora_B[j][o][r] * (loop_M[p][j] * alpha / q).
+__global__ void k_lora_b(const float* __restrict__ lora_b, const float* __restrict__ loop_m, int P, int p, float scale,
+                         int d_out, int q, float* __restrict__ dst) {
+    const int64_t n = (int64_t)d_out * 3 * q;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int o = (int)(i / (3 * q));
+        const int jr = (int)(i % (3 * q));
+        const int j = jr / q, r = jr % q;
+        const float ms = loop_m[p * P + j] * scale;
+        dst[i] = lora_b[((int64_t)j * d_out + o) * q + r] * ms;
+    }
+}
+
+// RoPE tables (src/model.py:545-552): angle = fp32(pos * inv_freq[j]), cos / sin in fp32.
+__global__ void k_rope_table(const float* __restrict__ inv_freq, int n, float* __restrict__ cs, float* __restrict__ sn) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)n * 32; i += (int64_t)gridDim.x * blockDim.x) {
+        const int pos = (int)(i / 32), j = (int)(i % 32);
+        const float a = __fmul_rn((float)pos, inv_freq[j]);
+        cs[i] = cosf(a);
+        sn[i] = sinf(a);
+    }
+}
+
+// ------------------------------------------------------------------ decode-loop state kernels
+struct SeqDev {
+    int len;      // committed positions
+    int pending;  // next token to process (already emitted)
+    int n_out;    // tokens emitted
+    int done;
+};
+
+__global__ void k_seq_init(SeqDev* seqs, const int* lens, const int* first_tok, int n, int* out, int n_new) {
+    const int i = threadIdx.x;
+    if (i >= n) return;
+    seqs[i].len = lens[i];
+    seqs[i].pending = first_tok[i];
+    seqs[i].n_out = 1;
+    seqs[i].done = n_new <= 1;
+    out[(int64_t)i * n_new] = first_tok[i];
+}
+
+__global__ void k_rows_step(const SeqDev* seqs, const int* slots, int n, int4* rows) {
+    const int i = threadIdx.x;
+    if (i < n) rows[i] = make_int4(slots[i], seqs[i].len, seqs[i].pending, 0);
+}
+
+__global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, int* out, int n_new) {
+    const int i = threadIdx.x;
+    if (i >= n || seqs[i].done) return;
+    const int t = amax[i];
+    out[(int64_t)i * n_new + seqs[i].n_out] = t;
+    seqs[i].n_out += 1;
+    seqs[i].pending = t;
+    seqs[i].len += 1;
+    if (seqs[i].n_out >= n_new) seqs[i].done = 1;
+}
+
+// Speculative round: row j of sequence i is (slot, len + j, toks[i][j]); toks[i][0] = pending.
+__global__ void k_rows_spec(const SeqDev* seqs, const int* slots, int n, int gamma, int j, int* toks, int4* rows) {
+    const int i = threadIdx.x;
+    if (i >= n) return;
+    if (j == 0) toks[i * (gamma + 1)] = seqs[i].pending;
+    rows[i] = make_int4(slots[i], seqs[i].len + j, toks[i * (gamma + 1) + j], 0);
+}
+
+__global__ void k_store_draft(const int* amax, int n, int gamma, int j, int* toks) {
+    const int i = threadIdx.x;
+    if (i < n) toks[i * (gamma + 1) + j + 1] = amax[i];
+}
+
+__global__ void k_rows_verify(const SeqDev* seqs, const int* slots, int n, int gamma, const int* toks, int4* rows) {
+    const int i = threadIdx.x;
+    if (i >= n * (gamma + 1)) return;
+    const int s = i / (gamma + 1), j = i % (gamma + 1);
+    rows[i] = make_int4(slots[s], seqs[s].len + j, toks[i], 0);
+}
+
+__global__ void k_scatter_rows(const float* __restrict__ src, int n, int stride_rows, int j, float* __restrict__ dst) {
+    // dst[i * stride_rows + j] = src[i] (rows of D floats)
+    const int i = blockIdx.x;
+    for (int d = threadIdx.x; d < D; d += blockDim.x)
+        dst[((int64_t)i * stride_rows + j) * D + d] = src[(int64_t)i * D + d];
+}
+
+// Greedy acceptance: accept drafts while the verify argmax of the previous row matches;
+// the next pending token is the verify argmax after the last accepted draft.
+__global__ void k_accept_greedy(SeqDev* seqs, const int* toks, const int* amax_v, int n, int gamma, int* out,
+                                int n_new, long long* stats) {
+    const int i = threadIdx.x;
+    if (i >= n || seqs[i].done) return;
+    const int* tk = toks + i * (gamma + 1);
+    const int* am = amax_v + i * (gamma + 1);
+    int a = 0;
+    while (a < gamma && am[a] == tk[a + 1]) ++a;
+    const int nxt = am[a];
+    int no = seqs[i].n_out;
+    for (int j = 1; j <= a && no < n_new; ++j) out[(int64_t)i * n_new + no++] = tk[j];
+    if (no < n_new) out[(int64_t)i * n_new + no++] = nxt;
+    seqs[i].n_out = no;
+    seqs[i].len += a + 1;
+    seqs[i].pending = nxt;
+    if (no >= n_new) seqs[i].done = 1;
+    stats[i * 3 + 0] += 1;
+    stats[i * 3 + 1] += gamma;
+    stats[i * 3 + 2] += a;
+}
+
+int prefill_capacity(int T) {
+    // src/model.py:1339-1342 with top_k 4, 16 experts, factor 1.25, align 32
+    const double avg = (double)T * TOPK / E;
+    const int raw = (int)std::ceil(avg * 1.25);
+    return std::max(32, ((raw + 31) / 32) * 32);
+}
+
+}  // namespace
+
+// ====================================================================================
+struct pulsar_engine {
+    pulsar_engine_config cfg{};
+    int V = 0, P = 0;
+    bool finalized = false, has_lora = false;
+    std::map<std::string, float*> t;            // staged fp32 tensors (device)
+    std::map<std::string, int64_t> expect;      // name -> numel
+    std::vector<void*> allocs;
+    // bf16 arena
+    __nv_bfloat16* emb = nullptr;
+    __nv_bfloat16 *wqkv[NL] = {}, *wo[NL] = {}, *sh_gu[NL] = {}, *sh_dn[NL] = {}, *r_gu[NL] = {}, *r_dn[NL] = {};
+    float *lb_qkv[NP][NL] = {}, *lb_wo[NP][NL] = {};
+    float vres[NP][NL] = {};
+    float *cos_l = nullptr, *sin_l = nullptr, *cos_g = nullptr, *sin_g = nullptr;
+    int rope_len = 0;
+    // KV
+    void* kv = nullptr;
+    int64_t kv_bytes = 0, arena_bytes = 0, work_bytes = 0;
+    KVLayer kvl[NL];
+    int nch[NL] = {};
+    std::vector<int> len;
+    // decode workspace (R <= MAX_ROWS)
+    struct {
+        float *h, *h_in, *xn, *qkv, *q, *vfirst, *part, *att, *act_sh, *act_r, *hn, *t_qkv, *t_wo, *wts, *pmax;
+        int *idx, *pidx;
+    } w{};
+    // prefill workspace
+    struct {
+        int* ids;
+        float *h0, *h0n_pre, *h0n, *hp, *h, *h_in, *xn, *qkv, *q, *o, *att, *vfirst, *t, *wts, *act_sh, *sh, *act_e,
+            *ye, *hn, *pmax;
+        int *idx, *lists, *cnt, *slot, *rows_e, *kept, *pidx;
+        int cap;
+    } pf{};
+    // decode-loop state
+    SeqDev* seqs = nullptr;
+    int *slots_dev = nullptr, *toks = nullptr, *amax = nullptr, *lens_dev = nullptr, *first_dev = nullptr;
+    int4 *rows = nullptr, *rows_v = nullptr;
+    float *hblk = nullptr, *h0blk = nullptr, *htmp = nullptr, *htmp2 = nullptr, *h0tmp = nullptr, *logits_tmp = nullptr;
+    long long* stats = nullptr;
+    std::map<std::string, cudaGraphExec_t> graphs;
+
+    int dmalloc(void** p, size_t bytes, int64_t* counter) {
+        cudaError_t e = cudaMalloc(p, bytes);
+        if (e != cudaSuccess) return cuda_status(e, "cudaMalloc");
+        allocs.push_back(*p);
+        if (counter) *counter += (int64_t)bytes;
+        return PULSAR_OK;
+    }
+    template <typename T>
+    int wmalloc(T** p, size_t n) { return dmalloc(reinterpret_cast<void**>(p), n * sizeof(T), &work_bytes); }
+
+    const float* T_(const std::string& n) const {
+        auto it = t.find(n);
+        return it == t.end() ? nullptr : it->second;
+    }
+    std::string L(int l, const char* s) const { return "core." + std::to_string(l) + "." + s; }
+    bool kv32() const { return cfg.kv_fp32 != 0; }
+    // positions a row may use: inside every global layer's cache and the RoPE tables
+    int max_pos() const { return std::min(kvl[3].cap, rope_len); }
+};
+
+namespace {
+
+void build_expect(pulsar_engine* e) {
+    const int P = e->P, V = e->V, q = 8;
+    auto& x = e->expect;
+    x["tok_emb.weight"] = (int64_t)V * D;
+    x["lm_head.weight"] = (int64_t)V * D;
+    x["pulse_step_emb.weight"] = (int64_t)P * D;
+    x["pulse_state_norm.weight"] = D;
+    x["anchor_norm.weight"] = D;
+    x["final_norm.weight"] = D;
+    x["stem_canon_weight"] = (int64_t)D * 4;
+    x["reinject_gate_down"] = (int64_t)P * RG * 2 * D;
+    x["reinject_gate_up"] = (int64_t)P * D * RG;
+    x["reinject_gate_bias"] = (int64_t)P * D;
+    x["pulse_res_scale"] = (int64_t)P * D;
+    x["rope_local.inv_freq"] = DH / 2;
+    x["rope_global.inv_freq"] = DH / 2;
+    for (int l = 0; l < NL; ++l) {
+        x[e->L(l, "attn_norm.weight")] = (int64_t)P * D;
+        x[e->L(l, "attn.q_norm_weight")] = (int64_t)P * H * DH;
+        x[e->L(l, "attn.k_norm_weight")] = (int64_t)P * HKV * DH;
+        x[e->L(l, "attn.v_resid_lambda")] = P;
+        x[e->L(l, "attn.attn_gate")] = (int64_t)P * H * D;
+        x[e->L(l, "attn.attn_gate_bias")] = (int64_t)P * H;
+        x[e->L(l, "attn.wqkv.weight")] = (int64_t)QKV * D;
+        x[e->L(l, "attn.wo.weight")] = (int64_t)D * D;
+        x[e->L(l, "attn.wqkv_adapter.lora_A")] = (int64_t)P * q * D;
+        x[e->L(l, "attn.wqkv_adapter.lora_B")] = (int64_t)P * QKV * q;
+        x[e->L(l, "attn.wqkv_adapter.loop_M")] = (int64_t)P * P;
+        x[e->L(l, "attn.wo_adapter.lora_A")] = (int64_t)P * q * D;
+        x[e->L(l, "attn.wo_adapter.lora_B")] = (int64_t)P * D * q;
+        x[e->L(l, "attn.wo_adapter.loop_M")] = (int64_t)P * P;
+        x[e->L(l, "mlp_norm.weight")] = (int64_t)P * D;
+        x[e->L(l, "mlp.routed_gate_up")] = (int64_t)E * D * 2 * DE;
+        x[e->L(l, "mlp.routed_down")] = (int64_t)E * DE * D;
+        x[e->L(l, "mlp.router_weight")] = (int64_t)P * E * D;
+        x[e->L(l, "mlp.routed_scale")] = (int64_t)P * D;
+        x[e->L(l, "mlp.expert_bias")] = e->cfg.per_pulse_bias ? (int64_t)P * E : E;
+        x[e->L(l, "mlp.expert_counts_accum")] = E;
+        x[e->L(l, "mlp.expert_pulse_counts")] = (int64_t)P * E;
+        x[e->L(l, "mlp.shared_expert.w_gate_up.weight")] = (int64_t)2 * DS * D;
+        x[e->L(l, "mlp.shared_expert.w_down.weight")] = (int64_t)D * DS;
+    }
+}
+
+template <typename T>
+T* offs(T* p, int64_t n) { return p ? p + n : nullptr; }
+
+// ------------------------------------------------------------------ pulse pass (R <= MAX_ROWS)
+template <typename KVT>
+int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
+                  float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+    auto& w = e->w;
+    const float eps = e->cfg.rms_eps;
+    if (p == 0) {
+        k_pulse0_input<<<R, 256, 0, st>>>(rows, e->emb, e->T_("anchor_norm.weight"), e->T_("stem_canon_weight"),
+                                          e->T_("pulse_step_emb.weight"), eps, e->cfg.use_canon_conv, w.h, w.h_in,
+                                          h0n_out, e->V);
+    } else {
+        k_reinject<<<R, 256, 0, st>>>(R, h_prev, h0n_in, e->T_("pulse_state_norm.weight"),
+                                      e->T_("reinject_gate_down") + (int64_t)p * RG * 2 * D,
+                                      e->T_("reinject_gate_up") + (int64_t)p * D * RG,
+                                      e->T_("reinject_gate_bias") + (int64_t)p * D,
+                                      e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, w.h, w.h_in, h0n_out);
+    }
+    PULSAR_LAUNCH_CHECK("pulse input");
+    for (int l = 0; l < NL; ++l) {
+        const bool lora = e->has_lora;
+        k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, w.xn,
+                                          lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv);
+        k_gemv<1024, EPI_STORE><<<QKV / 8, 128, 0, st>>>(e->wqkv[l], QKV, w.xn, R, w.qkv, QKV,
+                                                         lora ? e->lb_qkv[p][l] : nullptr, w.t_qkv);
+        const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
+        const bool local = is_local_layer(l);
+        k_qkv_post<KVT><<<R, (H + HKV) * 32, 0, st>>>(
+            rows, w.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
+            e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
+            local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
+            e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
+        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, R), 128, 0, st>>>(rows, w.q, e->kvl[l], local ? 1 : 0, e->nch[l],
+                                                                    w.part, e->max_pos(), e->cfg.max_batch);
+        k_attn_combine<<<R, H * 32, 0, st>>>(w.part, e->nch[l], w.xn,
+                                             e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
+                                             e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
+                                             lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
+        k_gemv<1024, EPI_ADD><<<D / 8, 128, 0, st>>>(e->wo[l], D, w.att, R, w.h, D, lora ? e->lb_wo[p][l] : nullptr,
+                                                     w.t_wo);
+        k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, w.xn,
+                                          nullptr, nullptr);
+        const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
+        k_router<<<R, E * 32, 0, st>>>(w.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, w.idx,
+                                       w.wts);
+        k_moe_up<<<(DS + R * TOPK * DE) / 4, 128, 0, st>>>(R, w.xn, e->sh_gu[l], e->r_gu[l], w.idx, w.act_sh,
+                                                          w.act_r);
+        k_moe_down<<<D / 4, 128, 0, st>>>(R, w.act_sh, w.act_r, e->sh_dn[l], e->r_dn[l], w.idx, w.wts,
+                                          e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D, w.h);
+        PULSAR_LAUNCH_CHECK("pulse layer");
+    }
+    const bool want = logits != nullptr || amax != nullptr;
+    k_pulse_end<<<R, 256, 0, st>>>(w.h, w.h_in, e->T_("pulse_res_scale") + (int64_t)p * D, e->T_("final_norm.weight"),
+                                   eps, h_out, want ? w.hn : nullptr);
+    PULSAR_LAUNCH_CHECK("k_pulse_end");
+    if (want) {
+        const int nblk = e->V / LM_ROWS_PER_BLOCK;
+        for (int rb = 0; rb < R; rb += 8) {
+            const int n = std::min(8, R - rb);
+            k_lmhead<<<nblk, 128, 0, st>>>(e->emb, e->V, w.hn + (int64_t)rb * D, n, e->cfg.logit_softcap,
+                                           logits ? logits + (int64_t)rb * ld_logits : nullptr, ld_logits,
+                                           w.pmax + (int64_t)rb * nblk, w.pidx + (int64_t)rb * nblk);
+        }
+        PULSAR_LAUNCH_CHECK("k_lmhead");
+        if (amax) {
+            k_argmax_final<<<R, 32, 0, st>>>(w.pmax, w.pidx, nblk, R, amax);
+            PULSAR_LAUNCH_CHECK("k_argmax_final");
+        }
+    }
+    return PULSAR_OK;
+}
+
+int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in, float* h_out,
+          float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+    if (e->kv32())
+        return enqueue_pulse<float>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
+    return enqueue_pulse<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
+}
+
+// ------------------------------------------------------------------ prefill
+template <int EPI>
+int gemm(const GemmArgs& g, int batches, cudaStream_t st) {
+    const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2 + 31) / 32 : (g.N + GB_N - 1) / GB_N;
+    dim3 grid(ntiles, (g.M + GB_M - 1) / GB_M, batches);
+    k_gemm<EPI><<<grid, 256, 0, st>>>(g);
+    return launch_status("k_gemm");
+}
+
+GemmArgs gargs(const float* A, int lda, int M, const __nv_bfloat16* W, int N, int K, float* C, int ldc) {
+    GemmArgs g{};
+    g.A = A;
+    g.lda = lda;
+    g.M = M;
+    g.W = W;
+    g.N = N;
+    g.K = K;
+    g.C = C;
+    g.ldc = ldc;
+    return g;
+}
+
+template <typename KVT>
+int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* logits, cudaStream_t st) {
+    auto& f = e->pf;
+    const float eps = e->cfg.rms_eps;
+    k_embed_rows<<<T, 256, 0, st>>>(ids, e->emb, e->T_("anchor_norm.weight"), eps, f.h0, f.h0n_pre);
+    if (e->cfg.use_canon_conv)
+        k_conv_seq<<<T, 256, 0, st>>>(f.h0n_pre, e->T_("stem_canon_weight"), T, f.h0n);
+    else
+        PULSAR_TRY(cuda_status(cudaMemcpyAsync(f.h0n, f.h0n_pre, (size_t)T * D * 4, cudaMemcpyDeviceToDevice, st),
+                               "prefill copy"));
+    PULSAR_LAUNCH_CHECK("prefill embed");
+    const int cap = prefill_capacity(T);
+    const int M4 = T * TOPK;
+    for (int p = 0; p < NP; ++p) {
+        if (p == 0)
+            k_pulse0_rows<<<T, 256, 0, st>>>(f.h0n, e->T_("pulse_step_emb.weight"), f.h, f.h_in);
+        else
+            k_reinject<<<T, 256, 0, st>>>(T, f.hp, f.h0n, e->T_("pulse_state_norm.weight"),
+                                          e->T_("reinject_gate_down") + (int64_t)p * RG * 2 * D,
+                                          e->T_("reinject_gate_up") + (int64_t)p * D * RG,
+                                          e->T_("reinject_gate_bias") + (int64_t)p * D,
+                                          e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, f.h, f.h_in, nullptr);
+        PULSAR_LAUNCH_CHECK("prefill pulse input");
+        for (int l = 0; l < NL; ++l) {
+            const bool lora = e->has_lora;
+            const bool local = is_local_layer(l);
+            k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, f.xn,
+                                              lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, f.t);
+            GemmArgs g = gargs(f.xn, D, T, e->wqkv[l], QKV, D, f.qkv, QKV);
+            if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = f.t; }
+            PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st));
+            const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
+            k_qkv_post_prefill<KVT><<<T, (H + HKV) * 32, 0, st>>>(
+                slot, T, f.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
+                e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
+                local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], f.vfirst, e->kvl[l], local ? 1 : 0, f.q);
+            k_attn_prefill<KVT><<<dim3((T + PA_Q - 1) / PA_Q, H), 256, 0, st>>>(slot, T, f.q, e->kvl[l], local ? 1 : 0,
+                                                                               f.o);
+            k_gate_rows<<<T, H * 32, 0, st>>>(f.o, f.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
+                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, f.att,
+                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, f.t);
+            PULSAR_LAUNCH_CHECK("prefill attention");
+            g = gargs(f.att, D, T, e->wo[l], D, D, f.h, D);
+            if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = f.t; }
+            PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st));
+            k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, f.xn,
+                                              nullptr, nullptr);
+            const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
+            k_router<<<T, E * 32, 0, st>>>(f.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, f.idx,
+                                           f.wts);
+            PULSAR_LAUNCH_CHECK("prefill router");
+            PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(f.xn, D, T, e->sh_gu[l], 2 * DS, D, f.act_sh, DS), 1, st));
+            PULSAR_TRY(gemm<GEPI_STORE>(gargs(f.act_sh, DS, T, e->sh_dn[l], D, DS, f.sh, D), 1, st));
+            k_moe_bucket<<<E, 1024, 0, st>>>(f.idx, M4, f.lists, M4, f.cnt);
+            k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(f.lists, M4, f.cnt, f.wts, cap, f.slot, f.rows_e,
+                                                                  f.kept);
+            PULSAR_LAUNCH_CHECK("prefill slots");
+            GemmArgs gu = gargs(f.xn, D, cap, e->r_gu[l], 2 * DE, D, f.act_e, DE);
+            gu.a_rows = f.rows_e;
+            gu.m_count = f.kept;
+            gu.w_stride = (int64_t)2 * DE * D;
+            gu.c_stride = (int64_t)cap * DE;
+            PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st));
+            GemmArgs gd = gargs(f.act_e, DE, cap, e->r_dn[l], D, DE, f.ye, D);
+            gd.a_stride = (int64_t)cap * DE;
+            gd.m_count = f.kept;
+            gd.w_stride = (int64_t)D * DE;
+            gd.c_stride = (int64_t)cap * D;
+            PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st));
+            k_moe_combine_rows<<<T, 256, 0, st>>>(f.sh, f.ye, cap, f.idx, f.wts, f.slot,
+                                                  e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D, f.h);
+            PULSAR_LAUNCH_CHECK("prefill moe combine");
+        }
+        k_pulse_end<<<T, 256, 0, st>>>(f.h, f.h_in, e->T_("pulse_res_scale") + (int64_t)p * D,
+                                       e->T_("final_norm.weight"), eps, f.hp, nullptr);
+        PULSAR_LAUNCH_CHECK("prefill pulse end");
+    }
+    // last position logits without softcap (src/infer.py:458-461)
+    k_rmsnorm_lora<<<1, 256, 0, st>>>(f.hp + (int64_t)(T - 1) * D, e->T_("final_norm.weight"), eps, f.hn, nullptr,
+                                      nullptr);
+    const int nblk = e->V / LM_ROWS_PER_BLOCK;
+    k_lmhead<<<nblk, 128, 0, st>>>(e->emb, e->V, f.hn, 1, 0.f, logits, e->V, f.pmax, f.pidx);
+    PULSAR_LAUNCH_CHECK("prefill lm head");
+    return PULSAR_OK;
+}
+
+int check_engine(pulsar_engine* e, bool need_final) {
+    PULSAR_CHECK_ARG(e != nullptr, "null engine handle");
+    if (need_final && !e->finalized) {
+        set_error("engine not finalized: call pulsar_engine_finalize after uploading every tensor");
+        return PULSAR_ERR_STATE;
+    }
+    return PULSAR_OK;
+}
+
+int run_graph(pulsar_engine* e, const std::string& key, cudaStream_t st, int (*body)(pulsar_engine*, cudaStream_t, void*),
+              void* ctx) {
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end()) {
+        cudaGraph_t g;
+        cudaStream_t cs;
+        PULSAR_TRY(cuda_status(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate"));
+        PULSAR_TRY(cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "BeginCapture"));
+        int st_body = body(e, cs, ctx);
+        cudaError_t ce = cudaStreamEndCapture(cs, &g);
+        cudaStreamDestroy(cs);
+        PULSAR_TRY(st_body);
+        PULSAR_TRY(cuda_status(ce, "EndCapture"));
+        cudaGraphExec_t ex;
+        ce = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        PULSAR_TRY(cuda_status(ce, "cudaGraphInstantiate"));
+        it = e->graphs.emplace(key, ex).first;
+    }
+    return cuda_status(cudaGraphLaunch(it->second, st), "cudaGraphLaunch");
+}
+
+struct LoopCtx {
+    int n, gamma, n_new;
+    int* out;
+};
+
+int body_step(pulsar_engine* e, cudaStream_t st, void* vctx) {
+    LoopCtx* c = static_cast<LoopCtx*>(vctx);
+    const int n = c->n;
+    k_rows_step<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, e->rows);
+    PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, nullptr, 0, nullptr, st));
+    PULSAR_TRY(pulse(e, 1, n, e->rows, e->htmp, e->h0tmp, e->htmp2, e->h0tmp, nullptr, 0, nullptr, st));
+    PULSAR_TRY(pulse(e, 2, n, e->rows, e->htmp2, e->h0tmp, e->htmp, e->h0tmp, nullptr, 0, e->amax, st));
+    k_commit_greedy<<<1, 32, 0, st>>>(e->seqs, e->amax, n, c->out, c->n_new);
+    return launch_status("k_commit_greedy");
+}
+
+int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
+    LoopCtx* c = static_cast<LoopCtx*>(vctx);
+    const int n = c->n, g = c->gamma, rows_v = n * (g + 1);
+    for (int j = 0; j <= g; ++j) {
+        k_rows_spec<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->toks, e->rows);
+        const bool draft = j < g;
+        PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, nullptr, 0, draft ? e->amax : nullptr,
+                         st));
+        k_scatter_rows<<<n, 256, 0, st>>>(e->htmp, n, g + 1, j, e->hblk);
+        k_scatter_rows<<<n, 256, 0, st>>>(e->h0tmp, n, g + 1, j, e->h0blk);
+        if (draft) k_store_draft<<<1, 32, 0, st>>>(e->amax, n, g, j, e->toks);
+        PULSAR_LAUNCH_CHECK("draft");
+    }
+    k_rows_verify<<<1, 128, 0, st>>>(e->seqs, e->slots_dev, n, g, e->toks, e->rows_v);
+    PULSAR_TRY(pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, e->h0tmp, nullptr, 0, nullptr, st));
+    PULSAR_TRY(pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, e->h0tmp, nullptr, 0, e->amax, st));
+    k_accept_greedy<<<1, 32, 0, st>>>(e->seqs, e->toks, e->amax, n, g, c->out, c->n_new, e->stats);
+    return launch_status("k_accept_greedy");
+}
+
+}  // namespace
+
+// ==================================================================================== C ABI
+extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engine** out) {
+    PULSAR_CHECK_ARG(cfg && out, "pulsar_engine_create: null argument");
+    PULSAR_CHECK_ARG(cfg->vocab_size > 0 && cfg->vocab_size % 256 == 0, "vocab_size must be a positive multiple of 256");
+    PULSAR_CHECK_ARG(cfg->max_pulses >= NP, "max_pulses must be >= %d", NP);
+    PULSAR_CHECK_ARG(cfg->loop_lora_rank == 0 || cfg->loop_lora_rank == 8, "loop_lora_rank must be 0 or 8");
+    PULSAR_CHECK_ARG(cfg->max_batch >= 1 && cfg->max_batch <= MAX_ROWS, "max_batch must be in [1, %d]", MAX_ROWS);
+    PULSAR_CHECK_ARG(cfg->max_seq_len >= 16, "max_seq_len too small");
+    PULSAR_CHECK_ARG(cfg->max_prefill >= 1 && cfg->max_prefill <= cfg->max_seq_len, "max_prefill must be in [1, max_seq_len]");
+    PULSAR_TRY(cuda_status(cudaSetDevice(cfg->device), "cudaSetDevice"));
+    auto* e = new pulsar_engine();
+    e->cfg = *cfg;
+    e->V = cfg->vocab_size;
+    e->P = cfg->max_pulses;
+    build_expect(e);
+    auto fail = [&](int st) {
+        pulsar_engine_destroy(e);
+        return st;
+    };
+    // KV cache
+    const int maxlen = ((cfg->max_seq_len + 63) / 64) * 64;
+    const int cap_local = maxlen <= LOCAL_RING ? maxlen : LOCAL_RING;
+    const int esz = cfg->kv_fp32 ? 4 : 2;
+    int64_t off = 0;
+    int64_t layer_off[NL];
+    for (int l = 0; l < NL; ++l) {
+        const int cap = is_local_layer(l) ? cap_local : maxlen;
+        layer_off[l] = off;
+        off += (int64_t)2 * HKV * cap * DH;
+        e->kvl[l].cap = cap;
+        e->kvl[l].mask = (is_local_layer(l) && cap == LOCAL_RING) ? (LOCAL_RING - 1) : -1;
+        e->nch[l] = is_local_layer(l) ? (WINDOW / ATT_CHUNK) : (maxlen + ATT_CHUNK - 1) / ATT_CHUNK;
+    }
+    const int64_t slot_elems = off;
+    int st = e->dmalloc(&e->kv, (size_t)slot_elems * cfg->max_batch * esz, &e->kv_bytes);
+    if (st) return fail(st);
+    for (int l = 0; l < NL; ++l) {
+        e->kvl[l].base = static_cast<char*>(e->kv) + layer_off[l] * esz;
+        e->kvl[l].slot_stride = slot_elems;
+    }
+    e->len.assign(cfg->max_batch, 0);
+    // decode workspace
+    const int R = MAX_ROWS;
+    int nch_max = 0;
+    for (int l = 0; l < NL; ++l) nch_max = std::max(nch_max, e->nch[l]);
+    auto& w = e->w;
+    const int nblk = e->V / LM_ROWS_PER_BLOCK;
+    if ((st = e->wmalloc(&w.h, (size_t)R * D)) || (st = e->wmalloc(&w.h_in, (size_t)R * D)) ||
+        (st = e->wmalloc(&w.xn, (size_t)R * D)) || (st = e->wmalloc(&w.qkv, (size_t)R * QKV)) ||
+        (st = e->wmalloc(&w.q, (size_t)R * H * DH)) || (st = e->wmalloc(&w.vfirst, (size_t)R * HKV * DH)) ||
+        (st = e->wmalloc(&w.part, (size_t)R * H * nch_max * PART)) || (st = e->wmalloc(&w.att, (size_t)R * D)) ||
+        (st = e->wmalloc(&w.act_sh, (size_t)R * DS)) || (st = e->wmalloc(&w.act_r, (size_t)R * TOPK * DE)) ||
+        (st = e->wmalloc(&w.hn, (size_t)R * D)) || (st = e->wmalloc(&w.t_qkv, (size_t)R * LORA_R)) ||
+        (st = e->wmalloc(&w.t_wo, (size_t)R * LORA_R)) || (st = e->wmalloc(&w.wts, (size_t)R * TOPK)) ||
+        (st = e->wmalloc(&w.pmax, (size_t)R * nblk)) || (st = e->wmalloc(&w.idx, (size_t)R * TOPK)) ||
+        (st = e->wmalloc(&w.pidx, (size_t)R * nblk)))
+        return fail(st);
+    // prefill workspace
+    auto& f = e->pf;
+    const int T = cfg->max_prefill;
+    const int cap = prefill_capacity(T);
+    f.cap = cap;
+    const size_t TD = (size_t)T * D;
+    if ((st = e->wmalloc(&f.ids, T)) || (st = e->wmalloc(&f.h0, TD)) || (st = e->wmalloc(&f.h0n_pre, TD)) ||
+        (st = e->wmalloc(&f.h0n, TD)) || (st = e->wmalloc(&f.hp, TD)) || (st = e->wmalloc(&f.h, TD)) ||
+        (st = e->wmalloc(&f.h_in, TD)) || (st = e->wmalloc(&f.xn, TD)) || (st = e->wmalloc(&f.qkv, (size_t)T * QKV)) ||
+        (st = e->wmalloc(&f.q, (size_t)T * H * DH)) || (st = e->wmalloc(&f.o, (size_t)T * H * DH)) ||
+        (st = e->wmalloc(&f.att, TD)) || (st = e->wmalloc(&f.vfirst, (size_t)T * HKV * DH)) ||
+        (st = e->wmalloc(&f.t, (size_t)T * LORA_R)) || (st = e->wmalloc(&f.wts, (size_t)T * TOPK)) ||
+        (st = e->wmalloc(&f.act_sh, (size_t)T * DS)) || (st = e->wmalloc(&f.sh, TD)) ||
+        (st = e->wmalloc(&f.act_e, (size_t)E * cap * DE)) || (st = e->wmalloc(&f.ye, (size_t)E * cap * D)) ||
+        (st = e->wmalloc(&f.hn, (size_t)D)) || (st = e->wmalloc(&f.pmax, (size_t)nblk)) ||
+        (st = e->wmalloc(&f.idx, (size_t)T * TOPK)) || (st = e->wmalloc(&f.lists, (size_t)E * T * TOPK)) ||
+        (st = e->wmalloc(&f.cnt, E)) || (st = e->wmalloc(&f.slot, (size_t)T * TOPK)) ||
+        (st = e->wmalloc(&f.rows_e, (size_t)E * cap)) || (st = e->wmalloc(&f.kept, E)) ||
+        (st = e->wmalloc(&f.pidx, (size_t)nblk)))
+        return fail(st);
+    // decode-loop state
+    if ((st = e->wmalloc(&e->seqs, MAX_ROWS)) || (st = e->wmalloc(&e->slots_dev, MAX_ROWS)) ||
+        (st = e->wmalloc(&e->toks, MAX_ROWS)) || (st = e->wmalloc(&e->amax, MAX_ROWS)) ||
+        (st = e->wmalloc(&e->lens_dev, MAX_ROWS)) || (st = e->wmalloc(&e->first_dev, MAX_ROWS)) ||
+        (st = e->wmalloc(&e->rows, MAX_ROWS)) || (st = e->wmalloc(&e->rows_v, MAX_ROWS)) ||
+        (st = e->wmalloc(&e->hblk, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->h0blk, (size_t)MAX_ROWS * D)) ||
+        (st = e->wmalloc(&e->htmp, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->htmp2, (size_t)MAX_ROWS * D)) ||
+        (st = e->wmalloc(&e->h0tmp, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->stats, (size_t)MAX_ROWS * 3)))
+        return fail(st);
+    *out = e;
+    clear_error();
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_destroy(pulsar_engine* e) {
+    if (!e) return PULSAR_OK;
+    cudaSetDevice(e->cfg.device);
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : e->t) cudaFree(kv.second);
+    for (void* p : e->allocs) cudaFree(p);
+    delete e;
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_set_tensor(pulsar_engine* e, const char* name, const float* data, int64_t numel) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(name && data, "set_tensor: null argument");
+    auto it = e->expect.find(name);
+    PULSAR_CHECK_ARG(it != e->expect.end(), "set_tensor: unknown tensor name '%s'", name);
+    PULSAR_CHECK_ARG(it->second == numel, "set_tensor: '%s' has %lld elements, expected %lld", name, (long long)numel,
+                     (long long)it->second);
+    if (e->finalized) {
+        set_error("set_tensor after finalize is not supported ('%s')", name);
+        return PULSAR_ERR_STATE;
+    }
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    float*& dst = e->t[name];
+    if (!dst) PULSAR_TRY(cuda_status(cudaMalloc(&dst, (size_t)numel * 4), "cudaMalloc(staging)"));
+    PULSAR_TRY(cuda_status(cudaMemcpy(dst, data, (size_t)numel * 4, cudaMemcpyHostToDevice), "set_tensor copy"));
+    if (strstr(name, "lora_B")) {
+        for (int64_t i = 0; i < numel; ++i)
+            if (data[i] != 0.f) { e->has_lora = e->cfg.loop_lora_rank > 0; break; }
+    }
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_finalize(pulsar_engine* e) {
+    PULSAR_TRY(check_engine(e, false));
+    if (e->finalized) return PULSAR_OK;
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    for (auto& kv : e->expect) {
+        if (kv.first == "lm_head.weight" || kv.first.find("expert_counts") != std::string::npos ||
+            kv.first.find("expert_pulse_counts") != std::string::npos)
+            continue;
+        if (!e->cfg.loop_lora_rank && (kv.first.find("_adapter.") != std::string::npos)) continue;
+        if (!e->T_(kv.first)) {
+            set_error("finalize: tensor '%s' was never uploaded", kv.first.c_str());
+            return PULSAR_ERR_STATE;
+        }
+    }
+    cudaStream_t st = 0;
+    auto conv = [&](const std::string& n, __nv_bfloat16** dst, int64_t numel) -> int {
+        PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(dst), (size_t)numel * 2, &e->arena_bytes));
+        k_f32_to_bf16<<<1024, 256, 0, st>>>(e->T_(n), *dst, numel);
+        return launch_status("k_f32_to_bf16");
+    };
+    PULSAR_TRY(conv("tok_emb.weight", &e->emb, (int64_t)e->V * D));
+    for (int l = 0; l < NL; ++l) {
+        PULSAR_TRY(conv(e->L(l, "attn.wqkv.weight"), &e->wqkv[l], (int64_t)QKV * D));
+        PULSAR_TRY(conv(e->L(l, "attn.wo.weight"), &e->wo[l], (int64_t)D * D));
+        PULSAR_TRY(conv(e->L(l, "mlp.shared_expert.w_gate_up.weight"), &e->sh_gu[l], (int64_t)2 * DS * D));
+        PULSAR_TRY(conv(e->L(l, "mlp.shared_expert.w_down.weight"), &e->sh_dn[l], (int64_t)D * DS));
+        PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->r_gu[l]), (size_t)E * D * 2 * DE * 2, &e->arena_bytes));
+        PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->r_dn[l]), (size_t)E * DE * D * 2, &e->arena_bytes));
+        // routed_gate_up [E][D in][2*DE out] -> [E][2*DE out][D in]
+        k_transpose_bf16<<<dim3(2 * DE / 32, D / 32, E), dim3(32, 8), 0, st>>>(e->T_(e->L(l, "mlp.routed_gate_up")),
+                                                                                e->r_gu[l], D, 2 * DE);
+        // routed_down [E][DE in][D out] -> [E][D out][DE in]
+        k_transpose_bf16<<<dim3(D / 32, DE / 32, E), dim3(32, 8), 0, st>>>(e->T_(e->L(l, "mlp.routed_down")),
+                                                                            e->r_dn[l], DE, D);
+        PULSAR_LAUNCH_CHECK("expert transpose");
+        std::vector<float> lam(e->P);
+        PULSAR_TRY(cuda_status(cudaMemcpy(lam.data(), e->T_(e->L(l, "attn.v_resid_lambda")), e->P * 4,
+                                          cudaMemcpyDeviceToHost),
+                               "read v_resid_lambda"));
+        for (int p = 0; p < NP; ++p) e->vres[p][l] = 1.f / (1.f + std::exp(-lam[p]));
+        if (e->has_lora) {
+            const float scale = e->cfg.loop_lora_alpha / 8.f;
+            for (int p = 0; p < NP; ++p) {
+                PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->lb_qkv[p][l]), (size_t)QKV * LORA_R * 4, &e->arena_bytes));
+                PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->lb_wo[p][l]), (size_t)D * LORA_R * 4, &e->arena_bytes));
+                k_lora_b<<<256, 256, 0, st>>>(e->T_(e->L(l, "attn.wqkv_adapter.lora_B")),
+                                              e->T_(e->L(l, "attn.wqkv_adapter.loop_M")), e->P, p, scale, QKV, 8,
+                                              e->lb_qkv[p][l]);
+                k_lora_b<<<256, 256, 0, st>>>(e->T_(e->L(l, "attn.wo_adapter.lora_B")),
+                                              e->T_(e->L(l, "attn.wo_adapter.loop_M")), e->P, p, scale, D, 8,
+                                              e->lb_wo[p][l]);
+                PULSAR_LAUNCH_CHECK("k_lora_b");
+            }
+        }
+    }
+    // RoPE tables covering every position the KV cache can hold
+    e->rope_len = ((e->cfg.max_seq_len + 63) / 64) * 64 + 64;
+    for (float** p : {&e->cos_l, &e->sin_l, &e->cos_g, &e->sin_g})
+        PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(p), (size_t)e->rope_len * 32 * 4, &e->arena_bytes));
+    k_rope_table<<<256, 256, 0, st>>>(e->T_("rope_local.inv_freq"), e->rope_len, e->cos_l, e->sin_l);
+    k_rope_table<<<256, 256, 0, st>>>(e->T_("rope_global.inv_freq"), e->rope_len, e->cos_g, e->sin_g);
+    PULSAR_LAUNCH_CHECK("k_rope_table");
+    PULSAR_TRY(cuda_status(cudaDeviceSynchronize(), "finalize"));
+    // the big fp32 staging copies are no longer needed
+    const char* big[] = {"attn.wqkv.weight", "attn.wo.weight", "mlp.shared_expert.w_gate_up.weight",
+                         "mlp.shared_expert.w_down.weight", "mlp.routed_gate_up", "mlp.routed_down"};
+    for (int l = 0; l < NL; ++l)
+        for (const char* b : big) {
+            auto it = e->t.find(e->L(l, b));
+            if (it != e->t.end()) { cudaFree(it->second); e->t.erase(it); }
+        }
+    for (const char* b : {"tok_emb.weight", "lm_head.weight"}) {
+        auto it = e->t.find(b);
+        if (it != e->t.end()) { cudaFree(it->second); e->t.erase(it); }
+    }
+    e->finalized = true;
+    clear_error();
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_memory(const pulsar_engine* e, int64_t* a, int64_t* k, int64_t* w) {
+    PULSAR_CHECK_ARG(e, "null engine handle");
+    if (a) *a = e->arena_bytes;
+    if (k) *k = e->kv_bytes;
+    if (w) *w = e->work_bytes;
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_prefill(pulsar_engine* e, int32_t slot, const int32_t* ids, int32_t T, float* logits,
+                                     void* stream) {
+    PULSAR_TRY(check_engine(e, true));
+    PULSAR_CHECK_ARG(slot >= 0 && slot < e->cfg.max_batch, "prefill: slot %d out of range", slot);
+    PULSAR_CHECK_ARG(T >= 1, "prefill: empty prompt");
+    if (T > e->cfg.max_prefill) {
+        set_error("prefill: prompt of %d tokens exceeds max_prefill %d", T, e->cfg.max_prefill);
+        return PULSAR_ERR_CAPACITY;
+    }
+    PULSAR_CHECK_ARG(ids && logits, "prefill: null pointer");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    {
+        std::vector<int32_t> h(T);
+        PULSAR_TRY(cuda_status(cudaMemcpyAsync(h.data(), ids, (size_t)T * 4, cudaMemcpyDeviceToHost, st), "copy ids"));
+        PULSAR_TRY(cuda_status(cudaStreamSynchronize(st), "copy ids"));
+        for (int i = 0; i < T; ++i)
+            if (h[i] < 0 || h[i] >= e->V) {
+                set_error("prefill: token %d at index %d outside [0, %d)", h[i], i, e->V);
+                return PULSAR_ERR_INVALID;
+            }
+    }
+    const int rc = e->kv32() ? enqueue_prefill<float>(e, slot, ids, T, logits, st)
+                             : enqueue_prefill<__nv_bfloat16>(e, slot, ids, T, logits, st);
+    if (rc == PULSAR_OK) e->len[slot] = T;
+    return rc;
+}
+
+extern "C" int pulsar_engine_pulse(pulsar_engine* e, int32_t p, int32_t R, const int32_t* rows, const float* h_prev,
+                                   const float* h0n, float* h_out, float* h0n_out, float* logits, void* stream) {
+    PULSAR_TRY(check_engine(e, true));
+    PULSAR_CHECK_ARG(p >= 0 && p < NP, "pulse index %d out of range [0, %d)", p, NP);
+    PULSAR_CHECK_ARG(R >= 1 && R <= MAX_ROWS, "rows %d out of range [1, %d]", R, MAX_ROWS);
+    PULSAR_CHECK_ARG(rows && h_out && h0n_out, "pulse: null pointer");
+    PULSAR_CHECK_ARG(p == 0 || (h_prev && h0n), "pulse %d needs h_prev and h0n", p);
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    {
+        // validate the row descriptors before any kernel indexes the cache with them
+        int4 hr[MAX_ROWS];
+        cudaStream_t vs = reinterpret_cast<cudaStream_t>(stream);
+        PULSAR_TRY(cuda_status(cudaMemcpyAsync(hr, rows, (size_t)R * sizeof(int4), cudaMemcpyDeviceToHost, vs), "copy rows"));
+        PULSAR_TRY(cuda_status(cudaStreamSynchronize(vs), "copy rows"));
+        for (int r = 0; r < R; ++r) {
+            if (hr[r].x < 0 || hr[r].x >= e->cfg.max_batch) {
+                set_error("pulse: row %d has slot %d outside [0, %d)", r, hr[r].x, e->cfg.max_batch);
+                return PULSAR_ERR_INVALID;
+            }
+            if (hr[r].y < 0 || hr[r].y >= e->max_pos()) {
+                set_error("pulse: row %d position %d outside [0, %d)", r, hr[r].y, e->max_pos());
+                return PULSAR_ERR_CAPACITY;
+            }
+            if (hr[r].z < 0 || hr[r].z >= e->V) {
+                set_error("pulse: row %d token %d outside [0, %d)", r, hr[r].z, e->V);
+                return PULSAR_ERR_INVALID;
+            }
+        }
+    }
+    return pulse(e, p, R, reinterpret_cast<const int4*>(rows), h_prev, h0n, h_out, h0n_out, logits, e->V, nullptr,
+                 reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pulsar_engine_get_length(pulsar_engine* e, int32_t slot, int32_t* length) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(slot >= 0 && slot < e->cfg.max_batch && length, "get_length: bad slot %d", slot);
+    *length = e->len[slot];
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_set_length(pulsar_engine* e, int32_t slot, int32_t length) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(slot >= 0 && slot < e->cfg.max_batch, "set_length: bad slot %d", slot);
+    if (length < 0 || length > e->cfg.max_seq_len) {
+        set_error("set_length: %d outside [0, max_seq_len=%d]", length, e->cfg.max_seq_len);
+        return PULSAR_ERR_CAPACITY;
+    }
+    e->len[slot] = length;
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const int32_t* slots_host,
+                                             const float* first_logits, int32_t n_new, int32_t gamma, int32_t* out,
+                                             int64_t* stats_host, void* stream) {
+    PULSAR_TRY(check_engine(e, true));
+    PULSAR_CHECK_ARG(n >= 1 && n <= e->cfg.max_batch, "generate: n_seq %d out of range", n);
+    PULSAR_CHECK_ARG(gamma >= 0 && n * (gamma + 1) <= MAX_ROWS, "generate: n_seq * (gamma + 1) must be <= %d", MAX_ROWS);
+    PULSAR_CHECK_ARG(n_new >= 1 && slots_host && first_logits && out, "generate: bad arguments");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    std::vector<int> lens(n);
+    for (int i = 0; i < n; ++i) {
+        const int s = slots_host[i];
+        PULSAR_CHECK_ARG(s >= 0 && s < e->cfg.max_batch, "generate: slot %d out of range", s);
+        PULSAR_CHECK_ARG(e->len[s] >= 1, "generate: slot %d has no prefilled context", s);
+        lens[i] = e->len[s];
+        if (lens[i] + n_new + gamma + 1 > e->cfg.max_seq_len) {
+            set_error("generate: slot %d needs %d positions, max_seq_len is %d", s, lens[i] + n_new + gamma + 1,
+                      e->cfg.max_seq_len);
+            return PULSAR_ERR_CAPACITY;
+        }
+    }
+    PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->slots_dev, slots_host, n * 4, cudaMemcpyHostToDevice, st), "copy slots"));
+    PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->lens_dev, lens.data(), n * 4, cudaMemcpyHostToDevice, st), "copy lens"));
+    PULSAR_TRY(cuda_status(cudaMemsetAsync(e->stats, 0, (size_t)MAX_ROWS * 3 * 8, st), "zero stats"));
+    k_argmax_rows<<<n, 1024, 0, st>>>(first_logits, e->V, e->V, e->first_dev);
+    k_seq_init<<<1, 32, 0, st>>>(e->seqs, e->lens_dev, e->first_dev, n, out, n_new);
+    PULSAR_LAUNCH_CHECK("generate init");
+    LoopCtx ctx{n, gamma, n_new, out};
+    const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + ":" + std::to_string(n_new) + ":" +
+                            std::to_string(reinterpret_cast<uintptr_t>(out));
+    std::vector<SeqDev> hs(n);
+    int remaining_steps = n_new - 1;
+    while (true) {
+        if (gamma == 0) {
+            for (int s = 0; s < remaining_steps; ++s) PULSAR_TRY(run_graph(e, key, st, body_step, &ctx));
+        } else {
+            // each round emits between 1 and gamma+1 tokens; launch the minimum, then check
+            const int rounds = std::max(1, (remaining_steps + gamma) / (gamma + 1));
+            for (int s = 0; s < rounds; ++s) PULSAR_TRY(run_graph(e, key, st, body_round, &ctx));
+        }
+        PULSAR_TRY(cuda_status(cudaMemcpyAsync(hs.data(), e->seqs, n * sizeof(SeqDev), cudaMemcpyDeviceToHost, st),
+                               "read state"));
+        PULSAR_TRY(cuda_status(cudaStreamSynchronize(st), "generate sync"));
+        int min_out = n_new;
+        for (int i = 0; i < n; ++i) min_out = std::min(min_out, hs[i].n_out);
+        if (min_out >= n_new) break;
+        remaining_steps = n_new - min_out;
+    }
+    for (int i = 0; i < n; ++i) e->len[slots_host[i]] = hs[i].len;
+    if (stats_host) {
+        std::vector<long long> sv((size_t)n * 3);
+        PULSAR_TRY(cuda_status(cudaMemcpy(sv.data(), e->stats, sv.size() * 8, cudaMemcpyDeviceToHost), "read stats"));
+        stats_host[0] = stats_host[1] = stats_host[2] = 0;
+        for (int i = 0; i < n; ++i)
+            for (int k = 0; k < 3; ++k) stats_host[k] += sv[(size_t)i * 3 + k];
+    }
+    return PULSAR_OK;
+}

@@ -1,0 +1,370 @@
+// The pulsar_cuda forward ops behind the C ABI (include/pulsar_b200.h, pulsar_op_*).
+//
+// Each op keeps the reference binding's argument meaning (csrc/pulsar_cuda.cpp:199-279)
+// but is written for sm_100a: 128-bit vector loads where the layout allows, fp32
+// arithmetic, launches on the caller's stream with every launch checked, and
+// deterministic reductions (no float atomics) for the router's z-loss / probs_mean.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "capi_util.h"
+#include "common.cuh"
+
+using namespace pulsar;
+
+namespace {
+
+inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline int grid_cap(int64_t n, int64_t per) {
+    int64_t g = (n + per - 1) / per;
+    if (g > 65535 * 16) g = 65535 * 16;
+    return (int)(g < 1 ? 1 : g);
+}
+
+// ---------------------------------------------------------------- rmsnorm
+__global__ void k_rmsnorm_rows(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, int64_t rows,
+                               int D, float eps, __nv_bfloat16* __restrict__ y, float* __restrict__ rs) {
+    __shared__ float red[32];
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const __nv_bfloat16* xr = x + r * D;
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < D; i += blockDim.x) {
+            float v = __bfloat162float(xr[i]);
+            ss += v * v;
+        }
+        ss = block_sum(ss, red);
+        const float inv = rsqrtf(ss / (float)D + eps);
+        if (threadIdx.x == 0 && rs) rs[r] = inv;
+        for (int i = threadIdx.x; i < D; i += blockDim.x)
+            y[r * D + i] = __float2bfloat16(w[i] * (__bfloat162float(xr[i]) * inv));
+    }
+}
+
+// ---------------------------------------------------------------- rope
+__global__ void k_rope(const __nv_bfloat16* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
+                       int64_t rows, int64_t T, int half, __nv_bfloat16* __restrict__ y) {
+    const int64_t n = rows * half;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / half;
+        const int j = (int)(i % half);
+        const int64_t t = r % T;
+        const float c = cs[t * half + j], s = sn[t * half + j];
+        const float x1 = __bfloat162float(x[r * 2 * half + j]);
+        const float x2 = __bfloat162float(x[r * 2 * half + j + half]);
+        y[r * 2 * half + j] = __float2bfloat16(x1 * c - x2 * s);
+        y[r * 2 * half + j + half] = __float2bfloat16(x2 * c + x1 * s);
+    }
+}
+
+// ---------------------------------------------------------------- swiglu
+__global__ void k_swiglu(const __nv_bfloat16* __restrict__ gu, int64_t rows, int64_t d, __nv_bfloat16* __restrict__ out) {
+    const int64_t n = rows * d;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / d, j = i % d;
+        const float g = __bfloat162float(gu[r * 2 * d + j]);
+        const float u = __bfloat162float(gu[r * 2 * d + d + j]);
+        out[i] = __float2bfloat16(siluf_(g) * u);
+    }
+}
+
+// ---------------------------------------------------------------- router top-k
+// One warp per token; lane e holds expert e. Top-K by K rounds of a warp argmax with ties
+// to the lowest expert index (the order the reference's insertion sort with strict '>'
+// produces). Per-token lse^2 and sigmoid scores go to `ws` for a deterministic mean.
+template <bool BF16>
+__global__ void k_router_topk(const void* __restrict__ logits_v, const float* __restrict__ bias, int64_t N, int E,
+                              int K, int64_t* __restrict__ idx_out, __nv_bfloat16* __restrict__ w_out,
+                              float* __restrict__ ws) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t t = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); t < N; t += warps) {
+        float l = 0.f;
+        if (lane < E) {
+            if (BF16)
+                l = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits_v)[t * E + lane]);
+            else
+                l = reinterpret_cast<const float*>(logits_v)[t * E + lane];
+        }
+        const float mean = warp_sum(l) / (float)E;
+        const float c = l - mean;
+        const float s = sigmoidf_(c);
+        float b = (lane < E) ? s + bias[lane] : -INFINITY;
+        float sel_s[8];
+        int sel_i[8];
+        for (int k = 0; k < K; ++k) {
+            ArgMax a{b, lane < E ? lane : 1 << 30};
+            a = warp_argmax(a);
+            sel_i[k] = a.i;
+            sel_s[k] = __shfl_sync(0xffffffffu, s, a.i & 31);
+            if (lane == a.i) b = -INFINITY;
+        }
+        float sum = 0.f;
+        for (int k = 0; k < K; ++k) sum += sel_s[k];
+        sum += 1e-6f;
+        if (lane < K) {
+            float my_s = 0.f;
+            int my_i = 0;
+            for (int k = 0; k < K; ++k)
+                if (k == lane) { my_s = sel_s[k]; my_i = sel_i[k]; }
+            idx_out[t * K + lane] = my_i;
+            w_out[t * K + lane] = __float2bfloat16(my_s / sum);
+        }
+        // centred-logit logsumexp for the z-loss, sigmoid scores for probs_mean
+        const float mx = warp_max(lane < E ? c : -INFINITY);
+        const float se = warp_sum(lane < E ? expf(c - mx) : 0.f);
+        if (lane == 0) {
+            const float lse = mx + logf(fmaxf(se, 1e-20f));
+            ws[t] = lse * lse;
+        }
+        if (lane < E) ws[N + t * E + lane] = s;
+    }
+}
+
+// Deterministic column means over the per-token workspace (fixed summation order).
+__global__ void k_router_means(const float* __restrict__ ws, int64_t N, int E, float zw, float* __restrict__ z_loss,
+                               float* __restrict__ probs_mean) {
+    __shared__ float red[32];
+    for (int col = -1; col < E; ++col) {
+        float acc = 0.f;
+        for (int64_t t = threadIdx.x; t < N; t += blockDim.x) acc += (col < 0) ? ws[t] : ws[N + t * E + col];
+        acc = block_sum(acc, red);
+        if (threadIdx.x == 0) {
+            if (col < 0) {
+                if (z_loss) z_loss[0] = (zw > 0.f && N > 0) ? zw * acc / (float)N : 0.f;
+            } else if (probs_mean) {
+                probs_mean[col] = N > 0 ? acc / (float)N : 0.f;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- qk rmsnorm + rope
+__global__ void k_qk_rmsnorm_rope(const __nv_bfloat16* __restrict__ x, int64_t sB, int64_t sH, int64_t sT,
+                                  int64_t n_vec, int n_heads, int64_t T, const float* __restrict__ w,
+                                  const float* __restrict__ cs, const float* __restrict__ sn, float eps,
+                                  __nv_bfloat16* __restrict__ y, float* __restrict__ rs) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t v = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); v < n_vec; v += warps) {
+        const int64_t t = v % T;
+        const int h = (int)((v / T) % n_heads);
+        const int64_t b = v / (T * n_heads);
+        const __nv_bfloat16* xv = x + b * sB + (int64_t)h * sH + t * sT;
+        const float x1 = __bfloat162float(xv[lane]);
+        const float x2 = __bfloat162float(xv[lane + 32]);
+        const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / 64.f + eps);
+        if (lane == 0 && rs) rs[v] = inv;
+        const float q1 = w[h * 64 + lane] * (x1 * inv);
+        const float q2 = w[h * 64 + lane + 32] * (x2 * inv);
+        const float c = cs[t * 32 + lane], s = sn[t * 32 + lane];
+        y[v * 64 + lane] = __float2bfloat16(q1 * c - q2 * s);
+        y[v * 64 + lane + 32] = __float2bfloat16(q2 * c + q1 * s);
+    }
+}
+
+// ---------------------------------------------------------------- attention gate
+__global__ void k_attn_gate(const __nv_bfloat16* __restrict__ attn, const float* __restrict__ gl, int64_t B, int H,
+                            int64_t T, __nv_bfloat16* __restrict__ out) {
+    const int64_t n = B * T * H * 8;   // 8 chunks of 8 elements per head vector
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i & 7);
+        const int64_t bth = i >> 3;            // (b, t, h)
+        const int h = (int)(bth % H);
+        const int64_t bt = bth / H;
+        const int64_t t = bt % T, b = bt / T;
+        const float g = sigmoidf_(gl[bt * H + h]);
+        const uint4 v = *reinterpret_cast<const uint4*>(attn + (((b * H + h) * T + t) * 64 + c * 8));
+        float f[8];
+        bf16x8_to_f32(v, f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) f[k] *= g;
+        *reinterpret_cast<uint4*>(out + (bt * H + h) * 64 + c * 8) = f32_to_bf16x8(f);
+    }
+}
+
+// ---------------------------------------------------------------- causal conv k4
+__global__ void k_conv1d_k4(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, int64_t B, int64_t T,
+                            int64_t D, __nv_bfloat16* __restrict__ y) {
+    const int64_t n = B * T * D;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t d = i % D;
+        const int64_t t = (i / D) % T;
+        float acc = __bfloat162float(x[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (t >= k) acc += w[d * 4 + k] * __bfloat162float(x[i - k * D]);
+        y[i] = __float2bfloat16(acc);
+    }
+}
+
+// ---------------------------------------------------------------- moe combine / dispatch
+__global__ void k_moe_combine(const __nv_bfloat16* __restrict__ eo, const int64_t* __restrict__ idx,
+                              const __nv_bfloat16* __restrict__ tw, const int32_t* __restrict__ slot,
+                              const __nv_bfloat16* __restrict__ sh, int64_t N, int K, int64_t E, int64_t C, int64_t D,
+                              __nv_bfloat16* __restrict__ out) {
+    for (int64_t t = blockIdx.x; t < N; t += gridDim.x) {
+        for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+            float acc = sh ? __bfloat162float(sh[t * D + d]) : 0.f;
+            for (int k = 0; k < K; ++k) {
+                const int64_t e = idx[t * K + k];
+                const int s = slot[t * K + k];
+                if (s >= 0 && s < C && e >= 0 && e < E)
+                    acc += __bfloat162float(tw[t * K + k]) * __bfloat162float(eo[(e * C + s) * D + d]);
+            }
+            out[t * D + d] = __float2bfloat16(acc);
+        }
+    }
+}
+
+__global__ void k_moe_tail_zero(__nv_bfloat16* __restrict__ buf, const int64_t* __restrict__ counts, int64_t E,
+                                int64_t C, int64_t D) {
+    for (int64_t e = blockIdx.y; e < E; e += gridDim.y) {
+        int64_t c = counts[e];
+        const int64_t start = c < 0 ? 0 : (c > C ? C : c);
+        const int64_t n = (C - start) * D;
+        __nv_bfloat16* p = buf + (e * C + start) * D;
+        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+            p[i] = __float2bfloat16(0.f);
+    }
+}
+
+__global__ void k_moe_dispatch(const __nv_bfloat16* __restrict__ x, const int64_t* __restrict__ idx,
+                               const int32_t* __restrict__ slot, int64_t N, int K, int64_t E, int64_t C, int64_t D,
+                               __nv_bfloat16* __restrict__ ei) {
+    for (int64_t t = blockIdx.x; t < N; t += gridDim.x) {
+        for (int k = 0; k < K; ++k) {
+            const int64_t e = idx[t * K + k];
+            const int s = slot[t * K + k];
+            if (s < 0 || s >= C || e < 0 || e >= E) continue;
+            for (int64_t d = threadIdx.x; d < D; d += blockDim.x) ei[(e * C + s) * D + d] = x[t * D + d];
+        }
+    }
+}
+
+}  // namespace
+
+// ==================================================================================== C ABI
+
+extern "C" int pulsar_op_rmsnorm(const void* x, const float* w, int64_t rows, int64_t D, float eps, void* y,
+                                 float* rsqrt_out, void* stream) {
+    PULSAR_CHECK_ARG(rows >= 0 && D > 0, "rmsnorm: invalid shape rows=%lld D=%lld", (long long)rows, (long long)D);
+    if (rows == 0) return PULSAR_OK;
+    PULSAR_CHECK_ARG(x && w && y, "rmsnorm: null pointer");
+    k_rmsnorm_rows<<<grid_cap(rows, 1), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, rows, (int)D, eps,
+                                                              (__nv_bfloat16*)y, rsqrt_out);
+    PULSAR_LAUNCH_CHECK("k_rmsnorm_rows");
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_rope(const void* qk, const float* cs, const float* sn, int64_t rows, int64_t T, int64_t Dh,
+                              void* y, void* stream) {
+    PULSAR_CHECK_ARG(rows >= 0 && Dh > 0 && Dh % 2 == 0, "rope: head dim must be even, got %lld", (long long)Dh);
+    if (rows == 0) return PULSAR_OK;
+    PULSAR_CHECK_ARG(T > 0 && qk && cs && sn && y, "rope: invalid arguments (T=%lld)", (long long)T);
+    const int64_t n = rows * (Dh / 2);
+    k_rope<<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)qk, cs, sn, rows, T, (int)(Dh / 2),
+                                                    (__nv_bfloat16*)y);
+    PULSAR_LAUNCH_CHECK("k_rope");
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_swiglu(const void* gu, int64_t rows, int64_t d_ff, void* out, void* stream) {
+    PULSAR_CHECK_ARG(rows >= 0 && d_ff > 0, "swiglu: invalid shape");
+    if (rows == 0) return PULSAR_OK;
+    k_swiglu<<<grid_cap(rows * d_ff, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)gu, rows, d_ff,
+                                                                (__nv_bfloat16*)out);
+    PULSAR_LAUNCH_CHECK("k_swiglu");
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_moe_router_topk(const void* logits, int logits_bf16, const float* bias, int64_t N, int64_t E,
+                                         int64_t K, float zw, int64_t* idx, void* w, float* z_loss,
+                                         float* probs_mean, float* ws, void* stream) {
+    PULSAR_CHECK_ARG(E >= 1 && E <= 32, "moe_router_topk_forward_cuda supports E <= 32, got %lld", (long long)E);
+    PULSAR_CHECK_ARG(K > 0 && K <= 8 && K <= E, "top_k must be in [1, min(8, E)], got %lld", (long long)K);
+    PULSAR_CHECK_ARG(N >= 0, "moe_router_topk: N must be >= 0");
+    if (N > 0) {
+        PULSAR_CHECK_ARG(logits && bias && idx && w && ws, "moe_router_topk: null pointer");
+        const int threads = 256;
+        const int grid = grid_cap(N, threads / 32);
+        if (logits_bf16)
+            k_router_topk<true><<<grid, threads, 0, S(stream)>>>(logits, bias, N, (int)E, (int)K, idx,
+                                                                 (__nv_bfloat16*)w, ws);
+        else
+            k_router_topk<false><<<grid, threads, 0, S(stream)>>>(logits, bias, N, (int)E, (int)K, idx,
+                                                                  (__nv_bfloat16*)w, ws);
+        PULSAR_LAUNCH_CHECK("k_router_topk");
+    }
+    if (z_loss || probs_mean) {
+        k_router_means<<<1, 256, 0, S(stream)>>>(ws, N, (int)E, zw, z_loss, probs_mean);
+        PULSAR_LAUNCH_CHECK("k_router_means");
+    }
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_qk_rmsnorm_rope(const void* x, int64_t sB, int64_t sH, int64_t sT, int64_t n_vec,
+                                         int64_t n_heads, int64_t T, const float* w, const float* cs, const float* sn,
+                                         float eps, void* y, float* rs, void* stream) {
+    PULSAR_CHECK_ARG(n_vec >= 0 && n_heads > 0, "qk_rmsnorm_rope: invalid shape");
+    if (n_vec == 0) return PULSAR_OK;
+    PULSAR_CHECK_ARG(T > 0 && x && w && cs && sn && y, "qk_rmsnorm_rope: invalid arguments");
+    k_qk_rmsnorm_rope<<<grid_cap(n_vec, 8), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, sB, sH, sT, n_vec,
+                                                                  (int)n_heads, T, w, cs, sn, eps,
+                                                                  (__nv_bfloat16*)y, rs);
+    PULSAR_LAUNCH_CHECK("k_qk_rmsnorm_rope");
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_attn_gate(const void* attn, const float* gl, int64_t B, int64_t H, int64_t T, void* out,
+                                   void* stream) {
+    PULSAR_CHECK_ARG(B >= 0 && H >= 0 && T >= 0, "fused_attn_gate: invalid shape");
+    const int64_t n = B * T * H * 8;
+    if (n == 0) return PULSAR_OK;
+    k_attn_gate<<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)attn, gl, B, (int)H, T,
+                                                          (__nv_bfloat16*)out);
+    PULSAR_LAUNCH_CHECK("k_attn_gate");
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_conv1d_k4(const void* x, const float* w, int64_t B, int64_t T, int64_t D, void* y,
+                                   void* stream) {
+    PULSAR_CHECK_ARG(B >= 0 && T >= 0 && D > 0, "causal_depthwise_conv1d_k4: invalid shape");
+    const int64_t n = B * T * D;
+    if (n == 0) return PULSAR_OK;
+    k_conv1d_k4<<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, B, T, D, (__nv_bfloat16*)y);
+    PULSAR_LAUNCH_CHECK("k_conv1d_k4");
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_moe_combine(const void* eo, const int64_t* idx, const void* tw, const int32_t* slot,
+                                     const void* sh, int64_t N, int64_t K, int64_t E, int64_t C, int64_t D, void* out,
+                                     void* stream) {
+    PULSAR_CHECK_ARG(N >= 0 && K >= 0 && E > 0 && C >= 0 && D > 0, "moe_combine: invalid shape");
+    if (N == 0) return PULSAR_OK;
+    k_moe_combine<<<grid_cap(N, 1), 128, 0, S(stream)>>>((const __nv_bfloat16*)eo, idx, (const __nv_bfloat16*)tw,
+                                                          slot, (const __nv_bfloat16*)sh, N, (int)K, E, C, D,
+                                                          (__nv_bfloat16*)out);
+    PULSAR_LAUNCH_CHECK("k_moe_combine");
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_op_moe_dispatch(const void* x, const int64_t* idx, const int32_t* slot, const int64_t* counts,
+                                      int64_t N, int64_t K, int64_t E, int64_t C, int64_t D, void* ei, void* stream) {
+    PULSAR_CHECK_ARG(N >= 0 && K >= 0 && E > 0 && C >= 0 && D > 0, "moe_dispatch: invalid shape");
+    PULSAR_CHECK_ARG(D % 8 == 0, "D must be a multiple of 8 for vectorised dispatch, got %lld", (long long)D);
+    if (E * C * D > 0) {
+        if (counts) {
+            dim3 grid(64, (unsigned)(E < 65535 ? E : 65535));
+            k_moe_tail_zero<<<grid, 256, 0, S(stream)>>>((__nv_bfloat16*)ei, counts, E, C, D);
+            PULSAR_LAUNCH_CHECK("k_moe_tail_zero");
+        } else {
+            PULSAR_TRY(cuda_status(cudaMemsetAsync(ei, 0, (size_t)(E * C * D) * 2, S(stream)), "moe_dispatch memset"));
+        }
+    }
+    if (N > 0 && K > 0) {
+        k_moe_dispatch<<<grid_cap(N, 1), 128, 0, S(stream)>>>((const __nv_bfloat16*)x, idx, slot, N, (int)K, E, C, D,
+                                                               (__nv_bfloat16*)ei);
+        PULSAR_LAUNCH_CHECK("k_moe_dispatch");
+    }
+    return PULSAR_OK;
+}

@@ -84,7 +84,7 @@ def run_case(name, cfg_dict, recipe, seed, prompt_len, n_new, n_pulse_steps, out
     assert all(k.startswith("rope_") for k in missing) or not missing, missing
     eng = PulsarInferenceEngine(model, device="cpu", dtype=torch.float32)
     ids = random_prompts(1, prompt_len, cfg.vocab_size, seed=seed)[0].tolist()
-    probe_idx = torch.randperm(cfg.vocab_size, generator=torch.Generator().manual_seed(7))[:N_PROBE]
+    probe_idx = torch.randperm(cfg.vocab_size, generator=torch.Generator().manual_seed(7))[:N_PROBE].clone()
     rec = {"name": name, "cfg": cfg_dict, "recipe": recipe, "seed": seed, "b_std": b_std, "prompt": ids,
            "n_new": n_new, "probe_idx": probe_idx}
 

@@ -1,0 +1,206 @@
+"""Parity of the sm_100a decode engine with the CPU oracle (the restatement of src/infer.py
+pinned to the reference by tests/test_oracle_golden.py), through the C ABI.
+
+Tolerances (written per test):
+  * per-step logits: max |engine - oracle| <= 2e-2 (bf16 weights/KV vs fp32 CPU). Recipe A
+    (the reference init) is checked with both KV dtypes. Recipe B amplifies perturbations
+    about 100x (a 1e-6 relative weight change moves logits by 1e-4), so there the bf16 KV
+    cache alone drifts 3e-2 - 6e-2; recipe B is checked with the fp32-KV parity mode.
+  * greedy tokens: identical wherever the oracle's top-1 margin exceeds 2e-2; the first
+    decision below that margin ends the comparison (tie tolerance).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import pulsar_oracle as O
+from pulsar_b200.config import PulsarConfig
+from pulsar_b200.weights import make_state_dict, random_prompts
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+_CACHE = {}
+
+
+def _setup(recipe, kv_dtype, max_seq_len=2048, max_prefill=1280, max_batch=4):
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA not available")
+    from pulsar_b200.engine import DeviceEngine
+    key = (recipe, kv_dtype, max_seq_len, max_prefill, max_batch)
+    if key not in _CACHE:
+        for k in list(_CACHE):
+            _CACHE.pop(k)[0].close()
+        cfg = PulsarConfig(eos_token_id=-1)
+        sd = make_state_dict(cfg, recipe=recipe, seed=0)
+        eng = DeviceEngine(cfg, sd, device=0, max_batch=max_batch, max_seq_len=max_seq_len, max_prefill=max_prefill,
+                           kv_dtype=kv_dtype)
+        _CACHE[key] = (eng, O.OracleModel(sd, cfg), cfg)
+    return _CACHE[key]
+
+
+def _margin(lg):
+    v = lg.topk(2).values
+    return float(v[0] - v[1])
+
+
+@pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("A", torch.float32), ("B", torch.float32)])
+def test_prefill_and_pulse_logits_match_oracle(recipe, kv):
+    eng, m, cfg = _setup(recipe, kv)
+    ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
+    okv = O.OracleKV(m, 256)
+    ref = O.prefill(m, ids, okv)
+    got = eng.prefill(0, ids).cpu()
+    assert (got - ref).abs().max().item() <= TOL, "prefill logits"
+    tok, pos = int(ref.argmax()), len(ids)
+    for step in range(4):
+        h = h0 = hr = h0r = None
+        for p in range(3):
+            lg, h, h0 = eng.pulse(p, [(0, pos, tok)], h, h0)
+            lr, hr, h0r = O.pulse_pass(m, p, [tok], [pos], okv, hr, h0r)
+            err = (lg.cpu() - lr).abs().max().item()
+            assert err <= TOL, f"step {step} pulse {p}: max |logit err| = {err:.3e}"
+        eng.set_length(0, pos + 1)
+        okv.length = pos + 1
+        tok, pos = int(lr[0].argmax()), pos + 1
+
+
+def test_long_prompt_local_quirk_and_yarn():
+    """T = 1100 > 1024: the local layers' truncated top-left prefill mask, no YaRN in
+    prefill, YaRN on global layers at decode (pos + 1 > 1024)."""
+    eng, m, cfg = _setup("B", torch.float32)
+    ids = random_prompts(1, 1100, cfg.vocab_size, seed=5)[0].tolist()
+    okv = O.OracleKV(m, 1200)
+    ref = O.prefill(m, ids, okv)
+    got = eng.prefill(1, ids).cpu()
+    assert (got - ref).abs().max().item() <= TOL
+    tok, pos = int(ref.argmax()), len(ids)
+    for _ in range(2):
+        h = h0 = hr = h0r = None
+        for p in range(3):
+            lg, h, h0 = eng.pulse(p, [(1, pos, tok)], h, h0)
+            lr, hr, h0r = O.pulse_pass(m, p, [tok], [pos], okv, hr, h0r)
+            assert (lg.cpu() - lr).abs().max().item() <= TOL
+        eng.set_length(1, pos + 1)
+        okv.length = pos + 1
+        tok, pos = int(lr[0].argmax()), pos + 1
+
+
+def test_rollback_is_exact():
+    """Length reset (rollback) then recomputation reproduces the logits bit for bit."""
+    eng, m, cfg = _setup("B", torch.float32)
+    ids = random_prompts(1, 64, cfg.vocab_size, seed=9)[0].tolist()
+    eng.prefill(2, ids)
+    toks = [5, 77, 901, 4242]
+    first = []
+    for i, t in enumerate(toks):
+        lg, h, h0 = eng.pulse(0, [(2, 64 + i, t)])
+        first.append(lg)
+    eng.set_length(2, 64)
+    for i, t in enumerate(toks):
+        lg, _, _ = eng.pulse(0, [(2, 64 + i, 999 + i)])  # overwrite with other tokens
+    for i, t in enumerate(toks):
+        lg, _, _ = eng.pulse(0, [(2, 64 + i, t)])
+        assert torch.equal(lg, first[i])
+
+
+def test_rows_of_different_slots_are_independent():
+    eng, m, cfg = _setup("B", torch.float32)
+    a = random_prompts(1, 40, cfg.vocab_size, seed=1)[0].tolist()
+    b = random_prompts(1, 70, cfg.vocab_size, seed=2)[0].tolist()
+    eng.prefill(0, a)
+    eng.prefill(3, b)
+    l2, h2, z2 = eng.pulse(0, [(0, 40, 11), (3, 70, 22)])
+    la, ha, za = eng.pulse(0, [(0, 40, 11)])
+    lb, hb, zb = eng.pulse(0, [(3, 70, 22)])
+    assert torch.equal(l2[0], la[0]) and torch.equal(l2[1], lb[0])
+    assert torch.equal(h2[1], hb[0])
+
+
+def _compare_tokens(got, ref, margins, what):
+    for i, (g, r) in enumerate(zip(got, ref)):
+        if g != r:
+            assert margins[i] <= TOL, f"{what}: token {i} differs ({g} vs {r}) with oracle margin {margins[i]:.3e}"
+            return i
+    return len(ref)
+
+
+@pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("B", torch.float32)])
+def test_greedy_generate_matches_oracle_stream(recipe, kv):
+    """generate_greedy(gamma=0) == reference stream_generate (greedy, penalty 1.0)."""
+    eng, m, cfg = _setup(recipe, kv)
+    ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
+    n = 48
+    trace = []
+    ref = O.stream_generate_ids(m, ids, n, trace=trace)
+    margins = [_margin(lg) for _, lg in trace]
+    first = eng.prefill(0, ids)
+    got, _ = eng.generate_greedy([0], first.view(1, -1), n, gamma=0)
+    _compare_tokens(got[0].tolist(), ref, margins, f"greedy {recipe}")
+
+
+@pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("B", torch.float32)])
+def test_spec_gamma4_matches_oracle_block_verify(recipe, kv):
+    """gamma = 4 drafting + one batched verify per round == the oracle's block-verify loop."""
+    eng, m, cfg = _setup(recipe, kv)
+    ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
+    n = 40
+    trace = []
+    st = O.SpecStats()
+    ref = O.block_spec_generate_ids(m, ids, n, gamma=4, stats=st, trace=trace)
+    # margins per emitted token: the decision that produced it (draft accept or verify argmax)
+    first = eng.prefill(0, ids)
+    got, stats = eng.generate_greedy([0], first.view(1, -1), n, gamma=4)
+    got = got[0].tolist()
+    if got != ref:
+        # locate the round of the first difference and require a near-tie there
+        k = next(i for i, (a, b) in enumerate(zip(got, ref)) if a != b)
+        lows = [min(_margin(P[j]) for j in range(P.shape[0])) for (_, _, _, P) in trace]
+        assert min(lows) <= TOL, f"spec tokens differ at {k} without a near-tie in the oracle"
+    if recipe == "A":
+        assert stats["accepted"] == stats["drafted"], "copy regime: every draft is accepted"
+
+
+def test_batch_generate_matches_single():
+    eng, m, cfg = _setup("B", torch.float32)
+    P = random_prompts(2, 48, cfg.vocab_size, seed=4)
+    f0 = eng.prefill(0, P[0].tolist())
+    f1 = eng.prefill(1, P[1].tolist())
+    both, _ = eng.generate_greedy([0, 1], torch.stack([f0, f1]), 16, gamma=2)
+    eng.prefill(0, P[0].tolist())
+    one, _ = eng.generate_greedy([0], f0.view(1, -1), 16, gamma=2)
+    assert both[0].tolist() == one[0].tolist()
+
+
+def test_reference_api_generate(gpu):
+    """PulsarInferenceEngine.generate (src/infer.py:733-782) on both loops."""
+    from pulsar_b200.engine import PulsarInferenceEngine
+    cfg = PulsarConfig(eos_token_id=-1)
+    sd = make_state_dict(cfg, recipe="A", seed=0)
+    ids = random_prompts(1, 32, cfg.vocab_size, seed=0)[0].tolist()
+
+    class Tok:
+        unk_token_id = None
+
+        def encode(self, prompt, return_tensors="pt"):
+            return torch.tensor([ids])
+
+        def decode(self, t, skip_special_tokens=False):
+            return f"{t[0]},"
+
+        def convert_tokens_to_ids(self, s):
+            return None
+
+    for k in list(_CACHE):
+        _CACHE.pop(k)[0].close()
+    eng = PulsarInferenceEngine((sd, cfg), device="cuda", max_batch=2, max_seq_len=256)
+    m = O.OracleModel(sd, cfg)
+    for spec, fn in ((False, O.stream_generate_ids), (True, O.self_speculative_ids)):
+        txt = eng.generate(Tok(), "", max_new_tokens=12, temperature=0.0, repetition_penalty=1.0, speculative=spec)
+        got = [int(x) for x in txt.split(",") if x]
+        assert got == fn(m, ids, 12)
+    out = eng.generate_batch(torch.tensor([ids]), 12, gamma=3)
+    assert out.shape == (1, 44)
+    assert out[0, 32:].tolist() == O.stream_generate_ids(m, ids, 12)
+    eng.dev.close()

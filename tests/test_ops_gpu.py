@@ -1,0 +1,198 @@
+"""The pulsar_cuda drop-in ops on the B200 against plain fp32 torch references, mirroring
+the reference's own kernel tests (tests/test_kernels.py of the reference: RMSNorm :40-69,
+RoPE :129-186, SwiGLU :189-211, router :271-328, dispatch/combine :373-408, QK-norm+RoPE
+:494-530, attention gate :533-561, canon conv :808-835) with their tolerances."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def pc():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA not available")
+    import pulsar_cuda
+    return pulsar_cuda
+
+
+def _bf16(*shape, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(device="cuda", dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("D", [64, 1000, 1024, 4096])
+def test_rmsnorm(pc, D):
+    x = _bf16(3, 17, D, seed=1)
+    w = torch.randn(D, device="cuda") * 0.1 + 1
+    y, rs = pc.rmsnorm_forward(x, w, 1e-6)
+    xf = x.float()
+    ref = (w * xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16()
+    assert_close(y, ref, atol=2e-2, msg="rmsnorm")
+    assert rs.shape == (51,)
+    assert_close(rs, torch.rsqrt(xf.pow(2).mean(-1) + 1e-6).reshape(-1), atol=1e-4, msg="rsqrt")
+    e, r = pc.rmsnorm_forward(torch.empty(0, D, device="cuda", dtype=torch.bfloat16), w, 1e-6)
+    assert e.numel() == 0 and r.numel() == 0
+
+
+def _ref_rope(x, cos, sin):
+    d = x.shape[-1] // 2
+    xf = x.float()
+    x1, x2 = xf[..., :d], xf[..., d:]
+    c, s = cos.float(), sin.float()
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1).to(x.dtype)
+
+
+def _tables(T, D, theta=10000.0):
+    inv = 1.0 / (theta ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    f = torch.outer(torch.arange(T, device="cuda").float(), inv)
+    return f.cos(), f.sin()
+
+
+def test_rope(pc):
+    B, Hh, T, D = 2, 4, 32, 64
+    x = _bf16(B, Hh, T, D, seed=7)
+    cos, sin = _tables(T, D)
+    assert_close(pc.rope_forward(x, cos, sin), _ref_rope(x, cos, sin), atol=2e-2, msg="rope")
+
+
+def test_rope_empty_and_long(pc):
+    assert pc.rope_forward(torch.empty(1, 1, 0, 64, device="cuda", dtype=torch.bfloat16),
+                           torch.empty(0, 32, device="cuda"), torch.empty(0, 32, device="cuda")).numel() == 0
+    T = 66000
+    q = torch.randn(1, 1, T, 64, device="cuda", dtype=torch.bfloat16)
+    out = pc.rope_forward(q, torch.ones(T, 32, device="cuda"), torch.zeros(T, 32, device="cuda"))
+    assert out.shape == q.shape and torch.isfinite(out).all()
+    assert torch.equal(out, q)
+
+
+def test_swiglu(pc):
+    gu = _bf16(4, 16, 256, seed=8)
+    out = pc.fused_swiglu_forward(gu, 128)
+    ref = (F.silu(gu[..., :128].float()) * gu[..., 128:].float()).bfloat16()
+    assert_close(out, ref, atol=2e-2, msg="swiglu")
+
+
+@pytest.mark.parametrize("E,K", [(8, 2), (16, 4), (32, 8), (5, 3)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_router_topk(pc, E, K, dtype):
+    N = 64
+    logits = _bf16(N, E, seed=13).to(dtype)
+    bias = torch.randn(E, device="cuda") * 0.1
+    idx, w, z, pm = pc.moe_router_topk_forward(logits, bias, K, 1e-4)
+    c = logits.float() - logits.float().mean(-1, keepdim=True)
+    s = torch.sigmoid(c)
+    idx_ref = torch.topk(s + bias, k=K, dim=-1).indices
+    assert torch.equal(idx, idx_ref), "top-k indices must match exactly"
+    raw = torch.gather(s, -1, idx_ref)
+    assert_close(w, raw / (raw.sum(-1, keepdim=True) + 1e-6), atol=2e-3, msg="weights")
+    assert_close(pm, s.mean(0), atol=2e-3, msg="probs_mean")
+    zr = 1e-4 * torch.logsumexp(c, -1).pow(2).mean()
+    assert_close(z, zr, atol=1e-6, rtol=1e-3, msg="z_loss")
+
+
+def test_router_topk_default_overload(pc):
+    logits = _bf16(8, 8, seed=3).float()
+    idx, w, z, pm = pc.moe_router_topk_forward(logits, torch.zeros(8, device="cuda"), 1e-4)
+    assert idx.shape == (8, 2)
+
+
+def test_router_topk_errors(pc):
+    with pytest.raises(RuntimeError, match="E <= 32"):
+        pc.moe_router_topk_forward(torch.randn(4, 33, device="cuda"), torch.zeros(33, device="cuda"), 2)
+
+
+def test_qk_rmsnorm_rope(pc):
+    B, Hh, T, D = 2, 4, 16, 64
+    x = _bf16(B, Hh, T, D, seed=42)
+    w = torch.randn(Hh, D, device="cuda")
+    cos, sin = _tables(T, D)
+    y, rs = pc.qk_rmsnorm_rope_forward(x, w, cos, sin, T, 1e-6)
+    xf = x.float()
+    n = (w.view(1, Hh, 1, D) * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6))).bfloat16()
+    assert_close(y, _ref_rope(n, cos, sin), atol=3.5e-2, msg="qk_rmsnorm_rope")
+
+
+def test_qk_rmsnorm_rope_strided(pc):
+    """A [B, T, H, 64] view transposed to [B, H, T, 64] (stride(-1) == 1)."""
+    B, T, Hh, D = 2, 8, 4, 64
+    base = _bf16(B, T, Hh, D, seed=5)
+    x = base.transpose(1, 2)
+    w = torch.rand(Hh, D, device="cuda") + 0.5
+    cos, sin = _tables(T, D)
+    y, _ = pc.qk_rmsnorm_rope_forward(x, w, cos, sin, T)
+    y2, _ = pc.qk_rmsnorm_rope_forward(x.contiguous(), w, cos, sin, T)
+    assert torch.equal(y, y2)
+    with pytest.raises(RuntimeError, match="head_dim == 64"):
+        pc.qk_rmsnorm_rope_forward(_bf16(1, 1, 4, 32), torch.ones(1, 32, device="cuda"), cos, sin, 4)
+
+
+def test_attn_gate(pc):
+    B, Hh, T, D = 2, 4, 16, 64
+    a = _bf16(B, Hh, T, D, seed=101)
+    g = torch.randn(B, T, Hh, device="cuda")
+    ref = (a.float().transpose(1, 2) * torch.sigmoid(g).unsqueeze(-1)).reshape(B, T, -1)
+    assert_close(pc.fused_attn_gate_forward(a, g), ref, atol=2e-3, msg="attn gate")
+
+
+def test_conv1d_k4(pc):
+    B, T, D = 4, 32, 1024
+    torch.manual_seed(42)
+    x = torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(D, 4, device="cuda")
+    xp = F.pad(x.float().transpose(1, 2), (3, 0))
+    y_ref = (x.float() + F.conv1d(xp, w.unsqueeze(1).flip(-1), groups=D).transpose(1, 2)).bfloat16()
+    assert_close(pc.causal_depthwise_conv1d_k4_forward(x, w), y_ref, atol=2e-2, msg="conv")
+
+
+def test_dispatch_and_combine(pc):
+    N, D, E, K, Cap = 16, 32, 4, 2, 32
+    torch.manual_seed(3)
+    x = _bf16(N, D, seed=15)
+    idx = torch.randint(0, E, (N, K), device="cuda")
+    tw = torch.rand(N, K, device="cuda")
+    tw = (tw / tw.sum(-1, keepdim=True)).bfloat16()
+    slots = torch.full((N, K), -1, dtype=torch.int32, device="cuda")
+    fill = [0] * E
+    for t in range(N):
+        for k in range(K):
+            e = int(idx[t, k])
+            slots[t, k] = fill[e]
+            fill[e] += 1
+    slots[3, 1] = -1                       # a dropped assignment
+    (ei,) = pc.moe_dispatch_forward(x, idx, slots, E, Cap)
+    for t in range(N):
+        for k in range(K):
+            s = int(slots[t, k])
+            if s >= 0:
+                assert torch.equal(ei[int(idx[t, k]), s], x[t])
+    eo = _bf16(E, Cap, D, seed=18)
+    sh = _bf16(N, D, seed=19)
+    out = pc.moe_combine_forward(eo, idx, tw, slots, sh)
+    ref = sh.float().clone()
+    for t in range(N):
+        for k in range(K):
+            s = int(slots[t, k])
+            if s >= 0:
+                ref[t] += eo[int(idx[t, k]), s].float() * tw[t, k].float()
+    assert_close(out, ref, atol=3e-2, msg="combine")
+    counts = torch.tensor(fill, dtype=torch.int64, device="cuda")
+    (ei2,) = pc.moe_dispatch_forward(x, idx, slots, E, Cap, counts)
+    for e in range(E):
+        assert (ei2[e, fill[e]:] == 0).all()
+
+
+def test_reference_model_uses_shim(pc):
+    """src/model.py's wrappers call these names unguarded; the shim must expose them."""
+    for name in ("rmsnorm_forward", "rope_forward", "fused_swiglu_forward", "moe_router_topk_forward",
+                 "qk_rmsnorm_rope_forward", "fused_attn_gate_forward", "causal_depthwise_conv1d_k4_forward",
+                 "moe_combine_forward", "moe_dispatch_forward"):
+        assert callable(getattr(pc, name))
+    with pytest.raises(NotImplementedError):
+        pc.rmsnorm_backward(None, None, None, None)
