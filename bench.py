@@ -1,0 +1,322 @@
+#!/usr/bin/env python3
+"""Decode benchmark of the pulsar_b200 engine (the BASELINE.json metric on its config 2).
+
+Workload (N = 1): Pulsar-283M, random-init weights (recipe A = the reference init, seed 0),
+batch 1, a 2048-token uniform-random prompt, 512 new tokens, greedy self-speculative decode
+with gamma = 4 (drafts from the pulse-1 exit, one batched pulse-2/3 verify per round).
+A step = decoding the 512 new tokens from the prefilled prompt (the KV cache is rolled back
+to the prompt between steps). value = new tokens / device time. The weights (~0.57 GB bf16)
+are larger than the 126 MB L2, so no flush is needed between steps.
+
+N > 1 (torchrun): independent replicas, one per GPU (seed + rank prompts), no collective on
+the token path; time = max over ranks (CUDA events), value = all ranks' tokens / time.
+
+--impl reference: the reference algorithm's CPU implementation (the oracle port of
+src/infer.py, fp32 torch on the host cores), greedy decode_step loop on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "pulsar-300m_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "decode tokens/sec/GPU (B=1 latency, B=256 throughput); accept rate; % HBM roof"
+PROMPT, NEW, GAMMA = 2048, 512, 4
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def bytes_per_pass(cfg, d_routed: float, kv_keys: int, rows: int, with_lm_head: bool) -> float:
+    """Algorithmic bytes of one pulse pass (the per-unit figure of the roofline): bf16
+    weights read once (wqkv, wo, shared expert, d_routed distinct routed experts per
+    layer), fp32 small tensors, KV keys read once per (layer, sequence) and written per
+    row, LM head once, embedding gathers."""
+    D = cfg.d_model
+    attn = (cfg.qkv_dim * D + D * D) * 2
+    shared = (2 * cfg.d_shared * D + D * cfg.d_shared) * 2
+    routed = (2 * cfg.d_expert * D + cfg.d_expert * D) * 2
+    small = (16 * D + 16 * D + 4 * D) * 4       # gate, router, norms/scales (fp32)
+    per_layer = attn + shared + small + routed * d_routed
+    kv = kv_keys * 1024 + rows * 8 * 1024        # bf16 K+V: 4 heads x 64 x 2 x 2 B per key per layer
+    lm = cfg.vocab_size * D * 2 if with_lm_head else 0
+    return cfg.n_core * per_layer + kv + lm + rows * D * 2
+
+
+def kv_keys_for(L: int) -> int:
+    return 6 * min(L, 1024) + 2 * L
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.f.name):
+            c = [x.strip() for x in line.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                sm.append(float(c[1]))
+                mx = float(c[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, c[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, local: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_oracle_rate(n_tokens: int, prompt_len: int, seed: int = 0):
+    """Greedy decode_step loop of the oracle port (src/infer.py:526-621 restated) on the host
+    cores: prefill untimed, then n_tokens decode steps timed. Returns (tok/s, threads, sample)."""
+    from oracle import pulsar_oracle as O
+    from pulsar_b200.config import PulsarConfig
+    from pulsar_b200.weights import make_state_dict, random_prompts
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = PulsarConfig(eos_token_id=-1)
+    sd = make_state_dict(cfg, recipe="A", seed=0)
+    m = O.OracleModel(sd, cfg)
+    ids = random_prompts(1, prompt_len, cfg.vocab_size, seed=seed)[0].tolist()
+    kv = O.OracleKV(m, prompt_len + n_tokens + 8)
+    lg = O.prefill(m, ids, kv)
+    tok, pos = int(lg.argmax()), prompt_len
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        lg = O.decode_step(m, tok, pos, kv)
+        tok, pos = int(lg.argmax()), pos + 1
+    dt = time.perf_counter() - t0
+    sample = (f"oracle port (fp32 torch, {threads} threads): prefill {prompt_len} untimed, then {n_tokens} greedy "
+              f"decode_step tokens at context {prompt_len}..{prompt_len + n_tokens}")
+    return n_tokens / dt, threads, sample
+
+
+def run_reference(args):
+    world, rank, local = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    if rank != 0:
+        return
+    per_step = 4
+    from oracle import pulsar_oracle as O
+    from pulsar_b200.config import PulsarConfig
+    from pulsar_b200.weights import make_state_dict, random_prompts
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = PulsarConfig(eos_token_id=-1)
+    sd = make_state_dict(cfg, recipe="A", seed=0)
+    m = O.OracleModel(sd, cfg)
+    ids = random_prompts(1, PROMPT, cfg.vocab_size, seed=0)[0].tolist()
+    kv = O.OracleKV(m, PROMPT + (args.steps + args.warmup) * per_step + 8)
+    lg = O.prefill(m, ids, kv)
+    tok, pos = int(lg.argmax()), PROMPT
+    times = []
+    for s in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        for _ in range(per_step):
+            lg = O.decode_step(m, tok, pos, kv)
+            tok, pos = int(lg.argmax()), pos + 1
+        if s >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    value = per_step * args.steps / tot
+    sample = (f"oracle port of src/infer.py (fp32 torch, {threads} threads), B=1 prompt {PROMPT}: each step = "
+              f"{per_step} greedy decode_step tokens (prefill untimed)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"pulsar-283M decode B=1 prompt {PROMPT}, greedy (reference loop)",
+                       "prompt": PROMPT, "new_tokens_per_step": per_step},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_engine(args):
+    world, rank, local = dist_setup()
+    from pulsar_b200.config import PulsarConfig
+    from pulsar_b200.engine import DeviceEngine
+    from pulsar_b200.weights import make_state_dict, random_prompts
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = PulsarConfig(eos_token_id=-1)
+    sd = make_state_dict(cfg, recipe=args.recipe, seed=0)
+    eng = DeviceEngine(cfg, sd, device=local, max_batch=1, max_seq_len=PROMPT + NEW + 64, max_prefill=PROMPT,
+                       kv_dtype=torch.bfloat16)
+    del sd
+    ids = random_prompts(1, PROMPT, cfg.vocab_size, seed=rank)[0]
+    first = eng.prefill(0, ids.tolist())
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        eng.set_length(0, PROMPT)
+        return eng.generate_greedy([0], first.view(1, -1), NEW, gamma=args.gamma)
+
+    for _ in range(args.warmup):
+        out, st = step()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = Clocks(local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stats = {"rounds": 0, "drafted": 0, "accepted": 0}
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        out, st = step()
+        for k in stats:
+            stats[k] += st[k]
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, world, local)
+    tokens = NEW * args.steps * world
+    value = tokens / (ms_max / 1e3)
+    # ---- end-to-end through the C ABI with host buffers (prompt H2D, prefill, decode, tokens D2H)
+    pinned_ids = ids.to(torch.int32).pin_memory()
+    host_out = torch.empty(NEW, dtype=torch.int32).pin_memory()
+    e2e_ms = []
+    for s in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        d_ids = pinned_ids.to(dev, non_blocking=True)
+        lg = eng.prefill(0, d_ids)
+        toks, _ = eng.generate_greedy([0], lg.view(1, -1), NEW, gamma=args.gamma)
+        host_out.copy_(toks[0], non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if s >= args.warmup:
+            e2e_ms.append(e0.elapsed_time(e1))
+    e2e_ms_max = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, local)
+    e2e_value = NEW * world / (e2e_ms_max / 1e3)
+    # ---- roofline of the decode path (bytes per emitted token from the measured accept rate)
+    peak, peak_kind = load_peaks()
+    rounds = max(1, stats["rounds"])
+    acc = stats["accepted"] / rounds
+    L = PROMPT + NEW // 2
+    g = args.gamma
+    d_draft = 4.0
+    d_verify = min(16.0, 4.0 * (g + 1)) if args.recipe == "B" else 4.0
+    if g > 0:
+        round_bytes = ((g + 1) * bytes_per_pass(cfg, d_draft, kv_keys_for(L), 1, False) + g * cfg.vocab_size * 2048
+                       + 2 * bytes_per_pass(cfg, d_verify, kv_keys_for(L), g + 1, True))
+        bytes_per_token = round_bytes / (acc + 1)
+    else:
+        bytes_per_token = 3 * bytes_per_pass(cfg, 4.0, kv_keys_for(L), 1, False) + cfg.vocab_size * 2048
+    achieved = bytes_per_token * value / world / 1e9
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"pulsar-283M decode, B=1 per GPU, prompt {PROMPT}, {NEW} new tokens, greedy "
+                                   f"gamma={g} self-speculative, recipe {args.recipe} weights",
+                       "batch_per_gpu": 1, "prompt": PROMPT, "new_tokens": NEW, "gamma": g,
+                       "l2": "no flush: weights (~0.57 GB) exceed the 126 MB L2", "kv_dtype": "bf16",
+                       "parallelism": f"{world} independent replicas"},
+            "accept_rate": stats["accepted"] / max(1, stats["drafted"]),
+            "tokens_per_round": acc + 1 if g > 0 else 1.0,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
+                    "d2h_bytes_per_step": NEW * 4, "includes": "prompt H2D, prefill, decode, tokens D2H"},
+            "roofline": {"bound": "hbm", "scope": "whole decode path (all kernels of a round)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "bytes_per_token": bytes_per_token},
+            "clocks": clocks,
+            "gpu_launches": None}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, sample = cpu_oracle_rate(args.cpu_tokens, PROMPT)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--gamma", type=int, default=GAMMA)
+    ap.add_argument("--recipe", default="A", choices=["A", "B"])
+    ap.add_argument("--cpu-tokens", type=int, default=12)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_engine(args)
+
+
+if __name__ == "__main__":
+    main()
