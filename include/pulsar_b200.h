@@ -173,6 +173,13 @@ int pulsar_engine_generate_greedy(pulsar_engine* eng, int32_t n_seq, const int32
                                   const float* first_logits_dev, int32_t n_new, int32_t gamma,
                                   int32_t* out_tokens_dev, int64_t* stats_host, void* stream);
 
+/* Engine options. "megakernel" (0/1, default 1 when the GPU can co-schedule one CTA per
+ * SM): run each pulse pass of <= 5 rows as one persistent kernel instead of per-op
+ * kernels. Read-only: "megakernel_grid" (CTAs of the persistent kernel), "loop_adapter"
+ * (1 when some loop-adapter lora_B is non-zero; such weights use the per-op kernels). */
+int pulsar_engine_set_option(pulsar_engine* eng, const char* name, int64_t value);
+int pulsar_engine_get_option(pulsar_engine* eng, const char* name, int64_t* value);
+
 #ifdef __cplusplus
 }
 #endif

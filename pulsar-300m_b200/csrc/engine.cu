@@ -13,6 +13,7 @@
 #include "capi_util.h"
 #include "engine_kernels.cuh"
 #include "prefill_kernels.cuh"
+#include "mega_launch.h"
 
 using namespace pulsar;
 
@@ -199,6 +200,12 @@ struct pulsar_engine {
     float *hblk = nullptr, *h0blk = nullptr, *htmp = nullptr, *htmp2 = nullptr, *h0tmp = nullptr, *logits_tmp = nullptr;
     long long* stats = nullptr;
     std::map<std::string, cudaGraphExec_t> graphs;
+    // persistent pulse kernel
+    bool use_mega = false;
+    int mega_grid = 0, mega_nch = 0;
+    float *m_gate = nullptr, *m_part = nullptr, *m_g8 = nullptr, *m_pmax = nullptr;
+    int *m_pidx = nullptr, *m_err = nullptr;
+    unsigned *m_bar = nullptr, *m_tickets = nullptr;
 
     int dmalloc(void** p, size_t bytes, int64_t* counter) {
         cudaError_t e = cudaMalloc(p, bytes);
@@ -340,8 +347,82 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
     return PULSAR_OK;
 }
 
+int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
+               float* h_out, float* h0n_out, float* logits, int* amax, cudaStream_t st) {
+    MegaArgs a{};
+    a.R = R;
+    a.pulse = p;
+    a.n_slots = e->cfg.max_batch;
+    a.max_pos = e->max_pos();
+    a.V = e->V;
+    a.use_conv = e->cfg.use_canon_conv;
+    a.base_seq_len = e->cfg.base_seq_len;
+    a.eps = e->cfg.rms_eps;
+    a.softcap = e->cfg.logit_softcap;
+    a.rows = rows;
+    for (int l = 0; l < NL; ++l) {
+        a.wqkv[l] = e->wqkv[l];
+        a.wo[l] = e->wo[l];
+        a.sh_gu[l] = e->sh_gu[l];
+        a.sh_dn[l] = e->sh_dn[l];
+        a.r_gu[l] = e->r_gu[l];
+        a.r_dn[l] = e->r_dn[l];
+        a.attn_norm[l] = e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D;
+        a.mlp_norm[l] = e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D;
+        a.qn[l] = e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH;
+        a.kn[l] = e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH;
+        a.gate_w[l] = e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D;
+        a.gate_b[l] = e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H;
+        a.router[l] = e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D;
+        a.ebias[l] = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
+        a.rscale[l] = e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D;
+        a.vres[l] = e->vres[p][l];
+        a.kvl[l] = e->kvl[l];
+    }
+    a.emb = e->emb;
+    a.anchor = e->T_("anchor_norm.weight");
+    a.stem = e->T_("stem_canon_weight");
+    a.step = e->T_("pulse_step_emb.weight") + (int64_t)p * D;
+    a.psn = e->T_("pulse_state_norm.weight");
+    a.rg_down = e->T_("reinject_gate_down") + (int64_t)p * RG * 2 * D;
+    a.rg_up = e->T_("reinject_gate_up") + (int64_t)p * D * RG;
+    a.rg_bias = e->T_("reinject_gate_bias") + (int64_t)p * D;
+    a.res_scale = e->T_("pulse_res_scale") + (int64_t)p * D;
+    a.fnorm = e->T_("final_norm.weight");
+    a.cos_l = e->cos_l;
+    a.sin_l = e->sin_l;
+    a.cos_g = e->cos_g;
+    a.sin_g = e->sin_g;
+    a.h_prev = h_prev;
+    a.h0n_in = h0n_in;
+    a.h_out = h_out;
+    a.h0n_out = h0n_out;
+    a.logits = logits;
+    a.amax = amax;
+    auto& w = e->w;
+    a.h = w.h;
+    a.h_in = w.h_in;
+    a.qkv = w.qkv;
+    a.gate = e->m_gate;
+    a.att = w.att;
+    a.act_sh = w.act_sh;
+    a.act_r = w.act_r;
+    a.part = e->m_part;
+    a.vfirst = w.vfirst;
+    a.g8 = e->m_g8;
+    a.pmax = e->m_pmax;
+    a.pidx = e->m_pidx;
+    a.nch_max = e->mega_nch;
+    a.bar = e->m_bar;
+    a.tickets = e->m_tickets;
+    a.err = e->m_err;
+    return launch_mega(a, e->kv32(), e->mega_grid, st);
+}
+
 int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in, float* h_out,
           float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+    if (e->use_mega && !e->has_lora && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V))
+        return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st);
     if (e->kv32())
         return enqueue_pulse<float>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
     return enqueue_pulse<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
@@ -452,6 +533,20 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
     const int nblk = e->V / LM_ROWS_PER_BLOCK;
     k_lmhead<<<nblk, 128, 0, st>>>(e->emb, e->V, f.hn, 1, 0.f, logits, e->V, f.pmax, f.pidx);
     PULSAR_LAUNCH_CHECK("prefill lm head");
+    return PULSAR_OK;
+}
+
+// The persistent kernel raises a device flag when a bounded wait runs out; report it once.
+int check_kernel_err(pulsar_engine* e) {
+    if (!e->m_err) return PULSAR_OK;
+    int v = 0;
+    PULSAR_TRY(cuda_status(cudaMemcpy(&v, e->m_err, 4, cudaMemcpyDeviceToHost), "read error flag"));
+    if (v) {
+        cudaMemset(e->m_err, 0, 4);
+        set_error("persistent pulse kernel: a bounded wait ran out (grid barrier or weight stream); results of the "
+                  "affected launch are invalid");
+        return PULSAR_ERR_CUDA;
+    }
     return PULSAR_OK;
 }
 
@@ -610,6 +705,27 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&e->htmp, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->htmp2, (size_t)MAX_ROWS * D)) ||
         (st = e->wmalloc(&e->h0tmp, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->stats, (size_t)MAX_ROWS * 3)))
         return fail(st);
+    // persistent pulse kernel: one CTA per SM, co-resident (cooperative launch)
+    {
+        int sms = 0, per_sm = 0;
+        if ((st = cuda_status(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device), "SM count")))
+            return fail(st);
+        if ((st = mega_occupancy(cfg->kv_fp32 != 0, &per_sm))) return fail(st);
+        // the per-CTA staging sizes assume >= 144 CTAs (ceil(8192 / C) + ceil(1024 / C) <= 64 pairs)
+        e->mega_grid = sms;
+        e->use_mega = per_sm >= 1 && sms >= 144;
+        e->mega_nch = (maxlen + MEGA_CHUNK - 1) / MEGA_CHUNK + 2;
+        if ((st = e->wmalloc(&e->m_gate, (size_t)MEGA_RMAX * H)) ||
+            (st = e->wmalloc(&e->m_part, (size_t)MEGA_RMAX * H * e->mega_nch * PART)) ||
+            (st = e->wmalloc(&e->m_g8, (size_t)MEGA_RMAX * RG)) ||
+            (st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
+            (st = e->wmalloc(&e->m_pidx, (size_t)MEGA_RMAX * std::max(sms, 1))) || (st = e->wmalloc(&e->m_err, 1)) ||
+            (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 1)))
+            return fail(st);
+        if ((st = cuda_status(cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 1) * 4), "zero tickets")) ||
+            (st = cuda_status(cudaMemset(e->m_err, 0, 4), "zero err")))
+            return fail(st);
+    }
     *out = e;
     clear_error();
     return PULSAR_OK;
@@ -777,6 +893,7 @@ extern "C" int pulsar_engine_pulse(pulsar_engine* e, int32_t p, int32_t R, const
         cudaStream_t vs = reinterpret_cast<cudaStream_t>(stream);
         PULSAR_TRY(cuda_status(cudaMemcpyAsync(hr, rows, (size_t)R * sizeof(int4), cudaMemcpyDeviceToHost, vs), "copy rows"));
         PULSAR_TRY(cuda_status(cudaStreamSynchronize(vs), "copy rows"));
+        PULSAR_TRY(check_kernel_err(e));
         for (int r = 0; r < R; ++r) {
             if (hr[r].x < 0 || hr[r].x >= e->cfg.max_batch) {
                 set_error("pulse: row %d has slot %d outside [0, %d)", r, hr[r].x, e->cfg.max_batch);
@@ -790,6 +907,16 @@ extern "C" int pulsar_engine_pulse(pulsar_engine* e, int32_t p, int32_t R, const
                 set_error("pulse: row %d token %d outside [0, %d)", r, hr[r].z, e->V);
                 return PULSAR_ERR_INVALID;
             }
+            // the rows of one sequence form one contiguous run of consecutive positions
+            if (r > 0 && hr[r].x == hr[r - 1].x && hr[r].y != hr[r - 1].y + 1) {
+                set_error("pulse: rows %d and %d of slot %d do not have consecutive positions", r - 1, r, hr[r].x);
+                return PULSAR_ERR_INVALID;
+            }
+            for (int q = 0; q + 1 < r; ++q)
+                if (hr[q].x == hr[r].x && hr[r - 1].x != hr[r].x) {
+                    set_error("pulse: rows of slot %d are not contiguous", hr[r].x);
+                    return PULSAR_ERR_INVALID;
+                }
         }
     }
     return pulse(e, p, R, reinterpret_cast<const int4*>(rows), h_prev, h0n, h_out, h0n_out, logits, e->V, nullptr,
@@ -863,6 +990,7 @@ extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const 
         remaining_steps = n_new - min_out;
     }
     for (int i = 0; i < n; ++i) e->len[slots_host[i]] = hs[i].len;
+    PULSAR_TRY(check_kernel_err(e));
     if (stats_host) {
         std::vector<long long> sv((size_t)n * 3);
         PULSAR_TRY(cuda_status(cudaMemcpy(sv.data(), e->stats, sv.size() * 8, cudaMemcpyDeviceToHost), "read stats"));
@@ -871,4 +999,34 @@ extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const 
             for (int k = 0; k < 3; ++k) stats_host[k] += sv[(size_t)i * 3 + k];
     }
     return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int64_t value) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(name, "set_option: null name");
+    if (strcmp(name, "megakernel") == 0) {
+        if (value && (e->mega_grid < 144)) {
+            set_error("set_option: the persistent pulse kernel needs >= 144 co-resident CTAs (this GPU: %d)", e->mega_grid);
+            return PULSAR_ERR_UNSUPPORTED;
+        }
+        const bool v = value != 0;
+        if (v != e->use_mega) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+            e->graphs.clear();
+        }
+        e->use_mega = v;
+        return PULSAR_OK;
+    }
+    set_error("set_option: unknown option '%s'", name);
+    return PULSAR_ERR_INVALID;
+}
+
+extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int64_t* value) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(name && value, "get_option: null argument");
+    if (strcmp(name, "megakernel") == 0) { *value = e->use_mega ? 1 : 0; return PULSAR_OK; }
+    if (strcmp(name, "megakernel_grid") == 0) { *value = e->mega_grid; return PULSAR_OK; }
+    if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }
+    set_error("get_option: unknown option '%s'", name);
+    return PULSAR_ERR_INVALID;
 }

@@ -1,0 +1,944 @@
+// Persistent per-pulse decode kernel (one CTA per SM, cooperative launch).
+//
+// One launch runs a whole pulse pass (src/infer.py:463-524) for R <= MEGA_RMAX rows: the
+// pulse input, 8 layers x 5 phases separated by grid barriers, the end-of-pulse residual,
+// the final norm and the LM head with argmax.
+//
+// Warp 0 is the producer: one lane streams every weight tile this CTA will consume, in
+// consumption order, through a ring of NS 8 KB shared-memory slots with 1-D TMA bulk copies
+// (cp.async.bulk + mbarrier complete_tx). Weights do not depend on activations, so the
+// producer runs ahead across grid barriers (only the routed-expert tiles wait for this
+// layer's router, computed from a flag in shared memory). Warps 1..15 are consumers: tile t
+// of the CTA's stream lives in slot t % NS and is consumed by warp t % 15.
+//
+// Phases per layer (work split evenly over the CTAs, outputs owned by one CTA each):
+//   A  xn = RMSNorm(h); QKV GEMV rows; gate logits sigmoid(xn.Wg + b) (CTAs < 16)
+//   B  attention items (sequence block, kv head, 64-key chunk): q of the 4 heads via
+//      QK-RMSNorm + RoPE (+YaRN); block rows' K/V produced (norm, RoPE, value residual)
+//      and written to the cache by the item that owns their chunk; other keys read from
+//      the cache; split-K partials; the last item of a (block, head group) combines the
+//      chunks and applies the gate (atomic ticket, fixed combine order)
+//   C  Wo GEMV, h += (owned rows)
+//   D  m = RMSNorm(h); fp32 router (16 x 1024, every CTA, identical result); top-4;
+//      shared + routed (distinct experts) gate/up GEMVs with the SwiGLU epilogue
+//   E  shared + routed down GEMVs for owned output rows, combine in top-k order, h +=
+// Then: h_out = h_in + (h - h_in) * res_scale, final RMSNorm, LM head rows, argmax.
+#pragma once
+
+#include "kv.cuh"
+#include "mega_ptx.cuh"
+
+namespace pulsar {
+
+constexpr int MEGA_THREADS = 512;
+constexpr int MEGA_NCW = 15;              // consumer warps
+constexpr int MEGA_NCT = MEGA_NCW * 32;   // consumer threads
+constexpr int MEGA_NS = 18;               // ring slots
+constexpr int MEGA_SLOT = 8192;           // bytes per slot
+constexpr int MEGA_RMAX = 5;              // rows per pass
+constexpr int MEGA_XS = MEGA_RMAX * 3072; // floats: act_sh [R][1024] + act_r [R][4][512]
+constexpr int MEGA_STAGE = 2048;          // floats
+constexpr int MEGA_CHUNK = 64;            // keys per attention item
+constexpr int MEGA_MAXPAIRS = 64;         // phase-D output pairs per CTA (>= ceil((1024+16*512)/C))
+constexpr int MEGA_MAXOROWS = 8;          // phase-E output rows per CTA (>= ceil(1024/C))
+
+struct MegaArgs {
+    int R, pulse, n_slots, max_pos, V, use_conv, base_seq_len;
+    float eps, softcap;
+    const int4* rows;
+    const __nv_bfloat16 *wqkv[NL], *wo[NL], *sh_gu[NL], *sh_dn[NL], *r_gu[NL], *r_dn[NL];
+    const float *attn_norm[NL], *mlp_norm[NL], *qn[NL], *kn[NL], *gate_w[NL], *gate_b[NL], *router[NL], *ebias[NL],
+        *rscale[NL];
+    float vres[NL];
+    KVLayer kvl[NL];
+    const __nv_bfloat16* emb;
+    const float *anchor, *stem, *step, *psn, *rg_down, *rg_up, *rg_bias, *res_scale, *fnorm;
+    const float *cos_l, *sin_l, *cos_g, *sin_g;
+    const float* h_prev;
+    const float* h0n_in;
+    float *h_out, *h0n_out, *logits;
+    int* amax;
+    // global workspace
+    float *h, *h_in, *qkv, *gate, *att, *act_sh, *act_r, *part, *vfirst, *g8, *pmax;
+    int* pidx;
+    int nch_max;          // chunks per (row, head) in `part`
+    unsigned* bar;        // grid barrier counter (zeroed before launch)
+    unsigned* tickets;    // [MEGA_RMAX * HKV + 1] (self-resetting)
+    int* err;             // error flag (non-zero: a bounded wait ran out)
+};
+
+struct MegaSmem {
+    uint64_t full[MEGA_NS];
+    uint64_t empty[MEGA_NS];
+    float logits[MEGA_RMAX][E];
+    float wts[MEGA_RMAX][TOPK];
+    int idx[MEGA_RMAX][TOPK];
+    int elist[E];
+    int n_e;
+    volatile int moe_ready;
+    int ticket;
+    int abort;
+    alignas(128) unsigned char ring[MEGA_NS][MEGA_SLOT];
+    alignas(16) float xs[MEGA_XS];
+    alignas(16) float stage[MEGA_STAGE];
+};
+
+__device__ __forceinline__ void rows_split(int N, int c, int C, int& r0, int& r1) {
+    r0 = (int)(((long long)N * c) / C);
+    r1 = (int)(((long long)N * (c + 1)) / C);
+}
+
+// ------------------------------------------------------------------ tile stream
+// The producer and the consumers walk the same sequence of tiles; `Ring` keeps the counter.
+struct Ring {
+    MegaSmem* s;
+    uint32_t t;     // tiles so far
+    int warp;       // consumer warp index (0..14), or -1 for the producer
+    bool ok;
+};
+
+// Producer side: issue tiles covering rows [r0, r1) of a row-major matrix with row_bytes
+// bytes per row, rows_per_tile rows per tile.
+__device__ __forceinline__ void produce_rows(Ring& g, const void* base, int row_bytes, int r0, int r1,
+                                             int rows_per_tile) {
+    for (int r = r0; r < r1 && g.ok; r += rows_per_tile) {
+        const int n = min(rows_per_tile, r1 - r);
+        const uint32_t slot = g.t % MEGA_NS;
+        const uint32_t use = g.t / MEGA_NS;
+        if (use > 0 && !mbar_wait(&g.s->empty[slot], (use - 1) & 1)) { g.ok = false; break; }
+        const uint32_t bytes = (uint32_t)n * row_bytes;
+        mbar_arrive_expect_tx(&g.s->full[slot], bytes);
+        tma_load_1d(g.s->ring[slot], static_cast<const char*>(base) + (int64_t)r * row_bytes, bytes, &g.s->full[slot]);
+        ++g.t;
+    }
+}
+
+// Consumer side: for each tile of the same range, if this warp owns it, wait for it and call
+// fn(tile_smem, first_row, n_rows); then release the slot.
+template <typename F>
+__device__ __forceinline__ void consume_rows(Ring& g, int r0, int r1, int rows_per_tile, F&& fn) {
+    const int lane = threadIdx.x & 31;
+    for (int r = r0; r < r1; r += rows_per_tile) {
+        const int n = min(rows_per_tile, r1 - r);
+        const uint32_t slot = g.t % MEGA_NS;
+        const uint32_t use = g.t / MEGA_NS;
+        if ((int)(g.t % MEGA_NCW) == g.warp && g.ok) {
+            if (!mbar_wait(&g.s->full[slot], use & 1)) {
+                g.ok = false;
+            } else {
+                fn(g.s->ring[slot], r, n);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&g.s->empty[slot]);
+            }
+        }
+        ++g.t;
+    }
+}
+
+// ------------------------------------------------------------------ warp GEMV on a tile
+// acc[i][r] = sum_k W[i][k] X_r[k] for tile rows i < nr (processed 4 at a time) with bf16
+// weights in shared memory and fp32 X rows in shared memory. Lane l covers the elements
+// seg*256 + j*128 + 4l + q (j < 2, q < 4): conflict-free 8-byte / 16-byte shared loads.
+template <int R, int KD>
+__device__ __forceinline__ void tile_gemv4(const __nv_bfloat16* w, int nr, const float* const* xr, float (&acc)[4][R]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[i][r] = 0.f;
+#pragma unroll
+    for (int seg = 0; seg < KD / 256; ++seg) {
+        float x[R][8];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float4 v = xr[r] ? *reinterpret_cast<const float4*>(xr[r] + seg * 256 + j * 128 + lane * 4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                x[r][j * 4 + 0] = v.x; x[r][j * 4 + 1] = v.y; x[r][j * 4 + 2] = v.z; x[r][j * 4 + 3] = v.w;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (i < nr) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const uint2 u = *reinterpret_cast<const uint2*>(w + (int64_t)i * KD + seg * 256 + j * 128 + lane * 4);
+                    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+                    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                        acc[i][r] += a.x * x[r][j * 4] + a.y * x[r][j * 4 + 1] + b.x * x[r][j * 4 + 2] + b.y * x[r][j * 4 + 3];
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[i][r] = warp_sum(acc[i][r]);
+}
+
+// fp32 rows (router): same mapping, float4 weight loads.
+template <int R>
+__device__ __forceinline__ void tile_gemv_f32(const float* w, int nr, const float* const* xr, float (&acc)[2][R]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[i][r] = 0.f;
+#pragma unroll
+    for (int seg = 0; seg < 4; ++seg) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int k = seg * 256 + j * 128 + lane * 4;
+            float4 xv[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) xv[r] = *reinterpret_cast<const float4*>(xr[r] + k);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                if (i < nr) {
+                    const float4 wv = *reinterpret_cast<const float4*>(w + i * D + k);
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                        acc[i][r] += wv.x * xv[r].x + wv.y * xv[r].y + wv.z * xv[r].z + wv.w * xv[r].w;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[i][r] = warp_sum(acc[i][r]);
+}
+
+// ------------------------------------------------------------------ grid barrier (consumers)
+__device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsigned& epoch) {
+    named_bar_sync(1, MEGA_NCT);
+    if (threadIdx.x == 32) {
+        epoch += 1;
+        __threadfence();
+        red_release_gpu_add(a.bar, 1u);
+        const unsigned target = epoch * gridDim.x;
+        bool ok = true;
+        if (ld_acquire_gpu(a.bar) < target) {
+            const unsigned long long t0 = globaltimer();
+            while (ld_acquire_gpu(a.bar) < target) {
+                if (globaltimer() - t0 > WAIT_NS || *(volatile int*)a.err) { ok = false; break; }
+            }
+        }
+        if (!ok) {
+            atomicExch(a.err, 1);
+            s->abort = 1;
+        }
+    }
+    named_bar_sync(1, MEGA_NCT);
+    return s->abort == 0;
+}
+
+// RMSNorm of R rows (global, [R][1024]) into xs with weight w: one consumer warp per row.
+template <int R>
+__device__ __forceinline__ void norm_rows(const float* src, const float* w, float eps, float* dst) {
+    const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+    for (int r = cw; r < R; r += MEGA_NCW) {
+        float v[32];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            v[i] = __ldcg(src + (int64_t)r * D + i * 32 + lane);   // written by other CTAs: bypass L1
+            ss += v[i] * v[i];
+        }
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[r * D + i * 32 + lane] = w[i * 32 + lane] * (v[i] * inv);
+    }
+}
+
+// ------------------------------------------------------------------ attention item
+template <int R, typename KVT>
+__device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr, int g, int c, int nch,
+                          int& vres_dummy) {
+    const int tid = threadIdx.x - 32;   // consumer thread 0..479
+    const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+    const bool local = is_local_layer(l);
+    const KVLayer& L = a.kvl[l];
+    const int slot = a.rows[r0].x;
+    const int pos0 = a.rows[r0].y, posL = a.rows[r0 + nr - 1].y;
+    const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
+    const int k0 = lo + c * MEGA_CHUNK;
+    const int k1 = min(k0 + MEGA_CHUNK, posL + 1);
+    float* qs = s->xs;                                   // [nr*4][64]
+    float* Ks = qs + MEGA_RMAX * GQA * DH;               // [64][65]
+    float* Vs = Ks + MEGA_CHUNK * (DH + 1);              // [64][65]
+    float* Ps = Vs + MEGA_CHUNK * (DH + 1);              // [nr*4][64]
+    const float* cos_t = local ? a.cos_l : a.cos_g;
+    const float* sin_t = local ? a.sin_l : a.sin_g;
+    const int nq = nr * GQA;
+    // 1) queries of heads 4g..4g+3 for the block rows
+    for (int qi = cw; qi < nq; qi += MEGA_NCW) {
+        const int rr = qi / GQA, h = g * GQA + qi % GQA;
+        const int pos = a.rows[r0 + rr].y;
+        const float* src = a.qkv + (int64_t)(r0 + rr) * QKV + h * DH;
+        const float x1 = __ldcg(src + lane), x2 = __ldcg(src + lane + 32);
+        const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + a.eps);
+        const float* qw = a.qn[l] + h * DH;
+        const float q1 = qw[lane] * (x1 * inv), q2 = qw[lane + 32] * (x2 * inv);
+        const float cs = cos_t[(int64_t)pos * 32 + lane], sn = sin_t[(int64_t)pos * 32 + lane];
+        float y1 = q1 * cs - q2 * sn, y2 = q2 * cs + q1 * sn;
+        if (!local && pos + 1 > a.base_seq_len) {
+            const double b = (double)a.base_seq_len;
+            const float sc = (float)(1.0 + 0.1 * log(fmax((double)(pos + 1), b) / b));
+            y1 *= sc;
+            y2 *= sc;
+        }
+        qs[qi * DH + lane] = y1 * 0.125f;
+        qs[qi * DH + lane + 32] = y2 * 0.125f;
+    }
+    // 2) keys / values of the chunk: block rows are produced here, older keys come from the cache
+    const int vres_mode = (a.pulse == 0) ? (l == 0 ? 1 : 2) : 0;
+    for (int kk = cw; kk < k1 - k0; kk += MEGA_NCW) {
+        const int key = k0 + kk;
+        if (key >= pos0) {
+            const int rr = r0 + (key - pos0);
+            const float* src = a.qkv + (int64_t)rr * QKV;
+            const float e1 = __ldcg(src + H * DH + g * DH + lane), e2 = __ldcg(src + H * DH + g * DH + lane + 32);
+            float v1 = __ldcg(src + H * DH + HKV * DH + g * DH + lane);
+            float v2 = __ldcg(src + H * DH + HKV * DH + g * DH + lane + 32);
+            float* vf = a.vfirst + ((int64_t)rr * HKV + g) * DH;
+            if (vres_mode == 1) {
+                vf[lane] = v1;
+                vf[lane + 32] = v2;
+            } else if (vres_mode == 2) {
+                const float lv = a.vres[l];
+                v1 = (1.f - lv) * v1 + lv * __ldcg(vf + lane);
+                v2 = (1.f - lv) * v2 + lv * __ldcg(vf + lane + 32);
+            }
+            const float inv = rsqrtf(warp_sum(e1 * e1 + e2 * e2) / (float)DH + a.eps);
+            const float* kw = a.kn[l] + g * DH;
+            const float b1 = kw[lane] * (e1 * inv), b2 = kw[lane + 32] * (e2 * inv);
+            const float cs = cos_t[(int64_t)key * 32 + lane], sn = sin_t[(int64_t)key * 32 + lane];
+            const float y1 = b1 * cs - b2 * sn, y2 = b2 * cs + b1 * sn;
+            KVT* kp = kv_k<KVT>(L, slot, g, key);
+            KVT* vp = kv_v<KVT>(L, slot, g, key);
+            kv_store(kp + lane, y1);
+            kv_store(kp + lane + 32, y2);
+            kv_store(vp + lane, v1);
+            kv_store(vp + lane + 32, v2);
+            // use the stored (rounded) values so every reader sees identical keys
+            Ks[kk * (DH + 1) + lane] = kv_load(kp + lane);
+            Ks[kk * (DH + 1) + lane + 32] = kv_load(kp + lane + 32);
+            Vs[kk * (DH + 1) + lane] = kv_load(vp + lane);
+            Vs[kk * (DH + 1) + lane + 32] = kv_load(vp + lane + 32);
+        } else {
+            const KVT* kp = kv_k<KVT>(L, slot, g, key);
+            const KVT* vp = kv_v<KVT>(L, slot, g, key);
+            Ks[kk * (DH + 1) + lane] = kv_load(kp + lane);
+            Ks[kk * (DH + 1) + lane + 32] = kv_load(kp + lane + 32);
+            Vs[kk * (DH + 1) + lane] = kv_load(vp + lane);
+            Vs[kk * (DH + 1) + lane + 32] = kv_load(vp + lane + 32);
+        }
+    }
+    // rows past the end of a partial chunk: zeros (their probabilities are 0, and 0 * stale
+    // shared memory could be NaN)
+    for (int kk = (k1 - k0) + cw; kk < MEGA_CHUNK; kk += MEGA_NCW) {
+        Ks[kk * (DH + 1) + lane] = 0.f;
+        Ks[kk * (DH + 1) + lane + 32] = 0.f;
+        Vs[kk * (DH + 1) + lane] = 0.f;
+        Vs[kk * (DH + 1) + lane + 32] = 0.f;
+    }
+    named_bar_sync(1, MEGA_NCT);
+    // 3) scores with per-row masks [lo_r, pos_r]
+    for (int e = tid; e < nq * MEGA_CHUNK; e += MEGA_NCT) {
+        const int qi = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
+        const int key = k0 + kk;
+        const int pos = a.rows[r0 + qi / GQA].y;
+        const int lor = local ? max(0, pos - WINDOW + 1) : 0;
+        float sc = -INFINITY;
+        if (key < k1 && key <= pos && key >= lor) {
+            sc = 0.f;
+            const float* qv = qs + qi * DH;
+            const float* kv = Ks + kk * (DH + 1);
+#pragma unroll 16
+            for (int d = 0; d < DH; ++d) sc += qv[d] * kv[d];
+        }
+        Ps[qi * MEGA_CHUNK + kk] = sc;
+    }
+    named_bar_sync(1, MEGA_NCT);
+    // 4) partial softmax and P.V per query
+    for (int qi = cw; qi < nq; qi += MEGA_NCW) {
+        const int rr = qi / GQA, h = g * GQA + qi % GQA;
+        const float p0 = Ps[qi * MEGA_CHUNK + lane], p1 = Ps[qi * MEGA_CHUNK + lane + 32];
+        const float m = warp_max(fmaxf(p0, p1));
+        float* out = a.part + (((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART;
+        if (m == -INFINITY) {
+            if (lane == 0) { out[0] = -INFINITY; out[1] = 0.f; }
+            continue;
+        }
+        const float e0 = (p0 == -INFINITY) ? 0.f : expf(p0 - m);
+        const float e1 = (p1 == -INFINITY) ? 0.f : expf(p1 - m);
+        const float lsum = warp_sum(e0 + e1);
+        float o1 = 0.f, o2 = 0.f;
+        for (int j = 0; j < 32; ++j) {
+            const float pa = __shfl_sync(0xffffffffu, e0, j);
+            const float pb = __shfl_sync(0xffffffffu, e1, j);
+            o1 += pa * Vs[j * (DH + 1) + lane] + pb * Vs[(j + 32) * (DH + 1) + lane];
+            o2 += pa * Vs[j * (DH + 1) + lane + 32] + pb * Vs[(j + 32) * (DH + 1) + lane + 32];
+        }
+        if (lane == 0) { out[0] = m; out[1] = lsum; }
+        out[2 + lane] = o1;
+        out[2 + lane + 32] = o2;
+    }
+    // 5) the last chunk item of (block, g) combines and gates
+    __threadfence();
+    named_bar_sync(1, MEGA_NCT);
+    if (threadIdx.x == 32) {
+        const unsigned t = atomicAdd(&a.tickets[r0 * HKV + g], 1u);
+        s->ticket = (t == (unsigned)(nch - 1));
+        if (s->ticket) a.tickets[r0 * HKV + g] = 0;
+        __threadfence();
+    }
+    named_bar_sync(1, MEGA_NCT);
+    if (s->ticket) {
+        for (int qi = cw; qi < nq; qi += MEGA_NCW) {
+            const int rr = qi / GQA, h = g * GQA + qi % GQA;
+            const float* pp = a.part + ((int64_t)(r0 + rr) * H + h) * a.nch_max * PART;
+            float M = -INFINITY;
+            for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(pp + cc * PART));
+            float Ls = 0.f, o1 = 0.f, o2 = 0.f;
+            for (int cc = 0; cc < nch; ++cc) {
+                const float mc = __ldcg(pp + cc * PART);
+                if (mc == -INFINITY) continue;
+                const float wgt = expf(mc - M);
+                Ls += wgt * __ldcg(pp + cc * PART + 1);
+                o1 += wgt * __ldcg(pp + cc * PART + 2 + lane);
+                o2 += wgt * __ldcg(pp + cc * PART + 2 + lane + 32);
+            }
+            const float gt = sigmoidf_(__ldcg(a.gate + (r0 + rr) * H + h));
+            const float inv = 1.f / Ls;
+            a.att[(int64_t)(r0 + rr) * D + h * DH + lane] = (o1 * inv) * gt;
+            a.att[(int64_t)(r0 + rr) * D + h * DH + lane + 32] = (o2 * inv) * gt;
+        }
+    }
+    named_bar_sync(1, MEGA_NCT);
+}
+
+// ------------------------------------------------------------------ the pulse
+template <int R, typename KVT>
+__global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    MegaSmem* s = reinterpret_cast<MegaSmem*>(smem_raw);
+    const int C = gridDim.x, cta = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < MEGA_NS; ++i) {
+            mbar_init(&s->full[i], 1);
+            mbar_init(&s->empty[i], 1);
+        }
+        s->moe_ready = 0;
+        s->abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // ================================================================ producer
+    if (warp == 0) {
+        if (lane != 0) return;
+        Ring g{s, 0u, -1, true};
+        for (int l = 0; l < NL && g.ok; ++l) {
+            int r0, r1;
+            rows_split(QKV, cta, C, r0, r1);
+            produce_rows(g, a.wqkv[l], D * 2, r0, r1, 4);
+            rows_split(D, cta, C, r0, r1);
+            produce_rows(g, a.wo[l], D * 2, r0, r1, 4);
+            produce_rows(g, a.router[l], D * 4, 0, E, 2);
+            {   // shared-expert pairs: a static split, prefetched before the router runs
+                int j0, j1;
+                rows_split(DS, cta, C, j0, j1);
+                produce_rows(g, a.sh_gu[l], D * 2, j0, j1, 4);
+                produce_rows(g, a.sh_gu[l], D * 2, DS + j0, DS + j1, 4);
+            }
+            // routed pairs depend on this layer's router
+            const unsigned long long t0 = globaltimer();
+            while (s->moe_ready != l + 1) {
+                if (globaltimer() - t0 > WAIT_NS || *(volatile int*)a.err || s->abort) { g.ok = false; break; }
+            }
+            if (!g.ok) break;
+            const int n_e = s->n_e;
+            int q0, q1;
+            rows_split(DE * n_e, cta, C, q0, q1);
+            for (int ei = 0; ei < n_e; ++ei) {
+                const int b0 = ei * DE;
+                const int j0 = max(q0, b0) - b0, j1 = min(q1, b0 + DE) - b0;
+                if (j1 <= j0) continue;
+                const __nv_bfloat16* we = a.r_gu[l] + (int64_t)s->elist[ei] * 2 * DE * D;
+                produce_rows(g, we, D * 2, j0, j1, 4);
+                produce_rows(g, we, D * 2, DE + j0, DE + j1, 4);
+            }
+            rows_split(D, cta, C, r0, r1);
+            produce_rows(g, a.sh_dn[l], DS * 2, r0, r1, 4);
+            for (int ei = 0; ei < n_e; ++ei)
+                produce_rows(g, a.r_dn[l] + (int64_t)s->elist[ei] * D * DE, DE * 2, r0, r1, 8);
+        }
+        if (g.ok) {
+            int v0, v1;
+            rows_split(a.V, cta, C, v0, v1);
+            produce_rows(g, a.emb, D * 2, v0, v1, 4);
+        }
+        if (!g.ok) atomicExch(a.err, 1);
+        // drain: wait for every copy this thread issued to land before the CTA can exit
+        for (uint32_t t = (g.t > MEGA_NS ? g.t - MEGA_NS : 0); t < g.t; ++t)
+            if (!mbar_wait(&s->full[t % MEGA_NS], (t / MEGA_NS) & 1)) break;
+        return;
+    }
+
+    // ================================================================ consumers
+    const int cw = warp - 1;
+    Ring g{s, 0u, cw, true};
+    unsigned epoch = 0;
+    float* xs = s->xs;
+    const float eps = a.eps;
+    const int p = a.pulse;
+    // ---- pulse input: every CTA builds h_in for all rows in xs[0 .. R*D) ----
+    if (p == 0) {
+        for (int r = cw; r < R; r += MEGA_NCW) {
+            const int tok = min(max(a.rows[r].z, 0), a.V - 1);
+            const __nv_bfloat16* e = a.emb + (int64_t)tok * D;
+            float v[32];
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                v[i] = __bfloat162float(e[i * 32 + lane]);
+                ss += v[i] * v[i];
+            }
+            const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int d = i * 32 + lane;
+                float n = a.anchor[d] * (v[i] * inv);
+                if (a.use_conv) n = n + a.stem[d * 4] * n;
+                xs[r * D + d] = n + a.step[d];
+                if (cta == 0) a.h0n_out[r * D + d] = n;
+            }
+        }
+    } else {
+        // g8[r][j] = Wd[j][:D] . h0n[r] + Wd[j][D:] . RMSNorm(h_prev[r])   (CTAs < 8)
+        if (cta < RG) {
+            const int j = cta;
+            for (int r = cw; r < R; r += MEGA_NCW) {
+                float ss = 0.f;
+                for (int i = lane; i < D; i += 32) ss += a.h_prev[r * D + i] * a.h_prev[r * D + i];
+                const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+                float pe = 0.f, pr = 0.f;
+                for (int i = lane; i < D; i += 32) {
+                    pe += a.rg_down[j * 2 * D + i] * a.h0n_in[r * D + i];
+                    pr += a.rg_down[j * 2 * D + D + i] * (a.psn[i] * (a.h_prev[r * D + i] * inv));
+                }
+                pe = warp_sum(pe);
+                pr = warp_sum(pr);
+                if (lane == 0) a.g8[r * RG + j] = pe + pr;
+            }
+        }
+        if (!grid_sync(a, s, epoch)) goto done;
+        for (int r = cw; r < R; r += MEGA_NCW) {
+            float ss = 0.f;
+            for (int i = lane; i < D; i += 32) ss += a.h_prev[r * D + i] * a.h_prev[r * D + i];
+            const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+            float gg[RG];
+#pragma unroll
+            for (int j = 0; j < RG; ++j) gg[j] = __ldcg(a.g8 + r * RG + j);
+            for (int d = lane; d < D; d += 32) {
+                float z = a.rg_bias[d];
+#pragma unroll
+                for (int j = 0; j < RG; ++j) z += a.rg_up[d * RG + j] * gg[j];
+                const float mix = sigmoidf_(z);
+                const float rn = a.psn[d] * (a.h_prev[r * D + d] * inv);
+                const float an = a.h0n_in[r * D + d];
+                const float diff = an - rn;
+                const float lerp = (mix < 0.5f) ? rn + mix * diff : an - diff * (1.f - mix);
+                xs[r * D + d] = lerp + a.step[d];
+                if (cta == 0) a.h0n_out[r * D + d] = an;
+            }
+        }
+    }
+    named_bar_sync(1, MEGA_NCT);
+    if (cta == 0)
+        for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT) {
+            a.h_in[i] = xs[i];
+            a.h[i] = xs[i];
+        }
+    named_bar_sync(1, MEGA_NCT);
+    // xs holds h_in; layer 0's attention norm reads it from xs, later layers from a.h
+    for (int l = 0; l < NL; ++l) {
+        // ---------------- phase A: xn, QKV, gate logits
+        {
+            const float* src = (l == 0) ? nullptr : a.h;
+            if (l == 0) {
+                // normalise in place (each warp owns its rows)
+                for (int r = cw; r < R; r += MEGA_NCW) {
+                    float v[32];
+                    float ss = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        v[i] = xs[r * D + i * 32 + lane];
+                        ss += v[i] * v[i];
+                    }
+                    const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = a.attn_norm[l][i * 32 + lane] * (v[i] * inv);
+                }
+            } else {
+                norm_rows<R>(src, a.attn_norm[l], eps, xs);
+            }
+            named_bar_sync(1, MEGA_NCT);
+            const float* xr[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
+            int r0, r1;
+            rows_split(QKV, cta, C, r0, r1);
+            consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
+                float acc[4][R];
+                tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                        if (lane == i * R + r && i < n) a.qkv[(int64_t)r * QKV + row0 + i] = acc[i][r];
+            });
+            if (cta < H) {
+                const int h = cta;
+                for (int r = cw; r < R; r += MEGA_NCW) {
+                    float z = 0.f;
+                    for (int k = lane; k < D; k += 32) z += a.gate_w[l][h * D + k] * xs[r * D + k];
+                    z = warp_sum(z);
+                    if (lane == 0) a.gate[r * H + h] = z + a.gate_b[l][h];
+                }
+            }
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
+        }
+        // ---------------- phase B: attention
+        {
+            const bool local = is_local_layer(l);
+            int item = 0;
+            int r0 = 0;
+            while (r0 < R) {
+                int nr = 1;
+                while (r0 + nr < R && a.rows[r0 + nr].x == a.rows[r0].x) ++nr;
+                const int pos0 = a.rows[r0].y, posL = a.rows[r0 + nr - 1].y;
+                const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
+                const int nch = (posL - lo + MEGA_CHUNK) / MEGA_CHUNK;
+                for (int gg = 0; gg < HKV; ++gg)
+                    for (int c = 0; c < nch; ++c, ++item)
+                        if (item % C == cta) {
+                            int dummy = 0;
+                            attn_item<R, KVT>(a, s, l, r0, nr, gg, c, nch, dummy);
+                        }
+                r0 += nr;
+            }
+            if (!grid_sync(a, s, epoch)) goto done;
+        }
+        // ---------------- phase C: Wo, h += (owned rows)
+        {
+            for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT) xs[i] = __ldcg(a.att + i);
+            named_bar_sync(1, MEGA_NCT);
+            const float* xr[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
+            int r0, r1;
+            rows_split(D, cta, C, r0, r1);
+            consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
+                float acc[4][R];
+                tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                        if (lane == i * R + r && i < n) a.h[(int64_t)r * D + row0 + i] = __ldcg(a.h + (int64_t)r * D + row0 + i) + acc[i][r];
+            });
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
+        }
+        // ---------------- phase D: router, shared + routed up-projections
+        {
+            norm_rows<R>(a.h, a.mlp_norm[l], eps, xs);
+            named_bar_sync(1, MEGA_NCT);
+            const float* xr[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
+            consume_rows(g, 0, E, 2, [&](const unsigned char* tile, int row0, int n) {
+                float acc[2][R];
+                tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xr, acc);
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                        if (lane == i * R + r && i < n) s->logits[r][row0 + i] = acc[i][r];
+            });
+            named_bar_sync(1, MEGA_NCT);
+            if (cw == 0) {
+                // centre, sigmoid, top-4 of s + bias (ties to the lower expert), weights
+                int used = 0;
+                for (int r = 0; r < R; ++r) {
+                    const float lg = lane < E ? s->logits[r][lane] : 0.f;
+                    const float mean = warp_sum(lg) / (float)E;
+                    const float sg = sigmoidf_(lg - mean);
+                    float b = lane < E ? sg + a.ebias[l][lane] : -INFINITY;
+                    float sel_s[TOPK];
+                    int sel_i[TOPK];
+#pragma unroll
+                    for (int k = 0; k < TOPK; ++k) {
+                        ArgMax am{b, lane < E ? lane : 1 << 30};
+                        am = warp_argmax(am);
+                        sel_i[k] = am.i;
+                        sel_s[k] = __shfl_sync(0xffffffffu, sg, am.i & 31);
+                        if (lane == am.i) b = -INFINITY;
+                    }
+                    float sum = 0.f;
+#pragma unroll
+                    for (int k = 0; k < TOPK; ++k) sum += sel_s[k];
+                    sum += 1e-6f;
+                    if (lane == 0) {
+#pragma unroll
+                        for (int k = 0; k < TOPK; ++k) {
+                            s->idx[r][k] = sel_i[k];
+                            s->wts[r][k] = sel_s[k] / sum;
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < TOPK; ++k) used |= 1 << sel_i[k];
+                }
+                if (lane == 0) {
+                    int n = 0;
+                    for (int e = 0; e < E; ++e)
+                        if (used & (1 << e)) s->elist[n++] = e;
+                    s->n_e = n;
+                    __threadfence_block();
+                    s->moe_ready = l + 1;
+                }
+            }
+            named_bar_sync(1, MEGA_NCT);
+            const int n_e = s->n_e;
+            int s0, s1, q0, q1;
+            rows_split(DS, cta, C, s0, s1);          // shared pairs [s0, s1)
+            rows_split(DE * n_e, cta, C, q0, q1);    // routed pairs [q0, q1) over the expert list
+            const int nsh = s1 - s0;
+            float* st_g = s->stage;                         // [pair][R] gate: shared pairs, then routed
+            float* st_u = s->stage + MEGA_MAXPAIRS * R;     // [pair][R] up
+            {
+                const int j0 = s0, j1 = s1;
+                consume_rows(g, j0, j1, 4, [&](const unsigned char* tile, int row0, int n) {
+                    float acc[4][R];
+                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            if (lane == i * R + r && i < n) st_g[(row0 + i - s0) * R + r] = acc[i][r];
+                });
+                consume_rows(g, DS + j0, DS + j1, 4, [&](const unsigned char* tile, int row0, int n) {
+                    float acc[4][R];
+                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            if (lane == i * R + r && i < n) st_u[(row0 - DS + i - s0) * R + r] = acc[i][r];
+                });
+            }
+            for (int ei = 0; ei < n_e; ++ei) {
+                const int b0 = ei * DE;
+                const int j0 = max(q0, b0) - b0, j1 = min(q1, b0 + DE) - b0;
+                if (j1 <= j0) continue;
+                const int base = nsh + b0 - q0;   // stage index = base + j
+                consume_rows(g, j0, j1, 4, [&](const unsigned char* tile, int row0, int n) {
+                    float acc[4][R];
+                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            if (lane == i * R + r && i < n) st_g[(base + row0 + i) * R + r] = acc[i][r];
+                });
+                consume_rows(g, DE + j0, DE + j1, 4, [&](const unsigned char* tile, int row0, int n) {
+                    float acc[4][R];
+                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            if (lane == i * R + r && i < n) st_u[(base + row0 - DE + i) * R + r] = acc[i][r];
+                });
+            }
+            named_bar_sync(1, MEGA_NCT);
+            // SwiGLU epilogue -> act_sh [R][1024], act_r [R][4][512]
+            for (int e = threadIdx.x - 32; e < (nsh + q1 - q0) * R; e += MEGA_NCT) {
+                const int pi = e / R, r = e % R;
+                const float v = siluf_(st_g[pi * R + r]) * st_u[pi * R + r];
+                if (pi < nsh) {
+                    a.act_sh[(int64_t)r * DS + s0 + pi] = v;
+                } else {
+                    const int q = q0 + pi - nsh;
+                    const int ei = q / DE, j = q % DE;
+                    const int ex = s->elist[ei];
+#pragma unroll
+                    for (int k = 0; k < TOPK; ++k)
+                        if (s->idx[r][k] == ex) a.act_r[((int64_t)r * TOPK + k) * DE + j] = v;
+                }
+            }
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
+        }
+        // ---------------- phase E: down projections + combine, h += (owned rows)
+        {
+            for (int i = threadIdx.x - 32; i < R * DS; i += MEGA_NCT) xs[i] = __ldcg(a.act_sh + i);
+            float* xa = xs + R * DS;
+            for (int i = threadIdx.x - 32; i < R * TOPK * DE; i += MEGA_NCT) xa[i] = __ldcg(a.act_r + i);
+            named_bar_sync(1, MEGA_NCT);
+            const int n_e = s->n_e;
+            int o0, o1;
+            rows_split(D, cta, C, o0, o1);
+            float* dsh = s->stage;                                   // [orow][R]
+            float* dex = s->stage + MEGA_MAXOROWS * R;               // [orow][ei][R]
+            {
+                const float* xr[R];
+#pragma unroll
+                for (int r = 0; r < R; ++r) xr[r] = xs + r * DS;
+                consume_rows(g, o0, o1, 4, [&](const unsigned char* tile, int row0, int n) {
+                    float acc[4][R];
+                    tile_gemv4<R, DS>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            if (lane == i * R + r && i < n) dsh[(row0 + i - o0) * R + r] = acc[i][r];
+                });
+            }
+            for (int ei = 0; ei < n_e; ++ei) {
+                const int ex = s->elist[ei];
+                const float* xr[R];
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    xr[r] = nullptr;
+#pragma unroll
+                    for (int k = 0; k < TOPK; ++k)
+                        if (s->idx[r][k] == ex) xr[r] = xa + (r * TOPK + k) * DE;
+                }
+                consume_rows(g, o0, o1, 8, [&](const unsigned char* tile, int row0, int n) {
+                    const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(tile);
+                    for (int half = 0; half < 2; ++half) {
+                        const int nn = min(4, n - half * 4);
+                        if (nn <= 0) break;
+                        float acc[4][R];
+                        tile_gemv4<R, DE>(w + half * 4 * DE, nn, xr, acc);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+#pragma unroll
+                            for (int r = 0; r < R; ++r)
+                                if (lane == i * R + r && i < nn)
+                                    dex[((row0 + half * 4 + i - o0) * E + ei) * R + r] = acc[i][r];
+                    }
+                });
+            }
+            named_bar_sync(1, MEGA_NCT);
+            for (int e = threadIdx.x - 32; e < (o1 - o0) * R; e += MEGA_NCT) {
+                const int oi = e / R, r = e % R;
+                const int o = o0 + oi;
+                float routed = 0.f;
+#pragma unroll
+                for (int k = 0; k < TOPK; ++k) {
+                    const int ex = s->idx[r][k];
+                    int ei = 0;
+                    for (int q = 0; q < n_e; ++q)
+                        if (s->elist[q] == ex) ei = q;
+                    routed = routed + dex[(oi * E + ei) * R + r] * s->wts[r][k];
+                }
+                a.h[(int64_t)r * D + o] = __ldcg(a.h + (int64_t)r * D + o) + (dsh[oi * R + r] + routed * a.rscale[l][o]);
+            }
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
+        }
+    }
+    // ---------------- end of pulse + LM head
+    {
+        for (int r = cw; r < R; r += MEGA_NCW) {
+            float v[32];
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int d = i * 32 + lane;
+                const float hi = __ldcg(a.h_in + r * D + d);
+                v[i] = hi + (__ldcg(a.h + r * D + d) - hi) * a.res_scale[d];
+                ss += v[i] * v[i];
+                if (cta == 0) a.h_out[r * D + d] = v[i];
+            }
+            const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = a.fnorm[i * 32 + lane] * (v[i] * inv);
+        }
+        named_bar_sync(1, MEGA_NCT);
+        const float* xr[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
+        ArgMax best[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) best[r] = ArgMax{-INFINITY, 1 << 30};
+        int v0, v1;
+        rows_split(a.V, cta, C, v0, v1);
+        consume_rows(g, v0, v1, 4, [&](const unsigned char* tile, int row0, int n) {
+            float acc[4][R];
+            tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (i < n) {
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        float y = acc[i][r];
+                        if (a.softcap > 0.f) y = a.softcap * tanhf(y / a.softcap);
+                        if (a.logits && lane == i * R + r) a.logits[(int64_t)r * a.V + row0 + i] = y;
+                        best[r] = argmax_merge(best[r], ArgMax{y, row0 + i});
+                    }
+                }
+            }
+        });
+        // per-CTA argmax -> pmax/pidx; the last CTA reduces
+        float* bv = s->stage;
+        int* bi = reinterpret_cast<int*>(s->stage + MEGA_NCW * R);
+        if (lane == 0)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                bv[cw * R + r] = best[r].v;
+                bi[cw * R + r] = best[r].i;
+            }
+        named_bar_sync(1, MEGA_NCT);
+        if (threadIdx.x - 32 < R) {
+            const int r = threadIdx.x - 32;
+            ArgMax b{bv[r], bi[r]};
+            for (int w = 1; w < MEGA_NCW; ++w) b = argmax_merge(b, ArgMax{bv[w * R + r], bi[w * R + r]});
+            a.pmax[r * C + cta] = b.v;
+            a.pidx[r * C + cta] = b.i;
+        }
+        __threadfence();
+        named_bar_sync(1, MEGA_NCT);
+        if (threadIdx.x == 32) {
+            const unsigned t = atomicAdd(&a.tickets[MEGA_RMAX * HKV], 1u);
+            s->ticket = (t == (unsigned)(C - 1));
+            if (s->ticket) a.tickets[MEGA_RMAX * HKV] = 0;
+            __threadfence();
+        }
+        named_bar_sync(1, MEGA_NCT);
+        if (s->ticket && a.amax) {
+            for (int r = cw; r < R; r += MEGA_NCW) {
+                ArgMax b{-INFINITY, 1 << 30};
+                for (int i = lane; i < C; i += 32) b = argmax_merge(b, ArgMax{__ldcg(a.pmax + r * C + i), __ldcg(a.pidx + r * C + i)});
+                b = warp_argmax(b);
+                if (lane == 0) a.amax[r] = b.i;
+            }
+        }
+        if (!g.ok) atomicExch(a.err, 1);
+    }
+done:
+    return;
+}
+
+}  // namespace pulsar

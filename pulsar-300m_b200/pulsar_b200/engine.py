@@ -127,6 +127,15 @@ class DeviceEngine:
     def set_length(self, slot: int, n: int) -> None:
         _lib.check(_lib.load().pulsar_engine_set_length(self._h, slot, int(n)), "set_length")
 
+    def set_option(self, name: str, value: int) -> None:
+        """Engine options (see include/pulsar_b200.h): "megakernel" 0/1."""
+        _lib.check(_lib.load().pulsar_engine_set_option(self._h, name.encode(), int(value)), f"set_option({name})")
+
+    def get_option(self, name: str) -> int:
+        v = C.c_int64()
+        _lib.check(_lib.load().pulsar_engine_get_option(self._h, name.encode(), C.byref(v)), f"get_option({name})")
+        return int(v.value)
+
     def memory(self) -> dict:
         a, k, w = C.c_int64(), C.c_int64(), C.c_int64()
         _lib.check(_lib.load().pulsar_engine_memory(self._h, C.byref(a), C.byref(k), C.byref(w)), "memory")

@@ -45,9 +45,15 @@ def _margin(lg):
     return float(v[0] - v[1])
 
 
+@pytest.fixture(params=[1, 0], ids=["megakernel", "per-op"])
+def path(request):
+    return request.param
+
+
 @pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("A", torch.float32), ("B", torch.float32)])
-def test_prefill_and_pulse_logits_match_oracle(recipe, kv):
+def test_prefill_and_pulse_logits_match_oracle(recipe, kv, path):
     eng, m, cfg = _setup(recipe, kv)
+    eng.set_option("megakernel", path)
     ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
     okv = O.OracleKV(m, 256)
     ref = O.prefill(m, ids, okv)
@@ -87,9 +93,10 @@ def test_long_prompt_local_quirk_and_yarn():
         tok, pos = int(lr[0].argmax()), pos + 1
 
 
-def test_rollback_is_exact():
+def test_rollback_is_exact(path):
     """Length reset (rollback) then recomputation reproduces the logits bit for bit."""
     eng, m, cfg = _setup("B", torch.float32)
+    eng.set_option("megakernel", path)
     ids = random_prompts(1, 64, cfg.vocab_size, seed=9)[0].tolist()
     eng.prefill(2, ids)
     toks = [5, 77, 901, 4242]
@@ -105,8 +112,9 @@ def test_rollback_is_exact():
         assert torch.equal(lg, first[i])
 
 
-def test_rows_of_different_slots_are_independent():
+def test_rows_of_different_slots_are_independent(path):
     eng, m, cfg = _setup("B", torch.float32)
+    eng.set_option("megakernel", path)
     a = random_prompts(1, 40, cfg.vocab_size, seed=1)[0].tolist()
     b = random_prompts(1, 70, cfg.vocab_size, seed=2)[0].tolist()
     eng.prefill(0, a)
@@ -127,9 +135,10 @@ def _compare_tokens(got, ref, margins, what):
 
 
 @pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("B", torch.float32)])
-def test_greedy_generate_matches_oracle_stream(recipe, kv):
+def test_greedy_generate_matches_oracle_stream(recipe, kv, path):
     """generate_greedy(gamma=0) == reference stream_generate (greedy, penalty 1.0)."""
     eng, m, cfg = _setup(recipe, kv)
+    eng.set_option("megakernel", path)
     ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
     n = 48
     trace = []
@@ -141,9 +150,10 @@ def test_greedy_generate_matches_oracle_stream(recipe, kv):
 
 
 @pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("B", torch.float32)])
-def test_spec_gamma4_matches_oracle_block_verify(recipe, kv):
+def test_spec_gamma4_matches_oracle_block_verify(recipe, kv, path):
     """gamma = 4 drafting + one batched verify per round == the oracle's block-verify loop."""
     eng, m, cfg = _setup(recipe, kv)
+    eng.set_option("megakernel", path)
     ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
     n = 40
     trace = []
@@ -204,3 +214,55 @@ def test_reference_api_generate(gpu):
     assert out.shape == (1, 44)
     assert out[0, 32:].tolist() == O.stream_generate_ids(m, ids, 12)
     eng.dev.close()
+
+
+def test_verify_block_rows_match_oracle(path):
+    """A 5-row verify block of one sequence (block-verify KV rule) at pulses 0-2 vs the
+    oracle's multi-row pulse pass."""
+    eng, m, cfg = _setup("B", torch.float32)
+    eng.set_option("megakernel", path)
+    ids = random_prompts(1, 96, cfg.vocab_size, seed=11)[0].tolist()
+    okv = O.OracleKV(m, 160)
+    O.prefill(m, ids, okv)
+    eng.prefill(0, ids)
+    toks = [17, 4093, 22, 30001, 9]
+    pos = list(range(96, 101))
+    rows = [(0, p_, t) for p_, t in zip(pos, toks)]
+    h = h0 = hr = h0r = None
+    for p in range(3):
+        lg, h, h0 = eng.pulse(p, rows, h, h0)
+        lr, hr, h0r = O.pulse_pass(m, p, toks, pos, okv, hr, h0r)
+        err = (lg.cpu() - lr).abs().max().item()
+        assert err <= TOL, f"verify block pulse {p}: {err:.3e}"
+
+
+def test_megakernel_matches_per_op_path():
+    """Both pulse implementations agree to fp32 reordering on the same rows."""
+    eng, m, cfg = _setup("B", torch.float32)
+    if not eng.get_option("megakernel_grid") >= 144:
+        pytest.skip("GPU cannot host the persistent kernel")
+    ids = random_prompts(1, 1100, cfg.vocab_size, seed=12)[0].tolist()
+    out = {}
+    for mode in (0, 1):
+        eng.set_option("megakernel", mode)
+        eng.prefill(1, ids)
+        rows = [(1, 1100 + j, 100 + 7 * j) for j in range(3)]
+        h = h0 = None
+        res = []
+        for p in range(3):
+            lg, h, h0 = eng.pulse(p, rows, h, h0)
+            res.append(lg.clone())
+        out[mode] = res
+    eng.set_option("megakernel", 1)
+    for p in range(3):
+        d = (out[0][p] - out[1][p]).abs().max().item()
+        assert d < 2e-3, f"pulse {p}: per-op vs persistent kernel differ by {d:.3e}"
+
+
+def test_rejects_non_consecutive_rows():
+    eng, m, cfg = _setup("B", torch.float32)
+    eng.prefill(0, [1, 2, 3, 4])
+    with pytest.raises(RuntimeError, match="consecutive"):
+        eng.pulse(0, [(0, 4, 5), (0, 6, 7)])
+    with pytest.raises(RuntimeError, match="outside"):
+        eng.pulse(0, [(0, 10**7, 5)])
