@@ -180,6 +180,14 @@ int pulsar_engine_generate_greedy(pulsar_engine* eng, int32_t n_seq, const int32
 int pulsar_engine_set_option(pulsar_engine* eng, const char* name, int64_t value);
 int pulsar_engine_get_option(pulsar_engine* eng, const char* name, int64_t* value);
 
+/* Phase tracing of the persistent pulse kernel (option "trace" = 1): every launch writes,
+ * per CTA, 256 %globaltimer stamps in ns (entry 0: start; 1 + 16*l + j: point j of layer l,
+ * j = 0 norm done, 1 QKV tiles, 2 gate, 3 barrier A left, 4 attention items, 5 barrier B left,
+ * 6 attention output loaded, 7 Wo tiles, 8 barrier C left, 9 norm, 10 router, 11 up tiles,
+ * 12 SwiGLU epilogue, 13 barrier D left, 14 activations loaded, 15 barrier E left; 254: end).
+ * host_out must hold megakernel_grid * 256 entries. */
+int pulsar_engine_read_trace(pulsar_engine* eng, uint64_t* host_out, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -206,6 +206,7 @@ struct pulsar_engine {
     float *m_gate = nullptr, *m_part = nullptr, *m_g8 = nullptr, *m_pmax = nullptr;
     int *m_pidx = nullptr, *m_err = nullptr;
     unsigned *m_bar = nullptr, *m_tickets = nullptr;
+    unsigned long long* m_trace = nullptr;   // phase stamps of the last traced launch (option "trace")
 
     int dmalloc(void** p, size_t bytes, int64_t* counter) {
         cudaError_t e = cudaMalloc(p, bytes);
@@ -416,6 +417,7 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.bar = e->m_bar;
     a.tickets = e->m_tickets;
     a.err = e->m_err;
+    a.trace = e->m_trace;
     return launch_mega(a, e->kv32(), e->mega_grid, st);
 }
 
@@ -714,7 +716,7 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         // the per-CTA staging sizes assume >= 144 CTAs (ceil(8192 / C) + ceil(1024 / C) <= 64 pairs)
         e->mega_grid = sms;
         e->use_mega = per_sm >= 1 && sms >= 144;
-        e->mega_nch = (maxlen + MEGA_CHUNK - 1) / MEGA_CHUNK + 2;
+        e->mega_nch = std::max(2400 / 32 + 2, (maxlen + MEGA_CHUNK - 1) / MEGA_CHUNK + 2);   // see attn_chunk()
         if ((st = e->wmalloc(&e->m_gate, (size_t)MEGA_RMAX * H)) ||
             (st = e->wmalloc(&e->m_part, (size_t)MEGA_RMAX * H * e->mega_nch * PART)) ||
             (st = e->wmalloc(&e->m_g8, (size_t)MEGA_RMAX * RG)) ||
@@ -1017,8 +1019,31 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
         e->use_mega = v;
         return PULSAR_OK;
     }
+    if (strcmp(name, "trace") == 0) {
+        if (value && !e->m_trace) {
+            PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->m_trace), (size_t)e->mega_grid * MEGA_TRACE * 8,
+                                  &e->work_bytes));
+            PULSAR_TRY(cuda_status(cudaMemset(e->m_trace, 0, (size_t)e->mega_grid * MEGA_TRACE * 8), "zero trace"));
+        }
+        if (!value) e->m_trace = nullptr;   // the buffer stays allocated until destroy
+        for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+        e->graphs.clear();
+        return PULSAR_OK;
+    }
     set_error("set_option: unknown option '%s'", name);
     return PULSAR_ERR_INVALID;
+}
+
+extern "C" int pulsar_engine_read_trace(pulsar_engine* e, uint64_t* host, int64_t n) {
+    PULSAR_TRY(check_engine(e, false));
+    if (!e->m_trace) {
+        set_error("read_trace: tracing is off (set option \"trace\" to 1 first)");
+        return PULSAR_ERR_STATE;
+    }
+    PULSAR_CHECK_ARG(host && n >= (int64_t)e->mega_grid * MEGA_TRACE, "read_trace: need %d entries",
+                     e->mega_grid * MEGA_TRACE);
+    return cuda_status(cudaMemcpy(host, e->m_trace, (size_t)e->mega_grid * MEGA_TRACE * 8, cudaMemcpyDeviceToHost),
+                       "read trace");
 }
 
 extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int64_t* value) {

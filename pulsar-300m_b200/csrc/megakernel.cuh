@@ -65,7 +65,10 @@ struct MegaArgs {
     unsigned* bar;        // grid barrier counter (zeroed before launch)
     unsigned* tickets;    // [MEGA_RMAX * HKV + 1] (self-resetting)
     int* err;             // error flag (non-zero: a bounded wait ran out)
+    unsigned long long* trace;   // optional [gridDim][MEGA_TRACE] %globaltimer stamps (null: off)
 };
+
+constexpr int MEGA_TRACE = 256;   // stamps per CTA: [0] start, [1 + 16*l + j] phase points of layer l, [255] end
 
 struct MegaSmem {
     uint64_t full[MEGA_NS];
@@ -81,7 +84,23 @@ struct MegaSmem {
     alignas(128) unsigned char ring[MEGA_NS][MEGA_SLOT];
     alignas(16) float xs[MEGA_XS];
     alignas(16) float stage[MEGA_STAGE];
+    float wout[MEGA_NCW][4 * MEGA_RMAX];   // per-warp reduced tile sums
+    int xoff[MEGA_RMAX];                   // X row offsets (elements into xs) of the current phase
+    int xoff_e[E][MEGA_RMAX];              // phase E: per routed expert, act_r row of each row or -1
+    int blk_r0[MEGA_RMAX + 1];             // sequence blocks of the rows: start row
+    int blk_nch[MEGA_RMAX];                // attention chunks per (block, head group)
+    int blk_chunk[MEGA_RMAX];
+    int n_blk;
 };
+
+__device__ __forceinline__ void stamp(const MegaArgs& a, int l, int j) {
+    if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 1 + 16 * l + j] = globaltimer();
+}
+
+// attention-item sub-steps of the first item a CTA runs in layer l (entries 130 + 8*l + k)
+__device__ __forceinline__ void astamp(const MegaArgs& a, int l, int k, bool first) {
+    if (first && a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 130 + 8 * l + k] = globaltimer();
+}
 
 __device__ __forceinline__ void rows_split(int N, int c, int C, int& r0, int& r1) {
     r0 = (int)(((long long)N * c) / C);
@@ -136,25 +155,31 @@ __device__ __forceinline__ void consume_rows(Ring& g, int r0, int r1, int rows_p
 }
 
 // ------------------------------------------------------------------ warp GEMV on a tile
-// acc[i][r] = sum_k W[i][k] X_r[k] for tile rows i < nr (processed 4 at a time) with bf16
-// weights in shared memory and fp32 X rows in shared memory. Lane l covers the elements
-// seg*256 + j*128 + 4l + q (j < 2, q < 4): conflict-free 8-byte / 16-byte shared loads.
+// out[i*R + r] = sum_k W[i][k] X_r[k] for tile rows i < nr (nr <= 4) with bf16 weights and
+// fp32 X rows in shared memory (X_r = xbase + xoff[r]; xoff[r] < 0: a zero row). Lane l
+// covers the elements seg*256 + j*128 + 4l + q (j < 2, q < 4): conflict-free 8-byte /
+// 16-byte shared loads. Not inlined: one copy per (R, KD) keeps the persistent kernel's
+// code inside the instruction cache.
 template <int R, int KD>
-__device__ __forceinline__ void tile_gemv4(const __nv_bfloat16* w, int nr, const float* const* xr, float (&acc)[4][R]) {
+__device__ __noinline__ void tile_gemv(const __nv_bfloat16* w, int nr, const float* xbase, const int* xoff, float* out) {
     const int lane = threadIdx.x & 31;
+    float acc[4][R];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[i][r] = 0.f;
+    int xo[R];
 #pragma unroll
+    for (int r = 0; r < R; ++r) xo[r] = xoff[r];
+#pragma unroll 1
     for (int seg = 0; seg < KD / 256; ++seg) {
         float x[R][8];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                float4 v = xr[r] ? *reinterpret_cast<const float4*>(xr[r] + seg * 256 + j * 128 + lane * 4)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (xo[r] >= 0) v = *reinterpret_cast<const float4*>(xbase + xo[r] + seg * 256 + j * 128 + lane * 4);
                 x[r][j * 4 + 0] = v.x; x[r][j * 4 + 1] = v.y; x[r][j * 4 + 2] = v.z; x[r][j * 4 + 3] = v.w;
             }
         }
@@ -176,25 +201,30 @@ __device__ __forceinline__ void tile_gemv4(const __nv_bfloat16* w, int nr, const
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[i][r] = warp_sum(acc[i][r]);
+        for (int r = 0; r < R; ++r) {
+            const float v = warp_sum(acc[i][r]);
+            if (lane == i * R + r) out[lane] = v;
+        }
+    __syncwarp();
 }
 
-// fp32 rows (router): same mapping, float4 weight loads.
+// fp32 rows (router), two rows per tile; same element mapping, float4 weight loads.
 template <int R>
-__device__ __forceinline__ void tile_gemv_f32(const float* w, int nr, const float* const* xr, float (&acc)[2][R]) {
+__device__ __noinline__ void tile_gemv_f32(const float* w, int nr, const float* xbase, const int* xoff, float* out) {
     const int lane = threadIdx.x & 31;
+    float acc[2][R];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int r = 0; r < R; ++r) acc[i][r] = 0.f;
-#pragma unroll
+#pragma unroll 1
     for (int seg = 0; seg < 4; ++seg) {
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int k = seg * 256 + j * 128 + lane * 4;
             float4 xv[R];
 #pragma unroll
-            for (int r = 0; r < R; ++r) xv[r] = *reinterpret_cast<const float4*>(xr[r] + k);
+            for (int r = 0; r < R; ++r) xv[r] = *reinterpret_cast<const float4*>(xbase + xoff[r] + k);
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 if (i < nr) {
@@ -209,7 +239,11 @@ __device__ __forceinline__ void tile_gemv_f32(const float* w, int nr, const floa
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[i][r] = warp_sum(acc[i][r]);
+        for (int r = 0; r < R; ++r) {
+            const float v = warp_sum(acc[i][r]);
+            if (lane == i * R + r) out[lane] = v;
+        }
+    __syncwarp();
 }
 
 // ------------------------------------------------------------------ grid barrier (consumers)
@@ -224,6 +258,7 @@ __device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsign
         if (ld_acquire_gpu(a.bar) < target) {
             const unsigned long long t0 = globaltimer();
             while (ld_acquire_gpu(a.bar) < target) {
+                __nanosleep(20);
                 if (globaltimer() - t0 > WAIT_NS || *(volatile int*)a.err) { ok = false; break; }
             }
         }
@@ -256,9 +291,54 @@ __device__ __forceinline__ void norm_rows(const float* src, const float* w, floa
 }
 
 // ------------------------------------------------------------------ attention item
+// Chunk of keys per attention item: 32 keys when the span is short (more items than CTAs
+// would otherwise sit idle), 64 keys for longer spans.
+__device__ __forceinline__ int attn_chunk(int span) { return span <= 32 * 37 ? 32 : 64; }
+
+// Copy n floats global -> shared with 16-byte loads, all issued before the stores.
+__device__ __forceinline__ void copy_g2s(float* __restrict__ dst, const float* __restrict__ src, int n) {
+    const int tid = threadIdx.x - 32;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    const int n4 = n >> 2;
+    int i = tid;
+    for (; i + 3 * MEGA_NCT < n4; i += 4 * MEGA_NCT) {
+        const float4 a0 = __ldcg(s4 + i), a1 = __ldcg(s4 + i + MEGA_NCT), a2 = __ldcg(s4 + i + 2 * MEGA_NCT),
+                     a3 = __ldcg(s4 + i + 3 * MEGA_NCT);
+        d4[i] = a0;
+        d4[i + MEGA_NCT] = a1;
+        d4[i + 2 * MEGA_NCT] = a2;
+        d4[i + 3 * MEGA_NCT] = a3;
+    }
+    for (; i < n4; i += MEGA_NCT) d4[i] = __ldcg(s4 + i);
+}
+
+template <typename KVT>
+__device__ __forceinline__ void load_kv_row16(const KVT* p, int part, float* dst);   // 16 bytes of a K/V row
+
+template <>
+__device__ __forceinline__ void load_kv_row16<__nv_bfloat16>(const __nv_bfloat16* p, int part, float* dst) {
+    // part 0..7: 8 bf16
+    const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p) + part);
+    float f[8];
+    bf16x8_to_f32(u, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[part * 8 + i] = f[i];
+}
+
+template <>
+__device__ __forceinline__ void load_kv_row16<float>(const float* p, int part, float* dst) {
+    // part 0..15: 4 floats
+    const float4 u = __ldcg(reinterpret_cast<const float4*>(p) + part);
+    dst[part * 4 + 0] = u.x;
+    dst[part * 4 + 1] = u.y;
+    dst[part * 4 + 2] = u.z;
+    dst[part * 4 + 3] = u.w;
+}
+
 template <int R, typename KVT>
-__device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr, int g, int c, int nch,
-                          int& vres_dummy) {
+__device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr, int g, int c, int nch,
+                                       int chunk, bool first) {
     const int tid = threadIdx.x - 32;   // consumer thread 0..479
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
     const bool local = is_local_layer(l);
@@ -266,8 +346,9 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
     const int slot = a.rows[r0].x;
     const int pos0 = a.rows[r0].y, posL = a.rows[r0 + nr - 1].y;
     const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
-    const int k0 = lo + c * MEGA_CHUNK;
-    const int k1 = min(k0 + MEGA_CHUNK, posL + 1);
+    const int k0 = lo + c * chunk;
+    const int k1 = min(k0 + chunk, posL + 1);
+    const int nk = k1 - k0;
     float* qs = s->xs;                                   // [nr*4][64]
     float* Ks = qs + MEGA_RMAX * GQA * DH;               // [64][65]
     float* Vs = Ks + MEGA_CHUNK * (DH + 1);              // [64][65]
@@ -275,31 +356,52 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
     const float* cos_t = local ? a.cos_l : a.cos_g;
     const float* sin_t = local ? a.sin_l : a.sin_g;
     const int nq = nr * GQA;
-    // 1) queries of heads 4g..4g+3 for the block rows
-    for (int qi = cw; qi < nq; qi += MEGA_NCW) {
-        const int rr = qi / GQA, h = g * GQA + qi % GQA;
-        const int pos = a.rows[r0 + rr].y;
-        const float* src = a.qkv + (int64_t)(r0 + rr) * QKV + h * DH;
-        const float x1 = __ldcg(src + lane), x2 = __ldcg(src + lane + 32);
-        const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + a.eps);
-        const float* qw = a.qn[l] + h * DH;
-        const float q1 = qw[lane] * (x1 * inv), q2 = qw[lane + 32] * (x2 * inv);
-        const float cs = cos_t[(int64_t)pos * 32 + lane], sn = sin_t[(int64_t)pos * 32 + lane];
-        float y1 = q1 * cs - q2 * sn, y2 = q2 * cs + q1 * sn;
-        if (!local && pos + 1 > a.base_seq_len) {
-            const double b = (double)a.base_seq_len;
-            const float sc = (float)(1.0 + 0.1 * log(fmax((double)(pos + 1), b) / b));
-            y1 *= sc;
-            y2 *= sc;
+    astamp(a, l, 0, first);
+    // 1) cached keys/values of the chunk: every thread issues its 16-byte loads at once
+    {
+        constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
+        const int nold = max(0, min(k1, pos0) - k0);          // keys < pos0 come from the cache
+        for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
+            const int isv = e >= nold * PARTS;
+            const int ee = isv ? e - nold * PARTS : e;
+            const int kk = ee / PARTS, part = ee % PARTS;
+            const KVT* row = isv ? kv_v<KVT>(L, slot, g, k0 + kk) : kv_k<KVT>(L, slot, g, k0 + kk);
+            load_kv_row16<KVT>(row, part, (isv ? Vs : Ks) + kk * (DH + 1));
         }
-        qs[qi * DH + lane] = y1 * 0.125f;
-        qs[qi * DH + lane + 32] = y2 * 0.125f;
+        // rows past the end of a partial chunk: zeros (probabilities are 0 there; 0 * stale
+        // shared memory could be NaN)
+        for (int e = tid; e < (MEGA_CHUNK - nk) * DH; e += MEGA_NCT) {
+            const int kk = nk + e / DH, d = e % DH;
+            Ks[kk * (DH + 1) + d] = 0.f;
+            Vs[kk * (DH + 1) + d] = 0.f;
+        }
     }
-    // 2) keys / values of the chunk: block rows are produced here, older keys come from the cache
+    astamp(a, l, 1, first);
+    // 2) queries of heads 4g..4g+3 (warps), and the block rows' own keys/values (produced here)
     const int vres_mode = (a.pulse == 0) ? (l == 0 ? 1 : 2) : 0;
-    for (int kk = cw; kk < k1 - k0; kk += MEGA_NCW) {
-        const int key = k0 + kk;
-        if (key >= pos0) {
+    const int nnew = max(0, k1 - max(k0, pos0));
+    for (int it = cw; it < nq + nnew; it += MEGA_NCW) {
+        if (it < nq) {
+            const int rr = it / GQA, h = g * GQA + it % GQA;
+            const int pos = a.rows[r0 + rr].y;
+            const float* src = a.qkv + (int64_t)(r0 + rr) * QKV + h * DH;
+            const float x1 = __ldcg(src + lane), x2 = __ldcg(src + lane + 32);
+            const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + a.eps);
+            const float* qw = a.qn[l] + h * DH;
+            const float q1 = qw[lane] * (x1 * inv), q2 = qw[lane + 32] * (x2 * inv);
+            const float cs = cos_t[(int64_t)pos * 32 + lane], sn = sin_t[(int64_t)pos * 32 + lane];
+            float y1 = q1 * cs - q2 * sn, y2 = q2 * cs + q1 * sn;
+            if (!local && pos + 1 > a.base_seq_len) {
+                const double b = (double)a.base_seq_len;
+                const float sc = (float)(1.0 + 0.1 * log(fmax((double)(pos + 1), b) / b));
+                y1 *= sc;
+                y2 *= sc;
+            }
+            qs[it * DH + lane] = y1 * 0.125f;
+            qs[it * DH + lane + 32] = y2 * 0.125f;
+        } else {
+            const int key = max(k0, pos0) + (it - nq);
+            const int kk = key - k0;
             const int rr = r0 + (key - pos0);
             const float* src = a.qkv + (int64_t)rr * QKV;
             const float e1 = __ldcg(src + H * DH + g * DH + lane), e2 = __ldcg(src + H * DH + g * DH + lane + 32);
@@ -325,29 +427,15 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
             kv_store(kp + lane + 32, y2);
             kv_store(vp + lane, v1);
             kv_store(vp + lane + 32, v2);
-            // use the stored (rounded) values so every reader sees identical keys
-            Ks[kk * (DH + 1) + lane] = kv_load(kp + lane);
-            Ks[kk * (DH + 1) + lane + 32] = kv_load(kp + lane + 32);
-            Vs[kk * (DH + 1) + lane] = kv_load(vp + lane);
-            Vs[kk * (DH + 1) + lane + 32] = kv_load(vp + lane + 32);
-        } else {
-            const KVT* kp = kv_k<KVT>(L, slot, g, key);
-            const KVT* vp = kv_v<KVT>(L, slot, g, key);
+            // the stored (rounded) values, so every reader sees identical keys
             Ks[kk * (DH + 1) + lane] = kv_load(kp + lane);
             Ks[kk * (DH + 1) + lane + 32] = kv_load(kp + lane + 32);
             Vs[kk * (DH + 1) + lane] = kv_load(vp + lane);
             Vs[kk * (DH + 1) + lane + 32] = kv_load(vp + lane + 32);
         }
     }
-    // rows past the end of a partial chunk: zeros (their probabilities are 0, and 0 * stale
-    // shared memory could be NaN)
-    for (int kk = (k1 - k0) + cw; kk < MEGA_CHUNK; kk += MEGA_NCW) {
-        Ks[kk * (DH + 1) + lane] = 0.f;
-        Ks[kk * (DH + 1) + lane + 32] = 0.f;
-        Vs[kk * (DH + 1) + lane] = 0.f;
-        Vs[kk * (DH + 1) + lane + 32] = 0.f;
-    }
     named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 2, first);
     // 3) scores with per-row masks [lo_r, pos_r]
     for (int e = tid; e < nq * MEGA_CHUNK; e += MEGA_NCT) {
         const int qi = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
@@ -355,7 +443,7 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
         const int pos = a.rows[r0 + qi / GQA].y;
         const int lor = local ? max(0, pos - WINDOW + 1) : 0;
         float sc = -INFINITY;
-        if (key < k1 && key <= pos && key >= lor) {
+        if (kk < nk && key <= pos && key >= lor) {
             sc = 0.f;
             const float* qv = qs + qi * DH;
             const float* kv = Ks + kk * (DH + 1);
@@ -365,6 +453,7 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
         Ps[qi * MEGA_CHUNK + kk] = sc;
     }
     named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 3, first);
     // 4) partial softmax and P.V per query
     for (int qi = cw; qi < nq; qi += MEGA_NCW) {
         const int rr = qi / GQA, h = g * GQA + qi % GQA;
@@ -379,6 +468,7 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
         const float e1 = (p1 == -INFINITY) ? 0.f : expf(p1 - m);
         const float lsum = warp_sum(e0 + e1);
         float o1 = 0.f, o2 = 0.f;
+#pragma unroll 8
         for (int j = 0; j < 32; ++j) {
             const float pa = __shfl_sync(0xffffffffu, e0, j);
             const float pb = __shfl_sync(0xffffffffu, e1, j);
@@ -389,9 +479,11 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
         out[2 + lane] = o1;
         out[2 + lane + 32] = o2;
     }
-    // 5) the last chunk item of (block, g) combines and gates
+    // 5) the last chunk item of (block, g) combines (fixed chunk order) and gates
+    astamp(a, l, 4, first);
     __threadfence();
     named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 5, first);
     if (threadIdx.x == 32) {
         const unsigned t = atomicAdd(&a.tickets[r0 * HKV + g], 1u);
         s->ticket = (t == (unsigned)(nch - 1));
@@ -399,20 +491,59 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
         __threadfence();
     }
     named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 6, first);
     if (s->ticket) {
-        for (int qi = cw; qi < nq; qi += MEGA_NCW) {
+        // W warps per query split the chunks; partials (M, L, o[64]) merged in shared memory
+        const int W = max(1, MEGA_NCW / nq);
+        float* cm = Ps;                                  // [nq*W][66] partial merges (reuses Ps/Ks)
+        for (int wi = cw; wi < nq * W; wi += MEGA_NCW) {
+            const int qi = wi / W, part_w = wi % W;
             const int rr = qi / GQA, h = g * GQA + qi % GQA;
             const float* pp = a.part + ((int64_t)(r0 + rr) * H + h) * a.nch_max * PART;
-            float M = -INFINITY;
-            for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(pp + cc * PART));
+            const int c_lo = (nch * part_w) / W, c_hi = (nch * (part_w + 1)) / W;
+            float mloc = -INFINITY;
+            for (int cc = c_lo + lane; cc < c_hi; cc += 32) mloc = fmaxf(mloc, __ldcg(pp + cc * PART));
+            const float M = warp_max(mloc);
             float Ls = 0.f, o1 = 0.f, o2 = 0.f;
-            for (int cc = 0; cc < nch; ++cc) {
-                const float mc = __ldcg(pp + cc * PART);
-                if (mc == -INFINITY) continue;
-                const float wgt = expf(mc - M);
-                Ls += wgt * __ldcg(pp + cc * PART + 1);
-                o1 += wgt * __ldcg(pp + cc * PART + 2 + lane);
-                o2 += wgt * __ldcg(pp + cc * PART + 2 + lane + 32);
+            for (int c0 = c_lo; c0 < c_hi; c0 += 8) {
+                float mc[8], lc[8], a1[8], a2[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int cc = min(c0 + u, c_hi - 1);
+                    mc[u] = __ldcg(pp + cc * PART);
+                    lc[u] = __ldcg(pp + cc * PART + 1);
+                    a1[u] = __ldcg(pp + cc * PART + 2 + lane);
+                    a2[u] = __ldcg(pp + cc * PART + 2 + lane + 32);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (c0 + u < c_hi && mc[u] != -INFINITY) {
+                        const float wgt = expf(mc[u] - M);
+                        Ls += wgt * lc[u];
+                        o1 += wgt * a1[u];
+                        o2 += wgt * a2[u];
+                    }
+                }
+            }
+            float* dst = cm + wi * PART;
+            if (lane == 0) { dst[0] = M; dst[1] = Ls; }
+            dst[2 + lane] = o1;
+            dst[2 + lane + 32] = o2;
+        }
+        named_bar_sync(1, MEGA_NCT);
+        for (int qi = cw; qi < nq; qi += MEGA_NCW) {
+            const int rr = qi / GQA, h = g * GQA + qi % GQA;
+            const float* src = cm + qi * W * PART;
+            float M = -INFINITY;
+            for (int w = 0; w < W; ++w) M = fmaxf(M, src[w * PART]);
+            float Ls = 0.f, o1 = 0.f, o2 = 0.f;
+            for (int w = 0; w < W; ++w) {
+                const float mw = src[w * PART];
+                if (mw == -INFINITY) continue;
+                const float wgt = expf(mw - M);
+                Ls += wgt * src[w * PART + 1];
+                o1 += wgt * src[w * PART + 2 + lane];
+                o2 += wgt * src[w * PART + 2 + lane + 32];
             }
             const float gt = sigmoidf_(__ldcg(a.gate + (r0 + rr) * H + h));
             const float inv = 1.f / Ls;
@@ -421,11 +552,12 @@ __device__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr,
         }
     }
     named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 7, first);
 }
 
 // ------------------------------------------------------------------ the pulse
 template <int R, typename KVT>
-__global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a) {
+__global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     MegaSmem* s = reinterpret_cast<MegaSmem*>(smem_raw);
     const int C = gridDim.x, cta = blockIdx.x;
@@ -449,6 +581,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
             int r0, r1;
             rows_split(QKV, cta, C, r0, r1);
             produce_rows(g, a.wqkv[l], D * 2, r0, r1, 4);
+            if (cta < H / 2) produce_rows(g, a.gate_w[l], D * 4, 2 * cta, 2 * cta + 2, 2);
             rows_split(D, cta, C, r0, r1);
             produce_rows(g, a.wo[l], D * 2, r0, r1, 4);
             produce_rows(g, a.router[l], D * 4, 0, E, 2);
@@ -459,8 +592,11 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
                 produce_rows(g, a.sh_gu[l], D * 2, DS + j0, DS + j1, 4);
             }
             // routed pairs depend on this layer's router
+            // sleep between polls: a tight spin on shared memory starves the consumers' loads
             const unsigned long long t0 = globaltimer();
             while (s->moe_ready != l + 1) {
+                __nanosleep(200);
+                if (s->moe_ready == l + 1) break;
                 if (globaltimer() - t0 > WAIT_NS || *(volatile int*)a.err || s->abort) { g.ok = false; break; }
             }
             if (!g.ok) break;
@@ -494,9 +630,11 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
 
     // ================================================================ consumers
     const int cw = warp - 1;
+    if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE] = globaltimer();
     Ring g{s, 0u, cw, true};
     unsigned epoch = 0;
     float* xs = s->xs;
+    float* wo_ = s->wout[cw];   // this warp's reduced tile sums
     const float eps = a.eps;
     const int p = a.pulse;
     // ---- pulse input: every CTA builds h_in for all rows in xs[0 .. R*D) ----
@@ -568,11 +706,23 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
             a.h[i] = xs[i];
         }
     named_bar_sync(1, MEGA_NCT);
+    // sequence blocks of the rows (consecutive rows of one slot), for the attention items
+    if (threadIdx.x == 32) {
+        int nb = 0, r0 = 0;
+        while (r0 < R) {
+            int nr = 1;
+            while (r0 + nr < R && a.rows[r0 + nr].x == a.rows[r0].x) ++nr;
+            s->blk_r0[nb++] = r0;
+            r0 += nr;
+        }
+        s->blk_r0[nb] = R;
+        s->n_blk = nb;
+    }
     // xs holds h_in; layer 0's attention norm reads it from xs, later layers from a.h
     for (int l = 0; l < NL; ++l) {
+        const bool local = is_local_layer(l);
         // ---------------- phase A: xn, QKV, gate logits
         {
-            const float* src = (l == 0) ? nullptr : a.h;
             if (l == 0) {
                 // normalise in place (each warp owns its rows)
                 for (int r = cw; r < R; r += MEGA_NCW) {
@@ -588,92 +738,85 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
                     for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = a.attn_norm[l][i * 32 + lane] * (v[i] * inv);
                 }
             } else {
-                norm_rows<R>(src, a.attn_norm[l], eps, xs);
+                norm_rows<R>(a.h, a.attn_norm[l], eps, xs);
+            }
+            if (threadIdx.x - 32 < R) s->xoff[threadIdx.x - 32] = (threadIdx.x - 32) * D;
+            // attention chunking of each block (used in phase B)
+            if (threadIdx.x == 33) {
+                for (int b = 0; b < s->n_blk; ++b) {
+                    const int pos0 = a.rows[s->blk_r0[b]].y, posL = a.rows[s->blk_r0[b + 1] - 1].y;
+                    const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
+                    const int chunk = attn_chunk(posL - lo + 1);
+                    s->blk_chunk[b] = chunk;
+                    s->blk_nch[b] = (posL - lo + chunk) / chunk;
+                }
             }
             named_bar_sync(1, MEGA_NCT);
-            const float* xr[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
+            stamp(a, l, 0);
             int r0, r1;
             rows_split(QKV, cta, C, r0, r1);
             consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
-                float acc[4][R];
-                tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        if (lane == i * R + r && i < n) a.qkv[(int64_t)r * QKV + row0 + i] = acc[i][r];
+                tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                if (lane < n * R) a.qkv[(int64_t)(lane % R) * QKV + row0 + lane / R] = wo_[lane];
             });
-            if (cta < H) {
-                const int h = cta;
-                for (int r = cw; r < R; r += MEGA_NCW) {
-                    float z = 0.f;
-                    for (int k = lane; k < D; k += 32) z += a.gate_w[l][h * D + k] * xs[r * D + k];
-                    z = warp_sum(z);
-                    if (lane == 0) a.gate[r * H + h] = z + a.gate_b[l][h];
-                }
-            }
+            stamp(a, l, 1);
+            if (cta < H / 2)
+                consume_rows(g, 2 * cta, 2 * cta + 2, 2, [&](const unsigned char* tile, int row0, int n) {
+                    tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xs, s->xoff, wo_);
+                    if (lane < n * R) {
+                        const int h = row0 + lane / R;
+                        a.gate[(lane % R) * H + h] = wo_[lane] + a.gate_b[l][h];
+                    }
+                });
+            stamp(a, l, 2);
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 3);
         }
-        // ---------------- phase B: attention
+        // ---------------- phase B: attention (items owned by this CTA: cta, cta + C, ...)
         {
-            const bool local = is_local_layer(l);
-            int item = 0;
-            int r0 = 0;
-            while (r0 < R) {
-                int nr = 1;
-                while (r0 + nr < R && a.rows[r0 + nr].x == a.rows[r0].x) ++nr;
-                const int pos0 = a.rows[r0].y, posL = a.rows[r0 + nr - 1].y;
-                const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
-                const int nch = (posL - lo + MEGA_CHUNK) / MEGA_CHUNK;
-                for (int gg = 0; gg < HKV; ++gg)
-                    for (int c = 0; c < nch; ++c, ++item)
-                        if (item % C == cta) {
-                            int dummy = 0;
-                            attn_item<R, KVT>(a, s, l, r0, nr, gg, c, nch, dummy);
-                        }
-                r0 += nr;
+            int total = 0;
+            for (int b = 0; b < s->n_blk; ++b) total += HKV * s->blk_nch[b];
+            bool first = true;
+            for (int item = cta; item < total; item += C) {
+                int b = 0, rem = item;
+                while (rem >= HKV * s->blk_nch[b]) { rem -= HKV * s->blk_nch[b]; ++b; }
+                const int nch = s->blk_nch[b];
+                const int r0 = s->blk_r0[b], nr = s->blk_r0[b + 1] - r0;
+                attn_item<R, KVT>(a, s, l, r0, nr, rem / nch, rem % nch, nch, s->blk_chunk[b], first);
+                first = false;
             }
+            stamp(a, l, 4);
             if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 5);
         }
         // ---------------- phase C: Wo, h += (owned rows)
         {
-            for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT) xs[i] = __ldcg(a.att + i);
+            copy_g2s(xs, a.att, R * D);
             named_bar_sync(1, MEGA_NCT);
-            const float* xr[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
+            stamp(a, l, 6);
             int r0, r1;
             rows_split(D, cta, C, r0, r1);
             consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
-                float acc[4][R];
-                tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        if (lane == i * R + r && i < n) a.h[(int64_t)r * D + row0 + i] = __ldcg(a.h + (int64_t)r * D + row0 + i) + acc[i][r];
+                tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                if (lane < n * R) {
+                    float* hp = a.h + (int64_t)(lane % R) * D + row0 + lane / R;
+                    *hp = __ldcg(hp) + wo_[lane];
+                }
             });
+            stamp(a, l, 7);
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 8);
         }
         // ---------------- phase D: router, shared + routed up-projections
         {
             norm_rows<R>(a.h, a.mlp_norm[l], eps, xs);
             named_bar_sync(1, MEGA_NCT);
-            const float* xr[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
+            stamp(a, l, 9);
             consume_rows(g, 0, E, 2, [&](const unsigned char* tile, int row0, int n) {
-                float acc[2][R];
-                tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xr, acc);
-#pragma unroll
-                for (int i = 0; i < 2; ++i)
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        if (lane == i * R + r && i < n) s->logits[r][row0 + i] = acc[i][r];
+                tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xs, s->xoff, wo_);
+                if (lane < n * R) s->logits[lane % R][row0 + lane / R] = wo_[lane];
             });
             named_bar_sync(1, MEGA_NCT);
             if (cw == 0) {
@@ -713,11 +856,20 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
                     for (int e = 0; e < E; ++e)
                         if (used & (1 << e)) s->elist[n++] = e;
                     s->n_e = n;
+                    // phase E: X row of each row for every routed expert (act_r row or none)
+                    for (int ei = 0; ei < n; ++ei)
+                        for (int r = 0; r < R; ++r) {
+                            int off = -1;
+                            for (int k = 0; k < TOPK; ++k)
+                                if (s->idx[r][k] == s->elist[ei]) off = R * DS + (r * TOPK + k) * DE;
+                            s->xoff_e[ei][r] = off;
+                        }
                     __threadfence_block();
                     s->moe_ready = l + 1;
                 }
             }
             named_bar_sync(1, MEGA_NCT);
+            stamp(a, l, 10);
             const int n_e = s->n_e;
             int s0, s1, q0, q1;
             rows_split(DS, cta, C, s0, s1);          // shared pairs [s0, s1)
@@ -725,51 +877,29 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
             const int nsh = s1 - s0;
             float* st_g = s->stage;                         // [pair][R] gate: shared pairs, then routed
             float* st_u = s->stage + MEGA_MAXPAIRS * R;     // [pair][R] up
-            {
-                const int j0 = s0, j1 = s1;
-                consume_rows(g, j0, j1, 4, [&](const unsigned char* tile, int row0, int n) {
-                    float acc[4][R];
-                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-#pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            if (lane == i * R + r && i < n) st_g[(row0 + i - s0) * R + r] = acc[i][r];
-                });
-                consume_rows(g, DS + j0, DS + j1, 4, [&](const unsigned char* tile, int row0, int n) {
-                    float acc[4][R];
-                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-#pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            if (lane == i * R + r && i < n) st_u[(row0 - DS + i - s0) * R + r] = acc[i][r];
-                });
-            }
+            consume_rows(g, s0, s1, 4, [&](const unsigned char* tile, int row0, int n) {
+                tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                if (lane < n * R) st_g[(row0 - s0 + lane / R) * R + lane % R] = wo_[lane];
+            });
+            consume_rows(g, DS + s0, DS + s1, 4, [&](const unsigned char* tile, int row0, int n) {
+                tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                if (lane < n * R) st_u[(row0 - DS - s0 + lane / R) * R + lane % R] = wo_[lane];
+            });
             for (int ei = 0; ei < n_e; ++ei) {
                 const int b0 = ei * DE;
                 const int j0 = max(q0, b0) - b0, j1 = min(q1, b0 + DE) - b0;
                 if (j1 <= j0) continue;
                 const int base = nsh + b0 - q0;   // stage index = base + j
                 consume_rows(g, j0, j1, 4, [&](const unsigned char* tile, int row0, int n) {
-                    float acc[4][R];
-                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-#pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            if (lane == i * R + r && i < n) st_g[(base + row0 + i) * R + r] = acc[i][r];
+                    tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                    if (lane < n * R) st_g[(base + row0 + lane / R) * R + lane % R] = wo_[lane];
                 });
                 consume_rows(g, DE + j0, DE + j1, 4, [&](const unsigned char* tile, int row0, int n) {
-                    float acc[4][R];
-                    tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-#pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            if (lane == i * R + r && i < n) st_u[(base + row0 - DE + i) * R + r] = acc[i][r];
+                    tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                    if (lane < n * R) st_u[(base + row0 - DE + lane / R) * R + lane % R] = wo_[lane];
                 });
             }
+            stamp(a, l, 11);
             named_bar_sync(1, MEGA_NCT);
             // SwiGLU epilogue -> act_sh [R][1024], act_r [R][4][512]
             for (int e = threadIdx.x - 32; e < (nsh + q1 - q0) * R; e += MEGA_NCT) {
@@ -786,57 +916,36 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
                         if (s->idx[r][k] == ex) a.act_r[((int64_t)r * TOPK + k) * DE + j] = v;
                 }
             }
+            stamp(a, l, 12);
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 13);
         }
         // ---------------- phase E: down projections + combine, h += (owned rows)
         {
-            for (int i = threadIdx.x - 32; i < R * DS; i += MEGA_NCT) xs[i] = __ldcg(a.act_sh + i);
-            float* xa = xs + R * DS;
-            for (int i = threadIdx.x - 32; i < R * TOPK * DE; i += MEGA_NCT) xa[i] = __ldcg(a.act_r + i);
+            copy_g2s(xs, a.act_sh, R * DS);
+            copy_g2s(xs + R * DS, a.act_r, R * TOPK * DE);
             named_bar_sync(1, MEGA_NCT);
+            stamp(a, l, 14);
             const int n_e = s->n_e;
             int o0, o1;
             rows_split(D, cta, C, o0, o1);
             float* dsh = s->stage;                                   // [orow][R]
             float* dex = s->stage + MEGA_MAXOROWS * R;               // [orow][ei][R]
-            {
-                const float* xr[R];
-#pragma unroll
-                for (int r = 0; r < R; ++r) xr[r] = xs + r * DS;
-                consume_rows(g, o0, o1, 4, [&](const unsigned char* tile, int row0, int n) {
-                    float acc[4][R];
-                    tile_gemv4<R, DS>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-#pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            if (lane == i * R + r && i < n) dsh[(row0 + i - o0) * R + r] = acc[i][r];
-                });
-            }
+            consume_rows(g, o0, o1, 4, [&](const unsigned char* tile, int row0, int n) {
+                tile_gemv<R, DS>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                if (lane < n * R) dsh[(row0 - o0 + lane / R) * R + lane % R] = wo_[lane];
+            });
             for (int ei = 0; ei < n_e; ++ei) {
-                const int ex = s->elist[ei];
-                const float* xr[R];
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    xr[r] = nullptr;
-#pragma unroll
-                    for (int k = 0; k < TOPK; ++k)
-                        if (s->idx[r][k] == ex) xr[r] = xa + (r * TOPK + k) * DE;
-                }
                 consume_rows(g, o0, o1, 8, [&](const unsigned char* tile, int row0, int n) {
                     const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(tile);
                     for (int half = 0; half < 2; ++half) {
                         const int nn = min(4, n - half * 4);
                         if (nn <= 0) break;
-                        float acc[4][R];
-                        tile_gemv4<R, DE>(w + half * 4 * DE, nn, xr, acc);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-#pragma unroll
-                            for (int r = 0; r < R; ++r)
-                                if (lane == i * R + r && i < nn)
-                                    dex[((row0 + half * 4 + i - o0) * E + ei) * R + r] = acc[i][r];
+                        tile_gemv<R, DE>(w + half * 4 * DE, nn, xs, s->xoff_e[ei], wo_);
+                        if (lane < nn * R)
+                            dex[((row0 + half * 4 - o0 + lane / R) * E + ei) * R + lane % R] = wo_[lane];
+                        __syncwarp();
                     }
                 });
             }
@@ -857,6 +966,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
             }
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 15);
         }
     }
     // ---------------- end of pulse + LM head
@@ -877,27 +987,26 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
             for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = a.fnorm[i * 32 + lane] * (v[i] * inv);
         }
         named_bar_sync(1, MEGA_NCT);
-        const float* xr[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) xr[r] = xs + r * D;
         ArgMax best[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) best[r] = ArgMax{-INFINITY, 1 << 30};
         int v0, v1;
         rows_split(a.V, cta, C, v0, v1);
         consume_rows(g, v0, v1, 4, [&](const unsigned char* tile, int row0, int n) {
-            float acc[4][R];
-            tile_gemv4<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xr, acc);
+            tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+            // lane i*R + r holds row i of the tile for output row r
+            float y = -INFINITY;
+            if (lane < n * R) {
+                y = wo_[lane];
+                if (a.softcap > 0.f) y = a.softcap * tanhf(y / a.softcap);
+                if (a.logits) a.logits[(int64_t)(lane % R) * a.V + row0 + lane / R] = y;
+            }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                if (i < n) {
+            for (int r = 0; r < R; ++r) {
 #pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        float y = acc[i][r];
-                        if (a.softcap > 0.f) y = a.softcap * tanhf(y / a.softcap);
-                        if (a.logits && lane == i * R + r) a.logits[(int64_t)r * a.V + row0 + i] = y;
-                        best[r] = argmax_merge(best[r], ArgMax{y, row0 + i});
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    const float yi = __shfl_sync(0xffffffffu, y, (i * R + r) & 31);
+                    if (i < n) best[r] = argmax_merge(best[r], ArgMax{yi, row0 + i});
                 }
             }
         });
@@ -936,6 +1045,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const MegaArgs a
             }
         }
         if (!g.ok) atomicExch(a.err, 1);
+        if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
     }
 done:
     return;

@@ -61,6 +61,7 @@ PROTOTYPES = {
                                               C.POINTER(c_int64), c_void_p]),
     "pulsar_engine_set_option": (c_int, [c_void_p, c_char_p, c_int64]),
     "pulsar_engine_get_option": (c_int, [c_void_p, c_char_p, C.POINTER(c_int64)]),
+    "pulsar_engine_read_trace": (c_int, [c_void_p, c_void_p, c_int64]),
 }
 
 

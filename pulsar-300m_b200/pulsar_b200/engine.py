@@ -136,6 +136,14 @@ class DeviceEngine:
         _lib.check(_lib.load().pulsar_engine_get_option(self._h, name.encode(), C.byref(v)), f"get_option({name})")
         return int(v.value)
 
+    def read_trace(self):
+        """Phase stamps of the last persistent-kernel launch: uint64 [grid, 256] (ns)."""
+        import numpy as np
+        n = self.get_option("megakernel_grid") * 256
+        buf = (C.c_uint64 * n)()
+        _lib.check(_lib.load().pulsar_engine_read_trace(self._h, C.cast(buf, C.c_void_p), n), "read_trace")
+        return np.frombuffer(buf, dtype=np.uint64).reshape(-1, 256).copy()
+
     def memory(self) -> dict:
         a, k, w = C.c_int64(), C.c_int64(), C.c_int64()
         _lib.check(_lib.load().pulsar_engine_memory(self._h, C.byref(a), C.byref(k), C.byref(w)), "memory")
