@@ -67,6 +67,20 @@ int pulsar_op_moe_router_topk(const void* logits_dev, int logits_bf16, const flo
                               void* topk_weights_dev, float* z_loss_dev, float* probs_mean_dev,
                               float* workspace_dev, void* stream);
 
+/* No counterpart in the reference. The router top-k above without a caller workspace, for
+ * callers that cannot allocate device memory (a host whose memory manager owns every
+ * device byte, or a foreign-language caller without a device allocator): the scratch is a
+ * 4 MiB array compiled into the library, present on every GPU that loads it until exit.
+ * Limit: N * (E + 1) <= 1,048,576 floats, else PULSAR_ERR_CAPACITY. Allocates nothing.
+ * The first call on each device looks up the array's device address (with that device
+ * current); make that first call before any stream capture begins. All calls share the
+ * array: calls whose executions overlap on the GPU (for example on two streams) race.
+ * Nothing in it has to start at zero: each call writes every element it reads. */
+int pulsar_op_moe_router_topk_noalloc(const void* logits_dev, int logits_bf16, const float* expert_bias_dev,
+                                      int64_t N, int64_t E, int64_t K, float z_loss_weight,
+                                      int64_t* topk_idx_dev, void* topk_weights_dev, float* z_loss_dev,
+                                      float* probs_mean_dev, void* stream);
+
 /* csrc/kernels.cu:2716-2765 qk_rmsnorm_rope_forward_cuda (binding :229-230).
  * x: n_vec vectors of 64 bf16 with element strides (sB, sH, sT) over the logical
  * [B, n_heads, T, 64] index, vector v = ((b * n_heads) + h) * T + t; weight [n_heads, 64]

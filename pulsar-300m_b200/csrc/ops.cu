@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "capi_util.h"
 #include "common.cuh"
 
@@ -365,6 +367,75 @@ extern "C" int pulsar_op_moe_dispatch(const void* x, const int64_t* idx, const i
         k_moe_dispatch<<<grid_cap(N, 1), 128, 0, S(stream)>>>((const __nv_bfloat16*)x, idx, slot, N, (int)K, E, C, D,
                                                                (__nv_bfloat16*)ei);
         PULSAR_LAUNCH_CHECK("k_moe_dispatch");
+    }
+    return PULSAR_OK;
+}
+
+// ==================================================================================== no-allocation router
+// The router top-k below needs N * (E + 1) floats of scratch for its deterministic means. The
+// regular entry point takes that scratch from the caller. This variant serves callers that
+// cannot allocate device memory at all - a host whose memory manager owns every device byte
+// and rejects outside allocations, or a foreign-language caller with no device allocator of
+// its own - by using a fixed array compiled into the library instead. Every GPU that loads
+// the library holds this 4 MiB array until the process exits.
+static constexpr int64_t kRouterScratchFloats = int64_t(1) << 20;   // N * (E + 1) <= 1,048,576
+static __device__ __align__(256) float g_router_scratch[kRouterScratchFloats];
+
+namespace {
+constexpr int kMaxDevices = 64;
+float* g_router_scratch_ptr[kMaxDevices] = {};
+std::mutex g_router_scratch_mu;
+
+// Device address of g_router_scratch on the current device. Host code cannot use the
+// symbol's name as a device pointer, so the address is looked up once per device (with that
+// device current) and cached.
+int router_scratch(float** out) {
+    int dev = 0;
+    PULSAR_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("moe_router_topk_noalloc: device ordinal %d outside [0, %d)", dev, kMaxDevices);
+        return PULSAR_ERR_UNSUPPORTED;
+    }
+    std::lock_guard<std::mutex> lock(g_router_scratch_mu);
+    if (!g_router_scratch_ptr[dev]) {
+        void* p = nullptr;
+        PULSAR_TRY(cuda_status(cudaGetSymbolAddress(&p, g_router_scratch), "cudaGetSymbolAddress(router scratch)"));
+        g_router_scratch_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_router_scratch_ptr[dev];
+    return PULSAR_OK;
+}
+}  // namespace
+
+extern "C" int pulsar_op_moe_router_topk_noalloc(const void* logits, int logits_bf16, const float* bias, int64_t N,
+                                                 int64_t E, int64_t K, float zw, int64_t* idx, void* w,
+                                                 float* z_loss, float* probs_mean, void* stream) {
+    PULSAR_CHECK_ARG(E >= 1 && E <= 32, "moe_router_topk_forward_cuda supports E <= 32, got %lld", (long long)E);
+    PULSAR_CHECK_ARG(K > 0 && K <= 8 && K <= E, "top_k must be in [1, min(8, E)], got %lld", (long long)K);
+    PULSAR_CHECK_ARG(N >= 0, "moe_router_topk: N must be >= 0");
+    if (N * (E + 1) > kRouterScratchFloats) {
+        set_error("moe_router_topk_noalloc: N * (E + 1) = %lld exceeds the built-in scratch of %lld floats "
+                  "(use pulsar_op_moe_router_topk with a caller workspace)",
+                  (long long)(N * (E + 1)), (long long)kRouterScratchFloats);
+        return PULSAR_ERR_CAPACITY;
+    }
+    float* ws = nullptr;
+    PULSAR_TRY(router_scratch(&ws));
+    if (N > 0) {
+        PULSAR_CHECK_ARG(logits && bias && idx && w, "moe_router_topk: null pointer");
+        const int threads = 256;
+        const int grid = grid_cap(N, threads / 32);
+        if (logits_bf16)
+            k_router_topk<true><<<grid, threads, 0, S(stream)>>>(logits, bias, N, (int)E, (int)K, idx,
+                                                                 (__nv_bfloat16*)w, ws);
+        else
+            k_router_topk<false><<<grid, threads, 0, S(stream)>>>(logits, bias, N, (int)E, (int)K, idx,
+                                                                  (__nv_bfloat16*)w, ws);
+        PULSAR_LAUNCH_CHECK("k_router_topk");
+    }
+    if (z_loss || probs_mean) {
+        k_router_means<<<1, 256, 0, S(stream)>>>(ws, N, (int)E, zw, z_loss, probs_mean);
+        PULSAR_LAUNCH_CHECK("k_router_means");
     }
     return PULSAR_OK;
 }

@@ -39,6 +39,8 @@ PROTOTYPES = {
     "pulsar_op_swiglu": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "pulsar_op_moe_router_topk": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p,
                                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "pulsar_op_moe_router_topk_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64, c_float,
+                                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "pulsar_op_qk_rmsnorm_rope": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p,
                                           c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p]),
     "pulsar_op_attn_gate": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
