@@ -65,6 +65,101 @@ def kv_keys_for(L: int) -> int:
     return 6 * min(L, 1024) + 2 * L
 
 
+# The launches of one self-speculative round (gamma drafts): pulse index, rows, LM head. The
+# persistent kernel k_mega_pulse runs each of them as one launch.
+def round_shapes(gamma: int):
+    return [("draft_lm", 0, 1, True, gamma), ("draft_nolm", 0, 1, False, 1),
+            ("verify_p1", 1, gamma + 1, False, 1), ("verify_p2", 2, gamma + 1, True, 1)]
+
+
+PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "k_mega_pulse_decode_shapes.txt")
+
+
+def load_traffic():
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of each round shape,
+    from the committed ncu summary (lines 'traffic <shape> <bytes>'); None when absent."""
+    out = {}
+    try:
+        for line in open(PROFILE_TRAFFIC):
+            f = line.split()
+            if len(f) == 3 and f[0] == "traffic":
+                out[f[1]] = float(f[2])
+    except OSError:
+        return None
+    return out or None
+
+
+def shape_launches(eng, cfg, gamma: int, seed: int = 1):
+    """Buffers and a launcher for the round shapes through the C ABI (pulsar_engine_pulse), at
+    positions PROMPT.. of slot 0 (the prompt context). Returns {shape: launch()}."""
+    from pulsar_b200 import _lib
+    lib = _lib.load()
+    dev = eng.device
+    D, V, R = cfg.d_model, cfg.vocab_size, gamma + 1
+    g = torch.Generator().manual_seed(seed)
+    toks = torch.randint(0, V, (R,), generator=g)
+    rows = torch.tensor([[0, PROMPT + i, int(toks[i]), 0] for i in range(R)], dtype=torch.int32, device=dev)
+    h0, z0 = torch.empty(R, D, device=dev), torch.empty(R, D, device=dev)
+    h1, h2 = torch.empty(R, D, device=dev), torch.empty(R, D, device=dev)
+    zo = torch.empty(R, D, device=dev)
+    logits = torch.empty(R, V, device=dev)
+    st = eng.stream()
+
+    def call(p, n, hp, hz, out, lg):
+        _lib.check(lib.pulsar_engine_pulse(eng.handle, p, n, rows.data_ptr(), hp.data_ptr() if hp is not None else None,
+                                           hz.data_ptr() if hz is not None else None, out.data_ptr(),
+                                           zo.data_ptr() if p else z0.data_ptr(),
+                                           lg.data_ptr() if lg is not None else None, st), f"pulse({p})")
+
+    call(0, R, None, None, h0, None)      # pulse-0 states of the block (the drafts' outputs)
+    return {
+        "draft_lm": lambda: call(0, 1, None, None, h1, logits),
+        "draft_nolm": lambda: call(0, 1, None, None, h1, None),
+        "verify_p1": lambda: call(1, R, h0, z0, h1, None),
+        "verify_p2": lambda: call(2, R, h1, z0, h2, logits),
+    }
+
+
+def kernel_roofline(eng, cfg, gamma: int, recipe: str, reps: int, peak: float, peak_kind: str):
+    """Roofline of the dominant kernel (k_mega_pulse): each round shape launched `reps` times
+    through the C ABI on the bench's engine and context, each launch bracketed by CUDA events on
+    the launching stream (option time_pulses); achieved = the round's algorithmic bytes / the
+    round's summed mean launch times."""
+    eng.set_length(0, PROMPT)
+    launch = shape_launches(eng, cfg, gamma)
+    eng.set_option("time_pulses", 1)
+    for f in launch.values():          # warm-up
+        f()
+    torch.cuda.synchronize()
+    shapes, tot_b, tot_t, tot_n = {}, 0.0, 0.0, 0
+    d_verify = min(16.0, 4.0 * (gamma + 1)) if recipe == "B" else 4.0
+    for name, p, R, lm, n in round_shapes(gamma):
+        ts = []
+        for _ in range(reps):
+            launch[name]()
+            ts.append(eng.get_option("last_pulse_ns") * 1e-9)
+        t = statistics.mean(ts)
+        d = 4.0 if p == 0 else d_verify
+        b = bytes_per_pass(cfg, d, kv_keys_for(PROMPT + R), R, lm) + (R * cfg.vocab_size * 4 if lm else 0)
+        shapes[name] = {"rows": R, "lm_head": lm, "per_round": n, "us": t * 1e6, "bytes": b,
+                        "gbs": b / t / 1e9}
+        tot_b += n * b
+        tot_t += n * t
+        tot_n += n
+    eng.set_option("time_pulses", 0)
+    achieved = tot_b / tot_t / 1e9
+    traffic = load_traffic()
+    tr = None
+    if traffic and all(k in traffic for k in shapes):
+        tr = sum(shapes[k]["per_round"] * traffic[k] for k in shapes) / tot_n
+    return {"bound": "hbm", "kernel": "k_mega_pulse", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_kind": peak_kind, "traffic": tr,
+            "bytes_per_launch": tot_b / tot_n, "us_per_launch": tot_t / tot_n * 1e6,
+            "timing": f"CUDA events around each launch on its stream, mean of {reps} launches per shape, "
+                      "weighted by the launches of one round",
+            "shapes": shapes}
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -224,6 +319,8 @@ def run_engine(args):
     clk = Clocks(local)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stats = {"rounds": 0, "drafted": 0, "accepted": 0}
+    launches0 = eng.get_option("kernel_launches")
+    mega0 = eng.get_option("mega_launches")
     torch.cuda.synchronize()
     ev0.record(stream)
     for _ in range(args.steps):
@@ -233,6 +330,8 @@ def run_engine(args):
     ev1.record(stream)
     torch.cuda.synchronize()
     clocks = clk.stop()
+    gpu_launches = eng.get_option("kernel_launches") - launches0
+    mega_launches = eng.get_option("mega_launches") - mega0
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, world, local)
     tokens = NEW * args.steps * world
@@ -255,8 +354,9 @@ def run_engine(args):
             e2e_ms.append(e0.elapsed_time(e1))
     e2e_ms_max = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, local)
     e2e_value = NEW * world / (e2e_ms_max / 1e3)
-    # ---- roofline of the decode path (bytes per emitted token from the measured accept rate)
+    # ---- roofline of the dominant kernel, then of the whole decode path
     peak, peak_kind = load_peaks()
+    roof = kernel_roofline(eng, cfg, args.gamma, args.recipe, args.kernel_reps, peak, peak_kind)
     rounds = max(1, stats["rounds"])
     acc = stats["accepted"] / rounds
     L = PROMPT + NEW // 2
@@ -282,12 +382,13 @@ def run_engine(args):
             "tokens_per_round": acc + 1 if g > 0 else 1.0,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
                     "d2h_bytes_per_step": NEW * 4, "includes": "prompt H2D, prefill, decode, tokens D2H"},
-            "roofline": {"bound": "hbm", "scope": "whole decode path (all kernels of a round)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": None,
-                         "bytes_per_token": bytes_per_token},
+            "roofline": roof,
+            "path_roofline": {"scope": "whole decode path: algorithmic bytes per emitted token x tokens/s",
+                              "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                              "peak_kind": peak_kind, "bytes_per_token": bytes_per_token},
             "clocks": clocks,
-            "gpu_launches": None}
+            "gpu_launches": gpu_launches,
+            "mega_launches": mega_launches}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, sample = cpu_oracle_rate(args.cpu_tokens, PROMPT)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
@@ -297,6 +398,25 @@ def run_engine(args):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_kernel_shapes(args):
+    """The bench engine and prompt, then one launch of each round shape (after the pulse-0 block
+    pass that feeds the verify shapes): five k_mega_pulse launches in total."""
+    from pulsar_b200.config import PulsarConfig
+    from pulsar_b200.engine import DeviceEngine
+    from pulsar_b200.weights import make_state_dict, random_prompts
+    cfg = PulsarConfig(eos_token_id=-1)
+    eng = DeviceEngine(cfg, make_state_dict(cfg, recipe=args.recipe, seed=0), device=0, max_batch=1,
+                       max_seq_len=PROMPT + NEW + 64, max_prefill=PROMPT, kv_dtype=torch.bfloat16)
+    eng.prefill(0, random_prompts(1, PROMPT, cfg.vocab_size, seed=0)[0].tolist())
+    launch = shape_launches(eng, cfg, args.gamma)
+    for name, *_ in round_shapes(args.gamma):
+        launch[name]()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_shapes": [n for n, *_ in round_shapes(args.gamma)],
+                      "mega_launches": eng.get_option("mega_launches")}), flush=True)
+    eng.close()
 
 
 def main():
@@ -309,11 +429,16 @@ def main():
     ap.add_argument("--recipe", default="A", choices=["A", "B"])
     ap.add_argument("--cpu-tokens", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-reps", type=int, default=20)
+    ap.add_argument("--kernel-shapes", action="store_true",
+                    help="launch each round shape of k_mega_pulse once after the prefill and exit (ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.kernel_shapes:
+        run_kernel_shapes(args)
     else:
         run_engine(args)
 

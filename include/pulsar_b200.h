@@ -190,15 +190,24 @@ int pulsar_engine_generate_greedy(pulsar_engine* eng, int32_t n_seq, const int32
 /* Engine options. "megakernel" (0/1, default 1 when the GPU can co-schedule one CTA per
  * SM): run each pulse pass of <= 5 rows as one persistent kernel instead of per-op
  * kernels. Read-only: "megakernel_grid" (CTAs of the persistent kernel), "loop_adapter"
- * (1 when some loop-adapter lora_B is non-zero; such weights use the per-op kernels). */
+ * (1 when some loop-adapter lora_B is non-zero; such weights use the per-op kernels),
+ * "kernel_launches" (kernels started by generate_greedy and pulse since create, each kernel
+ * node of a replayed CUDA graph counted per replay), "mega_launches" (the persistent pulse
+ * kernels among them). "time_pulses" (0/1): record CUDA events on the caller's stream
+ * around every pulse pass launched outside stream capture; "last_pulse_ns" (read-only,
+ * waits for the last such pass) is the device time between those events. */
 int pulsar_engine_set_option(pulsar_engine* eng, const char* name, int64_t value);
 int pulsar_engine_get_option(pulsar_engine* eng, const char* name, int64_t* value);
 
 /* Phase tracing of the persistent pulse kernel (option "trace" = 1): every launch writes,
  * per CTA, 256 %globaltimer stamps in ns (entry 0: start; 1 + 16*l + j: point j of layer l,
  * j = 0 norm done, 1 QKV tiles, 2 gate, 3 barrier A left, 4 attention items, 5 barrier B left,
- * 6 attention output loaded, 7 Wo tiles, 8 barrier C left, 9 norm, 10 router, 11 up tiles,
- * 12 SwiGLU epilogue, 13 barrier D left, 14 activations loaded, 15 barrier E left; 254: end).
+ * 6 partials merged, 7 barrier B2 left, 8 Wo tiles and router partials, 9 barrier C left,
+ * 10 router logits, 11 up tiles, 12 SwiGLU epilogue, 13 barrier D left, 14 activations
+ * loaded, 15 barrier E left; 130 + 8*l + k: steps of the CTA's first attention item (k = 0
+ * start, 1 cached keys loaded, 2 queries and new keys, 3 scores, 4 P.V, 5 done); 194 + l:
+ * the producer saw layer l's router; 202 LM head start, 203 LM tiles done, 204 argmax
+ * ticket, 205 the producer issued its last LM tile; 254: end).
  * host_out must hold megakernel_grid * 256 entries. */
 int pulsar_engine_read_trace(pulsar_engine* eng, uint64_t* host_out, int64_t n);
 

@@ -199,11 +199,22 @@ struct pulsar_engine {
     int4 *rows = nullptr, *rows_v = nullptr;
     float *hblk = nullptr, *h0blk = nullptr, *htmp = nullptr, *htmp2 = nullptr, *h0tmp = nullptr, *logits_tmp = nullptr;
     long long* stats = nullptr;
-    std::map<std::string, cudaGraphExec_t> graphs;
+    struct Graph {
+        cudaGraphExec_t ex;
+        int64_t kernels, mega;   // kernel nodes per replay, of which persistent pulse kernels
+    };
+    std::map<std::string, Graph> graphs;
+    // launch tallies of the decode loop: kernels started by pulsar_engine_generate_greedy and
+    // pulsar_engine_pulse (graph kernel nodes counted per replay), and the persistent kernels among them
+    int64_t n_kernels = 0, n_mega = 0;
+    // option "time_pulses": CUDA events recorded on the caller's stream around every pulse pass
+    // launched outside graph capture; get_option("last_pulse_ns") reads the last interval
+    cudaEvent_t tev[2] = {nullptr, nullptr};
+    bool time_pulses = false;
     // persistent pulse kernel
     bool use_mega = false;
     int mega_grid = 0, mega_nch = 0;
-    float *m_gate = nullptr, *m_part = nullptr, *m_g8 = nullptr, *m_pmax = nullptr;
+    float *m_gate = nullptr, *m_part = nullptr, *m_g8 = nullptr, *m_pmax = nullptr, *m_rpart = nullptr;
     int *m_pidx = nullptr, *m_err = nullptr;
     unsigned *m_bar = nullptr, *m_tickets = nullptr;
     unsigned long long* m_trace = nullptr;   // phase stamps of the last traced launch (option "trace")
@@ -411,6 +422,7 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.part = e->m_part;
     a.vfirst = w.vfirst;
     a.g8 = e->m_g8;
+    a.rpart = e->m_rpart;
     a.pmax = e->m_pmax;
     a.pidx = e->m_pidx;
     a.nch_max = e->mega_nch;
@@ -421,13 +433,29 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     return launch_mega(a, e->kv32(), e->mega_grid, st);
 }
 
-int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in, float* h_out,
-          float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
-    if (e->use_mega && !e->has_lora && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V))
+int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
+                   float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+    if (e->use_mega && !e->has_lora && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
+        e->n_kernels += 1;
+        e->n_mega += 1;
         return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st);
+    }
+    // per-op pass: input, 10 kernels per layer, end, LM head per 8 rows, argmax
+    const bool want = logits != nullptr || amax != nullptr;
+    e->n_kernels += 2 + 10 * NL + (want ? (R + 7) / 8 : 0) + (amax ? 1 : 0);
     if (e->kv32())
         return enqueue_pulse<float>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
     return enqueue_pulse<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
+}
+
+int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in, float* h_out,
+          float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    const bool timed = e->time_pulses && cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone;
+    if (timed) PULSAR_TRY(cuda_status(cudaEventRecord(e->tev[0], st), "cudaEventRecord"));
+    PULSAR_TRY(pulse_dispatch(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st));
+    if (timed) PULSAR_TRY(cuda_status(cudaEventRecord(e->tev[1], st), "cudaEventRecord"));
+    return PULSAR_OK;
 }
 
 // ------------------------------------------------------------------ prefill
@@ -569,18 +597,40 @@ int run_graph(pulsar_engine* e, const std::string& key, cudaStream_t st, int (*b
         cudaStream_t cs;
         PULSAR_TRY(cuda_status(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate"));
         PULSAR_TRY(cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "BeginCapture"));
+        const int64_t k0 = e->n_kernels, m0 = e->n_mega;   // the body tallies its launches while capturing
         int st_body = body(e, cs, ctx);
+        const int64_t mega = e->n_mega - m0;
+        e->n_kernels = k0;
+        e->n_mega = m0;
         cudaError_t ce = cudaStreamEndCapture(cs, &g);
         cudaStreamDestroy(cs);
         PULSAR_TRY(st_body);
         PULSAR_TRY(cuda_status(ce, "EndCapture"));
+        size_t n_nodes = 0;
+        int64_t kernels = 0;
+        ce = cudaGraphGetNodes(g, nullptr, &n_nodes);
+        if (ce == cudaSuccess && n_nodes) {
+            std::vector<cudaGraphNode_t> nodes(n_nodes);
+            ce = cudaGraphGetNodes(g, nodes.data(), &n_nodes);
+            for (size_t i = 0; ce == cudaSuccess && i < n_nodes; ++i) {
+                cudaGraphNodeType t;
+                ce = cudaGraphNodeGetType(nodes[i], &t);
+                if (ce == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+            }
+        }
+        if (ce != cudaSuccess) {
+            cudaGraphDestroy(g);
+            return cuda_status(ce, "count graph nodes");
+        }
         cudaGraphExec_t ex;
         ce = cudaGraphInstantiate(&ex, g, 0);
         cudaGraphDestroy(g);
         PULSAR_TRY(cuda_status(ce, "cudaGraphInstantiate"));
-        it = e->graphs.emplace(key, ex).first;
+        it = e->graphs.emplace(key, pulsar_engine::Graph{ex, kernels, mega}).first;
     }
-    return cuda_status(cudaGraphLaunch(it->second, st), "cudaGraphLaunch");
+    e->n_kernels += it->second.kernels;
+    e->n_mega += it->second.mega;
+    return cuda_status(cudaGraphLaunch(it->second.ex, st), "cudaGraphLaunch");
 }
 
 struct LoopCtx {
@@ -720,6 +770,7 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         if ((st = e->wmalloc(&e->m_gate, (size_t)MEGA_RMAX * H)) ||
             (st = e->wmalloc(&e->m_part, (size_t)MEGA_RMAX * H * e->mega_nch * PART)) ||
             (st = e->wmalloc(&e->m_g8, (size_t)MEGA_RMAX * RG)) ||
+            (st = e->wmalloc(&e->m_rpart, (size_t)std::max(sms, 1) * MEGA_RMAX * E)) ||
             (st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
             (st = e->wmalloc(&e->m_pidx, (size_t)MEGA_RMAX * std::max(sms, 1))) || (st = e->wmalloc(&e->m_err, 1)) ||
             (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 1)))
@@ -736,7 +787,9 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
 extern "C" int pulsar_engine_destroy(pulsar_engine* e) {
     if (!e) return PULSAR_OK;
     cudaSetDevice(e->cfg.device);
-    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+    for (cudaEvent_t ev : e->tev)
+        if (ev) cudaEventDestroy(ev);
     for (auto& kv : e->t) cudaFree(kv.second);
     for (void* p : e->allocs) cudaFree(p);
     delete e;
@@ -970,6 +1023,7 @@ extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const 
     k_argmax_rows<<<n, 1024, 0, st>>>(first_logits, e->V, e->V, e->first_dev);
     k_seq_init<<<1, 32, 0, st>>>(e->seqs, e->lens_dev, e->first_dev, n, out, n_new);
     PULSAR_LAUNCH_CHECK("generate init");
+    e->n_kernels += 2;
     LoopCtx ctx{n, gamma, n_new, out};
     const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + ":" + std::to_string(n_new) + ":" +
                             std::to_string(reinterpret_cast<uintptr_t>(out));
@@ -1013,10 +1067,16 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
         }
         const bool v = value != 0;
         if (v != e->use_mega) {
-            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
             e->graphs.clear();
         }
         e->use_mega = v;
+        return PULSAR_OK;
+    }
+    if (strcmp(name, "time_pulses") == 0) {
+        for (cudaEvent_t& ev : e->tev)
+            if (value && !ev) PULSAR_TRY(cuda_status(cudaEventCreate(&ev), "cudaEventCreate"));
+        e->time_pulses = value != 0;
         return PULSAR_OK;
     }
     if (strcmp(name, "trace") == 0) {
@@ -1026,7 +1086,7 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
             PULSAR_TRY(cuda_status(cudaMemset(e->m_trace, 0, (size_t)e->mega_grid * MEGA_TRACE * 8), "zero trace"));
         }
         if (!value) e->m_trace = nullptr;   // the buffer stays allocated until destroy
-        for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+        for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
         e->graphs.clear();
         return PULSAR_OK;
     }
@@ -1052,6 +1112,19 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     if (strcmp(name, "megakernel") == 0) { *value = e->use_mega ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "megakernel_grid") == 0) { *value = e->mega_grid; return PULSAR_OK; }
     if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }
+    if (strcmp(name, "kernel_launches") == 0) { *value = e->n_kernels; return PULSAR_OK; }
+    if (strcmp(name, "mega_launches") == 0) { *value = e->n_mega; return PULSAR_OK; }
+    if (strcmp(name, "last_pulse_ns") == 0) {
+        if (!e->time_pulses) {
+            set_error("get_option: last_pulse_ns needs option \"time_pulses\" = 1");
+            return PULSAR_ERR_STATE;
+        }
+        float ms = 0.f;
+        PULSAR_TRY(cuda_status(cudaEventSynchronize(e->tev[1]), "cudaEventSynchronize"));
+        PULSAR_TRY(cuda_status(cudaEventElapsedTime(&ms, e->tev[0], e->tev[1]), "cudaEventElapsedTime"));
+        *value = (int64_t)llround((double)ms * 1e6);
+        return PULSAR_OK;
+    }
     set_error("get_option: unknown option '%s'", name);
     return PULSAR_ERR_INVALID;
 }

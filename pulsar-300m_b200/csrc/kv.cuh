@@ -33,5 +33,12 @@ __device__ __forceinline__ float kv_load(const float* p) { return *p; }
 __device__ __forceinline__ float kv_load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ void kv_store(float* p, float v) { *p = v; }
 __device__ __forceinline__ void kv_store(__nv_bfloat16* p, float v) { *p = __float2bfloat16(v); }
+// The value a store of v to a cache of element type KVT reads back as.
+template <typename KVT>
+__device__ __forceinline__ float kv_round(float v);
+template <>
+__device__ __forceinline__ float kv_round<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float kv_round<__nv_bfloat16>(float v) { return __bfloat162float(__float2bfloat16(v)); }
 
 }  // namespace pulsar

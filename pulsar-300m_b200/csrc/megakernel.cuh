@@ -1,8 +1,8 @@
 // Persistent per-pulse decode kernel (one CTA per SM, cooperative launch).
 //
 // One launch runs a whole pulse pass (src/infer.py:463-524) for R <= MEGA_RMAX rows: the
-// pulse input, 8 layers x 5 phases separated by grid barriers, the end-of-pulse residual,
-// the final norm and the LM head with argmax.
+// pulse input, 8 layers x 6 phases separated by grid barriers, the end-of-pulse residual,
+// the final norm and, when logits or argmax are requested, the LM head with argmax.
 //
 // Warp 0 is the producer: one lane streams every weight tile this CTA will consume, in
 // consumption order, through a ring of NS 8 KB shared-memory slots with 1-D TMA bulk copies
@@ -11,16 +11,20 @@
 // layer's router, computed from a flag in shared memory). Warps 1..15 are consumers: tile t
 // of the CTA's stream lives in slot t % NS and is consumed by warp t % 15.
 //
-// Phases per layer (work split evenly over the CTAs, outputs owned by one CTA each):
-//   A  xn = RMSNorm(h); QKV GEMV rows; gate logits sigmoid(xn.Wg + b) (CTAs < 16)
-//   B  attention items (sequence block, kv head, 64-key chunk): q of the 4 heads via
+// Phases per layer (work split evenly over the CTAs, outputs owned by one CTA each; h rows
+// [own0, own1) of every sequence row are owned by one CTA, kept in its shared memory):
+//   A  xn = RMSNorm(h); QKV GEMV rows; gate logits xn.Wg + b (CTAs < 8)
+//   B  attention items (sequence block, kv head, key chunk): q of the 4 heads via
 //      QK-RMSNorm + RoPE (+YaRN); block rows' K/V produced (norm, RoPE, value residual)
 //      and written to the cache by the item that owns their chunk; other keys read from
-//      the cache; split-K partials; the last item of a (block, head group) combines the
-//      chunks and applies the gate (atomic ticket, fixed combine order)
-//   C  Wo GEMV, h += (owned rows)
-//   D  m = RMSNorm(h); fp32 router (16 x 1024, every CTA, identical result); top-4;
-//      shared + routed (distinct experts) gate/up GEMVs with the SwiGLU epilogue
+//      the cache; split-K partials (m, l, o[64]) per query head and chunk
+//   B2 one CTA per (row, query head) merges its chunk partials in a fixed order and applies
+//      the gate sigmoid
+//   C  Wo GEMV, h += (owned rows); partial router logits of the owned rows
+//      z[r][e] = sum_o router[e][o] * mlp_norm[o] * h[r][o]
+//   D  m = RMSNorm(h); router logits = (sum of the CTAs' z in CTA order) / rms(h) (every
+//      CTA, identical result); top-4; shared + routed (distinct experts) gate/up GEMVs with
+//      the SwiGLU epilogue
 //   E  shared + routed down GEMVs for owned output rows, combine in top-k order, h +=
 // Then: h_out = h_in + (h - h_in) * res_scale, final RMSNorm, LM head rows, argmax.
 #pragma once
@@ -60,6 +64,7 @@ struct MegaArgs {
     int* amax;
     // global workspace
     float *h, *h_in, *qkv, *gate, *att, *act_sh, *act_r, *part, *vfirst, *g8, *pmax;
+    float* rpart;         // router partial sums [grid][R][E] of the owned h rows (phase C)
     int* pidx;
     int nch_max;          // chunks per (row, head) in `part`
     unsigned* bar;        // grid barrier counter (zeroed before launch)
@@ -77,6 +82,7 @@ struct MegaSmem {
     float wts[MEGA_RMAX][TOPK];
     int idx[MEGA_RMAX][TOPK];
     int elist[E];
+    unsigned rmask[MEGA_RMAX];   // experts chosen by each row (bit mask)
     int n_e;
     volatile int moe_ready;
     int ticket;
@@ -91,6 +97,10 @@ struct MegaSmem {
     int blk_nch[MEGA_RMAX];                // attention chunks per (block, head group)
     int blk_chunk[MEGA_RMAX];
     int n_blk;
+    float rwn[NL][E][MEGA_MAXOROWS];       // router weight x mlp-norm weight of the owned h rows
+    float hown[MEGA_MAXOROWS * MEGA_RMAX]; // owned h rows [row - o0][R] (this CTA is their only writer)
+    float rinv[MEGA_RMAX];                 // 1 / rms of h per row (phase D)
+    float rsc[NL][MEGA_MAXOROWS];          // routed_scale of the owned h rows
 };
 
 __device__ __forceinline__ void stamp(const MegaArgs& a, int l, int j) {
@@ -198,13 +208,28 @@ __device__ __noinline__ void tile_gemv(const __nv_bfloat16* w, int nr, const flo
             }
         }
     }
+    // reduce-scatter of the 4R sums over the warp (P = 4R rounded up to a power of two):
+    // P - 1 + 5 - log2(P) shuffles instead of 5 per sum; lane L ends with sum L >> (5 - log2 P)
+    constexpr int P = (4 * R <= 4) ? 4 : (4 * R <= 8) ? 8 : (4 * R <= 16) ? 16 : 32;
+    constexpr int LP = (P == 4) ? 2 : (P == 8) ? 3 : (P == 16) ? 4 : 5;
+    float x[P];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int v = 0; v < P; ++v) x[v] = (v < 4 * R) ? acc[v / R][v % R] : 0.f;
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const float v = warp_sum(acc[i][r]);
-            if (lane == i * R + r) out[lane] = v;
+    for (int st = 0; st < LP; ++st) {
+        const int o = 16 >> st, half = P >> (st + 1);
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < half; ++j) {
+            const float send = upper ? x[j] : x[j + half];
+            const float keep = upper ? x[j + half] : x[j];
+            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
+    }
+#pragma unroll
+    for (int o = 16 >> LP; o >= 1; o >>= 1) x[0] += __shfl_xor_sync(0xffffffffu, x[0], o);
+    const int v = lane >> (5 - LP);
+    if ((lane & ((1 << (5 - LP)) - 1)) == 0 && v < 4 * R) out[v] = x[0];
     __syncwarp();
 }
 
@@ -251,7 +276,7 @@ __device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsign
     named_bar_sync(1, MEGA_NCT);
     if (threadIdx.x == 32) {
         epoch += 1;
-        __threadfence();
+        // release (cumulative over the CTA's writes ordered before it by the bar.sync above)
         red_release_gpu_add(a.bar, 1u);
         const unsigned target = epoch * gridDim.x;
         bool ok = true;
@@ -271,9 +296,11 @@ __device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsign
     return s->abort == 0;
 }
 
-// RMSNorm of R rows (global, [R][1024]) into xs with weight w: one consumer warp per row.
+// RMSNorm of R rows (global, [R][1024]) into xs with weight w: one consumer warp per row;
+// 1/rms of row r goes to rinv[r] when rinv is given.
 template <int R>
-__device__ __forceinline__ void norm_rows(const float* src, const float* w, float eps, float* dst) {
+__device__ __forceinline__ void norm_rows(const float* src, const float* w, float eps, float* dst,
+                                          float* rinv = nullptr) {
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
     for (int r = cw; r < R; r += MEGA_NCW) {
         float v[32];
@@ -285,6 +312,7 @@ __device__ __forceinline__ void norm_rows(const float* src, const float* w, floa
         }
         ss = warp_sum(ss);
         const float inv = rsqrtf(ss / (float)D + eps);
+        if (rinv && lane == 0) rinv[r] = inv;
 #pragma unroll
         for (int i = 0; i < 32; ++i) dst[r * D + i * 32 + lane] = w[i * 32 + lane] * (v[i] * inv);
     }
@@ -428,10 +456,10 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, in
             kv_store(vp + lane, v1);
             kv_store(vp + lane + 32, v2);
             // the stored (rounded) values, so every reader sees identical keys
-            Ks[kk * (DH + 1) + lane] = kv_load(kp + lane);
-            Ks[kk * (DH + 1) + lane + 32] = kv_load(kp + lane + 32);
-            Vs[kk * (DH + 1) + lane] = kv_load(vp + lane);
-            Vs[kk * (DH + 1) + lane + 32] = kv_load(vp + lane + 32);
+            Ks[kk * (DH + 1) + lane] = kv_round<KVT>(y1);
+            Ks[kk * (DH + 1) + lane + 32] = kv_round<KVT>(y2);
+            Vs[kk * (DH + 1) + lane] = kv_round<KVT>(v1);
+            Vs[kk * (DH + 1) + lane + 32] = kv_round<KVT>(v2);
         }
     }
     named_bar_sync(1, MEGA_NCT);
@@ -479,80 +507,71 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, in
         out[2 + lane] = o1;
         out[2 + lane + 32] = o2;
     }
-    // 5) the last chunk item of (block, g) combines (fixed chunk order) and gates
     astamp(a, l, 4, first);
-    __threadfence();
     named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 5, first);
-    if (threadIdx.x == 32) {
-        const unsigned t = atomicAdd(&a.tickets[r0 * HKV + g], 1u);
-        s->ticket = (t == (unsigned)(nch - 1));
-        if (s->ticket) a.tickets[r0 * HKV + g] = 0;
-        __threadfence();
-    }
-    named_bar_sync(1, MEGA_NCT);
-    astamp(a, l, 6, first);
-    if (s->ticket) {
-        // W warps per query split the chunks; partials (M, L, o[64]) merged in shared memory
-        const int W = max(1, MEGA_NCW / nq);
-        float* cm = Ps;                                  // [nq*W][66] partial merges (reuses Ps/Ks)
-        for (int wi = cw; wi < nq * W; wi += MEGA_NCW) {
-            const int qi = wi / W, part_w = wi % W;
-            const int rr = qi / GQA, h = g * GQA + qi % GQA;
-            const float* pp = a.part + ((int64_t)(r0 + rr) * H + h) * a.nch_max * PART;
-            const int c_lo = (nch * part_w) / W, c_hi = (nch * (part_w + 1)) / W;
-            float mloc = -INFINITY;
-            for (int cc = c_lo + lane; cc < c_hi; cc += 32) mloc = fmaxf(mloc, __ldcg(pp + cc * PART));
-            const float M = warp_max(mloc);
-            float Ls = 0.f, o1 = 0.f, o2 = 0.f;
-            for (int c0 = c_lo; c0 < c_hi; c0 += 8) {
-                float mc[8], lc[8], a1[8], a2[8];
+}
+
+// Merge the chunk partials (m, l, o[64]) of query head h of row r, apply the gate, write
+// att[r][h*64 ..]: consumer warps take chunks cw, cw + 15, ... (online softmax merge, loads of
+// four chunks in flight), then warp 0 merges the 15 warp states in warp order.
+static __device__ __noinline__ void attn_merge(const MegaArgs& a, MegaSmem* s, int r, int h, int nch) {
+    const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+    const float* pp = a.part + ((int64_t)r * H + h) * a.nch_max * PART;
+    const float graw = (cw == 0) ? __ldcg(a.gate + r * H + h) : 0.f;   // in flight with the partials
+    float M = -INFINITY, Ls = 0.f, o1 = 0.f, o2 = 0.f;
+    for (int c0 = cw; c0 < nch; c0 += 4 * MEGA_NCW) {
+        float mc[4], lc[4], a1[4], a2[4];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int cc = min(c0 + u, c_hi - 1);
-                    mc[u] = __ldcg(pp + cc * PART);
-                    lc[u] = __ldcg(pp + cc * PART + 1);
-                    a1[u] = __ldcg(pp + cc * PART + 2 + lane);
-                    a2[u] = __ldcg(pp + cc * PART + 2 + lane + 32);
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    if (c0 + u < c_hi && mc[u] != -INFINITY) {
-                        const float wgt = expf(mc[u] - M);
-                        Ls += wgt * lc[u];
-                        o1 += wgt * a1[u];
-                        o2 += wgt * a2[u];
-                    }
-                }
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * MEGA_NCW;
+            mc[u] = -INFINITY;
+            lc[u] = a1[u] = a2[u] = 0.f;
+            if (c < nch) {
+                const float* q = pp + (int64_t)c * PART;
+                mc[u] = __ldcg(q);
+                lc[u] = __ldcg(q + 1);
+                a1[u] = __ldcg(q + 2 + lane);
+                a2[u] = __ldcg(q + 2 + 32 + lane);
             }
-            float* dst = cm + wi * PART;
-            if (lane == 0) { dst[0] = M; dst[1] = Ls; }
-            dst[2 + lane] = o1;
-            dst[2 + lane + 32] = o2;
         }
-        named_bar_sync(1, MEGA_NCT);
-        for (int qi = cw; qi < nq; qi += MEGA_NCW) {
-            const int rr = qi / GQA, h = g * GQA + qi % GQA;
-            const float* src = cm + qi * W * PART;
-            float M = -INFINITY;
-            for (int w = 0; w < W; ++w) M = fmaxf(M, src[w * PART]);
-            float Ls = 0.f, o1 = 0.f, o2 = 0.f;
-            for (int w = 0; w < W; ++w) {
-                const float mw = src[w * PART];
-                if (mw == -INFINITY) continue;
-                const float wgt = expf(mw - M);
-                Ls += wgt * src[w * PART + 1];
-                o1 += wgt * src[w * PART + 2 + lane];
-                o2 += wgt * src[w * PART + 2 + lane + 32];
-            }
-            const float gt = sigmoidf_(__ldcg(a.gate + (r0 + rr) * H + h));
-            const float inv = 1.f / Ls;
-            a.att[(int64_t)(r0 + rr) * D + h * DH + lane] = (o1 * inv) * gt;
-            a.att[(int64_t)(r0 + rr) * D + h * DH + lane + 32] = (o2 * inv) * gt;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (mc[u] == -INFINITY) continue;
+            const float Mn = fmaxf(M, mc[u]);
+            const float so = expf(M - Mn), sn = expf(mc[u] - Mn);
+            Ls = Ls * so + lc[u] * sn;
+            o1 = o1 * so + a1[u] * sn;
+            o2 = o2 * so + a2[u] * sn;
+            M = Mn;
         }
     }
+    float* st = s->stage + cw * PART;   // [15][66]
+    if (lane == 0) {
+        st[0] = M;
+        st[1] = Ls;
+    }
+    st[2 + lane] = o1;
+    st[2 + 32 + lane] = o2;
     named_bar_sync(1, MEGA_NCT);
-    astamp(a, l, 7, first);
+    if (cw == 0) {
+        float Mx = -INFINITY;
+        for (int w = 0; w < MEGA_NCW; ++w) Mx = fmaxf(Mx, s->stage[w * PART]);
+        float L = 0.f, p1 = 0.f, p2 = 0.f;
+        for (int w = 0; w < MEGA_NCW; ++w) {
+            const float* q = s->stage + w * PART;
+            if (q[0] == -INFINITY) continue;
+            const float wt = expf(q[0] - Mx);
+            L += wt * q[1];
+            p1 += wt * q[2 + lane];
+            p2 += wt * q[2 + 32 + lane];
+        }
+        const float gt = sigmoidf_(graw);
+        const float inv = 1.f / L;
+        a.att[(int64_t)r * D + h * DH + lane] = (p1 * inv) * gt;
+        a.att[(int64_t)r * D + h * DH + 32 + lane] = (p2 * inv) * gt;
+    }
+    named_bar_sync(1, MEGA_NCT);
 }
 
 // ------------------------------------------------------------------ the pulse
@@ -562,6 +581,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
     MegaSmem* s = reinterpret_cast<MegaSmem*>(smem_raw);
     const int C = gridDim.x, cta = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool want_lm = a.logits != nullptr || a.amax != nullptr;
     if (threadIdx.x == 0) {
         for (int i = 0; i < MEGA_NS; ++i) {
             mbar_init(&s->full[i], 1);
@@ -584,7 +604,6 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             if (cta < H / 2) produce_rows(g, a.gate_w[l], D * 4, 2 * cta, 2 * cta + 2, 2);
             rows_split(D, cta, C, r0, r1);
             produce_rows(g, a.wo[l], D * 2, r0, r1, 4);
-            produce_rows(g, a.router[l], D * 4, 0, E, 2);
             {   // shared-expert pairs: a static split, prefetched before the router runs
                 int j0, j1;
                 rows_split(DS, cta, C, j0, j1);
@@ -600,6 +619,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 if (globaltimer() - t0 > WAIT_NS || *(volatile int*)a.err || s->abort) { g.ok = false; break; }
             }
             if (!g.ok) break;
+            __threadfence_block();   // the expert list was written before the flag
+            if (a.trace) a.trace[blockIdx.x * MEGA_TRACE + 194 + l] = globaltimer();
             const int n_e = s->n_e;
             int q0, q1;
             rows_split(DE * n_e, cta, C, q0, q1);
@@ -616,10 +637,11 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             for (int ei = 0; ei < n_e; ++ei)
                 produce_rows(g, a.r_dn[l] + (int64_t)s->elist[ei] * D * DE, DE * 2, r0, r1, 8);
         }
-        if (g.ok) {
+        if (g.ok && want_lm) {
             int v0, v1;
             rows_split(a.V, cta, C, v0, v1);
             produce_rows(g, a.emb, D * 2, v0, v1, 4);
+            if (a.trace) a.trace[blockIdx.x * MEGA_TRACE + 205] = globaltimer();
         }
         if (!g.ok) atomicExch(a.err, 1);
         // drain: wait for every copy this thread issued to land before the CTA can exit
@@ -637,6 +659,19 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
     float* wo_ = s->wout[cw];   // this warp's reduced tile sums
     const float eps = a.eps;
     const int p = a.pulse;
+    // h rows [own0, own1) are this CTA's outputs in phases C and E; their router weights
+    // (times the mlp-norm weight) for every layer go to shared memory now
+    int own0, own1;
+    rows_split(D, cta, C, own0, own1);
+    const int nown = own1 - own0;
+    for (int t = threadIdx.x - 32; t < NL * E * MEGA_MAXOROWS; t += MEGA_NCT) {
+        const int ll = t / (E * MEGA_MAXOROWS), e = (t / MEGA_MAXOROWS) % E, oi = t % MEGA_MAXOROWS;
+        s->rwn[ll][e][oi] = oi < nown ? a.router[ll][e * D + own0 + oi] * a.mlp_norm[ll][own0 + oi] : 0.f;
+    }
+    for (int t = threadIdx.x - 32; t < NL * MEGA_MAXOROWS; t += MEGA_NCT) {
+        const int ll = t / MEGA_MAXOROWS, oi = t % MEGA_MAXOROWS;
+        s->rsc[ll][oi] = oi < nown ? a.rscale[ll][own0 + oi] : 0.f;
+    }
     // ---- pulse input: every CTA builds h_in for all rows in xs[0 .. R*D) ----
     if (p == 0) {
         for (int r = cw; r < R; r += MEGA_NCW) {
@@ -646,18 +681,23 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             float ss = 0.f;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                v[i] = __bfloat162float(e[i * 32 + lane]);
+                v[i] = __bfloat162float(__ldg(e + i * 32 + lane));
                 ss += v[i] * v[i];
             }
             const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+            // read-only inputs through the non-coherent path (free to move ahead of the
+            // stores); global stores only after the loop
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const int d = i * 32 + lane;
-                float n = a.anchor[d] * (v[i] * inv);
-                if (a.use_conv) n = n + a.stem[d * 4] * n;
-                xs[r * D + d] = n + a.step[d];
-                if (cta == 0) a.h0n_out[r * D + d] = n;
+                float n = __ldg(a.anchor + d) * (v[i] * inv);
+                if (a.use_conv) n = n + __ldg(a.stem + d * 4) * n;
+                xs[r * D + d] = n + __ldg(a.step + d);
+                v[i] = n;
             }
+            if (cta == 0)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) a.h0n_out[r * D + i * 32 + lane] = v[i];
         }
     } else {
         // g8[r][j] = Wd[j][:D] . h0n[r] + Wd[j][D:] . RMSNorm(h_prev[r])   (CTAs < 8)
@@ -678,25 +718,38 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             }
         }
         if (!grid_sync(a, s, epoch)) goto done;
+        // h_prev and h0n_in are inputs this kernel never writes (h0n_out may alias h0n_in and is
+        // then not written): read-only loads, global stores after the loops
         for (int r = cw; r < R; r += MEGA_NCW) {
+            float hp[32];
             float ss = 0.f;
-            for (int i = lane; i < D; i += 32) ss += a.h_prev[r * D + i] * a.h_prev[r * D + i];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                hp[i] = __ldg(a.h_prev + r * D + i * 32 + lane);
+                ss += hp[i] * hp[i];
+            }
             const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
             float gg[RG];
 #pragma unroll
             for (int j = 0; j < RG; ++j) gg[j] = __ldcg(a.g8 + r * RG + j);
-            for (int d = lane; d < D; d += 32) {
-                float z = a.rg_bias[d];
 #pragma unroll
-                for (int j = 0; j < RG; ++j) z += a.rg_up[d * RG + j] * gg[j];
+            for (int i = 0; i < 32; ++i) {
+                const int d = i * 32 + lane;
+                const float4 u0 = __ldg(reinterpret_cast<const float4*>(a.rg_up + d * RG));
+                const float4 u1 = __ldg(reinterpret_cast<const float4*>(a.rg_up + d * RG + 4));
+                const float z = __ldg(a.rg_bias + d) + u0.x * gg[0] + u0.y * gg[1] + u0.z * gg[2] + u0.w * gg[3] +
+                                u1.x * gg[4] + u1.y * gg[5] + u1.z * gg[6] + u1.w * gg[7];
                 const float mix = sigmoidf_(z);
-                const float rn = a.psn[d] * (a.h_prev[r * D + d] * inv);
-                const float an = a.h0n_in[r * D + d];
+                const float rn = __ldg(a.psn + d) * (hp[i] * inv);
+                const float an = __ldg(a.h0n_in + r * D + d);
                 const float diff = an - rn;
                 const float lerp = (mix < 0.5f) ? rn + mix * diff : an - diff * (1.f - mix);
-                xs[r * D + d] = lerp + a.step[d];
-                if (cta == 0) a.h0n_out[r * D + d] = an;
+                xs[r * D + d] = lerp + __ldg(a.step + d);
             }
+        }
+        if (cta == 0 && a.h0n_out != a.h0n_in) {   // caller buffers: scalar accesses, no alignment assumed
+#pragma unroll 4
+            for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT) a.h0n_out[i] = __ldg(a.h0n_in + i);
         }
     }
     named_bar_sync(1, MEGA_NCT);
@@ -705,6 +758,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             a.h_in[i] = xs[i];
             a.h[i] = xs[i];
         }
+    for (int t = threadIdx.x - 32; t < nown * R; t += MEGA_NCT) s->hown[t] = xs[(t % R) * D + own0 + t / R];
     named_bar_sync(1, MEGA_NCT);
     // sequence blocks of the rows (consecutive rows of one slot), for the attention items
     if (threadIdx.x == 32) {
@@ -790,86 +844,155 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             if (!grid_sync(a, s, epoch)) goto done;
             stamp(a, l, 5);
         }
-        // ---------------- phase C: Wo, h += (owned rows)
+        // ---------------- phase B2: merge the chunk partials of each (row, head) and gate
+        {
+            for (int u = cta; u < R * H; u += C) {
+                const int r = u / H;
+                int b = 0;
+                while (s->blk_r0[b + 1] <= r) ++b;
+                attn_merge(a, s, r, u % H, s->blk_nch[b]);
+            }
+            stamp(a, l, 6);
+            if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 7);
+        }
+        // ---------------- phase C: Wo, h += (owned rows), router partial sums of the owned rows
         {
             copy_g2s(xs, a.att, R * D);
             named_bar_sync(1, MEGA_NCT);
-            stamp(a, l, 6);
-            int r0, r1;
-            rows_split(D, cta, C, r0, r1);
-            consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
+            consume_rows(g, own0, own1, 4, [&](const unsigned char* tile, int row0, int n) {
                 tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
                 if (lane < n * R) {
-                    float* hp = a.h + (int64_t)(lane % R) * D + row0 + lane / R;
-                    *hp = __ldcg(hp) + wo_[lane];
+                    const int r = lane % R, o = row0 + lane / R;
+                    const float v = s->hown[(o - own0) * R + r] + wo_[lane];
+                    s->hown[(o - own0) * R + r] = v;
+                    a.h[(int64_t)r * D + o] = v;
                 }
             });
-            stamp(a, l, 7);
+            named_bar_sync(1, MEGA_NCT);
+            // z[r][e] = sum over owned o of router[e][o] * mlp_norm[o] * h[r][o]  (logit = z / rms)
+            for (int t = threadIdx.x - 32; t < R * E; t += MEGA_NCT) {
+                const int r = t / E, e = t % E;
+                float z = 0.f;
+                for (int oi = 0; oi < nown; ++oi) z += s->rwn[l][e][oi] * s->hown[oi * R + r];
+                a.rpart[((int64_t)cta * R + r) * E + e] = z;
+            }
+            stamp(a, l, 8);
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
-            stamp(a, l, 8);
-        }
-        // ---------------- phase D: router, shared + routed up-projections
-        {
-            norm_rows<R>(a.h, a.mlp_norm[l], eps, xs);
-            named_bar_sync(1, MEGA_NCT);
             stamp(a, l, 9);
-            consume_rows(g, 0, E, 2, [&](const unsigned char* tile, int row0, int n) {
-                tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xs, s->xoff, wo_);
-                if (lane < n * R) s->logits[lane % R][row0 + lane / R] = wo_[lane];
-            });
+        }
+        // ---------------- phase D: router (sum of the CTAs' partials), shared + routed up-projections
+        {
+            {
+                // router logits = fixed-order sum over CTAs of the partials / rms: thread t adds
+                // float4 column t % (R*E/4) of CTAs t / (R*E/4), + G, ... (its loads issued
+                // before the norm's), then a warp per (row, expert) adds the G group sums
+                constexpr int NC4 = R * E / 4;
+                constexpr int G = MEGA_NCT / NC4;
+                constexpr int MAXL = (148 + G - 1) / G;   // loads per thread kept in flight
+                const int t = threadIdx.x - 32;
+                const int col = t % NC4, cg = t / NC4;
+                const bool active = t < G * NC4;
+                const float4* src = reinterpret_cast<const float4*>(a.rpart) + col;
+                float4 pv[MAXL];
+#pragma unroll
+                for (int k = 0; k < MAXL; ++k) {
+                    const int c = cg + k * G;
+                    pv[k] = (active && c < C) ? __ldcg(src + (int64_t)c * NC4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                norm_rows<R>(a.h, a.mlp_norm[l], eps, xs, s->rinv);
+                if (active) {
+                    float4 z = pv[0];
+#pragma unroll
+                    for (int k = 1; k < MAXL; ++k) {
+                        z.x += pv[k].x;
+                        z.y += pv[k].y;
+                        z.z += pv[k].z;
+                        z.w += pv[k].w;
+                    }
+                    for (int c = cg + MAXL * G; c < C; c += G) {   // grids above 148 CTAs
+                        const float4 v = __ldcg(src + (int64_t)c * NC4);
+                        z.x += v.x;
+                        z.y += v.y;
+                        z.z += v.z;
+                        z.w += v.w;
+                    }
+                    reinterpret_cast<float4*>(s->stage)[cg * NC4 + col] = z;
+                }
+                named_bar_sync(1, MEGA_NCT);
+                if constexpr (G <= 32) {   // few groups: one thread per (row, expert)
+                    if (t < R * E) {
+                        float z = 0.f;
+#pragma unroll
+                        for (int k = 0; k < G; ++k) z += s->stage[k * R * E + t];
+                        s->logits[t / E][t % E] = z * s->rinv[t / E];
+                    }
+                } else {
+                    for (int re = cw; re < R * E; re += MEGA_NCW) {
+                        float z = 0.f;
+                        for (int k = lane; k < G; k += 32) z += s->stage[k * R * E + re];
+                        z = warp_sum(z);
+                        if (lane == 0) s->logits[re / E][re % E] = z * s->rinv[re / E];
+                    }
+                }
+            }
+            named_bar_sync(1, MEGA_NCT);
+            for (int r = cw; r < R; r += MEGA_NCW) {
+                // centre, sigmoid, top-4 of s + bias (ties to the lower expert), weights
+                const float lg = lane < E ? s->logits[r][lane] : 0.f;
+                const float mean = warp_sum(lg) / (float)E;
+                const float sg = sigmoidf_(lg - mean);
+                float b = lane < E ? sg + a.ebias[l][lane] : -INFINITY;
+                float sel_s[TOPK];
+                int sel_i[TOPK];
+                unsigned used = 0;
+#pragma unroll
+                for (int k = 0; k < TOPK; ++k) {
+                    ArgMax am{b, lane < E ? lane : 1 << 30};
+                    am = warp_argmax(am);
+                    sel_i[k] = am.i;
+                    sel_s[k] = __shfl_sync(0xffffffffu, sg, am.i & 31);
+                    if (lane == am.i) b = -INFINITY;
+                    if (am.i < E) used |= 1u << am.i;
+                }
+                float sum = 0.f;
+#pragma unroll
+                for (int k = 0; k < TOPK; ++k) sum += sel_s[k];
+                sum += 1e-6f;
+#pragma unroll
+                for (int k = 0; k < TOPK; ++k)
+                    if (lane == k) {
+                        s->idx[r][k] = sel_i[k];
+                        s->wts[r][k] = sel_s[k] / sum;
+                    }
+                if (lane == 0) s->rmask[r] = used;
+            }
             named_bar_sync(1, MEGA_NCT);
             if (cw == 0) {
-                // centre, sigmoid, top-4 of s + bias (ties to the lower expert), weights
-                int used = 0;
-                for (int r = 0; r < R; ++r) {
-                    const float lg = lane < E ? s->logits[r][lane] : 0.f;
-                    const float mean = warp_sum(lg) / (float)E;
-                    const float sg = sigmoidf_(lg - mean);
-                    float b = lane < E ? sg + a.ebias[l][lane] : -INFINITY;
-                    float sel_s[TOPK];
-                    int sel_i[TOPK];
+                unsigned used = 0;
 #pragma unroll
-                    for (int k = 0; k < TOPK; ++k) {
-                        ArgMax am{b, lane < E ? lane : 1 << 30};
-                        am = warp_argmax(am);
-                        sel_i[k] = am.i;
-                        sel_s[k] = __shfl_sync(0xffffffffu, sg, am.i & 31);
-                        if (lane == am.i) b = -INFINITY;
-                    }
-                    float sum = 0.f;
-#pragma unroll
-                    for (int k = 0; k < TOPK; ++k) sum += sel_s[k];
-                    sum += 1e-6f;
-                    if (lane == 0) {
-#pragma unroll
-                        for (int k = 0; k < TOPK; ++k) {
-                            s->idx[r][k] = sel_i[k];
-                            s->wts[r][k] = sel_s[k] / sum;
-                        }
-                    }
-#pragma unroll
-                    for (int k = 0; k < TOPK; ++k) used |= 1 << sel_i[k];
-                }
+                for (int r = 0; r < R; ++r) used |= s->rmask[r];
+                // distinct experts in increasing order (the producer's routed stream), then the flag
+                if (lane < E && (used & (1u << lane))) s->elist[__popc(used & ((1u << lane) - 1u))] = lane;
+                if (lane == 0) s->n_e = __popc(used);
+                __syncwarp();
                 if (lane == 0) {
-                    int n = 0;
-                    for (int e = 0; e < E; ++e)
-                        if (used & (1 << e)) s->elist[n++] = e;
-                    s->n_e = n;
-                    // phase E: X row of each row for every routed expert (act_r row or none)
-                    for (int ei = 0; ei < n; ++ei)
-                        for (int r = 0; r < R; ++r) {
-                            int off = -1;
-                            for (int k = 0; k < TOPK; ++k)
-                                if (s->idx[r][k] == s->elist[ei]) off = R * DS + (r * TOPK + k) * DE;
-                            s->xoff_e[ei][r] = off;
-                        }
                     __threadfence_block();
                     s->moe_ready = l + 1;
                 }
             }
             named_bar_sync(1, MEGA_NCT);
             stamp(a, l, 10);
+            // phase E: X row of each row for every routed expert (act_r row, or -1)
+            for (int t = threadIdx.x - 32; t < s->n_e * R; t += MEGA_NCT) {
+                const int ei = t / R, r = t % R;
+                int off = -1;
+#pragma unroll
+                for (int k = 0; k < TOPK; ++k)
+                    if (s->idx[r][k] == s->elist[ei]) off = R * DS + (r * TOPK + k) * DE;
+                s->xoff_e[ei][r] = off;
+            }
             const int n_e = s->n_e;
             int s0, s1, q0, q1;
             rows_split(DS, cta, C, s0, s1);          // shared pairs [s0, s1)
@@ -962,7 +1085,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                         if (s->elist[q] == ex) ei = q;
                     routed = routed + dex[(oi * E + ei) * R + r] * s->wts[r][k];
                 }
-                a.h[(int64_t)r * D + o] = __ldcg(a.h + (int64_t)r * D + o) + (dsh[oi * R + r] + routed * a.rscale[l][o]);
+                const float v = s->hown[oi * R + r] + (dsh[oi * R + r] + routed * s->rsc[l][oi]);
+                s->hown[oi * R + r] = v;
+                a.h[(int64_t)r * D + o] = v;
             }
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
@@ -975,18 +1100,22 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             float v[32];
             float ss = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < 32; ++i) {   // loads only: all of them in flight
                 const int d = i * 32 + lane;
                 const float hi = __ldcg(a.h_in + r * D + d);
-                v[i] = hi + (__ldcg(a.h + r * D + d) - hi) * a.res_scale[d];
+                v[i] = hi + (__ldcg(a.h + r * D + d) - hi) * __ldg(a.res_scale + d);
                 ss += v[i] * v[i];
-                if (cta == 0) a.h_out[r * D + d] = v[i];
             }
             const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+            if (cta == 0)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = a.fnorm[i * 32 + lane] * (v[i] * inv);
+                for (int i = 0; i < 32; ++i) a.h_out[r * D + i * 32 + lane] = v[i];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = __ldg(a.fnorm + i * 32 + lane) * (v[i] * inv);
         }
+        if (!want_lm) goto done;
         named_bar_sync(1, MEGA_NCT);
+        if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 202] = globaltimer();
         ArgMax best[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) best[r] = ArgMax{-INFINITY, 1 << 30};
@@ -1010,6 +1139,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 }
             }
         });
+        if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 203] = globaltimer();
         // per-CTA argmax -> pmax/pidx; the last CTA reduces
         float* bv = s->stage;
         int* bi = reinterpret_cast<int*>(s->stage + MEGA_NCW * R);
@@ -1036,6 +1166,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             __threadfence();
         }
         named_bar_sync(1, MEGA_NCT);
+        if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 204] = globaltimer();
         if (s->ticket && a.amax) {
             for (int r = cw; r < R; r += MEGA_NCW) {
                 ArgMax b{-INFINITY, 1 << 30};
@@ -1045,9 +1176,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             }
         }
         if (!g.ok) atomicExch(a.err, 1);
-        if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
     }
 done:
+    if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
     return;
 }
 
