@@ -193,7 +193,9 @@ int pulsar_engine_generate_greedy(pulsar_engine* eng, int32_t n_seq, const int32
  * (1 when some loop-adapter lora_B is non-zero; such weights use the per-op kernels),
  * "kernel_launches" (kernels started by generate_greedy and pulse since create, each kernel
  * node of a replayed CUDA graph counted per replay), "mega_launches" (the persistent pulse
- * kernels among them). "time_pulses" (0/1): record CUDA events on the caller's stream
+ * kernels among them), "routed_experts" (distinct routed experts whose weights the persistent
+ * kernel streamed, summed over layers and launches; waits for the device). "time_pulses" (0/1):
+ * record CUDA events on the caller's stream
  * around every pulse pass launched outside stream capture; "last_pulse_ns" (read-only,
  * waits for the last such pass) is the device time between those events. */
 int pulsar_engine_set_option(pulsar_engine* eng, const char* name, int64_t value);

@@ -218,6 +218,7 @@ struct pulsar_engine {
     int *m_pidx = nullptr, *m_err = nullptr;
     unsigned *m_bar = nullptr, *m_tickets = nullptr;
     unsigned long long* m_trace = nullptr;   // phase stamps of the last traced launch (option "trace")
+    unsigned long long* m_experts = nullptr; // distinct routed experts streamed by persistent launches
 
     int dmalloc(void** p, size_t bytes, int64_t* counter) {
         cudaError_t e = cudaMalloc(p, bytes);
@@ -429,6 +430,7 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.bar = e->m_bar;
     a.tickets = e->m_tickets;
     a.err = e->m_err;
+    a.experts = e->m_experts;
     a.trace = e->m_trace;
     return launch_mega(a, e->kv32(), e->mega_grid, st);
 }
@@ -773,10 +775,12 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
             (st = e->wmalloc(&e->m_rpart, (size_t)std::max(sms, 1) * MEGA_RMAX * E)) ||
             (st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
             (st = e->wmalloc(&e->m_pidx, (size_t)MEGA_RMAX * std::max(sms, 1))) || (st = e->wmalloc(&e->m_err, 1)) ||
-            (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 1)))
+            (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 1)) ||
+            (st = e->wmalloc(&e->m_experts, 1)))
             return fail(st);
         if ((st = cuda_status(cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 1) * 4), "zero tickets")) ||
-            (st = cuda_status(cudaMemset(e->m_err, 0, 4), "zero err")))
+            (st = cuda_status(cudaMemset(e->m_err, 0, 4), "zero err")) ||
+            (st = cuda_status(cudaMemset(e->m_experts, 0, 8), "zero expert count")))
             return fail(st);
     }
     *out = e;
@@ -1114,6 +1118,13 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "kernel_launches") == 0) { *value = e->n_kernels; return PULSAR_OK; }
     if (strcmp(name, "mega_launches") == 0) { *value = e->n_mega; return PULSAR_OK; }
+    if (strcmp(name, "routed_experts") == 0) {
+        unsigned long long v = 0;
+        if (e->m_experts)
+            PULSAR_TRY(cuda_status(cudaMemcpy(&v, e->m_experts, 8, cudaMemcpyDeviceToHost), "read expert count"));
+        *value = (int64_t)v;
+        return PULSAR_OK;
+    }
     if (strcmp(name, "last_pulse_ns") == 0) {
         if (!e->time_pulses) {
             set_error("get_option: last_pulse_ns needs option \"time_pulses\" = 1");

@@ -70,6 +70,7 @@ struct MegaArgs {
     unsigned* bar;        // grid barrier counter (zeroed before launch)
     unsigned* tickets;    // [MEGA_RMAX * HKV + 1] (self-resetting)
     int* err;             // error flag (non-zero: a bounded wait ran out)
+    unsigned long long* experts;   // running count of distinct routed experts streamed (per layer)
     unsigned long long* trace;   // optional [gridDim][MEGA_TRACE] %globaltimer stamps (null: off)
 };
 
@@ -721,18 +722,17 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         // h_prev and h0n_in are inputs this kernel never writes (h0n_out may alias h0n_in and is
         // then not written): read-only loads, global stores after the loops
         for (int r = cw; r < R; r += MEGA_NCW) {
-            float hp[32];
             float ss = 0.f;
-#pragma unroll
+#pragma unroll 8
             for (int i = 0; i < 32; ++i) {
-                hp[i] = __ldg(a.h_prev + r * D + i * 32 + lane);
-                ss += hp[i] * hp[i];
+                const float x = __ldg(a.h_prev + r * D + i * 32 + lane);
+                ss += x * x;
             }
             const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
             float gg[RG];
 #pragma unroll
             for (int j = 0; j < RG; ++j) gg[j] = __ldcg(a.g8 + r * RG + j);
-#pragma unroll
+#pragma unroll 4
             for (int i = 0; i < 32; ++i) {
                 const int d = i * 32 + lane;
                 const float4 u0 = __ldg(reinterpret_cast<const float4*>(a.rg_up + d * RG));
@@ -740,7 +740,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 const float z = __ldg(a.rg_bias + d) + u0.x * gg[0] + u0.y * gg[1] + u0.z * gg[2] + u0.w * gg[3] +
                                 u1.x * gg[4] + u1.y * gg[5] + u1.z * gg[6] + u1.w * gg[7];
                 const float mix = sigmoidf_(z);
-                const float rn = __ldg(a.psn + d) * (hp[i] * inv);
+                const float rn = __ldg(a.psn + d) * (__ldg(a.h_prev + r * D + d) * inv);
                 const float an = __ldg(a.h0n_in + r * D + d);
                 const float diff = an - rn;
                 const float lerp = (mix < 0.5f) ? rn + mix * diff : an - diff * (1.f - mix);
@@ -984,6 +984,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             }
             named_bar_sync(1, MEGA_NCT);
             stamp(a, l, 10);
+            if (cta == 0 && threadIdx.x == 32) atomicAdd(a.experts, (unsigned long long)s->n_e);
             // phase E: X row of each row for every routed expert (act_r row, or -1)
             for (int t = threadIdx.x - 32; t < s->n_e * R; t += MEGA_NCT) {
                 const int ei = t / R, r = t % R;
