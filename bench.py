@@ -341,19 +341,21 @@ def run_engine(args):
     # ---- end-to-end through the C ABI with host buffers (prompt H2D, prefill, decode, tokens D2H)
     pinned_ids = ids.to(torch.int32).pin_memory()
     host_out = torch.empty(NEW, dtype=torch.int32).pin_memory()
-    e2e_ms = []
+    e2e_ms, pre_ms = [], []
     for s in range(args.warmup + args.steps):
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, em, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record(stream)
         d_ids = pinned_ids.to(dev, non_blocking=True)
         lg = eng.prefill(0, d_ids)
+        em.record(stream)
         toks, _ = eng.generate_greedy([0], lg.view(1, -1), NEW, gamma=args.gamma)
         host_out.copy_(toks[0], non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize()
         if s >= args.warmup:
             e2e_ms.append(e0.elapsed_time(e1))
+            pre_ms.append(e0.elapsed_time(em))
     e2e_ms_max = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, local)
     e2e_value = NEW * world / (e2e_ms_max / 1e3)
     # ---- roofline of the dominant kernel, then of the whole decode path
@@ -388,7 +390,8 @@ def run_engine(args):
             "accept_rate": stats["accepted"] / max(1, stats["drafted"]),
             "tokens_per_round": acc + 1 if g > 0 else 1.0,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
-                    "d2h_bytes_per_step": NEW * 4, "includes": "prompt H2D, prefill, decode, tokens D2H"},
+                    "d2h_bytes_per_step": NEW * 4, "includes": "prompt H2D, prefill, decode, tokens D2H",
+                    "prefill_ms": statistics.mean(pre_ms), "ms_per_step": statistics.mean(e2e_ms)},
             "roofline": roof,
             "path_roofline": {"scope": "whole decode path: algorithmic bytes of the timed region (routed experts counted on the device) / device time",
                               "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

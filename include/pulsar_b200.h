@@ -187,11 +187,26 @@ int pulsar_engine_generate_greedy(pulsar_engine* eng, int32_t n_seq, const int32
                                   const float* first_logits_dev, int32_t n_new, int32_t gamma,
                                   int32_t* out_tokens_dev, int64_t* stats_host, void* stream);
 
+/* Sampled self-speculative decoding (no reference counterpart: the reference samples with
+ * torch.multinomial one token at a time, src/infer.py:594-609, whose warping - temperature,
+ * then top-p over the sorted softmax - is kept). gamma >= 1 drafts from the pulse-1 exit,
+ * each drawn from its warped distribution q; one batched verify gives p; draft d_j is
+ * accepted iff u1 <= min(1, p_{j-1}(d_j) / q_{j-1}(d_j)); the first rejection draws the next
+ * token from norm(max(0, p - q)), full acceptance draws it from p_gamma. Every uniform comes
+ * from Philox4x32-10 with counter (seq_ids_host[i], round, slot, 0) and key (seed lo, seed hi),
+ * u_k = (x_k >> 8) * 2^-24; the first token uses round 0xFFFFFFFF. Draws are inverse-CDF in
+ * vocabulary order. temperature > 0, 0 < top_p <= 1, vocab_size <= 49152. Other arguments
+ * as in pulsar_engine_generate_greedy. */
+int pulsar_engine_generate_sampled(pulsar_engine* eng, int32_t n_seq, const int32_t* slots_host,
+                                   const int32_t* seq_ids_host, const float* first_logits_dev, int32_t n_new,
+                                   int32_t gamma, float temperature, float top_p, uint64_t seed,
+                                   int32_t* out_tokens_dev, int64_t* stats_host, void* stream);
+
 /* Engine options. "megakernel" (0/1, default 1 when the GPU can co-schedule one CTA per
  * SM): run each pulse pass of <= 5 rows as one persistent kernel instead of per-op
  * kernels. Read-only: "megakernel_grid" (CTAs of the persistent kernel), "loop_adapter"
  * (1 when some loop-adapter lora_B is non-zero; such weights use the per-op kernels),
- * "kernel_launches" (kernels started by generate_greedy and pulse since create, each kernel
+ * "kernel_launches" (kernels started by generate_* and pulse since create, each kernel
  * node of a replayed CUDA graph counted per replay), "mega_launches" (the persistent pulse
  * kernels among them), "routed_experts" (distinct routed experts whose weights the persistent
  * kernel streamed, summed over layers and launches; waits for the device). "time_pulses" (0/1):

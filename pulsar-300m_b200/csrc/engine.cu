@@ -14,6 +14,7 @@
 #include "engine_kernels.cuh"
 #include "prefill_kernels.cuh"
 #include "mega_launch.h"
+#include "sampling.cuh"
 
 using namespace pulsar;
 
@@ -72,16 +73,32 @@ struct SeqDev {
     int pending;  // next token to process (already emitted)
     int n_out;    // tokens emitted
     int done;
+    int rnd;      // speculative rounds so far (Philox stream index)
 };
 
-__global__ void k_seq_init(SeqDev* seqs, const int* lens, const int* first_tok, int n, int* out, int n_new) {
+// Output buffer, length and sampling parameters of the running generate call; read by the
+// graph kernels so a captured loop does not depend on the caller's output pointer.
+struct LoopOut {
+    int* out;
+    int n_new;
+    unsigned long long seed;   // sampled decoding: Philox key, temperature, top-p
+    float temperature, top_p;
+};
+
+// Starts a generate call: sequence state, first token, and the row descriptors of round 0
+// (speculative loop: toks[i][0] = first token, rows[i] = (slot, len, first)).
+__global__ void k_seq_init(SeqDev* seqs, const int* lens, const int* first_tok, int n, int* out, int n_new,
+                           const int* slots, int gamma, int* toks, int4* rows) {
     const int i = threadIdx.x;
     if (i >= n) return;
     seqs[i].len = lens[i];
     seqs[i].pending = first_tok[i];
     seqs[i].n_out = 1;
     seqs[i].done = n_new <= 1;
+    seqs[i].rnd = 0;
     out[(int64_t)i * n_new] = first_tok[i];
+    toks[i * (gamma + 1)] = first_tok[i];
+    rows[i] = make_int4(slots[i], lens[i], first_tok[i], 0);
 }
 
 __global__ void k_rows_step(const SeqDev* seqs, const int* slots, int n, int4* rows) {
@@ -89,51 +106,41 @@ __global__ void k_rows_step(const SeqDev* seqs, const int* slots, int n, int4* r
     if (i < n) rows[i] = make_int4(slots[i], seqs[i].len, seqs[i].pending, 0);
 }
 
-__global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, int* out, int n_new) {
+__global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, const LoopOut* lo) {
     const int i = threadIdx.x;
     if (i >= n || seqs[i].done) return;
+    const int n_new = lo->n_new;
     const int t = amax[i];
-    out[(int64_t)i * n_new + seqs[i].n_out] = t;
+    lo->out[(int64_t)i * n_new + seqs[i].n_out] = t;
     seqs[i].n_out += 1;
     seqs[i].pending = t;
     seqs[i].len += 1;
     if (seqs[i].n_out >= n_new) seqs[i].done = 1;
 }
 
-// Speculative round: row j of sequence i is (slot, len + j, toks[i][j]); toks[i][0] = pending.
-__global__ void k_rows_spec(const SeqDev* seqs, const int* slots, int n, int gamma, int j, int* toks, int4* rows) {
+// Speculative round, draft step j >= 1: toks[i][j] = the token drafted at step j - 1, row i is
+// (slot, len + j, toks[i][j]); at j = gamma also the verify block rows (slot, len + k, toks[i][k]).
+__global__ void k_rows_spec(const SeqDev* seqs, const int* slots, int n, int gamma, int j, const int* amax,
+                            int* toks, int4* rows, int4* rows_v) {
     const int i = threadIdx.x;
     if (i >= n) return;
-    if (j == 0) toks[i * (gamma + 1)] = seqs[i].pending;
-    rows[i] = make_int4(slots[i], seqs[i].len + j, toks[i * (gamma + 1) + j], 0);
-}
-
-__global__ void k_store_draft(const int* amax, int n, int gamma, int j, int* toks) {
-    const int i = threadIdx.x;
-    if (i < n) toks[i * (gamma + 1) + j + 1] = amax[i];
-}
-
-__global__ void k_rows_verify(const SeqDev* seqs, const int* slots, int n, int gamma, const int* toks, int4* rows) {
-    const int i = threadIdx.x;
-    if (i >= n * (gamma + 1)) return;
-    const int s = i / (gamma + 1), j = i % (gamma + 1);
-    rows[i] = make_int4(slots[s], seqs[s].len + j, toks[i], 0);
-}
-
-__global__ void k_scatter_rows(const float* __restrict__ src, int n, int stride_rows, int j, float* __restrict__ dst) {
-    // dst[i * stride_rows + j] = src[i] (rows of D floats)
-    const int i = blockIdx.x;
-    for (int d = threadIdx.x; d < D; d += blockDim.x)
-        dst[((int64_t)i * stride_rows + j) * D + d] = src[(int64_t)i * D + d];
+    int* tk = toks + i * (gamma + 1);
+    tk[j] = amax[i];
+    rows[i] = make_int4(slots[i], seqs[i].len + j, tk[j], 0);
+    if (j == gamma)
+        for (int k = 0; k <= gamma; ++k) rows_v[i * (gamma + 1) + k] = make_int4(slots[i], seqs[i].len + k, tk[k], 0);
 }
 
 // Greedy acceptance: accept drafts while the verify argmax of the previous row matches;
-// the next pending token is the verify argmax after the last accepted draft.
-__global__ void k_accept_greedy(SeqDev* seqs, const int* toks, const int* amax_v, int n, int gamma, int* out,
-                                int n_new, long long* stats) {
+// the next pending token is the verify argmax after the last accepted draft. Also writes the
+// next round's first row and toks[i][0].
+__global__ void k_accept_greedy(SeqDev* seqs, int* toks, const int* amax_v, int n, int gamma, const LoopOut* lo,
+                                long long* stats, const int* slots, int4* rows) {
     const int i = threadIdx.x;
     if (i >= n || seqs[i].done) return;
-    const int* tk = toks + i * (gamma + 1);
+    const int n_new = lo->n_new;
+    int* out = lo->out;
+    int* tk = toks + i * (gamma + 1);
     const int* am = amax_v + i * (gamma + 1);
     int a = 0;
     while (a < gamma && am[a] == tk[a + 1]) ++a;
@@ -144,10 +151,123 @@ __global__ void k_accept_greedy(SeqDev* seqs, const int* toks, const int* amax_v
     seqs[i].n_out = no;
     seqs[i].len += a + 1;
     seqs[i].pending = nxt;
+    seqs[i].rnd += 1;
     if (no >= n_new) seqs[i].done = 1;
     stats[i * 3 + 0] += 1;
     stats[i * 3 + 1] += gamma;
     stats[i * 3 + 2] += a;
+    tk[0] = nxt;
+    rows[i] = make_int4(slots[i], seqs[i].len, nxt, 0);
+}
+
+// ---- sampled decoding (temperature / top-p, Philox uniforms) ----------------------------------
+// Warp statistics of row r of `logits` (row stride ld) and, when tok_out is set, a draw with
+// uniform 0 of stream (seq_ids[r], round, slot), round = seqs[r].rnd (0xFFFFFFFF, the first
+// token of a sequence, when seqs is null). Dynamic shared memory: V floats.
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_warp_sample(const float* __restrict__ logits, int ld, int V,
+                                                                const LoopOut* lo, const int* seq_ids,
+                                                                const SeqDev* seqs, int slot, int* tok_out,
+                                                                WarpStats* stats_out) {
+    extern __shared__ float ev[];
+    __shared__ float red[32];
+    __shared__ double redd[33];
+    __shared__ int redi[2];
+    const int r = blockIdx.x;
+    const float* lg = logits + (int64_t)r * ld;
+    const WarpStats st = row_warp_stats(lg, V, lo->temperature, lo->top_p, ev, red);
+    if (stats_out && threadIdx.x == 0) stats_out[r] = st;
+    if (tok_out) {
+        const uint32_t rnd = seqs ? (uint32_t)seqs[r].rnd : 0xFFFFFFFFu;
+        const float u = stream_uniform(lo->seed, (uint32_t)seq_ids[r], rnd, (uint32_t)slot, 0);
+        const int t = draw_index(V, u, [&](int i) { return warped_prob(lg[i], st); }, redd, redi);
+        if (threadIdx.x == 0) tok_out[r] = t;
+    }
+}
+
+// Sampled acceptance of one round (one block per sequence): for j = 1..gamma accept draft
+// toks[j] iff u1 <= min(1, p_{j-1}(d) / q_{j-1}(d)); at the first rejection the next token is
+// drawn from norm(max(0, p - q)) with u2 (the target argmax if that is empty); if all are
+// accepted it is drawn from p_gamma with u2 of slot gamma. p rows: P[i*(gamma+1) + k];
+// q rows: Q[k*n + i]. Then the commit of k_accept_greedy and the next round's first row.
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_accept_sampled(SeqDev* seqs, int* toks, const float* __restrict__ P,
+                                                                   const float* __restrict__ Q,
+                                                                   const WarpStats* __restrict__ ps,
+                                                                   const WarpStats* __restrict__ qs, int n, int gamma,
+                                                                   int V, const int* seq_ids, const LoopOut* lo,
+                                                                   long long* stats, const int* slots, int4* rows) {
+    __shared__ float red[32];
+    __shared__ int redk[32];
+    __shared__ double redd[33];
+    __shared__ int redi[2];
+    const int i = blockIdx.x;
+    if (seqs[i].done) return;
+    const uint32_t rnd = (uint32_t)seqs[i].rnd, sq = (uint32_t)seq_ids[i];
+    const unsigned long long seed = lo->seed;
+    int* tk = toks + i * (gamma + 1);
+    int a = 0, nxt = -1;
+    for (int j = 1; j <= gamma; ++j) {
+        const int d = tk[j];
+        const float* prow = P + (int64_t)(i * (gamma + 1) + j - 1) * V;
+        const float* qrow = Q + (int64_t)((j - 1) * n + i) * V;
+        const WarpStats sp = ps[i * (gamma + 1) + j - 1], sqs = qs[(j - 1) * n + i];
+        const float pd = warped_prob(prow[d], sp), qd = warped_prob(qrow[d], sqs);
+        const double ratio = (qd <= 0.f) ? 1.0 : fmin(1.0, (double)pd / (double)qd);
+        const float u1 = stream_uniform(seed, sq, rnd, (uint32_t)(j - 1), 1);
+        if ((double)u1 <= ratio) {
+            ++a;
+            continue;
+        }
+        float sres = 0.f;
+        for (int k = threadIdx.x; k < V; k += SAMPLE_THREADS)
+            sres += fmaxf(warped_prob(prow[k], sp) - warped_prob(qrow[k], sqs), 0.f);
+        const float S = sblock_sum(sres, red);
+        if (S > 0.f) {
+            const float u2 = stream_uniform(seed, sq, rnd, (uint32_t)(j - 1), 2);
+            nxt = draw_index(
+                V, u2, [&](int k) { return fmaxf(warped_prob(prow[k], sp) - warped_prob(qrow[k], sqs), 0.f) / S; },
+                redd, redi);
+        } else {   // p <= q everywhere: the target argmax (ties to the lowest index)
+            ArgMax b{-INFINITY, 1 << 30};
+            for (int k = threadIdx.x; k < V; k += SAMPLE_THREADS) b = argmax_merge(b, ArgMax{prow[k], k});
+            b = warp_argmax(b);
+            __syncthreads();
+            if ((threadIdx.x & 31) == 0) {
+                red[threadIdx.x >> 5] = b.v;
+                redk[threadIdx.x >> 5] = b.i;
+            }
+            __syncthreads();
+            if (threadIdx.x < 32) {
+                ArgMax c2{red[threadIdx.x], redk[threadIdx.x]};
+                c2 = warp_argmax(c2);
+                if (threadIdx.x == 0) redi[0] = c2.i;
+            }
+            __syncthreads();
+            nxt = redi[0];
+        }
+        break;
+    }
+    if (nxt < 0) {
+        const float* prow = P + (int64_t)(i * (gamma + 1) + gamma) * V;
+        const WarpStats sp = ps[i * (gamma + 1) + gamma];
+        const float u2 = stream_uniform(seed, sq, rnd, (uint32_t)gamma, 2);
+        nxt = draw_index(V, u2, [&](int k) { return warped_prob(prow[k], sp); }, redd, redi);
+    }
+    if (threadIdx.x != 0) return;
+    const int n_new = lo->n_new;
+    int* out = lo->out;
+    int no = seqs[i].n_out;
+    for (int j = 1; j <= a && no < n_new; ++j) out[(int64_t)i * n_new + no++] = tk[j];
+    if (no < n_new) out[(int64_t)i * n_new + no++] = nxt;
+    seqs[i].n_out = no;
+    seqs[i].len += a + 1;
+    seqs[i].pending = nxt;
+    seqs[i].rnd += 1;
+    if (no >= n_new) seqs[i].done = 1;
+    stats[i * 3 + 0] += 1;
+    stats[i * 3 + 1] += gamma;
+    stats[i * 3 + 2] += a;
+    tk[0] = nxt;
+    rows[i] = make_int4(slots[i], seqs[i].len, nxt, 0);
 }
 
 int prefill_capacity(int T) {
@@ -199,6 +319,12 @@ struct pulsar_engine {
     int4 *rows = nullptr, *rows_v = nullptr;
     float *hblk = nullptr, *h0blk = nullptr, *htmp = nullptr, *htmp2 = nullptr, *h0tmp = nullptr, *logits_tmp = nullptr;
     long long* stats = nullptr;
+    LoopOut* loop_out = nullptr;   // output buffer / length / sampling parameters of the running generate call
+    // sampled decoding: draft logits rows [MAX_ROWS][V] (row j*n + i), verify logits rows
+    // [MAX_ROWS][V] (row i*(gamma+1) + k), their warp statistics, sequence stream ids
+    float *qbuf = nullptr, *pbuf = nullptr;
+    WarpStats *qstats = nullptr, *pstats = nullptr;
+    int* seq_ids_dev = nullptr;
     struct Graph {
         cudaGraphExec_t ex;
         int64_t kernels, mega;   // kernel nodes per replay, of which persistent pulse kernels
@@ -292,19 +418,19 @@ T* offs(T* p, int64_t n) { return p ? p + n : nullptr; }
 // ------------------------------------------------------------------ pulse pass (R <= MAX_ROWS)
 template <typename KVT>
 int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
-                  float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+                  float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs) {
     auto& w = e->w;
     const float eps = e->cfg.rms_eps;
     if (p == 0) {
         k_pulse0_input<<<R, 256, 0, st>>>(rows, e->emb, e->T_("anchor_norm.weight"), e->T_("stem_canon_weight"),
                                           e->T_("pulse_step_emb.weight"), eps, e->cfg.use_canon_conv, w.h, w.h_in,
-                                          h0n_out, e->V);
+                                          h0n_out, e->V, hs);
     } else {
         k_reinject<<<R, 256, 0, st>>>(R, h_prev, h0n_in, e->T_("pulse_state_norm.weight"),
                                       e->T_("reinject_gate_down") + (int64_t)p * RG * 2 * D,
                                       e->T_("reinject_gate_up") + (int64_t)p * D * RG,
                                       e->T_("reinject_gate_bias") + (int64_t)p * D,
-                                      e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, w.h, w.h_in, h0n_out);
+                                      e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, w.h, w.h_in, h0n_out, hs);
     }
     PULSAR_LAUNCH_CHECK("pulse input");
     for (int l = 0; l < NL; ++l) {
@@ -341,7 +467,7 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
     }
     const bool want = logits != nullptr || amax != nullptr;
     k_pulse_end<<<R, 256, 0, st>>>(w.h, w.h_in, e->T_("pulse_res_scale") + (int64_t)p * D, e->T_("final_norm.weight"),
-                                   eps, h_out, want ? w.hn : nullptr);
+                                   eps, h_out, want ? w.hn : nullptr, hs);
     PULSAR_LAUNCH_CHECK("k_pulse_end");
     if (want) {
         const int nblk = e->V / LM_ROWS_PER_BLOCK;
@@ -361,7 +487,7 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
 }
 
 int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
-               float* h_out, float* h0n_out, float* logits, int* amax, cudaStream_t st) {
+               float* h_out, float* h0n_out, float* logits, int* amax, cudaStream_t st, int hs) {
     MegaArgs a{};
     a.R = R;
     a.pulse = p;
@@ -410,6 +536,7 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.h0n_in = h0n_in;
     a.h_out = h_out;
     a.h0n_out = h0n_out;
+    a.hstride = hs;
     a.logits = logits;
     a.amax = amax;
     auto& w = e->w;
@@ -436,26 +563,28 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
 }
 
 int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
-                   float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+                   float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs) {
     if (e->use_mega && !e->has_lora && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
         e->n_kernels += 1;
         e->n_mega += 1;
-        return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st);
+        return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st, hs);
     }
     // per-op pass: input, 10 kernels per layer, end, LM head per 8 rows, argmax
     const bool want = logits != nullptr || amax != nullptr;
     e->n_kernels += 2 + 10 * NL + (want ? (R + 7) / 8 : 0) + (amax ? 1 : 0);
     if (e->kv32())
-        return enqueue_pulse<float>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
-    return enqueue_pulse<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st);
+        return enqueue_pulse<float>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st, hs);
+    return enqueue_pulse<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st,
+                                        hs);
 }
 
+// hs: row stride (in rows of D floats) of h_out and h0n_out
 int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in, float* h_out,
-          float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st) {
+          float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs = 1) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     const bool timed = e->time_pulses && cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone;
     if (timed) PULSAR_TRY(cuda_status(cudaEventRecord(e->tev[0], st), "cudaEventRecord"));
-    PULSAR_TRY(pulse_dispatch(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st));
+    PULSAR_TRY(pulse_dispatch(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st, hs));
     if (timed) PULSAR_TRY(cuda_status(cudaEventRecord(e->tev[1], st), "cudaEventRecord"));
     return PULSAR_OK;
 }
@@ -503,7 +632,7 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
                                           e->T_("reinject_gate_down") + (int64_t)p * RG * 2 * D,
                                           e->T_("reinject_gate_up") + (int64_t)p * D * RG,
                                           e->T_("reinject_gate_bias") + (int64_t)p * D,
-                                          e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, f.h, f.h_in, nullptr);
+                                          e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, f.h, f.h_in, nullptr, 1);
         PULSAR_LAUNCH_CHECK("prefill pulse input");
         for (int l = 0; l < NL; ++l) {
             const bool lora = e->has_lora;
@@ -556,7 +685,7 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             PULSAR_LAUNCH_CHECK("prefill moe combine");
         }
         k_pulse_end<<<T, 256, 0, st>>>(f.h, f.h_in, e->T_("pulse_res_scale") + (int64_t)p * D,
-                                       e->T_("final_norm.weight"), eps, f.hp, nullptr);
+                                       e->T_("final_norm.weight"), eps, f.hp, nullptr, 1);
         PULSAR_LAUNCH_CHECK("prefill pulse end");
     }
     // last position logits without softcap (src/infer.py:458-461)
@@ -575,6 +704,8 @@ int check_kernel_err(pulsar_engine* e) {
     PULSAR_TRY(cuda_status(cudaMemcpy(&v, e->m_err, 4, cudaMemcpyDeviceToHost), "read error flag"));
     if (v) {
         cudaMemset(e->m_err, 0, 4);
+        cudaMemset(e->m_bar, 0, 4);
+        cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 2) * 4);
         set_error("persistent pulse kernel: a bounded wait ran out (grid barrier or weight stream); results of the "
                   "affected launch are invalid");
         return PULSAR_ERR_CUDA;
@@ -636,8 +767,7 @@ int run_graph(pulsar_engine* e, const std::string& key, cudaStream_t st, int (*b
 }
 
 struct LoopCtx {
-    int n, gamma, n_new;
-    int* out;
+    int n, gamma;
 };
 
 int body_step(pulsar_engine* e, cudaStream_t st, void* vctx) {
@@ -645,30 +775,62 @@ int body_step(pulsar_engine* e, cudaStream_t st, void* vctx) {
     const int n = c->n;
     k_rows_step<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, e->rows);
     PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, nullptr, 0, nullptr, st));
-    PULSAR_TRY(pulse(e, 1, n, e->rows, e->htmp, e->h0tmp, e->htmp2, e->h0tmp, nullptr, 0, nullptr, st));
-    PULSAR_TRY(pulse(e, 2, n, e->rows, e->htmp2, e->h0tmp, e->htmp, e->h0tmp, nullptr, 0, e->amax, st));
-    k_commit_greedy<<<1, 32, 0, st>>>(e->seqs, e->amax, n, c->out, c->n_new);
+    PULSAR_TRY(pulse(e, 1, n, e->rows, e->htmp, e->h0tmp, e->htmp2, nullptr, nullptr, 0, nullptr, st));
+    PULSAR_TRY(pulse(e, 2, n, e->rows, e->htmp2, e->h0tmp, e->htmp, nullptr, nullptr, 0, e->amax, st));
+    k_commit_greedy<<<1, 32, 0, st>>>(e->seqs, e->amax, n, e->loop_out);
     return launch_status("k_commit_greedy");
 }
 
+// One speculative round: gamma + 1 pulse-0 passes (the drafts, then the last draft's own
+// pass), whose outputs land directly in the verify block buffers (row stride gamma + 1), then
+// the batched pulse-1 and pulse-2 verify passes and the acceptance. Round 0's first row is set
+// by k_seq_init, later rounds' by the acceptance kernel.
 int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
     LoopCtx* c = static_cast<LoopCtx*>(vctx);
     const int n = c->n, g = c->gamma, rows_v = n * (g + 1);
     for (int j = 0; j <= g; ++j) {
-        k_rows_spec<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->toks, e->rows);
-        const bool draft = j < g;
-        PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, nullptr, 0, draft ? e->amax : nullptr,
-                         st));
-        k_scatter_rows<<<n, 256, 0, st>>>(e->htmp, n, g + 1, j, e->hblk);
-        k_scatter_rows<<<n, 256, 0, st>>>(e->h0tmp, n, g + 1, j, e->h0blk);
-        if (draft) k_store_draft<<<1, 32, 0, st>>>(e->amax, n, g, j, e->toks);
-        PULSAR_LAUNCH_CHECK("draft");
+        if (j > 0) {
+            k_rows_spec<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->amax, e->toks, e->rows, e->rows_v);
+            PULSAR_LAUNCH_CHECK("k_rows_spec");
+        }
+        PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->hblk + (int64_t)j * D, e->h0blk + (int64_t)j * D,
+                         nullptr, 0, j < g ? e->amax : nullptr, st, g + 1));
     }
-    k_rows_verify<<<1, 128, 0, st>>>(e->seqs, e->slots_dev, n, g, e->toks, e->rows_v);
-    PULSAR_TRY(pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, e->h0tmp, nullptr, 0, nullptr, st));
-    PULSAR_TRY(pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, e->h0tmp, nullptr, 0, e->amax, st));
-    k_accept_greedy<<<1, 32, 0, st>>>(e->seqs, e->toks, e->amax, n, g, c->out, c->n_new, e->stats);
+    PULSAR_TRY(pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st));
+    PULSAR_TRY(pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, nullptr, 0, e->amax, st));
+    k_accept_greedy<<<1, 32, 0, st>>>(e->seqs, e->toks, e->amax, n, g, e->loop_out, e->stats, e->slots_dev, e->rows);
     return launch_status("k_accept_greedy");
+}
+
+// Sampled round: the drafts' logits are kept (rows j*n + i of qbuf) and each draft token is
+// drawn from its warped distribution; the verify pass writes its logits (pbuf), their warp
+// statistics are computed per row, and k_accept_sampled runs the ratio test per sequence.
+int body_round_sampled(pulsar_engine* e, cudaStream_t st, void* vctx) {
+    LoopCtx* c = static_cast<LoopCtx*>(vctx);
+    const int n = c->n, g = c->gamma, rows_v = n * (g + 1), V = e->V;
+    const size_t smem = (size_t)V * sizeof(float);
+    for (int j = 0; j <= g; ++j) {
+        if (j > 0) {
+            k_rows_spec<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->amax, e->toks, e->rows, e->rows_v);
+            PULSAR_LAUNCH_CHECK("k_rows_spec");
+        }
+        float* qrows = j < g ? e->qbuf + (int64_t)j * n * V : nullptr;
+        PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->hblk + (int64_t)j * D, e->h0blk + (int64_t)j * D,
+                         qrows, V, nullptr, st, g + 1));
+        if (j < g) {
+            k_warp_sample<<<n, SAMPLE_THREADS, smem, st>>>(qrows, V, V, e->loop_out, e->seq_ids_dev, e->seqs, j, e->amax,
+                                                           e->qstats + (int64_t)j * n);
+            PULSAR_LAUNCH_CHECK("k_warp_sample");
+        }
+    }
+    PULSAR_TRY(pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st));
+    PULSAR_TRY(pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, e->pbuf, V, nullptr, st));
+    k_warp_sample<<<rows_v, SAMPLE_THREADS, smem, st>>>(e->pbuf, V, V, e->loop_out, e->seq_ids_dev, nullptr, 0, nullptr,
+                                                        e->pstats);
+    PULSAR_LAUNCH_CHECK("k_warp_sample");
+    k_accept_sampled<<<n, SAMPLE_THREADS, 0, st>>>(e->seqs, e->toks, e->pbuf, e->qbuf, e->pstats, e->qstats, n, g, V,
+                                                  e->seq_ids_dev, e->loop_out, e->stats, e->slots_dev, e->rows);
+    return launch_status("k_accept_sampled");
 }
 
 }  // namespace
@@ -753,6 +915,9 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
     // decode-loop state
     if ((st = e->wmalloc(&e->seqs, MAX_ROWS)) || (st = e->wmalloc(&e->slots_dev, MAX_ROWS)) ||
         (st = e->wmalloc(&e->toks, MAX_ROWS)) || (st = e->wmalloc(&e->amax, MAX_ROWS)) ||
+        (st = e->wmalloc(&e->loop_out, 1)) || (st = e->wmalloc(&e->qbuf, (size_t)MAX_ROWS * cfg->vocab_size)) ||
+        (st = e->wmalloc(&e->pbuf, (size_t)MAX_ROWS * cfg->vocab_size)) || (st = e->wmalloc(&e->qstats, MAX_ROWS)) ||
+        (st = e->wmalloc(&e->pstats, MAX_ROWS)) || (st = e->wmalloc(&e->seq_ids_dev, MAX_ROWS)) ||
         (st = e->wmalloc(&e->lens_dev, MAX_ROWS)) || (st = e->wmalloc(&e->first_dev, MAX_ROWS)) ||
         (st = e->wmalloc(&e->rows, MAX_ROWS)) || (st = e->wmalloc(&e->rows_v, MAX_ROWS)) ||
         (st = e->wmalloc(&e->hblk, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->h0blk, (size_t)MAX_ROWS * D)) ||
@@ -765,6 +930,10 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         if ((st = cuda_status(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device), "SM count")))
             return fail(st);
         if ((st = mega_occupancy(cfg->kv_fp32 != 0, &per_sm))) return fail(st);
+        if ((st = cuda_status(cudaFuncSetAttribute(k_warp_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   SAMPLE_MAX_V * (int)sizeof(float)),
+                              "k_warp_sample shared memory")))
+            return fail(st);
         // the per-CTA staging sizes assume >= 144 CTAs (ceil(8192 / C) + ceil(1024 / C) <= 64 pairs)
         e->mega_grid = sms;
         e->use_mega = per_sm >= 1 && sms >= 144;
@@ -775,10 +944,11 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
             (st = e->wmalloc(&e->m_rpart, (size_t)std::max(sms, 1) * MEGA_RMAX * E)) ||
             (st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
             (st = e->wmalloc(&e->m_pidx, (size_t)MEGA_RMAX * std::max(sms, 1))) || (st = e->wmalloc(&e->m_err, 1)) ||
-            (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 1)) ||
+            (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 2)) ||
             (st = e->wmalloc(&e->m_experts, 1)))
             return fail(st);
-        if ((st = cuda_status(cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 1) * 4), "zero tickets")) ||
+        if ((st = cuda_status(cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 2) * 4), "zero tickets")) ||
+            (st = cuda_status(cudaMemset(e->m_bar, 0, 4), "zero grid barrier")) ||
             (st = cuda_status(cudaMemset(e->m_err, 0, 4), "zero err")) ||
             (st = cuda_status(cudaMemset(e->m_experts, 0, 8), "zero expert count")))
             return fail(st);
@@ -1000,13 +1170,21 @@ extern "C" int pulsar_engine_set_length(pulsar_engine* e, int32_t slot, int32_t 
     return PULSAR_OK;
 }
 
-extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const int32_t* slots_host,
-                                             const float* first_logits, int32_t n_new, int32_t gamma, int32_t* out,
-                                             int64_t* stats_host, void* stream) {
+namespace {
+int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const int32_t* seq_ids_host,
+                  const float* first_logits, int32_t n_new, int32_t gamma, bool sampled, float temperature, float top_p,
+                  uint64_t seed, int32_t* out, int64_t* stats_host, void* stream) {
     PULSAR_TRY(check_engine(e, true));
     PULSAR_CHECK_ARG(n >= 1 && n <= e->cfg.max_batch, "generate: n_seq %d out of range", n);
     PULSAR_CHECK_ARG(gamma >= 0 && n * (gamma + 1) <= MAX_ROWS, "generate: n_seq * (gamma + 1) must be <= %d", MAX_ROWS);
     PULSAR_CHECK_ARG(n_new >= 1 && slots_host && first_logits && out, "generate: bad arguments");
+    if (sampled) {
+        PULSAR_CHECK_ARG(gamma >= 1, "generate_sampled: gamma must be >= 1");
+        PULSAR_CHECK_ARG(seq_ids_host != nullptr, "generate_sampled: null seq_ids");
+        PULSAR_CHECK_ARG(temperature > 0.f && top_p > 0.f && top_p <= 1.f,
+                         "generate_sampled: need temperature > 0 and 0 < top_p <= 1");
+        PULSAR_CHECK_ARG(e->V <= SAMPLE_MAX_V, "generate_sampled: vocab_size %d above %d", e->V, SAMPLE_MAX_V);
+    }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
     std::vector<int> lens(n);
@@ -1014,6 +1192,7 @@ extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const 
         const int s = slots_host[i];
         PULSAR_CHECK_ARG(s >= 0 && s < e->cfg.max_batch, "generate: slot %d out of range", s);
         PULSAR_CHECK_ARG(e->len[s] >= 1, "generate: slot %d has no prefilled context", s);
+        for (int k = 0; k < i; ++k) PULSAR_CHECK_ARG(slots_host[k] != s, "generate: slot %d listed twice", s);
         lens[i] = e->len[s];
         if (lens[i] + n_new + gamma + 1 > e->cfg.max_seq_len) {
             set_error("generate: slot %d needs %d positions, max_seq_len is %d", s, lens[i] + n_new + gamma + 1,
@@ -1021,16 +1200,26 @@ extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const 
             return PULSAR_ERR_CAPACITY;
         }
     }
+    const LoopOut lp{out, n_new, (unsigned long long)seed, temperature, top_p};
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->slots_dev, slots_host, n * 4, cudaMemcpyHostToDevice, st), "copy slots"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->lens_dev, lens.data(), n * 4, cudaMemcpyHostToDevice, st), "copy lens"));
+    PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->loop_out, &lp, sizeof(lp), cudaMemcpyHostToDevice, st), "copy params"));
     PULSAR_TRY(cuda_status(cudaMemsetAsync(e->stats, 0, (size_t)MAX_ROWS * 3 * 8, st), "zero stats"));
-    k_argmax_rows<<<n, 1024, 0, st>>>(first_logits, e->V, e->V, e->first_dev);
-    k_seq_init<<<1, 32, 0, st>>>(e->seqs, e->lens_dev, e->first_dev, n, out, n_new);
+    if (sampled) {
+        PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->seq_ids_dev, seq_ids_host, n * 4, cudaMemcpyHostToDevice, st),
+                               "copy seq ids"));
+        k_warp_sample<<<n, SAMPLE_THREADS, (size_t)e->V * 4, st>>>(first_logits, e->V, e->V, e->loop_out,
+                                                                   e->seq_ids_dev, nullptr, 0, e->first_dev, nullptr);
+    } else {
+        k_argmax_rows<<<n, 1024, 0, st>>>(first_logits, e->V, e->V, e->first_dev);
+    }
+    k_seq_init<<<1, 32, 0, st>>>(e->seqs, e->lens_dev, e->first_dev, n, out, n_new, e->slots_dev, gamma, e->toks,
+                                 e->rows);
     PULSAR_LAUNCH_CHECK("generate init");
     e->n_kernels += 2;
-    LoopCtx ctx{n, gamma, n_new, out};
-    const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + ":" + std::to_string(n_new) + ":" +
-                            std::to_string(reinterpret_cast<uintptr_t>(out));
+    LoopCtx ctx{n, gamma};
+    // output, length and sampling parameters live on the device: graphs depend on (n, gamma, mode)
+    const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + (sampled ? ":s" : ":g");
     std::vector<SeqDev> hs(n);
     int remaining_steps = n_new - 1;
     while (true) {
@@ -1039,7 +1228,8 @@ extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const 
         } else {
             // each round emits between 1 and gamma+1 tokens; launch the minimum, then check
             const int rounds = std::max(1, (remaining_steps + gamma) / (gamma + 1));
-            for (int s = 0; s < rounds; ++s) PULSAR_TRY(run_graph(e, key, st, body_round, &ctx));
+            for (int s = 0; s < rounds; ++s)
+                PULSAR_TRY(run_graph(e, key, st, sampled ? body_round_sampled : body_round, &ctx));
         }
         PULSAR_TRY(cuda_status(cudaMemcpyAsync(hs.data(), e->seqs, n * sizeof(SeqDev), cudaMemcpyDeviceToHost, st),
                                "read state"));
@@ -1059,6 +1249,22 @@ extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const 
             for (int k = 0; k < 3; ++k) stats_host[k] += sv[(size_t)i * 3 + k];
     }
     return PULSAR_OK;
+}
+}  // namespace
+
+extern "C" int pulsar_engine_generate_greedy(pulsar_engine* e, int32_t n, const int32_t* slots_host,
+                                             const float* first_logits, int32_t n_new, int32_t gamma, int32_t* out,
+                                             int64_t* stats_host, void* stream) {
+    return generate_impl(e, n, slots_host, nullptr, first_logits, n_new, gamma, false, 0.f, 1.f, 0, out, stats_host,
+                         stream);
+}
+
+extern "C" int pulsar_engine_generate_sampled(pulsar_engine* e, int32_t n, const int32_t* slots_host,
+                                              const int32_t* seq_ids_host, const float* first_logits, int32_t n_new,
+                                              int32_t gamma, float temperature, float top_p, uint64_t seed,
+                                              int32_t* out, int64_t* stats_host, void* stream) {
+    return generate_impl(e, n, slots_host, seq_ids_host, first_logits, n_new, gamma, true, temperature, top_p, seed,
+                         out, stats_host, stream);
 }
 
 extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int64_t value) {

@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(256) k_pulse0_input(const int4* __restrict__ r
                                                       const float* __restrict__ anchor_w, const float* __restrict__ stem,
                                                       const float* __restrict__ step0, float eps, int use_conv,
                                                       float* __restrict__ h, float* __restrict__ h_in,
-                                                      float* __restrict__ h0n, int V) {
+                                                      float* __restrict__ h0n, int V, int hs) {
     __shared__ float red[32];
     const int r = blockIdx.x;
     const int tok = min(max(rows[r].z, 0), V - 1);   // host validates; clamp keeps reads in bounds
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(256) k_pulse0_input(const int4* __restrict__ r
         float n = anchor_w[d] * (x[i] * inv);
         if (use_conv) n = n + stem[d * 4] * n;
         const float hi = n + step0[d];
-        h0n[r * D + d] = n;
+        h0n[(int64_t)r * hs * D + d] = n;
         h_in[r * D + d] = hi;
         h[r * D + d] = hi;
     }
@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(256) k_reinject(int R, const float* __restrict
                                                   const float* __restrict__ psn_w, const float* __restrict__ wd,
                                                   const float* __restrict__ wu, const float* __restrict__ wb,
                                                   const float* __restrict__ step, float eps, float* __restrict__ h,
-                                                  float* __restrict__ h_in, float* __restrict__ h0n_out) {
+                                                  float* __restrict__ h_in, float* __restrict__ h0n_out, int hs) {
     __shared__ float red[32];
     __shared__ float g_s[RG];
     const int r = blockIdx.x;
@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(256) k_reinject(int R, const float* __restrict
         const float hi = lerp + step[d];
         h_in[r * D + d] = hi;
         h[r * D + d] = hi;
-        if (h0n_out) h0n_out[r * D + d] = a[i];
+        if (h0n_out) h0n_out[(int64_t)r * hs * D + d] = a[i];
     }
 }
 
@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(128) k_moe_down(int R, const float* __restrict
 // hn = final RMSNorm(h_out) for the LM head.
 __global__ void __launch_bounds__(256) k_pulse_end(const float* __restrict__ h, const float* __restrict__ h_in,
                                                    const float* __restrict__ res_scale, const float* __restrict__ fnorm,
-                                                   float eps, float* __restrict__ h_out, float* __restrict__ hn) {
+                                                   float eps, float* __restrict__ h_out, float* __restrict__ hn, int hs) {
     __shared__ float red[32];
     const int r = blockIdx.x;
     float y[4];
@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(256) k_pulse_end(const float* __restrict__ h, 
         const int d = threadIdx.x + i * 256;
         const float hi = h_in[(int64_t)r * D + d];
         y[i] = hi + (h[(int64_t)r * D + d] - hi) * res_scale[d];
-        h_out[(int64_t)r * D + d] = y[i];
+        h_out[(int64_t)r * hs * D + d] = y[i];
         ss += y[i] * y[i];
     }
     if (!hn) return;

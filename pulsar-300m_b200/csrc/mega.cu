@@ -45,8 +45,9 @@ static int launch_r(const MegaArgs& a, int grid, cudaStream_t st) {
     }
 }
 
+// The barrier counter starts at zero: zeroed at engine creation and re-armed by the last CTA
+// of every launch.
 int launch_mega(const MegaArgs& a, bool kv32, int grid, cudaStream_t st) {
-    PULSAR_TRY(cuda_status(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), st), "zero grid barrier"));
     return kv32 ? launch_r<float>(a, grid, st) : launch_r<__nv_bfloat16>(a, grid, st);
 }
 

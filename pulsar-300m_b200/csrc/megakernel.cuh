@@ -61,6 +61,7 @@ struct MegaArgs {
     const float* h_prev;
     const float* h0n_in;
     float *h_out, *h0n_out, *logits;
+    int hstride;          // row stride (rows of D floats) of h_out and h0n_out
     int* amax;
     // global workspace
     float *h, *h_in, *qkv, *gate, *att, *act_sh, *act_r, *part, *vfirst, *g8, *pmax;
@@ -68,7 +69,7 @@ struct MegaArgs {
     int* pidx;
     int nch_max;          // chunks per (row, head) in `part`
     unsigned* bar;        // grid barrier counter (zeroed before launch)
-    unsigned* tickets;    // [MEGA_RMAX * HKV + 1] (self-resetting)
+    unsigned* tickets;    // [MEGA_RMAX * HKV + 2]: [.. + 0] argmax ticket, [.. + 1] exit count (both self-resetting)
     int* err;             // error flag (non-zero: a bounded wait ran out)
     unsigned long long* experts;   // running count of distinct routed experts streamed (per layer)
     unsigned long long* trace;   // optional [gridDim][MEGA_TRACE] %globaltimer stamps (null: off)
@@ -698,7 +699,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             }
             if (cta == 0)
 #pragma unroll
-                for (int i = 0; i < 32; ++i) a.h0n_out[r * D + i * 32 + lane] = v[i];
+                for (int i = 0; i < 32; ++i) a.h0n_out[(int64_t)r * a.hstride * D + i * 32 + lane] = v[i];
         }
     } else {
         // g8[r][j] = Wd[j][:D] . h0n[r] + Wd[j][D:] . RMSNorm(h_prev[r])   (CTAs < 8)
@@ -747,9 +748,10 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 xs[r * D + d] = lerp + __ldg(a.step + d);
             }
         }
-        if (cta == 0 && a.h0n_out != a.h0n_in) {   // caller buffers: scalar accesses, no alignment assumed
+        if (cta == 0 && a.h0n_out && a.h0n_out != a.h0n_in) {   // caller buffers: scalar accesses, no alignment assumed
 #pragma unroll 4
-            for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT) a.h0n_out[i] = __ldg(a.h0n_in + i);
+            for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT)
+                a.h0n_out[(int64_t)(i / D) * a.hstride * D + i % D] = __ldg(a.h0n_in + i);
         }
     }
     named_bar_sync(1, MEGA_NCT);
@@ -1110,7 +1112,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
             if (cta == 0)
 #pragma unroll
-                for (int i = 0; i < 32; ++i) a.h_out[r * D + i * 32 + lane] = v[i];
+                for (int i = 0; i < 32; ++i) a.h_out[(int64_t)r * a.hstride * D + i * 32 + lane] = v[i];
 #pragma unroll
             for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = __ldg(a.fnorm + i * 32 + lane) * (v[i] * inv);
         }
@@ -1179,7 +1181,16 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         if (!g.ok) atomicExch(a.err, 1);
     }
 done:
-    if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
+    if (threadIdx.x == 32) {
+        if (a.trace) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
+        // the last CTA out (every CTA is past its last grid barrier) re-arms the barrier counter
+        // for the next launch on this stream
+        const unsigned t = atomicAdd(&a.tickets[MEGA_RMAX * HKV + 1], 1u);
+        if (t == gridDim.x - 1) {
+            a.tickets[MEGA_RMAX * HKV + 1] = 0;
+            atomicExch(a.bar, 0u);
+        }
+    }
     return;
 }
 

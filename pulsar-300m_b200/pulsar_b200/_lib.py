@@ -61,6 +61,9 @@ PROTOTYPES = {
     "pulsar_engine_set_length": (c_int, [c_void_p, c_int, c_int]),
     "pulsar_engine_generate_greedy": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                               C.POINTER(c_int64), c_void_p]),
+    "pulsar_engine_generate_sampled": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                               C.c_float, C.c_float, C.c_uint64, c_void_p, C.POINTER(c_int64),
+                                               c_void_p]),
     "pulsar_engine_set_option": (c_int, [c_void_p, c_char_p, c_int64]),
     "pulsar_engine_get_option": (c_int, [c_void_p, c_char_p, C.POINTER(c_int64)]),
     "pulsar_engine_read_trace": (c_int, [c_void_p, c_void_p, c_int64]),

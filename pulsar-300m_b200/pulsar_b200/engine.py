@@ -186,6 +186,22 @@ class DeviceEngine:
             "generate_greedy")
         return out, {"rounds": stats[0], "drafted": stats[1], "accepted": stats[2]}
 
+    def generate_sampled(self, slots, first_logits: torch.Tensor, n_new: int, gamma: int, temperature: float,
+                         top_p: float, seed: int, seq_ids=None):
+        """Sampled self-speculative decoding (pulsar_engine_generate_sampled): Philox streams
+        keyed by (seq_ids[i], round, slot) and ``seed``; seq_ids default to 0..n-1."""
+        n = len(slots)
+        out = torch.empty(n, n_new, dtype=torch.int32, device=self.device)
+        sl = (C.c_int32 * n)(*slots)
+        si = (C.c_int32 * n)(*(range(n) if seq_ids is None else seq_ids))
+        stats = (C.c_int64 * 3)()
+        fl = first_logits.float().contiguous().reshape(n, -1)
+        _lib.check(_lib.load().pulsar_engine_generate_sampled(
+            self._h, n, C.cast(sl, C.c_void_p), C.cast(si, C.c_void_p), fl.data_ptr(), n_new, gamma,
+            float(temperature), float(top_p), int(seed) & 0xFFFFFFFFFFFFFFFF, out.data_ptr(), stats, self.stream()),
+            "generate_sampled")
+        return out, {"rounds": stats[0], "drafted": stats[1], "accepted": stats[2]}
+
 
 class UnifiedKVCache:
     """src/infer.py:64-178. Backed by one sequence slot of a ``DeviceEngine`` when
@@ -520,11 +536,14 @@ class PulsarInferenceEngine:
         gamma = 0: exact sequential greedy decoding (the reference's stream_generate with
         temperature 0 and no repetition penalty). gamma >= 1: gamma drafts from the
         pulse-1 exit and one batched pulse-2/3 verify of the gamma+1 block per round,
-        greedy acceptance, rollback of the rejected tail. ``self.last_stats`` receives
+        greedy acceptance (temperature <= 1e-4) or sampled acceptance (ratio test with
+        residual resampling, Philox streams keyed by (sequence index, round, slot) and
+        ``seed``), rollback of the rejected tail. ``self.last_stats`` receives
         {rounds, drafted, accepted, accept_rate}.
         """
-        if temperature > 1e-4:
-            raise NotImplementedError("generate_batch: sampled acceptance is not available yet (use temperature=0)")
+        sampled = temperature > 1e-4
+        if sampled and gamma < 1:
+            raise ValueError("generate_batch: sampled decoding needs gamma >= 1")
         ids = torch.as_tensor(input_ids)
         if ids.dim() == 1:
             ids = ids.view(1, -1)
@@ -534,7 +553,11 @@ class PulsarInferenceEngine:
             first = torch.empty(B, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
             for b in range(B):
                 first[b] = self.dev.prefill(caches[b].slot, ids[b])
-            toks, stats = self.dev.generate_greedy([c.slot for c in caches], first, max_new_tokens, gamma)
+            slots = [c.slot for c in caches]
+            if sampled:
+                toks, stats = self.dev.generate_sampled(slots, first, max_new_tokens, gamma, temperature, top_p, seed)
+            else:
+                toks, stats = self.dev.generate_greedy(slots, first, max_new_tokens, gamma)
         finally:
             for c in caches:
                 c.release()

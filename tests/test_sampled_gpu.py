@@ -1,0 +1,158 @@
+"""Sampled self-speculative decoding on the device vs the oracle's block-verify loop with the
+same Philox uniforms (oracle.block_spec_generate_ids, temperature / top-p warping of
+src/infer.py:594-608).
+
+Acceptance decisions and draws are discontinuous in the logits, so exact token identity is
+required up to the first decision of the oracle that sits within a tie tolerance of its
+threshold: an acceptance with |u1 - ratio| < 1e-3 (the tolerance of record), or an
+inverse-CDF draw whose target lies within 1e-4 (relative to the total mass) of a bucket
+edge. Logits agree to about 1e-4 or better in these runs (fp32 KV for recipe B, see
+test_engine_gpu.py), far inside those margins.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import pulsar_oracle as O
+from pulsar_b200.config import PulsarConfig
+from pulsar_b200.weights import make_state_dict, random_prompts
+
+pytestmark = pytest.mark.gpu
+ACCEPT_TIE = 1e-3
+DRAW_TIE = 1e-4
+_CACHE = {}
+
+
+def _setup(recipe, kv_dtype):
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA not available")
+    from pulsar_b200.engine import DeviceEngine
+    key = (recipe, kv_dtype)
+    if key not in _CACHE:
+        for k in list(_CACHE):
+            _CACHE.pop(k)[0].close()
+        cfg = PulsarConfig(eos_token_id=-1)
+        sd = make_state_dict(cfg, recipe=recipe, seed=0)
+        eng = DeviceEngine(cfg, sd, device=0, max_batch=4, max_seq_len=512, max_prefill=256, kv_dtype=kv_dtype)
+        _CACHE[key] = (eng, O.OracleModel(sd, cfg), cfg)
+    return _CACHE[key]
+
+
+def _draw_margin(probs, u):
+    """Distance of the draw target u * total from the nearest bucket edge of the chosen index,
+    relative to the total (sample_from's inverse CDF)."""
+    p = probs.double().numpy()
+    c = np.cumsum(p)
+    t = u * c[-1]
+    i = min(int(np.searchsorted(c, t, side="right")), len(p) - 1)
+    lo = c[i - 1] if i > 0 else 0.0
+    return min(abs(t - lo), abs(c[i] - t)) / c[-1]
+
+
+def _safe_prefix(prefill_logits, trace, stats, gamma, T, top_p, seed, seq_id):
+    """Number of leading oracle tokens decided with every decision outside the tie tolerances."""
+    p0 = O.warped_probs(prefill_logits, T, top_p)
+    if _draw_margin(p0, O.uniforms(seed, seq_id, 0xFFFFFFFF, 0)[0]) < DRAW_TIE:
+        return 0
+    n = 1
+    log = {}
+    for (rnd, j, ok, u, ratio) in stats.accept_log:
+        log.setdefault(rnd, []).append((j, ok, u, ratio))
+    for (rnd, toks, q_logits, P) in trace:
+        for j in range(gamma):
+            qp = O.warped_probs(q_logits[j], T, top_p)
+            if _draw_margin(qp, O.uniforms(seed, seq_id, rnd, j)[0]) < DRAW_TIE:
+                return n
+        a, rejected = 0, None
+        for (j, ok, u, ratio) in log.get(rnd, []):
+            if abs(u - ratio) < ACCEPT_TIE:
+                return n
+            if ok:
+                a += 1
+            else:
+                rejected = j
+                break
+        if rejected is None:
+            p = O.warped_probs(P[gamma], T, top_p)
+            if _draw_margin(p, O.uniforms(seed, seq_id, rnd, gamma)[2]) < DRAW_TIE:
+                return n
+        else:
+            p = O.warped_probs(P[rejected - 1], T, top_p)
+            q = O.warped_probs(q_logits[rejected - 1], T, top_p)
+            resid = (p - q).clamp_min(0.0)
+            if float(resid.sum()) > 0 and _draw_margin(resid / resid.sum(), O.uniforms(seed, seq_id, rnd,
+                                                                                        rejected - 1)[2]) < DRAW_TIE:
+                return n
+        n += a + 1
+    return n
+
+
+@pytest.fixture(params=[1, 0], ids=["megakernel", "per-op"])
+def path(request):
+    return request.param
+
+
+@pytest.mark.parametrize("recipe,kv,gamma", [("A", torch.bfloat16, 4), ("B", torch.float32, 4),
+                                             ("B", torch.float32, 6)])
+def test_sampled_spec_matches_oracle(recipe, kv, gamma, path):
+    eng, m, cfg = _setup(recipe, kv)
+    eng.set_option("megakernel", path)
+    T, top_p, seed, seq_id, n = 0.8, 0.95, 7, 3, 24
+    ids = random_prompts(1, 40, cfg.vocab_size, seed=2)[0].tolist()
+    okv = O.OracleKV(m, 64)
+    pre = O.prefill(m, ids, okv)
+    st, trace = O.SpecStats(), []
+    ref = O.block_spec_generate_ids(m, ids, n, gamma=gamma, temperature=T, top_p=top_p, seed=seed, seq_id=seq_id,
+                                    stats=st, trace=trace)
+    first = eng.prefill(0, ids)
+    assert (first.cpu() - pre).abs().max().item() <= 2e-2
+    got, stats = eng.generate_sampled([0], first.view(1, -1), n, gamma, T, top_p, seed, seq_ids=[seq_id])
+    got = got[0].tolist()
+    safe = _safe_prefix(pre, trace, st, gamma, T, top_p, seed, seq_id)
+    k = min(safe, n)
+    assert got[:k] == ref[:k], f"sampled tokens differ inside the decided prefix ({k} tokens): {got} vs {ref}"
+    assert stats["drafted"] == gamma * stats["rounds"]
+    if recipe == "B":
+        assert st.accepted < st.drafted, "recipe B should exercise rejections and residual draws"
+
+
+def test_sampled_batch_streams_are_independent():
+    """Two sequences in one call == each alone with the same stream id (Philox streams are keyed
+    by sequence id, not by the batch position)."""
+    eng, m, cfg = _setup("B", torch.float32)
+    eng.set_option("megakernel", 1)
+    P = random_prompts(2, 32, cfg.vocab_size, seed=9)
+    f0 = eng.prefill(0, P[0].tolist())
+    f1 = eng.prefill(1, P[1].tolist())
+    both, _ = eng.generate_sampled([0, 1], torch.stack([f0, f1]), 20, 2, 0.8, 0.95, 11, seq_ids=[5, 6])
+    eng.prefill(1, P[1].tolist())
+    one, _ = eng.generate_sampled([1], f1.view(1, -1), 20, 2, 0.8, 0.95, 11, seq_ids=[6])
+    assert both[1].tolist() == one[0].tolist()
+    eng.prefill(0, P[0].tolist())
+    again, _ = eng.generate_sampled([0], f0.view(1, -1), 20, 2, 0.8, 0.95, 11, seq_ids=[5])
+    assert both[0].tolist() == again[0].tolist()
+
+
+def test_sampled_rejects_bad_arguments():
+    eng, m, cfg = _setup("B", torch.float32)
+    f = eng.prefill(0, [1, 2, 3])
+    with pytest.raises(RuntimeError, match="gamma must be >= 1"):
+        eng.generate_sampled([0], f.view(1, -1), 4, 0, 0.8, 0.9, 0)
+    with pytest.raises(RuntimeError, match="temperature > 0"):
+        eng.generate_sampled([0], f.view(1, -1), 4, 2, 0.0, 0.9, 0)
+
+
+def test_generate_batch_sampled_api():
+    """PulsarInferenceEngine.generate_batch with temperature > 0 (the north-star entry point)."""
+    from pulsar_b200.engine import PulsarInferenceEngine
+    cfg = PulsarConfig(eos_token_id=-1)
+    sd = make_state_dict(cfg, recipe="A", seed=0)
+    eng = PulsarInferenceEngine((sd, cfg), device="cuda", max_batch=2, max_seq_len=256)
+    ids = random_prompts(2, 16, cfg.vocab_size, seed=1)
+    a = eng.generate_batch(ids, 10, temperature=0.8, top_p=0.95, gamma=2, seed=3)
+    b = eng.generate_batch(ids, 10, temperature=0.8, top_p=0.95, gamma=2, seed=3)
+    assert a.shape == (2, 26) and torch.equal(a, b)
+    assert eng.last_stats["drafted"] > 0
