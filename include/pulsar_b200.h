@@ -130,7 +130,7 @@ typedef struct {
     int32_t base_seq_len;      /* YaRN base (1024) */
     int32_t use_canon_conv;
     int32_t per_pulse_bias;
-    int32_t max_batch;         /* sequence slots */
+    int32_t max_batch;         /* sequence slots, 1..1024 */
     int32_t max_seq_len;       /* KV positions per slot (prompt + generated + slack) */
     int32_t max_prefill;       /* longest prompt one prefill call accepts */
     int32_t kv_fp32;           /* 0: bf16 KV cache (default); 1: fp32 KV cache (parity mode) */
@@ -160,7 +160,10 @@ int pulsar_engine_memory(const pulsar_engine* eng, int64_t* arena_bytes, int64_t
 int pulsar_engine_prefill(pulsar_engine* eng, int32_t slot, const int32_t* ids_dev, int32_t T, float* logits_dev,
                           void* stream);
 
-/* decode_pulse_pass (src/infer.py:463-524) over R rows (1 <= R <= 32).
+/* decode_pulse_pass (src/infer.py:463-524) over R rows, 1 <= R <= max(32, 8 * max_batch)
+ * (option "wide_rows"). R <= 5: one persistent kernel; R <= 32: per-op GEMV kernels; more
+ * rows (or option "wide" = 1): tiled GEMMs over all rows with the routed experts grouped
+ * per expert.
  * rows_dev [R] x int4 {slot, pos, token, 0}. Rows of the same slot must have
  * consecutive positions (block-verify: a row sees in-block predecessors' K/V of this
  * pulse). h_prev_dev / h0n_dev [R, 1024] f32 (ignored for pulse 0). Outputs h_out,
@@ -179,6 +182,7 @@ int pulsar_engine_set_length(pulsar_engine* eng, int32_t slot, int32_t length);
  * in the slot's state, emit n_new tokens. gamma == 0: exact sequential decode (3 pulses
  * per token). gamma >= 1: draft gamma tokens from the pulse-1 exit, verify the gamma+1
  * block with pulses 2-3 in one batched pass, accept while argmax agrees, roll back.
+ * 1 <= n_seq <= max_batch, 0 <= gamma <= 7, distinct slots.
  * Runs device-resident (CUDA graphs, no per-token host sync).
  * first_logits_dev [n_seq, V] f32: logits that choose each sequence's first token.
  * slots_host [n_seq]; out_tokens_dev [n_seq, n_new] i32; stats_host (may be NULL)
@@ -206,7 +210,9 @@ int pulsar_engine_generate_sampled(pulsar_engine* eng, int32_t n_seq, const int3
  * SM): run each pulse pass of <= 5 rows as one persistent kernel instead of per-op
  * kernels. Read-only: "megakernel_grid" (CTAs of the persistent kernel), "loop_adapter"
  * (1 when some loop-adapter lora_B is non-zero; such weights use the per-op kernels),
- * "kernel_launches" (kernels started by generate_* and pulse since create, each kernel
+ * "wide" (0/1): run every pulse pass through the many-row GEMM path; read-only "wide_rows"
+ * (row capacity of a pass). "kernel_launches" (kernels started by generate_* and pulse since
+ * create, each kernel
  * node of a replayed CUDA graph counted per replay), "mega_launches" (the persistent pulse
  * kernels among them), "routed_experts" (distinct routed experts whose weights the persistent
  * kernel streamed, summed over layers and launches; waits for the device). "time_pulses" (0/1):

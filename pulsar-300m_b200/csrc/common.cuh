@@ -24,6 +24,8 @@ constexpr int RG = 8;            // re-injection gate rank
 constexpr int WINDOW = 1024;     // sliding window of local layers
 constexpr int LOCAL_RING = 2048; // ring slots per local layer (window + verify block slack)
 constexpr int MAX_ROWS = 32;     // rows of one small-batch pulse pass (GEMV regime)
+constexpr int MAX_BATCH = 1024;  // sequence slots of one engine
+constexpr int MAX_GAMMA = 7;     // drafts per speculative round (verify blocks of <= 8 rows)
 
 __host__ __device__ constexpr bool is_local_layer(int l) { return l != 3 && l != 7; }
 

@@ -89,7 +89,7 @@ struct LoopOut {
 // (speculative loop: toks[i][0] = first token, rows[i] = (slot, len, first)).
 __global__ void k_seq_init(SeqDev* seqs, const int* lens, const int* first_tok, int n, int* out, int n_new,
                            const int* slots, int gamma, int* toks, int4* rows) {
-    const int i = threadIdx.x;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     seqs[i].len = lens[i];
     seqs[i].pending = first_tok[i];
@@ -102,12 +102,12 @@ __global__ void k_seq_init(SeqDev* seqs, const int* lens, const int* first_tok, 
 }
 
 __global__ void k_rows_step(const SeqDev* seqs, const int* slots, int n, int4* rows) {
-    const int i = threadIdx.x;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) rows[i] = make_int4(slots[i], seqs[i].len, seqs[i].pending, 0);
 }
 
 __global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, const LoopOut* lo) {
-    const int i = threadIdx.x;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n || seqs[i].done) return;
     const int n_new = lo->n_new;
     const int t = amax[i];
@@ -122,7 +122,7 @@ __global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, const Loop
 // (slot, len + j, toks[i][j]); at j = gamma also the verify block rows (slot, len + k, toks[i][k]).
 __global__ void k_rows_spec(const SeqDev* seqs, const int* slots, int n, int gamma, int j, const int* amax,
                             int* toks, int4* rows, int4* rows_v) {
-    const int i = threadIdx.x;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int* tk = toks + i * (gamma + 1);
     tk[j] = amax[i];
@@ -136,7 +136,7 @@ __global__ void k_rows_spec(const SeqDev* seqs, const int* slots, int n, int gam
 // next round's first row and toks[i][0].
 __global__ void k_accept_greedy(SeqDev* seqs, int* toks, const int* amax_v, int n, int gamma, const LoopOut* lo,
                                 long long* stats, const int* slots, int4* rows) {
-    const int i = threadIdx.x;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n || seqs[i].done) return;
     const int n_new = lo->n_new;
     int* out = lo->out;
@@ -305,6 +305,15 @@ struct pulsar_engine {
         float *h, *h_in, *xn, *qkv, *q, *vfirst, *part, *att, *act_sh, *act_r, *hn, *t_qkv, *t_wo, *wts, *pmax;
         int *idx, *pidx;
     } w{};
+    // wide decode workspace: pulse passes of more than MAX_ROWS rows (GEMM regime), up to
+    // wide_rows rows; MoE rows bucketed per expert with capacity = rows (nothing dropped)
+    int wide_rows = 0;
+    bool force_wide = false;   // option "wide": every pulse pass through the wide path
+    struct {
+        float *h, *h_in, *xn, *qkv, *q, *vfirst, *part, *att, *act_sh, *sh, *hn, *t_qkv, *t_wo, *wts, *act_e, *ye,
+            *logits;
+        int *idx, *lists, *cnt, *slot, *rows_e, *kept;
+    } ww{};
     // prefill workspace
     struct {
         int* ids;
@@ -320,8 +329,8 @@ struct pulsar_engine {
     float *hblk = nullptr, *h0blk = nullptr, *htmp = nullptr, *htmp2 = nullptr, *h0tmp = nullptr, *logits_tmp = nullptr;
     long long* stats = nullptr;
     LoopOut* loop_out = nullptr;   // output buffer / length / sampling parameters of the running generate call
-    // sampled decoding: draft logits rows [MAX_ROWS][V] (row j*n + i), verify logits rows
-    // [MAX_ROWS][V] (row i*(gamma+1) + k), their warp statistics, sequence stream ids
+    // sampled decoding: draft logits rows [wide_rows][V] (row j*n + i), verify logits rows
+    // [wide_rows][V] (row i*(gamma+1) + k), their warp statistics, sequence stream ids
     float *qbuf = nullptr, *pbuf = nullptr;
     WarpStats *qstats = nullptr, *pstats = nullptr;
     int* seq_ids_dev = nullptr;
@@ -562,8 +571,22 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     return launch_mega(a, e->kv32(), e->mega_grid, st);
 }
 
+template <typename KVT>
+int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
+                       float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs);
+
 int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
                    float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs) {
+    if (R > MAX_ROWS || e->force_wide) {
+        // rms norm, QKV GEMM, qkv post, attention, combine, Wo GEMM, norm, router, shared GEMMs (2),
+        // bucket, slots, expert GEMMs (2), combine per layer; input, end, LM GEMM, argmax
+        const bool want = logits != nullptr || amax != nullptr;
+        e->n_kernels += 2 + 15 * NL + (want ? 1 : 0) + (amax ? 1 : 0);
+        if (e->kv32())
+            return enqueue_pulse_wide<float>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st, hs);
+        return enqueue_pulse_wide<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax,
+                                                 st, hs);
+    }
     if (e->use_mega && !e->has_lora && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
         e->n_kernels += 1;
         e->n_mega += 1;
@@ -697,6 +720,99 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
     return PULSAR_OK;
 }
 
+// Pulse pass over R rows in the GEMM regime (R > MAX_ROWS, or option "wide"): the same
+// arithmetic as enqueue_pulse with every weight product a tiled GEMM over all rows, the
+// routed experts bucketed per expert (capacity R: no row is dropped, unlike prefill), and
+// the LM head a GEMM with the softcap epilogue followed by a row argmax.
+template <typename KVT>
+int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
+                       float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs) {
+    if (R > e->wide_rows) {
+        set_error("pulse: %d rows exceed the wide workspace (%d rows)", R, e->wide_rows);
+        return PULSAR_ERR_CAPACITY;
+    }
+    auto& w = e->ww;
+    const float eps = e->cfg.rms_eps;
+    if (p == 0) {
+        k_pulse0_input<<<R, 256, 0, st>>>(rows, e->emb, e->T_("anchor_norm.weight"), e->T_("stem_canon_weight"),
+                                          e->T_("pulse_step_emb.weight"), eps, e->cfg.use_canon_conv, w.h, w.h_in,
+                                          h0n_out, e->V, hs);
+    } else {
+        k_reinject<<<R, 256, 0, st>>>(R, h_prev, h0n_in, e->T_("pulse_state_norm.weight"),
+                                      e->T_("reinject_gate_down") + (int64_t)p * RG * 2 * D,
+                                      e->T_("reinject_gate_up") + (int64_t)p * D * RG,
+                                      e->T_("reinject_gate_bias") + (int64_t)p * D,
+                                      e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, w.h, w.h_in, h0n_out, hs);
+    }
+    PULSAR_LAUNCH_CHECK("wide pulse input");
+    const int cap = R, M4 = R * TOPK;
+    for (int l = 0; l < NL; ++l) {
+        const bool lora = e->has_lora;
+        const bool local = is_local_layer(l);
+        k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, w.xn,
+                                          lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv);
+        GemmArgs g = gargs(w.xn, D, R, e->wqkv[l], QKV, D, w.qkv, QKV);
+        if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = w.t_qkv; }
+        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st));
+        const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
+        k_qkv_post<KVT><<<R, (H + HKV) * 32, 0, st>>>(
+            rows, w.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
+            e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
+            local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
+            e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
+        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, R), 128, 0, st>>>(rows, w.q, e->kvl[l], local ? 1 : 0, e->nch[l],
+                                                                    w.part, e->max_pos(), e->cfg.max_batch);
+        k_attn_combine<<<R, H * 32, 0, st>>>(w.part, e->nch[l], w.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
+                                             e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
+                                             lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
+        PULSAR_LAUNCH_CHECK("wide attention");
+        g = gargs(w.att, D, R, e->wo[l], D, D, w.h, D);
+        if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = w.t_wo; }
+        PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st));
+        k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, w.xn, nullptr,
+                                          nullptr);
+        const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
+        k_router<<<R, E * 32, 0, st>>>(w.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, w.idx, w.wts);
+        PULSAR_LAUNCH_CHECK("wide router");
+        PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(w.xn, D, R, e->sh_gu[l], 2 * DS, D, w.act_sh, DS), 1, st));
+        PULSAR_TRY(gemm<GEPI_STORE>(gargs(w.act_sh, DS, R, e->sh_dn[l], D, DS, w.sh, D), 1, st));
+        k_moe_bucket<<<E, 1024, 0, st>>>(w.idx, M4, w.lists, M4, w.cnt);
+        k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(w.lists, M4, w.cnt, w.wts, cap, w.slot, w.rows_e, w.kept);
+        PULSAR_LAUNCH_CHECK("wide slots");
+        GemmArgs gu = gargs(w.xn, D, cap, e->r_gu[l], 2 * DE, D, w.act_e, DE);
+        gu.a_rows = w.rows_e;
+        gu.m_count = w.kept;
+        gu.w_stride = (int64_t)2 * DE * D;
+        gu.c_stride = (int64_t)cap * DE;
+        PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st));
+        GemmArgs gd = gargs(w.act_e, DE, cap, e->r_dn[l], D, DE, w.ye, D);
+        gd.a_stride = (int64_t)cap * DE;
+        gd.m_count = w.kept;
+        gd.w_stride = (int64_t)D * DE;
+        gd.c_stride = (int64_t)cap * D;
+        PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st));
+        k_moe_combine_rows<<<R, 256, 0, st>>>(w.sh, w.ye, cap, w.idx, w.wts, w.slot,
+                                              e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D, w.h);
+        PULSAR_LAUNCH_CHECK("wide moe combine");
+    }
+    const bool want = logits != nullptr || amax != nullptr;
+    k_pulse_end<<<R, 256, 0, st>>>(w.h, w.h_in, e->T_("pulse_res_scale") + (int64_t)p * D, e->T_("final_norm.weight"),
+                                   eps, h_out, want ? w.hn : nullptr, hs);
+    PULSAR_LAUNCH_CHECK("wide pulse end");
+    if (want) {
+        float* lg = logits ? logits : w.logits;
+        const int ld = logits ? ld_logits : e->V;
+        GemmArgs g = gargs(w.hn, D, R, e->emb, e->V, D, lg, ld);
+        g.softcap = e->cfg.logit_softcap;
+        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st));
+        if (amax) {
+            k_argmax_rows<<<R, 1024, 0, st>>>(lg, e->V, ld, amax);
+            PULSAR_LAUNCH_CHECK("wide argmax");
+        }
+    }
+    return PULSAR_OK;
+}
+
 // The persistent kernel raises a device flag when a bounded wait runs out; report it once.
 int check_kernel_err(pulsar_engine* e) {
     if (!e->m_err) return PULSAR_OK;
@@ -773,11 +889,11 @@ struct LoopCtx {
 int body_step(pulsar_engine* e, cudaStream_t st, void* vctx) {
     LoopCtx* c = static_cast<LoopCtx*>(vctx);
     const int n = c->n;
-    k_rows_step<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, e->rows);
+    k_rows_step<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, e->rows);
     PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, nullptr, 0, nullptr, st));
     PULSAR_TRY(pulse(e, 1, n, e->rows, e->htmp, e->h0tmp, e->htmp2, nullptr, nullptr, 0, nullptr, st));
     PULSAR_TRY(pulse(e, 2, n, e->rows, e->htmp2, e->h0tmp, e->htmp, nullptr, nullptr, 0, e->amax, st));
-    k_commit_greedy<<<1, 32, 0, st>>>(e->seqs, e->amax, n, e->loop_out);
+    k_commit_greedy<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->amax, n, e->loop_out);
     return launch_status("k_commit_greedy");
 }
 
@@ -790,7 +906,7 @@ int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
     const int n = c->n, g = c->gamma, rows_v = n * (g + 1);
     for (int j = 0; j <= g; ++j) {
         if (j > 0) {
-            k_rows_spec<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->amax, e->toks, e->rows, e->rows_v);
+            k_rows_spec<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->amax, e->toks, e->rows, e->rows_v);
             PULSAR_LAUNCH_CHECK("k_rows_spec");
         }
         PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->hblk + (int64_t)j * D, e->h0blk + (int64_t)j * D,
@@ -798,7 +914,7 @@ int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
     }
     PULSAR_TRY(pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st));
     PULSAR_TRY(pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, nullptr, 0, e->amax, st));
-    k_accept_greedy<<<1, 32, 0, st>>>(e->seqs, e->toks, e->amax, n, g, e->loop_out, e->stats, e->slots_dev, e->rows);
+    k_accept_greedy<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->toks, e->amax, n, g, e->loop_out, e->stats, e->slots_dev, e->rows);
     return launch_status("k_accept_greedy");
 }
 
@@ -811,7 +927,7 @@ int body_round_sampled(pulsar_engine* e, cudaStream_t st, void* vctx) {
     const size_t smem = (size_t)V * sizeof(float);
     for (int j = 0; j <= g; ++j) {
         if (j > 0) {
-            k_rows_spec<<<1, 32, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->amax, e->toks, e->rows, e->rows_v);
+            k_rows_spec<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->amax, e->toks, e->rows, e->rows_v);
             PULSAR_LAUNCH_CHECK("k_rows_spec");
         }
         float* qrows = j < g ? e->qbuf + (int64_t)j * n * V : nullptr;
@@ -841,7 +957,7 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
     PULSAR_CHECK_ARG(cfg->vocab_size > 0 && cfg->vocab_size % 256 == 0, "vocab_size must be a positive multiple of 256");
     PULSAR_CHECK_ARG(cfg->max_pulses >= NP, "max_pulses must be >= %d", NP);
     PULSAR_CHECK_ARG(cfg->loop_lora_rank == 0 || cfg->loop_lora_rank == 8, "loop_lora_rank must be 0 or 8");
-    PULSAR_CHECK_ARG(cfg->max_batch >= 1 && cfg->max_batch <= MAX_ROWS, "max_batch must be in [1, %d]", MAX_ROWS);
+    PULSAR_CHECK_ARG(cfg->max_batch >= 1 && cfg->max_batch <= MAX_BATCH, "max_batch must be in [1, %d]", MAX_BATCH);
     PULSAR_CHECK_ARG(cfg->max_seq_len >= 16, "max_seq_len too small");
     PULSAR_CHECK_ARG(cfg->max_prefill >= 1 && cfg->max_prefill <= cfg->max_seq_len, "max_prefill must be in [1, max_seq_len]");
     PULSAR_TRY(cuda_status(cudaSetDevice(cfg->device), "cudaSetDevice"));
@@ -892,6 +1008,23 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&w.pmax, (size_t)R * nblk)) || (st = e->wmalloc(&w.idx, (size_t)R * TOPK)) ||
         (st = e->wmalloc(&w.pidx, (size_t)R * nblk)))
         return fail(st);
+    // wide workspace: every row of a speculative round of max_batch sequences (gamma <= 7)
+    const int RW = std::max(MAX_ROWS, cfg->max_batch * (MAX_GAMMA + 1));
+    e->wide_rows = RW;
+    auto& x = e->ww;
+    if ((st = e->wmalloc(&x.h, (size_t)RW * D)) || (st = e->wmalloc(&x.h_in, (size_t)RW * D)) ||
+        (st = e->wmalloc(&x.xn, (size_t)RW * D)) || (st = e->wmalloc(&x.qkv, (size_t)RW * QKV)) ||
+        (st = e->wmalloc(&x.q, (size_t)RW * H * DH)) || (st = e->wmalloc(&x.vfirst, (size_t)RW * HKV * DH)) ||
+        (st = e->wmalloc(&x.part, (size_t)RW * H * nch_max * PART)) || (st = e->wmalloc(&x.att, (size_t)RW * D)) ||
+        (st = e->wmalloc(&x.act_sh, (size_t)RW * DS)) || (st = e->wmalloc(&x.sh, (size_t)RW * D)) ||
+        (st = e->wmalloc(&x.hn, (size_t)RW * D)) || (st = e->wmalloc(&x.t_qkv, (size_t)RW * LORA_R)) ||
+        (st = e->wmalloc(&x.t_wo, (size_t)RW * LORA_R)) || (st = e->wmalloc(&x.wts, (size_t)RW * TOPK)) ||
+        (st = e->wmalloc(&x.act_e, (size_t)E * RW * DE)) || (st = e->wmalloc(&x.ye, (size_t)E * RW * D)) ||
+        (st = e->wmalloc(&x.logits, (size_t)RW * cfg->vocab_size)) || (st = e->wmalloc(&x.idx, (size_t)RW * TOPK)) ||
+        (st = e->wmalloc(&x.lists, (size_t)E * RW * TOPK)) || (st = e->wmalloc(&x.cnt, E)) ||
+        (st = e->wmalloc(&x.slot, (size_t)RW * TOPK)) || (st = e->wmalloc(&x.rows_e, (size_t)E * RW)) ||
+        (st = e->wmalloc(&x.kept, E)))
+        return fail(st);
     // prefill workspace
     auto& f = e->pf;
     const int T = cfg->max_prefill;
@@ -913,16 +1046,17 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&f.pidx, (size_t)nblk)))
         return fail(st);
     // decode-loop state
-    if ((st = e->wmalloc(&e->seqs, MAX_ROWS)) || (st = e->wmalloc(&e->slots_dev, MAX_ROWS)) ||
-        (st = e->wmalloc(&e->toks, MAX_ROWS)) || (st = e->wmalloc(&e->amax, MAX_ROWS)) ||
-        (st = e->wmalloc(&e->loop_out, 1)) || (st = e->wmalloc(&e->qbuf, (size_t)MAX_ROWS * cfg->vocab_size)) ||
-        (st = e->wmalloc(&e->pbuf, (size_t)MAX_ROWS * cfg->vocab_size)) || (st = e->wmalloc(&e->qstats, MAX_ROWS)) ||
-        (st = e->wmalloc(&e->pstats, MAX_ROWS)) || (st = e->wmalloc(&e->seq_ids_dev, MAX_ROWS)) ||
-        (st = e->wmalloc(&e->lens_dev, MAX_ROWS)) || (st = e->wmalloc(&e->first_dev, MAX_ROWS)) ||
-        (st = e->wmalloc(&e->rows, MAX_ROWS)) || (st = e->wmalloc(&e->rows_v, MAX_ROWS)) ||
-        (st = e->wmalloc(&e->hblk, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->h0blk, (size_t)MAX_ROWS * D)) ||
-        (st = e->wmalloc(&e->htmp, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->htmp2, (size_t)MAX_ROWS * D)) ||
-        (st = e->wmalloc(&e->h0tmp, (size_t)MAX_ROWS * D)) || (st = e->wmalloc(&e->stats, (size_t)MAX_ROWS * 3)))
+    const int NB = cfg->max_batch;
+    if ((st = e->wmalloc(&e->seqs, NB)) || (st = e->wmalloc(&e->slots_dev, NB)) ||
+        (st = e->wmalloc(&e->toks, RW)) || (st = e->wmalloc(&e->amax, RW)) ||
+        (st = e->wmalloc(&e->loop_out, 1)) || (st = e->wmalloc(&e->qbuf, (size_t)RW * cfg->vocab_size)) ||
+        (st = e->wmalloc(&e->pbuf, (size_t)RW * cfg->vocab_size)) || (st = e->wmalloc(&e->qstats, RW)) ||
+        (st = e->wmalloc(&e->pstats, RW)) || (st = e->wmalloc(&e->seq_ids_dev, NB)) ||
+        (st = e->wmalloc(&e->lens_dev, NB)) || (st = e->wmalloc(&e->first_dev, NB)) ||
+        (st = e->wmalloc(&e->rows, RW)) || (st = e->wmalloc(&e->rows_v, RW)) ||
+        (st = e->wmalloc(&e->hblk, (size_t)RW * D)) || (st = e->wmalloc(&e->h0blk, (size_t)RW * D)) ||
+        (st = e->wmalloc(&e->htmp, (size_t)RW * D)) || (st = e->wmalloc(&e->htmp2, (size_t)RW * D)) ||
+        (st = e->wmalloc(&e->h0tmp, (size_t)RW * D)) || (st = e->wmalloc(&e->stats, (size_t)NB * 3)))
         return fail(st);
     // persistent pulse kernel: one CTA per SM, co-resident (cooperative launch)
     {
@@ -1112,15 +1246,15 @@ extern "C" int pulsar_engine_pulse(pulsar_engine* e, int32_t p, int32_t R, const
                                    const float* h0n, float* h_out, float* h0n_out, float* logits, void* stream) {
     PULSAR_TRY(check_engine(e, true));
     PULSAR_CHECK_ARG(p >= 0 && p < NP, "pulse index %d out of range [0, %d)", p, NP);
-    PULSAR_CHECK_ARG(R >= 1 && R <= MAX_ROWS, "rows %d out of range [1, %d]", R, MAX_ROWS);
+    PULSAR_CHECK_ARG(R >= 1 && R <= e->wide_rows, "rows %d out of range [1, %d]", R, e->wide_rows);
     PULSAR_CHECK_ARG(rows && h_out && h0n_out, "pulse: null pointer");
     PULSAR_CHECK_ARG(p == 0 || (h_prev && h0n), "pulse %d needs h_prev and h0n", p);
     PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
     {
         // validate the row descriptors before any kernel indexes the cache with them
-        int4 hr[MAX_ROWS];
+        std::vector<int4> hr(R);
         cudaStream_t vs = reinterpret_cast<cudaStream_t>(stream);
-        PULSAR_TRY(cuda_status(cudaMemcpyAsync(hr, rows, (size_t)R * sizeof(int4), cudaMemcpyDeviceToHost, vs), "copy rows"));
+        PULSAR_TRY(cuda_status(cudaMemcpyAsync(hr.data(), rows, (size_t)R * sizeof(int4), cudaMemcpyDeviceToHost, vs), "copy rows"));
         PULSAR_TRY(cuda_status(cudaStreamSynchronize(vs), "copy rows"));
         PULSAR_TRY(check_kernel_err(e));
         for (int r = 0; r < R; ++r) {
@@ -1176,7 +1310,7 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
                   uint64_t seed, int32_t* out, int64_t* stats_host, void* stream) {
     PULSAR_TRY(check_engine(e, true));
     PULSAR_CHECK_ARG(n >= 1 && n <= e->cfg.max_batch, "generate: n_seq %d out of range", n);
-    PULSAR_CHECK_ARG(gamma >= 0 && n * (gamma + 1) <= MAX_ROWS, "generate: n_seq * (gamma + 1) must be <= %d", MAX_ROWS);
+    PULSAR_CHECK_ARG(gamma >= 0 && gamma <= MAX_GAMMA, "generate: gamma %d outside [0, %d]", gamma, MAX_GAMMA);
     PULSAR_CHECK_ARG(n_new >= 1 && slots_host && first_logits && out, "generate: bad arguments");
     if (sampled) {
         PULSAR_CHECK_ARG(gamma >= 1, "generate_sampled: gamma must be >= 1");
@@ -1204,7 +1338,7 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->slots_dev, slots_host, n * 4, cudaMemcpyHostToDevice, st), "copy slots"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->lens_dev, lens.data(), n * 4, cudaMemcpyHostToDevice, st), "copy lens"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->loop_out, &lp, sizeof(lp), cudaMemcpyHostToDevice, st), "copy params"));
-    PULSAR_TRY(cuda_status(cudaMemsetAsync(e->stats, 0, (size_t)MAX_ROWS * 3 * 8, st), "zero stats"));
+    PULSAR_TRY(cuda_status(cudaMemsetAsync(e->stats, 0, (size_t)n * 3 * 8, st), "zero stats"));
     if (sampled) {
         PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->seq_ids_dev, seq_ids_host, n * 4, cudaMemcpyHostToDevice, st),
                                "copy seq ids"));
@@ -1213,7 +1347,7 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
     } else {
         k_argmax_rows<<<n, 1024, 0, st>>>(first_logits, e->V, e->V, e->first_dev);
     }
-    k_seq_init<<<1, 32, 0, st>>>(e->seqs, e->lens_dev, e->first_dev, n, out, n_new, e->slots_dev, gamma, e->toks,
+    k_seq_init<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->lens_dev, e->first_dev, n, out, n_new, e->slots_dev, gamma, e->toks,
                                  e->rows);
     PULSAR_LAUNCH_CHECK("generate init");
     e->n_kernels += 2;
@@ -1283,6 +1417,14 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
         e->use_mega = v;
         return PULSAR_OK;
     }
+    if (strcmp(name, "wide") == 0) {
+        if ((value != 0) != e->force_wide) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+            e->graphs.clear();
+        }
+        e->force_wide = value != 0;
+        return PULSAR_OK;
+    }
     if (strcmp(name, "time_pulses") == 0) {
         for (cudaEvent_t& ev : e->tev)
             if (value && !ev) PULSAR_TRY(cuda_status(cudaEventCreate(&ev), "cudaEventCreate"));
@@ -1321,6 +1463,8 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     PULSAR_CHECK_ARG(name && value, "get_option: null argument");
     if (strcmp(name, "megakernel") == 0) { *value = e->use_mega ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "megakernel_grid") == 0) { *value = e->mega_grid; return PULSAR_OK; }
+    if (strcmp(name, "wide") == 0) { *value = e->force_wide ? 1 : 0; return PULSAR_OK; }
+    if (strcmp(name, "wide_rows") == 0) { *value = e->wide_rows; return PULSAR_OK; }
     if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "kernel_launches") == 0) { *value = e->n_kernels; return PULSAR_OK; }
     if (strcmp(name, "mega_launches") == 0) { *value = e->n_mega; return PULSAR_OK; }

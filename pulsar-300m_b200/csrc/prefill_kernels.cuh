@@ -28,6 +28,7 @@ struct GemmArgs {
     int64_t c_stride;
     const float* lora_b;     // [N][24] or null
     const float* lora_t;     // [M][24]
+    float softcap;           // STORE epilogue: y = softcap * tanh(y / softcap) when > 0
 };
 
 template <int EPI>
@@ -140,10 +141,12 @@ __global__ void __launch_bounds__(256) k_gemm(GemmArgs g) {
                 for (int q = 0; q < LORA_R; ++q) d += g.lora_b[(int64_t)n * LORA_R + q] * g.lora_t[(int64_t)m * LORA_R + q];
                 y += d;
             }
-            if (EPI == GEPI_ADD)
+            if (EPI == GEPI_ADD) {
                 C[(int64_t)m * g.ldc + n] += y;
-            else
+            } else {
+                if (g.softcap > 0.f) y = g.softcap * tanhf(y / g.softcap);
                 C[(int64_t)m * g.ldc + n] = y;
+            }
         }
     }
 }

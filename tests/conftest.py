@@ -11,6 +11,7 @@ import math
 import os
 import sys
 
+import numpy as np
 import pytest
 import torch
 
@@ -56,3 +57,69 @@ def gpu():
     if not HAS_CUDA:
         pytest.skip("CUDA not available")
     return torch.device("cuda")
+
+
+# ---- sampled decoding: tie tolerances of accept decisions and inverse-CDF draws -------------
+SAMPLED_ACCEPT_TIE = 1e-3   # |u1 - ratio| below this: the decision may flip (tolerance of record)
+SAMPLED_DRAW_TIE = 1e-4     # draw target this close (relative) to a bucket edge may change bucket
+
+
+def sampled_draw_margin(probs, u):
+    """Distance of the draw target u * total from the nearest bucket edge of the chosen index,
+    relative to the total (the oracle's sample_from inverse CDF)."""
+    p = probs.double().numpy()
+    c = np.cumsum(p)
+    t = u * c[-1]
+    i = min(int(np.searchsorted(c, t, side="right")), len(p) - 1)
+    lo = c[i - 1] if i > 0 else 0.0
+    return min(abs(t - lo), abs(c[i] - t)) / c[-1]
+
+
+def sampled_safe_prefix(prefill_logits, trace, stats, gamma, T, top_p, seed, seq_id):
+    """Number of leading tokens of an oracle block_spec_generate_ids run (its trace and
+    stats) whose every deciding draw and accept test lies outside the tie tolerances."""
+    from oracle import pulsar_oracle as O
+    p0 = O.warped_probs(prefill_logits, T, top_p)
+    if sampled_draw_margin(p0, O.uniforms(seed, seq_id, 0xFFFFFFFF, 0)[0]) < SAMPLED_DRAW_TIE:
+        return 0
+    n = 1
+    log = {}
+    for (rnd, j, ok, u, ratio) in stats.accept_log:
+        log.setdefault(rnd, []).append((j, ok, u, ratio))
+    for (rnd, toks, q_logits, P) in trace:
+        for j in range(gamma):
+            qp = O.warped_probs(q_logits[j], T, top_p)
+            if sampled_draw_margin(qp, O.uniforms(seed, seq_id, rnd, j)[0]) < SAMPLED_DRAW_TIE:
+                return n
+        a, rejected = 0, None
+        for (j, ok, u, ratio) in log.get(rnd, []):
+            if abs(u - ratio) < SAMPLED_ACCEPT_TIE:
+                return n
+            if ok:
+                a += 1
+            else:
+                rejected = j
+                break
+        if rejected is None:
+            p = O.warped_probs(P[gamma], T, top_p)
+            if sampled_draw_margin(p, O.uniforms(seed, seq_id, rnd, gamma)[2]) < SAMPLED_DRAW_TIE:
+                return n
+        else:
+            p = O.warped_probs(P[rejected - 1], T, top_p)
+            q = O.warped_probs(q_logits[rejected - 1], T, top_p)
+            resid = (p - q).clamp_min(0.0)
+            u2 = O.uniforms(seed, seq_id, rnd, rejected - 1)[2]
+            if float(resid.sum()) > 0 and sampled_draw_margin(resid / resid.sum(), u2) < SAMPLED_DRAW_TIE:
+                return n
+        n += a + 1
+    return n
+
+
+PATH_IDS = ["megakernel", "per-op", "wide"]
+
+
+def use_path(eng, path):
+    """Select the pulse implementation: 0 persistent kernel (rows <= 5, else the per-op
+    kernels), 1 per-op GEMV kernels, 2 the many-row GEMM path."""
+    eng.set_option("wide", 1 if path == 2 else 0)
+    eng.set_option("megakernel", 1 if path == 0 else 0)

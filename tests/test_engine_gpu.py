@@ -19,6 +19,8 @@ from oracle import pulsar_oracle as O
 from pulsar_b200.config import PulsarConfig
 from pulsar_b200.weights import make_state_dict, random_prompts
 
+from conftest import PATH_IDS, use_path
+
 pytestmark = pytest.mark.gpu
 TOL = 2e-2
 _CACHE = {}
@@ -37,6 +39,7 @@ def _setup(recipe, kv_dtype, max_seq_len=2048, max_prefill=1280, max_batch=4):
         eng = DeviceEngine(cfg, sd, device=0, max_batch=max_batch, max_seq_len=max_seq_len, max_prefill=max_prefill,
                            kv_dtype=kv_dtype)
         _CACHE[key] = (eng, O.OracleModel(sd, cfg), cfg)
+    use_path(_CACHE[key][0], 0)
     return _CACHE[key]
 
 
@@ -45,7 +48,7 @@ def _margin(lg):
     return float(v[0] - v[1])
 
 
-@pytest.fixture(params=[1, 0], ids=["megakernel", "per-op"])
+@pytest.fixture(params=[0, 1, 2], ids=PATH_IDS)
 def path(request):
     return request.param
 
@@ -53,7 +56,7 @@ def path(request):
 @pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("A", torch.float32), ("B", torch.float32)])
 def test_prefill_and_pulse_logits_match_oracle(recipe, kv, path):
     eng, m, cfg = _setup(recipe, kv)
-    eng.set_option("megakernel", path)
+    use_path(eng, path)
     ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
     okv = O.OracleKV(m, 256)
     ref = O.prefill(m, ids, okv)
@@ -96,7 +99,7 @@ def test_long_prompt_local_quirk_and_yarn():
 def test_rollback_is_exact(path):
     """Length reset (rollback) then recomputation reproduces the logits bit for bit."""
     eng, m, cfg = _setup("B", torch.float32)
-    eng.set_option("megakernel", path)
+    use_path(eng, path)
     ids = random_prompts(1, 64, cfg.vocab_size, seed=9)[0].tolist()
     eng.prefill(2, ids)
     toks = [5, 77, 901, 4242]
@@ -114,7 +117,7 @@ def test_rollback_is_exact(path):
 
 def test_rows_of_different_slots_are_independent(path):
     eng, m, cfg = _setup("B", torch.float32)
-    eng.set_option("megakernel", path)
+    use_path(eng, path)
     a = random_prompts(1, 40, cfg.vocab_size, seed=1)[0].tolist()
     b = random_prompts(1, 70, cfg.vocab_size, seed=2)[0].tolist()
     eng.prefill(0, a)
@@ -138,7 +141,7 @@ def _compare_tokens(got, ref, margins, what):
 def test_greedy_generate_matches_oracle_stream(recipe, kv, path):
     """generate_greedy(gamma=0) == reference stream_generate (greedy, penalty 1.0)."""
     eng, m, cfg = _setup(recipe, kv)
-    eng.set_option("megakernel", path)
+    use_path(eng, path)
     ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
     n = 48
     trace = []
@@ -153,7 +156,7 @@ def test_greedy_generate_matches_oracle_stream(recipe, kv, path):
 def test_spec_gamma4_matches_oracle_block_verify(recipe, kv, path):
     """gamma = 4 drafting + one batched verify per round == the oracle's block-verify loop."""
     eng, m, cfg = _setup(recipe, kv)
-    eng.set_option("megakernel", path)
+    use_path(eng, path)
     ids = random_prompts(1, 128, cfg.vocab_size, seed=0)[0].tolist()
     n = 40
     trace = []
@@ -220,7 +223,7 @@ def test_verify_block_rows_match_oracle(path):
     """A 5-row verify block of one sequence (block-verify KV rule) at pulses 0-2 vs the
     oracle's multi-row pulse pass."""
     eng, m, cfg = _setup("B", torch.float32)
-    eng.set_option("megakernel", path)
+    use_path(eng, path)
     ids = random_prompts(1, 96, cfg.vocab_size, seed=11)[0].tolist()
     okv = O.OracleKV(m, 160)
     O.prefill(m, ids, okv)
@@ -237,14 +240,14 @@ def test_verify_block_rows_match_oracle(path):
 
 
 def test_megakernel_matches_per_op_path():
-    """Both pulse implementations agree to fp32 reordering on the same rows."""
+    """The three pulse implementations agree to fp32 reordering on the same rows."""
     eng, m, cfg = _setup("B", torch.float32)
     if not eng.get_option("megakernel_grid") >= 144:
         pytest.skip("GPU cannot host the persistent kernel")
     ids = random_prompts(1, 1100, cfg.vocab_size, seed=12)[0].tolist()
     out = {}
-    for mode in (0, 1):
-        eng.set_option("megakernel", mode)
+    for mode in (0, 1, 2):
+        use_path(eng, mode)
         eng.prefill(1, ids)
         rows = [(1, 1100 + j, 100 + 7 * j) for j in range(3)]
         h = h0 = None
@@ -253,10 +256,11 @@ def test_megakernel_matches_per_op_path():
             lg, h, h0 = eng.pulse(p, rows, h, h0)
             res.append(lg.clone())
         out[mode] = res
-    eng.set_option("megakernel", 1)
+    use_path(eng, 0)
     for p in range(3):
-        d = (out[0][p] - out[1][p]).abs().max().item()
-        assert d < 2e-3, f"pulse {p}: per-op vs persistent kernel differ by {d:.3e}"
+        for mode, name in ((0, "persistent kernel"), (2, "many-row GEMM path")):
+            d = (out[mode][p] - out[1][p]).abs().max().item()
+            assert d < 2e-3, f"pulse {p}: per-op vs {name} differ by {d:.3e}"
 
 
 def test_rejects_non_consecutive_rows():

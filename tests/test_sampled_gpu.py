@@ -12,7 +12,6 @@ test_engine_gpu.py), far inside those margins.
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 
@@ -20,9 +19,9 @@ from oracle import pulsar_oracle as O
 from pulsar_b200.config import PulsarConfig
 from pulsar_b200.weights import make_state_dict, random_prompts
 
+from conftest import PATH_IDS, use_path, sampled_safe_prefix
+
 pytestmark = pytest.mark.gpu
-ACCEPT_TIE = 1e-3
-DRAW_TIE = 1e-4
 _CACHE = {}
 
 
@@ -38,59 +37,11 @@ def _setup(recipe, kv_dtype):
         sd = make_state_dict(cfg, recipe=recipe, seed=0)
         eng = DeviceEngine(cfg, sd, device=0, max_batch=4, max_seq_len=512, max_prefill=256, kv_dtype=kv_dtype)
         _CACHE[key] = (eng, O.OracleModel(sd, cfg), cfg)
+    use_path(_CACHE[key][0], 0)
     return _CACHE[key]
 
 
-def _draw_margin(probs, u):
-    """Distance of the draw target u * total from the nearest bucket edge of the chosen index,
-    relative to the total (sample_from's inverse CDF)."""
-    p = probs.double().numpy()
-    c = np.cumsum(p)
-    t = u * c[-1]
-    i = min(int(np.searchsorted(c, t, side="right")), len(p) - 1)
-    lo = c[i - 1] if i > 0 else 0.0
-    return min(abs(t - lo), abs(c[i] - t)) / c[-1]
-
-
-def _safe_prefix(prefill_logits, trace, stats, gamma, T, top_p, seed, seq_id):
-    """Number of leading oracle tokens decided with every decision outside the tie tolerances."""
-    p0 = O.warped_probs(prefill_logits, T, top_p)
-    if _draw_margin(p0, O.uniforms(seed, seq_id, 0xFFFFFFFF, 0)[0]) < DRAW_TIE:
-        return 0
-    n = 1
-    log = {}
-    for (rnd, j, ok, u, ratio) in stats.accept_log:
-        log.setdefault(rnd, []).append((j, ok, u, ratio))
-    for (rnd, toks, q_logits, P) in trace:
-        for j in range(gamma):
-            qp = O.warped_probs(q_logits[j], T, top_p)
-            if _draw_margin(qp, O.uniforms(seed, seq_id, rnd, j)[0]) < DRAW_TIE:
-                return n
-        a, rejected = 0, None
-        for (j, ok, u, ratio) in log.get(rnd, []):
-            if abs(u - ratio) < ACCEPT_TIE:
-                return n
-            if ok:
-                a += 1
-            else:
-                rejected = j
-                break
-        if rejected is None:
-            p = O.warped_probs(P[gamma], T, top_p)
-            if _draw_margin(p, O.uniforms(seed, seq_id, rnd, gamma)[2]) < DRAW_TIE:
-                return n
-        else:
-            p = O.warped_probs(P[rejected - 1], T, top_p)
-            q = O.warped_probs(q_logits[rejected - 1], T, top_p)
-            resid = (p - q).clamp_min(0.0)
-            if float(resid.sum()) > 0 and _draw_margin(resid / resid.sum(), O.uniforms(seed, seq_id, rnd,
-                                                                                        rejected - 1)[2]) < DRAW_TIE:
-                return n
-        n += a + 1
-    return n
-
-
-@pytest.fixture(params=[1, 0], ids=["megakernel", "per-op"])
+@pytest.fixture(params=[0, 1, 2], ids=PATH_IDS)
 def path(request):
     return request.param
 
@@ -99,7 +50,7 @@ def path(request):
                                              ("B", torch.float32, 6)])
 def test_sampled_spec_matches_oracle(recipe, kv, gamma, path):
     eng, m, cfg = _setup(recipe, kv)
-    eng.set_option("megakernel", path)
+    use_path(eng, path)
     T, top_p, seed, seq_id, n = 0.8, 0.95, 7, 3, 24
     ids = random_prompts(1, 40, cfg.vocab_size, seed=2)[0].tolist()
     okv = O.OracleKV(m, 64)
@@ -111,7 +62,7 @@ def test_sampled_spec_matches_oracle(recipe, kv, gamma, path):
     assert (first.cpu() - pre).abs().max().item() <= 2e-2
     got, stats = eng.generate_sampled([0], first.view(1, -1), n, gamma, T, top_p, seed, seq_ids=[seq_id])
     got = got[0].tolist()
-    safe = _safe_prefix(pre, trace, st, gamma, T, top_p, seed, seq_id)
+    safe = sampled_safe_prefix(pre, trace, st, gamma, T, top_p, seed, seq_id)
     k = min(safe, n)
     assert got[:k] == ref[:k], f"sampled tokens differ inside the decided prefix ({k} tokens): {got} vs {ref}"
     assert stats["drafted"] == gamma * stats["rounds"]
@@ -123,7 +74,7 @@ def test_sampled_batch_streams_are_independent():
     """Two sequences in one call == each alone with the same stream id (Philox streams are keyed
     by sequence id, not by the batch position)."""
     eng, m, cfg = _setup("B", torch.float32)
-    eng.set_option("megakernel", 1)
+    use_path(eng, 0)
     P = random_prompts(2, 32, cfg.vocab_size, seed=9)
     f0 = eng.prefill(0, P[0].tolist())
     f1 = eng.prefill(1, P[1].tolist())
