@@ -15,6 +15,7 @@
 #include "prefill_kernels.cuh"
 #include "mega_launch.h"
 #include "sampling.cuh"
+#include "tc_gemm.cuh"
 
 using namespace pulsar;
 
@@ -309,6 +310,7 @@ struct pulsar_engine {
     // wide_rows rows; MoE rows bucketed per expert with capacity = rows (nothing dropped)
     int wide_rows = 0;
     bool force_wide = false;   // option "wide": every pulse pass through the wide path
+    bool use_tc = true;        // option "tc_gemm": tensor-core GEMMs (prefill, wide path)
     struct {
         float *h, *h_in, *xn, *qkv, *q, *vfirst, *part, *att, *act_sh, *sh, *hn, *t_qkv, *t_wo, *wts, *act_e, *ye,
             *logits;
@@ -613,8 +615,25 @@ int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev,
 }
 
 // ------------------------------------------------------------------ prefill
+// Tiled GEMM launch: the tcgen05 tensor-core kernel when the shape fits its tiles (K a
+// multiple of 64, output columns a multiple of 128, or of 64 for SWIGLU), else the SIMT kernel.
 template <int EPI>
-int gemm(const GemmArgs& g, int batches, cudaStream_t st) {
+int gemm(const GemmArgs& g, int batches, cudaStream_t st, bool tc, int* err_flag) {
+    constexpr int BN = 128;
+    const bool fits = g.K % TC_BK == 0 && (EPI == GEPI_SWIGLU ? (g.N / 2) % (BN / 2) == 0 : g.N % BN == 0);
+    if (tc && fits) {
+        static bool configured = false;   // per instantiation
+        if (!configured) {
+            PULSAR_TRY(cuda_status(cudaFuncSetAttribute(k_tc_gemm<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)tc_smem_bytes<BN>()),
+                                   "k_tc_gemm shared memory"));
+            configured = true;
+        }
+        const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2) / (BN / 2) : g.N / BN;
+        dim3 grid(ntiles, (g.M + TC_BM - 1) / TC_BM, batches);
+        k_tc_gemm<EPI, BN><<<grid, TC_THREADS, tc_smem_bytes<BN>(), st>>>(g, err_flag);
+        return launch_status("k_tc_gemm");
+    }
     const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2 + 31) / 32 : (g.N + GB_N - 1) / GB_N;
     dim3 grid(ntiles, (g.M + GB_M - 1) / GB_M, batches);
     k_gemm<EPI><<<grid, 256, 0, st>>>(g);
@@ -664,7 +683,7 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
                                               lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, f.t);
             GemmArgs g = gargs(f.xn, D, T, e->wqkv[l], QKV, D, f.qkv, QKV);
             if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = f.t; }
-            PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st));
+            PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st, e->use_tc, e->m_err));
             const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
             k_qkv_post_prefill<KVT><<<T, (H + HKV) * 32, 0, st>>>(
                 slot, T, f.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
@@ -678,15 +697,15 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             PULSAR_LAUNCH_CHECK("prefill attention");
             g = gargs(f.att, D, T, e->wo[l], D, D, f.h, D);
             if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = f.t; }
-            PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st));
+            PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st, e->use_tc, e->m_err));
             k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, f.xn,
                                               nullptr, nullptr);
             const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
             k_router<<<T, E * 32, 0, st>>>(f.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, f.idx,
                                            f.wts);
             PULSAR_LAUNCH_CHECK("prefill router");
-            PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(f.xn, D, T, e->sh_gu[l], 2 * DS, D, f.act_sh, DS), 1, st));
-            PULSAR_TRY(gemm<GEPI_STORE>(gargs(f.act_sh, DS, T, e->sh_dn[l], D, DS, f.sh, D), 1, st));
+            PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(f.xn, D, T, e->sh_gu[l], 2 * DS, D, f.act_sh, DS), 1, st, e->use_tc, e->m_err));
+            PULSAR_TRY(gemm<GEPI_STORE>(gargs(f.act_sh, DS, T, e->sh_dn[l], D, DS, f.sh, D), 1, st, e->use_tc, e->m_err));
             k_moe_bucket<<<E, 1024, 0, st>>>(f.idx, M4, f.lists, M4, f.cnt);
             k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(f.lists, M4, f.cnt, f.wts, cap, f.slot, f.rows_e,
                                                                   f.kept);
@@ -696,13 +715,13 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             gu.m_count = f.kept;
             gu.w_stride = (int64_t)2 * DE * D;
             gu.c_stride = (int64_t)cap * DE;
-            PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st));
+            PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st, e->use_tc, e->m_err));
             GemmArgs gd = gargs(f.act_e, DE, cap, e->r_dn[l], D, DE, f.ye, D);
             gd.a_stride = (int64_t)cap * DE;
             gd.m_count = f.kept;
             gd.w_stride = (int64_t)D * DE;
             gd.c_stride = (int64_t)cap * D;
-            PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st));
+            PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st, e->use_tc, e->m_err));
             k_moe_combine_rows<<<T, 256, 0, st>>>(f.sh, f.ye, cap, f.idx, f.wts, f.slot,
                                                   e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D, f.h);
             PULSAR_LAUNCH_CHECK("prefill moe combine");
@@ -753,7 +772,7 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
                                           lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv);
         GemmArgs g = gargs(w.xn, D, R, e->wqkv[l], QKV, D, w.qkv, QKV);
         if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = w.t_qkv; }
-        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st));
+        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st, e->use_tc, e->m_err));
         const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
         k_qkv_post<KVT><<<R, (H + HKV) * 32, 0, st>>>(
             rows, w.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
@@ -768,14 +787,14 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         PULSAR_LAUNCH_CHECK("wide attention");
         g = gargs(w.att, D, R, e->wo[l], D, D, w.h, D);
         if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = w.t_wo; }
-        PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st));
+        PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st, e->use_tc, e->m_err));
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, w.xn, nullptr,
                                           nullptr);
         const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
         k_router<<<R, E * 32, 0, st>>>(w.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, w.idx, w.wts);
         PULSAR_LAUNCH_CHECK("wide router");
-        PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(w.xn, D, R, e->sh_gu[l], 2 * DS, D, w.act_sh, DS), 1, st));
-        PULSAR_TRY(gemm<GEPI_STORE>(gargs(w.act_sh, DS, R, e->sh_dn[l], D, DS, w.sh, D), 1, st));
+        PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(w.xn, D, R, e->sh_gu[l], 2 * DS, D, w.act_sh, DS), 1, st, e->use_tc, e->m_err));
+        PULSAR_TRY(gemm<GEPI_STORE>(gargs(w.act_sh, DS, R, e->sh_dn[l], D, DS, w.sh, D), 1, st, e->use_tc, e->m_err));
         k_moe_bucket<<<E, 1024, 0, st>>>(w.idx, M4, w.lists, M4, w.cnt);
         k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(w.lists, M4, w.cnt, w.wts, cap, w.slot, w.rows_e, w.kept);
         PULSAR_LAUNCH_CHECK("wide slots");
@@ -784,13 +803,13 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         gu.m_count = w.kept;
         gu.w_stride = (int64_t)2 * DE * D;
         gu.c_stride = (int64_t)cap * DE;
-        PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st));
+        PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st, e->use_tc, e->m_err));
         GemmArgs gd = gargs(w.act_e, DE, cap, e->r_dn[l], D, DE, w.ye, D);
         gd.a_stride = (int64_t)cap * DE;
         gd.m_count = w.kept;
         gd.w_stride = (int64_t)D * DE;
         gd.c_stride = (int64_t)cap * D;
-        PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st));
+        PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st, e->use_tc, e->m_err));
         k_moe_combine_rows<<<R, 256, 0, st>>>(w.sh, w.ye, cap, w.idx, w.wts, w.slot,
                                               e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D, w.h);
         PULSAR_LAUNCH_CHECK("wide moe combine");
@@ -804,7 +823,7 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         const int ld = logits ? ld_logits : e->V;
         GemmArgs g = gargs(w.hn, D, R, e->emb, e->V, D, lg, ld);
         g.softcap = e->cfg.logit_softcap;
-        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st));
+        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st, e->use_tc, e->m_err));
         if (amax) {
             k_argmax_rows<<<R, 1024, 0, st>>>(lg, e->V, ld, amax);
             PULSAR_LAUNCH_CHECK("wide argmax");
@@ -822,8 +841,8 @@ int check_kernel_err(pulsar_engine* e) {
         cudaMemset(e->m_err, 0, 4);
         cudaMemset(e->m_bar, 0, 4);
         cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 2) * 4);
-        set_error("persistent pulse kernel: a bounded wait ran out (grid barrier or weight stream); results of the "
-                  "affected launch are invalid");
+        set_error("a bounded device wait ran out (persistent pulse kernel grid barrier or weight stream, or a "
+                  "tensor-core GEMM's MMA completion); results of the affected launch are invalid");
         return PULSAR_ERR_CUDA;
     }
     return PULSAR_OK;
@@ -1417,6 +1436,14 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
         e->use_mega = v;
         return PULSAR_OK;
     }
+    if (strcmp(name, "tc_gemm") == 0) {
+        if ((value != 0) != e->use_tc) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+            e->graphs.clear();
+        }
+        e->use_tc = value != 0;
+        return PULSAR_OK;
+    }
     if (strcmp(name, "wide") == 0) {
         if ((value != 0) != e->force_wide) {
             for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
@@ -1464,6 +1491,7 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     if (strcmp(name, "megakernel") == 0) { *value = e->use_mega ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "megakernel_grid") == 0) { *value = e->mega_grid; return PULSAR_OK; }
     if (strcmp(name, "wide") == 0) { *value = e->force_wide ? 1 : 0; return PULSAR_OK; }
+    if (strcmp(name, "tc_gemm") == 0) { *value = e->use_tc ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "wide_rows") == 0) { *value = e->wide_rows; return PULSAR_OK; }
     if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "kernel_launches") == 0) { *value = e->n_kernels; return PULSAR_OK; }

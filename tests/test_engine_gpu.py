@@ -270,3 +270,33 @@ def test_rejects_non_consecutive_rows():
         eng.pulse(0, [(0, 4, 5), (0, 6, 7)])
     with pytest.raises(RuntimeError, match="outside"):
         eng.pulse(0, [(0, 10**7, 5)])
+
+
+def test_tensor_core_gemm_matches_simt():
+    """The tcgen05 GEMM (fp32 activations split into bf16 hi + lo parts, 2^-16 relative per
+    product) agrees with the fp32 SIMT GEMM: recipe B amplifies such perturbations about 100x,
+    so logits may move by a few 1e-3; the bound is 1e-2, inside the 2e-2 parity tolerance.
+
+    The prompt has 32 tokens: recipe B routes nearly every token to the same experts (its
+    router is the reference's small init), so longer prompts overflow prefill's expert
+    capacity, and which token is dropped is decided by router-weight near-ties that any
+    rounding difference can flip. Larger GEMM row counts are covered by the batch tests."""
+    eng, m, cfg = _setup("B", torch.float32)
+    T = 32
+    ids = random_prompts(1, T, cfg.vocab_size, seed=21)[0].tolist()
+    pre, wide = {}, {}
+    rows = [(s, T + j, 11 + 5 * j) for s in range(4) for j in range(8)]
+    for tc in (0, 1):
+        eng.set_option("tc_gemm", tc)
+        pre[tc] = eng.prefill(0, ids).cpu()
+        for sl in (1, 2, 3):
+            eng.prefill(sl, ids[sl:] + ids[:sl])
+        use_path(eng, 2)
+        lg, _, _ = eng.pulse(0, rows)
+        wide[tc] = lg.cpu()
+        use_path(eng, 0)
+    eng.set_option("tc_gemm", 1)
+    d = (pre[0] - pre[1]).abs().max().item()
+    assert d < 1e-2, f"prefill logits: tensor-core vs SIMT GEMM differ by {d:.3e}"
+    d = (wide[0] - wide[1]).abs().max().item()
+    assert d < 1e-2, f"many-row pulse logits: tensor-core vs SIMT GEMM differ by {d:.3e}"

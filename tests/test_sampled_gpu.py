@@ -52,7 +52,9 @@ def test_sampled_spec_matches_oracle(recipe, kv, gamma, path):
     eng, m, cfg = _setup(recipe, kv)
     use_path(eng, path)
     T, top_p, seed, seq_id, n = 0.8, 0.95, 7, 3, 24
-    ids = random_prompts(1, 40, cfg.vocab_size, seed=2)[0].tolist()
+    # 32 tokens: recipe B's prefill would overflow its expert capacity beyond that, and the
+    # tokens it drops are decided by router near-ties (see test_tensor_core_gemm_matches_simt)
+    ids = random_prompts(1, 32, cfg.vocab_size, seed=2)[0].tolist()
     okv = O.OracleKV(m, 64)
     pre = O.prefill(m, ids, okv)
     st, trace = O.SpecStats(), []
