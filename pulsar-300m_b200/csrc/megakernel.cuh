@@ -13,11 +13,13 @@
 //
 // Phases per layer (work split evenly over the CTAs, outputs owned by one CTA each; h rows
 // [own0, own1) of every sequence row are owned by one CTA, kept in its shared memory):
-//   A  xn = RMSNorm(h); QKV GEMV rows; gate logits xn.Wg + b (CTAs < 8)
-//   B  attention items (sequence block, kv head, key chunk): q of the 4 heads via
+//   A  xn = RMSNorm(h); QKV GEMV rows
+//   B  gate logits xn.Wg + b on the last 8 CTAs (which usually have no attention item);
+//      attention items (sequence block, kv head, key chunk): q of the 4 heads via
 //      QK-RMSNorm + RoPE (+YaRN); block rows' K/V produced (norm, RoPE, value residual)
-//      and written to the cache by the item that owns their chunk; other keys read from
-//      the cache; split-K partials (m, l, o[64]) per query head and chunk
+//      and written to the cache by the item that owns their chunk; the cached keys of the
+//      chunk arrive through the weight ring for passes of <= 2 rows (issued during phase A);
+//      split-K partials (m, l, o[64]) per query head and chunk
 //   B2 one CTA per (row, query head) merges its chunk partials in a fixed order and applies
 //      the gate sigmoid
 //   C  Wo GEMV, h += (owned rows); partial router logits of the owned rows
@@ -366,9 +368,122 @@ __device__ __forceinline__ void load_kv_row16<float>(const float* p, int part, f
     dst[part * 4 + 3] = u.w;
 }
 
+// ------------------------------------------------------------------ attention item geometry
+// Items of a layer: for each sequence block b (consecutive rows of one slot), HKV x nch_b
+// items (kv head, key chunk). Producer and consumers derive the same geometry from the rows.
+struct AttnGeo {
+    int r0, nr, g, c, nch, chunk, slot, pos0, k0, nk, nold;
+};
+
+__device__ __forceinline__ void attn_block_chunks(const MegaArgs& a, int r0, int r1, bool local, int& chunk, int& nch) {
+    const int pos0 = a.rows[r0].y, posL = a.rows[r1 - 1].y;
+    const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
+    chunk = attn_chunk(posL - lo + 1);
+    nch = (posL - lo + chunk) / chunk;
+}
+
+// Geometry of item `item` given the block starts blk_r0[0..n_blk] (blk_r0[n_blk] = R);
+// false past the last item.
+__device__ __forceinline__ bool attn_geo(const MegaArgs& a, const int* blk_r0, int n_blk, bool local, int item,
+                                         AttnGeo& o) {
+    for (int b = 0; b < n_blk; ++b) {
+        int chunk, nch;
+        attn_block_chunks(a, blk_r0[b], blk_r0[b + 1], local, chunk, nch);
+        if (item < HKV * nch) {
+            o.r0 = blk_r0[b];
+            o.nr = blk_r0[b + 1] - blk_r0[b];
+            o.g = item / nch;
+            o.c = item % nch;
+            o.nch = nch;
+            o.chunk = chunk;
+            o.slot = a.rows[o.r0].x;
+            o.pos0 = a.rows[o.r0].y;
+            const int posL = a.rows[o.r0 + o.nr - 1].y;
+            const int lo = local ? max(0, o.pos0 - WINDOW + 1) : 0;
+            o.k0 = lo + o.c * chunk;
+            const int k1 = min(o.k0 + chunk, posL + 1);
+            o.nk = k1 - o.k0;
+            o.nold = max(0, min(k1, o.pos0) - o.k0);   // keys < pos0 come from the cache
+            return true;
+        }
+        item -= HKV * nch;
+    }
+    return false;
+}
+
+// Passes of at most this many rows stream each attention item's cached K/V chunk through the
+// weight ring (issued during phase A); larger passes load it directly in phase B, because
+// their ring already carries many more routed-expert tiles per layer.
+constexpr int MEGA_RING_KV_MAX_R = 2;
+
+// Keys per ring slot of cached K (or V) rows.
+template <typename KVT>
+constexpr int kv_keys_per_tile() { return MEGA_SLOT / (DH * (int)sizeof(KVT)); }
+
+// Producer: cached K (isv = 0) or V rows of keys [k0, k0 + n) of (slot, head g), in tiles of
+// kv_keys_per_tile keys; a run that wraps around a local layer's ring takes two copies.
+template <typename KVT>
+__device__ __forceinline__ void produce_kv(Ring& g, const KVLayer& L, int slot, int head, int k0, int n, bool isv) {
+    constexpr int KPT = kv_keys_per_tile<KVT>();
+    constexpr uint32_t ROW = DH * sizeof(KVT);
+    for (int k = k0; k < k0 + n && g.ok; k += KPT) {
+        const int m = min(KPT, k0 + n - k);
+        const uint32_t slot_i = g.t % MEGA_NS;
+        const uint32_t use = g.t / MEGA_NS;
+        if (use > 0 && !mbar_wait(&g.s->empty[slot_i], (use - 1) & 1)) { g.ok = false; break; }
+        mbar_arrive_expect_tx(&g.s->full[slot_i], (uint32_t)m * ROW);
+        const KVT* p0 = isv ? kv_v<KVT>(L, slot, head, k) : kv_k<KVT>(L, slot, head, k);
+        const int i0 = k & L.mask;
+        const int m1 = (L.mask >= 0 && i0 + m > L.cap) ? L.cap - i0 : m;
+        tma_load_1d(g.s->ring[slot_i], p0, (uint32_t)m1 * ROW, &g.s->full[slot_i]);
+        if (m1 < m) {
+            const KVT* p1 = isv ? kv_v<KVT>(L, slot, head, k + m1) : kv_k<KVT>(L, slot, head, k + m1);
+            tma_load_1d(g.s->ring[slot_i] + m1 * ROW, p1, (uint32_t)(m - m1) * ROW, &g.s->full[slot_i]);
+        }
+        ++g.t;
+    }
+}
+
+// Consumers (all 15 warps): take the same tiles, widen them to fp32 rows of `dst` (stride
+// DH + 1), release each slot after every warp is done with it.
+template <typename KVT>
+__device__ __forceinline__ void consume_kv(Ring& g, int n, float* dst) {
+    constexpr int KPT = kv_keys_per_tile<KVT>();
+    constexpr int PARTS = DH * (int)sizeof(KVT) / 16;   // 16-byte pieces per row
+    const int tid = threadIdx.x - 32;
+    for (int k = 0; k < n; k += KPT) {
+        const int m = min(KPT, n - k);
+        const uint32_t slot_i = g.t % MEGA_NS;
+        const uint32_t use = g.t / MEGA_NS;
+        if (g.ok && !mbar_wait(&g.s->full[slot_i], use & 1)) g.ok = false;
+        if (g.ok) {
+            const unsigned char* tile = g.s->ring[slot_i];
+            for (int e = tid; e < m * PARTS; e += MEGA_NCT) {
+                const int kk = e / PARTS, part = e % PARTS;
+                const uint4 u = *reinterpret_cast<const uint4*>(tile + kk * DH * sizeof(KVT) + part * 16);
+                float* d = dst + (k + kk) * (DH + 1);
+                if constexpr (sizeof(KVT) == 2) {
+                    float f[8];
+                    bf16x8_to_f32(u, f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) d[part * 8 + i] = f[i];
+                } else {
+                    d[part * 4 + 0] = __uint_as_float(u.x);
+                    d[part * 4 + 1] = __uint_as_float(u.y);
+                    d[part * 4 + 2] = __uint_as_float(u.z);
+                    d[part * 4 + 3] = __uint_as_float(u.w);
+                }
+            }
+        }
+        named_bar_sync(1, MEGA_NCT);
+        if (threadIdx.x == 32 && g.ok) mbar_arrive(&g.s->empty[slot_i]);
+        ++g.t;
+    }
+}
+
 template <int R, typename KVT>
-__device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, int r0, int nr, int g, int c, int nch,
-                                       int chunk, bool first) {
+__device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& ring, int l, int r0, int nr, int g,
+                                       int c, int chunk, bool first) {
     const int tid = threadIdx.x - 32;   // consumer thread 0..479
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
     const bool local = is_local_layer(l);
@@ -387,16 +502,22 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, int l, in
     const float* sin_t = local ? a.sin_l : a.sin_g;
     const int nq = nr * GQA;
     astamp(a, l, 0, first);
-    // 1) cached keys/values of the chunk: every thread issues its 16-byte loads at once
+    // 1) cached keys/values of the chunk: streamed by the producer through the ring, or
+    //    (larger passes) loaded here with every thread's 16-byte loads issued at once
     {
-        constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
         const int nold = max(0, min(k1, pos0) - k0);          // keys < pos0 come from the cache
-        for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
-            const int isv = e >= nold * PARTS;
-            const int ee = isv ? e - nold * PARTS : e;
-            const int kk = ee / PARTS, part = ee % PARTS;
-            const KVT* row = isv ? kv_v<KVT>(L, slot, g, k0 + kk) : kv_k<KVT>(L, slot, g, k0 + kk);
-            load_kv_row16<KVT>(row, part, (isv ? Vs : Ks) + kk * (DH + 1));
+        if constexpr (R <= MEGA_RING_KV_MAX_R) {
+            consume_kv<KVT>(ring, nold, Ks);
+            consume_kv<KVT>(ring, nold, Vs);
+        } else {
+            constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
+            for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
+                const int isv = e >= nold * PARTS;
+                const int ee = isv ? e - nold * PARTS : e;
+                const int kk = ee / PARTS, part = ee % PARTS;
+                const KVT* row = isv ? kv_v<KVT>(L, slot, g, k0 + kk) : kv_k<KVT>(L, slot, g, k0 + kk);
+                load_kv_row16<KVT>(row, part, (isv ? Vs : Ks) + kk * (DH + 1));
+            }
         }
         // rows past the end of a partial chunk: zeros (probabilities are 0 there; 0 * stale
         // shared memory could be NaN)
@@ -599,11 +720,32 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
     if (warp == 0) {
         if (lane != 0) return;
         Ring g{s, 0u, -1, true};
+        int pblk[MEGA_RMAX + 1], pnb = 0;   // sequence blocks of the rows (as the consumers build them)
+        for (int r0 = 0; r0 < R;) {
+            int nr = 1;
+            while (r0 + nr < R && a.rows[r0 + nr].x == a.rows[r0].x) ++nr;
+            pblk[pnb++] = r0;
+            r0 += nr;
+        }
+        pblk[pnb] = R;
         for (int l = 0; l < NL && g.ok; ++l) {
             int r0, r1;
             rows_split(QKV, cta, C, r0, r1);
             produce_rows(g, a.wqkv[l], D * 2, r0, r1, 4);
-            if (cta < H / 2) produce_rows(g, a.gate_w[l], D * 4, 2 * cta, 2 * cta + 2, 2);
+            // gate rows: the last H/2 CTAs, consumed in phase B (usually CTAs without attention items)
+            if (cta >= C - H / 2) {
+                const int gr = 2 * (cta - (C - H / 2));
+                produce_rows(g, a.gate_w[l], D * 4, gr, gr + 2, 2);
+            }
+            if (R <= MEGA_RING_KV_MAX_R) {   // cached K/V chunks of this CTA's attention items (phase B)
+                const bool local = is_local_layer(l);
+                AttnGeo geo;
+                for (int item = cta; g.ok && attn_geo(a, pblk, pnb, local, item, geo); item += C) {
+                    if (geo.nold <= 0) continue;
+                    produce_kv<KVT>(g, a.kvl[l], geo.slot, geo.g, geo.k0, geo.nold, false);
+                    produce_kv<KVT>(g, a.kvl[l], geo.slot, geo.g, geo.k0, geo.nold, true);
+                }
+            }
             rows_split(D, cta, C, r0, r1);
             produce_rows(g, a.wo[l], D * 2, r0, r1, 4);
             {   // shared-expert pairs: a static split, prefetched before the router runs
@@ -816,14 +958,6 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 if (lane < n * R) a.qkv[(int64_t)(lane % R) * QKV + row0 + lane / R] = wo_[lane];
             });
             stamp(a, l, 1);
-            if (cta < H / 2)
-                consume_rows(g, 2 * cta, 2 * cta + 2, 2, [&](const unsigned char* tile, int row0, int n) {
-                    tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xs, s->xoff, wo_);
-                    if (lane < n * R) {
-                        const int h = row0 + lane / R;
-                        a.gate[(lane % R) * H + h] = wo_[lane] + a.gate_b[l][h];
-                    }
-                });
             stamp(a, l, 2);
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
@@ -831,6 +965,19 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         }
         // ---------------- phase B: attention (items owned by this CTA: cta, cta + C, ...)
         {
+            // gate logits xn . Wg + b of two heads on each of the last H/2 CTAs, first (xs
+            // still holds xn; the attention items reuse it)
+            if (cta >= C - H / 2) {
+                const int gr = 2 * (cta - (C - H / 2));
+                consume_rows(g, gr, gr + 2, 2, [&](const unsigned char* tile, int row0, int n) {
+                    tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xs, s->xoff, wo_);
+                    if (lane < n * R) {
+                        const int h = row0 + lane / R;
+                        a.gate[(lane % R) * H + h] = wo_[lane] + a.gate_b[l][h];
+                    }
+                });
+                named_bar_sync(1, MEGA_NCT);   // xs is scratch for the items below
+            }
             int total = 0;
             for (int b = 0; b < s->n_blk; ++b) total += HKV * s->blk_nch[b];
             bool first = true;
@@ -839,7 +986,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 while (rem >= HKV * s->blk_nch[b]) { rem -= HKV * s->blk_nch[b]; ++b; }
                 const int nch = s->blk_nch[b];
                 const int r0 = s->blk_r0[b], nr = s->blk_r0[b + 1] - r0;
-                attn_item<R, KVT>(a, s, l, r0, nr, rem / nch, rem % nch, nch, s->blk_chunk[b], first);
+                attn_item<R, KVT>(a, s, g, l, r0, nr, rem / nch, rem % nch, s->blk_chunk[b], first);
                 first = false;
             }
             stamp(a, l, 4);
