@@ -8,9 +8,10 @@
 // Tile: 128 rows x BN columns per CTA (one M=128, N=BN instruction shape), K in chunks of 64.
 // Operands are staged in shared memory in the K-major, no-swizzle canonical layout: core
 // matrices of 8 rows x 16 bytes stored contiguously (128 B), the 8 K-chunks of a 64-wide
-// chunk at 128 B strides (LBO), 8-row groups at 1 KB strides (SBO). Two stages: the 128
-// threads load and convert chunk i+1 while the tensor core runs chunk i; one thread issues
-// the MMAs and commits them to an mbarrier per stage. The accumulator is read back with
+// chunk at 128 B strides (LBO), 8-row groups at 1 KB strides (SBO). Two stages: while the
+// tensor core runs chunk i, the 128 threads hold chunk i+1's A in registers (all loads issued
+// at once) and copy its W with cp.async; one thread issues the MMAs and commits them to an
+// mbarrier per stage. The accumulator is read back with
 // tcgen05.ld (each warp its 32 lanes = rows) for the epilogue.
 #pragma once
 
@@ -102,46 +103,66 @@ __device__ __forceinline__ int tc_wrow(const GemmArgs& g, int n_tile, int j) {
     return n_tile * BN + j;
 }
 
-// Stage chunk kc (64 columns of K) of the A rows (split into hi/lo) and of the W rows.
-template <int EPI, int BN>
-__device__ __forceinline__ void tc_load_chunk(const GemmArgs& g, TcSmem<BN>* s, int st, int b, int m0, int m_valid,
-                                              int n_tile, int kc) {
-    const int t = threadIdx.x;
-    const int k0 = kc * TC_BK;
-    unsigned char* ahi = reinterpret_cast<unsigned char*>(s->a_hi[st]);
-    unsigned char* alo = reinterpret_cast<unsigned char*>(s->a_lo[st]);
-    // A: 128 rows x 64 fp32 = 2048 float4; thread t takes float4 i = t + 128 * q (row i / 16)
-#pragma unroll 4
+// A chunk of 128 rows x 64 fp32 is 2048 float4: thread t holds float4 i = t + 128 * q, q < 16
+// (row i / 16, columns 4 * (i % 16)); all 16 loads are issued together.
+struct TcARegs {
+    float4 v[16];
+};
+
+__device__ __forceinline__ void tc_load_a(const GemmArgs& g, int b, int m0, int m_valid, int kc, TcARegs& r) {
+    const int t = threadIdx.x, k0 = kc * TC_BK;
+#pragma unroll
     for (int q = 0; q < 16; ++q) {
         const int i = t + TC_THREADS * q;
-        const int r = i >> 4, c4 = (i & 15) * 4;
-        const float* src = tc_arow(g, b, m0 + r, m_valid);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (src) v = *reinterpret_cast<const float4*>(src + k0 + c4);
+        const float* src = tc_arow(g, b, m0 + (i >> 4), m_valid);
+        r.v[q] = src ? *reinterpret_cast<const float4*>(src + k0 + (i & 15) * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// Split the held A chunk into bf16 hi / lo and store both in the canonical layout.
+template <int BN>
+__device__ __forceinline__ void tc_store_a(TcSmem<BN>* s, int st, const TcARegs& r) {
+    const int t = threadIdx.x;
+    unsigned char* ahi = reinterpret_cast<unsigned char*>(s->a_hi[st]);
+    unsigned char* alo = reinterpret_cast<unsigned char*>(s->a_lo[st]);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        const int i = t + TC_THREADS * q;
+        const float4 v = r.v[q];
         const __nv_bfloat16 h0 = __float2bfloat16(v.x), h1 = __float2bfloat16(v.y), h2 = __float2bfloat16(v.z),
                             h3 = __float2bfloat16(v.w);
         const __nv_bfloat16 l0 = __float2bfloat16(v.x - __bfloat162float(h0)),
                             l1 = __float2bfloat16(v.y - __bfloat162float(h1)),
                             l2 = __float2bfloat16(v.z - __bfloat162float(h2)),
                             l3 = __float2bfloat16(v.w - __bfloat162float(h3));
-        const uint32_t off = tc_off(r, c4);   // 4 consecutive k stay inside one 16-byte chunk
+        const uint32_t off = tc_off(i >> 4, (i & 15) * 4);   // 4 consecutive k stay in one 16-byte chunk
         __nv_bfloat162 hp[2] = {__halves2bfloat162(h0, h1), __halves2bfloat162(h2, h3)};
         __nv_bfloat162 lp[2] = {__halves2bfloat162(l0, l1), __halves2bfloat162(l2, l3)};
         *reinterpret_cast<uint2*>(ahi + off) = *reinterpret_cast<uint2*>(hp);
         *reinterpret_cast<uint2*>(alo + off) = *reinterpret_cast<uint2*>(lp);
     }
-    // W: BN rows x 64 bf16 = BN * 8 chunks of 16 B
-    unsigned char* ws = reinterpret_cast<unsigned char*>(s->w[st]);
+}
+
+// W chunk: BN rows x 64 bf16 = BN * 8 pieces of 16 B, copied straight into the canonical
+// layout with cp.async (completion: cp.async.wait_all of the issuing thread).
+template <int EPI, int BN>
+__device__ __forceinline__ void tc_issue_w(const GemmArgs& g, TcSmem<BN>* s, int st, int b, int n_tile, int kc) {
+    const int t = threadIdx.x, k0 = kc * TC_BK;
+    const uint32_t ws = smem_u32(s->w[st]);
     const __nv_bfloat16* W = g.W + (int64_t)b * g.w_stride;
-#pragma unroll 4
+#pragma unroll
     for (int q = 0; q < BN * 8 / TC_THREADS; ++q) {
         const int i = t + TC_THREADS * q;
         const int j = i >> 3, c = i & 7;
         const int n = tc_wrow<EPI, BN>(g, n_tile, j);
-        const uint4 v = *reinterpret_cast<const uint4*>(W + (int64_t)n * g.K + k0 + c * 8);
-        *reinterpret_cast<uint4*>(ws + tc_off(j, c * 8)) = v;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ws + tc_off(j, c * 8)),
+                     "l"(W + (int64_t)n * g.K + k0 + c * 8)
+                     : "memory");
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
 }
+
+__device__ __forceinline__ void tc_wait_w() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <int EPI, int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_flag) {
@@ -172,10 +193,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_
     constexpr uint32_t idesc = tc_idesc<BN>();
     const int nk = g.K / TC_BK;
     uint32_t phase[2] = {0u, 0u};
-    tc_load_chunk<EPI, BN>(g, s, 0, b, m0, m_valid, n_tile, 0);
+    TcARegs ar;
+    tc_issue_w<EPI, BN>(g, s, 0, b, n_tile, 0);
+    tc_load_a(g, b, m0, m_valid, 0, ar);
+    tc_store_a(s, 0, ar);
     for (int kc = 0; kc < nk; ++kc) {
         const int st = kc & 1;
-        tc_fence_proxy_async();   // this thread's generic-proxy smem writes -> tensor-core reads
+        if (kc + 1 < nk) tc_load_a(g, b, m0, m_valid, kc + 1, ar);   // in flight during this chunk's MMAs
+        tc_wait_w();
+        tc_fence_proxy_async();   // this thread's smem writes (stores, cp.async) -> tensor-core reads
         __syncthreads();
         if (threadIdx.x == 0) {
             tc_fence_after();
@@ -194,7 +220,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_
                 if (!mbar_wait(&s->mma_done[st ^ 1], phase[st ^ 1])) s->err = 1;
                 phase[st ^ 1] ^= 1u;
             }
-            tc_load_chunk<EPI, BN>(g, s, st ^ 1, b, m0, m_valid, n_tile, kc + 1);
+            tc_issue_w<EPI, BN>(g, s, st ^ 1, b, n_tile, kc + 1);
+            tc_store_a(s, st ^ 1, ar);
         }
     }
     // the last commit covers every MMA issued before it
