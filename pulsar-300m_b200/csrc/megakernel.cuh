@@ -307,18 +307,20 @@ __device__ __forceinline__ void norm_rows(const float* src, const float* w, floa
                                           float* rinv = nullptr) {
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
     for (int r = cw; r < R; r += MEGA_NCW) {
-        float v[32];
+        float v[32], wv[32];
         float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             v[i] = __ldcg(src + (int64_t)r * D + i * 32 + lane);   // written by other CTAs: bypass L1
-            ss += v[i] * v[i];
+            wv[i] = __ldg(w + i * 32 + lane);                      // in flight with the rows
         }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
         ss = warp_sum(ss);
         const float inv = rsqrtf(ss / (float)D + eps);
         if (rinv && lane == 0) rinv[r] = inv;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[r * D + i * 32 + lane] = w[i * 32 + lane] * (v[i] * inv);
+        for (int i = 0; i < 32; ++i) dst[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
     }
 }
 
@@ -539,8 +541,8 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
             const float x1 = __ldcg(src + lane), x2 = __ldcg(src + lane + 32);
             const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + a.eps);
             const float* qw = a.qn[l] + h * DH;
-            const float q1 = qw[lane] * (x1 * inv), q2 = qw[lane + 32] * (x2 * inv);
-            const float cs = cos_t[(int64_t)pos * 32 + lane], sn = sin_t[(int64_t)pos * 32 + lane];
+            const float q1 = __ldg(qw + lane) * (x1 * inv), q2 = __ldg(qw + lane + 32) * (x2 * inv);
+            const float cs = __ldg(cos_t + (int64_t)pos * 32 + lane), sn = __ldg(sin_t + (int64_t)pos * 32 + lane);
             float y1 = q1 * cs - q2 * sn, y2 = q2 * cs + q1 * sn;
             if (!local && pos + 1 > a.base_seq_len) {
                 const double b = (double)a.base_seq_len;
@@ -569,8 +571,8 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
             }
             const float inv = rsqrtf(warp_sum(e1 * e1 + e2 * e2) / (float)DH + a.eps);
             const float* kw = a.kn[l] + g * DH;
-            const float b1 = kw[lane] * (e1 * inv), b2 = kw[lane + 32] * (e2 * inv);
-            const float cs = cos_t[(int64_t)key * 32 + lane], sn = sin_t[(int64_t)key * 32 + lane];
+            const float b1 = __ldg(kw + lane) * (e1 * inv), b2 = __ldg(kw + lane + 32) * (e2 * inv);
+            const float cs = __ldg(cos_t + (int64_t)key * 32 + lane), sn = __ldg(sin_t + (int64_t)key * 32 + lane);
             const float y1 = b1 * cs - b2 * sn, y2 = b2 * cs + b1 * sn;
             KVT* kp = kv_k<KVT>(L, slot, g, key);
             KVT* vp = kv_v<KVT>(L, slot, g, key);
@@ -924,16 +926,17 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             if (l == 0) {
                 // normalise in place (each warp owns its rows)
                 for (int r = cw; r < R; r += MEGA_NCW) {
-                    float v[32];
+                    float v[32], wv[32];
                     float ss = 0.f;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         v[i] = xs[r * D + i * 32 + lane];
+                        wv[i] = __ldg(a.attn_norm[l] + i * 32 + lane);
                         ss += v[i] * v[i];
                     }
                     const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = a.attn_norm[l][i * 32 + lane] * (v[i] * inv);
+                    for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
                 }
             } else {
                 norm_rows<R>(a.h, a.attn_norm[l], eps, xs);
@@ -1033,6 +1036,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         }
         // ---------------- phase D: router (sum of the CTAs' partials), shared + routed up-projections
         {
+            float ebias_lane;
             {
                 // router logits = fixed-order sum over CTAs of the partials / rms: thread t adds
                 // float4 column t % (R*E/4) of CTAs t / (R*E/4), + G, ... (its loads issued
@@ -1045,6 +1049,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 const bool active = t < G * NC4;
                 const float4* src = reinterpret_cast<const float4*>(a.rpart) + col;
                 float4 pv[MAXL];
+                ebias_lane = (lane < E) ? __ldg(a.ebias[l] + lane) : 0.f;   // for the top-k below
 #pragma unroll
                 for (int k = 0; k < MAXL; ++k) {
                     const int c = cg + k * G;
@@ -1092,7 +1097,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 const float lg = lane < E ? s->logits[r][lane] : 0.f;
                 const float mean = warp_sum(lg) / (float)E;
                 const float sg = sigmoidf_(lg - mean);
-                float b = lane < E ? sg + a.ebias[l][lane] : -INFINITY;
+                float b = lane < E ? sg + ebias_lane : -INFINITY;
                 float sel_s[TOPK];
                 int sel_i[TOPK];
                 unsigned used = 0;
