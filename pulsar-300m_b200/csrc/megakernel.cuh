@@ -680,14 +680,18 @@ static __device__ __noinline__ void attn_merge(const MegaArgs& a, MegaSmem* s, i
     st[2 + 32 + lane] = o2;
     named_bar_sync(1, MEGA_NCT);
     if (cw == 0) {
-        float Mx = -INFINITY;
-        for (int w = 0; w < MEGA_NCW; ++w) Mx = fmaxf(Mx, s->stage[w * PART]);
-        float L = 0.f, p1 = 0.f, p2 = 0.f;
+        // lane w < 15 holds warp w's (m, l); the weights exp(m_w - max) are computed in
+        // parallel and broadcast, so the fold below is FMAs only
+        const float mw = lane < MEGA_NCW ? s->stage[lane * PART] : -INFINITY;
+        const float lw = lane < MEGA_NCW ? s->stage[lane * PART + 1] : 0.f;
+        const float Mx = warp_max(mw);
+        const float ww = (mw == -INFINITY) ? 0.f : expf(mw - Mx);
+        const float L = warp_sum(ww * lw);
+        float p1 = 0.f, p2 = 0.f;
+#pragma unroll
         for (int w = 0; w < MEGA_NCW; ++w) {
+            const float wt = __shfl_sync(0xffffffffu, ww, w);
             const float* q = s->stage + w * PART;
-            if (q[0] == -INFINITY) continue;
-            const float wt = expf(q[0] - Mx);
-            L += wt * q[1];
             p1 += wt * q[2 + lane];
             p2 += wt * q[2 + 32 + lane];
         }
