@@ -429,6 +429,26 @@ def run_kernel_shapes(args):
     eng.close()
 
 
+def run_prefill_profile(args):
+    """The bench engine and prompt: one warm-up prefill, then one prefill between
+    cudaProfilerStart and cudaProfilerStop (ncu --profile-from-start off)."""
+    from pulsar_b200.config import PulsarConfig
+    from pulsar_b200.engine import DeviceEngine
+    from pulsar_b200.weights import make_state_dict, random_prompts
+    cfg = PulsarConfig(eos_token_id=-1)
+    eng = DeviceEngine(cfg, make_state_dict(cfg, recipe=args.recipe, seed=0), device=0, max_batch=1,
+                       max_seq_len=PROMPT + NEW + 64, max_prefill=PROMPT, kv_dtype=torch.bfloat16)
+    ids = random_prompts(1, PROMPT, cfg.vocab_size, seed=0)[0].tolist()
+    eng.prefill(0, ids)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    eng.prefill(0, ids)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"prefill_profile": PROMPT}), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -442,6 +462,8 @@ def main():
     ap.add_argument("--kernel-reps", type=int, default=20)
     ap.add_argument("--kernel-shapes", action="store_true",
                     help="launch each round shape of k_mega_pulse once after the prefill and exit (ncu captures)")
+    ap.add_argument("--prefill-profile", action="store_true",
+                    help="one profiled prefill of the bench prompt between cudaProfilerStart/Stop (ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -449,6 +471,8 @@ def main():
         run_reference(args)
     elif args.kernel_shapes:
         run_kernel_shapes(args)
+    elif args.prefill_profile:
+        run_prefill_profile(args)
     else:
         run_engine(args)
 
