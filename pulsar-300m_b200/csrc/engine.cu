@@ -311,6 +311,9 @@ struct pulsar_engine {
     int wide_rows = 0;
     bool force_wide = false;   // option "wide": every pulse pass through the wide path
     bool use_tc = true;        // option "tc_gemm": tensor-core GEMMs (prefill, wide path)
+    // bf16 hi / lo split of a GEMM's activations (tensor-core path), split_elems each
+    __nv_bfloat16 *split_hi = nullptr, *split_lo = nullptr;
+    int64_t split_elems = 0;
     struct {
         float *h, *h_in, *xn, *qkv, *q, *vfirst, *part, *att, *act_sh, *sh, *hn, *t_qkv, *t_wo, *wts, *act_e, *ye,
             *logits;
@@ -616,12 +619,16 @@ int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev,
 
 // ------------------------------------------------------------------ prefill
 // Tiled GEMM launch: the tcgen05 tensor-core kernel when the shape fits its tiles (K a
-// multiple of 64, output columns a multiple of 128, or of 64 for SWIGLU), else the SIMT kernel.
+// multiple of 64, output columns a multiple of 128, or of 64 for SWIGLU; 16-byte aligned rows)
+// and the activation split fits the engine's hi/lo buffers, else the SIMT kernel.
 template <int EPI>
-int gemm(const GemmArgs& g, int batches, cudaStream_t st, bool tc, int* err_flag) {
+int gemm(pulsar_engine* e, const GemmArgs& g, int batches, cudaStream_t st) {
     constexpr int BN = 128;
-    const bool fits = g.K % TC_BK == 0 && (EPI == GEPI_SWIGLU ? (g.N / 2) % (BN / 2) == 0 : g.N % BN == 0);
-    if (tc && fits) {
+    const bool fits = g.K % TC_BK == 0 && (EPI == GEPI_SWIGLU ? (g.N / 2) % (BN / 2) == 0 : g.N % BN == 0) &&
+                      (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 && g.ldc % 4 == 0 && g.c_stride % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 4 == 0 && g.a_stride % 4 == 0 &&
+                      (int64_t)batches * g.M * g.K <= e->split_elems;
+    if (e->use_tc && fits) {
         static bool configured = false;   // per instantiation
         if (!configured) {
             PULSAR_TRY(cuda_status(cudaFuncSetAttribute(k_tc_gemm<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -629,9 +636,12 @@ int gemm(const GemmArgs& g, int batches, cudaStream_t st, bool tc, int* err_flag
                                    "k_tc_gemm shared memory"));
             configured = true;
         }
+        const int64_t per_batch = (int64_t)g.M * g.K / 8;
+        k_split_hilo<<<dim3((unsigned)((per_batch + 255) / 256), batches), 256, 0, st>>>(g, e->split_hi, e->split_lo);
+        PULSAR_TRY(launch_status("k_split_hilo"));
         const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2) / (BN / 2) : g.N / BN;
         dim3 grid(ntiles, (g.M + TC_BM - 1) / TC_BM, batches);
-        k_tc_gemm<EPI, BN><<<grid, TC_THREADS, tc_smem_bytes<BN>(), st>>>(g, err_flag);
+        k_tc_gemm<EPI, BN><<<grid, TC_THREADS, tc_smem_bytes<BN>(), st>>>(g, e->split_hi, e->split_lo, e->m_err);
         return launch_status("k_tc_gemm");
     }
     const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2 + 31) / 32 : (g.N + GB_N - 1) / GB_N;
@@ -683,7 +693,7 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
                                               lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, f.t);
             GemmArgs g = gargs(f.xn, D, T, e->wqkv[l], QKV, D, f.qkv, QKV);
             if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = f.t; }
-            PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st, e->use_tc, e->m_err));
+            PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
             const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
             k_qkv_post_prefill<KVT><<<T, (H + HKV) * 32, 0, st>>>(
                 slot, T, f.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
@@ -697,15 +707,15 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             PULSAR_LAUNCH_CHECK("prefill attention");
             g = gargs(f.att, D, T, e->wo[l], D, D, f.h, D);
             if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = f.t; }
-            PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st, e->use_tc, e->m_err));
+            PULSAR_TRY(gemm<GEPI_ADD>(e, g, 1, st));
             k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, f.xn,
                                               nullptr, nullptr);
             const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
             k_router<<<T, E * 32, 0, st>>>(f.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, f.idx,
                                            f.wts);
             PULSAR_LAUNCH_CHECK("prefill router");
-            PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(f.xn, D, T, e->sh_gu[l], 2 * DS, D, f.act_sh, DS), 1, st, e->use_tc, e->m_err));
-            PULSAR_TRY(gemm<GEPI_STORE>(gargs(f.act_sh, DS, T, e->sh_dn[l], D, DS, f.sh, D), 1, st, e->use_tc, e->m_err));
+            PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gargs(f.xn, D, T, e->sh_gu[l], 2 * DS, D, f.act_sh, DS), 1, st));
+            PULSAR_TRY(gemm<GEPI_STORE>(e, gargs(f.act_sh, DS, T, e->sh_dn[l], D, DS, f.sh, D), 1, st));
             k_moe_bucket<<<E, 1024, 0, st>>>(f.idx, M4, f.lists, M4, f.cnt);
             k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(f.lists, M4, f.cnt, f.wts, cap, f.slot, f.rows_e,
                                                                   f.kept);
@@ -715,13 +725,13 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             gu.m_count = f.kept;
             gu.w_stride = (int64_t)2 * DE * D;
             gu.c_stride = (int64_t)cap * DE;
-            PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st, e->use_tc, e->m_err));
+            PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gu, E, st));
             GemmArgs gd = gargs(f.act_e, DE, cap, e->r_dn[l], D, DE, f.ye, D);
             gd.a_stride = (int64_t)cap * DE;
             gd.m_count = f.kept;
             gd.w_stride = (int64_t)D * DE;
             gd.c_stride = (int64_t)cap * D;
-            PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st, e->use_tc, e->m_err));
+            PULSAR_TRY(gemm<GEPI_STORE>(e, gd, E, st));
             k_moe_combine_rows<<<T, 256, 0, st>>>(f.sh, f.ye, cap, f.idx, f.wts, f.slot,
                                                   e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D, f.h);
             PULSAR_LAUNCH_CHECK("prefill moe combine");
@@ -772,7 +782,7 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
                                           lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv);
         GemmArgs g = gargs(w.xn, D, R, e->wqkv[l], QKV, D, w.qkv, QKV);
         if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = w.t_qkv; }
-        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st, e->use_tc, e->m_err));
+        PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
         const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
         k_qkv_post<KVT><<<R, (H + HKV) * 32, 0, st>>>(
             rows, w.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
@@ -787,14 +797,14 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         PULSAR_LAUNCH_CHECK("wide attention");
         g = gargs(w.att, D, R, e->wo[l], D, D, w.h, D);
         if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = w.t_wo; }
-        PULSAR_TRY(gemm<GEPI_ADD>(g, 1, st, e->use_tc, e->m_err));
+        PULSAR_TRY(gemm<GEPI_ADD>(e, g, 1, st));
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, w.xn, nullptr,
                                           nullptr);
         const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
         k_router<<<R, E * 32, 0, st>>>(w.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, w.idx, w.wts);
         PULSAR_LAUNCH_CHECK("wide router");
-        PULSAR_TRY(gemm<GEPI_SWIGLU>(gargs(w.xn, D, R, e->sh_gu[l], 2 * DS, D, w.act_sh, DS), 1, st, e->use_tc, e->m_err));
-        PULSAR_TRY(gemm<GEPI_STORE>(gargs(w.act_sh, DS, R, e->sh_dn[l], D, DS, w.sh, D), 1, st, e->use_tc, e->m_err));
+        PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gargs(w.xn, D, R, e->sh_gu[l], 2 * DS, D, w.act_sh, DS), 1, st));
+        PULSAR_TRY(gemm<GEPI_STORE>(e, gargs(w.act_sh, DS, R, e->sh_dn[l], D, DS, w.sh, D), 1, st));
         k_moe_bucket<<<E, 1024, 0, st>>>(w.idx, M4, w.lists, M4, w.cnt);
         k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(w.lists, M4, w.cnt, w.wts, cap, w.slot, w.rows_e, w.kept);
         PULSAR_LAUNCH_CHECK("wide slots");
@@ -803,13 +813,13 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         gu.m_count = w.kept;
         gu.w_stride = (int64_t)2 * DE * D;
         gu.c_stride = (int64_t)cap * DE;
-        PULSAR_TRY(gemm<GEPI_SWIGLU>(gu, E, st, e->use_tc, e->m_err));
+        PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gu, E, st));
         GemmArgs gd = gargs(w.act_e, DE, cap, e->r_dn[l], D, DE, w.ye, D);
         gd.a_stride = (int64_t)cap * DE;
         gd.m_count = w.kept;
         gd.w_stride = (int64_t)D * DE;
         gd.c_stride = (int64_t)cap * D;
-        PULSAR_TRY(gemm<GEPI_STORE>(gd, E, st, e->use_tc, e->m_err));
+        PULSAR_TRY(gemm<GEPI_STORE>(e, gd, E, st));
         k_moe_combine_rows<<<R, 256, 0, st>>>(w.sh, w.ye, cap, w.idx, w.wts, w.slot,
                                               e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D, w.h);
         PULSAR_LAUNCH_CHECK("wide moe combine");
@@ -823,7 +833,7 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         const int ld = logits ? ld_logits : e->V;
         GemmArgs g = gargs(w.hn, D, R, e->emb, e->V, D, lg, ld);
         g.softcap = e->cfg.logit_softcap;
-        PULSAR_TRY(gemm<GEPI_STORE>(g, 1, st, e->use_tc, e->m_err));
+        PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
         if (amax) {
             k_argmax_rows<<<R, 1024, 0, st>>>(lg, e->V, ld, amax);
             PULSAR_LAUNCH_CHECK("wide argmax");
@@ -1044,6 +1054,13 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&x.slot, (size_t)RW * TOPK)) || (st = e->wmalloc(&x.rows_e, (size_t)E * RW)) ||
         (st = e->wmalloc(&x.kept, E)))
         return fail(st);
+    {   // activation split for the tensor-core GEMMs: the largest A of prefill or a wide pass
+        const int cap_pf = prefill_capacity(cfg->max_prefill);
+        e->split_elems = (int64_t)E * std::max(cap_pf, RW) * std::max(D, DS);
+        e->split_elems = std::max(e->split_elems, (int64_t)cfg->max_prefill * std::max(D, DS));
+        if ((st = e->wmalloc(&e->split_hi, (size_t)e->split_elems)) || (st = e->wmalloc(&e->split_lo, (size_t)e->split_elems)))
+            return fail(st);
+    }
     // prefill workspace
     auto& f = e->pf;
     const int T = cfg->max_prefill;

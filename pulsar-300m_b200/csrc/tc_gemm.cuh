@@ -8,11 +8,12 @@
 // Tile: 128 rows x BN columns per CTA (one M=128, N=BN instruction shape), K in chunks of 64.
 // Operands are staged in shared memory in the K-major, no-swizzle canonical layout: core
 // matrices of 8 rows x 16 bytes stored contiguously (128 B), the 8 K-chunks of a 64-wide
-// chunk at 128 B strides (LBO), 8-row groups at 1 KB strides (SBO). Two stages: while the
-// tensor core runs chunk i, the 128 threads hold chunk i+1's A in registers (all loads issued
-// at once) and copy its W with cp.async; one thread issues the MMAs and commits them to an
-// mbarrier per stage. The accumulator is read back with
-// tcgen05.ld (each warp its 32 lanes = rows) for the epilogue.
+// chunk at 128 B strides (LBO), 8-row groups at 1 KB strides (SBO). The activations are split
+// into bf16 hi / lo once per GEMM (k_split_hilo, gathered rows compacted per batch); then every
+// operand chunk (A hi, A lo, W) is copied with cp.async into a 4-stage ring, three chunks ahead
+// of the tensor core. One thread issues the MMAs and commits them to an mbarrier per stage.
+// The accumulator is read back with tcgen05.ld (each warp its 32 lanes = rows) for the
+// epilogue (vectorised stores).
 #pragma once
 
 #include <stdint.h>
@@ -26,13 +27,16 @@ constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;
 constexpr int TC_THREADS = 128;
 
+constexpr int TC_STAGES = 4;
+
 template <int BN>
 struct TcSmem {
     // per stage: A hi, A lo [128 x 64] bf16, W [BN x 64] bf16 (canonical layout)
-    alignas(1024) __nv_bfloat16 a_hi[2][TC_BM * TC_BK];
-    alignas(1024) __nv_bfloat16 a_lo[2][TC_BM * TC_BK];
-    alignas(1024) __nv_bfloat16 w[2][BN * TC_BK];
-    uint64_t mma_done[2];
+    alignas(1024) __nv_bfloat16 a_hi[TC_STAGES][TC_BM * TC_BK];
+    alignas(1024) __nv_bfloat16 a_lo[TC_STAGES][TC_BM * TC_BK];
+    alignas(1024) __nv_bfloat16 w[TC_STAGES][BN * TC_BK];
+    uint64_t mma_done[TC_STAGES];
+    uint64_t final_done;
     uint32_t tmem_base;
     int err;
 };
@@ -103,69 +107,71 @@ __device__ __forceinline__ int tc_wrow(const GemmArgs& g, int n_tile, int j) {
     return n_tile * BN + j;
 }
 
-// A chunk of 128 rows x 64 fp32 is 2048 float4: thread t holds float4 i = t + 128 * q, q < 16
-// (row i / 16, columns 4 * (i % 16)); all 16 loads are issued together.
-struct TcARegs {
-    float4 v[16];
-};
-
-__device__ __forceinline__ void tc_load_a(const GemmArgs& g, int b, int m0, int m_valid, int kc, TcARegs& r) {
-    const int t = threadIdx.x, k0 = kc * TC_BK;
+// Split of the activation rows: hi/lo [batch][M][K] bf16 (row m of batch b = the GEMM's
+// A row of tile row m, gathered rows compacted); rows past the batch's valid count are not
+// written (the GEMM zero-fills them). Thread: 8 consecutive k.
+__global__ void __launch_bounds__(256) k_split_hilo(GemmArgs g, __nv_bfloat16* __restrict__ hi,
+                                                    __nv_bfloat16* __restrict__ lo) {
+    const int b = blockIdx.y;
+    const int m_valid = g.m_count ? g.m_count[b] : g.M;
+    const int per_row = g.K / 8;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int m = (int)(i / per_row), k = (int)(i % per_row) * 8;
+    if (m >= m_valid) return;
+    const float* src = tc_arow(g, b, m, m_valid) + k;
+    const float4 v0 = *reinterpret_cast<const float4*>(src), v1 = *reinterpret_cast<const float4*>(src + 4);
+    const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    __nv_bfloat16 h[8], l[8];
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-        const int i = t + TC_THREADS * q;
-        const float* src = tc_arow(g, b, m0 + (i >> 4), m_valid);
-        r.v[q] = src ? *reinterpret_cast<const float4*>(src + k0 + (i & 15) * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < 8; ++j) {
+        h[j] = __float2bfloat16(x[j]);
+        l[j] = __float2bfloat16(x[j] - __bfloat162float(h[j]));
     }
+    const int64_t o = ((int64_t)b * g.M + m) * g.K + k;
+    *reinterpret_cast<uint4*>(hi + o) = *reinterpret_cast<const uint4*>(h);
+    *reinterpret_cast<uint4*>(lo + o) = *reinterpret_cast<const uint4*>(l);
 }
 
-// Split the held A chunk into bf16 hi / lo and store both in the canonical layout.
-template <int BN>
-__device__ __forceinline__ void tc_store_a(TcSmem<BN>* s, int st, const TcARegs& r) {
-    const int t = threadIdx.x;
-    unsigned char* ahi = reinterpret_cast<unsigned char*>(s->a_hi[st]);
-    unsigned char* alo = reinterpret_cast<unsigned char*>(s->a_lo[st]);
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-        const int i = t + TC_THREADS * q;
-        const float4 v = r.v[q];
-        const __nv_bfloat16 h0 = __float2bfloat16(v.x), h1 = __float2bfloat16(v.y), h2 = __float2bfloat16(v.z),
-                            h3 = __float2bfloat16(v.w);
-        const __nv_bfloat16 l0 = __float2bfloat16(v.x - __bfloat162float(h0)),
-                            l1 = __float2bfloat16(v.y - __bfloat162float(h1)),
-                            l2 = __float2bfloat16(v.z - __bfloat162float(h2)),
-                            l3 = __float2bfloat16(v.w - __bfloat162float(h3));
-        const uint32_t off = tc_off(i >> 4, (i & 15) * 4);   // 4 consecutive k stay in one 16-byte chunk
-        __nv_bfloat162 hp[2] = {__halves2bfloat162(h0, h1), __halves2bfloat162(h2, h3)};
-        __nv_bfloat162 lp[2] = {__halves2bfloat162(l0, l1), __halves2bfloat162(l2, l3)};
-        *reinterpret_cast<uint2*>(ahi + off) = *reinterpret_cast<uint2*>(hp);
-        *reinterpret_cast<uint2*>(alo + off) = *reinterpret_cast<uint2*>(lp);
-    }
+__device__ __forceinline__ void tc_cp16(uint32_t dst, const void* src, bool valid) {
+    // zero-fill when !valid (source size 0)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
 }
 
-// W chunk: BN rows x 64 bf16 = BN * 8 pieces of 16 B, copied straight into the canonical
-// layout with cp.async (completion: cp.async.wait_all of the issuing thread).
+// Issue chunk kc (64 columns of K) of A hi, A lo and W into stage st (one cp.async group).
 template <int EPI, int BN>
-__device__ __forceinline__ void tc_issue_w(const GemmArgs& g, TcSmem<BN>* s, int st, int b, int n_tile, int kc) {
+__device__ __forceinline__ void tc_issue_chunk(const GemmArgs& g, const __nv_bfloat16* ahi,
+                                               const __nv_bfloat16* alo, TcSmem<BN>* s, int st, int b, int m0,
+                                               int m_valid, int n_tile, int kc) {
     const int t = threadIdx.x, k0 = kc * TC_BK;
-    const uint32_t ws = smem_u32(s->w[st]);
+    const uint32_t sh = smem_u32(s->a_hi[st]), sl = smem_u32(s->a_lo[st]), sw = smem_u32(s->w[st]);
+    // A: 128 rows x 8 pieces of 16 B, for hi and lo
+#pragma unroll
+    for (int q = 0; q < TC_BM * 8 / TC_THREADS; ++q) {
+        const int i = t + TC_THREADS * q;
+        const int r = i >> 3, c = i & 7;
+        const bool ok = m0 + r < m_valid;
+        const int64_t off = ((int64_t)b * g.M + (ok ? m0 + r : 0)) * g.K + k0 + c * 8;
+        tc_cp16(sh + tc_off(r, c * 8), ahi + off, ok);
+        tc_cp16(sl + tc_off(r, c * 8), alo + off, ok);
+    }
     const __nv_bfloat16* W = g.W + (int64_t)b * g.w_stride;
 #pragma unroll
     for (int q = 0; q < BN * 8 / TC_THREADS; ++q) {
         const int i = t + TC_THREADS * q;
         const int j = i >> 3, c = i & 7;
         const int n = tc_wrow<EPI, BN>(g, n_tile, j);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ws + tc_off(j, c * 8)),
-                     "l"(W + (int64_t)n * g.K + k0 + c * 8)
-                     : "memory");
+        tc_cp16(sw + tc_off(j, c * 8), W + (int64_t)n * g.K + k0 + c * 8, true);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__device__ __forceinline__ void tc_wait_w() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void tc_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int EPI, int BN>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_flag) {
+__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, const __nv_bfloat16* __restrict__ ahi,
+                                                           const __nv_bfloat16* __restrict__ alo, int* err_flag) {
     extern __shared__ __align__(1024) unsigned char tc_raw[];
     TcSmem<BN>* s = reinterpret_cast<TcSmem<BN>*>(tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023));
     const int b = blockIdx.z;
@@ -175,8 +181,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_
     const int n_tile = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        mbar_init(&s->mma_done[0], 1);
-        mbar_init(&s->mma_done[1], 1);
+        for (int i = 0; i < TC_STAGES; ++i) mbar_init(&s->mma_done[i], 1);
+        mbar_init(&s->final_done, 1);
         s->err = 0;
         fence_mbar_init();
     }
@@ -192,16 +198,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_
     const uint32_t tmem = s->tmem_base;
     constexpr uint32_t idesc = tc_idesc<BN>();
     const int nk = g.K / TC_BK;
-    uint32_t phase[2] = {0u, 0u};
-    TcARegs ar;
-    tc_issue_w<EPI, BN>(g, s, 0, b, n_tile, 0);
-    tc_load_a(g, b, m0, m_valid, 0, ar);
-    tc_store_a(s, 0, ar);
+    // prologue: chunks 0 .. STAGES-2 (one cp.async group each, empty groups past the end)
+#pragma unroll
+    for (int c = 0; c < TC_STAGES - 1; ++c) {
+        if (c < nk) tc_issue_chunk<EPI, BN>(g, ahi, alo, s, c, b, m0, m_valid, n_tile, c);
+        tc_commit_group();
+    }
     for (int kc = 0; kc < nk; ++kc) {
-        const int st = kc & 1;
-        if (kc + 1 < nk) tc_load_a(g, b, m0, m_valid, kc + 1, ar);   // in flight during this chunk's MMAs
-        tc_wait_w();
-        tc_fence_proxy_async();   // this thread's smem writes (stores, cp.async) -> tensor-core reads
+        const int st = kc % TC_STAGES;
+        tc_wait_group<TC_STAGES - 2>();   // chunk kc landed (this thread's copies)
+        tc_fence_proxy_async();           // -> visible to the tensor core (async proxy)
         __syncthreads();
         if (threadIdx.x == 0) {
             tc_fence_after();
@@ -213,20 +219,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_
                 tc_mma(tmem, tc_desc(al + ks * 256), bd, idesc, 1u);
             }
             tc_commit(&s->mma_done[st]);
+            if (kc == nk - 1) tc_commit(&s->final_done);
         }
-        if (kc + 1 < nk) {
-            // the other stage is free once the MMAs of chunk kc-1 completed
+        // refill the stage of chunk kc-1 with chunk kc+STAGES-1 once that chunk's MMAs are done
+        const int nc = kc + TC_STAGES - 1;
+        if (nc < nk) {
             if (kc >= 1) {
-                if (!mbar_wait(&s->mma_done[st ^ 1], phase[st ^ 1])) s->err = 1;
-                phase[st ^ 1] ^= 1u;
+                const int ps = (kc - 1) % TC_STAGES;
+                if (!mbar_wait(&s->mma_done[ps], ((kc - 1) / TC_STAGES) & 1)) s->err = 1;
             }
-            tc_issue_w<EPI, BN>(g, s, st ^ 1, b, n_tile, kc + 1);
-            tc_store_a(s, st ^ 1, ar);
+            tc_issue_chunk<EPI, BN>(g, ahi, alo, s, nc % TC_STAGES, b, m0, m_valid, n_tile, nc);
         }
+        tc_commit_group();
     }
-    // the last commit covers every MMA issued before it
-    const int last = (nk - 1) & 1;
-    if (!mbar_wait(&s->mma_done[last], phase[last])) s->err = 1;
+    if (!mbar_wait(&s->final_done, 0)) s->err = 1;
     tc_fence_after();
     __syncthreads();
     if (s->err) {
@@ -235,7 +241,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_
         // epilogue: warp w holds rows 32w..32w+31 (lanes), 16 columns per load
         const int m = m0 + warp * 32 + lane;
         const bool row_ok = m < m_valid;
-        float* C = g.C + (int64_t)b * g.c_stride;
+        float* C = g.C + (int64_t)b * g.c_stride + (int64_t)m * g.ldc;
         const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
         if (EPI == GEPI_SWIGLU) {
             const int n0 = n_tile * (BN / 2);
@@ -245,29 +251,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, int* err_
                 tc_ld16(lane_addr + BN / 2 + c, up);
                 if (row_ok)
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) C[(int64_t)m * g.ldc + n0 + c + i] = siluf_(gt[i]) * up[i];
+                    for (int i = 0; i < 16; i += 4)
+                        *reinterpret_cast<float4*>(C + n0 + c + i) =
+                            make_float4(siluf_(gt[i]) * up[i], siluf_(gt[i + 1]) * up[i + 1],
+                                        siluf_(gt[i + 2]) * up[i + 2], siluf_(gt[i + 3]) * up[i + 3]);
             }
         } else {
             for (int c = 0; c < BN; c += 16) {
                 float v[16];
                 tc_ld16(lane_addr + c, v);
                 if (!row_ok) continue;
+                const int nb = n_tile * BN + c;
+                if (g.lora_b) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int n = n_tile * BN + c + i;
-                    float y = v[i];
-                    if (g.lora_b) {
+                    for (int i = 0; i < 16; ++i) {
                         float d = 0.f;
 #pragma unroll
                         for (int q = 0; q < LORA_R; ++q)
-                            d += g.lora_b[(int64_t)n * LORA_R + q] * g.lora_t[(int64_t)m * LORA_R + q];
-                        y += d;
+                            d += g.lora_b[(int64_t)(nb + i) * LORA_R + q] * g.lora_t[(int64_t)m * LORA_R + q];
+                        v[i] += d;
                     }
+                }
+#pragma unroll
+                for (int i = 0; i < 16; i += 4) {
+                    float4* dst = reinterpret_cast<float4*>(C + nb + i);
                     if (EPI == GEPI_ADD) {
-                        C[(int64_t)m * g.ldc + n] += y;
+                        const float4 o = *dst;
+                        *dst = make_float4(o.x + v[i], o.y + v[i + 1], o.z + v[i + 2], o.w + v[i + 3]);
                     } else {
-                        if (g.softcap > 0.f) y = g.softcap * tanhf(y / g.softcap);
-                        C[(int64_t)m * g.ldc + n] = y;
+                        float4 y = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                        if (g.softcap > 0.f) {
+                            const float sc = g.softcap;
+                            y = make_float4(sc * tanhf(y.x / sc), sc * tanhf(y.y / sc), sc * tanhf(y.z / sc),
+                                            sc * tanhf(y.w / sc));
+                        }
+                        *dst = y;
                     }
                 }
             }
