@@ -194,88 +194,152 @@ __global__ void __launch_bounds__((H + HKV) * 32) k_qkv_post_prefill(
     }
 }
 
-// Causal prefill attention with the reference's masks (src/infer.py:428-435):
-// query i attends keys [kbase, kbase + min(i, S-1)] where, on local layers with T > WINDOW,
-// S = WINDOW and kbase = T - WINDOW (SDPA is_causal aligned top-left on the truncated
-// cache); otherwise S = T, kbase = 0 (plain causal). Block = 32 queries x one head,
-// 8 warps x 4 queries; key tiles of 64 staged in shared memory; online softmax in fp32.
-constexpr int PA_Q = 32, PA_K = 64;
+// Causal prefill attention of one head over the prompt, flash style, register tiled.
+// Local layers with T > WINDOW see the truncated cache of the last WINDOW positions: relative
+// keys kr in [0, S) at position kbase + kr, S = WINDOW and kbase = T - WINDOW (SDPA is_causal
+// aligned top-left on the truncated cache); otherwise S = T, kbase = 0 (plain causal). Query
+// qi sees relative keys 0 .. min(qi, S - 1). Block = 64 queries x one head, key tiles of 64;
+// thread (ty, tx) = (tid / 16, tid % 16) owns queries 4ty..4ty+3 and, per tile, the scores of
+// keys 4tx..4tx+3 and the outputs of dims 4tx..4tx+3 (float4 shared-memory operands); online
+// softmax in fp32 with row statistics reduced over the 16 threads of a row group.
+constexpr int PA_Q = 64, PA_K = 64;
 template <typename KVT>
 __global__ void __launch_bounds__(256) k_attn_prefill(int slot, int T, const float* __restrict__ q, KVLayer L,
                                                       int is_local, float* __restrict__ out) {
-    __shared__ float Ks[PA_K][DH + 1];
-    __shared__ float Vs[PA_K][DH + 1];
-    __shared__ float Qs[PA_Q][DH];
+    __shared__ __align__(16) float Qt[DH * PA_Q];    // [d][query], pre-scaled by 1/8
+    __shared__ __align__(16) float KtP[DH * PA_K];   // [d][key] for the scores, then P [query][key]
+    __shared__ __align__(16) float Vs[PA_K * DH];    // [key][d]
     const int h = blockIdx.y, g = h / GQA;
     const int q0 = blockIdx.x * PA_Q;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
     const bool trunc = is_local && T > WINDOW;
     const int S = trunc ? WINDOW : T;
     const int kbase = trunc ? T - WINDOW : 0;
-    for (int i = threadIdx.x; i < PA_Q * DH; i += 256) {
-        const int qi = q0 + i / DH;
-        Qs[i / DH][i % DH] = (qi < T) ? q[((int64_t)qi * H + h) * DH + (i % DH)] * 0.125f : 0.f;
+    // Q tile, transposed: thread -> (query tid & 63, dims 16 * (tid >> 6) .. +15)
+    {
+        const int ql = tid & 63, d0 = (tid >> 6) * 16, qi = q0 + ql;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (qi < T) v = *reinterpret_cast<const float4*>(q + ((int64_t)qi * H + h) * DH + d0 + j);
+            Qt[(d0 + j) * PA_Q + ql] = v.x * 0.125f;
+            Qt[(d0 + j + 1) * PA_Q + ql] = v.y * 0.125f;
+            Qt[(d0 + j + 2) * PA_Q + ql] = v.z * 0.125f;
+            Qt[(d0 + j + 3) * PA_Q + ql] = v.w * 0.125f;
+        }
     }
-    float m[4], l[4], o1[4], o2[4];
+    float m[4], l[4], o[4][4];
     int qlast[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        m[j] = -INFINITY; l[j] = 0.f; o1[j] = 0.f; o2[j] = 0.f;
-        const int qi = q0 + warp * 4 + j;
-        qlast[j] = (qi < T) ? min(qi, S - 1) : -1;     // last relative key index
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[i][j] = 0.f;
+        const int qi = q0 + ty * 4 + i;
+        qlast[i] = (qi < T) ? min(qi, S - 1) : -1;   // last relative key of this query
     }
     const int qmax = min(q0 + PA_Q - 1, T - 1);
-    const int rel_end = min(qmax, S - 1);               // last relative key any query needs
+    const int rel_end = min(qmax, S - 1);             // last relative key any query needs
     for (int kt = 0; kt <= rel_end; kt += PA_K) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < PA_K * DH; i += 256) {
-            const int kr = kt + i / DH, d = i % DH;
-            float kv = 0.f, vv = 0.f;
+        __syncthreads();   // previous tile's P and V consumed
+        {   // K (transposed) and V of relative keys kt .. kt+63: thread -> (key tid & 63, 16 dims)
+            const int kl = tid & 63, d0 = (tid >> 6) * 16, kr = kt + kl;
+            float kv[16], vv[16];
             if (kr <= rel_end) {
-                kv = kv_load(kv_k<KVT>(L, slot, g, kbase + kr) + d);
-                vv = kv_load(kv_v<KVT>(L, slot, g, kbase + kr) + d);
+                const KVT* kp = kv_k<KVT>(L, slot, g, kbase + kr) + d0;
+                const KVT* vp = kv_v<KVT>(L, slot, g, kbase + kr) + d0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    kv[j] = kv_load(kp + j);
+                    vv[j] = kv_load(vp + j);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) kv[j] = vv[j] = 0.f;
             }
-            Ks[i / DH][d] = kv;
-            Vs[i / DH][d] = vv;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) KtP[(d0 + j) * PA_K + kl] = kv[j];
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(Vs + kl * DH + d0 + j) = make_float4(vv[j], vv[j + 1], vv[j + 2], vv[j + 3]);
         }
         __syncthreads();
+        // scores of queries 4ty.. x keys 4tx..
+        float sc[4][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int ql = warp * 4 + j;
-            if (qlast[j] < kt) continue;
-            const float* qr = Qs[ql];
-            float s0 = 0.f, s1 = 0.f;
-#pragma unroll 16
-            for (int d = 0; d < DH; ++d) {
-                s0 += qr[d] * Ks[lane][d];
-                s1 += qr[d] * Ks[lane + 32][d];
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < DH; ++d) {
+            const float4 qa = *reinterpret_cast<const float4*>(Qt + d * PA_Q + ty * 4);
+            const float4 ka = *reinterpret_cast<const float4*>(KtP + d * PA_K + tx * 4);
+            const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kvv[4] = {ka.x, ka.y, ka.z, ka.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sc[i][j] += qv[i] * kvv[j];
+        }
+        // online softmax per query row (16 threads per row group share a row)
+        float p[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float mt = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (kt + tx * 4 + j > qlast[i]) sc[i][j] = -INFINITY;
+                mt = fmaxf(mt, sc[i][j]);
             }
-            if (kt + lane > qlast[j]) s0 = -INFINITY;
-            if (kt + lane + 32 > qlast[j]) s1 = -INFINITY;
-            const float mt = warp_max(fmaxf(s0, s1));
-            const float mn = fmaxf(m[j], mt);
-            const float corr = (m[j] == -INFINITY) ? 0.f : expf(m[j] - mn);
-            const float p0 = (s0 == -INFINITY) ? 0.f : expf(s0 - mn);
-            const float p1 = (s1 == -INFINITY) ? 0.f : expf(s1 - mn);
-            l[j] = l[j] * corr + warp_sum(p0 + p1);
-            o1[j] *= corr;
-            o2[j] *= corr;
-            m[j] = mn;
-            for (int kk = 0; kk < 32; ++kk) {
-                const float pa = __shfl_sync(0xffffffffu, p0, kk);
-                const float pb = __shfl_sync(0xffffffffu, p1, kk);
-                o1[j] += pa * Vs[kk][lane] + pb * Vs[kk + 32][lane];
-                o2[j] += pa * Vs[kk][lane + 32] + pb * Vs[kk + 32][lane + 32];
+#pragma unroll
+            for (int o2 = 1; o2 < 16; o2 <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o2));
+            const float mn = fmaxf(m[i], mt);
+            const float corr = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mn);
+            float ps = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                p[i][j] = (sc[i][j] == -INFINITY) ? 0.f : expf(sc[i][j] - mn);
+                ps += p[i][j];
+            }
+#pragma unroll
+            for (int o2 = 1; o2 < 16; o2 <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o2);
+            l[i] = l[i] * corr + ps;
+            m[i] = mn;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[i][j] *= corr;
+        }
+        __syncthreads();   // K^T consumed: the buffer becomes P [query][key]
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<float4*>(KtP + (ty * 4 + i) * PA_K + tx * 4) = make_float4(p[i][0], p[i][1], p[i][2], p[i][3]);
+        __syncthreads();
+        // O[4 queries][dims 4tx..] += P[queries][keys] V[keys][dims]
+#pragma unroll 4
+        for (int k = 0; k < PA_K; k += 4) {
+            float4 pr[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pr[i] = *reinterpret_cast<const float4*>(KtP + (ty * 4 + i) * PA_K + k);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const float4 v = *reinterpret_cast<const float4*>(Vs + (k + kk) * DH + tx * 4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float pk = kk == 0 ? pr[i].x : kk == 1 ? pr[i].y : kk == 2 ? pr[i].z : pr[i].w;
+                    o[i][0] += pk * v.x;
+                    o[i][1] += pk * v.y;
+                    o[i][2] += pk * v.z;
+                    o[i][3] += pk * v.w;
+                }
             }
         }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int qi = q0 + warp * 4 + j;
+    for (int i = 0; i < 4; ++i) {
+        const int qi = q0 + ty * 4 + i;
         if (qi >= T) continue;
-        const float inv = 1.f / l[j];
-        out[((int64_t)qi * H + h) * DH + lane] = o1[j] * inv;
-        out[((int64_t)qi * H + h) * DH + lane + 32] = o2[j] * inv;
+        const float inv = 1.f / l[i];
+        *reinterpret_cast<float4*>(out + ((int64_t)qi * H + h) * DH + tx * 4) =
+            make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
     }
 }
 
