@@ -97,6 +97,7 @@ struct MegaSmem {
     float wout[MEGA_NCW][4 * MEGA_RMAX];   // per-warp reduced tile sums
     int xoff[MEGA_RMAX];                   // X row offsets (elements into xs) of the current phase
     int xoff_e[E][MEGA_RMAX];              // phase E: per routed expert, act_r row of each row or -1
+    int eslot[MEGA_RMAX][TOPK];            // phase E: position of expert idx[r][k] in the expert list
     int blk_r0[MEGA_RMAX + 1];             // sequence blocks of the rows: start row
     int blk_nch[MEGA_RMAX];                // attention chunks per (block, head group)
     int blk_chunk[MEGA_RMAX];
@@ -1152,6 +1153,14 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                     if (s->idx[r][k] == s->elist[ei]) off = R * DS + (r * TOPK + k) * DE;
                 s->xoff_e[ei][r] = off;
             }
+            for (int t = threadIdx.x - 32; t < R * TOPK; t += MEGA_NCT) {
+                const int r = t / TOPK, k = t % TOPK;
+                const int ex = s->idx[r][k];
+                int ei = 0;
+                for (int q = 0; q < s->n_e; ++q)
+                    if (s->elist[q] == ex) ei = q;
+                s->eslot[r][k] = ei;
+            }
             const int n_e = s->n_e;
             int s0, s1, q0, q1;
             rows_split(DS, cta, C, s0, s1);          // shared pairs [s0, s1)
@@ -1232,22 +1241,18 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 });
             }
             named_bar_sync(1, MEGA_NCT);
+            if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 130 + 8 * l + 6] = globaltimer();
             for (int e = threadIdx.x - 32; e < (o1 - o0) * R; e += MEGA_NCT) {
                 const int oi = e / R, r = e % R;
                 const int o = o0 + oi;
                 float routed = 0.f;
 #pragma unroll
-                for (int k = 0; k < TOPK; ++k) {
-                    const int ex = s->idx[r][k];
-                    int ei = 0;
-                    for (int q = 0; q < n_e; ++q)
-                        if (s->elist[q] == ex) ei = q;
-                    routed = routed + dex[(oi * E + ei) * R + r] * s->wts[r][k];
-                }
+                for (int k = 0; k < TOPK; ++k) routed = routed + dex[(oi * E + s->eslot[r][k]) * R + r] * s->wts[r][k];
                 const float v = s->hown[oi * R + r] + (dsh[oi * R + r] + routed * s->rsc[l][oi]);
                 s->hown[oi * R + r] = v;
                 a.h[(int64_t)r * D + o] = v;
             }
+            if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 130 + 8 * l + 7] = globaltimer();
             if (!g.ok) atomicExch(a.err, 1);
             if (!grid_sync(a, s, epoch)) goto done;
             stamp(a, l, 15);
@@ -1328,8 +1333,20 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 204] = globaltimer();
         if (s->ticket && a.amax) {
             for (int r = cw; r < R; r += MEGA_NCW) {
+                // the first 192 partials with all loads in flight, then any remainder
+                float pv[6];
+                int pi[6];
+#pragma unroll
+                for (int j = 0; j < 6; ++j) {
+                    const int i = lane + 32 * j;
+                    pv[j] = i < C ? __ldcg(a.pmax + r * C + i) : -INFINITY;
+                    pi[j] = i < C ? __ldcg(a.pidx + r * C + i) : 1 << 30;
+                }
                 ArgMax b{-INFINITY, 1 << 30};
-                for (int i = lane; i < C; i += 32) b = argmax_merge(b, ArgMax{__ldcg(a.pmax + r * C + i), __ldcg(a.pidx + r * C + i)});
+#pragma unroll
+                for (int j = 0; j < 6; ++j) b = argmax_merge(b, ArgMax{pv[j], pi[j]});
+                for (int i = lane + 192; i < C; i += 32)
+                    b = argmax_merge(b, ArgMax{__ldcg(a.pmax + r * C + i), __ldcg(a.pidx + r * C + i)});
                 b = warp_argmax(b);
                 if (lane == 0) a.amax[r] = b.i;
             }
