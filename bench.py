@@ -213,12 +213,19 @@ def dist_setup():
 
 
 def max_over_ranks(x: float, world: int, local: int) -> float:
+    """Maximum of x over the ranks (a device tensor under NCCL, a host tensor under gloo)."""
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+    dev = f"cuda:{local}" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def job_rate(tokens_per_rank: int, world: int, ms_max: float) -> float:
+    """Whole-job tokens/s: every rank's tokens over the slowest rank's device time."""
+    return tokens_per_rank * world / (ms_max / 1e3)
 
 
 def barrier(world: int):
@@ -336,8 +343,7 @@ def run_engine(args):
     experts_streamed = eng.get_option("routed_experts") - experts0
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, world, local)
-    tokens = NEW * args.steps * world
-    value = tokens / (ms_max / 1e3)
+    value = job_rate(NEW * args.steps, world, ms_max)
     # ---- end-to-end through the C ABI with host buffers (prompt H2D, prefill, decode, tokens D2H)
     pinned_ids = ids.to(torch.int32).pin_memory()
     host_out = torch.empty(NEW, dtype=torch.int32).pin_memory()
@@ -357,7 +363,7 @@ def run_engine(args):
             e2e_ms.append(e0.elapsed_time(e1))
             pre_ms.append(e0.elapsed_time(em))
     e2e_ms_max = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, local)
-    e2e_value = NEW * world / (e2e_ms_max / 1e3)
+    e2e_value = job_rate(NEW, world, e2e_ms_max)
     # ---- roofline of the dominant kernel, then of the whole decode path
     peak, peak_kind = load_peaks()
     roof = kernel_roofline(eng, cfg, args.gamma, args.recipe, args.kernel_reps, peak, peak_kind)
