@@ -1,5 +1,5 @@
 // Hand-written PTX wrappers for the persistent decode kernel: mbarriers, 1-D TMA bulk
-// copies into this CTA's own shared memory), acquire/release global atomics and named barriers.
+// copies (cp.async.bulk into this CTA's own shared memory), acquire/release global atomics and named barriers.
 // Every wait is bounded by a %globaltimer deadline; a wait that runs out returns false and
 // the caller raises the kernel's error flag instead of hanging.
 #pragma once
