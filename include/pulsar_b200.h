@@ -164,7 +164,8 @@ int pulsar_engine_prefill(pulsar_engine* eng, int32_t slot, const int32_t* ids_d
  * (option "wide_rows"). R <= 5: one persistent kernel; R <= 32: per-op GEMV kernels; more
  * rows (or option "wide" = 1): tiled GEMMs over all rows with the routed experts grouped
  * per expert.
- * rows_dev [R] x int4 {slot, pos, token, 0}. Rows of the same slot must have
+ * rows_dev [R] x int4 {slot, pos, token, 0} (the last field is reserved: bit 0 marks a row
+ * that exited early inside generate_greedy and must be 0 here). Rows of the same slot must have
  * consecutive positions (block-verify: a row sees in-block predecessors' K/V of this
  * pulse). h_prev_dev / h0n_dev [R, 1024] f32 (ignored for pulse 0). Outputs h_out,
  * h0n_out [R, 1024] f32; logits [R, V] f32 (softcapped) unless logits_dev is NULL. */
@@ -205,6 +206,22 @@ int pulsar_engine_generate_sampled(pulsar_engine* eng, int32_t n_seq, const int3
                                    const int32_t* seq_ids_host, const float* first_logits_dev, int32_t n_new,
                                    int32_t gamma, float temperature, float top_p, uint64_t seed,
                                    int32_t* out_tokens_dev, int64_t* stats_host, void* stream);
+
+/* Adaptive early exit (src/infer.py:211-232 set_early_exit_threshold / get_early_exit_stats,
+ * the exit rule of decode_step :536-546). enabled != 0: the sequential greedy loop
+ * (pulsar_engine_generate_greedy with gamma == 0) ends a token's pulses after pulse k < 2
+ * when the softmax of that pulse's (softcapped) logits has max-probability >= threshold;
+ * the token is that pulse's argmax and the cached K/V of the position stay the exiting
+ * pulse's. The decision runs on the device per sequence; a persistent pulse pass whose rows
+ * have all exited returns at once. Speculative rounds (gamma >= 1) run every pulse as
+ * before. Each call resets the exit tallies (as the reference's setter does); call it
+ * between generate calls, not while one runs on another stream. */
+int pulsar_engine_set_early_exit(pulsar_engine* eng, int32_t enabled, float threshold);
+
+/* counts_host[3]: tokens that exited after pulse 1, 2 and 3 (the reference's
+ * early_exit_counts) since the last pulsar_engine_set_early_exit or create. Waits for the
+ * device. */
+int pulsar_engine_early_exit_counts(pulsar_engine* eng, int64_t* counts_host);
 
 /* Engine options. "megakernel" (0/1, default 1 when the GPU can co-schedule one CTA per
  * SM): run each pulse pass of <= 5 rows as one persistent kernel instead of per-op

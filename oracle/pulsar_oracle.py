@@ -473,16 +473,20 @@ def prefill(m: OracleModel, ids: list[int], kv: OracleKV, record=None) -> torch.
 # --------------------------------------------------------------------------------------
 
 def decode_step(m: OracleModel, token: int, pos: int, kv: OracleKV, early_exit_threshold=None,
-                exit_counts=None, record=None) -> torch.Tensor:
+                exit_counts=None, record=None, exit_probs=None) -> torch.Tensor:
     """src/infer.py:526-549: three pulses on one token (optional early exit on the
-    softmax max); commits ``pos + 1`` positions."""
+    softmax max); commits ``pos + 1`` positions. ``exit_probs`` (a list) receives the
+    softmax max-probability of every pulse the exit rule examined."""
     h = h0n = None
     logits = None
     for k in range(m.K):
         lg, h, h0n = pulse_pass(m, k, [token], [pos], kv, h, h0n, record=record)
         logits = lg[0]
         if early_exit_threshold is not None and k < m.K - 1:
-            if torch.softmax(logits, dim=-1).max().item() >= early_exit_threshold:
+            pmax = torch.softmax(logits, dim=-1).max().item()
+            if exit_probs is not None:
+                exit_probs.append(pmax)
+            if pmax >= early_exit_threshold:
                 if exit_counts is not None:
                     exit_counts[k] += 1
                 break
@@ -532,9 +536,12 @@ def warped_probs(logits: torch.Tensor, temperature: float, top_p: float) -> torc
 
 def stream_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: int, temperature: float = 0.0,
                         top_p: float = 1.0, repetition_penalty: float = 1.0, stop_ids=(), capacity=None,
-                        generator: torch.Generator | None = None, trace=None) -> list[int]:
+                        generator: torch.Generator | None = None, trace=None, early_exit_threshold=None,
+                        exit_counts=None, exit_probs=None) -> list[int]:
     """src/infer.py:551-621 returning token ids. Greedy when temperature <= 1e-4 (ties to
-    the lowest index, as torch.argmax); sampling uses torch.multinomial on ``generator``."""
+    the lowest index, as torch.argmax); sampling uses torch.multinomial on ``generator``.
+    ``early_exit_threshold`` / ``exit_counts`` / ``exit_probs``: the engine's adaptive early
+    exit inside decode_step (src/infer.py:199-200, 536-546)."""
     kv = OracleKV(m, capacity or (len(prompt) + max_new_tokens + 8))
     logits = prefill(m, prompt, kv)
     if trace is not None:
@@ -554,7 +561,8 @@ def stream_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: int, 
         all_ids.append(tok)
         out.append(tok)
         pos += 1
-        logits = decode_step(m, tok, pos, kv)
+        logits = decode_step(m, tok, pos, kv, early_exit_threshold=early_exit_threshold, exit_counts=exit_counts,
+                             exit_probs=exit_probs)
         if trace is not None:
             trace.append(("step", logits.clone()))
     return out

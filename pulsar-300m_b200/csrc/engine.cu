@@ -84,6 +84,7 @@ struct LoopOut {
     int n_new;
     unsigned long long seed;   // sampled decoding: Philox key, temperature, top-p
     float temperature, top_p;
+    float ee_thr;              // early exit: softmax max-probability threshold
 };
 
 // Starts a generate call: sequence state, first token, and the row descriptors of round 0
@@ -105,6 +106,62 @@ __global__ void k_seq_init(SeqDev* seqs, const int* lens, const int* first_tok, 
 __global__ void k_rows_step(const SeqDev* seqs, const int* slots, int n, int4* rows) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) rows[i] = make_int4(slots[i], seqs[i].len, seqs[i].pending, 0);
+}
+
+// Early-exit step state (ee: [0] skip flag of the persistent kernel, [1] rows exited so far,
+// [2 + i] the pulse row i exits at). rows[i].w bit 0 set = row i exited early: later pulses
+// keep its cached K/V (the exiting pulse's) and their outputs for it are not used.
+__global__ void k_rows_step_ee(const SeqDev* seqs, const int* slots, int n, int4* rows, int* ee) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i == 0) ee[0] = ee[1] = 0;
+    if (i < n) {
+        rows[i] = make_int4(slots[i], seqs[i].len, seqs[i].pending, 0);
+        ee[2 + i] = NP - 1;
+    }
+}
+
+// src/infer.py:536-543: after pulse `pulse` (< K - 1), row i exits when the softmax of its
+// logits has max-probability >= threshold, i.e. 1 / sum_j exp(l_j - max) >= threshold.
+// Finished sequences count as exited (not tallied). The last row to exit sets the skip flag,
+// so a persistent pulse kernel launched afterwards returns at once.
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_ee_check(const float* __restrict__ lg, int V, int n, int pulse,
+                                                   const LoopOut* lo, const SeqDev* seqs, int4* rows, int* ee) {
+    __shared__ float red[32];
+    const int i = blockIdx.x;
+    if (rows[i].w & 1) return;   // exited at an earlier pulse (uniform over the block)
+    const bool done = seqs[i].done != 0;
+    bool ex = done;
+    if (!done) {
+        const float* x = lg + (int64_t)i * V;
+        float mx = -INFINITY;
+        for (int j = threadIdx.x; j < V; j += SAMPLE_THREADS) mx = fmaxf(mx, x[j]);
+        mx = sblock_max(mx, red);
+        float z = 0.f;
+        for (int j = threadIdx.x; j < V; j += SAMPLE_THREADS) z += expf(x[j] - mx);
+        z = sblock_sum(z, red);
+        ex = 1.f / z >= lo->ee_thr;
+    }
+    if (ex && threadIdx.x == 0) {
+        rows[i].w |= 1;
+        if (!done) ee[2 + i] = pulse;
+        if (atomicAdd(&ee[1], 1) + 1 == n) ee[0] = 1;
+    }
+}
+
+// Commit of an early-exit step: the token is the argmax of the exiting pulse (amax_p[k] rows).
+__global__ void k_commit_ee(SeqDev* seqs, const int* amax0, const int* amax1, const int* amax2, const int* ee, int n,
+                            const LoopOut* lo, unsigned long long* counts) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n || seqs[i].done) return;
+    const int k = ee[2 + i];
+    const int t = k == 0 ? amax0[i] : k == 1 ? amax1[i] : amax2[i];
+    atomicAdd(&counts[k], 1ull);
+    const int n_new = lo->n_new;
+    lo->out[(int64_t)i * n_new + seqs[i].n_out] = t;
+    seqs[i].n_out += 1;
+    seqs[i].pending = t;
+    seqs[i].len += 1;
+    if (seqs[i].n_out >= n_new) seqs[i].done = 1;
 }
 
 __global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, const LoopOut* lo) {
@@ -334,6 +391,12 @@ struct pulsar_engine {
     float *hblk = nullptr, *h0blk = nullptr, *htmp = nullptr, *htmp2 = nullptr, *h0tmp = nullptr, *logits_tmp = nullptr;
     long long* stats = nullptr;
     LoopOut* loop_out = nullptr;   // output buffer / length / sampling parameters of the running generate call
+    // adaptive early exit of the sequential greedy loop: threshold (off: ee_on false), step
+    // state [2 + max_batch], per-pulse argmax of pulses 0 and 1 [2][max_batch], exit tallies [NP]
+    bool ee_on = false;
+    float ee_thr = 1.f;
+    int *ee = nullptr, *ee_amax = nullptr;
+    unsigned long long* ee_counts = nullptr;
     // sampled decoding: draft logits rows [wide_rows][V] (row j*n + i), verify logits rows
     // [wide_rows][V] (row i*(gamma+1) + k), their warp statistics, sequence stream ids
     float *qbuf = nullptr, *pbuf = nullptr;
@@ -501,7 +564,7 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
 }
 
 int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
-               float* h_out, float* h0n_out, float* logits, int* amax, cudaStream_t st, int hs) {
+               float* h_out, float* h0n_out, float* logits, int* amax, cudaStream_t st, int hs, const int* skip) {
     MegaArgs a{};
     a.R = R;
     a.pulse = p;
@@ -573,6 +636,7 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.err = e->m_err;
     a.experts = e->m_experts;
     a.trace = e->m_trace;
+    a.skip = skip;
     return launch_mega(a, e->kv32(), e->mega_grid, st);
 }
 
@@ -580,8 +644,11 @@ template <typename KVT>
 int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
                        float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs);
 
+// skip (optional): a device flag; when it is non-zero at launch the persistent kernel returns
+// at once (every row exited early). The per-op and many-row passes run regardless.
 int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
-                   float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs) {
+                   float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs,
+                   const int* skip) {
     if (R > MAX_ROWS || e->force_wide) {
         // rms norm, QKV GEMM, qkv post, attention, combine, Wo GEMM, norm, router, shared GEMMs (2),
         // bucket, slots, expert GEMMs (2), combine per layer; input, end, LM GEMM, argmax
@@ -595,7 +662,7 @@ int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float
     if (e->use_mega && !e->has_lora && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
         e->n_kernels += 1;
         e->n_mega += 1;
-        return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st, hs);
+        return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st, hs, skip);
     }
     // per-op pass: input, 10 kernels per layer, end, LM head per 8 rows, argmax
     const bool want = logits != nullptr || amax != nullptr;
@@ -608,11 +675,12 @@ int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float
 
 // hs: row stride (in rows of D floats) of h_out and h0n_out
 int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in, float* h_out,
-          float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs = 1) {
+          float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs = 1,
+          const int* skip = nullptr) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     const bool timed = e->time_pulses && cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone;
     if (timed) PULSAR_TRY(cuda_status(cudaEventRecord(e->tev[0], st), "cudaEventRecord"));
-    PULSAR_TRY(pulse_dispatch(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st, hs));
+    PULSAR_TRY(pulse_dispatch(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax, st, hs, skip));
     if (timed) PULSAR_TRY(cuda_status(cudaEventRecord(e->tev[1], st), "cudaEventRecord"));
     return PULSAR_OK;
 }
@@ -926,6 +994,27 @@ int body_step(pulsar_engine* e, cudaStream_t st, void* vctx) {
     return launch_status("k_commit_greedy");
 }
 
+// Sequential step with adaptive early exit (src/infer.py:526-549): pulses 0 and 1 also write
+// logits (qbuf rows [k * n, k * n + n)) and argmax; k_ee_check marks the rows that exit; the
+// commit takes the exiting pulse's argmax and tallies the exit depth.
+int body_step_ee(pulsar_engine* e, cudaStream_t st, void* vctx) {
+    LoopCtx* c = static_cast<LoopCtx*>(vctx);
+    const int n = c->n, V = e->V, NB = e->cfg.max_batch;
+    float* lg0 = e->qbuf;
+    float* lg1 = e->qbuf + (int64_t)n * V;
+    k_rows_step_ee<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, e->rows, e->ee);
+    PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, lg0, V, e->ee_amax, st));
+    k_ee_check<<<n, SAMPLE_THREADS, 0, st>>>(lg0, V, n, 0, e->loop_out, e->seqs, e->rows, e->ee);
+    PULSAR_LAUNCH_CHECK("k_ee_check");
+    PULSAR_TRY(pulse(e, 1, n, e->rows, e->htmp, e->h0tmp, e->htmp2, nullptr, lg1, V, e->ee_amax + NB, st, 1, e->ee));
+    k_ee_check<<<n, SAMPLE_THREADS, 0, st>>>(lg1, V, n, 1, e->loop_out, e->seqs, e->rows, e->ee);
+    PULSAR_LAUNCH_CHECK("k_ee_check");
+    PULSAR_TRY(pulse(e, 2, n, e->rows, e->htmp2, e->h0tmp, e->htmp, nullptr, nullptr, 0, e->amax, st, 1, e->ee));
+    k_commit_ee<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->ee_amax, e->ee_amax + NB, e->amax, e->ee, n, e->loop_out,
+                                                 e->ee_counts);
+    return launch_status("k_commit_ee");
+}
+
 // One speculative round: gamma + 1 pulse-0 passes (the drafts, then the last draft's own
 // pass), whose outputs land directly in the verify block buffers (row stride gamma + 1), then
 // the batched pulse-1 and pulse-2 verify passes and the acceptance. Round 0's first row is set
@@ -1092,7 +1181,11 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&e->rows, RW)) || (st = e->wmalloc(&e->rows_v, RW)) ||
         (st = e->wmalloc(&e->hblk, (size_t)RW * D)) || (st = e->wmalloc(&e->h0blk, (size_t)RW * D)) ||
         (st = e->wmalloc(&e->htmp, (size_t)RW * D)) || (st = e->wmalloc(&e->htmp2, (size_t)RW * D)) ||
-        (st = e->wmalloc(&e->h0tmp, (size_t)RW * D)) || (st = e->wmalloc(&e->stats, (size_t)NB * 3)))
+        (st = e->wmalloc(&e->h0tmp, (size_t)RW * D)) || (st = e->wmalloc(&e->stats, (size_t)NB * 3)) ||
+        (st = e->wmalloc(&e->ee, (size_t)NB + 2)) || (st = e->wmalloc(&e->ee_amax, (size_t)2 * NB)) ||
+        (st = e->wmalloc(&e->ee_counts, NP)))
+        return fail(st);
+    if ((st = cuda_status(cudaMemset(e->ee_counts, 0, NP * sizeof(unsigned long long)), "zero exit tallies")))
         return fail(st);
     // persistent pulse kernel: one CTA per SM, co-resident (cooperative launch)
     {
@@ -1370,7 +1463,7 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
             return PULSAR_ERR_CAPACITY;
         }
     }
-    const LoopOut lp{out, n_new, (unsigned long long)seed, temperature, top_p};
+    const LoopOut lp{out, n_new, (unsigned long long)seed, temperature, top_p, e->ee_thr};
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->slots_dev, slots_host, n * 4, cudaMemcpyHostToDevice, st), "copy slots"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->lens_dev, lens.data(), n * 4, cudaMemcpyHostToDevice, st), "copy lens"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->loop_out, &lp, sizeof(lp), cudaMemcpyHostToDevice, st), "copy params"));
@@ -1389,12 +1482,15 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
     e->n_kernels += 2;
     LoopCtx ctx{n, gamma};
     // output, length and sampling parameters live on the device: graphs depend on (n, gamma, mode)
-    const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + (sampled ? ":s" : ":g");
+    // (gamma = 0 with early exit on: its own body, key suffix ":e")
+    const bool ee = gamma == 0 && e->ee_on;
+    const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + (sampled ? ":s" : ee ? ":e" : ":g");
     std::vector<SeqDev> hs(n);
     int remaining_steps = n_new - 1;
     while (true) {
         if (gamma == 0) {
-            for (int s = 0; s < remaining_steps; ++s) PULSAR_TRY(run_graph(e, key, st, body_step, &ctx));
+            for (int s = 0; s < remaining_steps; ++s)
+                PULSAR_TRY(run_graph(e, key, st, ee ? body_step_ee : body_step, &ctx));
         } else {
             // each round emits between 1 and gamma+1 tokens; launch the minimum, then check
             const int rounds = std::max(1, (remaining_steps + gamma) / (gamma + 1));
@@ -1435,6 +1531,25 @@ extern "C" int pulsar_engine_generate_sampled(pulsar_engine* e, int32_t n, const
                                               int32_t* out, int64_t* stats_host, void* stream) {
     return generate_impl(e, n, slots_host, seq_ids_host, first_logits, n_new, gamma, true, temperature, top_p, seed,
                          out, stats_host, stream);
+}
+
+extern "C" int pulsar_engine_set_early_exit(pulsar_engine* e, int32_t enabled, float threshold) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(!enabled || std::isfinite(threshold), "set_early_exit: threshold must be finite");
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    e->ee_on = enabled != 0;
+    e->ee_thr = enabled ? threshold : 1.f;
+    return cuda_status(cudaMemset(e->ee_counts, 0, NP * sizeof(unsigned long long)), "zero exit tallies");
+}
+
+extern "C" int pulsar_engine_early_exit_counts(pulsar_engine* e, int64_t* counts_host) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(counts_host, "early_exit_counts: null argument");
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    unsigned long long c[NP];
+    PULSAR_TRY(cuda_status(cudaMemcpy(c, e->ee_counts, sizeof(c), cudaMemcpyDeviceToHost), "read exit tallies"));
+    for (int k = 0; k < NP; ++k) counts_host[k] = (int64_t)c[k];
+    return PULSAR_OK;
 }
 
 extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int64_t value) {

@@ -274,10 +274,12 @@ __global__ void __launch_bounds__((H + HKV) * 32) k_qkv_post(
         const float a2 = kn_w[g * DH + lane + 32] * (k2 * inv);
         KVT* kp = kv_k<KVT>(L, row.x, g, pos);
         KVT* vp = kv_v<KVT>(L, row.x, g, pos);
-        kv_store(kp + lane, a1 * c - a2 * s);
-        kv_store(kp + lane + 32, a2 * c + a1 * s);
-        kv_store(vp + lane, v1);
-        kv_store(vp + lane + 32, v2);
+        if (!(rows[r].w & 1)) {   // bit 0: the row keeps its cached K/V (exited early)
+            kv_store(kp + lane, a1 * c - a2 * s);
+            kv_store(kp + lane + 32, a2 * c + a1 * s);
+            kv_store(vp + lane, v1);
+            kv_store(vp + lane + 32, v2);
+        }
     }
 }
 

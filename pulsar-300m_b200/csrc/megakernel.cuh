@@ -74,6 +74,7 @@ struct MegaArgs {
     unsigned* tickets;    // [MEGA_RMAX * HKV + 2]: [.. + 0] argmax ticket, [.. + 1] exit count (both self-resetting)
     int* err;             // error flag (non-zero: a bounded wait ran out)
     unsigned long long* experts;   // running count of distinct routed experts streamed (per layer)
+    const int* skip;      // optional: non-zero -> the whole pass is skipped (every row exited early)
     unsigned long long* trace;   // optional [gridDim][MEGA_TRACE] %globaltimer stamps (null: off)
 };
 
@@ -577,10 +578,12 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
             const float y1 = b1 * cs - b2 * sn, y2 = b2 * cs + b1 * sn;
             KVT* kp = kv_k<KVT>(L, slot, g, key);
             KVT* vp = kv_v<KVT>(L, slot, g, key);
-            kv_store(kp + lane, y1);
-            kv_store(kp + lane + 32, y2);
-            kv_store(vp + lane, v1);
-            kv_store(vp + lane + 32, v2);
+            if (!(a.rows[rr].w & 1)) {   // bit 0: the row keeps its cached K/V (exited early)
+                kv_store(kp + lane, y1);
+                kv_store(kp + lane + 32, y2);
+                kv_store(vp + lane, v1);
+                kv_store(vp + lane + 32, v2);
+            }
             // the stored (rounded) values, so every reader sees identical keys
             Ks[kk * (DH + 1) + lane] = kv_round<KVT>(y1);
             Ks[kk * (DH + 1) + lane + 32] = kv_round<KVT>(y2);
@@ -704,6 +707,19 @@ static __device__ __noinline__ void attn_merge(const MegaArgs& a, MegaSmem* s, i
     named_bar_sync(1, MEGA_NCT);
 }
 
+// Consumer exit of every CTA: the last CTA out (every CTA is past its last grid barrier)
+// re-arms the barrier counter for the next launch on this stream.
+__device__ __forceinline__ void mega_leave(const MegaArgs& a) {
+    if (threadIdx.x == 32) {
+        if (a.trace) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
+        const unsigned t = atomicAdd(&a.tickets[MEGA_RMAX * HKV + 1], 1u);
+        if (t == gridDim.x - 1) {
+            a.tickets[MEGA_RMAX * HKV + 1] = 0;
+            atomicExch(a.bar, 0u);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ the pulse
 template <int R, typename KVT>
 __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_constant__ MegaArgs a) {
@@ -712,6 +728,10 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
     const int C = gridDim.x, cta = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool want_lm = a.logits != nullptr || a.amax != nullptr;
+    if (a.skip && __ldcg(a.skip) != 0) {   // every row exited early (flag written by an earlier kernel)
+        mega_leave(a);
+        return;
+    }
     if (threadIdx.x == 0) {
         for (int i = 0; i < MEGA_NS; ++i) {
             mbar_init(&s->full[i], 1);
@@ -1354,17 +1374,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         if (!g.ok) atomicExch(a.err, 1);
     }
 done:
-    if (threadIdx.x == 32) {
-        if (a.trace) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
-        // the last CTA out (every CTA is past its last grid barrier) re-arms the barrier counter
-        // for the next launch on this stream
-        const unsigned t = atomicAdd(&a.tickets[MEGA_RMAX * HKV + 1], 1u);
-        if (t == gridDim.x - 1) {
-            a.tickets[MEGA_RMAX * HKV + 1] = 0;
-            atomicExch(a.bar, 0u);
-        }
-    }
-    return;
+    mega_leave(a);
 }
 
 }  // namespace pulsar

@@ -186,6 +186,19 @@ class DeviceEngine:
             "generate_greedy")
         return out, {"rounds": stats[0], "drafted": stats[1], "accepted": stats[2]}
 
+    def set_early_exit(self, threshold: Optional[float]) -> None:
+        """pulsar_engine_set_early_exit: device early exit of the gamma = 0 greedy loop (None:
+        off); resets the exit tallies."""
+        on = threshold is not None
+        _lib.check(_lib.load().pulsar_engine_set_early_exit(self._h, int(on), float(threshold) if on else 1.0),
+                   "set_early_exit")
+
+    def early_exit_counts(self) -> list[int]:
+        """Tokens that exited after pulse 1, 2, 3 since the last set_early_exit."""
+        c = (C.c_int64 * 3)()
+        _lib.check(_lib.load().pulsar_engine_early_exit_counts(self._h, c), "early_exit_counts")
+        return [int(x) for x in c]
+
     def generate_sampled(self, slots, first_logits: torch.Tensor, n_new: int, gamma: int, temperature: float,
                          top_p: float, seed: int, seq_ids=None):
         """Sampled self-speculative decoding (pulsar_engine_generate_sampled): Philox streams
@@ -347,6 +360,7 @@ class PulsarInferenceEngine:
     def set_early_exit_threshold(self, threshold: Optional[float]):
         self.early_exit_threshold = threshold
         self.early_exit_counts = [0] * self.cfg.default_pulses
+        self.dev.set_early_exit(threshold)
 
     def get_early_exit_stats(self) -> dict:
         total = sum(self.early_exit_counts)
@@ -534,7 +548,9 @@ class PulsarInferenceEngine:
         """Decode ``input_ids`` [B, T] and return [B, T + max_new_tokens] (int64).
 
         gamma = 0: exact sequential greedy decoding (the reference's stream_generate with
-        temperature 0 and no repetition penalty). gamma >= 1: gamma drafts from the
+        temperature 0 and no repetition penalty), with the adaptive early exit of
+        ``set_early_exit_threshold`` decided on the device per sequence (exit depths added to
+        ``early_exit_counts``). gamma >= 1: gamma drafts from the
         pulse-1 exit and one batched pulse-2/3 verify of the gamma+1 block per round,
         greedy acceptance (temperature <= 1e-4) or sampled acceptance (ratio test with
         residual resampling, Philox streams keyed by (sequence index, round, slot) and
@@ -557,7 +573,13 @@ class PulsarInferenceEngine:
             if sampled:
                 toks, stats = self.dev.generate_sampled(slots, first, max_new_tokens, gamma, temperature, top_p, seed)
             else:
+                ee = gamma == 0 and self.early_exit_threshold is not None
+                if ee:
+                    self.dev.set_early_exit(self.early_exit_threshold)   # zero the device tallies
                 toks, stats = self.dev.generate_greedy(slots, first, max_new_tokens, gamma)
+                if ee:
+                    for k, c in enumerate(self.dev.early_exit_counts()):
+                        self.early_exit_counts[k] += c
         finally:
             for c in caches:
                 c.release()

@@ -37,6 +37,19 @@ def load_golden(name: str):
     return torch.load(path, weights_only=False)
 
 
+def early_exit_model(g):
+    """(state_dict, config) of an early_exit_* golden case: the synthetic weights with the
+    case's sharpening (tests/golden/make_golden.py:sharpen)."""
+    from pulsar_b200.config import PulsarConfig
+    from pulsar_b200.weights import make_state_dict
+    if GOLDEN not in sys.path:
+        sys.path.insert(0, GOLDEN)
+    from make_golden import sharpen
+    cfg = PulsarConfig(**g["cfg"])
+    sd = make_state_dict(cfg, recipe=g["recipe"], seed=g["seed"], b_std=g["b_std"])
+    return sharpen(sd, g["final_scale"], g["res0_scale"], g.get("zero_lora", False)), cfg
+
+
 def assert_close(actual, expected, *, atol=2e-2, rtol=2e-2, msg=""):
     """Fails only when BOTH max-abs > atol and max-rel > rtol (the reference's rule,
     tests/conftest.py:118-144 of the reference)."""

@@ -13,6 +13,14 @@ summaries to ``tests/golden/*.pt``. The reference is never needed at test time.
 Cases:
   tiny_*  - the reference test-suite's tiny config (tests/conftest.py:30-51): full logits.
   full_*  - the production Pulsar-283M config, recipes A and B: top-k + sampled logits.
+  early_exit_* - greedy token streams and exit tallies of the reference's adaptive early
+            exit (set_early_exit_threshold, src/infer.py:211-214, 536-546) at a few
+            thresholds. Random-init logits are nearly flat (max-probability ~1/V), so these
+            cases sharpen the model: final_norm.weight x final_scale and pulse 0's
+            pulse_res_scale x res0_scale (recorded in the file), which spreads the pulses'
+            max-probabilities over a range where the thresholds split exits across depths.
+            early_exit_nolora also zeroes every loop-adapter lora_B (the reference's own
+            initialisation of lora_B, src/model.py:710-714).
 """
 
 from __future__ import annotations
@@ -128,6 +136,50 @@ def run_case(name, cfg_dict, recipe, seed, prompt_len, n_new, n_pulse_steps, out
     print(f"wrote {path}: greedy={rec['greedy_ids'][:12]}... spec={rec['spec_ids'][:12]}...", flush=True)
 
 
+def sharpen(sd, final_scale, res0_scale, zero_lora=False):
+    """The early-exit cases' weight change (applied identically by the tests)."""
+    sd = dict(sd)
+    if zero_lora:
+        for k in list(sd):
+            if k.endswith("lora_B"):
+                sd[k] = torch.zeros_like(sd[k])
+    sd["final_norm.weight"] = sd["final_norm.weight"] * final_scale
+    rs = sd["pulse_res_scale"].clone()
+    rs[0] = rs[0] * res0_scale
+    sd["pulse_res_scale"] = rs
+    return sd
+
+
+def run_early_exit(name, cfg_dict, recipe, seed, prompt_seed, prompt_len, n_new, thresholds, final_scale, res0_scale,
+                   zero_lora, out_dir, b_std=0.09):
+    from src.infer import PulsarInferenceEngine
+    from src.model import PulsarConfig, PulsarForCausalLM
+    from pulsar_b200.config import PulsarConfig as MyCfg
+
+    cfg = PulsarConfig(**cfg_dict)
+    sd = sharpen(make_state_dict(MyCfg(**cfg_dict), recipe=recipe, seed=seed, b_std=b_std), final_scale, res0_scale,
+                 zero_lora)
+    torch.manual_seed(1234)
+    model = PulsarForCausalLM(cfg)
+    _, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected, unexpected
+    eng = PulsarInferenceEngine(model, device="cpu", dtype=torch.float32)
+    ids = random_prompts(1, prompt_len, cfg.vocab_size, seed=prompt_seed)[0].tolist()
+    rec = {"name": name, "cfg": cfg_dict, "recipe": recipe, "seed": seed, "b_std": b_std, "prompt": ids,
+           "n_new": n_new, "final_scale": final_scale, "res0_scale": res0_scale, "zero_lora": zero_lora, "runs": []}
+    for thr in thresholds:
+        eng.set_early_exit_threshold(thr)
+        tk = MockTokenizer(ids)
+        txt = eng.generate(tk, "", max_new_tokens=n_new, temperature=0.0, top_p=1.0, repetition_penalty=1.0,
+                           stream=False, speculative=False)
+        toks = [int(s) for s in txt.split(",") if s != ""]
+        rec["runs"].append({"threshold": thr, "ids": toks, "counts": list(eng.early_exit_counts)})
+        print(f"{name} threshold {thr}: counts {eng.early_exit_counts} ids {toks[:10]}...", flush=True)
+    path = os.path.join(out_dir, f"{name}.pt")
+    torch.save(rec, path)
+    print(f"wrote {path}", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("PULSAR_REFERENCE", "/root/reference"))
@@ -149,6 +201,18 @@ def main():
         if args.only and c[0] != args.only:
             continue
         run_case(c[0], c[1], c[2], c[3], c[4], c[5], c[6], args.out, c[7], *c[8:])
+    ee_cases = [
+        # name, cfg, recipe, seed, prompt seed, prompt len, n_new, thresholds, final x, res0 x, zero lora_B, b_std
+        ("early_exit_tiny", tiny_cfg_dict(), "B", 0, 0, 12, 24, [0.03, 0.04, 0.06], 16.0, 3.0, False, 0.35),
+        ("early_exit_full", full, "B", 0, 1, 32, 32, [0.0075, 0.02], 8.0, 3.0, False, 0.09),
+        # prompt seed 8: the router's 4th/5th score gap stays >= 1.3e-5 along both streams
+        # (a near-tie there flips an expert between any two fp32 implementations)
+        ("early_exit_nolora", full, "B", 0, 8, 32, 32, [0.2, 0.3], 16.0, 3.0, True, 0.09),
+    ]
+    for c in ee_cases:
+        if args.only and c[0] != args.only:
+            continue
+        run_early_exit(*c[:11], args.out, *c[11:])
 
 
 if __name__ == "__main__":

@@ -6,7 +6,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from conftest import load_golden
+from conftest import early_exit_model, load_golden
 from oracle import pulsar_oracle as O
 from pulsar_b200.config import PulsarConfig
 from pulsar_b200.weights import make_state_dict
@@ -88,6 +88,25 @@ def test_oracle_generate_full(name):
     n = min(g["n_new"], 24)
     assert O.stream_generate_ids(m, g["prompt"], n) == g["greedy_ids"][:n]
     assert O.self_speculative_ids(m, g["prompt"], n) == g["spec_ids"][:n]
+
+
+@pytest.mark.parametrize("name", ["early_exit_tiny", pytest.param("early_exit_full", marks=pytest.mark.slow),
+                                  pytest.param("early_exit_nolora", marks=pytest.mark.slow)])
+def test_oracle_early_exit(name):
+    """src/infer.py:526-549 with set_early_exit_threshold: the oracle's greedy stream and
+    exit tallies equal the reference's at every recorded threshold."""
+    g = load_golden(name)
+    sd, cfg = early_exit_model(g)
+    m = O.OracleModel(sd, cfg)
+    depths = set()
+    for run in g["runs"]:
+        cnt = [0] * m.K
+        out = O.stream_generate_ids(m, g["prompt"], g["n_new"], early_exit_threshold=run["threshold"],
+                                    exit_counts=cnt)
+        assert out == run["ids"], f"threshold {run['threshold']}: tokens differ"
+        assert cnt == run["counts"], f"threshold {run['threshold']}: exit tallies {cnt} vs {run['counts']}"
+        depths |= {k for k, c in enumerate(cnt) if c}
+    assert len(depths) >= 2, "the cases should exit at more than one depth"
 
 
 def test_block_spec_gamma1_greedy_matches_reference_stream_on_tiny():
