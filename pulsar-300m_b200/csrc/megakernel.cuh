@@ -83,7 +83,8 @@ constexpr int MEGA_TRACE = 256;   // stamps per CTA: [0] start, [1 + 16*l + j] p
 struct MegaSmem {
     uint64_t full[MEGA_NS];
     uint64_t empty[MEGA_NS];
-    float logits[MEGA_RMAX][E];
+    float logits[MEGA_RMAX][E];   // router: score + bias per (row, expert)
+    float rsg[MEGA_RMAX][E];      // router: sigmoid score per (row, expert)
     float wts[MEGA_RMAX][TOPK];
     int idx[MEGA_RMAX][TOPK];
     int elist[E];
@@ -103,14 +104,23 @@ struct MegaSmem {
     int blk_nch[MEGA_RMAX];                // attention chunks per (block, head group)
     int blk_chunk[MEGA_RMAX];
     int n_blk;
+    int4 rows[MEGA_RMAX];                  // the row descriptors (read everywhere; L1 holds little here)
     float rwn[NL][E][MEGA_MAXOROWS];       // router weight x mlp-norm weight of the owned h rows
     float hown[MEGA_MAXOROWS * MEGA_RMAX]; // owned h rows [row - o0][R] (this CTA is their only writer)
     float rinv[MEGA_RMAX];                 // 1 / rms of h per row (phase D)
+    float nred[D / 128];                   // norm_rows (one row): sums of squares of the 128-element slices
     float rsc[NL][MEGA_MAXOROWS];          // routed_scale of the owned h rows
+    float ebias[NL][E];                    // expert bias of every layer (router top-k)
+    float rope[2][MEGA_RMAX][DH];          // [local, global][row]: cos (32) then sin (32) at the row's position
 };
 
 __device__ __forceinline__ void stamp(const MegaArgs& a, int l, int j) {
     if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 1 + 16 * l + j] = globaltimer();
+}
+
+// router-phase sub-steps of layer l (entries 206 + 5*l + k, k < 5)
+__device__ __forceinline__ void rstamp(const MegaArgs& a, int l, int k) {
+    if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 206 + 5 * l + k] = globaltimer();
 }
 
 // attention-item sub-steps of the first item a CTA runs in layer l (entries 130 + 8*l + k)
@@ -286,11 +296,17 @@ __device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsign
         red_release_gpu_add(a.bar, 1u);
         const unsigned target = epoch * gridDim.x;
         bool ok = true;
+        // one acquire poll at a time; the global error flag costs an L2 round trip of its own,
+        // so it is read every 64th poll only (more polls in flight measured slower: they
+        // contend with the arrivals at the counter's L2 slice)
         if (ld_acquire_gpu(a.bar) < target) {
             const unsigned long long t0 = globaltimer();
-            while (ld_acquire_gpu(a.bar) < target) {
+            for (unsigned it = 1; ld_acquire_gpu(a.bar) < target; ++it) {
                 __nanosleep(20);
-                if (globaltimer() - t0 > WAIT_NS || *(volatile int*)a.err) { ok = false; break; }
+                if (globaltimer() - t0 > WAIT_NS || ((it & 63) == 0 && *(volatile int*)a.err)) {
+                    ok = false;
+                    break;
+                }
             }
         }
         if (!ok) {
@@ -302,27 +318,52 @@ __device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsign
     return s->abort == 0;
 }
 
-// RMSNorm of R rows (global, [R][1024]) into xs with weight w: one consumer warp per row;
-// 1/rms of row r goes to rinv[r] when rinv is given.
+// RMSNorm of R rows (global, [R][1024]) into dst with weight w; 1/rms of row r goes to rinv[r]
+// when rinv is given. One row: every consumer thread loads float4 pieces (all loads in flight
+// at once), warps reduce their 128-element slices, the eight slice sums are added in order
+// from shared memory (red: 8 floats). More rows (register pressure): one warp per row.
 template <int R>
-__device__ __forceinline__ void norm_rows(const float* src, const float* w, float eps, float* dst,
+__device__ __forceinline__ void norm_rows(const float* src, const float* w, float eps, float* dst, float* red,
                                           float* rinv = nullptr) {
-    const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
-    for (int r = cw; r < R; r += MEGA_NCW) {
-        float v[32], wv[32];
-        float ss = 0.f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            v[i] = __ldcg(src + (int64_t)r * D + i * 32 + lane);   // written by other CTAs: bypass L1
-            wv[i] = __ldg(w + i * 32 + lane);                      // in flight with the rows
+    const int lane = threadIdx.x & 31;
+    if constexpr (R == 1) {
+        const int tid = threadIdx.x - 32;
+        constexpr int N4 = D / 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f), wv = v;
+        if (tid < N4) {
+            v = __ldcg(reinterpret_cast<const float4*>(src) + tid);   // written by other CTAs: bypass L1
+            wv = __ldg(reinterpret_cast<const float4*>(w) + tid);
+            const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);   // warp-uniform branch
+            if (lane == 0) red[tid / 32] = ss;
         }
+        named_bar_sync(1, MEGA_NCT);
+        if (tid < N4) {
+            float t = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
-        ss = warp_sum(ss);
-        const float inv = rsqrtf(ss / (float)D + eps);
-        if (rinv && lane == 0) rinv[r] = inv;
+            for (int j = 0; j < D / 128; ++j) t += red[j];
+            const float inv = rsqrtf(t / (float)D + eps);
+            if (rinv && tid == 0) rinv[0] = inv;
+            reinterpret_cast<float4*>(dst)[tid] =
+                make_float4(wv.x * (v.x * inv), wv.y * (v.y * inv), wv.z * (v.z * inv), wv.w * (v.w * inv));
+        }
+    } else {
+        const int cw = (threadIdx.x >> 5) - 1;
+        for (int r = cw; r < R; r += MEGA_NCW) {
+            float v[32], wv[32];
+            float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
+            for (int i = 0; i < 32; ++i) {
+                v[i] = __ldcg(src + (int64_t)r * D + i * 32 + lane);   // written by other CTAs: bypass L1
+                wv[i] = __ldg(w + i * 32 + lane);                      // in flight with the rows
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+            ss = warp_sum(ss);
+            const float inv = rsqrtf(ss / (float)D + eps);
+            if (rinv && lane == 0) rinv[r] = inv;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) dst[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
+        }
     }
 }
 
@@ -379,8 +420,8 @@ struct AttnGeo {
     int r0, nr, g, c, nch, chunk, slot, pos0, k0, nk, nold;
 };
 
-__device__ __forceinline__ void attn_block_chunks(const MegaArgs& a, int r0, int r1, bool local, int& chunk, int& nch) {
-    const int pos0 = a.rows[r0].y, posL = a.rows[r1 - 1].y;
+__device__ __forceinline__ void attn_block_chunks(const int4* rows, int r0, int r1, bool local, int& chunk, int& nch) {
+    const int pos0 = rows[r0].y, posL = rows[r1 - 1].y;
     const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
     chunk = attn_chunk(posL - lo + 1);
     nch = (posL - lo + chunk) / chunk;
@@ -388,11 +429,11 @@ __device__ __forceinline__ void attn_block_chunks(const MegaArgs& a, int r0, int
 
 // Geometry of item `item` given the block starts blk_r0[0..n_blk] (blk_r0[n_blk] = R);
 // false past the last item.
-__device__ __forceinline__ bool attn_geo(const MegaArgs& a, const int* blk_r0, int n_blk, bool local, int item,
+__device__ __forceinline__ bool attn_geo(const int4* rows, const int* blk_r0, int n_blk, bool local, int item,
                                          AttnGeo& o) {
     for (int b = 0; b < n_blk; ++b) {
         int chunk, nch;
-        attn_block_chunks(a, blk_r0[b], blk_r0[b + 1], local, chunk, nch);
+        attn_block_chunks(rows, blk_r0[b], blk_r0[b + 1], local, chunk, nch);
         if (item < HKV * nch) {
             o.r0 = blk_r0[b];
             o.nr = blk_r0[b + 1] - blk_r0[b];
@@ -400,9 +441,9 @@ __device__ __forceinline__ bool attn_geo(const MegaArgs& a, const int* blk_r0, i
             o.c = item % nch;
             o.nch = nch;
             o.chunk = chunk;
-            o.slot = a.rows[o.r0].x;
-            o.pos0 = a.rows[o.r0].y;
-            const int posL = a.rows[o.r0 + o.nr - 1].y;
+            o.slot = rows[o.r0].x;
+            o.pos0 = rows[o.r0].y;
+            const int posL = rows[o.r0 + o.nr - 1].y;
             const int lo = local ? max(0, o.pos0 - WINDOW + 1) : 0;
             o.k0 = lo + o.c * chunk;
             const int k1 = min(o.k0 + chunk, posL + 1);
@@ -492,104 +533,112 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
     const bool local = is_local_layer(l);
     const KVLayer& L = a.kvl[l];
-    const int slot = a.rows[r0].x;
-    const int pos0 = a.rows[r0].y, posL = a.rows[r0 + nr - 1].y;
+    const int4* rows = s->rows;
+    const int slot = rows[r0].x;
+    const int pos0 = rows[r0].y, posL = rows[r0 + nr - 1].y;
     const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
     const int k0 = lo + c * chunk;
     const int k1 = min(k0 + chunk, posL + 1);
     const int nk = k1 - k0;
+    const int nold = max(0, min(k1, pos0) - k0);          // keys < pos0 come from the cache
     float* qs = s->xs;                                   // [nr*4][64]
     float* Ks = qs + MEGA_RMAX * GQA * DH;               // [64][65]
     float* Vs = Ks + MEGA_CHUNK * (DH + 1);              // [64][65]
     float* Ps = Vs + MEGA_CHUNK * (DH + 1);              // [nr*4][64]
-    const float* cos_t = local ? a.cos_l : a.cos_g;
-    const float* sin_t = local ? a.sin_l : a.sin_g;
     const int nq = nr * GQA;
     astamp(a, l, 0, first);
-    // 1) cached keys/values of the chunk: streamed by the producer through the ring, or
-    //    (larger passes) loaded here with every thread's 16-byte loads issued at once
-    {
-        const int nold = max(0, min(k1, pos0) - k0);          // keys < pos0 come from the cache
-        if constexpr (R <= MEGA_RING_KV_MAX_R) {
-            consume_kv<KVT>(ring, nold, Ks);
-            consume_kv<KVT>(ring, nold, Vs);
-        } else {
-            constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
-            for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
-                const int isv = e >= nold * PARTS;
-                const int ee = isv ? e - nold * PARTS : e;
-                const int kk = ee / PARTS, part = ee % PARTS;
-                const KVT* row = isv ? kv_v<KVT>(L, slot, g, k0 + kk) : kv_k<KVT>(L, slot, g, k0 + kk);
-                load_kv_row16<KVT>(row, part, (isv ? Vs : Ks) + kk * (DH + 1));
+    // queries of heads 4g..4g+3 (warps), and the block rows' own keys/values (produced here);
+    // they land in rows [nold, nk) of Ks / Vs, disjoint from the cached rows
+    auto queries_and_new_keys = [&]() {
+        const int vres_mode = (a.pulse == 0) ? (l == 0 ? 1 : 2) : 0;
+        const int nnew = max(0, k1 - max(k0, pos0));
+        for (int it = cw; it < nq + nnew; it += MEGA_NCW) {
+            if (it < nq) {
+                const int rr = it / GQA, h = g * GQA + it % GQA;
+                const int pos = rows[r0 + rr].y;
+                const float* src = a.qkv + (int64_t)(r0 + rr) * QKV + h * DH;
+                const float x1 = __ldcg(src + lane), x2 = __ldcg(src + lane + 32);
+                const float* qw = a.qn[l] + h * DH;
+                const float w1 = __ldg(qw + lane), w2 = __ldg(qw + lane + 32);
+                const float* rp = s->rope[local ? 0 : 1][r0 + rr];
+                const float cs = rp[lane], sn = rp[32 + lane];
+                const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + a.eps);
+                const float q1 = w1 * (x1 * inv), q2 = w2 * (x2 * inv);
+                float y1 = q1 * cs - q2 * sn, y2 = q2 * cs + q1 * sn;
+                if (!local && pos + 1 > a.base_seq_len) {
+                    const double b = (double)a.base_seq_len;
+                    const float sc = (float)(1.0 + 0.1 * log(fmax((double)(pos + 1), b) / b));
+                    y1 *= sc;
+                    y2 *= sc;
+                }
+                qs[it * DH + lane] = y1 * 0.125f;
+                qs[it * DH + lane + 32] = y2 * 0.125f;
+            } else {
+                const int key = max(k0, pos0) + (it - nq);
+                const int kk = key - k0;
+                const int rr = r0 + (key - pos0);
+                const float* src = a.qkv + (int64_t)rr * QKV;
+                const float e1 = __ldcg(src + H * DH + g * DH + lane), e2 = __ldcg(src + H * DH + g * DH + lane + 32);
+                float v1 = __ldcg(src + H * DH + HKV * DH + g * DH + lane);
+                float v2 = __ldcg(src + H * DH + HKV * DH + g * DH + lane + 32);
+                float* vf = a.vfirst + ((int64_t)rr * HKV + g) * DH;
+                const float* kw = a.kn[l] + g * DH;
+                const float w1 = __ldg(kw + lane), w2 = __ldg(kw + lane + 32);
+                const float* rp = s->rope[local ? 0 : 1][rr];   // row rr sits at position key
+                const float cs = rp[lane], sn = rp[32 + lane];
+                if (vres_mode == 1) {
+                    vf[lane] = v1;
+                    vf[lane + 32] = v2;
+                } else if (vres_mode == 2) {
+                    const float lv = a.vres[l];
+                    v1 = (1.f - lv) * v1 + lv * __ldcg(vf + lane);
+                    v2 = (1.f - lv) * v2 + lv * __ldcg(vf + lane + 32);
+                }
+                const float inv = rsqrtf(warp_sum(e1 * e1 + e2 * e2) / (float)DH + a.eps);
+                const float b1 = w1 * (e1 * inv), b2 = w2 * (e2 * inv);
+                const float y1 = b1 * cs - b2 * sn, y2 = b2 * cs + b1 * sn;
+                if (!(rows[rr].w & 1)) {   // bit 0: the row keeps its cached K/V (exited early)
+                    KVT* kp = kv_k<KVT>(L, slot, g, key);
+                    KVT* vp = kv_v<KVT>(L, slot, g, key);
+                    kv_store(kp + lane, y1);
+                    kv_store(kp + lane + 32, y2);
+                    kv_store(vp + lane, v1);
+                    kv_store(vp + lane + 32, v2);
+                }
+                // the stored (rounded) values, so every reader sees identical keys
+                Ks[kk * (DH + 1) + lane] = kv_round<KVT>(y1);
+                Ks[kk * (DH + 1) + lane + 32] = kv_round<KVT>(y2);
+                Vs[kk * (DH + 1) + lane] = kv_round<KVT>(v1);
+                Vs[kk * (DH + 1) + lane + 32] = kv_round<KVT>(v2);
             }
         }
-        // rows past the end of a partial chunk: zeros (probabilities are 0 there; 0 * stale
-        // shared memory could be NaN)
-        for (int e = tid; e < (MEGA_CHUNK - nk) * DH; e += MEGA_NCT) {
-            const int kk = nk + e / DH, d = e % DH;
-            Ks[kk * (DH + 1) + d] = 0.f;
-            Vs[kk * (DH + 1) + d] = 0.f;
+    };
+    // 1) cached keys/values of the chunk. One- and two-row passes: the producer streamed them
+    //    through the ring during phase A, so the queries' L2 reads go first and the tiles land
+    //    meanwhile. Larger passes load them here, every thread's 16-byte loads issued first.
+    if constexpr (R <= MEGA_RING_KV_MAX_R) {
+        queries_and_new_keys();
+        astamp(a, l, 1, first);
+        consume_kv<KVT>(ring, nold, Ks);
+        consume_kv<KVT>(ring, nold, Vs);
+    } else {
+        constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
+        for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
+            const int isv = e >= nold * PARTS;
+            const int ee = isv ? e - nold * PARTS : e;
+            const int kk = ee / PARTS, part = ee % PARTS;
+            const KVT* row = isv ? kv_v<KVT>(L, slot, g, k0 + kk) : kv_k<KVT>(L, slot, g, k0 + kk);
+            load_kv_row16<KVT>(row, part, (isv ? Vs : Ks) + kk * (DH + 1));
         }
+        astamp(a, l, 1, first);
+        queries_and_new_keys();
     }
-    astamp(a, l, 1, first);
-    // 2) queries of heads 4g..4g+3 (warps), and the block rows' own keys/values (produced here)
-    const int vres_mode = (a.pulse == 0) ? (l == 0 ? 1 : 2) : 0;
-    const int nnew = max(0, k1 - max(k0, pos0));
-    for (int it = cw; it < nq + nnew; it += MEGA_NCW) {
-        if (it < nq) {
-            const int rr = it / GQA, h = g * GQA + it % GQA;
-            const int pos = a.rows[r0 + rr].y;
-            const float* src = a.qkv + (int64_t)(r0 + rr) * QKV + h * DH;
-            const float x1 = __ldcg(src + lane), x2 = __ldcg(src + lane + 32);
-            const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + a.eps);
-            const float* qw = a.qn[l] + h * DH;
-            const float q1 = __ldg(qw + lane) * (x1 * inv), q2 = __ldg(qw + lane + 32) * (x2 * inv);
-            const float cs = __ldg(cos_t + (int64_t)pos * 32 + lane), sn = __ldg(sin_t + (int64_t)pos * 32 + lane);
-            float y1 = q1 * cs - q2 * sn, y2 = q2 * cs + q1 * sn;
-            if (!local && pos + 1 > a.base_seq_len) {
-                const double b = (double)a.base_seq_len;
-                const float sc = (float)(1.0 + 0.1 * log(fmax((double)(pos + 1), b) / b));
-                y1 *= sc;
-                y2 *= sc;
-            }
-            qs[it * DH + lane] = y1 * 0.125f;
-            qs[it * DH + lane + 32] = y2 * 0.125f;
-        } else {
-            const int key = max(k0, pos0) + (it - nq);
-            const int kk = key - k0;
-            const int rr = r0 + (key - pos0);
-            const float* src = a.qkv + (int64_t)rr * QKV;
-            const float e1 = __ldcg(src + H * DH + g * DH + lane), e2 = __ldcg(src + H * DH + g * DH + lane + 32);
-            float v1 = __ldcg(src + H * DH + HKV * DH + g * DH + lane);
-            float v2 = __ldcg(src + H * DH + HKV * DH + g * DH + lane + 32);
-            float* vf = a.vfirst + ((int64_t)rr * HKV + g) * DH;
-            if (vres_mode == 1) {
-                vf[lane] = v1;
-                vf[lane + 32] = v2;
-            } else if (vres_mode == 2) {
-                const float lv = a.vres[l];
-                v1 = (1.f - lv) * v1 + lv * __ldcg(vf + lane);
-                v2 = (1.f - lv) * v2 + lv * __ldcg(vf + lane + 32);
-            }
-            const float inv = rsqrtf(warp_sum(e1 * e1 + e2 * e2) / (float)DH + a.eps);
-            const float* kw = a.kn[l] + g * DH;
-            const float b1 = __ldg(kw + lane) * (e1 * inv), b2 = __ldg(kw + lane + 32) * (e2 * inv);
-            const float cs = __ldg(cos_t + (int64_t)key * 32 + lane), sn = __ldg(sin_t + (int64_t)key * 32 + lane);
-            const float y1 = b1 * cs - b2 * sn, y2 = b2 * cs + b1 * sn;
-            KVT* kp = kv_k<KVT>(L, slot, g, key);
-            KVT* vp = kv_v<KVT>(L, slot, g, key);
-            if (!(a.rows[rr].w & 1)) {   // bit 0: the row keeps its cached K/V (exited early)
-                kv_store(kp + lane, y1);
-                kv_store(kp + lane + 32, y2);
-                kv_store(vp + lane, v1);
-                kv_store(vp + lane + 32, v2);
-            }
-            // the stored (rounded) values, so every reader sees identical keys
-            Ks[kk * (DH + 1) + lane] = kv_round<KVT>(y1);
-            Ks[kk * (DH + 1) + lane + 32] = kv_round<KVT>(y2);
-            Vs[kk * (DH + 1) + lane] = kv_round<KVT>(v1);
-            Vs[kk * (DH + 1) + lane + 32] = kv_round<KVT>(v2);
-        }
+    // rows past the end of a partial chunk: zeros (probabilities are 0 there; 0 * stale
+    // shared memory could be NaN)
+    for (int e = tid; e < (MEGA_CHUNK - nk) * DH; e += MEGA_NCT) {
+        const int kk = nk + e / DH, d = e % DH;
+        Ks[kk * (DH + 1) + d] = 0.f;
+        Vs[kk * (DH + 1) + d] = 0.f;
     }
     named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 2, first);
@@ -597,7 +646,7 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     for (int e = tid; e < nq * MEGA_CHUNK; e += MEGA_NCT) {
         const int qi = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
         const int key = k0 + kk;
-        const int pos = a.rows[r0 + qi / GQA].y;
+        const int pos = rows[r0 + qi / GQA].y;
         const int lor = local ? max(0, pos - WINDOW + 1) : 0;
         float sc = -INFINITY;
         if (kk < nk && key <= pos && key >= lor) {
@@ -611,32 +660,34 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     }
     named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 3, first);
-    // 4) partial softmax and P.V per query
+    // 4) partial softmax per query (warps): max m, weights e = exp(s - m) back into Ps, sum
     for (int qi = cw; qi < nq; qi += MEGA_NCW) {
         const int rr = qi / GQA, h = g * GQA + qi % GQA;
         const float p0 = Ps[qi * MEGA_CHUNK + lane], p1 = Ps[qi * MEGA_CHUNK + lane + 32];
         const float m = warp_max(fmaxf(p0, p1));
-        float* out = a.part + (((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART;
-        if (m == -INFINITY) {
-            if (lane == 0) { out[0] = -INFINITY; out[1] = 0.f; }
-            continue;
-        }
         const float e0 = (p0 == -INFINITY) ? 0.f : expf(p0 - m);
         const float e1 = (p1 == -INFINITY) ? 0.f : expf(p1 - m);
         const float lsum = warp_sum(e0 + e1);
-        float o1 = 0.f, o2 = 0.f;
-#pragma unroll 8
-        for (int j = 0; j < 32; ++j) {
-            const float pa = __shfl_sync(0xffffffffu, e0, j);
-            const float pb = __shfl_sync(0xffffffffu, e1, j);
-            o1 += pa * Vs[j * (DH + 1) + lane] + pb * Vs[(j + 32) * (DH + 1) + lane];
-            o2 += pa * Vs[j * (DH + 1) + lane + 32] + pb * Vs[(j + 32) * (DH + 1) + lane + 32];
+        Ps[qi * MEGA_CHUNK + lane] = e0;
+        Ps[qi * MEGA_CHUNK + lane + 32] = e1;
+        float* out = a.part + (((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART;
+        if (lane == 0) {
+            out[0] = m;   // -inf: no key of the chunk is visible to this row (weights all 0)
+            out[1] = m == -INFINITY ? 0.f : lsum;
         }
-        if (lane == 0) { out[0] = m; out[1] = lsum; }
-        out[2 + lane] = o1;
-        out[2 + lane + 32] = o2;
     }
+    named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 4, first);
+    // 5) P.V: one thread per (query, dimension), keys in order
+    for (int e = tid; e < nq * DH; e += MEGA_NCT) {
+        const int qi = e / DH, d = e % DH;
+        const int rr = qi / GQA, h = g * GQA + qi % GQA;
+        const float* pr = Ps + qi * MEGA_CHUNK;
+        float o = 0.f;
+#pragma unroll 16
+        for (int kk = 0; kk < MEGA_CHUNK; ++kk) o += pr[kk] * Vs[kk * (DH + 1) + d];
+        a.part[(((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART + 2 + d] = o;
+    }
     named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 5, first);
 }
@@ -741,6 +792,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         s->abort = 0;
         fence_mbar_init();
     }
+    if (threadIdx.x >= 32 && threadIdx.x < 32 + R) s->rows[threadIdx.x - 32] = a.rows[threadIdx.x - 32];
     __syncthreads();
 
     // ================================================================ producer
@@ -750,7 +802,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         int pblk[MEGA_RMAX + 1], pnb = 0;   // sequence blocks of the rows (as the consumers build them)
         for (int r0 = 0; r0 < R;) {
             int nr = 1;
-            while (r0 + nr < R && a.rows[r0 + nr].x == a.rows[r0].x) ++nr;
+            while (r0 + nr < R && s->rows[r0 + nr].x == s->rows[r0].x) ++nr;
             pblk[pnb++] = r0;
             r0 += nr;
         }
@@ -767,7 +819,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             if (R <= MEGA_RING_KV_MAX_R) {   // cached K/V chunks of this CTA's attention items (phase B)
                 const bool local = is_local_layer(l);
                 AttnGeo geo;
-                for (int item = cta; g.ok && attn_geo(a, pblk, pnb, local, item, geo); item += C) {
+                for (int item = cta; g.ok && attn_geo(s->rows, pblk, pnb, local, item, geo); item += C) {
                     if (geo.nold <= 0) continue;
                     produce_kv<KVT>(g, a.kvl[l], geo.slot, geo.g, geo.k0, geo.nold, false);
                     produce_kv<KVT>(g, a.kvl[l], geo.slot, geo.g, geo.k0, geo.nold, true);
@@ -781,13 +833,16 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 produce_rows(g, a.sh_gu[l], D * 2, j0, j1, 4);
                 produce_rows(g, a.sh_gu[l], D * 2, DS + j0, DS + j1, 4);
             }
-            // routed pairs depend on this layer's router
-            // sleep between polls: a tight spin on shared memory starves the consumers' loads
+            // routed pairs depend on this layer's router. Short sleeps between polls (a tight
+            // spin on shared memory starves the consumers' loads); the global error flag costs
+            // an L2 round trip, so it is read every 256th poll only
             const unsigned long long t0 = globaltimer();
-            while (s->moe_ready != l + 1) {
-                __nanosleep(200);
-                if (s->moe_ready == l + 1) break;
-                if (globaltimer() - t0 > WAIT_NS || *(volatile int*)a.err || s->abort) { g.ok = false; break; }
+            for (unsigned it = 1; s->moe_ready != l + 1; ++it) {
+                __nanosleep(32);
+                if (globaltimer() - t0 > WAIT_NS || s->abort || ((it & 255) == 0 && *(volatile int*)a.err)) {
+                    g.ok = false;
+                    break;
+                }
             }
             if (!g.ok) break;
             __threadfence_block();   // the expert list was written before the flag
@@ -843,10 +898,16 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         const int ll = t / MEGA_MAXOROWS, oi = t % MEGA_MAXOROWS;
         s->rsc[ll][oi] = oi < nown ? a.rscale[ll][own0 + oi] : 0.f;
     }
+    for (int t = threadIdx.x - 32; t < NL * E; t += MEGA_NCT) s->ebias[t / E][t % E] = a.ebias[t / E][t % E];
+    for (int t = threadIdx.x - 32; t < 2 * R * DH; t += MEGA_NCT) {
+        const int tab = t / (R * DH), r = (t / DH) % R, j = t % DH;
+        const float* T = (j < 32) ? (tab ? a.cos_g : a.cos_l) : (tab ? a.sin_g : a.sin_l);
+        s->rope[tab][r][j] = T[(int64_t)s->rows[r].y * 32 + (j & 31)];
+    }
     // ---- pulse input: every CTA builds h_in for all rows in xs[0 .. R*D) ----
     if (p == 0) {
         for (int r = cw; r < R; r += MEGA_NCW) {
-            const int tok = min(max(a.rows[r].z, 0), a.V - 1);
+            const int tok = min(max(s->rows[r].z, 0), a.V - 1);
             const __nv_bfloat16* e = a.emb + (int64_t)tok * D;
             float v[32];
             float ss = 0.f;
@@ -936,7 +997,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         int nb = 0, r0 = 0;
         while (r0 < R) {
             int nr = 1;
-            while (r0 + nr < R && a.rows[r0 + nr].x == a.rows[r0].x) ++nr;
+            while (r0 + nr < R && s->rows[r0 + nr].x == s->rows[r0].x) ++nr;
             s->blk_r0[nb++] = r0;
             r0 += nr;
         }
@@ -964,13 +1025,13 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                     for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
                 }
             } else {
-                norm_rows<R>(a.h, a.attn_norm[l], eps, xs);
+                norm_rows<R>(a.h, a.attn_norm[l], eps, xs, s->nred);
             }
             if (threadIdx.x - 32 < R) s->xoff[threadIdx.x - 32] = (threadIdx.x - 32) * D;
             // attention chunking of each block (used in phase B)
             if (threadIdx.x == 33) {
                 for (int b = 0; b < s->n_blk; ++b) {
-                    const int pos0 = a.rows[s->blk_r0[b]].y, posL = a.rows[s->blk_r0[b + 1] - 1].y;
+                    const int pos0 = s->rows[s->blk_r0[b]].y, posL = s->rows[s->blk_r0[b + 1] - 1].y;
                     const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
                     const int chunk = attn_chunk(posL - lo + 1);
                     s->blk_chunk[b] = chunk;
@@ -1065,7 +1126,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             {
                 // router logits = fixed-order sum over CTAs of the partials / rms: thread t adds
                 // float4 column t % (R*E/4) of CTAs t / (R*E/4), + G, ... (its loads issued
-                // before the norm's), then a warp per (row, expert) adds the G group sums
+                // before the norm's), then a warp per row adds the G group sums
                 constexpr int NC4 = R * E / 4;
                 constexpr int G = MEGA_NCT / NC4;
                 constexpr int MAXL = (148 + G - 1) / G;   // loads per thread kept in flight
@@ -1074,13 +1135,14 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 const bool active = t < G * NC4;
                 const float4* src = reinterpret_cast<const float4*>(a.rpart) + col;
                 float4 pv[MAXL];
-                ebias_lane = (lane < E) ? __ldg(a.ebias[l] + lane) : 0.f;   // for the top-k below
+                ebias_lane = (lane < E) ? s->ebias[l][lane] : 0.f;   // for the top-k below
 #pragma unroll
                 for (int k = 0; k < MAXL; ++k) {
                     const int c = cg + k * G;
                     pv[k] = (active && c < C) ? __ldcg(src + (int64_t)c * NC4) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                norm_rows<R>(a.h, a.mlp_norm[l], eps, xs, s->rinv);
+                norm_rows<R>(a.h, a.mlp_norm[l], eps, xs, s->nred, s->rinv);
+                rstamp(a, l, 0);
                 if (active) {
                     float4 z = pv[0];
 #pragma unroll
@@ -1099,57 +1161,57 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                     }
                     reinterpret_cast<float4*>(s->stage)[cg * NC4 + col] = z;
                 }
-                named_bar_sync(1, MEGA_NCT);
-                if constexpr (G <= 32) {   // few groups: one thread per (row, expert)
-                    if (t < R * E) {
-                        float z = 0.f;
-#pragma unroll
-                        for (int k = 0; k < G; ++k) z += s->stage[k * R * E + t];
-                        s->logits[t / E][t % E] = z * s->rinv[t / E];
-                    }
-                } else {
-                    for (int re = cw; re < R * E; re += MEGA_NCW) {
-                        float z = 0.f;
-                        for (int k = lane; k < G; k += 32) z += s->stage[k * R * E + re];
-                        z = warp_sum(z);
-                        if (lane == 0) s->logits[re / E][re % E] = z * s->rinv[re / E];
-                    }
-                }
+                rstamp(a, l, 1);
             }
             named_bar_sync(1, MEGA_NCT);
+            rstamp(a, l, 2);
+            // a warp per row: logit of expert e = lanes e and e + 16 adding the even / odd
+            // groups of the staged sums; centre, sigmoid; top-4 of s + bias by rank (expert e
+            // is chosen iff fewer than 4 experts beat it, ties to the lower expert), weights
             for (int r = cw; r < R; r += MEGA_NCW) {
-                // centre, sigmoid, top-4 of s + bias (ties to the lower expert), weights
-                const float lg = lane < E ? s->logits[r][lane] : 0.f;
+                constexpr int G = MEGA_NCT / (R * E / 4);
+                const int e = lane & (E - 1), hf = lane >> 4;
+                float z0 = 0.f, z1 = 0.f;
+#pragma unroll 8
+                for (int k = hf; k < G; k += 4) {
+                    z0 += s->stage[k * R * E + r * E + e];
+                    if (k + 2 < G) z1 += s->stage[(k + 2) * R * E + r * E + e];
+                }
+                float z = z0 + z1;
+                z += __shfl_xor_sync(0xffffffffu, z, 16);
+                const float lg = lane < E ? z * s->rinv[r] : 0.f;
                 const float mean = warp_sum(lg) / (float)E;
                 const float sg = sigmoidf_(lg - mean);
-                float b = lane < E ? sg + ebias_lane : -INFINITY;
-                float sel_s[TOPK];
-                int sel_i[TOPK];
-                unsigned used = 0;
-#pragma unroll
-                for (int k = 0; k < TOPK; ++k) {
-                    ArgMax am{b, lane < E ? lane : 1 << 30};
-                    am = warp_argmax(am);
-                    sel_i[k] = am.i;
-                    sel_s[k] = __shfl_sync(0xffffffffu, sg, am.i & 31);
-                    if (lane == am.i) b = -INFINITY;
-                    if (am.i < E) used |= 1u << am.i;
+                const float b = sg + ebias_lane;
+                if (lane < E) {
+                    s->logits[r][lane] = b;
+                    s->rsg[r][lane] = sg;
                 }
+                __syncwarp();
+                int rank = 0;
+#pragma unroll
+                for (int j = 0; j < E; ++j) {
+                    const float bj = s->logits[r][j];
+                    rank += (bj > b || (bj == b && j < lane)) ? 1 : 0;
+                }
+                const bool chosen = lane < E && rank < TOPK;
+                if (chosen) s->idx[r][rank] = lane;
+                const unsigned used = __ballot_sync(0xffffffffu, chosen);
+                __syncwarp();
+                // weights: the chosen scores summed in rank order (as the reference's top-k order)
+                const float sk = lane < TOPK ? s->rsg[r][s->idx[r][lane]] : 0.f;
                 float sum = 0.f;
 #pragma unroll
-                for (int k = 0; k < TOPK; ++k) sum += sel_s[k];
+                for (int k = 0; k < TOPK; ++k) sum += __shfl_sync(0xffffffffu, sk, k);
                 sum += 1e-6f;
-#pragma unroll
-                for (int k = 0; k < TOPK; ++k)
-                    if (lane == k) {
-                        s->idx[r][k] = sel_i[k];
-                        s->wts[r][k] = sel_s[k] / sum;
-                    }
+                if (lane < TOPK) s->wts[r][lane] = sk / sum;
                 if (lane == 0) s->rmask[r] = used;
             }
-            named_bar_sync(1, MEGA_NCT);
+            if constexpr (R > 1) named_bar_sync(1, MEGA_NCT);   // every row's expert mask
+            rstamp(a, l, 3);
             if (cw == 0) {
                 unsigned used = 0;
+                __syncwarp();
 #pragma unroll
                 for (int r = 0; r < R; ++r) used |= s->rmask[r];
                 // distinct experts in increasing order (the producer's routed stream), then the flag
