@@ -218,6 +218,15 @@ int pulsar_engine_generate_sampled(pulsar_engine* eng, int32_t n_seq, const int3
  * between generate calls, not while one runs on another stream. */
 int pulsar_engine_set_early_exit(pulsar_engine* eng, int32_t enabled, float threshold);
 
+/* Repetition penalty of the sequential greedy loop (src/infer.py:582-589, the reference's
+ * default 1.15 in stream_generate / generate): when choosing each token of
+ * pulsar_engine_generate_greedy with gamma == 0, logits of ids already seen are divided by
+ * the penalty when positive and multiplied by it otherwise, then the argmax is taken. The
+ * seen set of a slot is the prompt of its last pulsar_engine_prefill plus every token that
+ * generate calls emitted for it since (a bitmap on the device). penalty > 0; 1 turns it off.
+ * Speculative and sampled generate calls return PULSAR_ERR_UNSUPPORTED while it is on. */
+int pulsar_engine_set_repetition_penalty(pulsar_engine* eng, float penalty);
+
 /* counts_host[3]: tokens that exited after pulse 1, 2 and 3 (the reference's
  * early_exit_counts) since the last pulsar_engine_set_early_exit or create. Waits for the
  * device. */
@@ -236,6 +245,11 @@ int pulsar_engine_early_exit_counts(pulsar_engine* eng, int64_t* counts_host);
  * record CUDA events on the caller's stream
  * around every pulse pass launched outside stream capture; "last_pulse_ns" (read-only,
  * waits for the last such pass) is the device time between those events. */
+/* "merged_adapter" (0/1, needs a finalized engine): with a live loop adapter (non-zero
+ * lora_B), build per-pulse bf16 merged wqkv / wo (src/model.py:716-727 with a bf16 base:
+ * bf16 A, bf16(bf16 B * bf16(loop_M[p] * alpha / q)), fp32 product sum in order plus the
+ * base, one rounding) and run every pass on them, the persistent kernel included; 0 returns
+ * to the exact fp32 adapter correction. Without a live adapter it stays 0. */
 int pulsar_engine_set_option(pulsar_engine* eng, const char* name, int64_t value);
 int pulsar_engine_get_option(pulsar_engine* eng, const char* name, int64_t* value);
 

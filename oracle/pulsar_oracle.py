@@ -101,6 +101,24 @@ def merged_weight(base, lora_A, lora_B, loop_M, pulse: int, K: int, alpha: float
     return torch.addmm(base, B_scaled, A_all)
 
 
+def merged_weight_bf16(base, lora_A, lora_B, loop_M, pulse: int, K: int, alpha: float) -> torch.Tensor:
+    """src/model.py:716-727 with a bf16 base weight (the reference's GPU inference dtype):
+    A_all = bf16(lora_A), B_scaled = bf16(bf16(lora_B) * bf16(loop_M[p] * alpha/q)), and the
+    bf16 addmm taken as one rounding of (sum_c B_scaled[:, c] A_all[c] in fp32, in order c) +
+    base. Each bf16 x bf16 product is exact in fp32, so the order fixes the value; the
+    reference's GEMM may order its fp32 sum differently (last-bit differences)."""
+    q = lora_A.shape[1]
+    bf = torch.bfloat16
+    A_all = lora_A[:K].to(bf).float().reshape(K * q, -1)
+    ms = (loop_M[pulse, :K].float() * (alpha / q)).to(bf)
+    B_perm = lora_B[:K].to(bf).permute(1, 0, 2)                       # [d_out][K][q]
+    B_scaled = (B_perm * ms.view(1, K, 1)).float().reshape(B_perm.shape[0], K * q)
+    acc = torch.zeros(B_scaled.shape[0], A_all.shape[1])
+    for c in range(K * q):
+        acc = acc + B_scaled[:, c:c + 1] * A_all[c:c + 1, :]
+    return (acc + base.to(bf).float()).to(bf).float()
+
+
 def router_topk(logits: torch.Tensor, bias: torch.Tensor, top_k: int):
     """src/infer.py:325-333 (and the fallback at src/model.py:1312-1317): centre the fp32
     logits, sigmoid, top-k of (scores + bias), weights = s_k / (sum s_k + 1e-6)."""
@@ -156,7 +174,9 @@ class OracleModel:
     (src/infer.py:250-254, 308-312).
     """
 
-    def __init__(self, state_dict, cfg):
+    def __init__(self, state_dict, cfg, merge: str = "fp32"):
+        """merge: "fp32" (the reference's fp32 run, the default) or "bf16" (its GPU path's
+        bf16 merged weights, merged_weight_bf16)."""
         self.cfg = cfg
         g = lambda n: _cfg_get(cfg, n)
         self.D = g("d_model")
@@ -188,12 +208,13 @@ class OracleModel:
             b = f"core.{i}.attn."
             for p in range(self.K):
                 if (b + "wqkv_adapter.lora_A") in sd and g("loop_lora_rank") > 0:
-                    self.wqkv[p][i] = merged_weight(sd[b + "wqkv.weight"], sd[b + "wqkv_adapter.lora_A"],
-                                                    sd[b + "wqkv_adapter.lora_B"], sd[b + "wqkv_adapter.loop_M"],
-                                                    p, self.K, self.alpha)
-                    self.wo[p][i] = merged_weight(sd[b + "wo.weight"], sd[b + "wo_adapter.lora_A"],
-                                                  sd[b + "wo_adapter.lora_B"], sd[b + "wo_adapter.loop_M"],
-                                                  p, self.K, self.alpha)
+                    mw = merged_weight_bf16 if merge == "bf16" else merged_weight
+                    self.wqkv[p][i] = mw(sd[b + "wqkv.weight"], sd[b + "wqkv_adapter.lora_A"],
+                                         sd[b + "wqkv_adapter.lora_B"], sd[b + "wqkv_adapter.loop_M"],
+                                         p, self.K, self.alpha)
+                    self.wo[p][i] = mw(sd[b + "wo.weight"], sd[b + "wo_adapter.lora_A"],
+                                       sd[b + "wo_adapter.lora_B"], sd[b + "wo_adapter.loop_M"],
+                                       p, self.K, self.alpha)
                 else:
                     self.wqkv[p][i] = sd[b + "wqkv.weight"]
                     self.wo[p][i] = sd[b + "wo.weight"]

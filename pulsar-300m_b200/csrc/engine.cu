@@ -45,6 +45,32 @@ __global__ void k_transpose_bf16(const float* __restrict__ src, __nv_bfloat16* _
     }
 }
 
+// Per-pulse merged weight in bf16, the reference's GPU path (get_merged_weight with a bf16
+// base weight, src/model.py:716-727): A16 = bf16(lora_A[:3]) as [3q][d_in];
+// Bs16[o][j*q + r] = bf16(bf16(lora_B[j][o][r]) * bf16(loop_M[p][j] * alpha / q));
+// out[o][i] = bf16(sum_c Bs16[o][c] * A16[c][i] + W[o][i]): the product sum in fp32 in order
+// c = 0 .. 3q-1 (each bf16 x bf16 product is exact in fp32), then the base weight added, one
+// rounding (a GEMM's alpha * AB + beta * C epilogue).
+__global__ void k_merge_adapter(const __nv_bfloat16* __restrict__ w, const float* __restrict__ lora_a,
+                                const float* __restrict__ lora_b, const float* __restrict__ loop_m, int P, int p,
+                                float scale, int d_out, int d_in, int q, __nv_bfloat16* __restrict__ out) {
+    const int64_t n = (int64_t)d_out * d_in;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int o = (int)(e / d_in), i = (int)(e % d_in);
+        float acc = 0.f;
+        for (int j = 0; j < 3; ++j) {
+            const float ms = __bfloat162float(__float2bfloat16(loop_m[p * P + j] * scale));
+            for (int r = 0; r < q; ++r) {
+                const float b = __bfloat162float(__float2bfloat16(
+                    __bfloat162float(__float2bfloat16(lora_b[((int64_t)j * d_out + o) * q + r])) * ms));
+                const float a = __bfloat162float(__float2bfloat16(lora_a[((int64_t)j * q + r) * d_in + i]));
+                acc = __fadd_rn(acc, __fmul_rn(b, a));
+            }
+        }
+        out[e] = __float2bfloat16(__fadd_rn(acc, __bfloat162float(w[e])));
+    }
+}
+
 // Loop-adapter up factor for pulse p: dst[o][j*q + r] = lora_B[j][o][r] * (loop_M[p][j] * alpha / q).
 __global__ void k_lora_b(const float* __restrict__ lora_b, const float* __restrict__ loop_m, int P, int p, float scale,
                          int d_out, int q, float* __restrict__ dst) {
@@ -85,6 +111,7 @@ struct LoopOut {
     unsigned long long seed;   // sampled decoding: Philox key, temperature, top-p
     float temperature, top_p;
     float ee_thr;              // early exit: softmax max-probability threshold
+    float rep_penalty;         // repetition penalty of the sequential greedy loop
 };
 
 // Starts a generate call: sequence state, first token, and the row descriptors of round 0
@@ -162,6 +189,83 @@ __global__ void k_commit_ee(SeqDev* seqs, const int* amax0, const int* amax1, co
     seqs[i].pending = t;
     seqs[i].len += 1;
     if (seqs[i].n_out >= n_new) seqs[i].done = 1;
+}
+
+// Seen-token bitmap of a slot (W = V / 32 words): cleared, then the prompt's ids set.
+__global__ void k_seen_init(uint32_t* __restrict__ sb, const int* __restrict__ ids, int T, int W) {
+    for (int i = threadIdx.x; i < W; i += blockDim.x) sb[i] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < T; i += blockDim.x) atomicOr(&sb[ids[i] >> 5], 1u << (ids[i] & 31));
+}
+
+// src/infer.py:582-589: logits of seen ids divided by the penalty when positive, multiplied
+// otherwise (IEEE division, as torch's), then the argmax (ties to the lowest index) of one
+// logits row per block. Every thread returns the index.
+__device__ int penalized_argmax(const float* __restrict__ lg, int V, const uint32_t* __restrict__ sb, float pen,
+                                float* bv, int* bi) {
+    ArgMax b{-INFINITY, 1 << 30};
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        float v = lg[j];
+        if ((sb[j >> 5] >> (j & 31)) & 1u) v = v > 0.f ? v / pen : v * pen;
+        b = argmax_merge(b, ArgMax{v, j});
+    }
+    b = warp_argmax(b);
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+        bv[w] = b.v;
+        bi[w] = b.i;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int nw = blockDim.x >> 5;
+        ArgMax c = threadIdx.x < nw ? ArgMax{bv[threadIdx.x], bi[threadIdx.x]} : ArgMax{-INFINITY, 1 << 30};
+        c = warp_argmax(c);
+        if (threadIdx.x == 0) bi[0] = c.i;
+    }
+    __syncthreads();
+    return bi[0];
+}
+
+// First token of a penalized loop: penalized argmax of the first logits (seen = the prompt),
+// which then joins the seen set.
+__global__ void __launch_bounds__(1024) k_first_penalized(const float* __restrict__ lg, int V, const int* slots,
+                                                         uint32_t* seen, const LoopOut* lo, int* out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int i = blockIdx.x;
+    uint32_t* sb = seen + (int64_t)slots[i] * (V / 32);
+    const int t = penalized_argmax(lg + (int64_t)i * V, V, sb, lo->rep_penalty, bv, bi);
+    if (threadIdx.x == 0) {
+        out[i] = t;
+        sb[t >> 5] |= 1u << (t & 31);
+    }
+}
+
+// Commit of a penalized sequential step (one block per sequence): the logits row of the
+// exiting pulse (ee given) or of the last pulse, penalized argmax, seen set, exit tally.
+__global__ void __launch_bounds__(1024) k_commit_penalized(SeqDev* seqs, const float* lg0, const float* lg1,
+                                                          const float* lg2, const int* ee, int n, int V,
+                                                          const LoopOut* lo, const int* slots, uint32_t* seen,
+                                                          unsigned long long* counts) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int i = blockIdx.x;
+    if (seqs[i].done) return;   // uniform
+    const int k = ee ? ee[2 + i] : NP - 1;
+    const float* lg = (k == 0 ? lg0 : k == 1 ? lg1 : lg2) + (int64_t)i * V;
+    uint32_t* sb = seen + (int64_t)slots[i] * (V / 32);
+    const int t = penalized_argmax(lg, V, sb, lo->rep_penalty, bv, bi);
+    if (threadIdx.x == 0) {
+        if (ee) atomicAdd(&counts[k], 1ull);
+        sb[t >> 5] |= 1u << (t & 31);
+        const int n_new = lo->n_new;
+        lo->out[(int64_t)i * n_new + seqs[i].n_out] = t;
+        seqs[i].n_out += 1;
+        seqs[i].pending = t;
+        seqs[i].len += 1;
+        if (seqs[i].n_out >= n_new) seqs[i].done = 1;
+    }
 }
 
 __global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, const LoopOut* lo) {
@@ -348,6 +452,10 @@ struct pulsar_engine {
     // bf16 arena
     __nv_bfloat16* emb = nullptr;
     __nv_bfloat16 *wqkv[NL] = {}, *wo[NL] = {}, *sh_gu[NL] = {}, *sh_dn[NL] = {}, *r_gu[NL] = {}, *r_dn[NL] = {};
+    // option "merged_adapter": per-pulse bf16 merged wqkv / wo (the reference's GPU numerics);
+    // every pass then runs without the fp32 adapter correction (and on the persistent kernel)
+    bool merge_adapter = false;
+    __nv_bfloat16 *wqkv_m[NP][NL] = {}, *wo_m[NP][NL] = {};
     float *lb_qkv[NP][NL] = {}, *lb_wo[NP][NL] = {};
     float vres[NP][NL] = {};
     float *cos_l = nullptr, *sin_l = nullptr, *cos_g = nullptr, *sin_g = nullptr;
@@ -397,6 +505,11 @@ struct pulsar_engine {
     float ee_thr = 1.f;
     int *ee = nullptr, *ee_amax = nullptr;
     unsigned long long* ee_counts = nullptr;
+    // repetition penalty of the sequential greedy loop (off: rp_on false) and the seen-token
+    // bitmap of every slot [max_batch][V / 32] (set by prefill and by every emitted token)
+    bool rp_on = false;
+    float rp = 1.f;
+    uint32_t* seen = nullptr;
     // sampled decoding: draft logits rows [wide_rows][V] (row j*n + i), verify logits rows
     // [wide_rows][V] (row i*(gamma+1) + k), their warp statistics, sequence stream ids
     float *qbuf = nullptr, *pbuf = nullptr;
@@ -444,6 +557,12 @@ struct pulsar_engine {
 };
 
 namespace {
+
+// wqkv / wo of pulse p (merged per pulse under option "merged_adapter"), and whether the fp32
+// adapter correction applies
+const __nv_bfloat16* w_qkv(const pulsar_engine* e, int p, int l) { return e->merge_adapter ? e->wqkv_m[p][l] : e->wqkv[l]; }
+const __nv_bfloat16* w_o(const pulsar_engine* e, int p, int l) { return e->merge_adapter ? e->wo_m[p][l] : e->wo[l]; }
+bool lora_live(const pulsar_engine* e) { return e->has_lora && !e->merge_adapter; }
 
 void build_expect(pulsar_engine* e) {
     const int P = e->P, V = e->V, q = 8;
@@ -511,10 +630,10 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
     }
     PULSAR_LAUNCH_CHECK("pulse input");
     for (int l = 0; l < NL; ++l) {
-        const bool lora = e->has_lora;
+        const bool lora = lora_live(e);
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, w.xn,
                                           lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv);
-        k_gemv<1024, EPI_STORE><<<QKV / 8, 128, 0, st>>>(e->wqkv[l], QKV, w.xn, R, w.qkv, QKV,
+        k_gemv<1024, EPI_STORE><<<QKV / 8, 128, 0, st>>>(w_qkv(e, p, l), QKV, w.xn, R, w.qkv, QKV,
                                                          lora ? e->lb_qkv[p][l] : nullptr, w.t_qkv);
         const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
         const bool local = is_local_layer(l);
@@ -529,7 +648,7 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
                                              e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
-        k_gemv<1024, EPI_ADD><<<D / 8, 128, 0, st>>>(e->wo[l], D, w.att, R, w.h, D, lora ? e->lb_wo[p][l] : nullptr,
+        k_gemv<1024, EPI_ADD><<<D / 8, 128, 0, st>>>(w_o(e, p, l), D, w.att, R, w.h, D, lora ? e->lb_wo[p][l] : nullptr,
                                                      w.t_wo);
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, w.xn,
                                           nullptr, nullptr);
@@ -577,8 +696,8 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.softcap = e->cfg.logit_softcap;
     a.rows = rows;
     for (int l = 0; l < NL; ++l) {
-        a.wqkv[l] = e->wqkv[l];
-        a.wo[l] = e->wo[l];
+        a.wqkv[l] = w_qkv(e, p, l);
+        a.wo[l] = w_o(e, p, l);
         a.sh_gu[l] = e->sh_gu[l];
         a.sh_dn[l] = e->sh_dn[l];
         a.r_gu[l] = e->r_gu[l];
@@ -659,7 +778,7 @@ int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float
         return enqueue_pulse_wide<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax,
                                                  st, hs);
     }
-    if (e->use_mega && !e->has_lora && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
+    if (e->use_mega && !lora_live(e) && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
         e->n_kernels += 1;
         e->n_mega += 1;
         return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st, hs, skip);
@@ -755,11 +874,11 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
                                           e->T_("pulse_step_emb.weight") + (int64_t)p * D, eps, f.h, f.h_in, nullptr, 1);
         PULSAR_LAUNCH_CHECK("prefill pulse input");
         for (int l = 0; l < NL; ++l) {
-            const bool lora = e->has_lora;
+            const bool lora = lora_live(e);
             const bool local = is_local_layer(l);
             k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, f.xn,
                                               lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, f.t);
-            GemmArgs g = gargs(f.xn, D, T, e->wqkv[l], QKV, D, f.qkv, QKV);
+            GemmArgs g = gargs(f.xn, D, T, w_qkv(e, p, l), QKV, D, f.qkv, QKV);
             if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = f.t; }
             PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
             const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
@@ -773,7 +892,7 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
                                               e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, f.att,
                                               lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, f.t);
             PULSAR_LAUNCH_CHECK("prefill attention");
-            g = gargs(f.att, D, T, e->wo[l], D, D, f.h, D);
+            g = gargs(f.att, D, T, w_o(e, p, l), D, D, f.h, D);
             if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = f.t; }
             PULSAR_TRY(gemm<GEPI_ADD>(e, g, 1, st));
             k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, f.xn,
@@ -844,11 +963,11 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
     PULSAR_LAUNCH_CHECK("wide pulse input");
     const int cap = R, M4 = R * TOPK;
     for (int l = 0; l < NL; ++l) {
-        const bool lora = e->has_lora;
+        const bool lora = lora_live(e);
         const bool local = is_local_layer(l);
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, w.xn,
                                           lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv);
-        GemmArgs g = gargs(w.xn, D, R, e->wqkv[l], QKV, D, w.qkv, QKV);
+        GemmArgs g = gargs(w.xn, D, R, w_qkv(e, p, l), QKV, D, w.qkv, QKV);
         if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = w.t_qkv; }
         PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
         const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
@@ -863,7 +982,7 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
         PULSAR_LAUNCH_CHECK("wide attention");
-        g = gargs(w.att, D, R, e->wo[l], D, D, w.h, D);
+        g = gargs(w.att, D, R, w_o(e, p, l), D, D, w.h, D);
         if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = w.t_wo; }
         PULSAR_TRY(gemm<GEPI_ADD>(e, g, 1, st));
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, w.xn, nullptr,
@@ -994,22 +1113,39 @@ int body_step(pulsar_engine* e, cudaStream_t st, void* vctx) {
     return launch_status("k_commit_greedy");
 }
 
-// Sequential step with adaptive early exit (src/infer.py:526-549): pulses 0 and 1 also write
-// logits (qbuf rows [k * n, k * n + n)) and argmax; k_ee_check marks the rows that exit; the
-// commit takes the exiting pulse's argmax and tallies the exit depth.
-int body_step_ee(pulsar_engine* e, cudaStream_t st, void* vctx) {
+// Sequential step with adaptive early exit (src/infer.py:526-549) and / or a repetition
+// penalty (src/infer.py:582-589). Early exit: pulses 0 and 1 also write logits (qbuf rows
+// [k * n, k * n + n)) and argmax; k_ee_check marks the rows that exit; later pulses keep their
+// K/V and a persistent pass whose rows have all exited returns at once. Penalty: the last
+// pulse writes logits (pbuf) and the commit takes the penalized argmax of the exiting (or last)
+// pulse's row and adds the token to the seen set. Which of the two is on is fixed at capture.
+int body_step_x(pulsar_engine* e, cudaStream_t st, void* vctx) {
     LoopCtx* c = static_cast<LoopCtx*>(vctx);
     const int n = c->n, V = e->V, NB = e->cfg.max_batch;
+    const bool ee = e->ee_on, rp = e->rp_on;
     float* lg0 = e->qbuf;
     float* lg1 = e->qbuf + (int64_t)n * V;
-    k_rows_step_ee<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, e->rows, e->ee);
-    PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, lg0, V, e->ee_amax, st));
-    k_ee_check<<<n, SAMPLE_THREADS, 0, st>>>(lg0, V, n, 0, e->loop_out, e->seqs, e->rows, e->ee);
-    PULSAR_LAUNCH_CHECK("k_ee_check");
-    PULSAR_TRY(pulse(e, 1, n, e->rows, e->htmp, e->h0tmp, e->htmp2, nullptr, lg1, V, e->ee_amax + NB, st, 1, e->ee));
-    k_ee_check<<<n, SAMPLE_THREADS, 0, st>>>(lg1, V, n, 1, e->loop_out, e->seqs, e->rows, e->ee);
-    PULSAR_LAUNCH_CHECK("k_ee_check");
-    PULSAR_TRY(pulse(e, 2, n, e->rows, e->htmp2, e->h0tmp, e->htmp, nullptr, nullptr, 0, e->amax, st, 1, e->ee));
+    if (ee) k_rows_step_ee<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, e->rows, e->ee);
+    else k_rows_step<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, e->rows);
+    PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->htmp, e->h0tmp, ee ? lg0 : nullptr, V,
+                     ee ? e->ee_amax : nullptr, st));
+    if (ee) {
+        k_ee_check<<<n, SAMPLE_THREADS, 0, st>>>(lg0, V, n, 0, e->loop_out, e->seqs, e->rows, e->ee);
+        PULSAR_LAUNCH_CHECK("k_ee_check");
+    }
+    PULSAR_TRY(pulse(e, 1, n, e->rows, e->htmp, e->h0tmp, e->htmp2, nullptr, ee ? lg1 : nullptr, V,
+                     ee ? e->ee_amax + NB : nullptr, st, 1, ee ? e->ee : nullptr));
+    if (ee) {
+        k_ee_check<<<n, SAMPLE_THREADS, 0, st>>>(lg1, V, n, 1, e->loop_out, e->seqs, e->rows, e->ee);
+        PULSAR_LAUNCH_CHECK("k_ee_check");
+    }
+    PULSAR_TRY(pulse(e, 2, n, e->rows, e->htmp2, e->h0tmp, e->htmp, nullptr, rp ? e->pbuf : nullptr, V,
+                     rp ? nullptr : e->amax, st, 1, ee ? e->ee : nullptr));
+    if (rp) {
+        k_commit_penalized<<<n, 1024, 0, st>>>(e->seqs, lg0, lg1, e->pbuf, ee ? e->ee : nullptr, n, V, e->loop_out,
+                                               e->slots_dev, e->seen, e->ee_counts);
+        return launch_status("k_commit_penalized");
+    }
     k_commit_ee<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->ee_amax, e->ee_amax + NB, e->amax, e->ee, n, e->loop_out,
                                                  e->ee_counts);
     return launch_status("k_commit_ee");
@@ -1183,7 +1319,7 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&e->htmp, (size_t)RW * D)) || (st = e->wmalloc(&e->htmp2, (size_t)RW * D)) ||
         (st = e->wmalloc(&e->h0tmp, (size_t)RW * D)) || (st = e->wmalloc(&e->stats, (size_t)NB * 3)) ||
         (st = e->wmalloc(&e->ee, (size_t)NB + 2)) || (st = e->wmalloc(&e->ee_amax, (size_t)2 * NB)) ||
-        (st = e->wmalloc(&e->ee_counts, NP)))
+        (st = e->wmalloc(&e->ee_counts, NP)) || (st = e->wmalloc(&e->seen, (size_t)NB * (cfg->vocab_size / 32))))
         return fail(st);
     if ((st = cuda_status(cudaMemset(e->ee_counts, 0, NP * sizeof(unsigned long long)), "zero exit tallies")))
         return fail(st);
@@ -1367,8 +1503,11 @@ extern "C" int pulsar_engine_prefill(pulsar_engine* e, int32_t slot, const int32
     }
     const int rc = e->kv32() ? enqueue_prefill<float>(e, slot, ids, T, logits, st)
                              : enqueue_prefill<__nv_bfloat16>(e, slot, ids, T, logits, st);
-    if (rc == PULSAR_OK) e->len[slot] = T;
-    return rc;
+    if (rc != PULSAR_OK) return rc;
+    e->len[slot] = T;
+    // the slot's seen-token set for the repetition penalty: the prompt
+    k_seen_init<<<1, 1024, 0, st>>>(e->seen + (int64_t)slot * (e->V / 32), ids, T, e->V / 32);
+    return launch_status("k_seen_init");
 }
 
 extern "C" int pulsar_engine_pulse(pulsar_engine* e, int32_t p, int32_t R, const int32_t* rows, const float* h_prev,
@@ -1463,7 +1602,11 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
             return PULSAR_ERR_CAPACITY;
         }
     }
-    const LoopOut lp{out, n_new, (unsigned long long)seed, temperature, top_p, e->ee_thr};
+    if (e->rp_on && (sampled || gamma != 0)) {
+        set_error("generate: the repetition penalty runs in the sequential greedy loop only (gamma = 0)");
+        return PULSAR_ERR_UNSUPPORTED;
+    }
+    const LoopOut lp{out, n_new, (unsigned long long)seed, temperature, top_p, e->ee_thr, e->rp};
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->slots_dev, slots_host, n * 4, cudaMemcpyHostToDevice, st), "copy slots"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->lens_dev, lens.data(), n * 4, cudaMemcpyHostToDevice, st), "copy lens"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->loop_out, &lp, sizeof(lp), cudaMemcpyHostToDevice, st), "copy params"));
@@ -1473,6 +1616,8 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
                                "copy seq ids"));
         k_warp_sample<<<n, SAMPLE_THREADS, (size_t)e->V * 4, st>>>(first_logits, e->V, e->V, e->loop_out,
                                                                    e->seq_ids_dev, nullptr, 0, e->first_dev, nullptr);
+    } else if (e->rp_on) {
+        k_first_penalized<<<n, 1024, 0, st>>>(first_logits, e->V, e->slots_dev, e->seen, e->loop_out, e->first_dev);
     } else {
         k_argmax_rows<<<n, 1024, 0, st>>>(first_logits, e->V, e->V, e->first_dev);
     }
@@ -1482,15 +1627,17 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
     e->n_kernels += 2;
     LoopCtx ctx{n, gamma};
     // output, length and sampling parameters live on the device: graphs depend on (n, gamma, mode)
-    // (gamma = 0 with early exit on: its own body, key suffix ":e")
-    const bool ee = gamma == 0 && e->ee_on;
-    const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + (sampled ? ":s" : ee ? ":e" : ":g");
+    // (gamma = 0 with early exit and / or a repetition penalty: its own body, key suffixes
+    // ":e" / ":r")
+    const bool ee = gamma == 0 && e->ee_on, rp = gamma == 0 && e->rp_on;
+    const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + (sampled ? ":s" : ":g") +
+                            (ee ? ":e" : "") + (rp ? ":r" : "");
     std::vector<SeqDev> hs(n);
     int remaining_steps = n_new - 1;
     while (true) {
         if (gamma == 0) {
             for (int s = 0; s < remaining_steps; ++s)
-                PULSAR_TRY(run_graph(e, key, st, ee ? body_step_ee : body_step, &ctx));
+                PULSAR_TRY(run_graph(e, key, st, (ee || rp) ? body_step_x : body_step, &ctx));
         } else {
             // each round emits between 1 and gamma+1 tokens; launch the minimum, then check
             const int rounds = std::max(1, (remaining_steps + gamma) / (gamma + 1));
@@ -1542,6 +1689,14 @@ extern "C" int pulsar_engine_set_early_exit(pulsar_engine* e, int32_t enabled, f
     return cuda_status(cudaMemset(e->ee_counts, 0, NP * sizeof(unsigned long long)), "zero exit tallies");
 }
 
+extern "C" int pulsar_engine_set_repetition_penalty(pulsar_engine* e, float penalty) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(std::isfinite(penalty) && penalty > 0.f, "set_repetition_penalty: penalty must be finite and > 0");
+    e->rp = penalty;
+    e->rp_on = penalty != 1.f;
+    return PULSAR_OK;
+}
+
 extern "C" int pulsar_engine_early_exit_counts(pulsar_engine* e, int64_t* counts_host) {
     PULSAR_TRY(check_engine(e, false));
     PULSAR_CHECK_ARG(counts_host, "early_exit_counts: null argument");
@@ -1566,6 +1721,37 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
             e->graphs.clear();
         }
         e->use_mega = v;
+        return PULSAR_OK;
+    }
+    if (strcmp(name, "merged_adapter") == 0) {
+        // weights without a live loop adapter have nothing to merge: the option stays off
+        const bool v = value != 0 && e->has_lora;
+        if (v && !e->wqkv_m[0][0]) {
+            PULSAR_CHECK_ARG(e->finalized, "set_option(merged_adapter): finalize the engine first");
+            PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+            const int q = e->cfg.loop_lora_rank;   // rank per pulse (8); LORA_R is 3 x q
+            const float scale = e->cfg.loop_lora_alpha / (float)q;
+            for (int p = 0; p < NP; ++p)
+                for (int l = 0; l < NL; ++l) {
+                    PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->wqkv_m[p][l]), (size_t)QKV * D * 2, &e->arena_bytes));
+                    PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->wo_m[p][l]), (size_t)D * D * 2, &e->arena_bytes));
+                    k_merge_adapter<<<592, 256>>>(e->wqkv[l], e->T_(e->L(l, "attn.wqkv_adapter.lora_A")),
+                                                  e->T_(e->L(l, "attn.wqkv_adapter.lora_B")),
+                                                  e->T_(e->L(l, "attn.wqkv_adapter.loop_M")), e->P, p, scale, QKV, D,
+                                                  q, e->wqkv_m[p][l]);
+                    k_merge_adapter<<<592, 256>>>(e->wo[l], e->T_(e->L(l, "attn.wo_adapter.lora_A")),
+                                                  e->T_(e->L(l, "attn.wo_adapter.lora_B")),
+                                                  e->T_(e->L(l, "attn.wo_adapter.loop_M")), e->P, p, scale, D, D, q,
+                                                  e->wo_m[p][l]);
+                    PULSAR_LAUNCH_CHECK("k_merge_adapter");
+                }
+            PULSAR_TRY(cuda_status(cudaDeviceSynchronize(), "merge adapter"));
+        }
+        if (v != e->merge_adapter) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+            e->graphs.clear();
+        }
+        e->merge_adapter = v;
         return PULSAR_OK;
     }
     if (strcmp(name, "tc_gemm") == 0) {
@@ -1624,6 +1810,7 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     if (strcmp(name, "megakernel_grid") == 0) { *value = e->mega_grid; return PULSAR_OK; }
     if (strcmp(name, "wide") == 0) { *value = e->force_wide ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "tc_gemm") == 0) { *value = e->use_tc ? 1 : 0; return PULSAR_OK; }
+    if (strcmp(name, "merged_adapter") == 0) { *value = e->merge_adapter ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "wide_rows") == 0) { *value = e->wide_rows; return PULSAR_OK; }
     if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "kernel_launches") == 0) { *value = e->n_kernels; return PULSAR_OK; }

@@ -807,6 +807,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             r0 += nr;
         }
         pblk[pnb] = R;
+#pragma unroll 1
         for (int l = 0; l < NL && g.ok; ++l) {
             int r0, r1;
             rows_split(QKV, cta, C, r0, r1);
@@ -1005,6 +1006,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         s->n_blk = nb;
     }
     // xs holds h_in; layer 0's attention norm reads it from xs, later layers from a.h
+    // one copy of the layer body (not unrolled), so it can stay in the instruction caches
+#pragma unroll 1
     for (int l = 0; l < NL; ++l) {
         const bool local = is_local_layer(l);
         // ---------------- phase A: xn, QKV, gate logits

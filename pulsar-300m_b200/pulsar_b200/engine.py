@@ -193,6 +193,11 @@ class DeviceEngine:
         _lib.check(_lib.load().pulsar_engine_set_early_exit(self._h, int(on), float(threshold) if on else 1.0),
                    "set_early_exit")
 
+    def set_repetition_penalty(self, penalty: float) -> None:
+        """pulsar_engine_set_repetition_penalty: penalty of the gamma = 0 greedy loop (1: off)."""
+        _lib.check(_lib.load().pulsar_engine_set_repetition_penalty(self._h, float(penalty)),
+                   "set_repetition_penalty")
+
     def early_exit_counts(self) -> list[int]:
         """Tokens that exited after pulse 1, 2, 3 since the last set_early_exit."""
         c = (C.c_int64 * 3)()
@@ -544,13 +549,15 @@ class PulsarInferenceEngine:
     # ---- new: batched device-resident greedy decoding ----
     @torch.inference_mode()
     def generate_batch(self, input_ids: torch.Tensor, max_new_tokens: int, temperature: float = 0.0,
-                       top_p: float = 1.0, gamma: int = 4, seed: int = 0) -> torch.Tensor:
+                       top_p: float = 1.0, gamma: int = 4, seed: int = 0,
+                       repetition_penalty: float = 1.0) -> torch.Tensor:
         """Decode ``input_ids`` [B, T] and return [B, T + max_new_tokens] (int64).
 
         gamma = 0: exact sequential greedy decoding (the reference's stream_generate with
         temperature 0 and no repetition penalty), with the adaptive early exit of
         ``set_early_exit_threshold`` decided on the device per sequence (exit depths added to
-        ``early_exit_counts``). gamma >= 1: gamma drafts from the
+        ``early_exit_counts``) and the ``repetition_penalty`` of src/infer.py:582-589 applied on
+        the device over each sequence's prompt and emitted tokens. gamma >= 1: gamma drafts from the
         pulse-1 exit and one batched pulse-2/3 verify of the gamma+1 block per round,
         greedy acceptance (temperature <= 1e-4) or sampled acceptance (ratio test with
         residual resampling, Philox streams keyed by (sequence index, round, slot) and
@@ -560,6 +567,8 @@ class PulsarInferenceEngine:
         sampled = temperature > 1e-4
         if sampled and gamma < 1:
             raise ValueError("generate_batch: sampled decoding needs gamma >= 1")
+        if repetition_penalty != 1.0 and (sampled or gamma != 0):
+            raise ValueError("generate_batch: the device repetition penalty needs greedy decoding with gamma = 0")
         ids = torch.as_tensor(input_ids)
         if ids.dim() == 1:
             ids = ids.view(1, -1)
@@ -576,7 +585,11 @@ class PulsarInferenceEngine:
                 ee = gamma == 0 and self.early_exit_threshold is not None
                 if ee:
                     self.dev.set_early_exit(self.early_exit_threshold)   # zero the device tallies
-                toks, stats = self.dev.generate_greedy(slots, first, max_new_tokens, gamma)
+                self.dev.set_repetition_penalty(repetition_penalty)
+                try:
+                    toks, stats = self.dev.generate_greedy(slots, first, max_new_tokens, gamma)
+                finally:
+                    self.dev.set_repetition_penalty(1.0)
                 if ee:
                     for k, c in enumerate(self.dev.early_exit_counts()):
                         self.early_exit_counts[k] += c

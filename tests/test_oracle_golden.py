@@ -88,6 +88,8 @@ def test_oracle_generate_full(name):
     n = min(g["n_new"], 24)
     assert O.stream_generate_ids(m, g["prompt"], n) == g["greedy_ids"][:n]
     assert O.self_speculative_ids(m, g["prompt"], n) == g["spec_ids"][:n]
+    r = g["greedy_rep115_ids"]
+    assert O.stream_generate_ids(m, g["prompt"], len(r), repetition_penalty=1.15) == r
 
 
 @pytest.mark.parametrize("name", ["early_exit_tiny", pytest.param("early_exit_full", marks=pytest.mark.slow),
