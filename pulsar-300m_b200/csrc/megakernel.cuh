@@ -582,6 +582,9 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
                 float v1 = __ldcg(src + H * DH + HKV * DH + g * DH + lane);
                 float v2 = __ldcg(src + H * DH + HKV * DH + g * DH + lane + 32);
                 float* vf = a.vfirst + ((int64_t)rr * HKV + g) * DH;
+                // the first layer's values (value residual) in flight with the rest
+                const float f1 = vres_mode == 2 ? __ldcg(vf + lane) : 0.f;
+                const float f2 = vres_mode == 2 ? __ldcg(vf + lane + 32) : 0.f;
                 const float* kw = a.kn[l] + g * DH;
                 const float w1 = __ldg(kw + lane), w2 = __ldg(kw + lane + 32);
                 const float* rp = s->rope[local ? 0 : 1][rr];   // row rr sits at position key
@@ -591,8 +594,8 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
                     vf[lane + 32] = v2;
                 } else if (vres_mode == 2) {
                     const float lv = a.vres[l];
-                    v1 = (1.f - lv) * v1 + lv * __ldcg(vf + lane);
-                    v2 = (1.f - lv) * v2 + lv * __ldcg(vf + lane + 32);
+                    v1 = (1.f - lv) * v1 + lv * f1;
+                    v2 = (1.f - lv) * v2 + lv * f2;
                 }
                 const float inv = rsqrtf(warp_sum(e1 * e1 + e2 * e2) / (float)DH + a.eps);
                 const float b1 = w1 * (e1 * inv), b2 = w2 * (e2 * inv);
