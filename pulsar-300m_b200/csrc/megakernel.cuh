@@ -645,7 +645,33 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     }
     named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 2, first);
-    // 3) scores with per-row masks [lo_r, pos_r]
+    // 3) scores with per-row masks [lo_r, pos_r]. Several rows: a thread per (key, row) covers
+    //    the row's four heads (float4 query loads shared by the key's element); one row: a
+    //    thread per (key, head)
+    if (nq >= 2 * GQA) {
+        for (int e = tid; e < nr * MEGA_CHUNK; e += MEGA_NCT) {
+            const int rq = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
+            const int key = k0 + kk;
+            const int pos = rows[r0 + rq].y;
+            const int lor = local ? max(0, pos - WINDOW + 1) : 0;
+            const bool vis = kk < nk && key <= pos && key >= lor;
+            float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
+            if (vis) {
+                const float* kv = Ks + kk * (DH + 1);
+#pragma unroll 4
+                for (int d = 0; d < DH; d += 4) {
+                    const float c0 = kv[d], c1 = kv[d + 1], c2 = kv[d + 2], c3 = kv[d + 3];
+#pragma unroll
+                    for (int i = 0; i < GQA; ++i) {
+                        const float4 q = *reinterpret_cast<const float4*>(qs + (rq * GQA + i) * DH + d);
+                        acc[i] += q.x * c0 + q.y * c1 + q.z * c2 + q.w * c3;
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < GQA; ++i) Ps[(rq * GQA + i) * MEGA_CHUNK + kk] = vis ? acc[i] : -INFINITY;
+        }
+    } else
     for (int e = tid; e < nq * MEGA_CHUNK; e += MEGA_NCT) {
         const int qi = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
         const int key = k0 + kk;
@@ -681,7 +707,27 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     }
     named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 4, first);
-    // 5) P.V: one thread per (query, dimension), keys in order
+    // 5) P.V. Several rows: a thread per (dimension, row) covers the row's four heads (float4
+    //    weight loads); one row: a thread per (query, dimension), keys in order
+    if (nq >= 2 * GQA) {
+        for (int e = tid; e < nr * DH; e += MEGA_NCT) {
+            const int rq = e / DH, d = e % DH;
+            float o[GQA] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+            for (int kk = 0; kk < MEGA_CHUNK; kk += 4) {
+                const float v0 = Vs[kk * (DH + 1) + d], v1 = Vs[(kk + 1) * (DH + 1) + d];
+                const float v2 = Vs[(kk + 2) * (DH + 1) + d], v3 = Vs[(kk + 3) * (DH + 1) + d];
+#pragma unroll
+                for (int i = 0; i < GQA; ++i) {
+                    const float4 pw = *reinterpret_cast<const float4*>(Ps + (rq * GQA + i) * MEGA_CHUNK + kk);
+                    o[i] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < GQA; ++i)
+                a.part[(((int64_t)(r0 + rq) * H + g * GQA + i) * a.nch_max + c) * PART + 2 + d] = o[i];
+        }
+    } else
     for (int e = tid; e < nq * DH; e += MEGA_NCT) {
         const int qi = e / DH, d = e % DH;
         const int rr = qi / GQA, h = g * GQA + qi % GQA;
