@@ -298,6 +298,55 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+TP_BATCH, TP_PROMPT, TP_NEW = 256, 512, 256   # BASELINE config 5 (throughput sweep), per GPU
+
+
+def throughput_b256(args, world, rank, local):
+    """BASELINE config 5 on this rank's GPU: 256 sequences of 512-token prompts, 256 new tokens,
+    greedy gamma=4, one generate call over all sequences (the many-row path). Prefill untimed;
+    decode timed with CUDA events, max over ranks; whole-job tokens/s."""
+    from pulsar_b200.config import PulsarConfig
+    from pulsar_b200.engine import DeviceEngine
+    from pulsar_b200.weights import make_state_dict, random_prompts
+    cfg = PulsarConfig(eos_token_id=-1)
+    eng = DeviceEngine(cfg, make_state_dict(cfg, recipe=args.recipe, seed=0), device=local, max_batch=TP_BATCH,
+                       max_seq_len=TP_PROMPT + TP_NEW + 64, max_prefill=TP_PROMPT, kv_dtype=torch.bfloat16)
+    P = random_prompts(TP_BATCH, TP_PROMPT, cfg.vocab_size, seed=1000 + rank)
+    first = torch.stack([eng.prefill(i, P[i].tolist()) for i in range(TP_BATCH)])
+    slots = list(range(TP_BATCH))
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+
+    def run(n):
+        for i in slots:
+            eng.set_length(i, TP_PROMPT)
+        return eng.generate_greedy(slots, first, n, gamma=4)
+
+    run(16)   # graph capture and warm-up
+    torch.cuda.synchronize()
+    if getattr(args, "throughput_profile", False):
+        # one speculative round (5 tokens) between cudaProfilerStart / Stop (ncu captures)
+        torch.cuda.cudart().cudaProfilerStart()
+        run(5)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        eng.close()
+        return {"throughput_profile": TP_BATCH}
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    _, st = run(TP_NEW)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world, local)
+    eng.close()
+    return {"value": job_rate(TP_BATCH * TP_NEW, world, ms_max), "unit": "tokens/s", "ms": ms_max,
+            "accept_rate": st["accepted"] / max(1, st["drafted"]),
+            "config": {"workload": f"BASELINE config 5: {TP_BATCH} sequences per GPU, prompt {TP_PROMPT}, {TP_NEW} new "
+                                   f"tokens, greedy gamma=4, recipe {args.recipe} weights", "batch_per_gpu": TP_BATCH,
+                       "timed": "decode of one generate call (prefill untimed), CUDA events, max over ranks"}}
+
+
 def run_engine(args):
     world, rank, local = dist_setup()
     from pulsar_b200.config import PulsarConfig
@@ -405,12 +454,15 @@ def run_engine(args):
             "clocks": clocks,
             "gpu_launches": gpu_launches,
             "mega_launches": mega_launches}
+    eng.close()
+    if not args.no_throughput:
+        # the metric's B=256 half: every rank runs its replica (same collective steps on all ranks)
+        line["throughput_b256"] = throughput_b256(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, sample = cpu_oracle_rate(args.cpu_tokens, PROMPT)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    eng.close()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -465,6 +517,9 @@ def main():
     ap.add_argument("--recipe", default="A", choices=["A", "B"])
     ap.add_argument("--cpu-tokens", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-throughput", action="store_true", help="skip the B=256 throughput measurement (config 5)")
+    ap.add_argument("--throughput-profile", action="store_true",
+                    help="config 5 only: one decode round between cudaProfilerStart/Stop (ncu captures)")
     ap.add_argument("--kernel-reps", type=int, default=20)
     ap.add_argument("--kernel-shapes", action="store_true",
                     help="launch each round shape of k_mega_pulse once after the prefill and exit (ncu captures)")
@@ -475,6 +530,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.throughput_profile:
+        world, rank, local = dist_setup()
+        torch.cuda.set_device(local)
+        print(json.dumps(throughput_b256(args, world, rank, local)), flush=True)
     elif args.kernel_shapes:
         run_kernel_shapes(args)
     elif args.prefill_profile:

@@ -474,6 +474,9 @@ struct pulsar_engine {
     // wide decode workspace: pulse passes of more than MAX_ROWS rows (GEMM regime), up to
     // wide_rows rows; MoE rows bucketed per expert with capacity = rows (nothing dropped)
     int wide_rows = 0;
+    // rows per block of the split-K decode attention (the verify passes of the speculative loops
+    // set gamma + 1 so a block stages each chunk of K/V once for its rows; 1 otherwise)
+    int attn_rpb = 1;
     bool force_wide = false;   // option "wide": every pulse pass through the wide path
     bool use_tc = true;        // option "tc_gemm": tensor-core GEMMs (prefill, wide path)
     // bf16 hi / lo split of a GEMM's activations (tensor-core path), split_elems each
@@ -642,8 +645,9 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
             e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
             local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
-        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, R), 128, 0, st>>>(rows, w.q, e->kvl[l], local ? 1 : 0, e->nch[l],
-                                                                    w.part, e->max_pos(), e->cfg.max_batch);
+        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, (R + e->attn_rpb - 1) / e->attn_rpb), 128,
+                             attn_decode_smem(e->attn_rpb), st>>>(rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0,
+                                                                  e->nch[l], w.part, e->max_pos(), e->cfg.max_batch);
         k_attn_combine<<<R, H * 32, 0, st>>>(w.part, e->nch[l], w.xn,
                                              e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
@@ -976,8 +980,9 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
             e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
             local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
-        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, R), 128, 0, st>>>(rows, w.q, e->kvl[l], local ? 1 : 0, e->nch[l],
-                                                                    w.part, e->max_pos(), e->cfg.max_batch);
+        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, (R + e->attn_rpb - 1) / e->attn_rpb), 128,
+                             attn_decode_smem(e->attn_rpb), st>>>(rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0,
+                                                                  e->nch[l], w.part, e->max_pos(), e->cfg.max_batch);
         k_attn_combine<<<R, H * 32, 0, st>>>(w.part, e->nch[l], w.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
@@ -1166,8 +1171,11 @@ int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
         PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->hblk + (int64_t)j * D, e->h0blk + (int64_t)j * D,
                          nullptr, 0, j < g ? e->amax : nullptr, st, g + 1));
     }
-    PULSAR_TRY(pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st));
-    PULSAR_TRY(pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, nullptr, 0, e->amax, st));
+    e->attn_rpb = g + 1;   // verify blocks: one K/V staging per block in the split-K attention
+    const int v1 = pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st);
+    const int v2 = v1 ? v1 : pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, nullptr, 0, e->amax, st);
+    e->attn_rpb = 1;
+    PULSAR_TRY(v2);
     k_accept_greedy<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->toks, e->amax, n, g, e->loop_out, e->stats, e->slots_dev, e->rows);
     return launch_status("k_accept_greedy");
 }
@@ -1193,8 +1201,11 @@ int body_round_sampled(pulsar_engine* e, cudaStream_t st, void* vctx) {
             PULSAR_LAUNCH_CHECK("k_warp_sample");
         }
     }
-    PULSAR_TRY(pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st));
-    PULSAR_TRY(pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, e->pbuf, V, nullptr, st));
+    e->attn_rpb = g + 1;   // verify blocks: one K/V staging per block in the split-K attention
+    const int v1 = pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st);
+    const int v2 = v1 ? v1 : pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, e->pbuf, V, nullptr, st);
+    e->attn_rpb = 1;
+    PULSAR_TRY(v2);
     k_warp_sample<<<rows_v, SAMPLE_THREADS, smem, st>>>(e->pbuf, V, V, e->loop_out, e->seq_ids_dev, nullptr, 0, nullptr,
                                                         e->pstats);
     PULSAR_LAUNCH_CHECK("k_warp_sample");
@@ -1236,7 +1247,9 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         off += (int64_t)2 * HKV * cap * DH;
         e->kvl[l].cap = cap;
         e->kvl[l].mask = (is_local_layer(l) && cap == LOCAL_RING) ? (LOCAL_RING - 1) : -1;
-        e->nch[l] = is_local_layer(l) ? (WINDOW / ATT_CHUNK) : (maxlen + ATT_CHUNK - 1) / ATT_CHUNK;
+        // local layers: one chunk more than the window, because a run of verify rows spans up to
+        // WINDOW + rows - 1 keys from its first row's window start
+        e->nch[l] = is_local_layer(l) ? (WINDOW / ATT_CHUNK + 1) : (maxlen + ATT_CHUNK - 1) / ATT_CHUNK;
     }
     const int64_t slot_elems = off;
     int st = e->dmalloc(&e->kv, (size_t)slot_elems * cfg->max_batch * esz, &e->kv_bytes);
@@ -1331,7 +1344,14 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         if ((st = mega_occupancy(cfg->kv_fp32 != 0, &per_sm))) return fail(st);
         if ((st = cuda_status(cudaFuncSetAttribute(k_warp_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    SAMPLE_MAX_V * (int)sizeof(float)),
-                              "k_warp_sample shared memory")))
+                              "k_warp_sample shared memory")) ||
+            (st = cuda_status(cudaFuncSetAttribute(k_attn_decode<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)attn_decode_smem(ATT_RPB_MAX)),
+                              "k_attn_decode shared memory")) ||
+            (st = cuda_status(cudaFuncSetAttribute(k_attn_decode<__nv_bfloat16>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)attn_decode_smem(ATT_RPB_MAX)),
+                              "k_attn_decode shared memory")))
             return fail(st);
         // the per-CTA staging sizes assume >= 144 CTAs (ceil(8192 / C) + ceil(1024 / C) <= 64 pairs)
         e->mega_grid = sms;

@@ -283,69 +283,154 @@ __global__ void __launch_bounds__((H + HKV) * 32) k_qkv_post(
     }
 }
 
-// Split-K decode attention: block (chunk, kv head g, row r), 128 threads. Keys of row r
-// are positions [lo, pos] (lo = pos - WINDOW + 1 on local layers). Writes per q head
-// (m, l, o[64]) of its chunk.
+// Split-K decode attention: block (chunk c, kv head g, group of rpb rows), 128 threads. A group
+// is cut into runs of consecutive rows of one slot at consecutive positions (a verify block);
+// each run stages its chunk of cached K/V - keys lo_first + [c * 128, c * 128 + 128), lo_first
+// the run's first row's window start - once in shared memory with 16-byte loads, and every row
+// of the run scores it under its own mask [lo_r, pos_r] (lo_r = pos_r - WINDOW + 1 on local
+// layers). Writes per q head (m, l, o[64]) of its chunk; a chunk with no visible key writes
+// m = -inf. Rows with an invalid slot or position read nothing. Dynamic shared memory:
+// attn_decode_smem(rpb) bytes.
+constexpr int ATT_RPB_MAX = 8;
+constexpr int ATT_KST = DH + 1;   // shared row stride of the staged K / V (conflict-free columns)
+__host__ __device__ constexpr size_t attn_decode_smem(int rpb) {
+    return (size_t)(2 * ATT_CHUNK * ATT_KST + rpb * GQA * DH + rpb * GQA * ATT_CHUNK) * sizeof(float);
+}
+
 template <typename KVT>
-__global__ void __launch_bounds__(128) k_attn_decode(const int4* __restrict__ rows, const float* __restrict__ q,
-                                                     KVLayer L, int is_local, int nchunk, float* __restrict__ part,
-                                                     int max_pos, int n_slots) {
-    __shared__ float qs[GQA][DH];
-    __shared__ float ps[GQA][ATT_CHUNK];
-    const int c = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
-    const int4 row = rows[r];
-    const bool bad = row.y < 0 || row.y >= max_pos || row.x < 0 || row.x >= n_slots;
-    const int pos = bad ? -1 : row.y;   // a rejected row reads nothing (every chunk empty)
-    const int lo = is_local ? max(0, pos - WINDOW + 1) : 0;
-    const int k0 = bad ? 0 : lo + c * ATT_CHUNK;
-    const int k1 = min(k0 + ATT_CHUNK, pos + 1);
+__global__ void __launch_bounds__(128) k_attn_decode(const int4* __restrict__ rows, int R, int rpb,
+                                                     const float* __restrict__ q, KVLayer L, int is_local, int nchunk,
+                                                     float* __restrict__ part, int max_pos, int n_slots) {
+    extern __shared__ float sm_att[];
+    float* Ks = sm_att;                        // [128][65]
+    float* Vs = Ks + ATT_CHUNK * ATT_KST;      // [128][65]
+    float* qs = Vs + ATT_CHUNK * ATT_KST;      // [rows][4][64]
+    float* ps = qs + rpb * GQA * DH;           // [rows][4][128]
+    const int c = blockIdx.x, g = blockIdx.y;
+    const int rb0 = blockIdx.z * rpb, rb1 = min(R, rb0 + rpb);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    float* out = part + (((int64_t)r * H + g * GQA + warp) * nchunk + c) * PART;
-    if (k0 > pos) {                      // empty chunk
-        if (lane == 0) { out[0] = -INFINITY; out[1] = 0.f; }
-        return;
-    }
-    for (int i = tid; i < GQA * DH; i += 128) qs[i / DH][i % DH] = q[((int64_t)r * H + g * GQA) * DH + i];
-    __syncthreads();
-    const int key = k0 + tid;
-    if (key < k1) {
-        const KVT* kp = kv_k<KVT>(L, row.x, g, key);
-        float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-        for (int d = 0; d < DH; ++d) {
-            const float kv = kv_load(kp + d);
-#pragma unroll
-            for (int h = 0; h < GQA; ++h) acc[h] += qs[h][d] * kv;
+    auto bad_row = [&](const int4& rw) { return rw.y < 0 || rw.y >= max_pos || rw.x < 0 || rw.x >= n_slots; };
+    for (int s0 = rb0; s0 < rb1;) {
+        const int4 first = rows[s0];
+        int s1 = s0 + 1;
+        if (!bad_row(first))
+            while (s1 < rb1 && s1 - s0 < ATT_RPB_MAX) {
+                const int4 nx = rows[s1];
+                if (bad_row(nx) || nx.x != first.x || nx.y != rows[s1 - 1].y + 1) break;
+                ++s1;
+            }
+        const int nr = s1 - s0;
+        const int posF = first.y, posL = posF + nr - 1;
+        const int lo0 = is_local ? max(0, posF - WINDOW + 1) : 0;
+        const int k0 = lo0 + c * ATT_CHUNK;
+        const int k1 = bad_row(first) ? k0 : min(k0 + ATT_CHUNK, posL + 1);
+        const int nk = max(0, k1 - k0);
+        if (nk == 0) {   // no key of this chunk is visible to the run's rows
+            if (tid < nr * GQA) part[(((int64_t)(s0 + tid / GQA) * H + g * GQA + tid % GQA) * nchunk + c) * PART] = -INFINITY;
+            if (tid < nr * GQA) part[(((int64_t)(s0 + tid / GQA) * H + g * GQA + tid % GQA) * nchunk + c) * PART + 1] = 0.f;
+            s0 = s1;
+            continue;
         }
+        // stage K and V rows [k0, k1) (fp32, stride 65) and the run's queries
+        constexpr int EPP = 16 / (int)sizeof(KVT);   // elements per 16-byte piece
+        constexpr int PIECES = DH / EPP;
+        for (int e = tid; e < 2 * nk * PIECES; e += 128) {
+            const int isv = e >= nk * PIECES;
+            const int ee = isv ? e - nk * PIECES : e;
+            const int kk = ee / PIECES, pc = ee % PIECES;
+            const KVT* src = (isv ? kv_v<KVT>(L, first.x, g, k0 + kk) : kv_k<KVT>(L, first.x, g, k0 + kk)) + pc * EPP;
+            float* dst = (isv ? Vs : Ks) + kk * ATT_KST + pc * EPP;
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+            if constexpr (sizeof(KVT) == 2) {
+                const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int h = 0; h < GQA; ++h) ps[h][tid] = acc[h] * 0.125f;
-    } else {
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = __bfloat1622float2(b[i]);
+                    dst[2 * i] = f.x;
+                    dst[2 * i + 1] = f.y;
+                }
+            } else {
+                dst[0] = __uint_as_float(u.x);
+                dst[1] = __uint_as_float(u.y);
+                dst[2] = __uint_as_float(u.z);
+                dst[3] = __uint_as_float(u.w);
+            }
+        }
+        for (int i = tid; i < nr * GQA * DH; i += 128) {
+            const int rr = i / (GQA * DH), rem = i % (GQA * DH);
+            qs[i] = q[((int64_t)(s0 + rr) * H + g * GQA) * DH + rem];
+        }
+        __syncthreads();
+        // scores: a thread per key, every row and head of the run
+        {
+            const int kk = tid, key = k0 + kk;
+            for (int rr = 0; rr < nr; ++rr) {
+                const int pos = posF + rr;
+                const int lor = is_local ? max(0, pos - WINDOW + 1) : 0;
+                const bool vis = kk < nk && key <= pos && key >= lor;
+                float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
+                if (vis) {
+                    const float* kr = Ks + kk * ATT_KST;
+#pragma unroll 4
+                    for (int d = 0; d < DH; d += 4) {
+                        const float c0 = kr[d], c1 = kr[d + 1], c2 = kr[d + 2], c3 = kr[d + 3];
 #pragma unroll
-        for (int h = 0; h < GQA; ++h) ps[h][tid] = -INFINITY;
+                        for (int h = 0; h < GQA; ++h) {
+                            const float4 qv = *reinterpret_cast<const float4*>(qs + (rr * GQA + h) * DH + d);
+                            acc[h] += qv.x * c0 + qv.y * c1 + qv.z * c2 + qv.w * c3;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < GQA; ++h) ps[(rr * GQA + h) * ATT_CHUNK + kk] = vis ? acc[h] * 0.125f : -INFINITY;
+            }
+        }
+        __syncthreads();
+        // softmax per (row, head): a warp per unit; weights back into ps
+        for (int u = warp; u < nr * GQA; u += 4) {
+            float* pu = ps + u * ATT_CHUNK;
+            float m = -INFINITY;
+            for (int i = lane; i < ATT_CHUNK; i += 32) m = fmaxf(m, pu[i]);
+            m = warp_max(m);
+            float l = 0.f;
+            for (int i = lane; i < ATT_CHUNK; i += 32) {
+                const float pv = (pu[i] == -INFINITY) ? 0.f : expf(pu[i] - m);
+                pu[i] = pv;
+                l += pv;
+            }
+            l = warp_sum(l);
+            float* out = part + (((int64_t)(s0 + u / GQA) * H + g * GQA + u % GQA) * nchunk + c) * PART;
+            if (lane == 0) {
+                out[0] = m;
+                out[1] = m == -INFINITY ? 0.f : l;
+            }
+        }
+        __syncthreads();
+        // P.V: thread (dimension d, head pair hp) over every row of the run, keys in order
+        {
+            const int d = tid & (DH - 1), hp = tid >> 6;
+            float o[ATT_RPB_MAX][2];
+#pragma unroll
+            for (int rr = 0; rr < ATT_RPB_MAX; ++rr) o[rr][0] = o[rr][1] = 0.f;
+            for (int kk = 0; kk < nk; ++kk) {
+                const float v = Vs[kk * ATT_KST + d];
+#pragma unroll
+                for (int rr = 0; rr < ATT_RPB_MAX; ++rr)
+                    if (rr < nr) {
+                        o[rr][0] += ps[(rr * GQA + 2 * hp) * ATT_CHUNK + kk] * v;
+                        o[rr][1] += ps[(rr * GQA + 2 * hp + 1) * ATT_CHUNK + kk] * v;
+                    }
+            }
+#pragma unroll
+            for (int rr = 0; rr < ATT_RPB_MAX; ++rr)
+                if (rr < nr)
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        part[(((int64_t)(s0 + rr) * H + g * GQA + 2 * hp + j) * nchunk + c) * PART + 2 + d] = o[rr][j];
+        }
+        __syncthreads();   // shared memory is reused by the next run
+        s0 = s1;
     }
-    __syncthreads();
-    // warp `warp` owns q head g*GQA + warp
-    float m = -INFINITY;
-    for (int i = lane; i < ATT_CHUNK; i += 32) m = fmaxf(m, ps[warp][i]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int i = lane; i < ATT_CHUNK; i += 32) {
-        const float p = (ps[warp][i] == -INFINITY) ? 0.f : expf(ps[warp][i] - m);
-        ps[warp][i] = p;
-        l += p;
-    }
-    l = warp_sum(l);
-    __syncwarp();
-    float o1 = 0.f, o2 = 0.f;
-    for (int key2 = k0; key2 < k1; ++key2) {
-        const float p = ps[warp][key2 - k0];
-        const KVT* vp = kv_v<KVT>(L, row.x, g, key2);
-        o1 += p * kv_load(vp + lane);
-        o2 += p * kv_load(vp + lane + 32);
-    }
-    if (lane == 0) { out[0] = m; out[1] = l; }
-    out[2 + lane] = o1;
-    out[2 + lane + 32] = o2;
 }
 
 // Combine the chunks of each head, apply the head gate sigmoid(xn . Wg[h] + bg[h])
