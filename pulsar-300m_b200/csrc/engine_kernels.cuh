@@ -331,29 +331,47 @@ __global__ void __launch_bounds__(128) k_attn_decode(const int4* __restrict__ ro
             s0 = s1;
             continue;
         }
-        // stage K and V rows [k0, k1) (fp32, stride 65) and the run's queries
+        // stage K and V rows [k0, k1) (fp32, stride 65) and the run's queries: eight 16-byte
+        // loads per thread in flight before any is converted and stored
         constexpr int EPP = 16 / (int)sizeof(KVT);   // elements per 16-byte piece
         constexpr int PIECES = DH / EPP;
-        for (int e = tid; e < 2 * nk * PIECES; e += 128) {
-            const int isv = e >= nk * PIECES;
-            const int ee = isv ? e - nk * PIECES : e;
-            const int kk = ee / PIECES, pc = ee % PIECES;
-            const KVT* src = (isv ? kv_v<KVT>(L, first.x, g, k0 + kk) : kv_k<KVT>(L, first.x, g, k0 + kk)) + pc * EPP;
-            float* dst = (isv ? Vs : Ks) + kk * ATT_KST + pc * EPP;
-            const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
-            if constexpr (sizeof(KVT) == 2) {
-                const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const int npc = 2 * nk * PIECES;
+        for (int b0 = 0; b0 < npc; b0 += 8 * 128) {
+            uint4 u[8];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 f = __bfloat1622float2(b[i]);
-                    dst[2 * i] = f.x;
-                    dst[2 * i + 1] = f.y;
+            for (int j = 0; j < 8; ++j) {
+                const int e = b0 + j * 128 + tid;
+                if (e < npc) {
+                    const int isv = e >= nk * PIECES;
+                    const int ee = isv ? e - nk * PIECES : e;
+                    const int kk = ee / PIECES, pc = ee % PIECES;
+                    const KVT* src = (isv ? kv_v<KVT>(L, first.x, g, k0 + kk) : kv_k<KVT>(L, first.x, g, k0 + kk)) + pc * EPP;
+                    u[j] = __ldg(reinterpret_cast<const uint4*>(src));
                 }
-            } else {
-                dst[0] = __uint_as_float(u.x);
-                dst[1] = __uint_as_float(u.y);
-                dst[2] = __uint_as_float(u.z);
-                dst[3] = __uint_as_float(u.w);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int e = b0 + j * 128 + tid;
+                if (e < npc) {
+                    const int isv = e >= nk * PIECES;
+                    const int ee = isv ? e - nk * PIECES : e;
+                    const int kk = ee / PIECES, pc = ee % PIECES;
+                    float* dst = (isv ? Vs : Ks) + kk * ATT_KST + pc * EPP;
+                    if constexpr (sizeof(KVT) == 2) {
+                        const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float2 f = __bfloat1622float2(bp[i]);
+                            dst[2 * i] = f.x;
+                            dst[2 * i + 1] = f.y;
+                        }
+                    } else {
+                        dst[0] = __uint_as_float(u[j].x);
+                        dst[1] = __uint_as_float(u[j].y);
+                        dst[2] = __uint_as_float(u[j].z);
+                        dst[3] = __uint_as_float(u[j].w);
+                    }
+                }
             }
         }
         for (int i = tid; i < nr * GQA * DH; i += 128) {
