@@ -182,10 +182,13 @@ def run_early_exit(name, cfg_dict, recipe, seed, prompt_seed, prompt_len, n_new,
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("PULSAR_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("PULSAR_REFERENCE"),
+                    help="path of the reference source tree (or set PULSAR_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or PULSAR_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     torch.set_num_threads(os.cpu_count() or 1)
     full = dict(eos_token_id=-1)
