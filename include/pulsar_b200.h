@@ -218,6 +218,21 @@ int pulsar_engine_generate_sampled(pulsar_engine* eng, int32_t n_seq, const int3
  * between generate calls, not while one runs on another stream. */
 int pulsar_engine_set_early_exit(pulsar_engine* eng, int32_t enabled, float threshold);
 
+/* Repacked weight arena (the checkpoint repack of the engine's load path; the reference
+ * reloads and re-merges its .pt checkpoint, src/infer.py:785-817). After finalize the bf16
+ * arena - tok_emb (also the LM head), per layer wqkv, wo, shared gate_up / down, routed
+ * gate_up / down in the engine's transposed layouts - can be read tensor by tensor; a new
+ * engine takes them back with pulsar_engine_arena_write before finalize, in place of the fp32
+ * tok_emb / lm_head / wqkv / wo / shared / routed state_dict tensors (the other, small fp32
+ * tensors are still uploaded with pulsar_engine_set_tensor). Names: "arena.tok_emb",
+ * "arena.<layer>.{wqkv,wo,shared_gate_up,shared_down,routed_gate_up_t,routed_down_t}".
+ * arena_info's name pointer stays valid for the engine's lifetime. host buffers hold bf16
+ * bit patterns (2 bytes per element). */
+int pulsar_engine_arena_count(pulsar_engine* eng, int32_t* count);
+int pulsar_engine_arena_info(pulsar_engine* eng, int32_t index, const char** name, int64_t* numel);
+int pulsar_engine_arena_read(pulsar_engine* eng, const char* name, void* host_dst, int64_t numel);
+int pulsar_engine_arena_write(pulsar_engine* eng, const char* name, const void* host_src, int64_t numel);
+
 /* Repetition penalty of the sequential greedy loop (src/infer.py:582-589, the reference's
  * default 1.15 in stream_generate / generate): when choosing each token of
  * pulsar_engine_generate_greedy with gamma == 0, logits of ids already seen are divided by

@@ -452,6 +452,11 @@ struct pulsar_engine {
     // bf16 arena
     __nv_bfloat16* emb = nullptr;
     __nv_bfloat16 *wqkv[NL] = {}, *wo[NL] = {}, *sh_gu[NL] = {}, *sh_dn[NL] = {}, *r_gu[NL] = {}, *r_dn[NL] = {};
+    // repacked bf16 arena tensors written before finalize (pulsar_engine_arena_write): the fp32
+    // state_dict tensors they stand for need not be uploaded
+    std::vector<std::string> arena_names;
+    std::map<std::string, std::vector<std::string>> arena_covers;
+    std::map<std::string, bool> arena_written;
     // option "merged_adapter": per-pulse bf16 merged wqkv / wo (the reference's GPU numerics);
     // every pass then runs without the fp32 adapter correction (and on the persistent kernel)
     bool merge_adapter = false;
@@ -566,6 +571,53 @@ namespace {
 const __nv_bfloat16* w_qkv(const pulsar_engine* e, int p, int l) { return e->merge_adapter ? e->wqkv_m[p][l] : e->wqkv[l]; }
 const __nv_bfloat16* w_o(const pulsar_engine* e, int p, int l) { return e->merge_adapter ? e->wo_m[p][l] : e->wo[l]; }
 bool lora_live(const pulsar_engine* e) { return e->has_lora && !e->merge_adapter; }
+
+// The engine's bf16 weight arena, tensor by tensor: name, slot, elements, and the fp32 state_dict
+// tensors it is built from. Layouts are the engine's: wqkv [1536][1024], wo [1024][1024],
+// shared gate_up [2048][1024] and down [1024][1024], routed gate_up transposed to
+// [16][1024 out][1024 in] and down to [16][1024 out][512 in], tok_emb [V][1024] (also the LM head).
+struct ArenaRef {
+    __nv_bfloat16** ptr;
+    int64_t numel;
+};
+ArenaRef arena_ref(pulsar_engine* e, const std::string& name) {
+    if (name == "arena.tok_emb") return {&e->emb, (int64_t)e->V * D};
+    for (int l = 0; l < NL; ++l) {
+        const std::string p = "arena." + std::to_string(l) + ".";
+        if (name == p + "wqkv") return {&e->wqkv[l], (int64_t)QKV * D};
+        if (name == p + "wo") return {&e->wo[l], (int64_t)D * D};
+        if (name == p + "shared_gate_up") return {&e->sh_gu[l], (int64_t)2 * DS * D};
+        if (name == p + "shared_down") return {&e->sh_dn[l], (int64_t)D * DS};
+        if (name == p + "routed_gate_up_t") return {&e->r_gu[l], (int64_t)E * 2 * DE * D};
+        if (name == p + "routed_down_t") return {&e->r_dn[l], (int64_t)E * D * DE};
+    }
+    return {nullptr, 0};
+}
+
+void build_arena_names(pulsar_engine* e) {
+    e->arena_names.push_back("arena.tok_emb");
+    e->arena_covers["arena.tok_emb"] = {"tok_emb.weight", "lm_head.weight"};
+    const char* parts[][2] = {{"wqkv", "attn.wqkv.weight"},
+                              {"wo", "attn.wo.weight"},
+                              {"shared_gate_up", "mlp.shared_expert.w_gate_up.weight"},
+                              {"shared_down", "mlp.shared_expert.w_down.weight"},
+                              {"routed_gate_up_t", "mlp.routed_gate_up"},
+                              {"routed_down_t", "mlp.routed_down"}};
+    for (int l = 0; l < NL; ++l)
+        for (auto& pc : parts) {
+            const std::string n = "arena." + std::to_string(l) + "." + pc[0];
+            e->arena_names.push_back(n);
+            e->arena_covers[n] = {e->L(l, pc[1])};
+        }
+}
+
+bool arena_covered(const pulsar_engine* e, const std::string& tensor) {
+    for (auto& kv : e->arena_written)
+        if (kv.second)
+            for (auto& c : e->arena_covers.at(kv.first))
+                if (c == tensor) return true;
+    return false;
+}
 
 void build_expect(pulsar_engine* e) {
     const int P = e->P, V = e->V, q = 8;
@@ -1231,6 +1283,7 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
     e->V = cfg->vocab_size;
     e->P = cfg->max_pulses;
     build_expect(e);
+    build_arena_names(e);
     auto fail = [&](int st) {
         pulsar_engine_destroy(e);
         return st;
@@ -1420,13 +1473,14 @@ extern "C" int pulsar_engine_finalize(pulsar_engine* e) {
             kv.first.find("expert_pulse_counts") != std::string::npos)
             continue;
         if (!e->cfg.loop_lora_rank && (kv.first.find("_adapter.") != std::string::npos)) continue;
-        if (!e->T_(kv.first)) {
+        if (!e->T_(kv.first) && !arena_covered(e, kv.first)) {
             set_error("finalize: tensor '%s' was never uploaded", kv.first.c_str());
             return PULSAR_ERR_STATE;
         }
     }
     cudaStream_t st = 0;
     auto conv = [&](const std::string& n, __nv_bfloat16** dst, int64_t numel) -> int {
+        if (*dst) return PULSAR_OK;   // written from a repacked arena
         PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(dst), (size_t)numel * 2, &e->arena_bytes));
         k_f32_to_bf16<<<1024, 256, 0, st>>>(e->T_(n), *dst, numel);
         return launch_status("k_f32_to_bf16");
@@ -1437,14 +1491,18 @@ extern "C" int pulsar_engine_finalize(pulsar_engine* e) {
         PULSAR_TRY(conv(e->L(l, "attn.wo.weight"), &e->wo[l], (int64_t)D * D));
         PULSAR_TRY(conv(e->L(l, "mlp.shared_expert.w_gate_up.weight"), &e->sh_gu[l], (int64_t)2 * DS * D));
         PULSAR_TRY(conv(e->L(l, "mlp.shared_expert.w_down.weight"), &e->sh_dn[l], (int64_t)D * DS));
-        PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->r_gu[l]), (size_t)E * D * 2 * DE * 2, &e->arena_bytes));
-        PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->r_dn[l]), (size_t)E * DE * D * 2, &e->arena_bytes));
-        // routed_gate_up [E][D in][2*DE out] -> [E][2*DE out][D in]
-        k_transpose_bf16<<<dim3(2 * DE / 32, D / 32, E), dim3(32, 8), 0, st>>>(e->T_(e->L(l, "mlp.routed_gate_up")),
-                                                                                e->r_gu[l], D, 2 * DE);
-        // routed_down [E][DE in][D out] -> [E][D out][DE in]
-        k_transpose_bf16<<<dim3(D / 32, DE / 32, E), dim3(32, 8), 0, st>>>(e->T_(e->L(l, "mlp.routed_down")),
-                                                                            e->r_dn[l], DE, D);
+        if (!e->r_gu[l]) {
+            PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->r_gu[l]), (size_t)E * D * 2 * DE * 2, &e->arena_bytes));
+            // routed_gate_up [E][D in][2*DE out] -> [E][2*DE out][D in]
+            k_transpose_bf16<<<dim3(2 * DE / 32, D / 32, E), dim3(32, 8), 0, st>>>(
+                e->T_(e->L(l, "mlp.routed_gate_up")), e->r_gu[l], D, 2 * DE);
+        }
+        if (!e->r_dn[l]) {
+            PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(&e->r_dn[l]), (size_t)E * DE * D * 2, &e->arena_bytes));
+            // routed_down [E][DE in][D out] -> [E][D out][DE in]
+            k_transpose_bf16<<<dim3(D / 32, DE / 32, E), dim3(32, 8), 0, st>>>(e->T_(e->L(l, "mlp.routed_down")),
+                                                                                e->r_dn[l], DE, D);
+        }
         PULSAR_LAUNCH_CHECK("expert transpose");
         std::vector<float> lam(e->P);
         PULSAR_TRY(cuda_status(cudaMemcpy(lam.data(), e->T_(e->L(l, "attn.v_resid_lambda")), e->P * 4,
@@ -1488,6 +1546,51 @@ extern "C" int pulsar_engine_finalize(pulsar_engine* e) {
     }
     e->finalized = true;
     clear_error();
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_arena_count(pulsar_engine* e, int32_t* count) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(count, "arena_count: null argument");
+    *count = (int32_t)e->arena_names.size();
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_arena_info(pulsar_engine* e, int32_t index, const char** name, int64_t* numel) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(name && numel, "arena_info: null argument");
+    PULSAR_CHECK_ARG(index >= 0 && index < (int32_t)e->arena_names.size(), "arena_info: index %d out of range", index);
+    *name = e->arena_names[index].c_str();
+    *numel = arena_ref(e, e->arena_names[index]).numel;
+    return PULSAR_OK;
+}
+
+extern "C" int pulsar_engine_arena_read(pulsar_engine* e, const char* name, void* host_dst, int64_t numel) {
+    PULSAR_TRY(check_engine(e, true));
+    PULSAR_CHECK_ARG(name && host_dst, "arena_read: null argument");
+    const ArenaRef r = arena_ref(e, name);
+    PULSAR_CHECK_ARG(r.ptr, "arena_read: unknown arena tensor '%s'", name);
+    PULSAR_CHECK_ARG(numel == r.numel, "arena_read: '%s' has %lld elements, asked for %lld", name, (long long)r.numel,
+                     (long long)numel);
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    return cuda_status(cudaMemcpy(host_dst, *r.ptr, (size_t)numel * 2, cudaMemcpyDeviceToHost), "arena_read copy");
+}
+
+extern "C" int pulsar_engine_arena_write(pulsar_engine* e, const char* name, const void* host_src, int64_t numel) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(name && host_src, "arena_write: null argument");
+    if (e->finalized) {
+        set_error("arena_write after finalize is not supported ('%s')", name);
+        return PULSAR_ERR_STATE;
+    }
+    const ArenaRef r = arena_ref(e, name);
+    PULSAR_CHECK_ARG(r.ptr, "arena_write: unknown arena tensor '%s'", name);
+    PULSAR_CHECK_ARG(numel == r.numel, "arena_write: '%s' has %lld elements, got %lld", name, (long long)r.numel,
+                     (long long)numel);
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    if (!*r.ptr) PULSAR_TRY(e->dmalloc(reinterpret_cast<void**>(r.ptr), (size_t)numel * 2, &e->arena_bytes));
+    PULSAR_TRY(cuda_status(cudaMemcpy(*r.ptr, host_src, (size_t)numel * 2, cudaMemcpyHostToDevice), "arena_write copy"));
+    e->arena_written[name] = true;
     return PULSAR_OK;
 }
 

@@ -67,6 +67,10 @@ PROTOTYPES = {
     "pulsar_engine_set_early_exit": (c_int, [c_void_p, c_int, C.c_float]),
     "pulsar_engine_early_exit_counts": (c_int, [c_void_p, C.POINTER(c_int64)]),
     "pulsar_engine_set_repetition_penalty": (c_int, [c_void_p, C.c_float]),
+    "pulsar_engine_arena_count": (c_int, [c_void_p, C.POINTER(C.c_int32)]),
+    "pulsar_engine_arena_info": (c_int, [c_void_p, c_int, C.POINTER(c_char_p), C.POINTER(c_int64)]),
+    "pulsar_engine_arena_read": (c_int, [c_void_p, c_char_p, c_void_p, c_int64]),
+    "pulsar_engine_arena_write": (c_int, [c_void_p, c_char_p, c_void_p, c_int64]),
     "pulsar_engine_set_option": (c_int, [c_void_p, c_char_p, c_int64]),
     "pulsar_engine_get_option": (c_int, [c_void_p, c_char_p, C.POINTER(c_int64)]),
     "pulsar_engine_read_trace": (c_int, [c_void_p, c_void_p, c_int64]),

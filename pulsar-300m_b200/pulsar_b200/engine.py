@@ -18,6 +18,7 @@ from __future__ import annotations
 import ctypes as C
 import math
 import os
+import re
 import sys
 from typing import Generator, Optional
 
@@ -36,11 +37,25 @@ def _rope_inv_freq(theta: float, dim: int) -> torch.Tensor:
     return 1.0 / (theta ** (torch.arange(0, dim, 2).float() / dim))
 
 
+# fp32 state_dict tensors that the bf16 weight arena replaces (pulsar_engine_arena_write)
+_ARENA_SOURCE = re.compile(r"^(tok_emb\.weight|lm_head\.weight|core\.\d+\.(attn\.wqkv\.weight|attn\.wo\.weight|"
+                           r"mlp\.shared_expert\.w_gate_up\.weight|mlp\.shared_expert\.w_down\.weight|"
+                           r"mlp\.routed_gate_up|mlp\.routed_down))$")
+
+
 class DeviceEngine:
     """Owner of one ``pulsar_engine`` handle (weights, KV slots, workspaces) on one GPU."""
 
     def __init__(self, cfg: PulsarConfig, state_dict, device: int | str | torch.device = 0, max_batch: int = 1,
                  max_seq_len: int = 4096, max_prefill: Optional[int] = None, kv_dtype: torch.dtype = torch.bfloat16):
+        self._create(cfg, device, max_batch, max_seq_len, max_prefill, kv_dtype)
+        try:
+            self._upload(state_dict)
+        except Exception:
+            self.close()
+            raise
+
+    def _create(self, cfg, device, max_batch, max_seq_len, max_prefill, kv_dtype):
         why = engine_supported(cfg)
         if why is not None:
             raise RuntimeError(f"pulsar_b200 engine does not support this config: {why}")
@@ -66,11 +81,7 @@ class DeviceEngine:
         _lib.check(lib.pulsar_engine_create(C.byref(ec), C.byref(h)), "pulsar_engine_create")
         self._h = h
         self._free_slots = list(range(max_batch))
-        try:
-            self._upload(state_dict)
-        except Exception:
-            self.close()
-            raise
+        self._small = {}   # the fp32 tensors outside the bf16 arena (kept for save_repacked)
 
     def _upload(self, sd):
         lib = _lib.load()
@@ -84,11 +95,91 @@ class DeviceEngine:
             a = t.detach().to("cpu", torch.float32).contiguous()
             _lib.check(lib.pulsar_engine_set_tensor(self._h, name.encode(), a.data_ptr(), a.numel()),
                        f"set_tensor({name})")
+            if not _ARENA_SOURCE.search(name):
+                self._small[name] = a
+        self._finalize()
+
+    def _finalize(self):
+        lib = _lib.load()
         for key, theta in (("rope_local.inv_freq", self.cfg.rope_theta_local),
                            ("rope_global.inv_freq", self.cfg.rope_theta_global)):
             a = _rope_inv_freq(theta, self.cfg.head_dim).contiguous()
             _lib.check(lib.pulsar_engine_set_tensor(self._h, key.encode(), a.data_ptr(), a.numel()), key)
         _lib.check(lib.pulsar_engine_finalize(self._h), "pulsar_engine_finalize")
+
+    # ---- checkpoint repack: safetensors-format file of the bf16 arena + the small fp32 tensors ----
+    def save_repacked(self, path: str) -> None:
+        """Write the engine's weights as a safetensors-format file: the bf16 arena tensors in
+        the engine's layouts (BF16, 1-D) and the remaining fp32 state_dict tensors (F32, their
+        shapes), the config in the header's __metadata__. Load with ``from_repacked``."""
+        import json
+        import struct
+        import numpy as np
+        lib = _lib.load()
+        n = C.c_int32()
+        _lib.check(lib.pulsar_engine_arena_count(self._h, C.byref(n)), "arena_count")
+        blobs, header, off = [], {}, 0
+        for i in range(n.value):
+            name, numel = C.c_char_p(), C.c_int64()
+            _lib.check(lib.pulsar_engine_arena_info(self._h, i, C.byref(name), C.byref(numel)), "arena_info")
+            buf = np.empty(numel.value, dtype=np.uint16)
+            _lib.check(lib.pulsar_engine_arena_read(self._h, name.value, buf.ctypes.data, numel.value), "arena_read")
+            b = buf.tobytes()
+            header[name.value.decode()] = {"dtype": "BF16", "shape": [numel.value], "data_offsets": [off, off + len(b)]}
+            blobs.append(b)
+            off += len(b)
+        for name, t in self._small.items():
+            b = t.numpy().tobytes()
+            header[name] = {"dtype": "F32", "shape": list(t.shape), "data_offsets": [off, off + len(b)]}
+            blobs.append(b)
+            off += len(b)
+        header["__metadata__"] = {"format": "pulsar_b200.arena.v1", "config": json.dumps(self.cfg.to_dict())}
+        hj = json.dumps(header).encode()
+        hj += b" " * (-len(hj) % 8)
+        with open(path, "wb") as f:
+            f.write(struct.pack("<Q", len(hj)))
+            f.write(hj)
+            for b in blobs:
+                f.write(b)
+
+    @classmethod
+    def from_repacked(cls, path: str, device: int | str | torch.device = 0, max_batch: int = 1,
+                      max_seq_len: int = 4096, max_prefill: Optional[int] = None,
+                      kv_dtype: torch.dtype = torch.bfloat16) -> "DeviceEngine":
+        """An engine from a ``save_repacked`` file: bf16 arena tensors go to the device as they
+        are (no fp32 staging, conversion or expert transposes)."""
+        import json
+        import struct
+        import numpy as np
+        with open(path, "rb") as f:
+            (hl,) = struct.unpack("<Q", f.read(8))
+            header = json.loads(f.read(hl))
+            data = f.read()
+        meta = header.pop("__metadata__", {})
+        if meta.get("format") != "pulsar_b200.arena.v1":
+            raise ValueError(f"{path}: not a pulsar_b200 repacked arena (format {meta.get('format')!r})")
+        cfg = PulsarConfig.from_dict(json.loads(meta["config"]))
+        self = cls.__new__(cls)
+        self._create(cfg, device, max_batch, max_seq_len, max_prefill, kv_dtype)
+        try:
+            lib = _lib.load()
+            for name, h in header.items():
+                b0, b1 = h["data_offsets"]
+                if h["dtype"] == "BF16":
+                    buf = np.frombuffer(data, dtype=np.uint16, count=(b1 - b0) // 2, offset=b0)
+                    _lib.check(lib.pulsar_engine_arena_write(self._h, name.encode(), buf.ctypes.data, buf.size),
+                               f"arena_write({name})")
+                else:
+                    a = torch.from_numpy(np.frombuffer(data, dtype=np.float32, count=(b1 - b0) // 4,
+                                                       offset=b0).copy()).reshape(h["shape"])
+                    _lib.check(lib.pulsar_engine_set_tensor(self._h, name.encode(), a.data_ptr(), a.numel()),
+                               f"set_tensor({name})")
+                    self._small[name] = a
+            self._finalize()
+        except Exception:
+            self.close()
+            raise
+        return self
 
     def close(self):
         if getattr(self, "_h", None) is not None and self._h.value:
