@@ -109,38 +109,26 @@ class DeviceEngine:
 
     # ---- checkpoint repack: safetensors-format file of the bf16 arena + the small fp32 tensors ----
     def save_repacked(self, path: str) -> None:
-        """Write the engine's weights as a safetensors-format file: the bf16 arena tensors in
-        the engine's layouts (BF16, 1-D) and the remaining fp32 state_dict tensors (F32, their
-        shapes), the config in the header's __metadata__. Load with ``from_repacked``."""
+        """Write the engine's weights as a safetensors-format file (pulsar_b200.repack): the bf16
+        arena tensors in the engine's layouts (BF16, 1-D) and the remaining fp32 state_dict
+        tensors (F32, their shapes), the config in the header's __metadata__. Load with
+        ``from_repacked``."""
         import json
-        import struct
         import numpy as np
+        from . import repack
         lib = _lib.load()
         n = C.c_int32()
         _lib.check(lib.pulsar_engine_arena_count(self._h, C.byref(n)), "arena_count")
-        blobs, header, off = [], {}, 0
+        tensors = []
         for i in range(n.value):
             name, numel = C.c_char_p(), C.c_int64()
             _lib.check(lib.pulsar_engine_arena_info(self._h, i, C.byref(name), C.byref(numel)), "arena_info")
             buf = np.empty(numel.value, dtype=np.uint16)
             _lib.check(lib.pulsar_engine_arena_read(self._h, name.value, buf.ctypes.data, numel.value), "arena_read")
-            b = buf.tobytes()
-            header[name.value.decode()] = {"dtype": "BF16", "shape": [numel.value], "data_offsets": [off, off + len(b)]}
-            blobs.append(b)
-            off += len(b)
+            tensors.append((name.value.decode(), "BF16", [numel.value], buf.tobytes()))
         for name, t in self._small.items():
-            b = t.numpy().tobytes()
-            header[name] = {"dtype": "F32", "shape": list(t.shape), "data_offsets": [off, off + len(b)]}
-            blobs.append(b)
-            off += len(b)
-        header["__metadata__"] = {"format": "pulsar_b200.arena.v1", "config": json.dumps(self.cfg.to_dict())}
-        hj = json.dumps(header).encode()
-        hj += b" " * (-len(hj) % 8)
-        with open(path, "wb") as f:
-            f.write(struct.pack("<Q", len(hj)))
-            f.write(hj)
-            for b in blobs:
-                f.write(b)
+            tensors.append((name, "F32", list(t.shape), t.numpy().tobytes()))
+        repack.write(path, tensors, {"format": repack.FORMAT, "config": json.dumps(self.cfg.to_dict())})
 
     @classmethod
     def from_repacked(cls, path: str, device: int | str | torch.device = 0, max_batch: int = 1,
@@ -149,15 +137,9 @@ class DeviceEngine:
         """An engine from a ``save_repacked`` file: bf16 arena tensors go to the device as they
         are (no fp32 staging, conversion or expert transposes)."""
         import json
-        import struct
         import numpy as np
-        with open(path, "rb") as f:
-            (hl,) = struct.unpack("<Q", f.read(8))
-            header = json.loads(f.read(hl))
-            data = f.read()
-        meta = header.pop("__metadata__", {})
-        if meta.get("format") != "pulsar_b200.arena.v1":
-            raise ValueError(f"{path}: not a pulsar_b200 repacked arena (format {meta.get('format')!r})")
+        from . import repack
+        header, meta, data = repack.read(path)
         cfg = PulsarConfig.from_dict(json.loads(meta["config"]))
         self = cls.__new__(cls)
         self._create(cfg, device, max_batch, max_seq_len, max_prefill, kv_dtype)
