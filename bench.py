@@ -259,6 +259,15 @@ def cpu_oracle_rate(n_tokens: int, prompt_len: int, seed: int = 0):
     return n_tokens / dt, threads, sample
 
 
+def arm_config(gamma: int, recipe: str, world: int) -> dict:
+    """The workload both arms report (BASELINE config 2 on every GPU)."""
+    return {"workload": f"pulsar-283M decode, B=1 per GPU, prompt {PROMPT}, {NEW} new tokens, greedy "
+                        f"gamma={gamma} self-speculative, recipe {recipe} weights",
+            "batch_per_gpu": 1, "prompt": PROMPT, "new_tokens": NEW, "gamma": gamma,
+            "l2": "no flush: weights (~0.57 GB) exceed the 126 MB L2", "kv_dtype": "bf16",
+            "parallelism": f"{world} independent replicas"}
+
+
 def run_reference(args):
     world, rank, local = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
     if rank != 0:
@@ -270,7 +279,7 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     cfg = PulsarConfig(eos_token_id=-1)
-    sd = make_state_dict(cfg, recipe="A", seed=0)
+    sd = make_state_dict(cfg, recipe=args.recipe, seed=0)
     m = O.OracleModel(sd, cfg)
     ids = random_prompts(1, PROMPT, cfg.vocab_size, seed=0)[0].tolist()
     kv = O.OracleKV(m, PROMPT + (args.steps + args.warmup) * per_step + 8)
@@ -287,12 +296,12 @@ def run_reference(args):
     tot = sum(times)
     value = per_step * args.steps / tot
     sample = (f"oracle port of src/infer.py (fp32 torch, {threads} threads), B=1 prompt {PROMPT}: each step = "
-              f"{per_step} greedy decode_step tokens (prefill untimed)")
+              f"{per_step} greedy decode_step tokens of the reference's sequential loop (prefill untimed; its tokens "
+              f"equal the gamma={args.gamma} loop's, and the rate is per emitted token)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"pulsar-283M decode B=1 prompt {PROMPT}, greedy (reference loop)",
-                       "prompt": PROMPT, "new_tokens_per_step": per_step},
+            "config": arm_config(args.gamma, args.recipe, args.gpus),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -437,11 +446,7 @@ def run_engine(args):
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"pulsar-283M decode, B=1 per GPU, prompt {PROMPT}, {NEW} new tokens, greedy "
-                                   f"gamma={g} self-speculative, recipe {args.recipe} weights",
-                       "batch_per_gpu": 1, "prompt": PROMPT, "new_tokens": NEW, "gamma": g,
-                       "l2": "no flush: weights (~0.57 GB) exceed the 126 MB L2", "kv_dtype": "bf16",
-                       "parallelism": f"{world} independent replicas"},
+            "config": arm_config(g, args.recipe, world),
             "accept_rate": stats["accepted"] / max(1, stats["drafted"]),
             "tokens_per_round": acc + 1 if g > 0 else 1.0,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
