@@ -178,6 +178,15 @@ int pulsar_engine_pulse(pulsar_engine* eng, int32_t pulse, int32_t R, const int3
 int pulsar_engine_get_length(pulsar_engine* eng, int32_t slot, int32_t* length);
 int pulsar_engine_set_length(pulsar_engine* eng, int32_t slot, int32_t length);
 
+/* Read cached keys / values (UnifiedKVCache.layers[layer]["k"], ["v"] of the reference,
+ * src/infer.py:86-96, which scripts/benchmark.py:411-417 reads): positions [pos0, pos0 + n)
+ * of one slot and layer, every kv head, as fp32 [4][n][64] into k_host and v_host (converted
+ * from bf16 when the cache is bf16). Local layers keep a ring of their last 2048 positions:
+ * a position older than that reads whatever later position shares its ring entry. Waits for
+ * the device; not for the token path (it allocates a staging buffer). */
+int pulsar_engine_read_kv(pulsar_engine* eng, int32_t slot, int32_t layer, int32_t pos0, int32_t n, float* k_host,
+                          float* v_host);
+
 /* Greedy decode loop, reference semantics (stream_generate with temperature 0 and
  * repetition_penalty 1, src/infer.py:551-621): starting from the prefill logits already
  * in the slot's state, emit n_new tokens. gamma == 0: exact sequential decode (3 pulses

@@ -555,16 +555,30 @@ def warped_probs(logits: torch.Tensor, temperature: float, top_p: float) -> torc
     return probs / s
 
 
+def _start(m: OracleModel, prompt: list[int], kv, first_logits, capacity: int):
+    """The cache and first-token logits a generate loop starts from: a fresh prefill, or a
+    given cache that already holds the prompt (its length must be len(prompt)) with the
+    logits computed alongside it."""
+    if kv is None:
+        kv = OracleKV(m, capacity)
+        return kv, prefill(m, prompt, kv)
+    if first_logits is None or kv.length != len(prompt):
+        raise ValueError("a given cache needs first_logits and must hold exactly the prompt's positions")
+    return kv, first_logits.float().reshape(-1).cpu()
+
+
 def stream_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: int, temperature: float = 0.0,
                         top_p: float = 1.0, repetition_penalty: float = 1.0, stop_ids=(), capacity=None,
                         generator: torch.Generator | None = None, trace=None, early_exit_threshold=None,
-                        exit_counts=None, exit_probs=None) -> list[int]:
+                        exit_counts=None, exit_probs=None, kv: OracleKV | None = None,
+                        first_logits: torch.Tensor | None = None) -> list[int]:
     """src/infer.py:551-621 returning token ids. Greedy when temperature <= 1e-4 (ties to
     the lowest index, as torch.argmax); sampling uses torch.multinomial on ``generator``.
     ``early_exit_threshold`` / ``exit_counts`` / ``exit_probs``: the engine's adaptive early
-    exit inside decode_step (src/infer.py:199-200, 536-546)."""
-    kv = OracleKV(m, capacity or (len(prompt) + max_new_tokens + 8))
-    logits = prefill(m, prompt, kv)
+    exit inside decode_step (src/infer.py:199-200, 536-546).
+    ``kv`` + ``first_logits``: start from a cache already holding the prompt (length
+    len(prompt)) and the logits that choose the first token, instead of running prefill."""
+    kv, logits = _start(m, prompt, kv, first_logits, capacity or (len(prompt) + max_new_tokens + 8))
     if trace is not None:
         trace.append(("prefill", logits.clone()))
     all_ids = list(prompt)
@@ -699,7 +713,8 @@ class SpecStats:
 
 def block_spec_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: int, gamma: int = 4,
                             temperature: float = 0.0, top_p: float = 1.0, seed: int = 0, seq_id: int = 0,
-                            capacity=None, stats: SpecStats | None = None, trace=None) -> list[int]:
+                            capacity=None, stats: SpecStats | None = None, trace=None, kv: OracleKV | None = None,
+                            first_logits: torch.Tensor | None = None) -> list[int]:
     """Self-speculative decoding with gamma drafts and one batched verify.
 
     Round with committed length n and pending token t0 (position n):
@@ -714,11 +729,11 @@ def block_spec_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: i
          at the first rejection the next token is argmax(P_{j-1}) / a draw from
          norm(max(0, p - q)) with u2; if all are accepted it is drawn from P_gamma;
       4. commit n..n+a (a = accepted drafts) and roll back the rest (length reset).
-    The first pending token comes from the (unsoftcapped) prefill logits.
+    The first pending token comes from the (unsoftcapped) prefill logits. ``kv`` +
+    ``first_logits``: start from a cache already holding the prompt instead of prefilling.
     """
     greedy = temperature <= 1e-4
-    kv = OracleKV(m, capacity or (len(prompt) + max_new_tokens + gamma + 8))
-    logits = prefill(m, prompt, kv)
+    kv, logits = _start(m, prompt, kv, first_logits, capacity or (len(prompt) + max_new_tokens + gamma + 8))
     n = len(prompt)
     out: list[int] = []
     rnd = 0

@@ -1696,6 +1696,51 @@ extern "C" int pulsar_engine_set_length(pulsar_engine* e, int32_t slot, int32_t 
 }
 
 namespace {
+// out[0][g][i][d] = K, out[1][g][i][d] = V of position pos0 + i, head g, as fp32.
+template <typename KVT>
+__global__ void k_kv_gather(KVLayer L, int slot, int pos0, int n, float* __restrict__ out) {
+    const int64_t per = (int64_t)HKV * n * DH;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < 2 * per; e += (int64_t)gridDim.x * blockDim.x) {
+        const int isv = (int)(e / per);
+        const int64_t r = e % per;
+        const int g = (int)(r / ((int64_t)n * DH)), i = (int)((r / DH) % n), d = (int)(r % DH);
+        const KVT* p = isv ? kv_v<KVT>(L, slot, g, pos0 + i) : kv_k<KVT>(L, slot, g, pos0 + i);
+        out[e] = kv_load(p + d);
+    }
+}
+}  // namespace
+
+extern "C" int pulsar_engine_read_kv(pulsar_engine* e, int32_t slot, int32_t layer, int32_t pos0, int32_t n,
+                                     float* k_host, float* v_host) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(slot >= 0 && slot < e->cfg.max_batch, "read_kv: slot %d out of range", slot);
+    PULSAR_CHECK_ARG(layer >= 0 && layer < NL, "read_kv: layer %d out of range [0, %d)", layer, NL);
+    PULSAR_CHECK_ARG(k_host && v_host, "read_kv: null pointer");
+    PULSAR_CHECK_ARG(n >= 0 && pos0 >= 0, "read_kv: negative position or count");
+    const KVLayer& L = e->kvl[layer];
+    if ((int64_t)pos0 + n > e->max_pos() || n > L.cap) {
+        set_error("read_kv: positions [%d, %lld) exceed the layer's %d cached positions (max position %d)", pos0,
+                  (long long)pos0 + n, L.cap, e->max_pos());
+        return PULSAR_ERR_CAPACITY;
+    }
+    if (n == 0) return PULSAR_OK;
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    PULSAR_TRY(cuda_status(cudaDeviceSynchronize(), "read_kv: pending work"));
+    PULSAR_TRY(check_kernel_err(e));
+    const size_t per = (size_t)HKV * n * DH;
+    float* tmp = nullptr;
+    PULSAR_TRY(cuda_status(cudaMalloc(&tmp, 2 * per * sizeof(float)), "read_kv: staging"));
+    if (e->kv32()) k_kv_gather<float><<<256, 256>>>(L, slot, pos0, n, tmp);
+    else k_kv_gather<__nv_bfloat16><<<256, 256>>>(L, slot, pos0, n, tmp);
+    int st = launch_status("k_kv_gather");
+    if (st == PULSAR_OK) st = cuda_status(cudaMemcpy(k_host, tmp, per * sizeof(float), cudaMemcpyDeviceToHost), "read_kv: copy K");
+    if (st == PULSAR_OK)
+        st = cuda_status(cudaMemcpy(v_host, tmp + per, per * sizeof(float), cudaMemcpyDeviceToHost), "read_kv: copy V");
+    cudaFree(tmp);
+    return st;
+}
+
+namespace {
 int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const int32_t* seq_ids_host,
                   const float* first_logits, int32_t n_new, int32_t gamma, bool sampled, float temperature, float top_p,
                   uint64_t seed, int32_t* out, int64_t* stats_host, void* stream) {

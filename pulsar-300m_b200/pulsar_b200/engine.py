@@ -200,6 +200,16 @@ class DeviceEngine:
     def set_length(self, slot: int, n: int) -> None:
         _lib.check(_lib.load().pulsar_engine_set_length(self._h, slot, int(n)), "set_length")
 
+    def read_kv(self, slot: int, layer: int, pos0: int, n: int):
+        """Cached keys and values of positions [pos0, pos0 + n) of one slot and layer
+        (pulsar_engine_read_kv): fp32 CPU tensors K, V of shape [n_kv_heads, n, head_dim]."""
+        cfg = self.cfg
+        k = torch.empty(cfg.n_kv_heads, n, cfg.head_dim, dtype=torch.float32)
+        v = torch.empty_like(k)
+        _lib.check(_lib.load().pulsar_engine_read_kv(self._h, slot, layer, pos0, n, k.data_ptr(), v.data_ptr()),
+                   "read_kv")
+        return k, v
+
     def set_option(self, name: str, value: int) -> None:
         """Engine options (see include/pulsar_b200.h): "megakernel" 0/1."""
         _lib.check(_lib.load().pulsar_engine_set_option(self._h, name.encode(), int(value)), f"set_option({name})")

@@ -136,3 +136,58 @@ def use_path(eng, path):
     kernels), 1 per-op GEMV kernels, 2 the many-row GEMM path."""
     eng.set_option("wide", 1 if path == 2 else 0)
     eng.set_option("megakernel", 1 if path == 0 else 0)
+
+
+# ---- oracle state taken from the device (long prompts) --------------------------------------
+def oracle_kv_from_engine(eng, m, slot, T, capacity):
+    """An OracleKV holding the engine's cached K/V of prompt positions [0, T) of ``slot``
+    (read through pulsar_engine_read_kv), with length T: the window of the local layers (their
+    last 1024 positions, all a later query can see) and every position of the global layers.
+    Decoding then starts from the same state on both sides; used for prompts whose recipe-B
+    prefill is chaotic (capacity dropping decided by router near-ties)."""
+    from oracle import pulsar_oracle as O
+    kv = O.OracleKV(m, capacity)
+    for layer in range(m.L):
+        lo = max(0, T - m.window) if layer in O.LOCAL_LAYERS else 0
+        k, v = eng.read_kv(slot, layer, lo, T - lo)
+        kv.k[layer][:, lo:T] = k
+        kv.v[layer][:, lo:T] = v
+    kv.length = T
+    return kv
+
+
+def logit_margin(lg):
+    v = lg.float().reshape(-1).topk(2).values
+    return float(v[0] - v[1])
+
+
+def spec_stream_divergence(got, ref, first_logits, trace, gamma, tol):
+    """Where a device greedy speculative stream first differs from the oracle's
+    block_spec_generate_ids stream (``trace`` from that run), and whether the difference is a
+    tie within ``tol``. Returns (index or None, reason).
+
+    Every emitted token is the argmax of one verify row (or of the first logits): round r emits
+    argmax(P_r[0..a]) where a counts the accepted drafts. A first difference at a token is
+    explained when that row's top-1 margin is <= tol. Draft decisions (argmax of the pulse-1
+    exit rows q) do not change the emitted tokens of their round, but a different draft changes
+    where the device's next block starts, and so the in-block K/V every later verify row sees;
+    a draft near-tie in that round or an earlier one therefore also explains a later
+    difference. Any other first difference is a parity failure (the reason starts with
+    'FAIL')."""
+    k = next((i for i, (a, b) in enumerate(zip(got, ref)) if a != b), None)
+    if k is None:
+        return None, "identical"
+    rows = [(-1, logit_margin(first_logits))]   # (round, margin) per emitted token
+    for (rnd, toks, q, P) in trace:
+        a = 0
+        while a < gamma and int(P[a].argmax()) == toks[a + 1]:
+            a += 1
+        rows.extend((rnd, logit_margin(P[j])) for j in range(a + 1))
+    rnd, mg = rows[k] if k < len(rows) else (trace[-1][0], 0.0)
+    if mg <= tol:
+        return k, f"token {k}: verify-row tie (margin {mg:.2e})"
+    draft = [(r, min(logit_margin(q[j]) for j in range(q.shape[0]))) for (r, _, q, _) in trace if r <= rnd]
+    lo = min(draft, key=lambda x: x[1]) if draft else (None, float("inf"))
+    if lo[1] <= tol:
+        return k, f"token {k}: draft tie in round {lo[0]} (margin {lo[1]:.2e}) changed the block boundaries"
+    return k, f"FAIL token {k} (round {rnd}): {got[k]} vs oracle {ref[k]}, margin {mg:.2e}, no tie"
