@@ -538,9 +538,12 @@ struct pulsar_engine {
     // persistent pulse kernel
     bool use_mega = false;
     int mega_grid = 0, mega_nch = 0;
-    float *m_gate = nullptr, *m_part = nullptr, *m_g8 = nullptr, *m_pmax = nullptr, *m_rpart = nullptr;
+    MegaX mx{};                 // exchange buffers of the persistent kernel (flag-carrying units)
+    float* m_pmax = nullptr;
     int *m_pidx = nullptr, *m_err = nullptr;
-    unsigned *m_bar = nullptr, *m_tickets = nullptr;
+    unsigned *m_epoch = nullptr, *m_tickets = nullptr;   // launch counter (flag of the next launch - 1), tickets
+    unsigned long long mega_wait_ns = WAIT_NS;   // option "wait_ns": bound of every wait in the persistent kernel
+    int mega_stall_cta = -1;                     // option "stall_cta": test hook (a CTA whose layer-0 wait runs out)
     unsigned long long* m_trace = nullptr;   // phase stamps of the last traced launch (option "trace")
     unsigned long long* m_experts = nullptr; // distinct routed experts streamed by persistent launches
 
@@ -769,6 +772,12 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
         a.rscale[l] = e->T_(e->L(l, "mlp.routed_scale")) + (int64_t)p * D;
         a.vres[l] = e->vres[p][l];
         a.kvl[l] = e->kvl[l];
+        if (lora_live(e)) {   // exact fp32 loop adapter: W x + Bs (A x), A = the three pulses' lora_A rows
+            a.la_qkv[l] = e->T_(e->L(l, "attn.wqkv_adapter.lora_A"));
+            a.lb_qkv[l] = e->lb_qkv[p][l];
+            a.la_wo[l] = e->T_(e->L(l, "attn.wo_adapter.lora_A"));
+            a.lb_wo[l] = e->lb_wo[p][l];
+        }
     }
     a.emb = e->emb;
     a.anchor = e->T_("anchor_norm.weight");
@@ -791,23 +800,14 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.hstride = hs;
     a.logits = logits;
     a.amax = amax;
-    auto& w = e->w;
-    a.h = w.h;
-    a.h_in = w.h_in;
-    a.qkv = w.qkv;
-    a.gate = e->m_gate;
-    a.att = w.att;
-    a.act_sh = w.act_sh;
-    a.act_r = w.act_r;
-    a.part = e->m_part;
-    a.vfirst = w.vfirst;
-    a.g8 = e->m_g8;
-    a.rpart = e->m_rpart;
     a.pmax = e->m_pmax;
     a.pidx = e->m_pidx;
     a.nch_max = e->mega_nch;
-    a.bar = e->m_bar;
+    a.x = e->mx;
+    a.epoch = e->m_epoch;
     a.tickets = e->m_tickets;
+    a.wait_ns = e->mega_wait_ns;
+    a.stall_cta = e->mega_stall_cta;
     a.err = e->m_err;
     a.experts = e->m_experts;
     a.trace = e->m_trace;
@@ -834,7 +834,7 @@ int pulse_dispatch(pulsar_engine* e, int p, int R, const int4* rows, const float
         return enqueue_pulse_wide<__nv_bfloat16>(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, ld_logits, amax,
                                                  st, hs);
     }
-    if (e->use_mega && !lora_live(e) && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
+    if (e->use_mega && R <= MEGA_RMAX && (logits == nullptr || ld_logits == e->V)) {
         e->n_kernels += 1;
         e->n_mega += 1;
         return pulse_mega(e, p, R, rows, h_prev, h0n_in, h_out, h0n_out, logits, amax, st, hs, skip);
@@ -1093,9 +1093,8 @@ int check_kernel_err(pulsar_engine* e) {
     PULSAR_TRY(cuda_status(cudaMemcpy(&v, e->m_err, 4, cudaMemcpyDeviceToHost), "read error flag"));
     if (v) {
         cudaMemset(e->m_err, 0, 4);
-        cudaMemset(e->m_bar, 0, 4);
-        cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 2) * 4);
-        set_error("a bounded device wait ran out (persistent pulse kernel grid barrier or weight stream, or a "
+        cudaMemset(e->m_tickets, 0, 2 * 4);
+        set_error("a bounded device wait ran out (persistent pulse kernel data exchange or weight stream, or a "
                   "tensor-core GEMM's MMA completion); results of the affected launch are invalid");
         return PULSAR_ERR_CUDA;
     }
@@ -1410,17 +1409,31 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         e->mega_grid = sms;
         e->use_mega = per_sm >= 1 && sms >= 144;
         e->mega_nch = std::max(2400 / 32 + 2, (maxlen + MEGA_CHUNK - 1) / MEGA_CHUNK + 2);   // see attn_chunk()
-        if ((st = e->wmalloc(&e->m_gate, (size_t)MEGA_RMAX * H)) ||
-            (st = e->wmalloc(&e->m_part, (size_t)MEGA_RMAX * H * e->mega_nch * PART)) ||
-            (st = e->wmalloc(&e->m_g8, (size_t)MEGA_RMAX * RG)) ||
-            (st = e->wmalloc(&e->m_rpart, (size_t)std::max(sms, 1) * MEGA_RMAX * E)) ||
-            (st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
+        // exchange units: zeroed below, so no unit carries a launch's flag (>= 1) before it is stored
+        auto& X = e->mx;
+        const size_t n_h = (size_t)NL * 2 * MEGA_RMAX * D, n_qkv = (size_t)NL * MEGA_RMAX * QKV,
+                     n_gate = (size_t)NL * MEGA_RMAX * H, n_part = (size_t)2 * MEGA_RMAX * H * e->mega_nch * PART,
+                     n_att = (size_t)NL * MEGA_RMAX * D, n_act = (size_t)NL * MEGA_RMAX * MEGA_ACT,
+                     n_vf = (size_t)MEGA_RMAX * HKV * DH, n_lt = (size_t)NL * 2 * MEGA_RMAX * LORA_R;
+        const size_t n_x = n_h + n_qkv + n_gate + n_part + n_att + n_act + n_vf + n_lt;
+        uint2* xb = nullptr;
+        if ((st = e->wmalloc(&xb, n_x)) || (st = cuda_status(cudaMemset(xb, 0, n_x * sizeof(uint2)), "zero exchange")))
+            return fail(st);
+        X.h = xb;
+        X.qkv = X.h + n_h;
+        X.gate = X.qkv + n_qkv;
+        X.part = X.gate + n_gate;
+        X.att = X.part + n_part;
+        X.act = X.att + n_att;
+        X.vfirst = X.act + n_act;
+        X.lt = X.vfirst + n_vf;
+        if ((st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
             (st = e->wmalloc(&e->m_pidx, (size_t)MEGA_RMAX * std::max(sms, 1))) || (st = e->wmalloc(&e->m_err, 1)) ||
-            (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 2)) ||
+            (st = e->wmalloc(&e->m_epoch, 1)) || (st = e->wmalloc(&e->m_tickets, 2)) ||
             (st = e->wmalloc(&e->m_experts, 1)))
             return fail(st);
-        if ((st = cuda_status(cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 2) * 4), "zero tickets")) ||
-            (st = cuda_status(cudaMemset(e->m_bar, 0, 4), "zero grid barrier")) ||
+        if ((st = cuda_status(cudaMemset(e->m_tickets, 0, 2 * 4), "zero tickets")) ||
+            (st = cuda_status(cudaMemset(e->m_epoch, 0, 4), "zero launch counter")) ||
             (st = cuda_status(cudaMemset(e->m_err, 0, 4), "zero err")) ||
             (st = cuda_status(cudaMemset(e->m_experts, 0, 8), "zero expert count")))
             return fail(st);
@@ -1955,6 +1968,26 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
         e->graphs.clear();
         return PULSAR_OK;
     }
+    if (strcmp(name, "wait_ns") == 0) {   // bound of every wait in the persistent kernel
+        PULSAR_CHECK_ARG(value >= 100000 && value <= (int64_t)WAIT_NS, "set_option(wait_ns): %lld outside [1e5, %llu]",
+                         (long long)value, (unsigned long long)WAIT_NS);
+        if ((unsigned long long)value != e->mega_wait_ns) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+            e->graphs.clear();
+        }
+        e->mega_wait_ns = (unsigned long long)value;
+        return PULSAR_OK;
+    }
+    if (strcmp(name, "stall_cta") == 0) {   // test hook: -1 off
+        PULSAR_CHECK_ARG(value >= -1 && value < e->mega_grid, "set_option(stall_cta): %lld outside [-1, %d)",
+                         (long long)value, e->mega_grid);
+        if (value != e->mega_stall_cta) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+            e->graphs.clear();
+        }
+        e->mega_stall_cta = (int)value;
+        return PULSAR_OK;
+    }
     set_error("set_option: unknown option '%s'", name);
     return PULSAR_ERR_INVALID;
 }
@@ -1976,6 +2009,8 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     PULSAR_CHECK_ARG(name && value, "get_option: null argument");
     if (strcmp(name, "megakernel") == 0) { *value = e->use_mega ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "megakernel_grid") == 0) { *value = e->mega_grid; return PULSAR_OK; }
+    if (strcmp(name, "wait_ns") == 0) { *value = (int64_t)e->mega_wait_ns; return PULSAR_OK; }
+    if (strcmp(name, "stall_cta") == 0) { *value = e->mega_stall_cta; return PULSAR_OK; }
     if (strcmp(name, "wide") == 0) { *value = e->force_wide ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "tc_gemm") == 0) { *value = e->use_tc ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "merged_adapter") == 0) { *value = e->merge_adapter ? 1 : 0; return PULSAR_OK; }
