@@ -45,17 +45,29 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
-def bytes_per_pass(cfg, d_routed: float, kv_keys: int, rows: int, with_lm_head: bool) -> float:
+def load_tflops():
+    """Sustained dense bf16 TFLOP/s of MEASURED_PEAKS.json (a kernel timed inside a long run), else
+    the recipe's fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
+
+
+def bytes_per_pass(cfg, d_routed: float, kv_keys: int, rows: int, with_lm_head: bool, adapter: bool = False) -> float:
     """Algorithmic bytes of one pulse pass (the per-unit figure of the roofline): bf16
     weights read once (wqkv, wo, shared expert, d_routed distinct routed experts per
     layer), fp32 small tensors, KV keys read once per (layer, sequence) and written per
-    row, LM head once, embedding gathers."""
+    row, LM head once, embedding gathers. adapter: the live loop adapter's fp32 factors
+    (A of wqkv and wo, 24 x 1024 each, and the per-pulse Bs, 1536 x 24 and 1024 x 24)."""
     D = cfg.d_model
     attn = (cfg.qkv_dim * D + D * D) * 2
     shared = (2 * cfg.d_shared * D + D * cfg.d_shared) * 2
     routed = (2 * cfg.d_expert * D + cfg.d_expert * D) * 2
     small = (16 * D + 16 * D + 4 * D) * 4       # gate, router, norms/scales (fp32)
-    per_layer = attn + shared + small + routed * d_routed
+    lora = (2 * 24 * D + cfg.qkv_dim * 24 + D * 24) * 4 if adapter else 0
+    per_layer = attn + shared + small + lora + routed * d_routed
     kv = kv_keys * 1024 + rows * 8 * 1024        # bf16 K+V: 4 heads x 64 x 2 x 2 B per key per layer
     lm = cfg.vocab_size * D * 2 if with_lm_head else 0
     return cfg.n_core * per_layer + kv + lm + rows * D * 2
@@ -140,7 +152,8 @@ def kernel_roofline(eng, cfg, gamma: int, recipe: str, reps: int, peak: float, p
             ts.append(eng.get_option("last_pulse_ns") * 1e-9)
         t = statistics.mean(ts)
         d = (eng.get_option("routed_experts") - e0) / (reps * cfg.n_core)   # distinct experts per layer
-        b = bytes_per_pass(cfg, d, kv_keys_for(PROMPT + R), R, lm) + (R * cfg.vocab_size * 4 if lm else 0)
+        b = bytes_per_pass(cfg, d, kv_keys_for(PROMPT + R), R, lm, adapter=recipe == "B") + \
+            (R * cfg.vocab_size * 4 if lm else 0)
         shapes[name] = {"rows": R, "lm_head": lm, "per_round": n, "us": t * 1e6, "bytes": b,
                         "experts_per_layer": d, "gbs": b / t / 1e9}
         tot_b += n * b
@@ -349,22 +362,48 @@ def throughput_b256(args, world, rank, local):
     torch.cuda.synchronize()
     ms_max = max_over_ranks(e0.elapsed_time(e1), world, local)
     eng.close()
+    # roofline of one decode round of the batch (algorithmic units, mean context): gamma + 1
+    # pulse-0 passes of B rows, pulse-1 and pulse-2 passes of B (gamma + 1) rows; every pass
+    # streams all 16 routed experts (hundreds of rows route to every expert) and reads each
+    # sequence's K/V once per layer; gamma + 1 LM heads. FLOPs: 2 x the active parameters of a
+    # row (4 routed experts) per row per pass, plus the LM head rows.
+    g = 4
+    rounds = st["rounds"] / TP_BATCH
+    L = TP_PROMPT + TP_NEW // 2
+    D = cfg.d_model
+    rows_pass = [TP_BATCH] * (g + 1) + [TP_BATCH * (g + 1)] * 2
+    b_round = sum(bytes_per_pass(cfg, cfg.n_routed_experts, TP_BATCH * kv_keys_for(L), r, False) for r in rows_pass)
+    b_round += (g + 1) * cfg.vocab_size * D * 2
+    act_params = cfg.n_core * ((cfg.qkv_dim + D) * D + 3 * cfg.d_shared * D + cfg.top_k * 3 * cfg.d_expert * D)
+    lm_rows = g * TP_BATCH + TP_BATCH * (g + 1)
+    f_round = 2.0 * act_params * sum(rows_pass) + 2.0 * cfg.vocab_size * D * lm_rows
+    bw = rounds * b_round / (ms_max / 1e3) / 1e9
+    fl = rounds * f_round / (ms_max / 1e3) / 1e12
+    peak, peak_kind = load_peaks()
+    tf_peak, tf_kind = load_tflops()
+    roof = {"bound": "hbm" if b_round / peak > f_round / 1e3 / tf_peak else "tensor",
+            "achieved": bw, "peak": peak, "unit": "GB/s", "frac": bw / peak, "peak_kind": peak_kind,
+            "tensor_achieved_tflops": fl, "tensor_peak_tflops": tf_peak, "tensor_frac": fl / tf_peak,
+            "tensor_peak_kind": tf_kind, "bytes_per_round": b_round, "flops_per_round": f_round,
+            "rounds": rounds, "scope": "per GPU: algorithmic bytes / FLOPs of the timed decode over its device time"}
     return {"value": job_rate(TP_BATCH * TP_NEW, world, ms_max), "unit": "tokens/s", "ms": ms_max,
+            "roofline": roof,
             "accept_rate": st["accepted"] / max(1, st["drafted"]),
             "config": {"workload": f"BASELINE config 5: {TP_BATCH} sequences per GPU, prompt {TP_PROMPT}, {TP_NEW} new "
                                    f"tokens, greedy gamma=4, recipe {args.recipe} weights", "batch_per_gpu": TP_BATCH,
                        "timed": "decode of one generate call (prefill untimed), CUDA events, max over ranks"}}
 
 
-def run_engine(args):
-    world, rank, local = dist_setup()
+def decode_leg(args, recipe: str, world: int, rank: int, local: int, full: bool):
+    """The metric's B=1 half on one weight recipe: timed decode of the bench workload (device
+    time, max over ranks), launch and expert counts, the dominant kernel's roofline and the
+    path roofline; with full=True also the clocks and the end-to-end run through the C ABI."""
     from pulsar_b200.config import PulsarConfig
     from pulsar_b200.engine import DeviceEngine
     from pulsar_b200.weights import make_state_dict, random_prompts
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     cfg = PulsarConfig(eos_token_id=-1)
-    sd = make_state_dict(cfg, recipe=args.recipe, seed=0)
+    sd = make_state_dict(cfg, recipe=recipe, seed=0)
     eng = DeviceEngine(cfg, sd, device=local, max_batch=1, max_seq_len=PROMPT + NEW + 64, max_prefill=PROMPT,
                        kv_dtype=torch.bfloat16)
     del sd
@@ -372,16 +411,17 @@ def run_engine(args):
     first = eng.prefill(0, ids.tolist())
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
+    g = args.gamma
 
     def step():
         eng.set_length(0, PROMPT)
-        return eng.generate_greedy([0], first.view(1, -1), NEW, gamma=args.gamma)
+        return eng.generate_greedy([0], first.view(1, -1), NEW, gamma=g)
 
     for _ in range(args.warmup):
         out, st = step()
     torch.cuda.synchronize()
     barrier(world)
-    clk = Clocks(local)
+    clk = Clocks(local) if full else None
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stats = {"rounds": 0, "drafted": 0, "accepted": 0}
     launches0 = eng.get_option("kernel_launches")
@@ -395,71 +435,87 @@ def run_engine(args):
             stats[k] += st[k]
     ev1.record(stream)
     torch.cuda.synchronize()
-    clocks = clk.stop()
+    clocks = clk.stop() if clk else None
     gpu_launches = eng.get_option("kernel_launches") - launches0
     mega_launches = eng.get_option("mega_launches") - mega0
     experts_streamed = eng.get_option("routed_experts") - experts0
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, world, local)
-    value = job_rate(NEW * args.steps, world, ms_max)
-    # ---- end-to-end through the C ABI with host buffers (prompt H2D, prefill, decode, tokens D2H)
-    pinned_ids = ids.to(torch.int32).pin_memory()
-    host_out = torch.empty(NEW, dtype=torch.int32).pin_memory()
-    e2e_ms, pre_ms = [], []
-    for s in range(args.warmup + args.steps):
-        torch.cuda.synchronize()
-        e0, em, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        e0.record(stream)
-        d_ids = pinned_ids.to(dev, non_blocking=True)
-        lg = eng.prefill(0, d_ids)
-        em.record(stream)
-        toks, _ = eng.generate_greedy([0], lg.view(1, -1), NEW, gamma=args.gamma)
-        host_out.copy_(toks[0], non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if s >= args.warmup:
-            e2e_ms.append(e0.elapsed_time(e1))
-            pre_ms.append(e0.elapsed_time(em))
-    e2e_ms_max = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, local)
-    e2e_value = job_rate(NEW, world, e2e_ms_max)
+    res = {"value": job_rate(NEW * args.steps, world, ms_max), "ms_per_step": ms_max / args.steps,
+           "accept_rate": stats["accepted"] / max(1, stats["drafted"]),
+           "tokens_per_round": stats["accepted"] / max(1, stats["rounds"]) + 1 if g > 0 else 1.0,
+           "gpu_launches": gpu_launches, "mega_launches": mega_launches, "clocks": clocks,
+           "loop_adapter": bool(eng.get_option("loop_adapter"))}
+    if full:
+        # ---- end-to-end through the C ABI with host buffers (prompt H2D, prefill, decode, tokens D2H)
+        pinned_ids = ids.to(torch.int32).pin_memory()
+        host_out = torch.empty(NEW, dtype=torch.int32).pin_memory()
+        e2e_ms, pre_ms = [], []
+        for s in range(args.warmup + args.steps):
+            torch.cuda.synchronize()
+            e0, em, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            d_ids = pinned_ids.to(dev, non_blocking=True)
+            lg = eng.prefill(0, d_ids)
+            em.record(stream)
+            toks, _ = eng.generate_greedy([0], lg.view(1, -1), NEW, gamma=g)
+            host_out.copy_(toks[0], non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if s >= args.warmup:
+                e2e_ms.append(e0.elapsed_time(e1))
+                pre_ms.append(e0.elapsed_time(em))
+        e2e_ms_max = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, local)
+        res["e2e"] = {"value": job_rate(NEW, world, e2e_ms_max), "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
+                      "d2h_bytes_per_step": NEW * 4, "includes": "prompt H2D, prefill, decode, tokens D2H",
+                      "prefill_ms": statistics.mean(pre_ms), "ms_per_step": statistics.mean(e2e_ms)}
     # ---- roofline of the dominant kernel, then of the whole decode path
     peak, peak_kind = load_peaks()
-    roof = kernel_roofline(eng, cfg, args.gamma, args.recipe, args.kernel_reps, peak, peak_kind)
-    rounds = max(1, stats["rounds"])
-    acc = stats["accepted"] / rounds
-    L = PROMPT + NEW // 2
-    g = args.gamma
+    res["roofline"] = kernel_roofline(eng, cfg, g, recipe, args.kernel_reps, peak, peak_kind)
     # algorithmic bytes of the timed region: every launch's fixed bytes plus the routed experts
     # the kernels actually streamed (device counter), at the mean context of the step
+    L = PROMPT + NEW // 2
+    ad = recipe == "B"
     routed = (2 * cfg.d_expert * cfg.d_model + cfg.d_expert * cfg.d_model) * 2
     kv = kv_keys_for(L)
     if g > 0:
         n_rounds = mega_launches / (g + 3)
-        fixed = n_rounds * ((g + 1) * bytes_per_pass(cfg, 0, kv, 1, False) + g * cfg.vocab_size * cfg.d_model * 2
-                            + bytes_per_pass(cfg, 0, kv, g + 1, False) + bytes_per_pass(cfg, 0, kv, g + 1, True))
+        fixed = n_rounds * ((g + 1) * bytes_per_pass(cfg, 0, kv, 1, False, ad) + g * cfg.vocab_size * cfg.d_model * 2
+                            + bytes_per_pass(cfg, 0, kv, g + 1, False, ad) + bytes_per_pass(cfg, 0, kv, g + 1, True, ad))
     else:
         n_steps = mega_launches / 3
-        fixed = n_steps * (3 * bytes_per_pass(cfg, 0, kv, 1, False) + cfg.vocab_size * cfg.d_model * 2)
+        fixed = n_steps * (3 * bytes_per_pass(cfg, 0, kv, 1, False, ad) + cfg.vocab_size * cfg.d_model * 2)
     path_bytes = fixed + experts_streamed * routed
-    bytes_per_token = path_bytes / (NEW * args.steps)
     achieved = path_bytes / (ms / 1e3) / 1e9
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+    res["path_roofline"] = {"scope": "whole decode path: algorithmic bytes of the timed region (routed experts counted "
+                                     "on the device) / device time",
+                            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                            "peak_kind": peak_kind, "bytes_per_token": path_bytes / (NEW * args.steps)}
+    eng.close()
+    return res
+
+
+def run_engine(args):
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    g = args.gamma
+    a = decode_leg(args, args.recipe, world, rank, local, full=True)
+    line = {"metric": METRIC, "value": a["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": a["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": arm_config(g, args.recipe, world),
-            "accept_rate": stats["accepted"] / max(1, stats["drafted"]),
-            "tokens_per_round": acc + 1 if g > 0 else 1.0,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 4,
-                    "d2h_bytes_per_step": NEW * 4, "includes": "prompt H2D, prefill, decode, tokens D2H",
-                    "prefill_ms": statistics.mean(pre_ms), "ms_per_step": statistics.mean(e2e_ms)},
-            "roofline": roof,
-            "path_roofline": {"scope": "whole decode path: algorithmic bytes of the timed region (routed experts counted on the device) / device time",
-                              "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                              "peak_kind": peak_kind, "bytes_per_token": bytes_per_token},
-            "clocks": clocks,
-            "gpu_launches": gpu_launches,
-            "mega_launches": mega_launches}
-    eng.close()
+            "accept_rate": a["accept_rate"], "tokens_per_round": a["tokens_per_round"],
+            "e2e": a["e2e"], "roofline": a["roofline"], "path_roofline": a["path_roofline"],
+            "clocks": a["clocks"], "gpu_launches": a["gpu_launches"], "mega_launches": a["mega_launches"]}
+    if not args.no_recipe_b and args.recipe == "A":
+        # the same workload on recipe-B weights (non-trivial acceptance, live loop adapter): its own
+        # rate, acceptance, tokens per round and rooflines (same collective steps on every rank)
+        b = decode_leg(args, "B", world, rank, local, full=False)
+        line["recipe_b"] = {"value": b["value"], "unit": "tokens/s", "ms_per_step": b["ms_per_step"],
+                            "accept_rate": b["accept_rate"], "tokens_per_round": b["tokens_per_round"],
+                            "loop_adapter": b["loop_adapter"], "gpu_launches": b["gpu_launches"],
+                            "roofline": b["roofline"], "path_roofline": b["path_roofline"],
+                            "config": arm_config(g, "B", world)}
     if not args.no_throughput:
         # the metric's B=256 half: every rank runs its replica (same collective steps on all ranks)
         line["throughput_b256"] = throughput_b256(args, world, rank, local)
@@ -523,6 +579,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-throughput", action="store_true", help="skip the B=256 throughput measurement (config 5)")
+    ap.add_argument("--no-recipe-b", action="store_true", help="skip the recipe-B decode leg")
     ap.add_argument("--throughput-profile", action="store_true",
                     help="config 5 only: one decode round between cudaProfilerStart/Stop (ncu captures)")
     ap.add_argument("--kernel-reps", type=int, default=20)

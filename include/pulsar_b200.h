@@ -73,7 +73,10 @@ int pulsar_op_moe_router_topk(const void* logits_dev, int logits_bf16, const flo
  * 4 MiB array compiled into the library, present on every GPU that loads it until exit.
  * Limit: N * (E + 1) <= 1,048,576 floats, else PULSAR_ERR_CAPACITY. Allocates nothing.
  * The first call on each device looks up the array's device address (with that device
- * current); make that first call before any stream capture begins. All calls share the
+ * current); make that first call before any stream capture begins. The address is looked up
+ * again when the calling thread's current context is not the one it was found in (after
+ * cudaDeviceReset, for instance); make the first call after such a reset before any stream
+ * capture too. All calls share the
  * array: calls whose executions overlap on the GPU (for example on two streams) race.
  * Nothing in it has to start at zero: each call writes every element it reads. */
 int pulsar_op_moe_router_topk_noalloc(const void* logits_dev, int logits_bf16, const float* expert_bias_dev,
@@ -209,8 +212,11 @@ int pulsar_engine_generate_greedy(pulsar_engine* eng, int32_t n_seq, const int32
  * token from norm(max(0, p - q)), full acceptance draws it from p_gamma. Every uniform comes
  * from Philox4x32-10 with counter (seq_ids_host[i], round, slot, 0) and key (seed lo, seed hi),
  * u_k = (x_k >> 8) * 2^-24; the first token uses round 0xFFFFFFFF. Draws are inverse-CDF in
- * vocabulary order. temperature > 0, 0 < top_p <= 1, vocab_size <= 49152. Other arguments
- * as in pulsar_engine_generate_greedy. */
+ * vocabulary order. temperature > 0, 0 < top_p <= 1, vocab_size <= 49152; a temperature of at
+ * most 1e-4 decodes greedily (pulsar_engine_generate_greedy), as the reference's sampler does
+ * (src/infer.py:591, 669). Top-p keeps every token whose warped weight is tied with the cutoff
+ * token's (the reference sorts, so among exactly tied weights it keeps those the sort puts
+ * first). Other arguments as in pulsar_engine_generate_greedy. */
 int pulsar_engine_generate_sampled(pulsar_engine* eng, int32_t n_seq, const int32_t* slots_host,
                                    const int32_t* seq_ids_host, const float* first_logits_dev, int32_t n_new,
                                    int32_t gamma, float temperature, float top_p, uint64_t seed,

@@ -1857,6 +1857,10 @@ extern "C" int pulsar_engine_generate_sampled(pulsar_engine* e, int32_t n, const
                                               const int32_t* seq_ids_host, const float* first_logits, int32_t n_new,
                                               int32_t gamma, float temperature, float top_p, uint64_t seed,
                                               int32_t* out, int64_t* stats_host, void* stream) {
+    // temperature <= 1e-4 is greedy decoding in the reference (src/infer.py:591, :669)
+    if (temperature > 0.f && temperature <= 1e-4f && top_p > 0.f && top_p <= 1.f)
+        return generate_impl(e, n, slots_host, nullptr, first_logits, n_new, gamma, false, 0.f, 1.f, 0, out,
+                             stats_host, stream);
     return generate_impl(e, n, slots_host, seq_ids_host, first_logits, n_new, gamma, true, temperature, top_p, seed,
                          out, stats_host, stream);
 }

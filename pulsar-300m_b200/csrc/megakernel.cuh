@@ -167,6 +167,10 @@ __device__ __forceinline__ uint2* xgate(const MegaArgs& a, int l, int r) { retur
 __device__ __forceinline__ uint2* xpart(const MegaArgs& a, int l, int r, int h, int c) {
     return a.x.part + ((((int64_t)(l & 1) * MEGA_RMAX + r) * H + h) * a.nch_max + c) * PART;
 }
+// Flag of the attention-partial units of layer l. Layers l and l + 2 share a region within one
+// launch, so these units carry the layer as well as the launch (a reader must not take a
+// layer-l unit for a layer-(l + 2) one).
+__device__ __forceinline__ unsigned part_flag(unsigned f, int l) { return (f << 3) | (unsigned)l; }
 __device__ __forceinline__ uint2* xatt(const MegaArgs& a, int l, int r) { return a.x.att + ((int64_t)l * MEGA_RMAX + r) * D; }
 __device__ __forceinline__ uint2* xact(const MegaArgs& a, int l, int r) {
     return a.x.act + ((int64_t)l * MEGA_RMAX + r) * MEGA_ACT;
@@ -592,46 +596,17 @@ __device__ __forceinline__ void produce_kv(Ring& g, const KVLayer& L, int slot, 
     }
 }
 
-// Consumers (all 15 warps): take the same tiles, widen them to fp32 rows of `dst` (stride
-// DH + 1), release each slot after every warp is done with it.
-template <typename KVT>
-__device__ __forceinline__ void consume_kv(Ring& g, int n, float* dst) {
-    constexpr int KPT = kv_keys_per_tile<KVT>();
-    constexpr int PARTS = DH * (int)sizeof(KVT) / 16;   // 16-byte pieces per row
-    const int tid = threadIdx.x - 32;
-    for (int k = 0; k < n; k += KPT) {
-        const int m = min(KPT, n - k);
-        const uint32_t slot_i = g.t % MEGA_NS;
-        const uint32_t use = g.t / MEGA_NS;
-        if (g.ok && !mbar_wait_ab(*g.a, g.s, &g.s->full[slot_i], use & 1)) {
-            g.ok = false;
-            raise_abort(*g.a, g.s);
-        }
-        if (g.ok) {
-            const unsigned char* tile = g.s->ring[slot_i];
-            for (int e = tid; e < m * PARTS; e += MEGA_NCT) {
-                const int kk = e / PARTS, part = e % PARTS;
-                const uint4 u = *reinterpret_cast<const uint4*>(tile + kk * DH * sizeof(KVT) + part * 16);
-                float* d = dst + (k + kk) * (DH + 1);
-                if constexpr (sizeof(KVT) == 2) {
-                    float f[8];
-                    bf16x8_to_f32(u, f);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) d[part * 8 + i] = f[i];
-                } else {
-                    d[part * 4 + 0] = __uint_as_float(u.x);
-                    d[part * 4 + 1] = __uint_as_float(u.y);
-                    d[part * 4 + 2] = __uint_as_float(u.z);
-                    d[part * 4 + 3] = __uint_as_float(u.w);
-                }
-            }
-        }
-        named_bar_sync(1, MEGA_NCT);
-        if (threadIdx.x == 32 && g.ok) mbar_arrive(&g.s->empty[slot_i]);
-        ++g.t;
-    }
+// Pair w (elements 2w, 2w + 1) of a 64-element K/V row stored as KVT.
+__device__ __forceinline__ float2 kv_pair(const __nv_bfloat16* row, int w) {
+    return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row)[w]);
 }
+__device__ __forceinline__ float2 kv_pair(const float* row, int w) { return reinterpret_cast<const float2*>(row)[w]; }
 
+// One attention item: queries of heads 4g..4g+3 of rows r0..r0+nr-1 against the chunk's keys
+// [k0, k1). Cached keys (< pos0) come from the ring tiles (R <= 2) or are loaded into shared
+// memory (R > 2); the block rows' own keys are produced here. Then a warp per query: scores with
+// the chunk's keys on the lanes, softmax with warp shuffles, P.V with dimension pairs on the lanes;
+// split-K partials (m, l, o[64]) published as units of the layer's partial flag.
 template <int R, typename KVT>
 __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& ring, int l, int r0, int nr, int g,
                                        int c, int chunk, unsigned f, bool first, bool& ok) {
@@ -647,15 +622,14 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     const int k1 = min(k0 + chunk, posL + 1);
     const int nk = k1 - k0;
     const int nold = max(0, min(k1, pos0) - k0);          // keys < pos0 come from the cache
+    const unsigned pf = part_flag(f, l);
     float* qs = s->xs;                                   // [nr*4][64]
-    float* Ks = qs + MEGA_RMAX * GQA * DH;               // [64][65]
+    float* Ks = qs + MEGA_RMAX * GQA * DH;               // [64][65] fp32 keys (new ones; R > 2: all)
     float* Vs = Ks + MEGA_CHUNK * (DH + 1);              // [64][65]
-    float* Ps = Vs + MEGA_CHUNK * (DH + 1);              // [nr*4][64]
     const int nq = nr * GQA;
     astamp(a, l, 0, first);
-    // queries of heads 4g..4g+3 (warps), and the block rows' own keys/values (produced here);
-    // they land in rows [nold, nk) of Ks / Vs, disjoint from the cached rows
-    auto queries_and_new_keys = [&]() {
+    // queries (warps) and the block rows' own keys/values, produced here into rows [nold, nk)
+    {
         const int vres_mode = (a.pulse == 0) ? (l == 0 ? 1 : 2) : 0;
         const int nnew = max(0, k1 - max(k0, pos0));
         for (int it = cw; it < nq + nnew; it += MEGA_NCW) {
@@ -722,15 +696,27 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
                 Vs[kk * (DH + 1) + lane + 32] = kv_round<KVT>(v2);
             }
         }
-    };
-    // 1) cached keys/values of the chunk. One- and two-row passes: the producer streamed them
-    //    through the ring during phase A, so the queries' polls go first and the tiles land
-    //    meanwhile. Larger passes load them here, every thread's 16-byte loads issued first.
+    }
+    astamp(a, l, 1, first);
+    // cached keys/values: R <= 2 the ring tiles the producer streamed during phase A (ntk tiles of
+    // K, then ntk of V, waited for here and released after the compute); larger passes load them
+    // here into Ks / Vs, every thread's 16-byte loads issued first
+    constexpr int KPT = kv_keys_per_tile<KVT>();
+    constexpr int ROW = DH;   // elements per cached row
+    const KVT* kt[MEGA_CHUNK / KPT + 1];
+    const KVT* vt[MEGA_CHUNK / KPT + 1];
+    int ntk = 0;
     if constexpr (R <= MEGA_RING_KV_MAX_R) {
-        queries_and_new_keys();
-        astamp(a, l, 1, first);
-        consume_kv<KVT>(ring, nold, Ks);
-        consume_kv<KVT>(ring, nold, Vs);
+        ntk = (nold + KPT - 1) / KPT;
+        for (int i = 0; i < 2 * ntk; ++i) {
+            const uint32_t t = ring.t + i;
+            if (ring.ok && !mbar_wait_ab(a, s, &s->full[t % MEGA_NS], (t / MEGA_NS) & 1)) {
+                ring.ok = false;
+                raise_abort(a, s);
+            }
+            const KVT* tile = reinterpret_cast<const KVT*>(s->ring[t % MEGA_NS]);
+            if (i < ntk) kt[i] = tile; else vt[i - ntk] = tile;
+        }
     } else {
         constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
         for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
@@ -740,160 +726,110 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
             const KVT* row = isv ? kv_v<KVT>(L, slot, g, k0 + kk) : kv_k<KVT>(L, slot, g, k0 + kk);
             load_kv_row16<KVT>(row, part, (isv ? Vs : Ks) + kk * (DH + 1));
         }
-        astamp(a, l, 1, first);
-        queries_and_new_keys();
     }
-    // rows past the end of a partial chunk: zeros (probabilities are 0 there; 0 * stale
-    // shared memory could be NaN)
-    for (int e = tid; e < (MEGA_CHUNK - nk) * DH; e += MEGA_NCT) {
-        const int kk = nk + e / DH, d = e % DH;
-        Ks[kk * (DH + 1) + d] = 0.f;
-        Vs[kk * (DH + 1) + d] = 0.f;
-    }
-    named_bar_sync(1, MEGA_NCT);
+    named_bar_sync(1, MEGA_NCT);   // queries, produced keys (and loaded keys) visible
     astamp(a, l, 2, first);
-    // 3) scores with per-row masks [lo_r, pos_r]. Several rows: a thread per (key, row) covers
-    //    the row's four heads (float4 query loads shared by the key's element); one row: a
-    //    thread per (key, head)
-    if (nq >= 2 * GQA) {
-        for (int e = tid; e < nr * MEGA_CHUNK; e += MEGA_NCT) {
-            const int rq = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
-            const int key = k0 + kk;
-            const int pos = rows[r0 + rq].y;
-            const int lor = local ? max(0, pos - WINDOW + 1) : 0;
-            const bool vis = kk < nk && key <= pos && key >= lor;
-            float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
-            if (vis) {
-                const float* kv = Ks + kk * (DH + 1);
-#pragma unroll 4
-                for (int d = 0; d < DH; d += 4) {
-                    const float c0 = kv[d], c1 = kv[d + 1], c2 = kv[d + 2], c3 = kv[d + 3];
-#pragma unroll
-                    for (int i = 0; i < GQA; ++i) {
-                        const float4 q = *reinterpret_cast<const float4*>(qs + (rq * GQA + i) * DH + d);
-                        acc[i] += q.x * c0 + q.y * c1 + q.z * c2 + q.w * c3;
-                    }
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < GQA; ++i) Ps[(rq * GQA + i) * MEGA_CHUNK + kk] = vis ? acc[i] : -INFINITY;
-        }
-    } else
-    for (int e = tid; e < nq * MEGA_CHUNK; e += MEGA_NCT) {
-        const int qi = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
-        const int key = k0 + kk;
-        const int pos = rows[r0 + qi / GQA].y;
-        const int lor = local ? max(0, pos - WINDOW + 1) : 0;
-        float sc = -INFINITY;
-        if (kk < nk && key <= pos && key >= lor) {
-            sc = 0.f;
-            const float* qv = qs + qi * DH;
-            const float* kv = Ks + kk * (DH + 1);
-#pragma unroll 16
-            for (int d = 0; d < DH; ++d) sc += qv[d] * kv[d];
-        }
-        Ps[qi * MEGA_CHUNK + kk] = sc;
-    }
-    named_bar_sync(1, MEGA_NCT);
-    astamp(a, l, 3, first);
-    // 4) partial softmax per query (warps): max m, weights e = exp(s - m) back into Ps, sum
+    constexpr bool TILES = R <= MEGA_RING_KV_MAX_R;
     for (int qi = cw; qi < nq; qi += MEGA_NCW) {
         const int rr = qi / GQA, h = g * GQA + qi % GQA;
-        const float p0 = Ps[qi * MEGA_CHUNK + lane], p1 = Ps[qi * MEGA_CHUNK + lane + 32];
-        const float m = warp_max(fmaxf(p0, p1));
-        const float e0 = (p0 == -INFINITY) ? 0.f : expf(p0 - m);
-        const float e1 = (p1 == -INFINITY) ? 0.f : expf(p1 - m);
+        const int pos = rows[r0 + rr].y;
+        const int lor = local ? max(0, pos - WINDOW + 1) : 0;
+        const float* q = qs + qi * DH;
+        // scores: lane holds keys lane and lane + 32 of the chunk. A cached row in a ring tile is
+        // read in rotated pair order (pair (j + lane) mod 32 at step j: one bank per lane)
+        float sc[2];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int kk = lane + 32 * half;
+            const int key = k0 + kk;
+            float v = -INFINITY;
+            if (kk < nk && key <= pos && key >= lor) {
+                float acc = 0.f;
+                if (TILES && kk < nold) {
+                    const KVT* row = kt[kk / KPT] + (kk % KPT) * ROW;
+#pragma unroll 8
+                    for (int j = 0; j < DH / 2; ++j) {
+                        const int w = (j + lane) & (DH / 2 - 1);
+                        const float2 kv2 = kv_pair(row, w);
+                        const float2 q2 = reinterpret_cast<const float2*>(q)[w];
+                        acc += q2.x * kv2.x + q2.y * kv2.y;
+                    }
+                } else {
+                    const float* row = Ks + kk * (DH + 1);
+#pragma unroll 16
+                    for (int d = 0; d < DH; ++d) acc += q[d] * row[d];
+                }
+                v = acc;
+            }
+            sc[half] = v;
+        }
+        const float m = warp_max(fmaxf(sc[0], sc[1]));   // -inf: no key of the chunk is visible to this row
+        const float e0 = (sc[0] == -INFINITY) ? 0.f : expf(sc[0] - m);
+        const float e1 = (sc[1] == -INFINITY) ? 0.f : expf(sc[1] - m);
         const float lsum = warp_sum(e0 + e1);
-        Ps[qi * MEGA_CHUNK + lane] = e0;
-        Ps[qi * MEGA_CHUNK + lane + 32] = e1;
+        // P.V: lane holds dimensions 2 lane, 2 lane + 1; keys in order
+        float o0 = 0.f, o1 = 0.f;
+        for (int kk = 0; kk < nk; ++kk) {
+            const float pw = __shfl_sync(0xffffffffu, kk < 32 ? e0 : e1, kk & 31);
+            if (pw == 0.f) continue;   // warp-uniform: masked key
+            float2 v2;
+            if (TILES && kk < nold) {
+                v2 = kv_pair(vt[kk / KPT] + (kk % KPT) * ROW, lane);
+            } else {
+                const float* row = Vs + kk * (DH + 1);
+                v2 = make_float2(row[2 * lane], row[2 * lane + 1]);
+            }
+            o0 += pw * v2.x;
+            o1 += pw * v2.y;
+        }
         uint2* out = xpart(a, l, r0 + rr, h, c);
         if (lane == 0) {
-            ll_st(out, m, f);   // -inf: no key of the chunk is visible to this row (weights all 0)
-            ll_st(out + 1, m == -INFINITY ? 0.f : lsum, f);
+            ll_st(out, m, pf);
+            ll_st(out + 1, m == -INFINITY ? 0.f : lsum, pf);
         }
+        ll_st(out + 2 + 2 * lane, o0, pf);
+        ll_st(out + 3 + 2 * lane, o1, pf);
     }
-    named_bar_sync(1, MEGA_NCT);
-    astamp(a, l, 4, first);
-    // 5) P.V. Several rows: a thread per (dimension, row) covers the row's four heads (float4
-    //    weight loads); one row: a thread per (query, dimension), keys in order
-    if (nq >= 2 * GQA) {
-        for (int e = tid; e < nr * DH; e += MEGA_NCT) {
-            const int rq = e / DH, d = e % DH;
-            float o[GQA] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-            for (int kk = 0; kk < MEGA_CHUNK; kk += 4) {
-                const float v0 = Vs[kk * (DH + 1) + d], v1 = Vs[(kk + 1) * (DH + 1) + d];
-                const float v2 = Vs[(kk + 2) * (DH + 1) + d], v3 = Vs[(kk + 3) * (DH + 1) + d];
-#pragma unroll
-                for (int i = 0; i < GQA; ++i) {
-                    const float4 pw = *reinterpret_cast<const float4*>(Ps + (rq * GQA + i) * MEGA_CHUNK + kk);
-                    o[i] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < GQA; ++i) ll_st(xpart(a, l, r0 + rq, g * GQA + i, c) + 2 + d, o[i], f);
-        }
-    } else
-    for (int e = tid; e < nq * DH; e += MEGA_NCT) {
-        const int qi = e / DH, d = e % DH;
-        const int rr = qi / GQA, h = g * GQA + qi % GQA;
-        const float* pr = Ps + qi * MEGA_CHUNK;
-        float o = 0.f;
-#pragma unroll 16
-        for (int kk = 0; kk < MEGA_CHUNK; ++kk) o += pr[kk] * Vs[kk * (DH + 1) + d];
-        ll_st(xpart(a, l, r0 + rr, h, c) + 2 + d, o, f);
+    named_bar_sync(1, MEGA_NCT);   // every warp is done with the tiles and with Ks / Vs
+    if constexpr (TILES) {
+        if (threadIdx.x == 32 && ring.ok)
+            for (int i = 0; i < 2 * ntk; ++i) mbar_arrive(&s->empty[(ring.t + i) % MEGA_NS]);
+        ring.t += 2 * ntk;
     }
-    named_bar_sync(1, MEGA_NCT);
-    astamp(a, l, 5, first);
+    astamp(a, l, 3, first);
 }
 
 // Merge the chunk partials (m, l, o[64]) of query head h of row r, apply the gate, publish
-// att[r][h*64 ..]: consumer warps take chunks cw, cw + 15, ... (online softmax merge), then
-// warp 0 merges the 15 warp states in warp order.
+// att[r][h*64 ..]: every consumer thread takes part of the partials in one batched poll into
+// shared memory; warp 0 then forms the softmax weights of the chunks and the weighted sums.
 static __device__ __noinline__ void attn_merge(const MegaArgs& a, MegaSmem* s, int l, int r, int h, int nch,
                                                unsigned f, bool& ok) {
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
-    float M = -INFINITY, Ls = 0.f, o1 = 0.f, o2 = 0.f;
-    for (int c = cw; c < nch; c += MEGA_NCW) {
-        const uint2* q = xpart(a, l, r, h, c);
-        float mc, lc, a1, a2;
-        ll_get2(a, s, q, q + 1, f, ok, mc, lc);
-        ll_get2(a, s, q + 2 + lane, q + 2 + 32 + lane, f, ok, a1, a2);
-        if (mc == -INFINITY) continue;
-        const float Mn = fmaxf(M, mc);
-        const float so = expf(M - Mn), sn = expf(mc - Mn);
-        Ls = Ls * so + lc * sn;
-        o1 = o1 * so + a1 * sn;
-        o2 = o2 * so + a2 * sn;
-        M = Mn;
-    }
-    float* st = s->stage + cw * PART;   // [15][66]
-    if (lane == 0) {
-        st[0] = M;
-        st[1] = Ls;
-    }
-    st[2 + lane] = o1;
-    st[2 + 32 + lane] = o2;
+    float* P = s->xs;   // [nch][PART]; xs is free between the attention items and phase C
+    ll_fetch(a, s, xpart(a, l, r, h, 0), nch * PART / 2, part_flag(f, l), P, ok);
     named_bar_sync(1, MEGA_NCT);
     if (cw == 0) {
         const float graw = ll_get(a, s, xgate(a, l, r) + h, f, ok);
-        // lane w < 15 holds warp w's (m, l); the weights exp(m_w - max) are computed in
-        // parallel and broadcast, so the fold below is FMAs only
-        const float mw = lane < MEGA_NCW ? s->stage[lane * PART] : -INFINITY;
-        const float lw = lane < MEGA_NCW ? s->stage[lane * PART + 1] : 0.f;
-        const float Mx = warp_max(mw);
-        const float ww = (mw == -INFINITY) ? 0.f : expf(mw - Mx);
-        const float L = warp_sum(ww * lw);
+        float mx = -INFINITY;
+        for (int c = lane; c < nch; c += 32) mx = fmaxf(mx, P[c * PART]);
+        const float M = warp_max(mx);
+        float lsum = 0.f;
+        for (int c = lane; c < nch; c += 32) {
+            const float m = P[c * PART];
+            const float w = (m == -INFINITY) ? 0.f : expf(m - M);
+            s->stage[c] = w;
+            lsum += w * P[c * PART + 1];
+        }
+        const float Ls = warp_sum(lsum);
+        __syncwarp();
         float p1 = 0.f, p2 = 0.f;
-#pragma unroll
-        for (int w = 0; w < MEGA_NCW; ++w) {
-            const float wt = __shfl_sync(0xffffffffu, ww, w);
-            const float* q = s->stage + w * PART;
-            p1 += wt * q[2 + lane];
-            p2 += wt * q[2 + 32 + lane];
+        for (int c = 0; c < nch; ++c) {
+            const float w = s->stage[c];
+            p1 += w * P[c * PART + 2 + lane];
+            p2 += w * P[c * PART + 2 + 32 + lane];
         }
         const float gt = sigmoidf_(graw);
-        const float inv = 1.f / L;
+        const float inv = 1.f / Ls;
         uint2* out = xatt(a, l, r) + h * DH;
         ll_st(out + lane, (p1 * inv) * gt, f);
         ll_st(out + 32 + lane, (p2 * inv) * gt, f);

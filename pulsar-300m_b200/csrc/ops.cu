@@ -383,12 +383,44 @@ static __device__ __align__(256) float g_router_scratch[kRouterScratchFloats];
 
 namespace {
 constexpr int kMaxDevices = 64;
-float* g_router_scratch_ptr[kMaxDevices] = {};
+struct ScratchAddr {
+    unsigned long long ctx_id;   // unique id of the context the address belongs to (0: none yet)
+    float* ptr;
+};
+ScratchAddr g_router_scratch_addr[kMaxDevices] = {};
 std::mutex g_router_scratch_mu;
 
-// Device address of g_router_scratch on the current device. Host code cannot use the
-// symbol's name as a device pointer, so the address is looked up once per device (with that
-// device current) and cached.
+// Unique id of the calling thread's current context (0 when none is current or the driver does
+// not export the calls). The driver functions are reached through the runtime, so the library
+// does not link the driver library itself.
+unsigned long long current_context_id() {
+    using CtxGetCurrent = int (*)(void**);
+    using CtxGetId = int (*)(void*, unsigned long long*);
+    static CtxGetCurrent get_current = nullptr;
+    static CtxGetId get_id = nullptr;
+    static bool resolved = false;
+    if (!resolved) {   // under g_router_scratch_mu
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrent>(f);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetId>(f);
+        resolved = true;
+    }
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+    return id;
+}
+
+// Device address of g_router_scratch in the current context. Host code cannot use the
+// symbol's name as a device pointer, so the address is looked up with the device current and
+// cached per device together with the id of the context it was looked up in; a different
+// context (after cudaDeviceReset, say, the module is loaded again and the array may move) looks
+// it up again. Without context ids the address is looked up on every call.
 int router_scratch(float** out) {
     int dev = 0;
     PULSAR_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
@@ -397,12 +429,15 @@ int router_scratch(float** out) {
         return PULSAR_ERR_UNSUPPORTED;
     }
     std::lock_guard<std::mutex> lock(g_router_scratch_mu);
-    if (!g_router_scratch_ptr[dev]) {
+    ScratchAddr& c = g_router_scratch_addr[dev];
+    const unsigned long long id = current_context_id();
+    if (id == 0 || c.ctx_id != id || !c.ptr) {
         void* p = nullptr;
         PULSAR_TRY(cuda_status(cudaGetSymbolAddress(&p, g_router_scratch), "cudaGetSymbolAddress(router scratch)"));
-        g_router_scratch_ptr[dev] = static_cast<float*>(p);
+        c.ptr = static_cast<float*>(p);
+        c.ctx_id = current_context_id();   // the lookup makes the device's primary context current
     }
-    *out = g_router_scratch_ptr[dev];
+    *out = c.ptr;
     return PULSAR_OK;
 }
 }  // namespace

@@ -36,9 +36,7 @@ struct TcSmem {
     alignas(1024) __nv_bfloat16 a_lo[TC_STAGES][TC_BM * TC_BK];
     alignas(1024) __nv_bfloat16 w[TC_STAGES][BN * TC_BK];
     uint64_t mma_done[TC_STAGES];
-    uint64_t final_done;
     uint32_t tmem_base;
-    int err;
 };
 
 // Byte offset of element (row, k) (k < 64) inside a canonical K-major no-swizzle tile.
@@ -182,8 +180,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, const __n
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < TC_STAGES; ++i) mbar_init(&s->mma_done[i], 1);
-        mbar_init(&s->final_done, 1);
-        s->err = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -204,11 +200,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, const __n
         if (c < nk) tc_issue_chunk<EPI, BN>(g, ahi, alo, s, c, b, m0, m_valid, n_tile, c);
         tc_commit_group();
     }
+    // A bounded wait that runs out ends the K loop for the whole CTA (the OR at the next
+    // barrier): no further copies or MMAs are issued. The results of such a launch are invalid;
+    // its tensor memory is read and released only after the last committed MMA group has been
+    // waited for (or that wait has run out too).
+    bool err = false;
+    int last = -1;   // last chunk whose MMAs were committed
     for (int kc = 0; kc < nk; ++kc) {
         const int st = kc % TC_STAGES;
         tc_wait_group<TC_STAGES - 2>();   // chunk kc landed (this thread's copies)
         tc_fence_proxy_async();           // -> visible to the tensor core (async proxy)
-        __syncthreads();
+        if (__syncthreads_or(err)) break;
         if (threadIdx.x == 0) {
             tc_fence_after();
             const uint32_t ah = smem_u32(s->a_hi[st]), al = smem_u32(s->a_lo[st]), wb = smem_u32(s->w[st]);
@@ -219,23 +221,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, const __n
                 tc_mma(tmem, tc_desc(al + ks * 256), bd, idesc, 1u);
             }
             tc_commit(&s->mma_done[st]);
-            if (kc == nk - 1) tc_commit(&s->final_done);
         }
+        last = kc;
         // refill the stage of chunk kc-1 with chunk kc+STAGES-1 once that chunk's MMAs are done
         const int nc = kc + TC_STAGES - 1;
         if (nc < nk) {
             if (kc >= 1) {
                 const int ps = (kc - 1) % TC_STAGES;
-                if (!mbar_wait(&s->mma_done[ps], ((kc - 1) / TC_STAGES) & 1)) s->err = 1;
+                if (!mbar_wait(&s->mma_done[ps], ((kc - 1) / TC_STAGES) & 1)) err = true;
             }
-            tc_issue_chunk<EPI, BN>(g, ahi, alo, s, nc % TC_STAGES, b, m0, m_valid, n_tile, nc);
+            if (!err) tc_issue_chunk<EPI, BN>(g, ahi, alo, s, nc % TC_STAGES, b, m0, m_valid, n_tile, nc);
         }
         tc_commit_group();
     }
-    if (!mbar_wait(&s->final_done, 0)) s->err = 1;
+    tc_wait_group<0>();   // this thread's copies have landed (none is left in flight at exit)
+    if (last >= 0 && !mbar_wait(&s->mma_done[last % TC_STAGES], (last / TC_STAGES) & 1)) err = true;
+    if (last != nk - 1) err = true;
     tc_fence_after();
-    __syncthreads();
-    if (s->err) {
+    if (__syncthreads_or(err)) {
         if (threadIdx.x == 0) atomicExch(err_flag, 1);
     } else {
         // epilogue: warp w holds rows 32w..32w+31 (lanes), 16 columns per load

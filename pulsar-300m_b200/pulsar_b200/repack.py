@@ -46,6 +46,9 @@ def read(path: str):
         raise ValueError(f"{path}: not a pulsar_b200 repacked arena (format {meta.get('format')!r})")
     end = 0
     for name, h in sorted(header.items(), key=lambda kv: kv[1]["data_offsets"][0]):
+        if h.get("dtype") not in _ITEM:
+            raise ValueError(f"{path}: tensor {name} has dtype {h.get('dtype')!r}; a repacked arena holds only "
+                             f"{', '.join(sorted(_ITEM))}")
         b0, b1 = h["data_offsets"]
         n = 1
         for d in h["shape"]:

@@ -42,3 +42,15 @@ def test_rejects_size_mismatch_and_foreign_files(tmp_path):
         f.write(b"junk")
     with pytest.raises(ValueError, match="trailing"):
         repack.read(p2)
+
+
+def test_rejects_foreign_dtype(tmp_path):
+    """A file with our format tag but a dtype the arena never holds fails validation with a
+    ValueError naming the tensor (not a bare KeyError)."""
+    p = tmp_path / "f16.safetensors"
+    h = json.dumps({"__metadata__": {"format": repack.FORMAT},
+                    "t": {"dtype": "F16", "shape": [2], "data_offsets": [0, 4]}}).encode()
+    h += b" " * (-len(h) % 8)
+    p.write_bytes(struct.pack("<Q", len(h)) + h + bytes(4))
+    with pytest.raises(ValueError, match="tensor t has dtype 'F16'"):
+        repack.read(str(p))
