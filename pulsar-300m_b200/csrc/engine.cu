@@ -538,12 +538,11 @@ struct pulsar_engine {
     // persistent pulse kernel
     bool use_mega = false;
     int mega_grid = 0, mega_nch = 0;
-    MegaX mx{};                 // exchange buffers of the persistent kernel (flag-carrying units)
-    float* m_pmax = nullptr;
+    float *m_gate = nullptr, *m_part = nullptr, *m_g8 = nullptr, *m_pmax = nullptr, *m_rpart = nullptr;
     int *m_pidx = nullptr, *m_err = nullptr;
-    unsigned *m_epoch = nullptr, *m_tickets = nullptr;   // launch counter (flag of the next launch - 1), tickets
+    unsigned *m_bar = nullptr, *m_tickets = nullptr;
     unsigned long long mega_wait_ns = WAIT_NS;   // option "wait_ns": bound of every wait in the persistent kernel
-    int mega_stall_cta = -1;                     // option "stall_cta": test hook (a CTA whose layer-0 wait runs out)
+    int mega_stall_cta = -1;                     // option "stall_cta": test hook (a CTA whose first grid barrier runs out)
     unsigned long long* m_trace = nullptr;   // phase stamps of the last traced launch (option "trace")
     unsigned long long* m_experts = nullptr; // distinct routed experts streamed by persistent launches
 
@@ -803,8 +802,19 @@ int pulse_mega(pulsar_engine* e, int p, int R, const int4* rows, const float* h_
     a.pmax = e->m_pmax;
     a.pidx = e->m_pidx;
     a.nch_max = e->mega_nch;
-    a.x = e->mx;
-    a.epoch = e->m_epoch;
+    auto& w = e->w;
+    a.h = w.h;
+    a.h_in = w.h_in;
+    a.qkv = w.qkv;
+    a.gate = e->m_gate;
+    a.att = w.att;
+    a.act_sh = w.act_sh;
+    a.act_r = w.act_r;
+    a.part = e->m_part;
+    a.vfirst = w.vfirst;
+    a.g8 = e->m_g8;
+    a.rpart = e->m_rpart;
+    a.bar = e->m_bar;
     a.tickets = e->m_tickets;
     a.wait_ns = e->mega_wait_ns;
     a.stall_cta = e->mega_stall_cta;
@@ -1093,8 +1103,9 @@ int check_kernel_err(pulsar_engine* e) {
     PULSAR_TRY(cuda_status(cudaMemcpy(&v, e->m_err, 4, cudaMemcpyDeviceToHost), "read error flag"));
     if (v) {
         cudaMemset(e->m_err, 0, 4);
-        cudaMemset(e->m_tickets, 0, 2 * 4);
-        set_error("a bounded device wait ran out (persistent pulse kernel data exchange or weight stream, or a "
+        cudaMemset(e->m_bar, 0, 4);
+        cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 2) * 4);
+        set_error("a bounded device wait ran out (persistent pulse kernel grid barrier or weight stream, or a "
                   "tensor-core GEMM's MMA completion); results of the affected launch are invalid");
         return PULSAR_ERR_CUDA;
     }
@@ -1409,31 +1420,17 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         e->mega_grid = sms;
         e->use_mega = per_sm >= 1 && sms >= 144;
         e->mega_nch = std::max(2400 / 32 + 2, (maxlen + MEGA_CHUNK - 1) / MEGA_CHUNK + 2);   // see attn_chunk()
-        // exchange units: zeroed below, so no unit carries a launch's flag (>= 1) before it is stored
-        auto& X = e->mx;
-        const size_t n_h = (size_t)NL * 2 * MEGA_RMAX * D, n_qkv = (size_t)NL * MEGA_RMAX * QKV,
-                     n_gate = (size_t)NL * MEGA_RMAX * H, n_part = (size_t)2 * MEGA_RMAX * H * e->mega_nch * PART,
-                     n_att = (size_t)NL * MEGA_RMAX * D, n_act = (size_t)NL * MEGA_RMAX * MEGA_ACT,
-                     n_vf = (size_t)MEGA_RMAX * HKV * DH, n_lt = (size_t)NL * 2 * MEGA_RMAX * LORA_R;
-        const size_t n_x = n_h + n_qkv + n_gate + n_part + n_att + n_act + n_vf + n_lt;
-        uint2* xb = nullptr;
-        if ((st = e->wmalloc(&xb, n_x)) || (st = cuda_status(cudaMemset(xb, 0, n_x * sizeof(uint2)), "zero exchange")))
-            return fail(st);
-        X.h = xb;
-        X.qkv = X.h + n_h;
-        X.gate = X.qkv + n_qkv;
-        X.part = X.gate + n_gate;
-        X.att = X.part + n_part;
-        X.act = X.att + n_att;
-        X.vfirst = X.act + n_act;
-        X.lt = X.vfirst + n_vf;
-        if ((st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
+        if ((st = e->wmalloc(&e->m_gate, (size_t)MEGA_RMAX * H)) ||
+            (st = e->wmalloc(&e->m_part, (size_t)MEGA_RMAX * H * e->mega_nch * PART)) ||
+            (st = e->wmalloc(&e->m_g8, (size_t)MEGA_RMAX * RG)) ||
+            (st = e->wmalloc(&e->m_rpart, (size_t)std::max(sms, 1) * MEGA_RMAX * E)) ||
+            (st = e->wmalloc(&e->m_pmax, (size_t)MEGA_RMAX * std::max(sms, 1))) ||
             (st = e->wmalloc(&e->m_pidx, (size_t)MEGA_RMAX * std::max(sms, 1))) || (st = e->wmalloc(&e->m_err, 1)) ||
-            (st = e->wmalloc(&e->m_epoch, 1)) || (st = e->wmalloc(&e->m_tickets, 2)) ||
+            (st = e->wmalloc(&e->m_bar, 1)) || (st = e->wmalloc(&e->m_tickets, (size_t)MEGA_RMAX * HKV + 2)) ||
             (st = e->wmalloc(&e->m_experts, 1)))
             return fail(st);
-        if ((st = cuda_status(cudaMemset(e->m_tickets, 0, 2 * 4), "zero tickets")) ||
-            (st = cuda_status(cudaMemset(e->m_epoch, 0, 4), "zero launch counter")) ||
+        if ((st = cuda_status(cudaMemset(e->m_tickets, 0, ((size_t)MEGA_RMAX * HKV + 2) * 4), "zero tickets")) ||
+            (st = cuda_status(cudaMemset(e->m_bar, 0, 4), "zero grid barrier")) ||
             (st = cuda_status(cudaMemset(e->m_err, 0, 4), "zero err")) ||
             (st = cuda_status(cudaMemset(e->m_experts, 0, 8), "zero expert count")))
             return fail(st);

@@ -84,45 +84,4 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Named barrier that also ORs a predicate over the participating threads: every thread gets
-// the same answer, so a branch on it is uniform (no thread can miss a later barrier).
-__device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(id), "r"(nthreads)
-        : "memory");
-    return r != 0;
-}
-
-// ---- flag-carrying exchange between CTAs of one launch (the LL protocol of NCCL's low-
-// latency transport, on one GPU). A unit is 8 bytes {float value, u32 flag} written by ONE
-// 8-byte store, so a reader that sees the flag of the current launch also sees the value
-// stored with it; no fence or counter is involved and a consumer polls the data itself.
-// Stores and loads are volatile (they go to L2, the coherence point, not to L1). A 16-byte
-// load covers two units and is complete when both flags match.
-__device__ __forceinline__ void ll_st(uint2* p, float v, unsigned flag) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(flag)
-                 : "memory");
-}
-
-__device__ __forceinline__ uint2 ll_ld(const uint2* p) {
-    uint2 r;
-    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
-    return r;
-}
-
-__device__ __forceinline__ uint4 ll_ld2(const uint4* p) {
-    uint4 r;
-    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p)
-                 : "memory");
-    return r;
-}
-
 }  // namespace pulsar

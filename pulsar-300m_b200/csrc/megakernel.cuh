@@ -1,44 +1,36 @@
 // Persistent per-pulse decode kernel (one CTA per SM, cooperative launch).
 //
 // One launch runs a whole pulse pass (src/infer.py:463-524) for R <= MEGA_RMAX rows: the
-// pulse input, 8 layers x 6 phases, the end-of-pulse residual, the final norm and, when
-// logits or argmax are requested, the LM head with argmax.
+// pulse input, 8 layers x 6 phases separated by grid barriers, the end-of-pulse residual,
+// the final norm and, when logits or argmax are requested, the LM head with argmax.
 //
 // Warp 0 is the producer: one lane streams every weight tile this CTA will consume, in
 // consumption order, through a ring of NS 8 KB shared-memory slots with 1-D TMA bulk copies
 // (cp.async.bulk + mbarrier complete_tx). Weights do not depend on activations, so the
-// producer runs ahead across phases (only the routed-expert tiles wait for this layer's
-// router, signalled through shared memory). Warps 1..15 are consumers: tile t of the CTA's
-// stream lives in slot t % NS and is consumed by warp t % 15.
+// producer runs ahead across grid barriers (only the routed-expert tiles wait for this
+// layer's router, computed from a flag in shared memory). Warps 1..15 are consumers: tile t
+// of the CTA's stream lives in slot t % NS and is consumed by warp t % 15.
 //
-// CTAs hand data to each other through exchange buffers of 8-byte units {value, flag}
-// (mega_ptx.cuh, ll_st / ll_ld): the flag is this launch's epoch, so a consumer polls the
-// data it needs until every unit carries the epoch. There is no grid-wide barrier: each phase
-// waits only for the values it reads, one L2 round trip after the producer stored them.
-// Every buffer region is written once per launch (per-layer regions; the attention partials
-// alternate between two regions, which the data dependencies of the layers in between keep
-// apart: a layer-l+2 item needs layer-l+2 QKV rows from CTAs that have consumed layer l+1's
-// h, which every merging CTA publishes only after its layer-l merges).
-//
-// Phases per layer (outputs split evenly over the CTAs; h rows [own0, own1) of every row are
-// owned by one CTA, which keeps them in shared memory):
-//   A  xn = RMSNorm(h) (h polled from the previous layer's E, or the pulse input); QKV GEMV
-//      rows -> qkv units; gate logits xn.Wg + b on the last 8 CTAs -> gate units. With a live
-//      loop adapter, CTAs < MEGA_TDES first compute two rows each of t = A xn and publish
-//      them; the QKV rows add Bs t once t is complete.
-//   B  attention items (sequence block, kv head, key chunk): q of the 4 heads via
-//      QK-RMSNorm + RoPE (+YaRN); the block rows' own K/V (norm, RoPE, value residual) written
-//      to the cache by the item that owns their chunk; cached keys of the chunk through the
-//      weight ring for passes of <= 2 rows; split-K partials (m, l, o[64]) per head and chunk
+// Phases per layer (work split evenly over the CTAs, outputs owned by one CTA each; h rows
+// [own0, own1) of every sequence row are owned by one CTA, kept in its shared memory):
+//   A  xn = RMSNorm(h); QKV GEMV rows (with a live loop adapter every CTA first computes
+//      t = A xn from the 24 fp32 A rows streamed through the ring, and the QKV rows add Bs t;
+//      phase C does the same for Wo on the attention output)
+//   B  gate logits xn.Wg + b on the last 8 CTAs (which usually have no attention item);
+//      attention items (sequence block, kv head, key chunk): q of the 4 heads via
+//      QK-RMSNorm + RoPE (+YaRN); block rows' K/V produced (norm, RoPE, value residual)
+//      and written to the cache by the item that owns their chunk; the cached keys of the
+//      chunk arrive through the weight ring for passes of <= 2 rows (issued during phase A);
+//      split-K partials (m, l, o[64]) per query head and chunk
 //   B2 one CTA per (row, query head) merges its chunk partials in a fixed order and applies
-//      the gate sigmoid -> att units
-//   C  att polled; Wo GEMV (+ adapter), h += (owned rows) -> h units
-//   D  h polled; m = RMSNorm(h); router logits from the fp32 router rows (streamed through
-//      the ring; the same arithmetic in every CTA, so every CTA picks the same experts);
-//      top-4; shared + routed (distinct experts) gate/up GEMVs, SwiGLU -> act units
-//   E  act polled; shared + routed down GEMVs of the owned rows, combine in top-k order,
-//      h += -> h units (the last layer publishes the pulse output h_in + (h - h_in) * res_scale)
-// Then: the pulse output polled, final RMSNorm, LM head rows, argmax.
+//      the gate sigmoid
+//   C  Wo GEMV, h += (owned rows); partial router logits of the owned rows
+//      z[r][e] = sum_o router[e][o] * mlp_norm[o] * h[r][o]
+//   D  m = RMSNorm(h); router logits = (sum of the CTAs' z in CTA order) / rms(h) (every
+//      CTA, identical result); top-4; shared + routed (distinct experts) gate/up GEMVs with
+//      the SwiGLU epilogue
+//   E  shared + routed down GEMVs for owned output rows, combine in top-k order, h +=
+// Then: h_out = h_in + (h - h_in) * res_scale, final RMSNorm, LM head rows, argmax.
 #pragma once
 
 #include "kv.cuh"
@@ -52,26 +44,11 @@ constexpr int MEGA_NCT = MEGA_NCW * 32;   // consumer threads
 constexpr int MEGA_NS = 18;               // ring slots
 constexpr int MEGA_SLOT = 8192;           // bytes per slot
 constexpr int MEGA_RMAX = 5;              // rows per pass
-constexpr int MEGA_ACT = DS + TOPK * DE;  // activations per row entering the down projections
-constexpr int MEGA_XS = MEGA_RMAX * MEGA_ACT;   // floats of the per-CTA activation staging
+constexpr int MEGA_XS = MEGA_RMAX * 3072; // floats: act_sh [R][1024] + act_r [R][4][512]
 constexpr int MEGA_STAGE = 2048;          // floats
 constexpr int MEGA_CHUNK = 64;            // keys per attention item
 constexpr int MEGA_MAXPAIRS = 64;         // phase-D output pairs per CTA (>= ceil((1024+16*512)/C))
 constexpr int MEGA_MAXOROWS = 8;          // phase-E output rows per CTA (>= ceil(1024/C))
-constexpr int MEGA_TDES = LORA_R / 2;     // CTAs computing the loop-adapter factor t (2 rows each)
-
-// Exchange buffers: units of {float, epoch} (zeroed at engine creation, so no unit carries a
-// valid epoch before its first store).
-struct MegaX {
-    uint2* h;       // [NL][2][RMAX][D]: after phase C (0) and phase E (1)
-    uint2* qkv;     // [NL][RMAX][QKV]
-    uint2* gate;    // [NL][RMAX][H]
-    uint2* part;    // [2][RMAX][H][nch_max][PART]
-    uint2* att;     // [NL][RMAX][D]
-    uint2* act;     // [NL][RMAX][MEGA_ACT]: shared SwiGLU (DS), then routed (TOPK x DE)
-    uint2* vfirst;  // [RMAX][HKV][DH]
-    uint2* lt;      // [NL][2][RMAX][LORA_R]: loop-adapter t of wqkv (0) and wo (1)
-};
 
 struct MegaArgs {
     int R, pulse, n_slots, max_pos, V, use_conv, base_seq_len;
@@ -92,18 +69,19 @@ struct MegaArgs {
     float *h_out, *h0n_out, *logits;
     int hstride;          // row stride (rows of D floats) of h_out and h0n_out
     int* amax;
-    MegaX x;
-    int nch_max;          // chunks per (row, head) in x.part
-    float* pmax;          // LM head: per-CTA argmax partials [R][grid]
+    // global workspace
+    float *h, *h_in, *qkv, *gate, *att, *act_sh, *act_r, *part, *vfirst, *g8, *pmax;
+    float* rpart;         // router partial sums [grid][R][E] of the owned h rows (phase C)
     int* pidx;
-    unsigned* epoch;      // launch counter: this launch's flag is *epoch + 1; the last CTA out increments it
-    unsigned* tickets;    // [0] argmax ticket, [1] leave ticket (both self-resetting)
+    int nch_max;          // chunks per (row, head) in `part`
+    unsigned* bar;        // grid barrier counter (zeroed before launch)
+    unsigned* tickets;    // [MEGA_RMAX * HKV + 2]: [.. + 0] argmax ticket, [.. + 1] exit count (both self-resetting)
     int* err;             // error flag (non-zero: a bounded wait ran out)
     unsigned long long wait_ns;   // bound of every wait
-    int stall_cta;        // test hook: this CTA (>= 0) waits in layer 0 for units nobody stores
-    unsigned long long* experts;  // running count of distinct routed experts streamed (per layer)
+    int stall_cta;        // test hook: this CTA (>= 0) waits at its first grid barrier for one arrival too many
+    unsigned long long* experts;   // running count of distinct routed experts streamed (per layer)
     const int* skip;      // optional: non-zero -> the whole pass is skipped (every row exited early)
-    unsigned long long* trace;    // optional [gridDim][MEGA_TRACE] %globaltimer stamps (null: off)
+    unsigned long long* trace;   // optional [gridDim][MEGA_TRACE] %globaltimer stamps (null: off)
 };
 
 constexpr int MEGA_TRACE = 256;   // stamps per CTA: [0] start, [1 + 16*l + j] phase points of layer l, [255] end
@@ -111,7 +89,6 @@ constexpr int MEGA_TRACE = 256;   // stamps per CTA: [0] start, [1 + 16*l + j] p
 struct MegaSmem {
     uint64_t full[MEGA_NS];
     uint64_t empty[MEGA_NS];
-    float rlog[MEGA_RMAX][E];     // router logits (raw) per (row, expert)
     float logits[MEGA_RMAX][E];   // router: score + bias per (row, expert)
     float rsg[MEGA_RMAX][E];      // router: sigmoid score per (row, expert)
     float wts[MEGA_RMAX][TOPK];
@@ -121,31 +98,36 @@ struct MegaSmem {
     int n_e;
     volatile int moe_ready;
     int ticket;
-    volatile int abort;
+    int abort;
     alignas(128) unsigned char ring[MEGA_NS][MEGA_SLOT];
     alignas(16) float xs[MEGA_XS];
     alignas(16) float stage[MEGA_STAGE];
     float wout[MEGA_NCW][4 * MEGA_RMAX];   // per-warp reduced tile sums
     int xoff[MEGA_RMAX];                   // X row offsets (elements into xs) of the current phase
-    int xoff_e[E][MEGA_RMAX];              // phase E: per routed expert, act row of each row or -1
+    int xoff_e[E][MEGA_RMAX];              // phase E: per routed expert, act_r row of each row or -1
     int eslot[MEGA_RMAX][TOPK];            // phase E: position of expert idx[r][k] in the expert list
     int blk_r0[MEGA_RMAX + 1];             // sequence blocks of the rows: start row
     int blk_nch[MEGA_RMAX];                // attention chunks per (block, head group)
     int blk_chunk[MEGA_RMAX];
     int n_blk;
-    int4 rows[MEGA_RMAX];                  // the row descriptors
+    int4 rows[MEGA_RMAX];                  // the row descriptors (read everywhere; L1 holds little here)
+    float rwn[NL][E][MEGA_MAXOROWS];       // router weight x mlp-norm weight of the owned h rows
     float hown[MEGA_MAXOROWS * MEGA_RMAX]; // owned h rows [row - o0][R] (this CTA is their only writer)
-    float hin[MEGA_MAXOROWS * MEGA_RMAX];  // the pulse input of the owned rows
-    float g8[MEGA_RMAX][RG];               // re-injection gate (pulses > 0)
-    alignas(16) float lt[MEGA_RMAX * LORA_R];   // loop-adapter t of the current GEMV
-    float nred[D / 128];                   // norm (one row): sums of squares of the 128-element slices
+    float rinv[MEGA_RMAX];                 // 1 / rms of h per row (phase D)
+    float nred[D / 128];                   // norm_rows (one row): sums of squares of the 128-element slices
     float rsc[NL][MEGA_MAXOROWS];          // routed_scale of the owned h rows
     float ebias[NL][E];                    // expert bias of every layer (router top-k)
     float rope[2][MEGA_RMAX][DH];          // [local, global][row]: cos (32) then sin (32) at the row's position
+    alignas(16) float lt[MEGA_RMAX * LORA_R];   // loop-adapter factor t = A x of the current GEMV
 };
 
 __device__ __forceinline__ void stamp(const MegaArgs& a, int l, int j) {
     if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 1 + 16 * l + j] = globaltimer();
+}
+
+// router-phase sub-steps of layer l (entries 206 + 5*l + k, k < 5)
+__device__ __forceinline__ void rstamp(const MegaArgs& a, int l, int k) {
+    if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 206 + 5 * l + k] = globaltimer();
 }
 
 // attention-item sub-steps of the first item a CTA runs in layer l (entries 130 + 8*l + k)
@@ -158,147 +140,24 @@ __device__ __forceinline__ void rows_split(int N, int c, int C, int& r0, int& r1
     r1 = (int)(((long long)N * (c + 1)) / C);
 }
 
-// ------------------------------------------------------------------ exchange addressing
-__device__ __forceinline__ uint2* xh(const MegaArgs& a, int l, int which, int r) {
-    return a.x.h + (((int64_t)l * 2 + which) * MEGA_RMAX + r) * D;
-}
-__device__ __forceinline__ uint2* xqkv(const MegaArgs& a, int l, int r) { return a.x.qkv + ((int64_t)l * MEGA_RMAX + r) * QKV; }
-__device__ __forceinline__ uint2* xgate(const MegaArgs& a, int l, int r) { return a.x.gate + ((int64_t)l * MEGA_RMAX + r) * H; }
-__device__ __forceinline__ uint2* xpart(const MegaArgs& a, int l, int r, int h, int c) {
-    return a.x.part + ((((int64_t)(l & 1) * MEGA_RMAX + r) * H + h) * a.nch_max + c) * PART;
-}
-// Flag of the attention-partial units of layer l. Layers l and l + 2 share a region within one
-// launch, so these units carry the layer as well as the launch (a reader must not take a
-// layer-l unit for a layer-(l + 2) one).
-__device__ __forceinline__ unsigned part_flag(unsigned f, int l) { return (f << 3) | (unsigned)l; }
-__device__ __forceinline__ uint2* xatt(const MegaArgs& a, int l, int r) { return a.x.att + ((int64_t)l * MEGA_RMAX + r) * D; }
-__device__ __forceinline__ uint2* xact(const MegaArgs& a, int l, int r) {
-    return a.x.act + ((int64_t)l * MEGA_RMAX + r) * MEGA_ACT;
-}
-__device__ __forceinline__ uint2* xvfirst(const MegaArgs& a, int r, int g) { return a.x.vfirst + ((int64_t)r * HKV + g) * DH; }
-__device__ __forceinline__ uint2* xlt(const MegaArgs& a, int l, int which, int r) {
-    return a.x.lt + (((int64_t)l * 2 + which) * MEGA_RMAX + r) * LORA_R;
-}
-
-// ------------------------------------------------------------------ bounded polling
-// A failed wait raises the kernel's error flag and this CTA's abort flag; every later poll of
-// the CTA gives up at once, and the phase ends with a uniform branch to the exit.
-__device__ __forceinline__ void raise_abort(const MegaArgs& a, MegaSmem* s) {
-    if (!s->abort) {
-        s->abort = 1;
-        atomicExch(a.err, 1);
-    }
-}
-
-struct Poll {
-    unsigned long long t0 = 0;
-    unsigned it = 0;
-};
-
-// May this thread poll once more? No when the CTA aborted, another CTA raised the error flag
-// (read every 128th poll: an L2 round trip of its own) or the wait ran past a.wait_ns.
-__device__ __forceinline__ bool poll_more(const MegaArgs& a, MegaSmem* s, Poll& w) {
-    if (w.it++ == 0) {
-        w.t0 = globaltimer();
-        return true;
-    }
-    if ((w.it & 7) == 0) {
-        if (s->abort) return false;
-        if (globaltimer() - w.t0 > a.wait_ns) return false;
-        if ((w.it & 127) == 0 && *(volatile int*)a.err) return false;
-    }
-    return true;
-}
-
-// One unit's value once it carries flag f (ok cleared on a failed wait).
-__device__ __forceinline__ float ll_get(const MegaArgs& a, MegaSmem* s, const uint2* p, unsigned f, bool& ok) {
-    uint2 v = ll_ld(p);
-    if (v.y != f) {
-        Poll w;
-        do {
-            if (!ok || !poll_more(a, s, w)) {
-                ok = false;
-                raise_abort(a, s);
-                break;
-            }
-            v = ll_ld(p);
-        } while (v.y != f);
-    }
-    return __uint_as_float(v.x);
-}
-
-// Two units, both loads in flight before either is checked.
-__device__ __forceinline__ void ll_get2(const MegaArgs& a, MegaSmem* s, const uint2* p0, const uint2* p1, unsigned f,
-                                        bool& ok, float& v0, float& v1) {
-    uint2 u0 = ll_ld(p0), u1 = ll_ld(p1);
-    if (u0.y != f) {
-        Poll w;
-        do {
-            if (!ok || !poll_more(a, s, w)) { ok = false; raise_abort(a, s); break; }
-            u0 = ll_ld(p0);
-        } while (u0.y != f);
-    }
-    if (u1.y != f) {
-        Poll w;
-        do {
-            if (!ok || !poll_more(a, s, w)) { ok = false; raise_abort(a, s); break; }
-            u1 = ll_ld(p1);
-        } while (u1.y != f);
-    }
-    v0 = __uint_as_float(u0.x);
-    v1 = __uint_as_float(u1.x);
-}
-
-// Every consumer thread: poll 2 * nl units from src (16-byte aligned) until all carry flag f;
-// values to dst[0 .. 2 nl). Eight 16-byte loads per thread in flight before any is checked.
-// Not inlined: its registers do not add to the callers' (the phase bodies around it).
-static __device__ __noinline__ void ll_fetch(const MegaArgs& a, MegaSmem* s, const uint2* src, int nl, unsigned f,
-                                      float* dst, bool& ok) {
-    const int tid = threadIdx.x - 32;
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    for (int i0 = tid; i0 < nl; i0 += 8 * MEGA_NCT) {
-        uint4 v[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int i = i0 + k * MEGA_NCT;
-            if (i < nl) v[k] = ll_ld2(s4 + i);
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int i = i0 + k * MEGA_NCT;
-            if (i < nl) {
-                if (v[k].y != f || v[k].w != f) {
-                    Poll w;
-                    do {
-                        if (!ok || !poll_more(a, s, w)) { ok = false; raise_abort(a, s); break; }
-                        v[k] = ll_ld2(s4 + i);
-                    } while (v[k].y != f || v[k].w != f);
-                }
-                reinterpret_cast<float2*>(dst)[i] = make_float2(__uint_as_float(v[k].x), __uint_as_float(v[k].z));
-            }
-        }
-    }
-}
-
-// Bounded mbarrier wait that also gives up when the CTA aborted.
-__device__ __forceinline__ bool mbar_wait_ab(const MegaArgs& a, MegaSmem* s, uint64_t* bar, uint32_t parity) {
-    if (mbar_test(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer();
-    for (unsigned it = 1; !mbar_test(bar, parity); ++it) {
-        if ((it & 15) == 0 && (s->abort || globaltimer() - t0 > a.wait_ns)) return false;
-    }
-    return true;
-}
-
 // ------------------------------------------------------------------ tile stream
 // The producer and the consumers walk the same sequence of tiles; `Ring` keeps the counter.
 struct Ring {
     MegaSmem* s;
-    const MegaArgs* a;
     uint32_t t;     // tiles so far
     int warp;       // consumer warp index (0..14), or -1 for the producer
     bool ok;
+    unsigned long long wait_ns;   // bound of each wait
 };
+
+// Bounded mbarrier wait that also gives up once the CTA has aborted.
+__device__ __forceinline__ bool ring_wait(const Ring& g, uint64_t* bar, uint32_t parity) {
+    if (mbar_test(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (unsigned it = 1; !mbar_test(bar, parity); ++it)
+        if ((it & 15) == 0 && (g.s->abort || globaltimer() - t0 > g.wait_ns)) return false;
+    return true;
+}
 
 // Producer side: issue tiles covering rows [r0, r1) of a row-major matrix with row_bytes
 // bytes per row, rows_per_tile rows per tile.
@@ -308,7 +167,7 @@ __device__ __forceinline__ void produce_rows(Ring& g, const void* base, int row_
         const int n = min(rows_per_tile, r1 - r);
         const uint32_t slot = g.t % MEGA_NS;
         const uint32_t use = g.t / MEGA_NS;
-        if (use > 0 && !mbar_wait_ab(*g.a, g.s, &g.s->empty[slot], (use - 1) & 1)) { g.ok = false; break; }
+        if (use > 0 && !ring_wait(g, &g.s->empty[slot], (use - 1) & 1)) { g.ok = false; break; }
         const uint32_t bytes = (uint32_t)n * row_bytes;
         mbar_arrive_expect_tx(&g.s->full[slot], bytes);
         tma_load_1d(g.s->ring[slot], static_cast<const char*>(base) + (int64_t)r * row_bytes, bytes, &g.s->full[slot]);
@@ -326,9 +185,8 @@ __device__ __forceinline__ void consume_rows(Ring& g, int r0, int r1, int rows_p
         const uint32_t slot = g.t % MEGA_NS;
         const uint32_t use = g.t / MEGA_NS;
         if ((int)(g.t % MEGA_NCW) == g.warp && g.ok) {
-            if (!mbar_wait_ab(*g.a, g.s, &g.s->full[slot], use & 1)) {
+            if (!ring_wait(g, &g.s->full[slot], use & 1)) {
                 g.ok = false;
-                raise_abort(*g.a, g.s);
             } else {
                 fn(g.s->ring[slot], r, n);
                 __syncwarp();
@@ -408,8 +266,7 @@ __device__ __noinline__ void tile_gemv(const __nv_bfloat16* w, int nr, const flo
     __syncwarp();
 }
 
-// fp32 rows of D elements (router, gate, loop-adapter A), two rows per tile; same element
-// mapping, float4 weight loads. Lane i*R + r of out gets row i for X row r.
+// fp32 rows (router), two rows per tile; same element mapping, float4 weight loads.
 template <int R>
 __device__ __noinline__ void tile_gemv_f32(const float* w, int nr, const float* xbase, const int* xoff, float* out) {
     const int lane = threadIdx.x & 31;
@@ -447,18 +304,74 @@ __device__ __noinline__ void tile_gemv_f32(const float* w, int nr, const float* 
     __syncwarp();
 }
 
-// RMSNorm of R rows of xs in place with weight w. One row: every consumer thread takes a
-// float4, warps reduce their 128-element slices, the eight slice sums are added in order from
-// shared memory (red: 8 floats). More rows: one warp per row.
+// ------------------------------------------------------------------ loop adapter
+// t[r][j] = A[j] . X_r for the 24 fp32 adapter rows streamed through the ring (two per tile) and
+// the current GEMV input rows of xs, into s->lt; every CTA computes it (no exchange).
 template <int R>
-__device__ __forceinline__ void norm_inplace(float* xs, const float* w, float eps, float* red) {
+__device__ __forceinline__ void adapter_t(Ring& g, MegaSmem* s, float* wo_) {
+    const int lane = threadIdx.x & 31;
+    consume_rows(g, 0, LORA_R, 2, [&](const unsigned char* tile, int row0, int n) {
+        tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, s->xs, s->xoff, wo_);
+        if (lane < n * R) s->lt[(lane % R) * LORA_R + row0 + lane / R] = wo_[lane];
+    });
+    named_bar_sync(1, MEGA_NCT);
+}
+
+// The adapter's correction Bs[o] . t of output row o (terms in order, as the per-op GEMV adds them).
+__device__ __forceinline__ float adapter_corr(const float* bs, int o, const float* t) {
+    float d = 0.f;
+#pragma unroll
+    for (int j = 0; j < LORA_R; ++j) d += __ldg(bs + (int64_t)o * LORA_R + j) * t[j];
+    return d;
+}
+
+// ------------------------------------------------------------------ grid barrier (consumers)
+__device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsigned& epoch) {
+    named_bar_sync(1, MEGA_NCT);
+    if (threadIdx.x == 32) {
+        epoch += 1;
+        // release (cumulative over the CTA's writes ordered before it by the bar.sync above)
+        red_release_gpu_add(a.bar, 1u);
+        // test hook: the stalled CTA waits for one arrival more than the grid has (a bounded wait
+        // that must run out)
+        const unsigned target = epoch * gridDim.x + ((int)blockIdx.x == a.stall_cta && epoch == 1 ? 1u : 0u);
+        bool ok = true;
+        // one acquire poll at a time; the global error flag costs an L2 round trip of its own,
+        // so it is read every 64th poll only (more polls in flight measured slower: they
+        // contend with the arrivals at the counter's L2 slice)
+        if (ld_acquire_gpu(a.bar) < target) {
+            const unsigned long long t0 = globaltimer();
+            for (unsigned it = 1; ld_acquire_gpu(a.bar) < target; ++it) {
+                __nanosleep(20);
+                if (globaltimer() - t0 > a.wait_ns || ((it & 63) == 0 && *(volatile int*)a.err)) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) {
+            atomicExch(a.err, 1);
+            s->abort = 1;
+        }
+    }
+    named_bar_sync(1, MEGA_NCT);
+    return s->abort == 0;
+}
+
+// RMSNorm of R rows (global, [R][1024]) into dst with weight w; 1/rms of row r goes to rinv[r]
+// when rinv is given. One row: every consumer thread loads float4 pieces (all loads in flight
+// at once), warps reduce their 128-element slices, the eight slice sums are added in order
+// from shared memory (red: 8 floats). More rows (register pressure): one warp per row.
+template <int R>
+__device__ __forceinline__ void norm_rows(const float* src, const float* w, float eps, float* dst, float* red,
+                                          float* rinv = nullptr) {
     const int lane = threadIdx.x & 31;
     if constexpr (R == 1) {
         const int tid = threadIdx.x - 32;
         constexpr int N4 = D / 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f), wv = v;
         if (tid < N4) {
-            v = reinterpret_cast<const float4*>(xs)[tid];
+            v = __ldcg(reinterpret_cast<const float4*>(src) + tid);   // written by other CTAs: bypass L1
             wv = __ldg(reinterpret_cast<const float4*>(w) + tid);
             const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);   // warp-uniform branch
             if (lane == 0) red[tid / 32] = ss;
@@ -469,7 +382,8 @@ __device__ __forceinline__ void norm_inplace(float* xs, const float* w, float ep
 #pragma unroll
             for (int j = 0; j < D / 128; ++j) t += red[j];
             const float inv = rsqrtf(t / (float)D + eps);
-            reinterpret_cast<float4*>(xs)[tid] =
+            if (rinv && tid == 0) rinv[0] = inv;
+            reinterpret_cast<float4*>(dst)[tid] =
                 make_float4(wv.x * (v.x * inv), wv.y * (v.y * inv), wv.z * (v.z * inv), wv.w * (v.w * inv));
         }
     } else {
@@ -479,15 +393,16 @@ __device__ __forceinline__ void norm_inplace(float* xs, const float* w, float ep
             float ss = 0.f;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                v[i] = xs[r * D + i * 32 + lane];
-                wv[i] = __ldg(w + i * 32 + lane);
+                v[i] = __ldcg(src + (int64_t)r * D + i * 32 + lane);   // written by other CTAs: bypass L1
+                wv[i] = __ldg(w + i * 32 + lane);                      // in flight with the rows
             }
 #pragma unroll
             for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
             ss = warp_sum(ss);
             const float inv = rsqrtf(ss / (float)D + eps);
+            if (rinv && lane == 0) rinv[r] = inv;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
+            for (int i = 0; i < 32; ++i) dst[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
         }
     }
 }
@@ -496,6 +411,24 @@ __device__ __forceinline__ void norm_inplace(float* xs, const float* w, float ep
 // Chunk of keys per attention item: 32 keys when the span is short (more items than CTAs
 // would otherwise sit idle), 64 keys for longer spans.
 __device__ __forceinline__ int attn_chunk(int span) { return span <= 32 * 37 ? 32 : 64; }
+
+// Copy n floats global -> shared with 16-byte loads, all issued before the stores.
+__device__ __forceinline__ void copy_g2s(float* __restrict__ dst, const float* __restrict__ src, int n) {
+    const int tid = threadIdx.x - 32;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    const int n4 = n >> 2;
+    int i = tid;
+    for (; i + 3 * MEGA_NCT < n4; i += 4 * MEGA_NCT) {
+        const float4 a0 = __ldcg(s4 + i), a1 = __ldcg(s4 + i + MEGA_NCT), a2 = __ldcg(s4 + i + 2 * MEGA_NCT),
+                     a3 = __ldcg(s4 + i + 3 * MEGA_NCT);
+        d4[i] = a0;
+        d4[i + MEGA_NCT] = a1;
+        d4[i + 2 * MEGA_NCT] = a2;
+        d4[i + 3 * MEGA_NCT] = a3;
+    }
+    for (; i < n4; i += MEGA_NCT) d4[i] = __ldcg(s4 + i);
+}
 
 template <typename KVT>
 __device__ __forceinline__ void load_kv_row16(const KVT* p, int part, float* dst);   // 16 bytes of a K/V row
@@ -582,7 +515,7 @@ __device__ __forceinline__ void produce_kv(Ring& g, const KVLayer& L, int slot, 
         const int m = min(KPT, k0 + n - k);
         const uint32_t slot_i = g.t % MEGA_NS;
         const uint32_t use = g.t / MEGA_NS;
-        if (use > 0 && !mbar_wait_ab(*g.a, g.s, &g.s->empty[slot_i], (use - 1) & 1)) { g.ok = false; break; }
+        if (use > 0 && !ring_wait(g, &g.s->empty[slot_i], (use - 1) & 1)) { g.ok = false; break; }
         mbar_arrive_expect_tx(&g.s->full[slot_i], (uint32_t)m * ROW);
         const KVT* p0 = isv ? kv_v<KVT>(L, slot, head, k) : kv_k<KVT>(L, slot, head, k);
         const int i0 = k & L.mask;
@@ -596,20 +529,46 @@ __device__ __forceinline__ void produce_kv(Ring& g, const KVLayer& L, int slot, 
     }
 }
 
-// Pair w (elements 2w, 2w + 1) of a 64-element K/V row stored as KVT.
-__device__ __forceinline__ float2 kv_pair(const __nv_bfloat16* row, int w) {
-    return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row)[w]);
+// Consumers (all 15 warps): take the same tiles, widen them to fp32 rows of `dst` (stride
+// DH + 1), release each slot after every warp is done with it.
+template <typename KVT>
+__device__ __forceinline__ void consume_kv(Ring& g, int n, float* dst) {
+    constexpr int KPT = kv_keys_per_tile<KVT>();
+    constexpr int PARTS = DH * (int)sizeof(KVT) / 16;   // 16-byte pieces per row
+    const int tid = threadIdx.x - 32;
+    for (int k = 0; k < n; k += KPT) {
+        const int m = min(KPT, n - k);
+        const uint32_t slot_i = g.t % MEGA_NS;
+        const uint32_t use = g.t / MEGA_NS;
+        if (g.ok && !ring_wait(g, &g.s->full[slot_i], use & 1)) g.ok = false;
+        if (g.ok) {
+            const unsigned char* tile = g.s->ring[slot_i];
+            for (int e = tid; e < m * PARTS; e += MEGA_NCT) {
+                const int kk = e / PARTS, part = e % PARTS;
+                const uint4 u = *reinterpret_cast<const uint4*>(tile + kk * DH * sizeof(KVT) + part * 16);
+                float* d = dst + (k + kk) * (DH + 1);
+                if constexpr (sizeof(KVT) == 2) {
+                    float f[8];
+                    bf16x8_to_f32(u, f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) d[part * 8 + i] = f[i];
+                } else {
+                    d[part * 4 + 0] = __uint_as_float(u.x);
+                    d[part * 4 + 1] = __uint_as_float(u.y);
+                    d[part * 4 + 2] = __uint_as_float(u.z);
+                    d[part * 4 + 3] = __uint_as_float(u.w);
+                }
+            }
+        }
+        named_bar_sync(1, MEGA_NCT);
+        if (threadIdx.x == 32 && g.ok) mbar_arrive(&g.s->empty[slot_i]);
+        ++g.t;
+    }
 }
-__device__ __forceinline__ float2 kv_pair(const float* row, int w) { return reinterpret_cast<const float2*>(row)[w]; }
 
-// One attention item: queries of heads 4g..4g+3 of rows r0..r0+nr-1 against the chunk's keys
-// [k0, k1). Cached keys (< pos0) come from the ring tiles (R <= 2) or are loaded into shared
-// memory (R > 2); the block rows' own keys are produced here. Then a warp per query: scores with
-// the chunk's keys on the lanes, softmax with warp shuffles, P.V with dimension pairs on the lanes;
-// split-K partials (m, l, o[64]) published as units of the layer's partial flag.
 template <int R, typename KVT>
 __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& ring, int l, int r0, int nr, int g,
-                                       int c, int chunk, unsigned f, bool first, bool& ok) {
+                                       int c, int chunk, bool first) {
     const int tid = threadIdx.x - 32;   // consumer thread 0..479
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
     const bool local = is_local_layer(l);
@@ -622,27 +581,27 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     const int k1 = min(k0 + chunk, posL + 1);
     const int nk = k1 - k0;
     const int nold = max(0, min(k1, pos0) - k0);          // keys < pos0 come from the cache
-    const unsigned pf = part_flag(f, l);
     float* qs = s->xs;                                   // [nr*4][64]
-    float* Ks = qs + MEGA_RMAX * GQA * DH;               // [64][65] fp32 keys (new ones; R > 2: all)
+    float* Ks = qs + MEGA_RMAX * GQA * DH;               // [64][65]
     float* Vs = Ks + MEGA_CHUNK * (DH + 1);              // [64][65]
+    float* Ps = Vs + MEGA_CHUNK * (DH + 1);              // [nr*4][64]
     const int nq = nr * GQA;
     astamp(a, l, 0, first);
-    // queries (warps) and the block rows' own keys/values, produced here into rows [nold, nk)
-    {
+    // queries of heads 4g..4g+3 (warps), and the block rows' own keys/values (produced here);
+    // they land in rows [nold, nk) of Ks / Vs, disjoint from the cached rows
+    auto queries_and_new_keys = [&]() {
         const int vres_mode = (a.pulse == 0) ? (l == 0 ? 1 : 2) : 0;
         const int nnew = max(0, k1 - max(k0, pos0));
         for (int it = cw; it < nq + nnew; it += MEGA_NCW) {
             if (it < nq) {
                 const int rr = it / GQA, h = g * GQA + it % GQA;
                 const int pos = rows[r0 + rr].y;
-                const uint2* src = xqkv(a, l, r0 + rr) + h * DH;
+                const float* src = a.qkv + (int64_t)(r0 + rr) * QKV + h * DH;
+                const float x1 = __ldcg(src + lane), x2 = __ldcg(src + lane + 32);
                 const float* qw = a.qn[l] + h * DH;
                 const float w1 = __ldg(qw + lane), w2 = __ldg(qw + lane + 32);
                 const float* rp = s->rope[local ? 0 : 1][r0 + rr];
                 const float cs = rp[lane], sn = rp[32 + lane];
-                float x1, x2;
-                ll_get2(a, s, src + lane, src + lane + 32, f, ok, x1, x2);
                 const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + a.eps);
                 const float q1 = w1 * (x1 * inv), q2 = w2 * (x2 * inv);
                 float y1 = q1 * cs - q2 * sn, y2 = q2 * cs + q1 * sn;
@@ -658,22 +617,22 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
                 const int key = max(k0, pos0) + (it - nq);
                 const int kk = key - k0;
                 const int rr = r0 + (key - pos0);
-                const uint2* src = xqkv(a, l, rr);
+                const float* src = a.qkv + (int64_t)rr * QKV;
+                const float e1 = __ldcg(src + H * DH + g * DH + lane), e2 = __ldcg(src + H * DH + g * DH + lane + 32);
+                float v1 = __ldcg(src + H * DH + HKV * DH + g * DH + lane);
+                float v2 = __ldcg(src + H * DH + HKV * DH + g * DH + lane + 32);
+                float* vf = a.vfirst + ((int64_t)rr * HKV + g) * DH;
+                // the first layer's values (value residual) in flight with the rest
+                const float f1 = vres_mode == 2 ? __ldcg(vf + lane) : 0.f;
+                const float f2 = vres_mode == 2 ? __ldcg(vf + lane + 32) : 0.f;
                 const float* kw = a.kn[l] + g * DH;
                 const float w1 = __ldg(kw + lane), w2 = __ldg(kw + lane + 32);
                 const float* rp = s->rope[local ? 0 : 1][rr];   // row rr sits at position key
                 const float cs = rp[lane], sn = rp[32 + lane];
-                float e1, e2, v1, v2;
-                ll_get2(a, s, src + H * DH + g * DH + lane, src + H * DH + g * DH + lane + 32, f, ok, e1, e2);
-                ll_get2(a, s, src + H * DH + HKV * DH + g * DH + lane, src + H * DH + HKV * DH + g * DH + lane + 32, f,
-                        ok, v1, v2);
-                uint2* vf = xvfirst(a, rr, g);
                 if (vres_mode == 1) {
-                    ll_st(vf + lane, v1, f);
-                    ll_st(vf + lane + 32, v2, f);
+                    vf[lane] = v1;
+                    vf[lane + 32] = v2;
                 } else if (vres_mode == 2) {
-                    float f1, f2;   // the first layer's values (value residual)
-                    ll_get2(a, s, vf + lane, vf + lane + 32, f, ok, f1, f2);
                     const float lv = a.vres[l];
                     v1 = (1.f - lv) * v1 + lv * f1;
                     v2 = (1.f - lv) * v2 + lv * f2;
@@ -696,27 +655,15 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
                 Vs[kk * (DH + 1) + lane + 32] = kv_round<KVT>(v2);
             }
         }
-    }
-    astamp(a, l, 1, first);
-    // cached keys/values: R <= 2 the ring tiles the producer streamed during phase A (ntk tiles of
-    // K, then ntk of V, waited for here and released after the compute); larger passes load them
-    // here into Ks / Vs, every thread's 16-byte loads issued first
-    constexpr int KPT = kv_keys_per_tile<KVT>();
-    constexpr int ROW = DH;   // elements per cached row
-    const KVT* kt[MEGA_CHUNK / KPT + 1];
-    const KVT* vt[MEGA_CHUNK / KPT + 1];
-    int ntk = 0;
+    };
+    // 1) cached keys/values of the chunk. One- and two-row passes: the producer streamed them
+    //    through the ring during phase A, so the queries' L2 reads go first and the tiles land
+    //    meanwhile. Larger passes load them here, every thread's 16-byte loads issued first.
     if constexpr (R <= MEGA_RING_KV_MAX_R) {
-        ntk = (nold + KPT - 1) / KPT;
-        for (int i = 0; i < 2 * ntk; ++i) {
-            const uint32_t t = ring.t + i;
-            if (ring.ok && !mbar_wait_ab(a, s, &s->full[t % MEGA_NS], (t / MEGA_NS) & 1)) {
-                ring.ok = false;
-                raise_abort(a, s);
-            }
-            const KVT* tile = reinterpret_cast<const KVT*>(s->ring[t % MEGA_NS]);
-            if (i < ntk) kt[i] = tile; else vt[i - ntk] = tile;
-        }
+        queries_and_new_keys();
+        astamp(a, l, 1, first);
+        consume_kv<KVT>(ring, nold, Ks);
+        consume_kv<KVT>(ring, nold, Vs);
     } else {
         constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
         for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
@@ -726,142 +673,191 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
             const KVT* row = isv ? kv_v<KVT>(L, slot, g, k0 + kk) : kv_k<KVT>(L, slot, g, k0 + kk);
             load_kv_row16<KVT>(row, part, (isv ? Vs : Ks) + kk * (DH + 1));
         }
+        astamp(a, l, 1, first);
+        queries_and_new_keys();
     }
-    named_bar_sync(1, MEGA_NCT);   // queries, produced keys (and loaded keys) visible
+    // rows past the end of a partial chunk: zeros (probabilities are 0 there; 0 * stale
+    // shared memory could be NaN)
+    for (int e = tid; e < (MEGA_CHUNK - nk) * DH; e += MEGA_NCT) {
+        const int kk = nk + e / DH, d = e % DH;
+        Ks[kk * (DH + 1) + d] = 0.f;
+        Vs[kk * (DH + 1) + d] = 0.f;
+    }
+    named_bar_sync(1, MEGA_NCT);
     astamp(a, l, 2, first);
-    constexpr bool TILES = R <= MEGA_RING_KV_MAX_R;
+    // 3) scores with per-row masks [lo_r, pos_r]. Several rows: a thread per (key, row) covers
+    //    the row's four heads (float4 query loads shared by the key's element); one row: a
+    //    thread per (key, head)
+    if (nq >= 2 * GQA) {
+        for (int e = tid; e < nr * MEGA_CHUNK; e += MEGA_NCT) {
+            const int rq = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
+            const int key = k0 + kk;
+            const int pos = rows[r0 + rq].y;
+            const int lor = local ? max(0, pos - WINDOW + 1) : 0;
+            const bool vis = kk < nk && key <= pos && key >= lor;
+            float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
+            if (vis) {
+                const float* kv = Ks + kk * (DH + 1);
+#pragma unroll 4
+                for (int d = 0; d < DH; d += 4) {
+                    const float c0 = kv[d], c1 = kv[d + 1], c2 = kv[d + 2], c3 = kv[d + 3];
+#pragma unroll
+                    for (int i = 0; i < GQA; ++i) {
+                        const float4 q = *reinterpret_cast<const float4*>(qs + (rq * GQA + i) * DH + d);
+                        acc[i] += q.x * c0 + q.y * c1 + q.z * c2 + q.w * c3;
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < GQA; ++i) Ps[(rq * GQA + i) * MEGA_CHUNK + kk] = vis ? acc[i] : -INFINITY;
+        }
+    } else
+    for (int e = tid; e < nq * MEGA_CHUNK; e += MEGA_NCT) {
+        const int qi = e / MEGA_CHUNK, kk = e % MEGA_CHUNK;
+        const int key = k0 + kk;
+        const int pos = rows[r0 + qi / GQA].y;
+        const int lor = local ? max(0, pos - WINDOW + 1) : 0;
+        float sc = -INFINITY;
+        if (kk < nk && key <= pos && key >= lor) {
+            sc = 0.f;
+            const float* qv = qs + qi * DH;
+            const float* kv = Ks + kk * (DH + 1);
+#pragma unroll 16
+            for (int d = 0; d < DH; ++d) sc += qv[d] * kv[d];
+        }
+        Ps[qi * MEGA_CHUNK + kk] = sc;
+    }
+    named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 3, first);
+    // 4) partial softmax per query (warps): max m, weights e = exp(s - m) back into Ps, sum
     for (int qi = cw; qi < nq; qi += MEGA_NCW) {
         const int rr = qi / GQA, h = g * GQA + qi % GQA;
-        const int pos = rows[r0 + rr].y;
-        const int lor = local ? max(0, pos - WINDOW + 1) : 0;
-        const float* q = qs + qi * DH;
-        // scores: lane holds keys lane and lane + 32 of the chunk. A cached row in a ring tile is
-        // read in rotated pair order (pair (j + lane) mod 32 at step j: one bank per lane)
-        float sc[2];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            const int kk = lane + 32 * half;
-            const int key = k0 + kk;
-            float v = -INFINITY;
-            if (kk < nk && key <= pos && key >= lor) {
-                float acc = 0.f;
-                if (TILES && kk < nold) {
-                    const KVT* row = kt[kk / KPT] + (kk % KPT) * ROW;
-#pragma unroll 8
-                    for (int j = 0; j < DH / 2; ++j) {
-                        const int w = (j + lane) & (DH / 2 - 1);
-                        const float2 kv2 = kv_pair(row, w);
-                        const float2 q2 = reinterpret_cast<const float2*>(q)[w];
-                        acc += q2.x * kv2.x + q2.y * kv2.y;
-                    }
-                } else {
-                    const float* row = Ks + kk * (DH + 1);
-#pragma unroll 16
-                    for (int d = 0; d < DH; ++d) acc += q[d] * row[d];
-                }
-                v = acc;
-            }
-            sc[half] = v;
-        }
-        const float m = warp_max(fmaxf(sc[0], sc[1]));   // -inf: no key of the chunk is visible to this row
-        const float e0 = (sc[0] == -INFINITY) ? 0.f : expf(sc[0] - m);
-        const float e1 = (sc[1] == -INFINITY) ? 0.f : expf(sc[1] - m);
+        const float p0 = Ps[qi * MEGA_CHUNK + lane], p1 = Ps[qi * MEGA_CHUNK + lane + 32];
+        const float m = warp_max(fmaxf(p0, p1));
+        const float e0 = (p0 == -INFINITY) ? 0.f : expf(p0 - m);
+        const float e1 = (p1 == -INFINITY) ? 0.f : expf(p1 - m);
         const float lsum = warp_sum(e0 + e1);
-        // P.V: lane holds dimensions 2 lane, 2 lane + 1; keys in order
-        float o0 = 0.f, o1 = 0.f;
-        for (int kk = 0; kk < nk; ++kk) {
-            const float pw = __shfl_sync(0xffffffffu, kk < 32 ? e0 : e1, kk & 31);
-            if (pw == 0.f) continue;   // warp-uniform: masked key
-            float2 v2;
-            if (TILES && kk < nold) {
-                v2 = kv_pair(vt[kk / KPT] + (kk % KPT) * ROW, lane);
-            } else {
-                const float* row = Vs + kk * (DH + 1);
-                v2 = make_float2(row[2 * lane], row[2 * lane + 1]);
-            }
-            o0 += pw * v2.x;
-            o1 += pw * v2.y;
-        }
-        uint2* out = xpart(a, l, r0 + rr, h, c);
+        Ps[qi * MEGA_CHUNK + lane] = e0;
+        Ps[qi * MEGA_CHUNK + lane + 32] = e1;
+        float* out = a.part + (((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART;
         if (lane == 0) {
-            ll_st(out, m, pf);
-            ll_st(out + 1, m == -INFINITY ? 0.f : lsum, pf);
+            out[0] = m;   // -inf: no key of the chunk is visible to this row (weights all 0)
+            out[1] = m == -INFINITY ? 0.f : lsum;
         }
-        ll_st(out + 2 + 2 * lane, o0, pf);
-        ll_st(out + 3 + 2 * lane, o1, pf);
     }
-    named_bar_sync(1, MEGA_NCT);   // every warp is done with the tiles and with Ks / Vs
-    if constexpr (TILES) {
-        if (threadIdx.x == 32 && ring.ok)
-            for (int i = 0; i < 2 * ntk; ++i) mbar_arrive(&s->empty[(ring.t + i) % MEGA_NS]);
-        ring.t += 2 * ntk;
+    named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 4, first);
+    // 5) P.V. Several rows: a thread per (dimension, row) covers the row's four heads (float4
+    //    weight loads); one row: a thread per (query, dimension), keys in order
+    if (nq >= 2 * GQA) {
+        for (int e = tid; e < nr * DH; e += MEGA_NCT) {
+            const int rq = e / DH, d = e % DH;
+            float o[GQA] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+            for (int kk = 0; kk < MEGA_CHUNK; kk += 4) {
+                const float v0 = Vs[kk * (DH + 1) + d], v1 = Vs[(kk + 1) * (DH + 1) + d];
+                const float v2 = Vs[(kk + 2) * (DH + 1) + d], v3 = Vs[(kk + 3) * (DH + 1) + d];
+#pragma unroll
+                for (int i = 0; i < GQA; ++i) {
+                    const float4 pw = *reinterpret_cast<const float4*>(Ps + (rq * GQA + i) * MEGA_CHUNK + kk);
+                    o[i] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < GQA; ++i)
+                a.part[(((int64_t)(r0 + rq) * H + g * GQA + i) * a.nch_max + c) * PART + 2 + d] = o[i];
+        }
+    } else
+    for (int e = tid; e < nq * DH; e += MEGA_NCT) {
+        const int qi = e / DH, d = e % DH;
+        const int rr = qi / GQA, h = g * GQA + qi % GQA;
+        const float* pr = Ps + qi * MEGA_CHUNK;
+        float o = 0.f;
+#pragma unroll 16
+        for (int kk = 0; kk < MEGA_CHUNK; ++kk) o += pr[kk] * Vs[kk * (DH + 1) + d];
+        a.part[(((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART + 2 + d] = o;
     }
-    astamp(a, l, 3, first);
+    named_bar_sync(1, MEGA_NCT);
+    astamp(a, l, 5, first);
 }
 
-// Merge the chunk partials (m, l, o[64]) of query head h of row r, apply the gate, publish
-// att[r][h*64 ..]: every consumer thread takes part of the partials in one batched poll into
-// shared memory; warp 0 then forms the softmax weights of the chunks and the weighted sums.
-static __device__ __noinline__ void attn_merge(const MegaArgs& a, MegaSmem* s, int l, int r, int h, int nch,
-                                               unsigned f, bool& ok) {
+// Merge the chunk partials (m, l, o[64]) of query head h of row r, apply the gate, write
+// att[r][h*64 ..]: consumer warps take chunks cw, cw + 15, ... (online softmax merge, loads of
+// four chunks in flight), then warp 0 merges the 15 warp states in warp order.
+static __device__ __noinline__ void attn_merge(const MegaArgs& a, MegaSmem* s, int r, int h, int nch) {
     const int cw = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
-    float* P = s->xs;   // [nch][PART]; xs is free between the attention items and phase C
-    ll_fetch(a, s, xpart(a, l, r, h, 0), nch * PART / 2, part_flag(f, l), P, ok);
+    const float* pp = a.part + ((int64_t)r * H + h) * a.nch_max * PART;
+    const float graw = (cw == 0) ? __ldcg(a.gate + r * H + h) : 0.f;   // in flight with the partials
+    float M = -INFINITY, Ls = 0.f, o1 = 0.f, o2 = 0.f;
+    for (int c0 = cw; c0 < nch; c0 += 4 * MEGA_NCW) {
+        float mc[4], lc[4], a1[4], a2[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = c0 + u * MEGA_NCW;
+            mc[u] = -INFINITY;
+            lc[u] = a1[u] = a2[u] = 0.f;
+            if (c < nch) {
+                const float* q = pp + (int64_t)c * PART;
+                mc[u] = __ldcg(q);
+                lc[u] = __ldcg(q + 1);
+                a1[u] = __ldcg(q + 2 + lane);
+                a2[u] = __ldcg(q + 2 + 32 + lane);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (mc[u] == -INFINITY) continue;
+            const float Mn = fmaxf(M, mc[u]);
+            const float so = expf(M - Mn), sn = expf(mc[u] - Mn);
+            Ls = Ls * so + lc[u] * sn;
+            o1 = o1 * so + a1[u] * sn;
+            o2 = o2 * so + a2[u] * sn;
+            M = Mn;
+        }
+    }
+    float* st = s->stage + cw * PART;   // [15][66]
+    if (lane == 0) {
+        st[0] = M;
+        st[1] = Ls;
+    }
+    st[2 + lane] = o1;
+    st[2 + 32 + lane] = o2;
     named_bar_sync(1, MEGA_NCT);
     if (cw == 0) {
-        const float graw = ll_get(a, s, xgate(a, l, r) + h, f, ok);
-        float mx = -INFINITY;
-        for (int c = lane; c < nch; c += 32) mx = fmaxf(mx, P[c * PART]);
-        const float M = warp_max(mx);
-        float lsum = 0.f;
-        for (int c = lane; c < nch; c += 32) {
-            const float m = P[c * PART];
-            const float w = (m == -INFINITY) ? 0.f : expf(m - M);
-            s->stage[c] = w;
-            lsum += w * P[c * PART + 1];
-        }
-        const float Ls = warp_sum(lsum);
-        __syncwarp();
+        // lane w < 15 holds warp w's (m, l); the weights exp(m_w - max) are computed in
+        // parallel and broadcast, so the fold below is FMAs only
+        const float mw = lane < MEGA_NCW ? s->stage[lane * PART] : -INFINITY;
+        const float lw = lane < MEGA_NCW ? s->stage[lane * PART + 1] : 0.f;
+        const float Mx = warp_max(mw);
+        const float ww = (mw == -INFINITY) ? 0.f : expf(mw - Mx);
+        const float L = warp_sum(ww * lw);
         float p1 = 0.f, p2 = 0.f;
-        for (int c = 0; c < nch; ++c) {
-            const float w = s->stage[c];
-            p1 += w * P[c * PART + 2 + lane];
-            p2 += w * P[c * PART + 2 + 32 + lane];
+#pragma unroll
+        for (int w = 0; w < MEGA_NCW; ++w) {
+            const float wt = __shfl_sync(0xffffffffu, ww, w);
+            const float* q = s->stage + w * PART;
+            p1 += wt * q[2 + lane];
+            p2 += wt * q[2 + 32 + lane];
         }
         const float gt = sigmoidf_(graw);
-        const float inv = 1.f / Ls;
-        uint2* out = xatt(a, l, r) + h * DH;
-        ll_st(out + lane, (p1 * inv) * gt, f);
-        ll_st(out + 32 + lane, (p2 * inv) * gt, f);
+        const float inv = 1.f / L;
+        a.att[(int64_t)r * D + h * DH + lane] = (p1 * inv) * gt;
+        a.att[(int64_t)r * D + h * DH + 32 + lane] = (p2 * inv) * gt;
     }
     named_bar_sync(1, MEGA_NCT);
 }
 
-// Consumer exit of every CTA: the last CTA out advances the launch counter (the next launch's
-// flag) and re-arms the leave ticket.
+// Consumer exit of every CTA: the last CTA out (every CTA is past its last grid barrier)
+// re-arms the barrier counter for the next launch on this stream.
 __device__ __forceinline__ void mega_leave(const MegaArgs& a) {
     if (threadIdx.x == 32) {
         if (a.trace) a.trace[blockIdx.x * MEGA_TRACE + MEGA_TRACE - 2] = globaltimer();
-        __threadfence();
-        const unsigned t = atomicAdd(&a.tickets[1], 1u);
+        const unsigned t = atomicAdd(&a.tickets[MEGA_RMAX * HKV + 1], 1u);
         if (t == gridDim.x - 1) {
-            a.tickets[1] = 0;
-            atomicAdd(a.epoch, 1u);
+            a.tickets[MEGA_RMAX * HKV + 1] = 0;
+            atomicExch(a.bar, 0u);
         }
     }
-}
-
-// Loop-adapter factor rows of this CTA (CTAs < MEGA_TDES): t[r][2 cta + i] = A[2 cta + i] . X_r,
-// published for every CTA of the phase.
-template <int R>
-__device__ __forceinline__ void adapter_t(Ring& g, MegaSmem* s, const MegaArgs& a, int l, int which, unsigned f) {
-    const int lane = threadIdx.x & 31;
-    const int cta = blockIdx.x;
-    float* wo = s->wout[(threadIdx.x >> 5) - 1];
-    consume_rows(g, 2 * cta, 2 * cta + 2, 2, [&](const unsigned char* tile, int row0, int n) {
-        tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, s->xs, s->xoff, wo);
-        if (lane < n * R) ll_st(xlt(a, l, which, lane % R) + row0 + lane / R, wo[lane], f);
-    });
 }
 
 // ------------------------------------------------------------------ the pulse
@@ -872,7 +868,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
     const int C = gridDim.x, cta = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool want_lm = a.logits != nullptr || a.amax != nullptr;
-    const bool adapter = a.la_qkv[0] != nullptr;
+    const bool lora = a.la_qkv[0] != nullptr;   // live loop adapter (exact fp32 correction)
     if (a.skip && __ldcg(a.skip) != 0) {   // every row exited early (flag written by an earlier kernel)
         mega_leave(a);
         return;
@@ -892,7 +888,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
     // ================================================================ producer
     if (warp == 0) {
         if (lane != 0) return;
-        Ring g{s, &a, 0u, -1, true};
+        Ring g{s, 0u, -1, true, a.wait_ns};
         int pblk[MEGA_RMAX + 1], pnb = 0;   // sequence blocks of the rows (as the consumers build them)
         for (int r0 = 0; r0 < R;) {
             int nr = 1;
@@ -901,14 +897,13 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             r0 += nr;
         }
         pblk[pnb] = R;
-        if (a.pulse > 0) produce_rows(g, a.rg_down, 2 * D * 4, 0, RG, 1);   // re-injection gate rows
 #pragma unroll 1
         for (int l = 0; l < NL && g.ok; ++l) {
             int r0, r1;
-            if (adapter && cta < MEGA_TDES) produce_rows(g, a.la_qkv[l], D * 4, 2 * cta, 2 * cta + 2, 2);
+            if (a.la_qkv[0]) produce_rows(g, a.la_qkv[l], D * 4, 0, LORA_R, 2);   // adapter A rows (fp32)
             rows_split(QKV, cta, C, r0, r1);
             produce_rows(g, a.wqkv[l], D * 2, r0, r1, 4);
-            // gate rows: the last H/2 CTAs
+            // gate rows: the last H/2 CTAs, consumed in phase B (usually CTAs without attention items)
             if (cta >= C - H / 2) {
                 const int gr = 2 * (cta - (C - H / 2));
                 produce_rows(g, a.gate_w[l], D * 4, gr, gr + 2, 2);
@@ -922,10 +917,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                     produce_kv<KVT>(g, a.kvl[l], geo.slot, geo.g, geo.k0, geo.nold, true);
                 }
             }
-            if (adapter && cta < MEGA_TDES) produce_rows(g, a.la_wo[l], D * 4, 2 * cta, 2 * cta + 2, 2);
+            if (a.la_qkv[0]) produce_rows(g, a.la_wo[l], D * 4, 0, LORA_R, 2);
             rows_split(D, cta, C, r0, r1);
             produce_rows(g, a.wo[l], D * 2, r0, r1, 4);
-            produce_rows(g, a.router[l], D * 4, 0, E, 2);   // fp32 router rows (every CTA)
             {   // shared-expert pairs: a static split, prefetched before the router runs
                 int j0, j1;
                 rows_split(DS, cta, C, j0, j1);
@@ -933,11 +927,12 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 produce_rows(g, a.sh_gu[l], D * 2, DS + j0, DS + j1, 4);
             }
             // routed pairs depend on this layer's router. Short sleeps between polls (a tight
-            // spin on shared memory starves the consumers' loads)
+            // spin on shared memory starves the consumers' loads); the global error flag costs
+            // an L2 round trip, so it is read every 256th poll only
             const unsigned long long t0 = globaltimer();
             for (unsigned it = 1; s->moe_ready != l + 1; ++it) {
                 __nanosleep(32);
-                if ((it & 15) == 0 && (s->abort || globaltimer() - t0 > a.wait_ns)) {
+                if (globaltimer() - t0 > a.wait_ns || s->abort || ((it & 255) == 0 && *(volatile int*)a.err)) {
                     g.ok = false;
                     break;
                 }
@@ -967,7 +962,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             produce_rows(g, a.emb, D * 2, v0, v1, 4);
             if (a.trace) a.trace[blockIdx.x * MEGA_TRACE + 205] = globaltimer();
         }
-        if (!g.ok) raise_abort(a, s);
+        if (!g.ok) atomicExch(a.err, 1);
         // drain: wait for every copy this thread issued to land before the CTA can exit
         for (uint32_t t = (g.t > MEGA_NS ? g.t - MEGA_NS : 0); t < g.t; ++t)
             if (!mbar_wait(&s->full[t % MEGA_NS], (t / MEGA_NS) & 1)) break;
@@ -976,30 +971,32 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
 
     // ================================================================ consumers
     const int cw = warp - 1;
-    const int tid = threadIdx.x - 32;
     if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE] = globaltimer();
-    const unsigned f = ld_acquire_gpu(a.epoch) + 1u;   // this launch's flag (same in every CTA)
-    Ring g{s, &a, 0u, cw, true};
-    bool ok = true;   // this thread's waits all succeeded
+    Ring g{s, 0u, cw, true, a.wait_ns};
+    unsigned epoch = 0;
     float* xs = s->xs;
     float* wo_ = s->wout[cw];   // this warp's reduced tile sums
     const float eps = a.eps;
     const int p = a.pulse;
-    // h rows [own0, own1) are this CTA's outputs in phases C and E
+    // h rows [own0, own1) are this CTA's outputs in phases C and E; their router weights
+    // (times the mlp-norm weight) for every layer go to shared memory now
     int own0, own1;
     rows_split(D, cta, C, own0, own1);
     const int nown = own1 - own0;
-    for (int t = tid; t < NL * MEGA_MAXOROWS; t += MEGA_NCT) {
+    for (int t = threadIdx.x - 32; t < NL * E * MEGA_MAXOROWS; t += MEGA_NCT) {
+        const int ll = t / (E * MEGA_MAXOROWS), e = (t / MEGA_MAXOROWS) % E, oi = t % MEGA_MAXOROWS;
+        s->rwn[ll][e][oi] = oi < nown ? a.router[ll][e * D + own0 + oi] * a.mlp_norm[ll][own0 + oi] : 0.f;
+    }
+    for (int t = threadIdx.x - 32; t < NL * MEGA_MAXOROWS; t += MEGA_NCT) {
         const int ll = t / MEGA_MAXOROWS, oi = t % MEGA_MAXOROWS;
         s->rsc[ll][oi] = oi < nown ? a.rscale[ll][own0 + oi] : 0.f;
     }
-    for (int t = tid; t < NL * E; t += MEGA_NCT) s->ebias[t / E][t % E] = a.ebias[t / E][t % E];
-    for (int t = tid; t < 2 * R * DH; t += MEGA_NCT) {
+    for (int t = threadIdx.x - 32; t < NL * E; t += MEGA_NCT) s->ebias[t / E][t % E] = a.ebias[t / E][t % E];
+    for (int t = threadIdx.x - 32; t < 2 * R * DH; t += MEGA_NCT) {
         const int tab = t / (R * DH), r = (t / DH) % R, j = t % DH;
         const float* T = (j < 32) ? (tab ? a.cos_g : a.cos_l) : (tab ? a.sin_g : a.sin_l);
         s->rope[tab][r][j] = T[(int64_t)s->rows[r].y * 32 + (j & 31)];
     }
-    if (tid < R) s->xoff[tid] = tid * D;
     // ---- pulse input: every CTA builds h_in for all rows in xs[0 .. R*D) ----
     if (p == 0) {
         for (int r = cw; r < R; r += MEGA_NCW) {
@@ -1013,6 +1010,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 ss += v[i] * v[i];
             }
             const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+            // read-only inputs through the non-coherent path (free to move ahead of the
+            // stores); global stores only after the loop
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const int d = i * 32 + lane;
@@ -1026,69 +1025,66 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 for (int i = 0; i < 32; ++i) a.h0n_out[(int64_t)r * a.hstride * D + i * 32 + lane] = v[i];
         }
     } else {
-        // xs[r*D ..] = h0n_in[r], xs[R*D + r*D ..] = RMSNorm(h_prev[r]) (pulse-state norm);
-        // g8[r][j] = Wd[j][:D] . h0n[r] + Wd[j][D:] . RMSNorm(h_prev[r]) from the ring's gate rows
-        float* rn = xs + R * D;
-        for (int r = cw; r < R; r += MEGA_NCW) {
-            float v[32];
-            float ss = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                v[i] = __ldg(a.h_prev + r * D + i * 32 + lane);
-                ss += v[i] * v[i];
-            }
-            const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int d = i * 32 + lane;
-                rn[r * D + d] = __ldg(a.psn + d) * (v[i] * inv);
-                xs[r * D + d] = __ldg(a.h0n_in + r * D + d);
-            }
-        }
-        named_bar_sync(1, MEGA_NCT);
-        consume_rows(g, 0, RG, 1, [&](const unsigned char* tile, int j, int) {
-            const float* wd = reinterpret_cast<const float*>(tile);
-            for (int r = 0; r < R; ++r) {
+        // g8[r][j] = Wd[j][:D] . h0n[r] + Wd[j][D:] . RMSNorm(h_prev[r])   (CTAs < 8)
+        if (cta < RG) {
+            const int j = cta;
+            for (int r = cw; r < R; r += MEGA_NCW) {
+                float ss = 0.f;
+                for (int i = lane; i < D; i += 32) ss += a.h_prev[r * D + i] * a.h_prev[r * D + i];
+                const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
                 float pe = 0.f, pr = 0.f;
-                for (int i = lane * 4; i < D; i += 128) {
-                    const float4 w0 = *reinterpret_cast<const float4*>(wd + i);
-                    const float4 w1 = *reinterpret_cast<const float4*>(wd + D + i);
-                    const float4 x0 = *reinterpret_cast<const float4*>(xs + r * D + i);
-                    const float4 x1 = *reinterpret_cast<const float4*>(rn + r * D + i);
-                    pe += w0.x * x0.x + w0.y * x0.y + w0.z * x0.z + w0.w * x0.w;
-                    pr += w1.x * x1.x + w1.y * x1.y + w1.z * x1.z + w1.w * x1.w;
+                for (int i = lane; i < D; i += 32) {
+                    pe += a.rg_down[j * 2 * D + i] * a.h0n_in[r * D + i];
+                    pr += a.rg_down[j * 2 * D + D + i] * (a.psn[i] * (a.h_prev[r * D + i] * inv));
                 }
                 pe = warp_sum(pe);
                 pr = warp_sum(pr);
-                if (lane == 0) s->g8[r][j] = pe + pr;
+                if (lane == 0) a.g8[r * RG + j] = pe + pr;
             }
-        });
-        named_bar_sync(1, MEGA_NCT);
-        for (int e = tid; e < R * D; e += MEGA_NCT) {
-            const int r = e / D, d = e % D;
-            const float4 u0 = __ldg(reinterpret_cast<const float4*>(a.rg_up + d * RG));
-            const float4 u1 = __ldg(reinterpret_cast<const float4*>(a.rg_up + d * RG + 4));
-            const float* gg = s->g8[r];
-            const float z = __ldg(a.rg_bias + d) + u0.x * gg[0] + u0.y * gg[1] + u0.z * gg[2] + u0.w * gg[3] +
-                            u1.x * gg[4] + u1.y * gg[5] + u1.z * gg[6] + u1.w * gg[7];
-            const float mix = sigmoidf_(z);
-            const float rv = rn[e], an = xs[e];
-            const float diff = an - rv;
-            const float lerp = (mix < 0.5f) ? rv + mix * diff : an - diff * (1.f - mix);
-            xs[e] = lerp + __ldg(a.step + d);
+        }
+        if (!grid_sync(a, s, epoch)) goto done;
+        // h_prev and h0n_in are inputs this kernel never writes (h0n_out may alias h0n_in and is
+        // then not written): read-only loads, global stores after the loops
+        for (int r = cw; r < R; r += MEGA_NCW) {
+            float ss = 0.f;
+#pragma unroll 8
+            for (int i = 0; i < 32; ++i) {
+                const float x = __ldg(a.h_prev + r * D + i * 32 + lane);
+                ss += x * x;
+            }
+            const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+            float gg[RG];
+#pragma unroll
+            for (int j = 0; j < RG; ++j) gg[j] = __ldcg(a.g8 + r * RG + j);
+#pragma unroll 4
+            for (int i = 0; i < 32; ++i) {
+                const int d = i * 32 + lane;
+                const float4 u0 = __ldg(reinterpret_cast<const float4*>(a.rg_up + d * RG));
+                const float4 u1 = __ldg(reinterpret_cast<const float4*>(a.rg_up + d * RG + 4));
+                const float z = __ldg(a.rg_bias + d) + u0.x * gg[0] + u0.y * gg[1] + u0.z * gg[2] + u0.w * gg[3] +
+                                u1.x * gg[4] + u1.y * gg[5] + u1.z * gg[6] + u1.w * gg[7];
+                const float mix = sigmoidf_(z);
+                const float rn = __ldg(a.psn + d) * (__ldg(a.h_prev + r * D + d) * inv);
+                const float an = __ldg(a.h0n_in + r * D + d);
+                const float diff = an - rn;
+                const float lerp = (mix < 0.5f) ? rn + mix * diff : an - diff * (1.f - mix);
+                xs[r * D + d] = lerp + __ldg(a.step + d);
+            }
         }
         if (cta == 0 && a.h0n_out && a.h0n_out != a.h0n_in) {   // caller buffers: scalar accesses, no alignment assumed
 #pragma unroll 4
-            for (int i = tid; i < R * D; i += MEGA_NCT)
+            for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT)
                 a.h0n_out[(int64_t)(i / D) * a.hstride * D + i % D] = __ldg(a.h0n_in + i);
         }
     }
     named_bar_sync(1, MEGA_NCT);
-    for (int t = tid; t < nown * R; t += MEGA_NCT) {
-        const float v = xs[(t % R) * D + own0 + t / R];
-        s->hown[t] = v;
-        s->hin[t] = v;
-    }
+    if (cta == 0)
+        for (int i = threadIdx.x - 32; i < R * D; i += MEGA_NCT) {
+            a.h_in[i] = xs[i];
+            a.h[i] = xs[i];
+        }
+    for (int t = threadIdx.x - 32; t < nown * R; t += MEGA_NCT) s->hown[t] = xs[(t % R) * D + own0 + t / R];
+    named_bar_sync(1, MEGA_NCT);
     // sequence blocks of the rows (consecutive rows of one slot), for the attention items
     if (threadIdx.x == 32) {
         int nb = 0, r0 = 0;
@@ -1101,18 +1097,32 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         s->blk_r0[nb] = R;
         s->n_blk = nb;
     }
-    named_bar_sync(1, MEGA_NCT);
+    // xs holds h_in; layer 0's attention norm reads it from xs, later layers from a.h
     // one copy of the layer body (not unrolled), so it can stay in the instruction caches
 #pragma unroll 1
     for (int l = 0; l < NL; ++l) {
         const bool local = is_local_layer(l);
         // ---------------- phase A: xn, QKV, gate logits
         {
-            if (l > 0) {
-                ll_fetch(a, s, xh(a, l - 1, 1, 0), R * D / 2, f, xs, ok);
-                if (named_bar_or(1, MEGA_NCT, !ok)) goto done;
+            if (l == 0) {
+                // normalise in place (each warp owns its rows)
+                for (int r = cw; r < R; r += MEGA_NCW) {
+                    float v[32], wv[32];
+                    float ss = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        v[i] = xs[r * D + i * 32 + lane];
+                        wv[i] = __ldg(a.attn_norm[l] + i * 32 + lane);
+                        ss += v[i] * v[i];
+                    }
+                    const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = wv[i] * (v[i] * inv);
+                }
+            } else {
+                norm_rows<R>(a.h, a.attn_norm[l], eps, xs, s->nred);
             }
-            norm_inplace<R>(xs, a.attn_norm[l], eps, s->nred);
+            if (threadIdx.x - 32 < R) s->xoff[threadIdx.x - 32] = (threadIdx.x - 32) * D;
             // attention chunking of each block (used in phase B)
             if (threadIdx.x == 33) {
                 for (int b = 0; b < s->n_blk; ++b) {
@@ -1125,50 +1135,39 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             }
             named_bar_sync(1, MEGA_NCT);
             stamp(a, l, 0);
-            if (adapter && cta < MEGA_TDES) adapter_t<R>(g, s, a, l, 0, f);
+            if (lora) adapter_t<R>(g, s, wo_);
             int r0, r1;
             rows_split(QKV, cta, C, r0, r1);
-            if (!adapter) {
-                consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
-                    tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
-                    if (lane < n * R) ll_st(xqkv(a, l, lane % R) + row0 + lane / R, wo_[lane], f);
-                });
-            } else {
-                float* st = s->stage;   // [row - r0][R]
-                consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
-                    tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
-                    if (lane < n * R) st[(row0 - r0 + lane / R) * R + lane % R] = wo_[lane];
-                });
-                ll_fetch(a, s, xlt(a, l, 0, 0), R * LORA_R / 2, f, s->lt, ok);
-                named_bar_sync(1, MEGA_NCT);
-                for (int e = tid; e < (r1 - r0) * R; e += MEGA_NCT) {
-                    const int o = r0 + e / R, r = e % R;
-                    const float* bt = a.lb_qkv[l] + (int64_t)o * LORA_R;
-                    float d = 0.f;
-#pragma unroll
-                    for (int j = 0; j < LORA_R; ++j) d += __ldg(bt + j) * s->lt[r * LORA_R + j];
-                    ll_st(xqkv(a, l, r) + o, st[e] + d, f);
+            consume_rows(g, r0, r1, 4, [&](const unsigned char* tile, int row0, int n) {
+                tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
+                if (lane < n * R) {
+                    const int r = lane % R, o = row0 + lane / R;
+                    float v = wo_[lane];
+                    if (lora) v += adapter_corr(a.lb_qkv[l], o, s->lt + r * LORA_R);
+                    a.qkv[(int64_t)r * QKV + o] = v;
                 }
-            }
+            });
             stamp(a, l, 1);
-            // gate logits xn . Wg + b of two heads on each of the last H/2 CTAs
+            stamp(a, l, 2);
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 3);
+        }
+        // ---------------- phase B: attention (items owned by this CTA: cta, cta + C, ...)
+        {
+            // gate logits xn . Wg + b of two heads on each of the last H/2 CTAs, first (xs
+            // still holds xn; the attention items reuse it)
             if (cta >= C - H / 2) {
                 const int gr = 2 * (cta - (C - H / 2));
                 consume_rows(g, gr, gr + 2, 2, [&](const unsigned char* tile, int row0, int n) {
                     tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xs, s->xoff, wo_);
                     if (lane < n * R) {
                         const int h = row0 + lane / R;
-                        ll_st(xgate(a, l, lane % R) + h, wo_[lane] + a.gate_b[l][h], f);
+                        a.gate[(lane % R) * H + h] = wo_[lane] + a.gate_b[l][h];
                     }
                 });
+                named_bar_sync(1, MEGA_NCT);   // xs is scratch for the items below
             }
-            stamp(a, l, 2);
-            // xs is scratch for the attention items below
-            if (named_bar_or(1, MEGA_NCT, !ok || !g.ok)) goto done;
-            stamp(a, l, 3);
-        }
-        // ---------------- phase B: attention (items owned by this CTA: cta, cta + C, ...)
-        {
             int total = 0;
             for (int b = 0; b < s->n_blk; ++b) total += HKV * s->blk_nch[b];
             bool first = true;
@@ -1177,73 +1176,114 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 while (rem >= HKV * s->blk_nch[b]) { rem -= HKV * s->blk_nch[b]; ++b; }
                 const int nch = s->blk_nch[b];
                 const int r0 = s->blk_r0[b], nr = s->blk_r0[b + 1] - r0;
-                attn_item<R, KVT>(a, s, g, l, r0, nr, rem / nch, rem % nch, s->blk_chunk[b], f, first, ok);
+                attn_item<R, KVT>(a, s, g, l, r0, nr, rem / nch, rem % nch, s->blk_chunk[b], first);
                 first = false;
             }
             stamp(a, l, 4);
+            if (!grid_sync(a, s, epoch)) goto done;
             stamp(a, l, 5);
         }
         // ---------------- phase B2: merge the chunk partials of each (row, head) and gate
-        // (units on the last CTAs, which have the fewest attention items)
         {
-            for (int u = C - 1 - cta; u < R * H; u += C) {
+            for (int u = cta; u < R * H; u += C) {
                 const int r = u / H;
                 int b = 0;
                 while (s->blk_r0[b + 1] <= r) ++b;
-                attn_merge(a, s, l, r, u % H, s->blk_nch[b], f, ok);
+                attn_merge(a, s, r, u % H, s->blk_nch[b]);
             }
             stamp(a, l, 6);
-            if (named_bar_or(1, MEGA_NCT, !ok || !g.ok)) goto done;
-        }
-        // ---------------- phase C: Wo, h += (owned rows)
-        {
-            // test hook: one CTA waits for units of a flag no launch stores (bounded wait)
-            ll_fetch(a, s, xatt(a, l, 0), R * D / 2, (cta == a.stall_cta && l == 0) ? (f ^ 0x80000000u) : f, xs, ok);
-            if (named_bar_or(1, MEGA_NCT, !ok)) goto done;
+            if (!grid_sync(a, s, epoch)) goto done;
             stamp(a, l, 7);
-            if (adapter && cta < MEGA_TDES) adapter_t<R>(g, s, a, l, 1, f);
-            float* st = s->stage;   // [row - own0][R]
+        }
+        // ---------------- phase C: Wo, h += (owned rows), router partial sums of the owned rows
+        {
+            copy_g2s(xs, a.att, R * D);
+            named_bar_sync(1, MEGA_NCT);
+            if (lora) adapter_t<R>(g, s, wo_);
             consume_rows(g, own0, own1, 4, [&](const unsigned char* tile, int row0, int n) {
                 tile_gemv<R, D>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
-                if (lane < n * R) st[(row0 - own0 + lane / R) * R + lane % R] = wo_[lane];
-            });
-            if (adapter) ll_fetch(a, s, xlt(a, l, 1, 0), R * LORA_R / 2, f, s->lt, ok);
-            named_bar_sync(1, MEGA_NCT);
-            for (int e = tid; e < nown * R; e += MEGA_NCT) {
-                const int o = own0 + e / R, r = e % R;
-                float y = st[e];
-                if (adapter) {
-                    const float* bt = a.lb_wo[l] + (int64_t)o * LORA_R;
-                    float d = 0.f;
-#pragma unroll
-                    for (int j = 0; j < LORA_R; ++j) d += __ldg(bt + j) * s->lt[r * LORA_R + j];
-                    y += d;
+                if (lane < n * R) {
+                    const int r = lane % R, o = row0 + lane / R;
+                    float y = wo_[lane];
+                    if (lora) y += adapter_corr(a.lb_wo[l], o, s->lt + r * LORA_R);
+                    const float v = s->hown[(o - own0) * R + r] + y;
+                    s->hown[(o - own0) * R + r] = v;
+                    a.h[(int64_t)r * D + o] = v;
                 }
-                const float v = s->hown[e] + y;
-                s->hown[e] = v;
-                ll_st(xh(a, l, 0, r) + o, v, f);
+            });
+            named_bar_sync(1, MEGA_NCT);
+            // z[r][e] = sum over owned o of router[e][o] * mlp_norm[o] * h[r][o]  (logit = z / rms)
+            for (int t = threadIdx.x - 32; t < R * E; t += MEGA_NCT) {
+                const int r = t / E, e = t % E;
+                float z = 0.f;
+                for (int oi = 0; oi < nown; ++oi) z += s->rwn[l][e][oi] * s->hown[oi * R + r];
+                a.rpart[((int64_t)cta * R + r) * E + e] = z;
             }
             stamp(a, l, 8);
-            if (named_bar_or(1, MEGA_NCT, !ok || !g.ok)) goto done;
-        }
-        // ---------------- phase D: router, shared + routed up-projections
-        {
-            ll_fetch(a, s, xh(a, l, 0, 0), R * D / 2, f, xs, ok);
-            if (named_bar_or(1, MEGA_NCT, !ok)) goto done;
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
             stamp(a, l, 9);
-            norm_inplace<R>(xs, a.mlp_norm[l], eps, s->nred);
+        }
+        // ---------------- phase D: router (sum of the CTAs' partials), shared + routed up-projections
+        {
+            float ebias_lane;
+            {
+                // router logits = fixed-order sum over CTAs of the partials / rms: thread t adds
+                // float4 column t % (R*E/4) of CTAs t / (R*E/4), + G, ... (its loads issued
+                // before the norm's), then a warp per row adds the G group sums
+                constexpr int NC4 = R * E / 4;
+                constexpr int G = MEGA_NCT / NC4;
+                constexpr int MAXL = (148 + G - 1) / G;   // loads per thread kept in flight
+                const int t = threadIdx.x - 32;
+                const int col = t % NC4, cg = t / NC4;
+                const bool active = t < G * NC4;
+                const float4* src = reinterpret_cast<const float4*>(a.rpart) + col;
+                float4 pv[MAXL];
+                ebias_lane = (lane < E) ? s->ebias[l][lane] : 0.f;   // for the top-k below
+#pragma unroll
+                for (int k = 0; k < MAXL; ++k) {
+                    const int c = cg + k * G;
+                    pv[k] = (active && c < C) ? __ldcg(src + (int64_t)c * NC4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                norm_rows<R>(a.h, a.mlp_norm[l], eps, xs, s->nred, s->rinv);
+                rstamp(a, l, 0);
+                if (active) {
+                    float4 z = pv[0];
+#pragma unroll
+                    for (int k = 1; k < MAXL; ++k) {
+                        z.x += pv[k].x;
+                        z.y += pv[k].y;
+                        z.z += pv[k].z;
+                        z.w += pv[k].w;
+                    }
+                    for (int c = cg + MAXL * G; c < C; c += G) {   // grids above 148 CTAs
+                        const float4 v = __ldcg(src + (int64_t)c * NC4);
+                        z.x += v.x;
+                        z.y += v.y;
+                        z.z += v.z;
+                        z.w += v.w;
+                    }
+                    reinterpret_cast<float4*>(s->stage)[cg * NC4 + col] = z;
+                }
+                rstamp(a, l, 1);
+            }
             named_bar_sync(1, MEGA_NCT);
-            // router logits of every row from the fp32 router rows (two per tile)
-            consume_rows(g, 0, E, 2, [&](const unsigned char* tile, int row0, int n) {
-                tile_gemv_f32<R>(reinterpret_cast<const float*>(tile), n, xs, s->xoff, wo_);
-                if (lane < n * R) s->rlog[lane % R][row0 + lane / R] = wo_[lane];
-            });
-            named_bar_sync(1, MEGA_NCT);
-            // a warp per row: centre, sigmoid; top-4 of s + bias by rank (expert e is chosen
-            // iff fewer than 4 experts beat it, ties to the lower expert), weights
-            const float ebias_lane = (lane < E) ? s->ebias[l][lane] : 0.f;
+            rstamp(a, l, 2);
+            // a warp per row: logit of expert e = lanes e and e + 16 adding the even / odd
+            // groups of the staged sums; centre, sigmoid; top-4 of s + bias by rank (expert e
+            // is chosen iff fewer than 4 experts beat it, ties to the lower expert), weights
             for (int r = cw; r < R; r += MEGA_NCW) {
-                const float lg = lane < E ? s->rlog[r][lane] : 0.f;
+                constexpr int G = MEGA_NCT / (R * E / 4);
+                const int e = lane & (E - 1), hf = lane >> 4;
+                float z0 = 0.f, z1 = 0.f;
+#pragma unroll 8
+                for (int k = hf; k < G; k += 4) {
+                    z0 += s->stage[k * R * E + r * E + e];
+                    if (k + 2 < G) z1 += s->stage[(k + 2) * R * E + r * E + e];
+                }
+                float z = z0 + z1;
+                z += __shfl_xor_sync(0xffffffffu, z, 16);
+                const float lg = lane < E ? z * s->rinv[r] : 0.f;
                 const float mean = warp_sum(lg) / (float)E;
                 const float sg = sigmoidf_(lg - mean);
                 const float b = sg + ebias_lane;
@@ -1272,6 +1312,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 if (lane == 0) s->rmask[r] = used;
             }
             if constexpr (R > 1) named_bar_sync(1, MEGA_NCT);   // every row's expert mask
+            rstamp(a, l, 3);
             if (cw == 0) {
                 unsigned used = 0;
                 __syncwarp();
@@ -1289,16 +1330,16 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             named_bar_sync(1, MEGA_NCT);
             stamp(a, l, 10);
             if (cta == 0 && threadIdx.x == 32) atomicAdd(a.experts, (unsigned long long)s->n_e);
-            // phase E: act row of each row for every routed expert (or -1)
-            for (int t = tid; t < s->n_e * R; t += MEGA_NCT) {
+            // phase E: X row of each row for every routed expert (act_r row, or -1)
+            for (int t = threadIdx.x - 32; t < s->n_e * R; t += MEGA_NCT) {
                 const int ei = t / R, r = t % R;
                 int off = -1;
 #pragma unroll
                 for (int k = 0; k < TOPK; ++k)
-                    if (s->idx[r][k] == s->elist[ei]) off = r * MEGA_ACT + DS + k * DE;
+                    if (s->idx[r][k] == s->elist[ei]) off = R * DS + (r * TOPK + k) * DE;
                 s->xoff_e[ei][r] = off;
             }
-            for (int t = tid; t < R * TOPK; t += MEGA_NCT) {
+            for (int t = threadIdx.x - 32; t < R * TOPK; t += MEGA_NCT) {
                 const int r = t / TOPK, k = t % TOPK;
                 const int ex = s->idx[r][k];
                 int ei = 0;
@@ -1337,80 +1378,92 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             }
             stamp(a, l, 11);
             named_bar_sync(1, MEGA_NCT);
-            // SwiGLU epilogue -> act units: shared [r][0 .. DS), routed [r][DS + k*DE + j]
-            for (int e = tid; e < (nsh + q1 - q0) * R; e += MEGA_NCT) {
+            // SwiGLU epilogue -> act_sh [R][1024], act_r [R][4][512]
+            for (int e = threadIdx.x - 32; e < (nsh + q1 - q0) * R; e += MEGA_NCT) {
                 const int pi = e / R, r = e % R;
                 const float v = siluf_(st_g[pi * R + r]) * st_u[pi * R + r];
                 if (pi < nsh) {
-                    ll_st(xact(a, l, r) + s0 + pi, v, f);
+                    a.act_sh[(int64_t)r * DS + s0 + pi] = v;
                 } else {
                     const int q = q0 + pi - nsh;
                     const int ei = q / DE, j = q % DE;
                     const int ex = s->elist[ei];
 #pragma unroll
                     for (int k = 0; k < TOPK; ++k)
-                        if (s->idx[r][k] == ex) ll_st(xact(a, l, r) + DS + k * DE + j, v, f);
+                        if (s->idx[r][k] == ex) a.act_r[((int64_t)r * TOPK + k) * DE + j] = v;
                 }
             }
             stamp(a, l, 12);
-            if (named_bar_or(1, MEGA_NCT, !ok || !g.ok)) goto done;
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
+            stamp(a, l, 13);
         }
         // ---------------- phase E: down projections + combine, h += (owned rows)
         {
-            ll_fetch(a, s, xact(a, l, 0), R * MEGA_ACT / 2, f, xs, ok);
-            if (tid < R) s->xoff[tid] = tid * MEGA_ACT;   // shared act rows
-            if (named_bar_or(1, MEGA_NCT, !ok)) goto done;
-            stamp(a, l, 13);
+            copy_g2s(xs, a.act_sh, R * DS);
+            copy_g2s(xs + R * DS, a.act_r, R * TOPK * DE);
+            named_bar_sync(1, MEGA_NCT);
+            stamp(a, l, 14);
             const int n_e = s->n_e;
+            int o0, o1;
+            rows_split(D, cta, C, o0, o1);
             float* dsh = s->stage;                                   // [orow][R]
             float* dex = s->stage + MEGA_MAXOROWS * R;               // [orow][ei][R]
-            consume_rows(g, own0, own1, 4, [&](const unsigned char* tile, int row0, int n) {
+            consume_rows(g, o0, o1, 4, [&](const unsigned char* tile, int row0, int n) {
                 tile_gemv<R, DS>(reinterpret_cast<const __nv_bfloat16*>(tile), n, xs, s->xoff, wo_);
-                if (lane < n * R) dsh[(row0 - own0 + lane / R) * R + lane % R] = wo_[lane];
+                if (lane < n * R) dsh[(row0 - o0 + lane / R) * R + lane % R] = wo_[lane];
             });
             for (int ei = 0; ei < n_e; ++ei) {
-                consume_rows(g, own0, own1, 8, [&](const unsigned char* tile, int row0, int n) {
+                consume_rows(g, o0, o1, 8, [&](const unsigned char* tile, int row0, int n) {
                     const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(tile);
                     for (int half = 0; half < 2; ++half) {
                         const int nn = min(4, n - half * 4);
                         if (nn <= 0) break;
                         tile_gemv<R, DE>(w + half * 4 * DE, nn, xs, s->xoff_e[ei], wo_);
                         if (lane < nn * R)
-                            dex[((row0 + half * 4 - own0 + lane / R) * E + ei) * R + lane % R] = wo_[lane];
+                            dex[((row0 + half * 4 - o0 + lane / R) * E + ei) * R + lane % R] = wo_[lane];
                         __syncwarp();
                     }
                 });
             }
             named_bar_sync(1, MEGA_NCT);
-            stamp(a, l, 14);
-            if (tid < R) s->xoff[tid] = tid * D;   // back to [R][D] activation rows
-            const bool last = l == NL - 1;
-            for (int e = tid; e < nown * R; e += MEGA_NCT) {
+            if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 130 + 8 * l + 6] = globaltimer();
+            for (int e = threadIdx.x - 32; e < (o1 - o0) * R; e += MEGA_NCT) {
                 const int oi = e / R, r = e % R;
-                const int o = own0 + oi;
+                const int o = o0 + oi;
                 float routed = 0.f;
 #pragma unroll
                 for (int k = 0; k < TOPK; ++k) routed = routed + dex[(oi * E + s->eslot[r][k]) * R + r] * s->wts[r][k];
-                const float v = s->hown[e] + (dsh[e] + routed * s->rsc[l][oi]);
-                s->hown[e] = v;
-                if (!last) {
-                    ll_st(xh(a, l, 1, r) + o, v, f);
-                } else {   // the pulse output h_in + (h - h_in) * res_scale
-                    const float hi = s->hin[e];
-                    const float out = hi + (v - hi) * __ldg(a.res_scale + o);
-                    a.h_out[(int64_t)r * a.hstride * D + o] = out;
-                    ll_st(xh(a, l, 1, r) + o, out, f);
-                }
+                const float v = s->hown[oi * R + r] + (dsh[oi * R + r] + routed * s->rsc[l][oi]);
+                s->hown[oi * R + r] = v;
+                a.h[(int64_t)r * D + o] = v;
             }
+            if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 130 + 8 * l + 7] = globaltimer();
+            if (!g.ok) atomicExch(a.err, 1);
+            if (!grid_sync(a, s, epoch)) goto done;
             stamp(a, l, 15);
-            if (named_bar_or(1, MEGA_NCT, !ok || !g.ok)) goto done;
         }
     }
-    // ---------------- final norm + LM head
-    if (want_lm) {
-        ll_fetch(a, s, xh(a, NL - 1, 1, 0), R * D / 2, f, xs, ok);
-        if (named_bar_or(1, MEGA_NCT, !ok)) goto done;
-        norm_inplace<R>(xs, a.fnorm, eps, s->nred);
+    // ---------------- end of pulse + LM head
+    {
+        for (int r = cw; r < R; r += MEGA_NCW) {
+            float v[32];
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {   // loads only: all of them in flight
+                const int d = i * 32 + lane;
+                const float hi = __ldcg(a.h_in + r * D + d);
+                v[i] = hi + (__ldcg(a.h + r * D + d) - hi) * __ldg(a.res_scale + d);
+                ss += v[i] * v[i];
+            }
+            const float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+            if (cta == 0)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) a.h_out[(int64_t)r * a.hstride * D + i * 32 + lane] = v[i];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xs[r * D + i * 32 + lane] = __ldg(a.fnorm + i * 32 + lane) * (v[i] * inv);
+        }
+        if (!want_lm) goto done;
         named_bar_sync(1, MEGA_NCT);
         if (a.trace && threadIdx.x == 32) a.trace[blockIdx.x * MEGA_TRACE + 202] = globaltimer();
         ArgMax best[R];
@@ -1447,8 +1500,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 bi[cw * R + r] = best[r].i;
             }
         named_bar_sync(1, MEGA_NCT);
-        if (tid < R) {
-            const int r = tid;
+        if (threadIdx.x - 32 < R) {
+            const int r = threadIdx.x - 32;
             ArgMax b{bv[r], bi[r]};
             for (int w = 1; w < MEGA_NCW; ++w) b = argmax_merge(b, ArgMax{bv[w * R + r], bi[w * R + r]});
             a.pmax[r * C + cta] = b.v;
@@ -1457,9 +1510,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
         __threadfence();
         named_bar_sync(1, MEGA_NCT);
         if (threadIdx.x == 32) {
-            const unsigned t = atomicAdd(&a.tickets[0], 1u);
+            const unsigned t = atomicAdd(&a.tickets[MEGA_RMAX * HKV], 1u);
             s->ticket = (t == (unsigned)(C - 1));
-            if (s->ticket) a.tickets[0] = 0;
+            if (s->ticket) a.tickets[MEGA_RMAX * HKV] = 0;
             __threadfence();
         }
         named_bar_sync(1, MEGA_NCT);
@@ -1484,7 +1537,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 if (lane == 0) a.amax[r] = b.i;
             }
         }
-        if (!g.ok) raise_abort(a, s);
+        if (!g.ok) atomicExch(a.err, 1);
     }
 done:
     mega_leave(a);
