@@ -268,8 +268,8 @@ int pulsar_engine_early_exit_counts(pulsar_engine* eng, int64_t* counts_host);
  * (1 when some loop-adapter lora_B is non-zero; every path, the persistent kernel included,
  * applies it exactly in fp32), "wait_ns" (bound of every wait inside the persistent kernel,
  * 1e5 .. 2e9 ns, default 2e9), "stall_cta" (test hook, default -1: CTA c >= 0 of every persistent
- * launch waits at its first grid barrier for one arrival more than the grid has, so the bounded
- * wait runs out and the call reports PULSAR_ERR_CUDA; nothing faults or hangs),
+ * launch waits at its first grid barrier for a count the grid never reaches, so the bounded wait
+ * runs out and the call reports PULSAR_ERR_CUDA; nothing faults or hangs),
  * "wide" (0/1): run every pulse pass through the many-row GEMM path; read-only "wide_rows"
  * (row capacity of a pass). "kernel_launches" (kernels started by generate_* and pulse since
  * create, each kernel

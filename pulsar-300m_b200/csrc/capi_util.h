@@ -15,6 +15,10 @@ namespace pulsar {
 void set_error(const char* fmt, ...);
 void clear_error();
 
+// cudaFuncSetAttribute(fn, MaxDynamicSharedMemorySize, bytes) once per (kernel, device): the
+// attribute belongs to the device current when it is set, so each GPU a process uses needs it.
+int ensure_smem_attr(const void* fn, int bytes, const char* what);
+
 inline int cuda_status(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return PULSAR_OK;
     set_error("%s: %s", what, cudaGetErrorString(e));

@@ -699,10 +699,11 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
             e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
             local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
-        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, (R + e->attn_rpb - 1) / e->attn_rpb), 128,
-                             attn_decode_smem(e->attn_rpb), st>>>(rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0,
-                                                                  e->nch[l], w.part, e->max_pos(), e->cfg.max_batch);
-        k_attn_combine<<<R, H * 32, 0, st>>>(w.part, e->nch[l], w.xn,
+        const int groups = (R + e->attn_rpb - 1) / e->attn_rpb;
+        const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l]);
+        k_attn_flash<KVT><<<dim3(nsplit, HKV, groups), ATT_FTHREADS, attn_flash_smem<KVT>(), st>>>(
+            rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0, nsplit, w.part, e->max_pos(), e->cfg.max_batch, e->m_err);
+        k_attn_combine<<<R, H * 32, 0, st>>>(w.part, nsplit, w.xn,
                                              e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
@@ -882,13 +883,8 @@ int gemm(pulsar_engine* e, const GemmArgs& g, int batches, cudaStream_t st) {
                       (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 4 == 0 && g.a_stride % 4 == 0 &&
                       (int64_t)batches * g.M * g.K <= e->split_elems;
     if (e->use_tc && fits) {
-        static bool configured = false;   // per instantiation
-        if (!configured) {
-            PULSAR_TRY(cuda_status(cudaFuncSetAttribute(k_tc_gemm<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)tc_smem_bytes<BN>()),
-                                   "k_tc_gemm shared memory"));
-            configured = true;
-        }
+        PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_tc_gemm<EPI, BN>), (int)tc_smem_bytes<BN>(),
+                                    "k_tc_gemm shared memory"));
         const int64_t per_batch = (int64_t)g.M * g.K / 8;
         k_split_hilo<<<dim3((unsigned)((per_batch + 255) / 256), batches), 256, 0, st>>>(g, e->split_hi, e->split_lo);
         PULSAR_TRY(launch_status("k_split_hilo"));
@@ -1042,10 +1038,11 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
             e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
             local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
-        k_attn_decode<KVT><<<dim3(e->nch[l], HKV, (R + e->attn_rpb - 1) / e->attn_rpb), 128,
-                             attn_decode_smem(e->attn_rpb), st>>>(rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0,
-                                                                  e->nch[l], w.part, e->max_pos(), e->cfg.max_batch);
-        k_attn_combine<<<R, H * 32, 0, st>>>(w.part, e->nch[l], w.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
+        const int groups = (R + e->attn_rpb - 1) / e->attn_rpb;
+        const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l]);
+        k_attn_flash<KVT><<<dim3(nsplit, HKV, groups), ATT_FTHREADS, attn_flash_smem<KVT>(), st>>>(
+            rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0, nsplit, w.part, e->max_pos(), e->cfg.max_batch, e->m_err);
+        k_attn_combine<<<R, H * 32, 0, st>>>(w.part, nsplit, w.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
         PULSAR_LAUNCH_CHECK("wide attention");
@@ -1233,7 +1230,7 @@ int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
         PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->hblk + (int64_t)j * D, e->h0blk + (int64_t)j * D,
                          nullptr, 0, j < g ? e->amax : nullptr, st, g + 1));
     }
-    e->attn_rpb = g + 1;   // verify blocks: one K/V staging per block in the split-K attention
+    e->attn_rpb = g + 1;   // verify blocks: one pass over each chunk of K/V per block in the attention
     const int v1 = pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st);
     const int v2 = v1 ? v1 : pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, nullptr, 0, e->amax, st);
     e->attn_rpb = 1;
@@ -1263,7 +1260,7 @@ int body_round_sampled(pulsar_engine* e, cudaStream_t st, void* vctx) {
             PULSAR_LAUNCH_CHECK("k_warp_sample");
         }
     }
-    e->attn_rpb = g + 1;   // verify blocks: one K/V staging per block in the split-K attention
+    e->attn_rpb = g + 1;   // verify blocks: one pass over each chunk of K/V per block in the attention
     const int v1 = pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st);
     const int v2 = v1 ? v1 : pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, e->pbuf, V, nullptr, st);
     e->attn_rpb = 1;
@@ -1408,13 +1405,13 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         if ((st = cuda_status(cudaFuncSetAttribute(k_warp_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    SAMPLE_MAX_V * (int)sizeof(float)),
                               "k_warp_sample shared memory")) ||
-            (st = cuda_status(cudaFuncSetAttribute(k_attn_decode<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)attn_decode_smem(ATT_RPB_MAX)),
-                              "k_attn_decode shared memory")) ||
-            (st = cuda_status(cudaFuncSetAttribute(k_attn_decode<__nv_bfloat16>,
+            (st = cuda_status(cudaFuncSetAttribute(k_attn_flash<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)attn_flash_smem<float>()),
+                              "k_attn_flash shared memory")) ||
+            (st = cuda_status(cudaFuncSetAttribute(k_attn_flash<__nv_bfloat16>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)attn_decode_smem(ATT_RPB_MAX)),
-                              "k_attn_decode shared memory")))
+                                                   (int)attn_flash_smem<__nv_bfloat16>()),
+                              "k_attn_flash shared memory")))
             return fail(st);
         // the per-CTA staging sizes assume >= 144 CTAs (ceil(8192 / C) + ceil(1024 / C) <= 64 pairs)
         e->mega_grid = sms;

@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "kv.cuh"
+#include "mega_ptx.cuh"
 
 namespace pulsar {
 
@@ -283,33 +284,74 @@ __global__ void __launch_bounds__((H + HKV) * 32) k_qkv_post(
     }
 }
 
-// Split-K decode attention: block (chunk c, kv head g, group of rpb rows), 128 threads. A group
-// is cut into runs of consecutive rows of one slot at consecutive positions (a verify block);
-// each run stages its chunk of cached K/V - keys lo_first + [c * 128, c * 128 + 128), lo_first
-// the run's first row's window start - once in shared memory with 16-byte loads, and every row
-// of the run scores it under its own mask [lo_r, pos_r] (lo_r = pos_r - WINDOW + 1 on local
-// layers). Writes per q head (m, l, o[64]) of its chunk; a chunk with no visible key writes
-// m = -inf. Rows with an invalid slot or position read nothing. Dynamic shared memory:
-// attn_decode_smem(rpb) bytes.
+// Flash-decoding attention of the per-op and many-row pulse passes. Block (split sp, kv head
+// g, group of rpb rows), 256 threads. A group is cut into runs of consecutive rows of one slot
+// at consecutive positions (a verify block). For each run the block walks the chunks
+// sp, sp + nsplit, ... of ATT_FCK keys (keys lo_first + [c * ATT_FCK, ...), lo_first the run's
+// first row's window start) with an online softmax: the chunk's cached K and V rows arrive as
+// stored (bf16 or fp32) by 1-D bulk copies into a two-stage shared-memory ring, two chunks ahead
+// of the compute; every row scores them under its own mask [lo_r, pos_r]. Per (row, q head)
+// the split writes (m, l, o[64]) (o not yet divided by l; m = -inf when no key was visible) at
+// partial index sp of a stride of nsplit, which k_attn_combine merges. Rows with an invalid
+// slot or position read nothing. A bulk copy that has not landed after a 2 s wait sets *err.
 constexpr int ATT_RPB_MAX = 8;
-constexpr int ATT_KST = DH + 1;   // shared row stride of the staged K / V (conflict-free columns)
-__host__ __device__ constexpr size_t attn_decode_smem(int rpb) {
-    return (size_t)(2 * ATT_CHUNK * ATT_KST + rpb * GQA * DH + rpb * GQA * ATT_CHUNK) * sizeof(float);
+constexpr int ATT_FCK = 64;          // keys per chunk
+constexpr int ATT_FTHREADS = 256;
+template <typename KVT>
+struct AttnFlashSmem {
+    uint64_t full[2];
+    alignas(128) KVT k[2][ATT_FCK * DH];
+    alignas(128) KVT v[2][ATT_FCK * DH];
+    alignas(16) float q[ATT_RPB_MAX * GQA][DH];
+    alignas(16) float sc[ATT_RPB_MAX * GQA][ATT_FCK];
+    float m[ATT_RPB_MAX * GQA], l[ATT_RPB_MAX * GQA], scale[ATT_RPB_MAX * GQA];
+};
+
+// Issue the bulk copies of chunk [k0, k0 + nk) of (slot, head g) into ring stage st (one thread).
+template <typename KVT>
+__device__ __forceinline__ void attn_issue(AttnFlashSmem<KVT>* s, int st, const KVLayer& L, int slot, int g, int k0,
+                                           int nk) {
+    constexpr uint32_t ROW = DH * sizeof(KVT);
+    mbar_arrive_expect_tx(&s->full[st], 2u * nk * ROW);
+    const int i0 = k0 & L.mask;
+    const int m1 = (L.mask >= 0 && i0 + nk > L.cap) ? L.cap - i0 : nk;   // a run wrapping around the ring
+    for (int isv = 0; isv < 2; ++isv) {
+        KVT* dst = isv ? s->v[st] : s->k[st];
+        const KVT* p0 = isv ? kv_v<KVT>(L, slot, g, k0) : kv_k<KVT>(L, slot, g, k0);
+        tma_load_1d(dst, p0, (uint32_t)m1 * ROW, &s->full[st]);
+        if (m1 < nk) {
+            const KVT* p1 = isv ? kv_v<KVT>(L, slot, g, k0 + m1) : kv_k<KVT>(L, slot, g, k0 + m1);
+            tma_load_1d(reinterpret_cast<unsigned char*>(dst) + m1 * ROW, p1, (uint32_t)(nk - m1) * ROW, &s->full[st]);
+        }
+    }
 }
 
+__device__ __forceinline__ float2 attn_pair(const __nv_bfloat16* row, int w) {
+    return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row)[w]);
+}
+__device__ __forceinline__ float2 attn_pair(const float* row, int w) { return reinterpret_cast<const float2*>(row)[w]; }
+__device__ __forceinline__ float attn_elem(const __nv_bfloat16* row, int d) { return __bfloat162float(row[d]); }
+__device__ __forceinline__ float attn_elem(const float* row, int d) { return row[d]; }
+
 template <typename KVT>
-__global__ void __launch_bounds__(128) k_attn_decode(const int4* __restrict__ rows, int R, int rpb,
-                                                     const float* __restrict__ q, KVLayer L, int is_local, int nchunk,
-                                                     float* __restrict__ part, int max_pos, int n_slots) {
-    extern __shared__ float sm_att[];
-    float* Ks = sm_att;                        // [128][65]
-    float* Vs = Ks + ATT_CHUNK * ATT_KST;      // [128][65]
-    float* qs = Vs + ATT_CHUNK * ATT_KST;      // [rows][4][64]
-    float* ps = qs + rpb * GQA * DH;           // [rows][4][128]
-    const int c = blockIdx.x, g = blockIdx.y;
+__global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restrict__ rows, int R, int rpb,
+                                                             const float* __restrict__ q, KVLayer L, int is_local,
+                                                             int nsplit, float* __restrict__ part, int max_pos,
+                                                             int n_slots, int* err) {
+    extern __shared__ __align__(128) unsigned char att_raw[];
+    auto* s = reinterpret_cast<AttnFlashSmem<KVT>*>(att_raw);
+    const int sp = blockIdx.x, g = blockIdx.y;
     const int rb0 = blockIdx.z * rpb, rb1 = min(R, rb0 + rpb);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int key = tid & (ATT_FCK - 1), grp = tid >> 6;   // scores / P.V: key or dimension, unit group
     auto bad_row = [&](const int4& rw) { return rw.y < 0 || rw.y >= max_pos || rw.x < 0 || rw.x >= n_slots; };
+    if (tid == 0) {
+        mbar_init(&s->full[0], 1);
+        mbar_init(&s->full[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    uint32_t uses[2] = {0u, 0u};   // completed phases of each stage's barrier
     for (int s0 = rb0; s0 < rb1;) {
         const int4 first = rows[s0];
         int s1 = s0 + 1;
@@ -319,139 +361,147 @@ __global__ void __launch_bounds__(128) k_attn_decode(const int4* __restrict__ ro
                 if (bad_row(nx) || nx.x != first.x || nx.y != rows[s1 - 1].y + 1) break;
                 ++s1;
             }
-        const int nr = s1 - s0;
+        const int nr = s1 - s0, nq = nr * GQA;
         const int posF = first.y, posL = posF + nr - 1;
         const int lo0 = is_local ? max(0, posF - WINDOW + 1) : 0;
-        const int k0 = lo0 + c * ATT_CHUNK;
-        const int k1 = bad_row(first) ? k0 : min(k0 + ATT_CHUNK, posL + 1);
-        const int nk = max(0, k1 - k0);
-        if (nk == 0) {   // no key of this chunk is visible to the run's rows
-            if (tid < nr * GQA) part[(((int64_t)(s0 + tid / GQA) * H + g * GQA + tid % GQA) * nchunk + c) * PART] = -INFINITY;
-            if (tid < nr * GQA) part[(((int64_t)(s0 + tid / GQA) * H + g * GQA + tid % GQA) * nchunk + c) * PART + 1] = 0.f;
-            s0 = s1;
-            continue;
+        const int nchunks = bad_row(first) ? 0 : (posL - lo0 + ATT_FCK) / ATT_FCK;
+        const int mine = nchunks > sp ? (nchunks - sp + nsplit - 1) / nsplit : 0;   // chunks of this split
+        // queries of the run (fp32, already normed and rotated), the online-softmax state
+        for (int i = tid; i < nq * DH; i += ATT_FTHREADS)
+            s->q[i / DH][i % DH] = q[((int64_t)(s0 + i / (GQA * DH)) * H + g * GQA) * DH + i % (GQA * DH)] * 0.125f;
+        if (tid < nq) {
+            s->m[tid] = -INFINITY;
+            s->l[tid] = 0.f;
         }
-        // stage K and V rows [k0, k1) (fp32, stride 65) and the run's queries: eight 16-byte
-        // loads per thread in flight before any is converted and stored
-        constexpr int EPP = 16 / (int)sizeof(KVT);   // elements per 16-byte piece
-        constexpr int PIECES = DH / EPP;
-        const int npc = 2 * nk * PIECES;
-        for (int b0 = 0; b0 < npc; b0 += 8 * 128) {
-            uint4 u[8];
+        auto chunk_k0 = [&](int i) { return lo0 + (sp + i * nsplit) * ATT_FCK; };
+        auto chunk_nk = [&](int i) { return min(chunk_k0(i) + ATT_FCK, posL + 1) - chunk_k0(i); };
+        if (tid == 0)
+            for (int i = 0; i < 2 && i < mine; ++i) attn_issue<KVT>(s, i, L, first.x, g, chunk_k0(i), chunk_nk(i));
+        float o[ATT_RPB_MAX];   // P.V accumulators of dimension `key` for units grp, grp + 4, ...
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int e = b0 + j * 128 + tid;
-                if (e < npc) {
-                    const int isv = e >= nk * PIECES;
-                    const int ee = isv ? e - nk * PIECES : e;
-                    const int kk = ee / PIECES, pc = ee % PIECES;
-                    const KVT* src = (isv ? kv_v<KVT>(L, first.x, g, k0 + kk) : kv_k<KVT>(L, first.x, g, k0 + kk)) + pc * EPP;
-                    u[j] = __ldg(reinterpret_cast<const uint4*>(src));
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int e = b0 + j * 128 + tid;
-                if (e < npc) {
-                    const int isv = e >= nk * PIECES;
-                    const int ee = isv ? e - nk * PIECES : e;
-                    const int kk = ee / PIECES, pc = ee % PIECES;
-                    float* dst = (isv ? Vs : Ks) + kk * ATT_KST + pc * EPP;
-                    if constexpr (sizeof(KVT) == 2) {
-                        const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float2 f = __bfloat1622float2(bp[i]);
-                            dst[2 * i] = f.x;
-                            dst[2 * i + 1] = f.y;
-                        }
-                    } else {
-                        dst[0] = __uint_as_float(u[j].x);
-                        dst[1] = __uint_as_float(u[j].y);
-                        dst[2] = __uint_as_float(u[j].z);
-                        dst[3] = __uint_as_float(u[j].w);
-                    }
-                }
-            }
-        }
-        for (int i = tid; i < nr * GQA * DH; i += 128) {
-            const int rr = i / (GQA * DH), rem = i % (GQA * DH);
-            qs[i] = q[((int64_t)(s0 + rr) * H + g * GQA) * DH + rem];
-        }
+        for (int j = 0; j < ATT_RPB_MAX; ++j) o[j] = 0.f;
         __syncthreads();
-        // scores: a thread per key, every row and head of the run
-        {
-            const int kk = tid, key = k0 + kk;
-            for (int rr = 0; rr < nr; ++rr) {
-                const int pos = posF + rr;
-                const int lor = is_local ? max(0, pos - WINDOW + 1) : 0;
-                const bool vis = kk < nk && key <= pos && key >= lor;
-                float acc[GQA] = {0.f, 0.f, 0.f, 0.f};
-                if (vis) {
-                    const float* kr = Ks + kk * ATT_KST;
+        for (int i = 0; i < mine; ++i) {
+            const int st = i & 1;
+            const int k0 = chunk_k0(i), nk = chunk_nk(i);
+            // a copy that has not landed after the bounded wait ends the block (uniformly), after
+            // a second bounded wait for the copies still in flight into either stage
+            if (__syncthreads_or(!mbar_wait(&s->full[st], uses[st] & 1))) {
+                if (tid == 0) {
+                    atomicExch(err, 1);
+                    mbar_wait(&s->full[st], uses[st] & 1);
+                    if (i + 1 < mine) mbar_wait(&s->full[st ^ 1], uses[st ^ 1] & 1);
+                }
+                __syncthreads();
+                return;
+            }
+            ++uses[st];
+            const KVT* Kt = s->k[st];
+            const KVT* Vt = s->v[st];
+            // scores: thread (key, unit group); the key's row is read in rotated pair order
+            // (pair (j + lane) mod 32 at step j: one bank per lane of the warp)
+            {
+                const int kk = key, kpos = k0 + kk;
+                float acc[ATT_RPB_MAX];
+#pragma unroll
+                for (int j = 0; j < ATT_RPB_MAX; ++j) acc[j] = 0.f;
+                if (kk < nk) {
+                    const KVT* kr = Kt + kk * DH;
 #pragma unroll 4
-                    for (int d = 0; d < DH; d += 4) {
-                        const float c0 = kr[d], c1 = kr[d + 1], c2 = kr[d + 2], c3 = kr[d + 3];
+                    for (int j = 0; j < DH / 2; ++j) {
+                        const int w = (j + lane) & (DH / 2 - 1);
+                        const float2 kv = attn_pair(kr, w);
 #pragma unroll
-                        for (int h = 0; h < GQA; ++h) {
-                            const float4 qv = *reinterpret_cast<const float4*>(qs + (rr * GQA + h) * DH + d);
-                            acc[h] += qv.x * c0 + qv.y * c1 + qv.z * c2 + qv.w * c3;
+                        for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+                            const int u = grp + 4 * uu;
+                            if (u < nq) {
+                                const float2 qv = reinterpret_cast<const float2*>(s->q[u])[w];
+                                acc[uu] += qv.x * kv.x + qv.y * kv.y;
+                            }
                         }
                     }
                 }
 #pragma unroll
-                for (int h = 0; h < GQA; ++h) ps[(rr * GQA + h) * ATT_CHUNK + kk] = vis ? acc[h] * 0.125f : -INFINITY;
-            }
-        }
-        __syncthreads();
-        // softmax per (row, head): a warp per unit; weights back into ps
-        for (int u = warp; u < nr * GQA; u += 4) {
-            float* pu = ps + u * ATT_CHUNK;
-            float m = -INFINITY;
-            for (int i = lane; i < ATT_CHUNK; i += 32) m = fmaxf(m, pu[i]);
-            m = warp_max(m);
-            float l = 0.f;
-            for (int i = lane; i < ATT_CHUNK; i += 32) {
-                const float pv = (pu[i] == -INFINITY) ? 0.f : expf(pu[i] - m);
-                pu[i] = pv;
-                l += pv;
-            }
-            l = warp_sum(l);
-            float* out = part + (((int64_t)(s0 + u / GQA) * H + g * GQA + u % GQA) * nchunk + c) * PART;
-            if (lane == 0) {
-                out[0] = m;
-                out[1] = m == -INFINITY ? 0.f : l;
-            }
-        }
-        __syncthreads();
-        // P.V: thread (dimension d, head pair hp) over every row of the run, keys in order
-        {
-            const int d = tid & (DH - 1), hp = tid >> 6;
-            float o[ATT_RPB_MAX][2];
-#pragma unroll
-            for (int rr = 0; rr < ATT_RPB_MAX; ++rr) o[rr][0] = o[rr][1] = 0.f;
-            for (int kk = 0; kk < nk; ++kk) {
-                const float v = Vs[kk * ATT_KST + d];
-#pragma unroll
-                for (int rr = 0; rr < ATT_RPB_MAX; ++rr)
-                    if (rr < nr) {
-                        o[rr][0] += ps[(rr * GQA + 2 * hp) * ATT_CHUNK + kk] * v;
-                        o[rr][1] += ps[(rr * GQA + 2 * hp + 1) * ATT_CHUNK + kk] * v;
+                for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+                    const int u = grp + 4 * uu;
+                    if (u < nq) {
+                        const int pos = posF + u / GQA;
+                        const int lor = is_local ? max(0, pos - WINDOW + 1) : 0;
+                        const bool vis = kk < nk && kpos <= pos && kpos >= lor;
+                        s->sc[u][kk] = vis ? acc[uu] : -INFINITY;
                     }
+                }
             }
+            __syncthreads();
+            // online softmax: a warp per unit; weights back into sc, the rescale of the old state
+            for (int u = warp; u < nq; u += ATT_FTHREADS / 32) {
+                const float a0 = s->sc[u][lane], a1 = s->sc[u][lane + 32];
+                const float mo = s->m[u];
+                const float mn = fmaxf(mo, warp_max(fmaxf(a0, a1)));
+                const float e0 = (a0 == -INFINITY) ? 0.f : expf(a0 - mn);
+                const float e1 = (a1 == -INFINITY) ? 0.f : expf(a1 - mn);
+                const float sum = warp_sum(e0 + e1);
+                s->sc[u][lane] = e0;
+                s->sc[u][lane + 32] = e1;
+                __syncwarp();
+                if (lane == 0) {
+                    const float scl = (mo == -INFINITY) ? 0.f : expf(mo - mn);
+                    s->scale[u] = scl;
+                    s->l[u] = s->l[u] * scl + sum;
+                    s->m[u] = mn;
+                }
+            }
+            __syncthreads();
+            // P.V: thread (dimension `key`, unit group), keys in order
 #pragma unroll
-            for (int rr = 0; rr < ATT_RPB_MAX; ++rr)
-                if (rr < nr)
+            for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+                const int u = grp + 4 * uu;
+                if (u < nq) {
+                    float acc = o[uu] * s->scale[u];
+                    const float* pw = s->sc[u];
+                    for (int kk = 0; kk < nk; ++kk) acc += pw[kk] * attn_elem(Vt + kk * DH, key);
+                    o[uu] = acc;
+                }
+            }
+            __syncthreads();   // stage st is free again
+            if (tid == 0 && i + 2 < mine) attn_issue<KVT>(s, st, L, first.x, g, chunk_k0(i + 2), chunk_nk(i + 2));
+        }
+        // partial (m, l, o) of every unit at index sp
 #pragma unroll
-                    for (int j = 0; j < 2; ++j)
-                        part[(((int64_t)(s0 + rr) * H + g * GQA + 2 * hp + j) * nchunk + c) * PART + 2 + d] = o[rr][j];
+        for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+            const int u = grp + 4 * uu;
+            if (u < nq) {
+                float* out = part + (((int64_t)(s0 + u / GQA) * H + g * GQA + u % GQA) * nsplit + sp) * PART;
+                out[2 + key] = o[uu];
+                if (key == 0) {
+                    out[0] = s->m[u];
+                    out[1] = s->m[u] == -INFINITY ? 0.f : s->l[u];
+                }
+            }
         }
         __syncthreads();   // shared memory is reused by the next run
         s0 = s1;
     }
 }
 
-// Combine the chunks of each head, apply the head gate sigmoid(xn . Wg[h] + bg[h])
+template <typename KVT>
+constexpr size_t attn_flash_smem() {
+    return sizeof(AttnFlashSmem<KVT>) + 128;
+}
+
+// Splits of a flash-decoding launch: enough blocks to fill the GPU (about 6 per SM) when a pass
+// has few row groups, never more than the chunks of the longest span nor than `cap` (the
+// partial stride the buffers hold).
+inline int attn_splits(int groups, int max_span, int sms, int cap) {
+    const int base = HKV * groups;
+    int n = (6 * sms + base - 1) / base;
+    const int chunks = (max_span + ATT_FCK - 1) / ATT_FCK + 1;
+    if (n > chunks) n = chunks;
+    if (n > cap) n = cap;
+    return n < 1 ? 1 : n;
+}
+
+// Combine the split partials of each head, apply the head gate sigmoid(xn . Wg[h] + bg[h])
 // (src/infer.py:302-306) and, if the loop adapter is on, project t = A_wo . out.
 __global__ void __launch_bounds__(H * 32) k_attn_combine(const float* __restrict__ part, int nchunk,
                                                          const float* __restrict__ xn, const float* __restrict__ gw,

@@ -12,12 +12,7 @@ size_t mega_smem_bytes() { return sizeof(MegaSmem) + 128; }
 template <int R, typename KVT>
 static int launch_one(const MegaArgs& a, int grid, cudaStream_t st) {
     auto fn = k_mega_pulse<R, KVT>;
-    static bool configured = false;   // per instantiation
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mega_smem_bytes());
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(mega)");
-        configured = true;
-    }
+    PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(fn), (int)mega_smem_bytes(), "cudaFuncSetAttribute(mega)"));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(MEGA_THREADS);

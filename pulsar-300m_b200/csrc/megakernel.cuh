@@ -78,7 +78,7 @@ struct MegaArgs {
     unsigned* tickets;    // [MEGA_RMAX * HKV + 2]: [.. + 0] argmax ticket, [.. + 1] exit count (both self-resetting)
     int* err;             // error flag (non-zero: a bounded wait ran out)
     unsigned long long wait_ns;   // bound of every wait
-    int stall_cta;        // test hook: this CTA (>= 0) waits at its first grid barrier for one arrival too many
+    int stall_cta;        // test hook: this CTA (>= 0) waits at its first grid barrier for a count never reached
     unsigned long long* experts;   // running count of distinct routed experts streamed (per layer)
     const int* skip;      // optional: non-zero -> the whole pass is skipped (every row exited early)
     unsigned long long* trace;   // optional [gridDim][MEGA_TRACE] %globaltimer stamps (null: off)
@@ -332,9 +332,9 @@ __device__ __forceinline__ bool grid_sync(const MegaArgs& a, MegaSmem* s, unsign
         epoch += 1;
         // release (cumulative over the CTA's writes ordered before it by the bar.sync above)
         red_release_gpu_add(a.bar, 1u);
-        // test hook: the stalled CTA waits for one arrival more than the grid has (a bounded wait
-        // that must run out)
-        const unsigned target = epoch * gridDim.x + ((int)blockIdx.x == a.stall_cta && epoch == 1 ? 1u : 0u);
+        // test hook: the stalled CTA waits at its first barrier for a count the grid never reaches
+        // (the others stop at the next barrier, one arrival short), so its bounded wait runs out
+        const unsigned target = ((int)blockIdx.x == a.stall_cta && epoch == 1) ? ~0u : epoch * gridDim.x;
         bool ok = true;
         // one acquire poll at a time; the global error flag costs an L2 round trip of its own,
         // so it is read every 64th poll only (more polls in flight measured slower: they

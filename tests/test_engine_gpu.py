@@ -125,8 +125,11 @@ def test_rows_of_different_slots_are_independent(path):
     l2, h2, z2 = eng.pulse(0, [(0, 40, 11), (3, 70, 22)])
     la, ha, za = eng.pulse(0, [(0, 40, 11)])
     lb, hb, zb = eng.pulse(0, [(3, 70, 22)])
-    assert torch.equal(l2[0], la[0]) and torch.equal(l2[1], lb[0])
-    assert torch.equal(h2[1], hb[0])
+    # the persistent kernel's one-row pass sums the RMSNorm squares in another order than its
+    # multi-row pass, so rows agree to rounding there and bit for bit on the other paths
+    same = (lambda x, y: torch.allclose(x, y, rtol=1e-5, atol=1e-5)) if path == 0 else torch.equal
+    assert same(l2[0], la[0]) and same(l2[1], lb[0])
+    assert same(h2[1], hb[0])
 
 
 def _compare_tokens(got, ref, margins, what):

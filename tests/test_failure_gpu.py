@@ -1,7 +1,7 @@
 """Failure handling of the persistent pulse kernel, made on purpose without a GPU fault.
 
 The test hook option ``stall_cta`` makes one CTA of the persistent kernel wait at its first
-grid barrier for one arrival more than the grid has; with ``wait_ns`` shortened to 2 ms the
+grid barrier for an arrival count the grid never reaches; with ``wait_ns`` shortened to 2 ms the
 wait runs out, the kernel raises its error flag, every other CTA gives up at its next barrier
 poll, and all of them return (nothing faults, traps or hangs). The host must report the failure
 as PULSAR_ERR_CUDA with the bounded-wait message, and the very next call on the same engine
