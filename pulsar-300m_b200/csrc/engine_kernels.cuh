@@ -452,16 +452,29 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                 }
             }
             __syncthreads();
-            // P.V: thread (dimension `key`, unit group), keys in order
+            // P.V: thread (dimension `key`, unit group), keys in order; each V element is read
+            // once for all the group's units, the weights four keys at a time
+            const int nu = (nq - grp + 3) / 4;   // units of this group
 #pragma unroll
-            for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
-                const int u = grp + 4 * uu;
-                if (u < nq) {
-                    float acc = o[uu] * s->scale[u];
-                    const float* pw = s->sc[u];
-                    for (int kk = 0; kk < nk; ++kk) acc += pw[kk] * attn_elem(Vt + kk * DH, key);
-                    o[uu] = acc;
+            for (int uu = 0; uu < ATT_RPB_MAX; ++uu)
+                if (uu < nu) o[uu] *= s->scale[grp + 4 * uu];
+            int kk = 0;
+            for (; kk + 4 <= nk; kk += 4) {
+                const float v0 = attn_elem(Vt + kk * DH, key), v1 = attn_elem(Vt + (kk + 1) * DH, key);
+                const float v2 = attn_elem(Vt + (kk + 2) * DH, key), v3 = attn_elem(Vt + (kk + 3) * DH, key);
+#pragma unroll
+                for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+                    if (uu < nu) {
+                        const float4 pw = *reinterpret_cast<const float4*>(&s->sc[grp + 4 * uu][kk]);
+                        o[uu] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
+                    }
                 }
+            }
+            for (; kk < nk; ++kk) {
+                const float v = attn_elem(Vt + kk * DH, key);
+#pragma unroll
+                for (int uu = 0; uu < ATT_RPB_MAX; ++uu)
+                    if (uu < nu) o[uu] += s->sc[grp + 4 * uu][kk] * v;
             }
             __syncthreads();   // stage st is free again
             if (tid == 0 && i + 2 < mine) attn_issue<KVT>(s, st, L, first.x, g, chunk_k0(i + 2), chunk_nk(i + 2));
