@@ -408,13 +408,9 @@ __device__ __forceinline__ void norm_rows(const float* src, const float* w, floa
 }
 
 // ------------------------------------------------------------------ attention item
-// Chunk of keys per attention item. Passes of <= 2 rows (ring_chunk > 0): ring_chunk keys, four
-// ring tiles of K and four of V, which the producer streams during phase A; few items and few
-// partials to merge. Larger passes: 32 keys when the span is short (more items than CTAs would
-// otherwise sit idle), 64 keys for longer spans.
-__device__ __forceinline__ int attn_chunk(int span, int ring_chunk) {
-    return ring_chunk > 0 ? ring_chunk : (span <= 32 * 37 ? 32 : 64);
-}
+// Chunk of keys per attention item: 32 keys when the span is short (more items than CTAs
+// would otherwise sit idle), 64 keys for longer spans.
+__device__ __forceinline__ int attn_chunk(int span) { return span <= 32 * 37 ? 32 : 64; }
 
 // Copy n floats global -> shared with 16-byte loads, all issued before the stores.
 __device__ __forceinline__ void copy_g2s(float* __restrict__ dst, const float* __restrict__ src, int n) {
@@ -464,21 +460,20 @@ struct AttnGeo {
     int r0, nr, g, c, nch, chunk, slot, pos0, k0, nk, nold;
 };
 
-__device__ __forceinline__ void attn_block_chunks(const int4* rows, int r0, int r1, bool local, int ring_chunk,
-                                                  int& chunk, int& nch) {
+__device__ __forceinline__ void attn_block_chunks(const int4* rows, int r0, int r1, bool local, int& chunk, int& nch) {
     const int pos0 = rows[r0].y, posL = rows[r1 - 1].y;
     const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
-    chunk = attn_chunk(posL - lo + 1, ring_chunk);
+    chunk = attn_chunk(posL - lo + 1);
     nch = (posL - lo + chunk) / chunk;
 }
 
 // Geometry of item `item` given the block starts blk_r0[0..n_blk] (blk_r0[n_blk] = R);
 // false past the last item.
-__device__ __forceinline__ bool attn_geo(const int4* rows, const int* blk_r0, int n_blk, bool local, int ring_chunk,
-                                         int item, AttnGeo& o) {
+__device__ __forceinline__ bool attn_geo(const int4* rows, const int* blk_r0, int n_blk, bool local, int item,
+                                         AttnGeo& o) {
     for (int b = 0; b < n_blk; ++b) {
         int chunk, nch;
-        attn_block_chunks(rows, blk_r0[b], blk_r0[b + 1], local, ring_chunk, chunk, nch);
+        attn_block_chunks(rows, blk_r0[b], blk_r0[b + 1], local, chunk, nch);
         if (item < HKV * nch) {
             o.r0 = blk_r0[b];
             o.nr = blk_r0[b + 1] - blk_r0[b];
@@ -510,10 +505,6 @@ constexpr int MEGA_RING_KV_MAX_R = 2;
 template <typename KVT>
 constexpr int kv_keys_per_tile() { return MEGA_SLOT / (DH * (int)sizeof(KVT)); }
 
-// Key chunk of the items of an R-row pass (0: the 32 / 64 rule of attn_chunk).
-template <int R, typename KVT>
-constexpr int mega_ring_chunk() { return R <= MEGA_RING_KV_MAX_R ? 4 * kv_keys_per_tile<KVT>() : 0; }
-
 // Producer: cached K (isv = 0) or V rows of keys [k0, k0 + n) of (slot, head g), in tiles of
 // kv_keys_per_tile keys; a run that wraps around a local layer's ring takes two copies.
 template <typename KVT>
@@ -538,13 +529,42 @@ __device__ __forceinline__ void produce_kv(Ring& g, const KVLayer& L, int slot, 
     }
 }
 
-// Pair w (elements 2w, 2w + 1) and element d of a 64-element K/V row stored as KVT.
-__device__ __forceinline__ float2 kv_pair(const __nv_bfloat16* row, int w) {
-    return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row)[w]);
+// Consumers (all 15 warps): take the same tiles, widen them to fp32 rows of `dst` (stride
+// DH + 1), release each slot after every warp is done with it.
+template <typename KVT>
+__device__ __forceinline__ void consume_kv(Ring& g, int n, float* dst) {
+    constexpr int KPT = kv_keys_per_tile<KVT>();
+    constexpr int PARTS = DH * (int)sizeof(KVT) / 16;   // 16-byte pieces per row
+    const int tid = threadIdx.x - 32;
+    for (int k = 0; k < n; k += KPT) {
+        const int m = min(KPT, n - k);
+        const uint32_t slot_i = g.t % MEGA_NS;
+        const uint32_t use = g.t / MEGA_NS;
+        if (g.ok && !ring_wait(g, &g.s->full[slot_i], use & 1)) g.ok = false;
+        if (g.ok) {
+            const unsigned char* tile = g.s->ring[slot_i];
+            for (int e = tid; e < m * PARTS; e += MEGA_NCT) {
+                const int kk = e / PARTS, part = e % PARTS;
+                const uint4 u = *reinterpret_cast<const uint4*>(tile + kk * DH * sizeof(KVT) + part * 16);
+                float* d = dst + (k + kk) * (DH + 1);
+                if constexpr (sizeof(KVT) == 2) {
+                    float f[8];
+                    bf16x8_to_f32(u, f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) d[part * 8 + i] = f[i];
+                } else {
+                    d[part * 4 + 0] = __uint_as_float(u.x);
+                    d[part * 4 + 1] = __uint_as_float(u.y);
+                    d[part * 4 + 2] = __uint_as_float(u.z);
+                    d[part * 4 + 3] = __uint_as_float(u.w);
+                }
+            }
+        }
+        named_bar_sync(1, MEGA_NCT);
+        if (threadIdx.x == 32 && g.ok) mbar_arrive(&g.s->empty[slot_i]);
+        ++g.t;
+    }
 }
-__device__ __forceinline__ float2 kv_pair(const float* row, int w) { return reinterpret_cast<const float2*>(row)[w]; }
-__device__ __forceinline__ float kv_elem(const __nv_bfloat16* row, int d) { return __bfloat162float(row[d]); }
-__device__ __forceinline__ float kv_elem(const float* row, int d) { return row[d]; }
 
 template <int R, typename KVT>
 __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& ring, int l, int r0, int nr, int g,
@@ -628,13 +648,11 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
                     kv_store(vp + lane, v1);
                     kv_store(vp + lane + 32, v2);
                 }
-                // the stored (rounded) values, so every reader sees identical keys (passes of
-                // <= 2 rows keep only the new keys in Ks / Vs, from row 0)
-                const int krow = (R <= MEGA_RING_KV_MAX_R) ? kk - nold : kk;
-                Ks[krow * (DH + 1) + lane] = kv_round<KVT>(y1);
-                Ks[krow * (DH + 1) + lane + 32] = kv_round<KVT>(y2);
-                Vs[krow * (DH + 1) + lane] = kv_round<KVT>(v1);
-                Vs[krow * (DH + 1) + lane + 32] = kv_round<KVT>(v2);
+                // the stored (rounded) values, so every reader sees identical keys
+                Ks[kk * (DH + 1) + lane] = kv_round<KVT>(y1);
+                Ks[kk * (DH + 1) + lane + 32] = kv_round<KVT>(y2);
+                Vs[kk * (DH + 1) + lane] = kv_round<KVT>(v1);
+                Vs[kk * (DH + 1) + lane + 32] = kv_round<KVT>(v2);
             }
         }
     };
@@ -642,91 +660,10 @@ __device__ __noinline__ void attn_item(const MegaArgs& a, MegaSmem* s, Ring& rin
     //    through the ring during phase A, so the queries' L2 reads go first and the tiles land
     //    meanwhile. Larger passes load them here, every thread's 16-byte loads issued first.
     if constexpr (R <= MEGA_RING_KV_MAX_R) {
-        // the chunk's cached rows stay in their ring tiles (KVT as stored); new keys in Ks / Vs
         queries_and_new_keys();
         astamp(a, l, 1, first);
-        constexpr int KPT = kv_keys_per_tile<KVT>();
-        const int ntk = (nold + KPT - 1) / KPT;   // <= 4 (the chunk is 4 * KPT keys)
-        const KVT* kt[4] = {nullptr, nullptr, nullptr, nullptr};
-        const KVT* vt[4] = {nullptr, nullptr, nullptr, nullptr};
-        for (int i = 0; i < 2 * ntk; ++i) {
-            const uint32_t t = ring.t + i;
-            if (ring.ok && !ring_wait(ring, &s->full[t % MEGA_NS], (t / MEGA_NS) & 1)) ring.ok = false;
-            const KVT* tile = reinterpret_cast<const KVT*>(s->ring[t % MEGA_NS]);
-            if (i < ntk) kt[i] = tile; else vt[i - ntk] = tile;
-        }
-        float* Pr = Vs + MEGA_RMAX * (DH + 1);   // [nq][chunk]
-        named_bar_sync(1, MEGA_NCT);
-        astamp(a, l, 2, first);
-        // scores: a thread per (query, key); a key row in a ring tile is read in rotated pair order
-        // (pair (j + lane) mod 32 at step j: one bank per lane of the warp)
-        for (int e = tid; e < nq * chunk; e += MEGA_NCT) {
-            const int qi = e / chunk, kk = e % chunk;
-            const int key = k0 + kk;
-            const int pos = rows[r0 + qi / GQA].y;
-            const int lor = local ? max(0, pos - WINDOW + 1) : 0;
-            float sc = -INFINITY;
-            if (kk < nk && key <= pos && key >= lor) {
-                const float* qv = qs + qi * DH;
-                float acc = 0.f;
-                if (kk < nold) {
-                    const KVT* kr = kt[kk / KPT] + (kk % KPT) * DH;
-#pragma unroll 8
-                    for (int j = 0; j < DH / 2; ++j) {
-                        const int w = (j + lane) & (DH / 2 - 1);
-                        const float2 k2 = kv_pair(kr, w);
-                        const float2 q2 = reinterpret_cast<const float2*>(qv)[w];
-                        acc += q2.x * k2.x + q2.y * k2.y;
-                    }
-                } else {
-                    const float* kr = Ks + (kk - nold) * (DH + 1);
-#pragma unroll 16
-                    for (int d = 0; d < DH; ++d) acc += qv[d] * kr[d];
-                }
-                sc = acc;
-            }
-            Pr[qi * chunk + kk] = sc;
-        }
-        named_bar_sync(1, MEGA_NCT);
-        astamp(a, l, 3, first);
-        // partial softmax per query (warps): max m, weights exp(s - m) back into Pr, sum
-        for (int qi = cw; qi < nq; qi += MEGA_NCW) {
-            const int rr = qi / GQA, h = g * GQA + qi % GQA;
-            float* pr = Pr + qi * chunk;
-            float mx = -INFINITY;
-            for (int kk = lane; kk < chunk; kk += 32) mx = fmaxf(mx, pr[kk]);
-            const float m = warp_max(mx);
-            float sum = 0.f;
-            for (int kk = lane; kk < chunk; kk += 32) {
-                const float ev = (pr[kk] == -INFINITY) ? 0.f : expf(pr[kk] - m);
-                pr[kk] = ev;
-                sum += ev;
-            }
-            const float lsum = warp_sum(sum);
-            float* out = a.part + (((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART;
-            if (lane == 0) {
-                out[0] = m;   // -inf: no key of the chunk is visible to this row (weights all 0)
-                out[1] = m == -INFINITY ? 0.f : lsum;
-            }
-        }
-        named_bar_sync(1, MEGA_NCT);
-        astamp(a, l, 4, first);
-        // P.V: a thread per (query, dimension), keys in order
-        for (int e = tid; e < nq * DH; e += MEGA_NCT) {
-            const int qi = e / DH, d = e % DH;
-            const int rr = qi / GQA, h = g * GQA + qi % GQA;
-            const float* pr = Pr + qi * chunk;
-            float o = 0.f;
-            for (int kk = 0; kk < nold; ++kk) o += pr[kk] * kv_elem(vt[kk / KPT] + (kk % KPT) * DH, d);
-            for (int kk = nold; kk < nk; ++kk) o += pr[kk] * Vs[(kk - nold) * (DH + 1) + d];
-            a.part[(((int64_t)(r0 + rr) * H + h) * a.nch_max + c) * PART + 2 + d] = o;
-        }
-        named_bar_sync(1, MEGA_NCT);   // every warp is done with the tiles
-        if (threadIdx.x == 32 && ring.ok)
-            for (int i = 0; i < 2 * ntk; ++i) mbar_arrive(&s->empty[(ring.t + i) % MEGA_NS]);
-        ring.t += 2 * ntk;
-        astamp(a, l, 5, first);
-        return;
+        consume_kv<KVT>(ring, nold, Ks);
+        consume_kv<KVT>(ring, nold, Vs);
     } else {
         constexpr int PARTS = (sizeof(KVT) == 2) ? 8 : 16;   // 16-byte pieces per 64-element row
         for (int e = tid; e < 2 * nold * PARTS; e += MEGA_NCT) {
@@ -974,8 +911,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
             if (R <= MEGA_RING_KV_MAX_R) {   // cached K/V chunks of this CTA's attention items (phase B)
                 const bool local = is_local_layer(l);
                 AttnGeo geo;
-                for (int item = cta; g.ok && attn_geo(s->rows, pblk, pnb, local, mega_ring_chunk<R, KVT>(), item, geo);
-                     item += C) {
+                for (int item = cta; g.ok && attn_geo(s->rows, pblk, pnb, local, item, geo); item += C) {
                     if (geo.nold <= 0) continue;
                     produce_kv<KVT>(g, a.kvl[l], geo.slot, geo.g, geo.k0, geo.nold, false);
                     produce_kv<KVT>(g, a.kvl[l], geo.slot, geo.g, geo.k0, geo.nold, true);
@@ -1192,7 +1128,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega_pulse(const __grid_con
                 for (int b = 0; b < s->n_blk; ++b) {
                     const int pos0 = s->rows[s->blk_r0[b]].y, posL = s->rows[s->blk_r0[b + 1] - 1].y;
                     const int lo = local ? max(0, pos0 - WINDOW + 1) : 0;
-                    const int chunk = attn_chunk(posL - lo + 1, mega_ring_chunk<R, KVT>());
+                    const int chunk = attn_chunk(posL - lo + 1);
                     s->blk_chunk[b] = chunk;
                     s->blk_nch[b] = (posL - lo + chunk) / chunk;
                 }
