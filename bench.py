@@ -568,6 +568,99 @@ def run_prefill_profile(args):
     eng.close()
 
 
+def run_ops(args):
+    """The drop-in op boundary: each pulsar_cuda forward op of the shim against the reference's
+    own kernel (csrc/kernels.cu built for sm_100a by oracle/build_ref_ops.py), same inputs at the
+    model's shapes (2048 tokens, d_model 1024, 16 experts, top-4), same B200. Each launch is
+    timed alone with CUDA events on the current stream, after an L2 flush (a 256 MB write) and a
+    device-side spin that keeps host launch overhead out of the bracket, median of
+    --kernel-reps launches after 3 warm-ups. GB/s counts each op's algorithmic bytes (inputs
+    read once, outputs written once)."""
+    from oracle import build_ref_ops
+    import pulsar_cuda as pc
+    ref = build_ref_ops.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    N, D, E, K, H, DH, CAP, T = 2048, 1024, 16, 4, 16, 64, 640, 2048
+    g = torch.Generator(device="cpu").manual_seed(0)
+    bf = lambda *s: torch.randn(*s, generator=g).to(dev, torch.bfloat16)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(N)]).to(dev)
+    slots = torch.full((N, K), -1, dtype=torch.int32)
+    fill = [0] * E
+    for t in range(N):
+        for k in range(K):
+            e = int(idx[t, k])
+            if fill[e] < CAP:
+                slots[t, k], fill[e] = fill[e], fill[e] + 1
+    slots = slots.to(dev)
+    counts = torch.tensor(fill, device=dev)
+    tw = torch.rand(N, K, generator=g).to(dev, torch.bfloat16)
+    x, sh, eo = bf(N, D), bf(N, D), bf(E, CAP, D)
+    w = torch.rand(D, device=dev) + 0.5
+    logits = torch.randn(N, E, generator=g).to(dev)
+    bias = torch.zeros(E, device=dev)
+    gu = bf(N, 1024)
+    q = bf(1, H, T, DH)
+    ang = torch.outer(torch.arange(T, device=dev, dtype=torch.float32),
+                      1.0 / (10000.0 ** (torch.arange(0, DH, 2, device=dev, dtype=torch.float32) / DH)))
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    wq = torch.rand(H, DH, device=dev) + 0.5
+    xc, wc = bf(4, 512, D), torch.randn(D, 4, generator=g).to(dev)
+    att, gl = bf(1, H, T, DH), torch.randn(1, T, H, generator=g).to(dev)
+    used = int((slots >= 0).sum())
+    cases = {   # name: (call(module), algorithmic bytes)
+        "moe_combine_forward": (lambda m: m.moe_combine_forward(eo, idx, tw, slots, sh),
+                                used * D * 2 + 2 * N * D * 2 + N * K * (8 + 4 + 2)),
+        "moe_dispatch_forward": (lambda m: m.moe_dispatch_forward(x, idx, slots, E, CAP, counts),
+                                 N * D * 2 + E * CAP * D * 2 + N * K * 12),
+        "moe_router_topk_forward": (lambda m: m.moe_router_topk_forward(logits, bias, K, 1e-3),
+                                    N * E * 4 + N * K * 12 + E * 4),
+        "rmsnorm_forward": (lambda m: m.rmsnorm_forward(x, w, 1e-6), 2 * N * D * 2 + N * 4),
+        "fused_swiglu_forward": (lambda m: m.fused_swiglu_forward(gu, 512), N * 1024 * 2 + N * 512 * 2),
+        "rope_forward": (lambda m: m.rope_forward(q, cos, sin), 2 * q.numel() * 2 + 2 * cos.numel() * 4),
+        "qk_rmsnorm_rope_forward": (lambda m: m.qk_rmsnorm_rope_forward(q, wq, cos, sin, T, 1e-6),
+                                    2 * q.numel() * 2 + 2 * cos.numel() * 4 + H * T * 4),
+        "fused_attn_gate_forward": (lambda m: m.fused_attn_gate_forward(att, gl), 2 * att.numel() * 2 + gl.numel() * 4),
+        "causal_depthwise_conv1d_k4_forward": (lambda m: m.causal_depthwise_conv1d_k4_forward(xc, wc),
+                                               2 * xc.numel() * 2 + wc.numel() * 4),
+    }
+    flush = torch.empty(256 * 2 ** 20 // 4, device=dev)
+    st = torch.cuda.current_stream()
+
+    def time_op(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(max(5, args.kernel_reps)):
+            flush.fill_(1.0)
+            # ~100 us of device-side spin after the flush: the host enqueues the op (its Python /
+            # binding overhead) before the GPU reaches the start event, so the events bracket
+            # device time only
+            torch.cuda._sleep(200_000)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return statistics.median(ts)
+
+    out = {}
+    for name, (call, nbytes) in cases.items():
+        row = {"bytes": nbytes}
+        us = time_op(lambda: call(pc))
+        row["shim_us"], row["shim_gbs"] = round(us, 2), round(nbytes / us / 1e3, 1)
+        if ref is not None:
+            ur = time_op(lambda: call(ref))
+            row["reference_us"], row["reference_gbs"] = round(ur, 2), round(nbytes / ur / 1e3, 1)
+            row["speedup"] = round(ur / us, 2)
+        out[name] = row
+    print(json.dumps({"metric": "pulsar_cuda forward op time (median us, L2 flushed)", "unit": "us",
+                      "shapes": {"tokens": N, "d_model": D, "experts": E, "top_k": K, "capacity": CAP, "heads": H},
+                      "reference": "csrc/kernels.cu built for sm_100a (oracle/build_ref_ops.py)" if ref is not None
+                      else "not built", "ops": out}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -587,6 +680,8 @@ def main():
                     help="launch each round shape of k_mega_pulse once after the prefill and exit (ncu captures)")
     ap.add_argument("--prefill-profile", action="store_true",
                     help="one profiled prefill of the bench prompt between cudaProfilerStart/Stop (ncu captures)")
+    ap.add_argument("--ops", action="store_true",
+                    help="time each pulsar_cuda forward op against the reference's own kernel (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -600,6 +695,8 @@ def main():
         run_kernel_shapes(args)
     elif args.prefill_profile:
         run_prefill_profile(args)
+    elif args.ops:
+        run_ops(args)
     else:
         run_engine(args)
 

@@ -190,6 +190,16 @@ int pulsar_engine_set_length(pulsar_engine* eng, int32_t slot, int32_t length);
 int pulsar_engine_read_kv(pulsar_engine* eng, int32_t slot, int32_t layer, int32_t pos0, int32_t n, float* k_host,
                           float* v_host);
 
+/* The attention step of pulsar_engine_prefill for one layer (src/infer.py:422-435 masks: causal,
+ * and for local layers with T > 1024 the truncated cache of the last 1024 positions with the
+ * causal mask aligned top-left), over the slot's cached keys and values of positions 0..T-1,
+ * which a prefill of T tokens wrote. q_dev: [T][16][64] fp32 normed and rotated queries
+ * (unscaled); out_dev: [T][16][64] fp32. tensor_cores 1: the tcgen05 kernel that prefill uses,
+ * 0: the fp32 SIMT kernel (the engine option "tc_attn" selects between them inside prefill).
+ * Device pointers; enqueued on `stream`. */
+int pulsar_engine_prefill_attention(pulsar_engine* eng, int32_t slot, int32_t layer, int32_t T, const float* q_dev,
+                                    float* out_dev, int32_t tensor_cores, void* stream);
+
 /* Greedy decode loop, reference semantics (stream_generate with temperature 0 and
  * repetition_penalty 1, src/infer.py:551-621): starting from the prefill logits already
  * in the slot's state, emit n_new tokens. gamma == 0: exact sequential decode (3 pulses
@@ -248,13 +258,16 @@ int pulsar_engine_arena_info(pulsar_engine* eng, int32_t index, const char** nam
 int pulsar_engine_arena_read(pulsar_engine* eng, const char* name, void* host_dst, int64_t numel);
 int pulsar_engine_arena_write(pulsar_engine* eng, const char* name, const void* host_src, int64_t numel);
 
-/* Repetition penalty of the sequential greedy loop (src/infer.py:582-589, the reference's
- * default 1.15 in stream_generate / generate): when choosing each token of
- * pulsar_engine_generate_greedy with gamma == 0, logits of ids already seen are divided by
- * the penalty when positive and multiplied by it otherwise, then the argmax is taken. The
- * seen set of a slot is the prompt of its last pulsar_engine_prefill plus every token that
- * generate calls emitted for it since (a bitmap on the device). penalty > 0; 1 turns it off.
- * Speculative and sampled generate calls return PULSAR_ERR_UNSUPPORTED while it is on. */
+/* Repetition penalty of every generate loop (src/infer.py:582-589 and 658-667, the
+ * reference's default 1.15 in stream_generate / self_speculative_stream_generate / generate):
+ * before each token is chosen, logits of ids already seen are divided by the penalty when
+ * positive and multiplied by it otherwise. The seen set of a slot is the prompt of its last
+ * pulsar_engine_prefill plus every token that generate calls emitted for it since (a bitmap on
+ * the device). In a speculative round the logits that choose the token at block position k
+ * (draft or verify) also count the round's drafts before k as seen, so greedy speculative
+ * decoding with the penalty emits the penalised sequential stream; sampled calls warp the
+ * penalised logits of both the draft and the verify distributions. penalty > 0; 1 turns it
+ * off; vocab sizes up to 393,216. */
 int pulsar_engine_set_repetition_penalty(pulsar_engine* eng, float penalty);
 
 /* counts_host[3]: tokens that exited after pulse 1, 2 and 3 (the reference's

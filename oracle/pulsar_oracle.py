@@ -714,7 +714,7 @@ class SpecStats:
 def block_spec_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: int, gamma: int = 4,
                             temperature: float = 0.0, top_p: float = 1.0, seed: int = 0, seq_id: int = 0,
                             capacity=None, stats: SpecStats | None = None, trace=None, kv: OracleKV | None = None,
-                            first_logits: torch.Tensor | None = None) -> list[int]:
+                            first_logits: torch.Tensor | None = None, repetition_penalty: float = 1.0) -> list[int]:
     """Self-speculative decoding with gamma drafts and one batched verify.
 
     Round with committed length n and pending token t0 (position n):
@@ -731,24 +731,37 @@ def block_spec_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: i
       4. commit n..n+a (a = accepted drafts) and roll back the rest (length reset).
     The first pending token comes from the (unsoftcapped) prefill logits. ``kv`` +
     ``first_logits``: start from a cache already holding the prompt instead of prefilling.
+    ``repetition_penalty``: src/infer.py:658-667 penalises every sample with the ids emitted
+    before it; here the logits choosing the token at block position k (draft q_k, verify P_k)
+    are penalised over the prompt, the emitted tokens (the pending t0 included) and the
+    round's drafts d_1..d_k, so that greedy decoding emits the penalised sequential stream.
+    The trace then holds the penalised logits (those the decisions are taken on).
     """
     greedy = temperature <= 1e-4
     kv, logits = _start(m, prompt, kv, first_logits, capacity or (len(prompt) + max_new_tokens + gamma + 8))
     n = len(prompt)
     out: list[int] = []
     rnd = 0
+    seen = list(prompt)
+
+    def penal(lg, extra):
+        return apply_repetition_penalty(lg, seen + list(extra), repetition_penalty) if repetition_penalty != 1.0 else lg
+
+    logits = penal(logits, [])
     if greedy:
         t0 = int(logits.argmax())
     else:
         probs = warped_probs(logits, temperature, top_p)
         t0 = int(logits.argmax()) if probs is None else sample_from(probs, uniforms(seed, seq_id, 0xFFFFFFFF, 0)[0])
     out.append(t0)
+    seen.append(t0)
     while len(out) < max_new_tokens:
         toks = [t0]
         q_logits = []
         h_rows, h0n_rows = [], []
         for j in range(gamma):
             lg, h, h0n = pulse_pass(m, 0, [toks[j]], [n + j], kv)
+            lg = penal(lg[0], toks[1:j + 1]).view(1, -1)
             q_logits.append(lg[0])
             h_rows.append(h)
             h0n_rows.append(h0n)
@@ -766,6 +779,8 @@ def block_spec_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: i
         H0 = torch.cat(h0n_rows, 0)
         _, H, _ = pulse_pass(m, 1, toks, positions, kv, H, H0, want_logits=False)
         P, _, _ = pulse_pass(m, 2, toks, positions, kv, H, H0)
+        if repetition_penalty != 1.0:
+            P = torch.stack([penal(P[k], toks[1:k + 1]) for k in range(gamma + 1)])
         if trace is not None:
             trace.append((rnd, list(toks), torch.stack(q_logits), P.clone()))
         a = 0
@@ -810,6 +825,7 @@ def block_spec_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: i
         for t in emitted:
             if len(out) < max_new_tokens:
                 out.append(t)
+                seen.append(t)
         n = n + a + 1
         kv.length = n
         t0 = nxt

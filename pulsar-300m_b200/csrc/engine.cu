@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -16,6 +17,8 @@
 #include "mega_launch.h"
 #include "sampling.cuh"
 #include "tc_gemm.cuh"
+#include "prefill_attn_tc.cuh"
+#include "tma_gemm.cuh"
 
 using namespace pulsar;
 
@@ -111,7 +114,7 @@ struct LoopOut {
     unsigned long long seed;   // sampled decoding: Philox key, temperature, top-p
     float temperature, top_p;
     float ee_thr;              // early exit: softmax max-probability threshold
-    float rep_penalty;         // repetition penalty of the sequential greedy loop
+    float rep_penalty;         // repetition penalty (1: off)
 };
 
 // Starts a generate call: sequence state, first token, and the row descriptors of round 0
@@ -268,6 +271,50 @@ __global__ void __launch_bounds__(1024) k_commit_penalized(SeqDev* seqs, const f
     }
 }
 
+// Repetition penalty of a speculative round, in place (src/infer.py:658-667 penalises every
+// sample with the ids emitted before it). Row r of `lg` (one block each) belongs to sequence
+// i = r / per_seq at block position k = (per_seq > 1 ? r % per_seq : kfix); its seen set is the
+// slot's bitmap (prompt and emitted tokens, the pending token toks[i][0] included) plus the
+// round's drafts toks[i][1..k] before it. Each seen id's logit is divided by the penalty when
+// positive and multiplied otherwise, once per id. Rows of finished sequences are left alone
+// (seqs null: every row is live). Dynamic shared memory: V / 8 bytes.
+__global__ void __launch_bounds__(1024) k_penalize_rows(float* __restrict__ lg, int V, int per_seq, int kfix, int gamma,
+                                                        const int* __restrict__ slots, const uint32_t* __restrict__ seen,
+                                                        const int* __restrict__ toks, const LoopOut* lo,
+                                                        const SeqDev* seqs) {
+    extern __shared__ uint32_t sbits[];
+    const int r = blockIdx.x;
+    const int i = r / per_seq, k = per_seq > 1 ? r % per_seq : kfix;
+    if (seqs && seqs[i].done) return;   // uniform
+    const int W = V >> 5;
+    const uint32_t* sb = seen + (int64_t)slots[i] * W;
+    for (int w = threadIdx.x; w < W; w += blockDim.x) sbits[w] = sb[w];
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int j = 1; j <= k; ++j) {
+            const int t = toks[i * (gamma + 1) + j];
+            sbits[t >> 5] |= 1u << (t & 31);
+        }
+    __syncthreads();
+    const float pen = lo->rep_penalty;
+    float* row = lg + (int64_t)r * V;
+    for (int w = threadIdx.x; w < W; w += blockDim.x) {
+        uint32_t b = sbits[w];
+        while (b) {
+            const int v = w * 32 + __ffs(b) - 1;
+            b &= b - 1;
+            const float x = row[v];
+            row[v] = x > 0.f ? x / pen : x * pen;
+        }
+    }
+}
+
+// Adds token t[i] to the seen set of slots[i] (the first token of a penalised sampled call).
+__global__ void k_seen_add(uint32_t* seen, const int* slots, const int* t, int n, int V) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) atomicOr(&seen[(int64_t)slots[i] * (V / 32) + (t[i] >> 5)], 1u << (t[i] & 31));
+}
+
 __global__ void k_commit_greedy(SeqDev* seqs, const int* amax, int n, const LoopOut* lo) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n || seqs[i].done) return;
@@ -295,9 +342,10 @@ __global__ void k_rows_spec(const SeqDev* seqs, const int* slots, int n, int gam
 
 // Greedy acceptance: accept drafts while the verify argmax of the previous row matches;
 // the next pending token is the verify argmax after the last accepted draft. Also writes the
-// next round's first row and toks[i][0].
+// next round's first row and toks[i][0]. With a repetition penalty (seen given) every emitted
+// token joins the slot's seen set.
 __global__ void k_accept_greedy(SeqDev* seqs, int* toks, const int* amax_v, int n, int gamma, const LoopOut* lo,
-                                long long* stats, const int* slots, int4* rows) {
+                                long long* stats, const int* slots, int4* rows, uint32_t* seen, int V) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n || seqs[i].done) return;
     const int n_new = lo->n_new;
@@ -308,8 +356,15 @@ __global__ void k_accept_greedy(SeqDev* seqs, int* toks, const int* amax_v, int 
     while (a < gamma && am[a] == tk[a + 1]) ++a;
     const int nxt = am[a];
     int no = seqs[i].n_out;
-    for (int j = 1; j <= a && no < n_new; ++j) out[(int64_t)i * n_new + no++] = tk[j];
-    if (no < n_new) out[(int64_t)i * n_new + no++] = nxt;
+    uint32_t* sb = seen ? seen + (int64_t)slots[i] * (V / 32) : nullptr;
+    for (int j = 1; j <= a && no < n_new; ++j) {
+        out[(int64_t)i * n_new + no++] = tk[j];
+        if (sb) sb[tk[j] >> 5] |= 1u << (tk[j] & 31);
+    }
+    if (no < n_new) {
+        out[(int64_t)i * n_new + no++] = nxt;
+        if (sb) sb[nxt >> 5] |= 1u << (nxt & 31);
+    }
     seqs[i].n_out = no;
     seqs[i].len += a + 1;
     seqs[i].pending = nxt;
@@ -356,7 +411,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_accept_sampled(SeqDev* seqs,
                                                                    const WarpStats* __restrict__ ps,
                                                                    const WarpStats* __restrict__ qs, int n, int gamma,
                                                                    int V, const int* seq_ids, const LoopOut* lo,
-                                                                   long long* stats, const int* slots, int4* rows) {
+                                                                   long long* stats, const int* slots, int4* rows,
+                                                                   uint32_t* seen) {
     __shared__ float red[32];
     __shared__ int redk[32];
     __shared__ double redd[33];
@@ -418,8 +474,15 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_accept_sampled(SeqDev* seqs,
     const int n_new = lo->n_new;
     int* out = lo->out;
     int no = seqs[i].n_out;
-    for (int j = 1; j <= a && no < n_new; ++j) out[(int64_t)i * n_new + no++] = tk[j];
-    if (no < n_new) out[(int64_t)i * n_new + no++] = nxt;
+    uint32_t* sb = seen ? seen + (int64_t)slots[i] * (V / 32) : nullptr;   // repetition penalty on
+    for (int j = 1; j <= a && no < n_new; ++j) {
+        out[(int64_t)i * n_new + no++] = tk[j];
+        if (sb) sb[tk[j] >> 5] |= 1u << (tk[j] & 31);
+    }
+    if (no < n_new) {
+        out[(int64_t)i * n_new + no++] = nxt;
+        if (sb) sb[nxt >> 5] |= 1u << (nxt & 31);
+    }
     seqs[i].n_out = no;
     seqs[i].len += a + 1;
     seqs[i].pending = nxt;
@@ -484,6 +547,8 @@ struct pulsar_engine {
     int attn_rpb = 1;
     bool force_wide = false;   // option "wide": every pulse pass through the wide path
     bool use_tc = true;        // option "tc_gemm": tensor-core GEMMs (prefill, wide path)
+    bool tc_attn = true;       // option "tc_attn": prefill attention on the tensor cores
+    bool use_tma = true;       // option "tma_gemm": TMA-fed warp-specialised GEMM where it applies
     // bf16 hi / lo split of a GEMM's activations (tensor-core path), split_elems each
     __nv_bfloat16 *split_hi = nullptr, *split_lo = nullptr;
     int64_t split_elems = 0;
@@ -669,6 +734,33 @@ template <typename T>
 T* offs(T* p, int64_t n) { return p ? p + n : nullptr; }
 
 // ------------------------------------------------------------------ pulse pass (R <= MAX_ROWS)
+// Flash-decoding attention of an R-row pass, instantiated for the pass's rows per block
+// (e->attn_rpb: 1 for one row per sequence, gamma + 1 for verify blocks).
+template <typename KVT, int NU>
+int launch_attn_flash_nu(pulsar_engine* e, dim3 grid, const int4* rows, int R, const float* q, const KVLayer& L,
+                         int local, int nsplit, float* part, cudaStream_t st) {
+    constexpr int smem = (int)attn_flash_smem<KVT>();
+    PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_attn_flash<KVT, NU>), smem, "k_attn_flash shared memory"));
+    k_attn_flash<KVT, NU><<<grid, ATT_FTHREADS, smem, st>>>(rows, R, e->attn_rpb, q, L, local, nsplit, part, e->max_pos(),
+                                                            e->cfg.max_batch, e->m_err);
+    return launch_status("k_attn_flash");
+}
+
+template <typename KVT>
+int launch_attn_flash(pulsar_engine* e, dim3 grid, const int4* rows, int R, const float* q, const KVLayer& L, int local,
+                      int nsplit, float* part, cudaStream_t st) {
+    switch (e->attn_rpb) {
+        case 1: return launch_attn_flash_nu<KVT, 1>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        case 2: return launch_attn_flash_nu<KVT, 2>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        case 3: return launch_attn_flash_nu<KVT, 3>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        case 4: return launch_attn_flash_nu<KVT, 4>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        case 5: return launch_attn_flash_nu<KVT, 5>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        case 6: return launch_attn_flash_nu<KVT, 6>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        case 7: return launch_attn_flash_nu<KVT, 7>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        default: return launch_attn_flash_nu<KVT, ATT_RPB_MAX>(e, grid, rows, R, q, L, local, nsplit, part, st);
+    }
+}
+
 template <typename KVT>
 int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev, const float* h0n_in,
                   float* h_out, float* h0n_out, float* logits, int ld_logits, int* amax, cudaStream_t st, int hs) {
@@ -701,8 +793,8 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
         const int groups = (R + e->attn_rpb - 1) / e->attn_rpb;
         const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l]);
-        k_attn_flash<KVT><<<dim3(nsplit, HKV, groups), ATT_FTHREADS, attn_flash_smem<KVT>(), st>>>(
-            rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0, nsplit, w.part, e->max_pos(), e->cfg.max_batch, e->m_err);
+        PULSAR_TRY(launch_attn_flash<KVT>(e, dim3(nsplit, HKV, groups), rows, R, w.q, e->kvl[l], local ? 1 : 0, nsplit,
+                                          w.part, st));
         k_attn_combine<<<R, H * 32, 0, st>>>(w.part, nsplit, w.xn,
                                              e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
@@ -875,6 +967,53 @@ int pulse(pulsar_engine* e, int p, int R, const int4* rows, const float* h_prev,
 // Tiled GEMM launch: the tcgen05 tensor-core kernel when the shape fits its tiles (K a
 // multiple of 64, output columns a multiple of 128, or of 64 for SWIGLU; 16-byte aligned rows)
 // and the activation split fits the engine's hi/lo buffers, else the SIMT kernel.
+// 2-D bf16 tensor map [rows][cols] (row-major, cols contiguous) with a box of 64 columns
+// (128 bytes) x box_rows rows and the 128-byte swizzle; false when the driver entry point is
+// missing or the operand does not qualify (alignment, sizes).
+bool encode_bf16_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static std::mutex mu;
+    static Encode fn = nullptr;
+    static bool looked = false;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!looked) {
+            void* f = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+                q == cudaDriverEntryPointSuccess)
+                fn = reinterpret_cast<Encode>(f);
+            looked = true;
+        }
+    }
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || cols % 64 || rows == 0 || box_rows > 256) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Returns PULSAR_OK / an error, or 1 when the weights do not fit a tensor map (the caller falls
+// back to k_tc_gemm).
+template <int EPI, int BN>
+int launch_tma_gemm(pulsar_engine* e, const GemmArgs& g, int batches, const CUtensorMap& ma, const CUtensorMap& mb,
+                    int w_rows_per_batch, cudaStream_t st) {
+    CUtensorMap mw;
+    const uint64_t w_rows = (uint64_t)(batches - 1) * w_rows_per_batch + g.N;
+    if (!encode_bf16_map(&mw, g.W, w_rows, g.K, EPI == GEPI_SWIGLU ? BN / 2 : BN)) return 1;   // not applicable
+    PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_tma_gemm<EPI, BN>), (int)tma_smem_bytes<BN>(),
+                                "k_tma_gemm shared memory"));
+    const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2) / (BN / 2) : g.N / BN;
+    dim3 grid(ntiles, (g.M + TC_BM - 1) / TC_BM, batches);
+    k_tma_gemm<EPI, BN><<<grid, TC_THREADS, tma_smem_bytes<BN>(), st>>>(ma, mb, mw, g, w_rows_per_batch, e->m_err);
+    return launch_status("k_tma_gemm");
+}
+
 template <int EPI>
 int gemm(pulsar_engine* e, const GemmArgs& g, int batches, cudaStream_t st) {
     constexpr int BN = 128;
@@ -883,11 +1022,24 @@ int gemm(pulsar_engine* e, const GemmArgs& g, int batches, cudaStream_t st) {
                       (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 4 == 0 && g.a_stride % 4 == 0 &&
                       (int64_t)batches * g.M * g.K <= e->split_elems;
     if (e->use_tc && fits) {
-        PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_tc_gemm<EPI, BN>), (int)tc_smem_bytes<BN>(),
-                                    "k_tc_gemm shared memory"));
         const int64_t per_batch = (int64_t)g.M * g.K / 8;
         k_split_hilo<<<dim3((unsigned)((per_batch + 255) / 256), batches), 256, 0, st>>>(g, e->split_hi, e->split_lo);
         PULSAR_TRY(launch_status("k_split_hilo"));
+        // TMA-fed kernel: weights of every batch at a whole number of rows from the first
+        CUtensorMap ma, mb;
+        if (e->use_tma && (batches == 1 || g.w_stride % g.K == 0) &&
+            encode_bf16_map(&ma, e->split_hi, (uint64_t)batches * g.M, g.K, TC_BM) &&
+            encode_bf16_map(&mb, e->split_lo, (uint64_t)batches * g.M, g.K, TC_BM)) {
+            const int wpb = batches > 1 ? (int)(g.w_stride / g.K) : 0;
+            // narrow grids (under one CTA per SM) take 64-column tiles: twice the CTAs
+            const int tiles128 = ((EPI == GEPI_SWIGLU) ? (g.N / 2) / (BN / 2) : g.N / BN) *
+                                 ((g.M + TC_BM - 1) / TC_BM) * batches;
+            int r = (tiles128 < e->mega_grid) ? launch_tma_gemm<EPI, 64>(e, g, batches, ma, mb, wpb, st)
+                                              : launch_tma_gemm<EPI, BN>(e, g, batches, ma, mb, wpb, st);
+            if (r != 1) return r;
+        }
+        PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_tc_gemm<EPI, BN>), (int)tc_smem_bytes<BN>(),
+                                    "k_tc_gemm shared memory"));
         const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2) / (BN / 2) : g.N / BN;
         dim3 grid(ntiles, (g.M + TC_BM - 1) / TC_BM, batches);
         k_tc_gemm<EPI, BN><<<grid, TC_THREADS, tc_smem_bytes<BN>(), st>>>(g, e->split_hi, e->split_lo, e->m_err);
@@ -948,8 +1100,15 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
                 slot, T, f.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
                 e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
                 local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], f.vfirst, e->kvl[l], local ? 1 : 0, f.q);
-            k_attn_prefill<KVT><<<dim3((T + PA_Q - 1) / PA_Q, H), 256, 0, st>>>(slot, T, f.q, e->kvl[l], local ? 1 : 0,
-                                                                               f.o);
+            if (e->tc_attn) {
+                PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_attn_prefill_tc<KVT>), (int)pt_smem_bytes<KVT>(),
+                                            "k_attn_prefill_tc shared memory"));
+                k_attn_prefill_tc<KVT><<<dim3((T + PT_Q - 1) / PT_Q, H), PT_THREADS, pt_smem_bytes<KVT>(), st>>>(
+                    slot, T, f.q, e->kvl[l], local ? 1 : 0, f.o, e->m_err);
+            } else {
+                k_attn_prefill<KVT><<<dim3((T + PA_Q - 1) / PA_Q, H), 256, 0, st>>>(slot, T, f.q, e->kvl[l],
+                                                                                   local ? 1 : 0, f.o);
+            }
             k_gate_rows<<<T, H * 32, 0, st>>>(f.o, f.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                               e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, f.att,
                                               lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, f.t);
@@ -1040,8 +1199,8 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
         const int groups = (R + e->attn_rpb - 1) / e->attn_rpb;
         const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l]);
-        k_attn_flash<KVT><<<dim3(nsplit, HKV, groups), ATT_FTHREADS, attn_flash_smem<KVT>(), st>>>(
-            rows, R, e->attn_rpb, w.q, e->kvl[l], local ? 1 : 0, nsplit, w.part, e->max_pos(), e->cfg.max_batch, e->m_err);
+        PULSAR_TRY(launch_attn_flash<KVT>(e, dim3(nsplit, HKV, groups), rows, R, w.q, e->kvl[l], local ? 1 : 0, nsplit,
+                                          w.part, st));
         k_attn_combine<<<R, H * 32, 0, st>>>(w.part, nsplit, w.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
@@ -1215,27 +1374,52 @@ int body_step_x(pulsar_engine* e, cudaStream_t st, void* vctx) {
     return launch_status("k_commit_ee");
 }
 
+// Repetition penalty of the rows of one speculative pass (k_penalize_rows), in place.
+int penalize(pulsar_engine* e, float* lg, int nrows, int per_seq, int kfix, int gamma, const SeqDev* seqs,
+             cudaStream_t st) {
+    k_penalize_rows<<<nrows, 1024, (size_t)e->V / 8, st>>>(lg, e->V, per_seq, kfix, gamma, e->slots_dev, e->seen,
+                                                           e->toks, e->loop_out, seqs);
+    return launch_status("k_penalize_rows");
+}
+
 // One speculative round: gamma + 1 pulse-0 passes (the drafts, then the last draft's own
 // pass), whose outputs land directly in the verify block buffers (row stride gamma + 1), then
 // the batched pulse-1 and pulse-2 verify passes and the acceptance. Round 0's first row is set
-// by k_seq_init, later rounds' by the acceptance kernel.
+// by k_seq_init, later rounds' by the acceptance kernel. With a repetition penalty (fixed at
+// capture) the draft and verify passes write logits, which are penalised with each row's seen
+// set (k_penalize_rows) before their argmax, and the acceptance adds the emitted tokens to it.
 int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
     LoopCtx* c = static_cast<LoopCtx*>(vctx);
-    const int n = c->n, g = c->gamma, rows_v = n * (g + 1);
+    const int n = c->n, g = c->gamma, rows_v = n * (g + 1), V = e->V;
+    const bool rp = e->rp_on;
     for (int j = 0; j <= g; ++j) {
         if (j > 0) {
             k_rows_spec<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->slots_dev, n, g, j, e->amax, e->toks, e->rows, e->rows_v);
             PULSAR_LAUNCH_CHECK("k_rows_spec");
         }
+        float* qrows = (rp && j < g) ? e->qbuf + (int64_t)j * n * V : nullptr;
         PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->hblk + (int64_t)j * D, e->h0blk + (int64_t)j * D,
-                         nullptr, 0, j < g ? e->amax : nullptr, st, g + 1));
+                         qrows, V, (j < g && !rp) ? e->amax : nullptr, st, g + 1));
+        if (qrows) {
+            PULSAR_TRY(penalize(e, qrows, n, 1, j, g, e->seqs, st));
+            k_argmax_rows<<<n, 1024, 0, st>>>(qrows, V, V, e->amax);
+            PULSAR_LAUNCH_CHECK("k_argmax_rows");
+        }
     }
     e->attn_rpb = g + 1;   // verify blocks: one pass over each chunk of K/V per block in the attention
     const int v1 = pulse(e, 1, rows_v, e->rows_v, e->hblk, e->h0blk, e->htmp2, nullptr, nullptr, 0, nullptr, st);
-    const int v2 = v1 ? v1 : pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, nullptr, 0, e->amax, st);
+    const int v2 = v1 ? v1
+                      : pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, rp ? e->pbuf : nullptr, V,
+                              rp ? nullptr : e->amax, st);
     e->attn_rpb = 1;
     PULSAR_TRY(v2);
-    k_accept_greedy<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->toks, e->amax, n, g, e->loop_out, e->stats, e->slots_dev, e->rows);
+    if (rp) {
+        PULSAR_TRY(penalize(e, e->pbuf, rows_v, g + 1, 0, g, e->seqs, st));
+        k_argmax_rows<<<rows_v, 1024, 0, st>>>(e->pbuf, V, V, e->amax);
+        PULSAR_LAUNCH_CHECK("k_argmax_rows");
+    }
+    k_accept_greedy<<<(n + 127) / 128, 128, 0, st>>>(e->seqs, e->toks, e->amax, n, g, e->loop_out, e->stats, e->slots_dev,
+                                                     e->rows, rp ? e->seen : nullptr, V);
     return launch_status("k_accept_greedy");
 }
 
@@ -1245,6 +1429,7 @@ int body_round(pulsar_engine* e, cudaStream_t st, void* vctx) {
 int body_round_sampled(pulsar_engine* e, cudaStream_t st, void* vctx) {
     LoopCtx* c = static_cast<LoopCtx*>(vctx);
     const int n = c->n, g = c->gamma, rows_v = n * (g + 1), V = e->V;
+    const bool rp = e->rp_on;   // repetition penalty: draft and verify logits penalised in place
     const size_t smem = (size_t)V * sizeof(float);
     for (int j = 0; j <= g; ++j) {
         if (j > 0) {
@@ -1255,6 +1440,7 @@ int body_round_sampled(pulsar_engine* e, cudaStream_t st, void* vctx) {
         PULSAR_TRY(pulse(e, 0, n, e->rows, nullptr, nullptr, e->hblk + (int64_t)j * D, e->h0blk + (int64_t)j * D,
                          qrows, V, nullptr, st, g + 1));
         if (j < g) {
+            if (rp) PULSAR_TRY(penalize(e, qrows, n, 1, j, g, e->seqs, st));
             k_warp_sample<<<n, SAMPLE_THREADS, smem, st>>>(qrows, V, V, e->loop_out, e->seq_ids_dev, e->seqs, j, e->amax,
                                                            e->qstats + (int64_t)j * n);
             PULSAR_LAUNCH_CHECK("k_warp_sample");
@@ -1265,11 +1451,13 @@ int body_round_sampled(pulsar_engine* e, cudaStream_t st, void* vctx) {
     const int v2 = v1 ? v1 : pulse(e, 2, rows_v, e->rows_v, e->htmp2, e->h0blk, e->htmp, nullptr, e->pbuf, V, nullptr, st);
     e->attn_rpb = 1;
     PULSAR_TRY(v2);
+    if (rp) PULSAR_TRY(penalize(e, e->pbuf, rows_v, g + 1, 0, g, e->seqs, st));
     k_warp_sample<<<rows_v, SAMPLE_THREADS, smem, st>>>(e->pbuf, V, V, e->loop_out, e->seq_ids_dev, nullptr, 0, nullptr,
                                                         e->pstats);
     PULSAR_LAUNCH_CHECK("k_warp_sample");
     k_accept_sampled<<<n, SAMPLE_THREADS, 0, st>>>(e->seqs, e->toks, e->pbuf, e->qbuf, e->pstats, e->qstats, n, g, V,
-                                                  e->seq_ids_dev, e->loop_out, e->stats, e->slots_dev, e->rows);
+                                                  e->seq_ids_dev, e->loop_out, e->stats, e->slots_dev, e->rows,
+                                                  rp ? e->seen : nullptr);
     return launch_status("k_accept_sampled");
 }
 
@@ -1404,14 +1592,7 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         if ((st = mega_occupancy(cfg->kv_fp32 != 0, &per_sm))) return fail(st);
         if ((st = cuda_status(cudaFuncSetAttribute(k_warp_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    SAMPLE_MAX_V * (int)sizeof(float)),
-                              "k_warp_sample shared memory")) ||
-            (st = cuda_status(cudaFuncSetAttribute(k_attn_flash<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)attn_flash_smem<float>()),
-                              "k_attn_flash shared memory")) ||
-            (st = cuda_status(cudaFuncSetAttribute(k_attn_flash<__nv_bfloat16>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)attn_flash_smem<__nv_bfloat16>()),
-                              "k_attn_flash shared memory")))
+                              "k_warp_sample shared memory")))
             return fail(st);
         // the per-CTA staging sizes assume >= 144 CTAs (ceil(8192 / C) + ceil(1024 / C) <= 64 pairs)
         e->mega_grid = sms;
@@ -1717,6 +1898,40 @@ __global__ void k_kv_gather(KVLayer L, int slot, int pos0, int n, float* __restr
 }
 }  // namespace
 
+namespace {
+template <typename KVT>
+int prefill_attention(pulsar_engine* e, int slot, int layer, int T, const float* q, float* out, bool tc,
+                      cudaStream_t st) {
+    const int local = is_local_layer(layer) ? 1 : 0;
+    if (tc) {
+        PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_attn_prefill_tc<KVT>), (int)pt_smem_bytes<KVT>(),
+                                    "k_attn_prefill_tc shared memory"));
+        k_attn_prefill_tc<KVT><<<dim3((T + PT_Q - 1) / PT_Q, H), PT_THREADS, pt_smem_bytes<KVT>(), st>>>(
+            slot, T, q, e->kvl[layer], local, out, e->m_err);
+        return launch_status("k_attn_prefill_tc");
+    }
+    k_attn_prefill<KVT><<<dim3((T + PA_Q - 1) / PA_Q, H), 256, 0, st>>>(slot, T, q, e->kvl[layer], local, out);
+    return launch_status("k_attn_prefill");
+}
+}  // namespace
+
+extern "C" int pulsar_engine_prefill_attention(pulsar_engine* e, int32_t slot, int32_t layer, int32_t T,
+                                               const float* q_dev, float* out_dev, int32_t tensor_cores,
+                                               void* stream) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(slot >= 0 && slot < e->cfg.max_batch, "prefill_attention: slot %d out of range", slot);
+    PULSAR_CHECK_ARG(layer >= 0 && layer < NL, "prefill_attention: layer %d out of range [0, %d)", layer, NL);
+    PULSAR_CHECK_ARG(q_dev && out_dev, "prefill_attention: null pointer");
+    PULSAR_CHECK_ARG(T >= 1 && T <= e->len[slot], "prefill_attention: T = %d, the slot holds %d positions", T,
+                     e->len[slot]);
+    PULSAR_CHECK_ARG(!is_local_layer(layer) || std::min(T, WINDOW) <= e->kvl[layer].cap,
+                     "prefill_attention: the local ring holds %d positions", e->kvl[layer].cap);
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return e->kv32() ? prefill_attention<float>(e, slot, layer, T, q_dev, out_dev, tensor_cores != 0, st)
+                     : prefill_attention<__nv_bfloat16>(e, slot, layer, T, q_dev, out_dev, tensor_cores != 0, st);
+}
+
 extern "C" int pulsar_engine_read_kv(pulsar_engine* e, int32_t slot, int32_t layer, int32_t pos0, int32_t n,
                                      float* k_host, float* v_host) {
     PULSAR_TRY(check_engine(e, false));
@@ -1777,10 +1992,6 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
             return PULSAR_ERR_CAPACITY;
         }
     }
-    if (e->rp_on && (sampled || gamma != 0)) {
-        set_error("generate: the repetition penalty runs in the sequential greedy loop only (gamma = 0)");
-        return PULSAR_ERR_UNSUPPORTED;
-    }
     const LoopOut lp{out, n_new, (unsigned long long)seed, temperature, top_p, e->ee_thr, e->rp};
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->slots_dev, slots_host, n * 4, cudaMemcpyHostToDevice, st), "copy slots"));
     PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->lens_dev, lens.data(), n * 4, cudaMemcpyHostToDevice, st), "copy lens"));
@@ -1789,8 +2000,16 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
     if (sampled) {
         PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->seq_ids_dev, seq_ids_host, n * 4, cudaMemcpyHostToDevice, st),
                                "copy seq ids"));
-        k_warp_sample<<<n, SAMPLE_THREADS, (size_t)e->V * 4, st>>>(first_logits, e->V, e->V, e->loop_out,
+        const float* fl = first_logits;
+        if (e->rp_on) {   // the first draw sees the penalised prompt ids (a copy: the caller's row stays)
+            PULSAR_TRY(cuda_status(cudaMemcpyAsync(e->pbuf, first_logits, (size_t)n * e->V * 4, cudaMemcpyDeviceToDevice, st),
+                                   "copy first logits"));
+            PULSAR_TRY(penalize(e, e->pbuf, n, 1, 0, 0, nullptr, st));
+            fl = e->pbuf;
+        }
+        k_warp_sample<<<n, SAMPLE_THREADS, (size_t)e->V * 4, st>>>(fl, e->V, e->V, e->loop_out,
                                                                    e->seq_ids_dev, nullptr, 0, e->first_dev, nullptr);
+        if (e->rp_on) k_seen_add<<<(n + 127) / 128, 128, 0, st>>>(e->seen, e->slots_dev, e->first_dev, n, e->V);
     } else if (e->rp_on) {
         k_first_penalized<<<n, 1024, 0, st>>>(first_logits, e->V, e->slots_dev, e->seen, e->loop_out, e->first_dev);
     } else {
@@ -1804,7 +2023,7 @@ int generate_impl(pulsar_engine* e, int32_t n, const int32_t* slots_host, const 
     // output, length and sampling parameters live on the device: graphs depend on (n, gamma, mode)
     // (gamma = 0 with early exit and / or a repetition penalty: its own body, key suffixes
     // ":e" / ":r")
-    const bool ee = gamma == 0 && e->ee_on, rp = gamma == 0 && e->rp_on;
+    const bool ee = gamma == 0 && e->ee_on, rp = e->rp_on;
     const std::string key = std::to_string(n) + ":" + std::to_string(gamma) + (sampled ? ":s" : ":g") +
                             (ee ? ":e" : "") + (rp ? ":r" : "");
     std::vector<SeqDev> hs(n);
@@ -1871,6 +2090,7 @@ extern "C" int pulsar_engine_set_early_exit(pulsar_engine* e, int32_t enabled, f
 extern "C" int pulsar_engine_set_repetition_penalty(pulsar_engine* e, float penalty) {
     PULSAR_TRY(check_engine(e, false));
     PULSAR_CHECK_ARG(std::isfinite(penalty) && penalty > 0.f, "set_repetition_penalty: penalty must be finite and > 0");
+    PULSAR_CHECK_ARG(penalty == 1.f || e->V <= 393216, "set_repetition_penalty: vocab_size %d above 393216", e->V);
     e->rp = penalty;
     e->rp_on = penalty != 1.f;
     return PULSAR_OK;
@@ -1939,6 +2159,18 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
             e->graphs.clear();
         }
         e->use_tc = value != 0;
+        return PULSAR_OK;
+    }
+    if (strcmp(name, "tc_attn") == 0) {   // prefill only (never captured in a graph)
+        e->tc_attn = value != 0;
+        return PULSAR_OK;
+    }
+    if (strcmp(name, "tma_gemm") == 0) {
+        if ((value != 0) != e->use_tma) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+            e->graphs.clear();
+        }
+        e->use_tma = value != 0;
         return PULSAR_OK;
     }
     if (strcmp(name, "wide") == 0) {
@@ -2011,6 +2243,8 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     if (strcmp(name, "stall_cta") == 0) { *value = e->mega_stall_cta; return PULSAR_OK; }
     if (strcmp(name, "wide") == 0) { *value = e->force_wide ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "tc_gemm") == 0) { *value = e->use_tc ? 1 : 0; return PULSAR_OK; }
+    if (strcmp(name, "tc_attn") == 0) { *value = e->tc_attn ? 1 : 0; return PULSAR_OK; }
+    if (strcmp(name, "tma_gemm") == 0) { *value = e->use_tma ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "merged_adapter") == 0) { *value = e->merge_adapter ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "wide_rows") == 0) { *value = e->wide_rows; return PULSAR_OK; }
     if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }

@@ -333,7 +333,10 @@ __device__ __forceinline__ float2 attn_pair(const float* row, int w) { return re
 __device__ __forceinline__ float attn_elem(const __nv_bfloat16* row, int d) { return __bfloat162float(row[d]); }
 __device__ __forceinline__ float attn_elem(const float* row, int d) { return row[d]; }
 
-template <typename KVT>
+// NU: query units (rows x GQA heads) per thread group of four = the launch's rows per block
+// (rpb <= NU <= ATT_RPB_MAX), a compile-time bound so that a one-row pass does not issue the
+// instructions of eight.
+template <typename KVT, int NU>
 __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restrict__ rows, int R, int rpb,
                                                              const float* __restrict__ q, KVLayer L, int is_local,
                                                              int nsplit, float* __restrict__ part, int max_pos,
@@ -377,9 +380,9 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
         auto chunk_nk = [&](int i) { return min(chunk_k0(i) + ATT_FCK, posL + 1) - chunk_k0(i); };
         if (tid == 0)
             for (int i = 0; i < 2 && i < mine; ++i) attn_issue<KVT>(s, i, L, first.x, g, chunk_k0(i), chunk_nk(i));
-        float o[ATT_RPB_MAX];   // P.V accumulators of dimension `key` for units grp, grp + 4, ...
+        float o[NU];   // P.V accumulators of dimension `key` for units grp, grp + 4, ...
 #pragma unroll
-        for (int j = 0; j < ATT_RPB_MAX; ++j) o[j] = 0.f;
+        for (int j = 0; j < NU; ++j) o[j] = 0.f;
         __syncthreads();
         for (int i = 0; i < mine; ++i) {
             const int st = i & 1;
@@ -402,9 +405,9 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
             // (pair (j + lane) mod 32 at step j: one bank per lane of the warp)
             {
                 const int kk = key, kpos = k0 + kk;
-                float acc[ATT_RPB_MAX];
+                float acc[NU];
 #pragma unroll
-                for (int j = 0; j < ATT_RPB_MAX; ++j) acc[j] = 0.f;
+                for (int j = 0; j < NU; ++j) acc[j] = 0.f;
                 if (kk < nk) {
                     const KVT* kr = Kt + kk * DH;
 #pragma unroll 4
@@ -412,7 +415,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                         const int w = (j + lane) & (DH / 2 - 1);
                         const float2 kv = attn_pair(kr, w);
 #pragma unroll
-                        for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+                        for (int uu = 0; uu < NU; ++uu) {
                             const int u = grp + 4 * uu;
                             if (u < nq) {
                                 const float2 qv = reinterpret_cast<const float2*>(s->q[u])[w];
@@ -422,7 +425,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                     }
                 }
 #pragma unroll
-                for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+                for (int uu = 0; uu < NU; ++uu) {
                     const int u = grp + 4 * uu;
                     if (u < nq) {
                         const int pos = posF + u / GQA;
@@ -456,14 +459,14 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
             // once for all the group's units, the weights four keys at a time
             const int nu = (nq - grp + 3) / 4;   // units of this group
 #pragma unroll
-            for (int uu = 0; uu < ATT_RPB_MAX; ++uu)
+            for (int uu = 0; uu < NU; ++uu)
                 if (uu < nu) o[uu] *= s->scale[grp + 4 * uu];
             int kk = 0;
             for (; kk + 4 <= nk; kk += 4) {
                 const float v0 = attn_elem(Vt + kk * DH, key), v1 = attn_elem(Vt + (kk + 1) * DH, key);
                 const float v2 = attn_elem(Vt + (kk + 2) * DH, key), v3 = attn_elem(Vt + (kk + 3) * DH, key);
 #pragma unroll
-                for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+                for (int uu = 0; uu < NU; ++uu) {
                     if (uu < nu) {
                         const float4 pw = *reinterpret_cast<const float4*>(&s->sc[grp + 4 * uu][kk]);
                         o[uu] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
@@ -473,7 +476,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
             for (; kk < nk; ++kk) {
                 const float v = attn_elem(Vt + kk * DH, key);
 #pragma unroll
-                for (int uu = 0; uu < ATT_RPB_MAX; ++uu)
+                for (int uu = 0; uu < NU; ++uu)
                     if (uu < nu) o[uu] += s->sc[grp + 4 * uu][kk] * v;
             }
             __syncthreads();   // stage st is free again
@@ -481,7 +484,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
         }
         // partial (m, l, o) of every unit at index sp
 #pragma unroll
-        for (int uu = 0; uu < ATT_RPB_MAX; ++uu) {
+        for (int uu = 0; uu < NU; ++uu) {
             const int u = grp + 4 * uu;
             if (u < nq) {
                 float* out = part + (((int64_t)(s0 + u / GQA) * H + g * GQA + u % GQA) * nsplit + sp) * PART;

@@ -50,11 +50,26 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Potentially blocking test of the phase with the given parity: try_wait suspends the thread
+// until the phase completes or a hardware time limit passes (then it returns false), so many
+// waiting threads do not spin on the issue slots that the working warps of the SM need.
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_try(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
-    while (!mbar_test(bar, parity)) {
+    while (!mbar_try(bar, parity)) {
         if (globaltimer() - t0 > WAIT_NS) return false;
     }
     return true;

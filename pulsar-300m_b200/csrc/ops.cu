@@ -22,6 +22,8 @@ inline int grid_cap(int64_t n, int64_t per) {
     if (g > 65535 * 16) g = 65535 * 16;
     return (int)(g < 1 ? 1 : g);
 }
+// 16-byte vector accesses need every base pointer 16-byte aligned (null counts as aligned).
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------- rmsnorm
 __global__ void k_rmsnorm_rows(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, int64_t rows,
@@ -199,6 +201,37 @@ __global__ void k_conv1d_k4(const __nv_bfloat16* __restrict__ x, const float* __
     }
 }
 
+// 16-byte form (D % 8 == 0, x / y / w 16-byte aligned): a thread per 8 channels of one (b, t);
+// the four taps' rows are 16-byte loads, the 8 channels' weights two float4 each. Same
+// summation order per channel as k_conv1d_k4, so the results are identical.
+__global__ void k_conv1d_k4_v8(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, int64_t B, int64_t T,
+                               int64_t D, __nv_bfloat16* __restrict__ y) {
+    const int64_t D8 = D >> 3, n = B * T * D8;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t d0 = (i % D8) * 8, bt = i / D8;
+        const int64_t t = bt % T;
+        const int64_t at = bt * D + d0;
+        float xs[4][8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (t >= k) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + at - k * D)), xs[k]);
+        }
+        const float4* w4 = reinterpret_cast<const float4*>(w + d0 * 4);   // w[d][0..3] per channel
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 wj = __ldg(w4 + j);
+            float a = xs[0][j];
+            a += wj.x * xs[0][j];
+            if (t >= 1) a += wj.y * xs[1][j];
+            if (t >= 2) a += wj.z * xs[2][j];
+            if (t >= 3) a += wj.w * xs[3][j];
+            acc[j] = a;
+        }
+        *reinterpret_cast<uint4*>(y + at) = f32_to_bf16x8(acc);
+    }
+}
+
 // ---------------------------------------------------------------- moe combine / dispatch
 __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ eo, const int64_t* __restrict__ idx,
                               const __nv_bfloat16* __restrict__ tw, const int32_t* __restrict__ slot,
@@ -218,6 +251,40 @@ __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ eo, const int64_
     }
 }
 
+// 16-byte form of k_moe_combine (D % 8 == 0, every bf16 tensor 16-byte aligned): a thread per
+// 8 channels of one token, same summation order (shared output, then the routes in k order).
+__global__ void k_moe_combine_v8(const __nv_bfloat16* __restrict__ eo, const int64_t* __restrict__ idx,
+                                 const __nv_bfloat16* __restrict__ tw, const int32_t* __restrict__ slot,
+                                 const __nv_bfloat16* __restrict__ sh, int64_t N, int K, int64_t E, int64_t C,
+                                 int64_t D, __nv_bfloat16* __restrict__ out) {
+    const int64_t D8 = D >> 3;
+    for (int64_t t = blockIdx.x; t < N; t += gridDim.x) {
+        for (int64_t c = threadIdx.x; c < D8; c += blockDim.x) {
+            float acc[8];
+            if (sh) {
+                bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(sh + t * D) + c), acc);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+            }
+            for (int k = 0; k < K; ++k) {
+                const int64_t e = __ldg(idx + t * K + k);
+                const int s = __ldg(slot + t * K + k);
+                if (s >= 0 && s < C && e >= 0 && e < E) {
+                    const float wt = __bfloat162float(tw[t * K + k]);
+                    float v[8];
+                    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(eo + (e * C + s) * D) + c), v);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[j] += wt * v[j];
+                }
+            }
+            reinterpret_cast<uint4*>(out + t * D)[c] = f32_to_bf16x8(acc);
+        }
+    }
+}
+
+__device__ __forceinline__ bool aligned16_dev(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 __global__ void k_moe_tail_zero(__nv_bfloat16* __restrict__ buf, const int64_t* __restrict__ counts, int64_t E,
                                 int64_t C, int64_t D) {
     for (int64_t e = blockIdx.y; e < E; e += gridDim.y) {
@@ -225,8 +292,16 @@ __global__ void k_moe_tail_zero(__nv_bfloat16* __restrict__ buf, const int64_t* 
         const int64_t start = c < 0 ? 0 : (c > C ? C : c);
         const int64_t n = (C - start) * D;
         __nv_bfloat16* p = buf + (e * C + start) * D;
-        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-            p[i] = __float2bfloat16(0.f);
+        if ((D & 7) == 0 && aligned16_dev(buf)) {   // 16-byte stores (D % 8 == 0 keeps rows aligned)
+            uint4* p4 = reinterpret_cast<uint4*>(p);
+            for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n / 8;
+                 i += (int64_t)gridDim.x * blockDim.x)
+                p4[i] = make_uint4(0u, 0u, 0u, 0u);
+        } else {
+            for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+                 i += (int64_t)gridDim.x * blockDim.x)
+                p[i] = __float2bfloat16(0.f);
+        }
     }
 }
 
@@ -239,6 +314,36 @@ __global__ void k_moe_dispatch(const __nv_bfloat16* __restrict__ x, const int64_
             const int s = slot[t * K + k];
             if (s < 0 || s >= C || e < 0 || e >= E) continue;
             for (int64_t d = threadIdx.x; d < D; d += blockDim.x) ei[(e * C + s) * D + d] = x[t * D + d];
+        }
+    }
+}
+
+// 16-byte form of k_moe_dispatch (x / ei 16-byte aligned; D % 8 == 0 is required anyway): the
+// token's row is read once into registers (up to 8 chunks a thread) and stored to each route.
+__global__ void k_moe_dispatch_v8(const __nv_bfloat16* __restrict__ x, const int64_t* __restrict__ idx,
+                                  const int32_t* __restrict__ slot, int64_t N, int K, int64_t E, int64_t C, int64_t D,
+                                  __nv_bfloat16* __restrict__ ei) {
+    const int64_t D8 = D >> 3;
+    for (int64_t t = blockIdx.x; t < N; t += gridDim.x) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
+        for (int64_t c0 = 0; c0 < D8; c0 += 8 * (int64_t)blockDim.x) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int64_t c = c0 + threadIdx.x + (int64_t)u * blockDim.x;
+                if (c < D8) v[u] = __ldg(src + c);
+            }
+            for (int k = 0; k < K; ++k) {
+                const int64_t e = __ldg(idx + t * K + k);
+                const int s = __ldg(slot + t * K + k);
+                if (s < 0 || s >= C || e < 0 || e >= E) continue;
+                uint4* dst = reinterpret_cast<uint4*>(ei + (e * C + s) * D);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int64_t c = c0 + threadIdx.x + (int64_t)u * blockDim.x;
+                    if (c < D8) dst[c] = v[u];
+                }
+            }
         }
     }
 }
@@ -333,6 +438,12 @@ extern "C" int pulsar_op_conv1d_k4(const void* x, const float* w, int64_t B, int
     PULSAR_CHECK_ARG(B >= 0 && T >= 0 && D > 0, "causal_depthwise_conv1d_k4: invalid shape");
     const int64_t n = B * T * D;
     if (n == 0) return PULSAR_OK;
+    if (D % 8 == 0 && aligned16(x) && aligned16(w) && aligned16(y)) {
+        k_conv1d_k4_v8<<<grid_cap(n / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, B, T, D,
+                                                                     (__nv_bfloat16*)y);
+        PULSAR_LAUNCH_CHECK("k_conv1d_k4_v8");
+        return PULSAR_OK;
+    }
     k_conv1d_k4<<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, B, T, D, (__nv_bfloat16*)y);
     PULSAR_LAUNCH_CHECK("k_conv1d_k4");
     return PULSAR_OK;
@@ -343,6 +454,14 @@ extern "C" int pulsar_op_moe_combine(const void* eo, const int64_t* idx, const v
                                      void* stream) {
     PULSAR_CHECK_ARG(N >= 0 && K >= 0 && E > 0 && C >= 0 && D > 0, "moe_combine: invalid shape");
     if (N == 0) return PULSAR_OK;
+    if (D % 8 == 0 && aligned16(eo) && aligned16(sh) && aligned16(out)) {
+        const int threads = D / 8 >= 128 ? 128 : (int)((D / 8 + 31) / 32 * 32);
+        k_moe_combine_v8<<<grid_cap(N, 1), threads, 0, S(stream)>>>(
+            (const __nv_bfloat16*)eo, idx, (const __nv_bfloat16*)tw, slot, (const __nv_bfloat16*)sh, N, (int)K, E, C, D,
+            (__nv_bfloat16*)out);
+        PULSAR_LAUNCH_CHECK("k_moe_combine_v8");
+        return PULSAR_OK;
+    }
     k_moe_combine<<<grid_cap(N, 1), 128, 0, S(stream)>>>((const __nv_bfloat16*)eo, idx, (const __nv_bfloat16*)tw,
                                                           slot, (const __nv_bfloat16*)sh, N, (int)K, E, C, D,
                                                           (__nv_bfloat16*)out);
@@ -363,7 +482,12 @@ extern "C" int pulsar_op_moe_dispatch(const void* x, const int64_t* idx, const i
             PULSAR_TRY(cuda_status(cudaMemsetAsync(ei, 0, (size_t)(E * C * D) * 2, S(stream)), "moe_dispatch memset"));
         }
     }
-    if (N > 0 && K > 0) {
+    if (N > 0 && K > 0 && aligned16(x) && aligned16(ei)) {
+        const int threads = D / 8 >= 128 ? 128 : (int)((D / 8 + 31) / 32 * 32);
+        k_moe_dispatch_v8<<<grid_cap(N, 1), threads, 0, S(stream)>>>((const __nv_bfloat16*)x, idx, slot, N, (int)K, E,
+                                                                      C, D, (__nv_bfloat16*)ei);
+        PULSAR_LAUNCH_CHECK("k_moe_dispatch_v8");
+    } else if (N > 0 && K > 0) {
         k_moe_dispatch<<<grid_cap(N, 1), 128, 0, S(stream)>>>((const __nv_bfloat16*)x, idx, slot, N, (int)K, E, C, D,
                                                                (__nv_bfloat16*)ei);
         PULSAR_LAUNCH_CHECK("k_moe_dispatch");

@@ -163,6 +163,65 @@ __device__ __forceinline__ void tc_issue_chunk(const GemmArgs& g, const __nv_bfl
     }
 }
 
+// Epilogue of a 128 x BN tile whose fp32 accumulator sits in TMEM columns [tmem, tmem + BN):
+// warp w holds rows 32w..32w+31 (its lanes), 16 columns per tcgen05.ld; STORE (optional
+// loop-adapter correction and softcap), ADD or SWIGLU into C. Every thread of the CTA calls it.
+template <int EPI, int BN>
+__device__ __forceinline__ void tc_epilogue(const GemmArgs& g, int b, int m0, int m_valid, int n_tile, uint32_t tmem) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m = m0 + warp * 32 + lane;
+    const bool row_ok = m < m_valid;
+    float* C = g.C + (int64_t)b * g.c_stride + (int64_t)m * g.ldc;
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    if (EPI == GEPI_SWIGLU) {
+        const int n0 = n_tile * (BN / 2);
+        for (int c = 0; c < BN / 2; c += 16) {
+            float gt[16], up[16];
+            tc_ld16(lane_addr + c, gt);
+            tc_ld16(lane_addr + BN / 2 + c, up);
+            if (row_ok)
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<float4*>(C + n0 + c + i) =
+                        make_float4(siluf_(gt[i]) * up[i], siluf_(gt[i + 1]) * up[i + 1],
+                                    siluf_(gt[i + 2]) * up[i + 2], siluf_(gt[i + 3]) * up[i + 3]);
+        }
+    } else {
+        for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tc_ld16(lane_addr + c, v);
+            if (!row_ok) continue;
+            const int nb = n_tile * BN + c;
+            if (g.lora_b) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float d = 0.f;
+#pragma unroll
+                    for (int q = 0; q < LORA_R; ++q)
+                        d += g.lora_b[(int64_t)(nb + i) * LORA_R + q] * g.lora_t[(int64_t)m * LORA_R + q];
+                    v[i] += d;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                float4* dst = reinterpret_cast<float4*>(C + nb + i);
+                if (EPI == GEPI_ADD) {
+                    const float4 o = *dst;
+                    *dst = make_float4(o.x + v[i], o.y + v[i + 1], o.z + v[i + 2], o.w + v[i + 3]);
+                } else {
+                    float4 y = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    if (g.softcap > 0.f) {
+                        const float sc = g.softcap;
+                        y = make_float4(sc * tanhf(y.x / sc), sc * tanhf(y.y / sc), sc * tanhf(y.z / sc),
+                                        sc * tanhf(y.w / sc));
+                    }
+                    *dst = y;
+                }
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ void tc_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void tc_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -241,58 +300,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemm(GemmArgs g, const __n
     if (__syncthreads_or(err)) {
         if (threadIdx.x == 0) atomicExch(err_flag, 1);
     } else {
-        // epilogue: warp w holds rows 32w..32w+31 (lanes), 16 columns per load
-        const int m = m0 + warp * 32 + lane;
-        const bool row_ok = m < m_valid;
-        float* C = g.C + (int64_t)b * g.c_stride + (int64_t)m * g.ldc;
-        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-        if (EPI == GEPI_SWIGLU) {
-            const int n0 = n_tile * (BN / 2);
-            for (int c = 0; c < BN / 2; c += 16) {
-                float gt[16], up[16];
-                tc_ld16(lane_addr + c, gt);
-                tc_ld16(lane_addr + BN / 2 + c, up);
-                if (row_ok)
-#pragma unroll
-                    for (int i = 0; i < 16; i += 4)
-                        *reinterpret_cast<float4*>(C + n0 + c + i) =
-                            make_float4(siluf_(gt[i]) * up[i], siluf_(gt[i + 1]) * up[i + 1],
-                                        siluf_(gt[i + 2]) * up[i + 2], siluf_(gt[i + 3]) * up[i + 3]);
-            }
-        } else {
-            for (int c = 0; c < BN; c += 16) {
-                float v[16];
-                tc_ld16(lane_addr + c, v);
-                if (!row_ok) continue;
-                const int nb = n_tile * BN + c;
-                if (g.lora_b) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float d = 0.f;
-#pragma unroll
-                        for (int q = 0; q < LORA_R; ++q)
-                            d += g.lora_b[(int64_t)(nb + i) * LORA_R + q] * g.lora_t[(int64_t)m * LORA_R + q];
-                        v[i] += d;
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 16; i += 4) {
-                    float4* dst = reinterpret_cast<float4*>(C + nb + i);
-                    if (EPI == GEPI_ADD) {
-                        const float4 o = *dst;
-                        *dst = make_float4(o.x + v[i], o.y + v[i + 1], o.z + v[i + 2], o.w + v[i + 3]);
-                    } else {
-                        float4 y = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                        if (g.softcap > 0.f) {
-                            const float sc = g.softcap;
-                            y = make_float4(sc * tanhf(y.x / sc), sc * tanhf(y.y / sc), sc * tanhf(y.z / sc),
-                                            sc * tanhf(y.w / sc));
-                        }
-                        *dst = y;
-                    }
-                }
-            }
-        }
+        tc_epilogue<EPI, BN>(g, b, m0, m_valid, n_tile, tmem);
     }
     tc_fence_before();
     __syncthreads();

@@ -210,6 +210,18 @@ class DeviceEngine:
                    "read_kv")
         return k, v
 
+    def prefill_attention(self, slot: int, layer: int, q: torch.Tensor, tensor_cores: bool = True) -> torch.Tensor:
+        """The prefill attention step of one layer (pulsar_engine_prefill_attention) over the
+        slot's cached positions 0..T-1: q [T, n_heads, head_dim] fp32 on this engine's device
+        (normed, rotated, unscaled) -> [T, n_heads, head_dim] fp32."""
+        q = q.to(device=self.device, dtype=torch.float32).contiguous()
+        out = torch.empty_like(q)
+        _lib.check(_lib.load().pulsar_engine_prefill_attention(self._h, slot, layer, q.shape[0], q.data_ptr(),
+                                                                out.data_ptr(), 1 if tensor_cores else 0,
+                                                                self.stream()),
+                   "prefill_attention")
+        return out
+
     def set_option(self, name: str, value: int) -> None:
         """Engine options (see include/pulsar_b200.h): "megakernel" 0/1."""
         _lib.check(_lib.load().pulsar_engine_set_option(self._h, name.encode(), int(value)), f"set_option({name})")
@@ -277,7 +289,7 @@ class DeviceEngine:
                    "set_early_exit")
 
     def set_repetition_penalty(self, penalty: float) -> None:
-        """pulsar_engine_set_repetition_penalty: penalty of the gamma = 0 greedy loop (1: off)."""
+        """pulsar_engine_set_repetition_penalty: penalty of every generate loop (1: off)."""
         _lib.check(_lib.load().pulsar_engine_set_repetition_penalty(self._h, float(penalty)),
                    "set_repetition_penalty")
 
@@ -639,8 +651,10 @@ class PulsarInferenceEngine:
         gamma = 0: exact sequential greedy decoding (the reference's stream_generate with
         temperature 0 and no repetition penalty), with the adaptive early exit of
         ``set_early_exit_threshold`` decided on the device per sequence (exit depths added to
-        ``early_exit_counts``) and the ``repetition_penalty`` of src/infer.py:582-589 applied on
-        the device over each sequence's prompt and emitted tokens. gamma >= 1: gamma drafts from the
+        ``early_exit_counts``). The ``repetition_penalty`` of src/infer.py:582-589 / 658-667
+        applies on the device to every path: the logits choosing a token are penalised over the
+        sequence's prompt, its emitted tokens and, inside a speculative round, the drafts
+        before it. gamma >= 1: gamma drafts from the
         pulse-1 exit and one batched pulse-2/3 verify of the gamma+1 block per round,
         greedy acceptance (temperature <= 1e-4) or sampled acceptance (ratio test with
         residual resampling, Philox streams keyed by (sequence index, round, slot) and
@@ -650,8 +664,6 @@ class PulsarInferenceEngine:
         sampled = temperature > 1e-4
         if sampled and gamma < 1:
             raise ValueError("generate_batch: sampled decoding needs gamma >= 1")
-        if repetition_penalty != 1.0 and (sampled or gamma != 0):
-            raise ValueError("generate_batch: the device repetition penalty needs greedy decoding with gamma = 0")
         ids = torch.as_tensor(input_ids)
         if ids.dim() == 1:
             ids = ids.view(1, -1)
@@ -662,17 +674,19 @@ class PulsarInferenceEngine:
             for b in range(B):
                 first[b] = self.dev.prefill(caches[b].slot, ids[b])
             slots = [c.slot for c in caches]
-            if sampled:
-                toks, stats = self.dev.generate_sampled(slots, first, max_new_tokens, gamma, temperature, top_p, seed)
-            else:
-                ee = gamma == 0 and self.early_exit_threshold is not None
-                if ee:
-                    self.dev.set_early_exit(self.early_exit_threshold)   # zero the device tallies
-                self.dev.set_repetition_penalty(repetition_penalty)
-                try:
+            self.dev.set_repetition_penalty(repetition_penalty)
+            try:
+                if sampled:
+                    toks, stats = self.dev.generate_sampled(slots, first, max_new_tokens, gamma, temperature, top_p,
+                                                            seed)
+                else:
+                    ee = gamma == 0 and self.early_exit_threshold is not None
+                    if ee:
+                        self.dev.set_early_exit(self.early_exit_threshold)   # zero the device tallies
                     toks, stats = self.dev.generate_greedy(slots, first, max_new_tokens, gamma)
-                finally:
-                    self.dev.set_repetition_penalty(1.0)
+            finally:
+                self.dev.set_repetition_penalty(1.0)
+            if not sampled:
                 if ee:
                     for k, c in enumerate(self.dev.early_exit_counts()):
                         self.early_exit_counts[k] += c

@@ -44,7 +44,8 @@ def _setup(case="early_exit_nolora"):
         g = load_golden(case)
         sd, cfg = early_exit_model(g)
         eng = DeviceEngine(cfg, sd, device=0, max_batch=4, max_seq_len=256, max_prefill=64, kv_dtype=torch.float32)
-        eng.set_option("tc_gemm", 0)
+        eng.set_option("tc_gemm", 0)   # fp32 prefill (GEMMs and attention): these streams are chaotic
+        eng.set_option("tc_attn", 0)
         _CACHE[case] = (eng, O.OracleModel(sd, cfg), cfg, g)
     eng = _CACHE[case][0]
     use_path(eng, 0)
@@ -146,6 +147,7 @@ def test_reference_api_early_exit_stats():
     sd, cfg = early_exit_model(g)
     eng = PulsarInferenceEngine((sd, cfg), device="cuda", dtype=torch.float32, max_batch=1, max_seq_len=128)
     eng.dev.set_option("tc_gemm", 0)
+    eng.dev.set_option("tc_attn", 0)
     run, n, T = g["runs"][0], g["n_new"], len(g["prompt"])
     _, _, safe = _oracle_run(m, g["prompt"], n, run["threshold"])
     eng.set_early_exit_threshold(run["threshold"])

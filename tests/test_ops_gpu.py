@@ -188,6 +188,51 @@ def test_dispatch_and_combine(pc):
         assert (ei2[e, fill[e]:] == 0).all()
 
 
+def _misaligned(t):
+    """A contiguous copy of ``t`` whose data starts 2 bytes past a 16-byte boundary (forces the
+    ops' element-wise forms instead of their 16-byte forms)."""
+    flat = torch.empty(t.numel() + 8, dtype=t.dtype, device=t.device)
+    v = flat[1:1 + t.numel()].view(t.shape)
+    v.copy_(t)
+    assert v.data_ptr() % 16 != 0
+    return v
+
+
+@pytest.mark.parametrize("D", [1024, 1000])
+def test_vector_and_scalar_forms_agree(pc, D):
+    """The 16-byte kernels (D % 8 == 0, aligned tensors) give bit-identical results to the
+    element-wise kernels (same summation order per element), for conv, combine and dispatch."""
+    torch.manual_seed(5)
+    B, T = 3, 40
+    x = torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(D, 4, device="cuda")
+    a = pc.causal_depthwise_conv1d_k4_forward(x, w)
+    b = pc.causal_depthwise_conv1d_k4_forward(_misaligned(x), w)
+    assert torch.equal(a, b)
+    N, E, K, Cap = 37, 8, 4, 64
+    idx = torch.randint(0, E, (N, K), device="cuda")
+    slots = torch.randint(-1, Cap, (N, K), dtype=torch.int32, device="cuda")
+    tw = torch.rand(N, K, device="cuda").bfloat16()
+    eo = _bf16(E, Cap, D, seed=21)
+    sh = _bf16(N, D, seed=22)
+    o1 = pc.moe_combine_forward(eo, idx, tw, slots, sh)
+    o2 = pc.moe_combine_forward(_misaligned(eo), idx, tw, slots, sh)
+    o3 = pc.moe_combine_forward(eo, idx, tw, slots, None)
+    o4 = pc.moe_combine_forward(_misaligned(eo), idx, tw, slots, None)
+    assert torch.equal(o1, o2) and torch.equal(o3, o4)
+    if D % 8 == 0:   # dispatch requires D % 8 == 0 (the reference's check)
+        xs = _bf16(N, D, seed=23)
+        # distinct (expert, slot) pairs so the copy order does not matter
+        perm = torch.randperm(E * Cap, device="cuda")[:N * K]
+        idx2 = (perm // Cap).view(N, K)
+        slots2 = (perm % Cap).to(torch.int32).view(N, K)
+        (e1,) = pc.moe_dispatch_forward(xs, idx2, slots2, E, Cap)
+        (e2,) = pc.moe_dispatch_forward(_misaligned(xs), idx2, slots2, E, Cap)
+        assert torch.equal(e1, e2)
+        for t in (0, N // 2, N - 1):
+            assert torch.equal(e1[int(idx2[t, 0]), int(slots2[t, 0])], xs[t])
+
+
 def test_reference_model_uses_shim(pc):
     """src/model.py's wrappers call these names unguarded; the shim must expose them."""
     for name in ("rmsnorm_forward", "rope_forward", "fused_swiglu_forward", "moe_router_topk_forward",

@@ -122,6 +122,19 @@ def test_block_spec_gamma1_greedy_matches_reference_stream_on_tiny():
     assert len(out) == g["n_new"]
 
 
+@pytest.mark.parametrize("gamma", [1, 2, 4])
+def test_block_spec_penalised_matches_reference_stream_on_tiny(gamma):
+    """Greedy block-verify decoding with the repetition penalty (each draft and verify row
+    penalised over the prompt, the emitted tokens and the round's earlier drafts) emits the
+    reference's own penalised greedy stream (golden greedy_rep115_ids, src/infer.py:551-621
+    with repetition_penalty 1.15); without the penalty the stream differs."""
+    g = load_golden("tiny_B")
+    m, _ = _model(g)
+    ref = g["greedy_rep115_ids"]
+    assert O.block_spec_generate_ids(m, g["prompt"], len(ref), gamma=gamma, repetition_penalty=1.15) == ref
+    assert O.block_spec_generate_ids(m, g["prompt"], len(ref), gamma=gamma) != ref
+
+
 def test_philox_known_answer():
     """Philox4x32-10 known-answer vectors from the Random123 distribution's kat_vectors
     (counter, key) -> output, the published test values for the SC'11 generator."""

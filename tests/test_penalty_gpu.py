@@ -1,6 +1,8 @@
 """Repetition penalty on the device (pulsar_engine_set_repetition_penalty; src/infer.py:582-589
-applied in the sequential greedy loop of src/infer.py:551-621) against the oracle, which is
-pinned to the reference's penalised greedy streams (golden ``greedy_rep115_ids``).
+applied in the sequential greedy loop of src/infer.py:551-621 and to every sample of the
+speculative loop, src/infer.py:658-667) against the oracle, which is pinned to the reference's
+penalised greedy streams (golden ``greedy_rep115_ids``; the penalised block-verify loop emits
+that stream too, tests/test_oracle_golden.py).
 
 Tokens must be identical up to the first decision whose top-1 margin on the penalised logits
 is below 2e-2 (tie tolerance, as in test_engine_gpu.py). Recipe B runs with the fp32 KV cache
@@ -16,7 +18,7 @@ from oracle import pulsar_oracle as O
 from pulsar_b200.config import PulsarConfig
 from pulsar_b200.weights import make_state_dict, random_prompts
 
-from conftest import PATH_IDS, early_exit_model, load_golden, use_path
+from conftest import PATH_IDS, early_exit_model, load_golden, sampled_safe_prefix, spec_stream_divergence, use_path
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-2
@@ -87,6 +89,7 @@ def test_penalty_sharpened_and_with_early_exit(thr, path):
     eng = DeviceEngine(cfg, sd, device=0, max_batch=2, max_seq_len=256, max_prefill=64, kv_dtype=torch.float32)
     try:
         eng.set_option("tc_gemm", 0)   # fp32 prefill: these streams are chaotic (test_early_exit_gpu.py)
+        eng.set_option("tc_attn", 0)
         use_path(eng, path)
         n = 24
         cnt, probs, trace = [0, 0, 0], [], []
@@ -120,15 +123,88 @@ def test_penalty_batch_matches_single():
     assert both[1].tolist() == one[0].tolist()
 
 
-def test_penalty_rejects_speculative_loops():
-    eng, m, cfg = _setup("A", torch.bfloat16)
-    f = eng.prefill(0, [1, 2, 3, 4])
+_SPEC_REF = {}
+
+
+def _spec_ref(m, recipe, ids, n, gamma, **kw):
+    key = (recipe, tuple(ids), n, gamma, tuple(sorted(kw.items())))
+    if key not in _SPEC_REF:
+        trace, st = [], O.SpecStats()
+        ref = O.block_spec_generate_ids(m, ids, n, gamma=gamma, repetition_penalty=PEN, trace=trace, stats=st, **kw)
+        _SPEC_REF[key] = (ref, trace, st)
+    return _SPEC_REF[key]
+
+
+@pytest.mark.parametrize("recipe,kv,T", [("A", torch.bfloat16, 128), ("B", torch.float32, 32)])
+@pytest.mark.parametrize("gamma", [1, 4])
+def test_penalised_speculative_matches_oracle(recipe, kv, T, gamma, path):
+    """Greedy speculative rounds with the penalty (src/infer.py:658-667 penalises every sample):
+    each draft and verify row is penalised over the slot's seen set plus the round's earlier
+    drafts, against oracle.block_spec_generate_ids(repetition_penalty=1.15); the first
+    difference must be explained by a tie of the penalised logits (conftest.spec_stream_divergence)."""
+    eng, m, cfg = _setup(recipe, kv)
+    use_path(eng, path)
+    ids = random_prompts(1, T, cfg.vocab_size, seed=4)[0].tolist()
+    n = 32
+    ref, trace, st = _spec_ref(m, recipe, ids, n, gamma)
     eng.set_repetition_penalty(PEN)
     try:
-        with pytest.raises(RuntimeError, match="sequential greedy loop only"):
-            eng.generate_greedy([0], f.view(1, -1), 8, gamma=2)
+        first = eng.prefill(0, ids)
+        got, stats = eng.generate_greedy([0], first.view(1, -1), n, gamma=gamma)
     finally:
         eng.set_repetition_penalty(1.0)
+    first_pen = O.apply_repetition_penalty(first.cpu().float(), ids, PEN)
+    k, why = spec_stream_divergence(got[0].tolist(), ref, first_pen, trace, gamma, TOL)
+    assert not why.startswith("FAIL"), why
+    if k is None:
+        assert stats["accepted"] == st.accepted, f"accepted drafts {stats['accepted']} vs oracle {st.accepted}"
+    if recipe == "B":   # the case discriminates: without the penalty the oracle stream differs
+        assert O.block_spec_generate_ids(m, ids, n, gamma=gamma) != ref
+
+
+def test_penalised_speculative_differs_from_plain():
+    """The penalty changes the device's speculative stream on recipe B weights (recipe A's
+    random-init streams repeat one id with a top-1 margin the penalty does not overturn)."""
+    eng, m, cfg = _setup("B", torch.float32)
+    ids = random_prompts(1, 32, cfg.vocab_size, seed=5)[0].tolist()
+    first = eng.prefill(0, ids)
+    plain, _ = eng.generate_greedy([0], first.view(1, -1), 48, gamma=4)
+    eng.set_repetition_penalty(PEN)
+    try:
+        first = eng.prefill(0, ids)
+        pen, _ = eng.generate_greedy([0], first.view(1, -1), 48, gamma=4)
+    finally:
+        eng.set_repetition_penalty(1.0)
+    assert plain[0].tolist() != pen[0].tolist()
+
+
+@pytest.mark.parametrize("recipe,kv", [("A", torch.bfloat16), ("A", torch.float32)])
+def test_penalised_sampled_matches_oracle(recipe, kv, path):
+    """Sampled speculative rounds with the penalty: draft and verify logits penalised before
+    the temperature / top-p warping, the first draw over the penalised prefill logits.
+    Temperature 0.3: at 0.8 (and for recipe B at any temperature) the warped distributions keep
+    ~30k tokens with buckets narrower than the draw tie tolerance, so no token is decided."""
+    eng, m, cfg = _setup(recipe, kv)
+    use_path(eng, path)
+    temp, top_p, seed, seq_id, n, gamma = 0.3, 0.9, 11, 2, 24, 4
+    ids = random_prompts(1, 32, cfg.vocab_size, seed=12)[0].tolist()
+    okv = O.OracleKV(m, 64)
+    pre = O.prefill(m, ids, okv)
+    ref, trace, st = _spec_ref(m, recipe, ids, n, gamma, temperature=temp, top_p=top_p, seed=seed, seq_id=seq_id)
+    eng.set_repetition_penalty(PEN)
+    try:
+        first = eng.prefill(0, ids)
+        got, stats = eng.generate_sampled([0], first.view(1, -1), n, gamma, temp, top_p, seed, seq_ids=[seq_id])
+    finally:
+        eng.set_repetition_penalty(1.0)
+    safe = sampled_safe_prefix(O.apply_repetition_penalty(pre, ids, PEN), trace, st, gamma, temp, top_p, seed, seq_id)
+    k = min(safe, n)
+    assert k >= 8, f"the case should stay decided for most of the stream ({k})"
+    assert got[0].tolist()[:k] == ref[:k], f"penalised sampled tokens differ inside the decided prefix ({k})"
+
+
+def test_penalty_argument_checks():
+    eng, m, cfg = _setup("A", torch.bfloat16)
     with pytest.raises(RuntimeError, match="finite and > 0"):
         eng.set_repetition_penalty(0.0)
 
@@ -148,5 +224,10 @@ def test_generate_batch_penalty_api():
     safe = _safe_prefix(ids[0].tolist(), ref, trace, PEN)
     out = eng.generate_batch(ids, 16, gamma=0, repetition_penalty=PEN)
     assert out[0, 64:64 + safe].tolist() == ref[:safe]
-    with pytest.raises(ValueError, match="gamma = 0"):
-        eng.generate_batch(ids, 4, gamma=2, repetition_penalty=PEN)
+    # speculative (gamma = 4) with the penalty: the oracle's penalised block-verify loop
+    trace = []
+    ref4 = O.block_spec_generate_ids(m, ids[0].tolist(), 16, gamma=4, repetition_penalty=PEN, trace=trace)
+    out4 = eng.generate_batch(ids, 16, gamma=4, repetition_penalty=PEN)
+    first_pen = O.apply_repetition_penalty(O.prefill(m, ids[0].tolist(), O.OracleKV(m, 96)), ids[0].tolist(), PEN)
+    k, why = spec_stream_divergence(out4[0, 64:].tolist(), ref4, first_pen, trace, 4, TOL)
+    assert not why.startswith("FAIL"), why

@@ -46,12 +46,16 @@ def path(request):
     return request.param
 
 
-@pytest.mark.parametrize("recipe,kv,gamma", [("A", torch.bfloat16, 4), ("B", torch.float32, 4),
-                                             ("B", torch.float32, 6)])
-def test_sampled_spec_matches_oracle(recipe, kv, gamma, path):
+@pytest.mark.parametrize("recipe,kv,gamma,T,top_p,min_decided", [
+    ("A", torch.bfloat16, 4, 0.8, 0.95, 0), ("B", torch.float32, 4, 0.8, 0.95, 0), ("B", torch.float32, 6, 0.8, 0.95, 0),
+    ("A", torch.bfloat16, 4, 0.3, 0.9, 8), ("A", torch.float32, 6, 0.3, 0.9, 8)])
+def test_sampled_spec_matches_oracle(recipe, kv, gamma, T, top_p, min_decided, path):
+    """At temperature 0.8 the random-init distributions keep ~30k tokens with buckets narrower
+    than the draw tie tolerance, so few or no tokens are decided there (the acceptance and
+    stats checks still run); the temperature-0.3 cases must stay decided for 8+ tokens."""
     eng, m, cfg = _setup(recipe, kv)
     use_path(eng, path)
-    T, top_p, seed, seq_id, n = 0.8, 0.95, 7, 3, 24
+    seed, seq_id, n = 7, 3, 24
     # 32 tokens: recipe B's prefill would overflow its expert capacity beyond that, and the
     # tokens it drops are decided by router near-ties (see test_tensor_core_gemm_matches_simt)
     ids = random_prompts(1, 32, cfg.vocab_size, seed=2)[0].tolist()
@@ -66,6 +70,7 @@ def test_sampled_spec_matches_oracle(recipe, kv, gamma, path):
     got = got[0].tolist()
     safe = sampled_safe_prefix(pre, trace, st, gamma, T, top_p, seed, seq_id)
     k = min(safe, n)
+    assert k >= min_decided, f"the case should stay decided for {min_decided}+ tokens ({k})"
     assert got[:k] == ref[:k], f"sampled tokens differ inside the decided prefix ({k} tokens): {got} vs {ref}"
     assert stats["drafted"] == gamma * stats["rounds"]
     if recipe == "B":
