@@ -150,12 +150,14 @@ struct Ring {
     unsigned long long wait_ns;   // bound of each wait
 };
 
-// Bounded mbarrier wait that also gives up once the CTA has aborted.
+// Bounded mbarrier wait that also gives up once the CTA has aborted. try_wait suspends the
+// waiting thread until the phase completes or a hardware time limit passes, so waiting warps do
+// not take issue slots from the warps that compute.
 __device__ __forceinline__ bool ring_wait(const Ring& g, uint64_t* bar, uint32_t parity) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_try(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
-    for (unsigned it = 1; !mbar_test(bar, parity); ++it)
-        if ((it & 15) == 0 && (g.s->abort || globaltimer() - t0 > g.wait_ns)) return false;
+    while (!mbar_try(bar, parity))
+        if (g.s->abort || globaltimer() - t0 > g.wait_ns) return false;
     return true;
 }
 

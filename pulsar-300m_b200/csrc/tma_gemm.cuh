@@ -3,7 +3,7 @@
 // fallback for operands a tensor map cannot describe.
 //
 // Roles (128 threads): warp 0 lane 0 is the producer. Per 64-wide K chunk it issues three
-// (SWIGLU: four) 2-D tensor-map loads (cp.async.bulk.tensor, SWIZZLE_128B, no multicast)
+// (SWIGLU: four) 2-D tensor-map loads (cp.async.bulk.tensor into this CTA only, SWIZZLE_128B)
 // into a STAGES-deep ring: A hi, A lo [128 rows x 64] and W [BN rows x 64], completion counted
 // in bytes on the stage's `full` mbarrier. Warp 1 lane 0 waits on `full`, issues the tcgen05
 // MMAs (M = 128, N = BN, K = 16 per instruction, A hi and A lo into the same TMEM accumulator)
