@@ -571,7 +571,8 @@ def run_prefill_profile(args):
 def run_ops(args):
     """The drop-in op boundary: each pulsar_cuda forward op of the shim against the reference's
     own kernel (csrc/kernels.cu built for sm_100a by oracle/build_ref_ops.py), same inputs at the
-    model's shapes (2048 tokens, d_model 1024, 16 experts, top-4), same B200. Each launch is
+    model's widths (d_model 1024, 16 heads of 64, 16 experts, top-4) over 16384 tokens (eight
+    2048-token prompts: every tensor of 32-168 MB, so each launch streams from HBM), same B200. Each launch is
     timed alone with CUDA events on the current stream, after an L2 flush (a 256 MB write) and a
     device-side spin that keeps host launch overhead out of the bracket, median of
     --kernel-reps launches after 3 warm-ups. GB/s counts each op's algorithmic bytes (inputs
@@ -581,7 +582,7 @@ def run_ops(args):
     ref = build_ref_ops.load()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    N, D, E, K, H, DH, CAP, T = 2048, 1024, 16, 4, 16, 64, 640, 2048
+    N, D, E, K, H, DH, CAP, T = 16384, 1024, 16, 4, 16, 64, 5120, 16384
     g = torch.Generator(device="cpu").manual_seed(0)
     bf = lambda *s: torch.randn(*s, generator=g).to(dev, torch.bfloat16)
     idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(N)]).to(dev)
@@ -599,13 +600,13 @@ def run_ops(args):
     w = torch.rand(D, device=dev) + 0.5
     logits = torch.randn(N, E, generator=g).to(dev)
     bias = torch.zeros(E, device=dev)
-    gu = bf(N, 1024)
+    gu = bf(N, 2 * 512)
     q = bf(1, H, T, DH)
     ang = torch.outer(torch.arange(T, device=dev, dtype=torch.float32),
                       1.0 / (10000.0 ** (torch.arange(0, DH, 2, device=dev, dtype=torch.float32) / DH)))
     cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
     wq = torch.rand(H, DH, device=dev) + 0.5
-    xc, wc = bf(4, 512, D), torch.randn(D, 4, generator=g).to(dev)
+    xc, wc = bf(8, 2048, D), torch.randn(D, 4, generator=g).to(dev)
     att, gl = bf(1, H, T, DH), torch.randn(1, T, H, generator=g).to(dev)
     used = int((slots >= 0).sum())
     cases = {   # name: (call(module), algorithmic bytes)

@@ -163,6 +163,18 @@ int pulsar_engine_memory(const pulsar_engine* eng, int64_t* arena_bytes, int64_t
 int pulsar_engine_prefill(pulsar_engine* eng, int32_t slot, const int32_t* ids_dev, int32_t T, float* logits_dev,
                           void* stream);
 
+/* PulsarForCausalLM.forward with labels=None (src/model.py:1956-2125), the full-sequence pass
+ * that model.generate (src/model.py:2246-2317) recomputes for every new token: ids [T] (device
+ * int32) -> the last position's softcapped logits [V] (device fp32). It differs from
+ * pulsar_engine_prefill in the reference's own ways: the value residual of layer 0 / pulse 0
+ * carries into every pulse, global layers scale queries by 1 + 0.1 ln(max(t + 1, 1024) / 1024),
+ * local layers attend causally over the whole sequence (the reference switches to its sliding
+ * window only beyond 4096 tokens), and the logits are softcapped. T <= min(max_prefill, 2048)
+ * (the local layers' ring holds every key); PULSAR_ERR_CAPACITY beyond. Uses the slot's cache
+ * as scratch and leaves the slot empty (length 0). */
+int pulsar_engine_forward(pulsar_engine* eng, int32_t slot, const int32_t* ids, int32_t T, float* logits,
+                          void* stream);
+
 /* decode_pulse_pass (src/infer.py:463-524) over R rows, 1 <= R <= max(32, 8 * max_batch)
  * (option "wide_rows"). R <= 5: one persistent kernel; R <= 32: per-op GEMV kernels; more
  * rows (or option "wide" = 1): tiled GEMMs over all rows with the routed experts grouped

@@ -430,6 +430,30 @@ def prefill(m: OracleModel, ids: list[int], kv: OracleKV, record=None) -> torch.
     ``is_causal`` mask is aligned top-left, so query i sees cached keys
     0..min(i, window-1) = absolute positions T-window .. T-window+min(i, window-1)
     (src/infer.py:128-137, 433-435); value residual only in pulse 0 (src/infer.py:390,408-412)."""
+    h_pulse = _full_sequence(m, ids, kv, m.K, forward=False)
+    return rmsnorm(h_pulse[-1], m.p("final_norm.weight"), m.eps) @ m.lm_head.t()
+
+
+def forward_logits(m: OracleModel, ids: list[int], num_pulses: int | None = None) -> torch.Tensor:
+    """PulsarForCausalLM.forward with labels=None (src/model.py:1956-2125), last position:
+    the training-style full-sequence pass that model.generate recomputes per token. It differs
+    from the inference prefill in four ways (src/model.py:837-899, 2119-2121): the value
+    residual of layer 0 / pulse 0 carries into every later pulse; global layers scale queries by
+    the YaRN factor 1 + 0.1 ln(max(t + 1, base) / base) of their position; local layers attend
+    causally over the whole sequence when T <= max(window, 4096) and through the sliding window
+    (0 <= i - j < window) beyond; the logits are softcapped."""
+    K = num_pulses if num_pulses is not None else m.K
+    h_pulse = _full_sequence(m, ids, OracleKV(m, len(ids)), K, forward=True)
+    logits = rmsnorm(h_pulse[-1], m.p("final_norm.weight"), m.eps) @ m.lm_head.t()
+    if m.softcap and m.softcap > 0:
+        logits = m.softcap * torch.tanh(logits / m.softcap)
+    return logits
+
+
+def _full_sequence(m: OracleModel, ids: list[int], kv: OracleKV, K: int, forward: bool) -> torch.Tensor:
+    """K pulses over the whole sequence; returns the final pulse output h [T, D]. forward=False:
+    the inference prefill (src/infer.py:353-461, its K/V written to ``kv``); forward=True:
+    PulsarForCausalLM.forward (see forward_logits)."""
     T = len(ids)
     H, Hkv, dh = m.H, m.Hkv, m.dh
     group = H // Hkv
@@ -440,13 +464,15 @@ def prefill(m: OracleModel, ids: list[int], kv: OracleKV, record=None) -> torch.
         h0n = causal_conv_k4(h0n, m.stem)
     h_pulse = h0
     positions = torch.arange(T)
-    for k in range(m.K):
+    v_first = None
+    for k in range(K):
         if k == 0:
             h_in = h0n + m.p("pulse_step_emb.weight")[0]
         else:
             h_in, _ = pulse_input(m, k, ids, h_pulse, h0n)
         h = h_in
-        v_first = None
+        if not forward:
+            v_first = None   # the inference prefill keeps the value residual inside pulse 0
         for i in range(m.L):
             b = f"core.{i}.attn."
             a = rmsnorm(h, m.p(f"core.{i}.attn_norm.weight")[k], m.eps)
@@ -468,12 +494,23 @@ def prefill(m: OracleModel, ids: list[int], kv: OracleKV, record=None) -> torch.
             kk = rotate_half_split(kk, cos, sin)
             kv.k[i][:, :T] = kk
             kv.v[i][:, :T] = v
-            if is_local and T > m.window:
-                kc, vc = kk[:, T - m.window:], v[:, T - m.window:]
-            else:
+            if forward:
+                if not is_local and T > m.base_seq_len:   # YaRN per query position
+                    pos1 = torch.arange(1, T + 1, dtype=torch.float32)
+                    q = q * (1.0 + 0.1 * torch.log(pos1.clamp_min(m.base_seq_len) / float(m.base_seq_len))).view(1, T, 1)
                 kc, vc = kk, v
-            S = kc.shape[1]
-            mask = torch.ones(T, S, dtype=torch.bool).tril(diagonal=0)   # top-left aligned
+                diff = positions.view(T, 1) - positions.view(1, T)
+                if is_local and T > max(m.window, 4096):
+                    mask = (diff >= 0) & (diff < m.window)
+                else:
+                    mask = diff >= 0
+            else:
+                if is_local and T > m.window:
+                    kc, vc = kk[:, T - m.window:], v[:, T - m.window:]
+                else:
+                    kc, vc = kk, v
+                S = kc.shape[1]
+                mask = torch.ones(T, S, dtype=torch.bool).tril(diagonal=0)   # top-left aligned
             Kq = kc.repeat_interleave(group, dim=0)
             Vq = vc.repeat_interleave(group, dim=0)
             s = torch.einsum("htd,hsd->hts", q, Kq) * scale
@@ -486,7 +523,7 @@ def prefill(m: OracleModel, ids: list[int], kv: OracleKV, record=None) -> torch.
             h = h + _prefill_moe(m, i, k, x)
         h_pulse = h_in + (h - h_in) * m.p("pulse_res_scale")[k]
     kv.length = T
-    return rmsnorm(h_pulse[-1], m.p("final_norm.weight"), m.eps) @ m.lm_head.t()
+    return h_pulse
 
 
 # --------------------------------------------------------------------------------------
@@ -601,6 +638,51 @@ def stream_generate_ids(m: OracleModel, prompt: list[int], max_new_tokens: int, 
         if trace is not None:
             trace.append(("step", logits.clone()))
     return out
+
+
+def model_generate_ids(m: OracleModel, input_ids, max_new_tokens: int = 64, temperature: float = 0.7,
+                       top_k: int = 50, top_p: float = 0.9, repetition_penalty: float = 1.15,
+                       num_pulses: int | None = None, eos_token_id: int | None = None,
+                       generator: torch.Generator | None = None) -> list[list[int]]:
+    """PulsarForCausalLM.generate (src/model.py:2246-2317): every step recomputes the whole
+    context (the last max_seq_len ids) with forward_logits, penalises the ids of the row seen
+    so far, then greedy argmax (temperature 0) or temperature, top-k (logits below the k-th
+    value -> -inf), top-p over the sorted softmax (the first token always kept) and a
+    multinomial draw; finished rows emit eos; the loop stops when every row has finished.
+    Rows are run one at a time: the reference's batched forward shares one MoE capacity
+    across the rows of a batch, which couples rows only when the capacity overflows."""
+    eos = eos_token_id if eos_token_id is not None else _cfg_get(m.cfg, "eos_token_id")
+    max_len = _cfg_get(m.cfg, "max_seq_len")
+    rows = [list(map(int, r)) for r in input_ids]
+    finished = [False] * len(rows)
+    for _ in range(max_new_tokens):
+        for b, row in enumerate(rows):
+            lg = forward_logits(m, row[-max_len:], num_pulses).clone()
+            if repetition_penalty != 1.0:
+                for tok in set(row):
+                    lg[tok] = lg[tok] / repetition_penalty if lg[tok] > 0 else lg[tok] * repetition_penalty
+            if temperature > 0:
+                lg = lg / temperature
+                if top_k > 0:
+                    v, _ = torch.topk(lg, min(top_k, lg.numel()))
+                    lg[lg < v[-1]] = float("-inf")
+                if top_p < 1.0:
+                    sl, si = torch.sort(lg, descending=True)
+                    cum = torch.cumsum(torch.softmax(sl, dim=-1), dim=-1)
+                    rm = cum > top_p
+                    rm[1:] = rm[:-1].clone()
+                    rm[0] = False
+                    lg[si[rm]] = float("-inf")
+                tok = int(torch.multinomial(torch.softmax(lg, dim=-1), 1, generator=generator))
+            else:
+                tok = int(lg.argmax())
+            if finished[b]:
+                tok = eos
+            row.append(tok)
+            finished[b] = finished[b] or tok == eos
+        if all(finished):
+            break
+    return rows
 
 
 def self_speculative_ids(m: OracleModel, prompt: list[int], max_new_tokens: int, temperature: float = 0.0,

@@ -1065,7 +1065,11 @@ GemmArgs gargs(const float* A, int lda, int M, const __nv_bfloat16* W, int N, in
 }
 
 template <typename KVT>
-int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* logits, cudaStream_t st) {
+// fwd = false: the inference prefill (src/infer.py:353-461). fwd = true: the training-style
+// forward of model.generate (src/model.py:1956-2125, T <= the local ring): value residual in every
+// pulse, YaRN query scale on global layers, plain causal attention on local layers, softcapped
+// last-position logits.
+int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* logits, cudaStream_t st, bool fwd) {
     auto& f = e->pf;
     const float eps = e->cfg.rms_eps;
     k_embed_rows<<<T, 256, 0, st>>>(ids, e->emb, e->T_("anchor_norm.weight"), eps, f.h0, f.h0n_pre);
@@ -1095,19 +1099,22 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             GemmArgs g = gargs(f.xn, D, T, w_qkv(e, p, l), QKV, D, f.qkv, QKV);
             if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = f.t; }
             PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
-            const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
+            const int vres_mode = fwd ? ((p == 0 && l == 0) ? 1 : 2) : ((p == 0) ? (l == 0 ? 1 : 2) : 0);
+            const int yarn_base = (fwd && !local && T > e->cfg.base_seq_len) ? e->cfg.base_seq_len : 0;
             k_qkv_post_prefill<KVT><<<T, (H + HKV) * 32, 0, st>>>(
                 slot, T, f.qkv, e->T_(e->L(l, "attn.q_norm_weight")) + (int64_t)p * H * DH,
                 e->T_(e->L(l, "attn.k_norm_weight")) + (int64_t)p * HKV * DH, local ? e->cos_l : e->cos_g,
-                local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], f.vfirst, e->kvl[l], local ? 1 : 0, f.q);
+                local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], f.vfirst, e->kvl[l], local ? 1 : 0, f.q,
+                yarn_base);
+            const int attn_local = (local && !fwd) ? 1 : 0;   // forward: plain causal (T <= 4096)
             if (e->tc_attn) {
                 PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_attn_prefill_tc<KVT>), (int)pt_smem_bytes<KVT>(),
                                             "k_attn_prefill_tc shared memory"));
                 k_attn_prefill_tc<KVT><<<dim3((T + PT_Q - 1) / PT_Q, H), PT_THREADS, pt_smem_bytes<KVT>(), st>>>(
-                    slot, T, f.q, e->kvl[l], local ? 1 : 0, f.o, e->m_err);
+                    slot, T, f.q, e->kvl[l], attn_local, f.o, e->m_err);
             } else {
                 k_attn_prefill<KVT><<<dim3((T + PA_Q - 1) / PA_Q, H), 256, 0, st>>>(slot, T, f.q, e->kvl[l],
-                                                                                   local ? 1 : 0, f.o);
+                                                                                   attn_local, f.o);
             }
             k_gate_rows<<<T, H * 32, 0, st>>>(f.o, f.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                               e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, f.att,
@@ -1152,7 +1159,8 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
     k_rmsnorm_lora<<<1, 256, 0, st>>>(f.hp + (int64_t)(T - 1) * D, e->T_("final_norm.weight"), eps, f.hn, nullptr,
                                       nullptr);
     const int nblk = e->V / LM_ROWS_PER_BLOCK;
-    k_lmhead<<<nblk, 128, 0, st>>>(e->emb, e->V, f.hn, 1, 0.f, logits, e->V, f.pmax, f.pidx);
+    k_lmhead<<<nblk, 128, 0, st>>>(e->emb, e->V, f.hn, 1, fwd ? e->cfg.logit_softcap : 0.f, logits, e->V, f.pmax,
+                                   f.pidx);
     PULSAR_LAUNCH_CHECK("prefill lm head");
     return PULSAR_OK;
 }
@@ -1812,13 +1820,44 @@ extern "C" int pulsar_engine_prefill(pulsar_engine* e, int32_t slot, const int32
                 return PULSAR_ERR_INVALID;
             }
     }
-    const int rc = e->kv32() ? enqueue_prefill<float>(e, slot, ids, T, logits, st)
-                             : enqueue_prefill<__nv_bfloat16>(e, slot, ids, T, logits, st);
+    const int rc = e->kv32() ? enqueue_prefill<float>(e, slot, ids, T, logits, st, false)
+                             : enqueue_prefill<__nv_bfloat16>(e, slot, ids, T, logits, st, false);
     if (rc != PULSAR_OK) return rc;
     e->len[slot] = T;
     // the slot's seen-token set for the repetition penalty: the prompt
     k_seen_init<<<1, 1024, 0, st>>>(e->seen + (int64_t)slot * (e->V / 32), ids, T, e->V / 32);
     return launch_status("k_seen_init");
+}
+
+extern "C" int pulsar_engine_forward(pulsar_engine* e, int32_t slot, const int32_t* ids, int32_t T, float* logits,
+                                     void* stream) {
+    PULSAR_TRY(check_engine(e, true));
+    PULSAR_CHECK_ARG(slot >= 0 && slot < e->cfg.max_batch, "forward: slot %d out of range", slot);
+    PULSAR_CHECK_ARG(T >= 1, "forward: empty sequence");
+    PULSAR_CHECK_ARG(ids && logits, "forward: null pointer");
+    const int lim = std::min(e->cfg.max_prefill, e->kvl[0].cap);   // every local key in the ring
+    if (T > lim) {
+        set_error("forward: %d tokens exceed %d (max_prefill, and the local layers' %d-position ring)", T, lim,
+                  e->kvl[0].cap);
+        return PULSAR_ERR_CAPACITY;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    {
+        std::vector<int32_t> h(T);
+        PULSAR_TRY(cuda_status(cudaMemcpyAsync(h.data(), ids, (size_t)T * 4, cudaMemcpyDeviceToHost, st), "copy ids"));
+        PULSAR_TRY(cuda_status(cudaStreamSynchronize(st), "copy ids"));
+        for (int i = 0; i < T; ++i)
+            if (h[i] < 0 || h[i] >= e->V) {
+                set_error("forward: token %d at index %d outside [0, %d)", h[i], i, e->V);
+                return PULSAR_ERR_INVALID;
+            }
+    }
+    const int rc = e->kv32() ? enqueue_prefill<float>(e, slot, ids, T, logits, st, true)
+                             : enqueue_prefill<__nv_bfloat16>(e, slot, ids, T, logits, st, true);
+    // the slot's cache now holds the forward's keys and values, not a decodable prefix
+    e->len[slot] = 0;
+    return rc;
 }
 
 extern "C" int pulsar_engine_pulse(pulsar_engine* e, int32_t p, int32_t R, const int32_t* rows, const float* h_prev,

@@ -44,6 +44,44 @@ __global__ void k_rmsnorm_rows(const __nv_bfloat16* __restrict__ x, const float*
     }
 }
 
+// Warp per row, 16-byte accesses (D % 256 == 0, D <= 2048, x / y / w 16-byte aligned): lane
+// holds chunks lane, lane + 32, ... of 8 elements; warp-only reduction.
+__global__ void k_rmsnorm_warp(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, int64_t rows, int D,
+                               float eps, __nv_bfloat16* __restrict__ y, float* __restrict__ rs) {
+    const int lane = threadIdx.x & 31;
+    const int nc = D >> 8;   // 8-element chunks per lane (<= 8)
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const uint4* xr = reinterpret_cast<const uint4*>(x + r * D);
+        float v[8][8];
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            if (c < nc) {
+                bf16x8_to_f32(__ldg(xr + lane + 32 * c), v[c]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
+            }
+        }
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / (float)D + eps);
+        if (lane == 0 && rs) rs[r] = inv;
+        uint4* yr = reinterpret_cast<uint4*>(y + r * D);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            if (c < nc) {
+                const float4* w4 = reinterpret_cast<const float4*>(w + (lane + 32 * c) * 8);
+                const float4 wa = __ldg(w4), wb = __ldg(w4 + 1);
+                const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                float o[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = wv[j] * (v[c][j] * inv);
+                yr[lane + 32 * c] = f32_to_bf16x8(o);
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------- rope
 __global__ void k_rope(const __nv_bfloat16* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
                        int64_t rows, int64_t T, int half, __nv_bfloat16* __restrict__ y) {
@@ -55,8 +93,38 @@ __global__ void k_rope(const __nv_bfloat16* __restrict__ x, const float* __restr
         const float c = cs[t * half + j], s = sn[t * half + j];
         const float x1 = __bfloat162float(x[r * 2 * half + j]);
         const float x2 = __bfloat162float(x[r * 2 * half + j + half]);
-        y[r * 2 * half + j] = __float2bfloat16(x1 * c - x2 * s);
-        y[r * 2 * half + j + half] = __float2bfloat16(x2 * c + x1 * s);
+        // explicit FMAs (the 16-byte form uses the same ones, so both round identically)
+        y[r * 2 * half + j] = __float2bfloat16(__fmaf_rn(x1, c, -(x2 * s)));
+        y[r * 2 * half + j + half] = __float2bfloat16(__fmaf_rn(x2, c, x1 * s));
+    }
+}
+
+// 16-byte form (half % 8 == 0, x / y / cs / sn 16-byte aligned): a thread per 8 rotation
+// pairs of one row; IT is the index type (32-bit when the element count allows).
+template <typename IT>
+__global__ void k_rope_v8(const __nv_bfloat16* __restrict__ x, const float* __restrict__ cs,
+                          const float* __restrict__ sn, IT rows, IT T, int half, __nv_bfloat16* __restrict__ y) {
+    const int h8 = half >> 3;
+    const IT n = rows * h8;
+    for (IT i = blockIdx.x * (IT)blockDim.x + threadIdx.x; i < n; i += (IT)gridDim.x * blockDim.x) {
+        const IT r = i / h8;
+        const int j = (int)(i - r * h8) * 8;
+        const IT t = r % T;
+        const float4* c4 = reinterpret_cast<const float4*>(cs + t * half + j);
+        const float4* s4 = reinterpret_cast<const float4*>(sn + t * half + j);
+        const float4 ca = __ldg(c4), cb = __ldg(c4 + 1), sa = __ldg(s4), sb = __ldg(s4 + 1);
+        const float c[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+        const float s[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+        float x1[8], x2[8], y1[8], y2[8];
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + r * 2 * half + j)), x1);
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + r * 2 * half + half + j)), x2);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            y1[k] = __fmaf_rn(x1[k], c[k], -(x2[k] * s[k]));
+            y2[k] = __fmaf_rn(x2[k], c[k], x1[k] * s[k]);
+        }
+        *reinterpret_cast<uint4*>(y + r * 2 * half + j) = f32_to_bf16x8(y1);
+        *reinterpret_cast<uint4*>(y + r * 2 * half + half + j) = f32_to_bf16x8(y2);
     }
 }
 
@@ -68,6 +136,21 @@ __global__ void k_swiglu(const __nv_bfloat16* __restrict__ gu, int64_t rows, int
         const float g = __bfloat162float(gu[r * 2 * d + j]);
         const float u = __bfloat162float(gu[r * 2 * d + d + j]);
         out[i] = __float2bfloat16(siluf_(g) * u);
+    }
+}
+
+// 16-byte form (d % 8 == 0, gu / out 16-byte aligned): a thread per 8 outputs.
+template <typename IT>
+__global__ void k_swiglu_v8(const __nv_bfloat16* __restrict__ gu, IT rows, IT d, __nv_bfloat16* __restrict__ out) {
+    const IT d8 = d >> 3, n = rows * d8;
+    for (IT i = blockIdx.x * (IT)blockDim.x + threadIdx.x; i < n; i += (IT)gridDim.x * blockDim.x) {
+        const IT r = i / d8, j = (i - r * d8) * 8;
+        float g[8], u[8], o[8];
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(gu + r * 2 * d + j)), g);
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(gu + r * 2 * d + d + j)), u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = siluf_(g[k]) * u[k];
+        *reinterpret_cast<uint4*>(out + r * d + j) = f32_to_bf16x8(o);
     }
 }
 
@@ -124,11 +207,13 @@ __global__ void k_router_topk(const void* __restrict__ logits_v, const float* __
     }
 }
 
-// Deterministic column means over the per-token workspace (fixed summation order).
+// Deterministic column means over the per-token workspace (fixed summation order): block c
+// reduces column c - 1 (-1: the lse^2 column), each thread a fixed stride of tokens.
 __global__ void k_router_means(const float* __restrict__ ws, int64_t N, int E, float zw, float* __restrict__ z_loss,
                                float* __restrict__ probs_mean) {
     __shared__ float red[32];
-    for (int col = -1; col < E; ++col) {
+    {
+        const int col = (int)blockIdx.x - 1;
         float acc = 0.f;
         for (int64_t t = threadIdx.x; t < N; t += blockDim.x) acc += (col < 0) ? ws[t] : ws[N + t * E + col];
         acc = block_sum(acc, red);
@@ -167,15 +252,17 @@ __global__ void k_qk_rmsnorm_rope(const __nv_bfloat16* __restrict__ x, int64_t s
 }
 
 // ---------------------------------------------------------------- attention gate
-__global__ void k_attn_gate(const __nv_bfloat16* __restrict__ attn, const float* __restrict__ gl, int64_t B, int H,
-                            int64_t T, __nv_bfloat16* __restrict__ out) {
-    const int64_t n = B * T * H * 8;   // 8 chunks of 8 elements per head vector
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+// IT: index type (32-bit when the element count allows: cheaper divisions).
+template <typename IT>
+__global__ void k_attn_gate(const __nv_bfloat16* __restrict__ attn, const float* __restrict__ gl, IT B, int H, IT T,
+                            __nv_bfloat16* __restrict__ out) {
+    const IT n = B * T * H * 8;   // 8 chunks of 8 elements per head vector
+    for (IT i = blockIdx.x * (IT)blockDim.x + threadIdx.x; i < n; i += (IT)gridDim.x * blockDim.x) {
         const int c = (int)(i & 7);
-        const int64_t bth = i >> 3;            // (b, t, h)
-        const int h = (int)(bth % H);
-        const int64_t bt = bth / H;
-        const int64_t t = bt % T, b = bt / T;
+        const IT bth = i >> 3;            // (b, t, h)
+        const IT bt = bth / H;
+        const int h = (int)(bth - bt * H);
+        const IT b = bt / T, t = bt - b * T;
         const float g = sigmoidf_(gl[bt * H + h]);
         const uint4 v = *reinterpret_cast<const uint4*>(attn + (((b * H + h) * T + t) * 64 + c * 8));
         float f[8];
@@ -204,13 +291,14 @@ __global__ void k_conv1d_k4(const __nv_bfloat16* __restrict__ x, const float* __
 // 16-byte form (D % 8 == 0, x / y / w 16-byte aligned): a thread per 8 channels of one (b, t);
 // the four taps' rows are 16-byte loads, the 8 channels' weights two float4 each. Same
 // summation order per channel as k_conv1d_k4, so the results are identical.
-__global__ void k_conv1d_k4_v8(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, int64_t B, int64_t T,
-                               int64_t D, __nv_bfloat16* __restrict__ y) {
-    const int64_t D8 = D >> 3, n = B * T * D8;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t d0 = (i % D8) * 8, bt = i / D8;
-        const int64_t t = bt % T;
-        const int64_t at = bt * D + d0;
+template <typename IT>
+__global__ void k_conv1d_k4_v8(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, IT B, IT T, IT D,
+                               __nv_bfloat16* __restrict__ y) {
+    const IT D8 = D >> 3, n = B * T * D8;
+    for (IT i = blockIdx.x * (IT)blockDim.x + threadIdx.x; i < n; i += (IT)gridDim.x * blockDim.x) {
+        const IT bt = i / D8, d0 = (i - bt * D8) * 8;
+        const IT t = bt % T;
+        const IT at = bt * D + d0;
         float xs[4][8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -267,15 +355,32 @@ __global__ void k_moe_combine_v8(const __nv_bfloat16* __restrict__ eo, const int
 #pragma unroll
                 for (int j = 0; j < 8; ++j) acc[j] = 0.f;
             }
-            for (int k = 0; k < K; ++k) {
-                const int64_t e = __ldg(idx + t * K + k);
-                const int s = __ldg(slot + t * K + k);
-                if (s >= 0 && s < C && e >= 0 && e < E) {
-                    const float wt = __bfloat162float(tw[t * K + k]);
-                    float v[8];
-                    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(eo + (e * C + s) * D) + c), v);
+            // up to 8 routes: every route's 16-byte load in flight before the accumulation (in k order)
+            int k0 = 0;
+            for (; k0 < K; k0 += 8) {
+                uint4 rv[8];
+                float wt[8];
+                bool ok[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[j] += wt * v[j];
+                for (int u = 0; u < 8; ++u) {
+                    const int k = k0 + u;
+                    ok[u] = false;
+                    if (k < K) {
+                        const int64_t e = __ldg(idx + t * K + k);
+                        const int s = __ldg(slot + t * K + k);
+                        ok[u] = s >= 0 && s < C && e >= 0 && e < E;
+                        wt[u] = __bfloat162float(tw[t * K + k]);
+                        if (ok[u]) rv[u] = __ldg(reinterpret_cast<const uint4*>(eo + (e * C + s) * D) + c);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (ok[u]) {
+                        float v[8];
+                        bf16x8_to_f32(rv[u], v);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc[j] += wt[u] * v[j];
+                    }
                 }
             }
             reinterpret_cast<uint4*>(out + t * D)[c] = f32_to_bf16x8(acc);
@@ -357,6 +462,12 @@ extern "C" int pulsar_op_rmsnorm(const void* x, const float* w, int64_t rows, in
     PULSAR_CHECK_ARG(rows >= 0 && D > 0, "rmsnorm: invalid shape rows=%lld D=%lld", (long long)rows, (long long)D);
     if (rows == 0) return PULSAR_OK;
     PULSAR_CHECK_ARG(x && w && y, "rmsnorm: null pointer");
+    if (D % 256 == 0 && D <= 2048 && aligned16(x) && aligned16(w) && aligned16(y)) {
+        k_rmsnorm_warp<<<grid_cap(rows, 8), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, rows, (int)D, eps,
+                                                                  (__nv_bfloat16*)y, rsqrt_out);
+        PULSAR_LAUNCH_CHECK("k_rmsnorm_warp");
+        return PULSAR_OK;
+    }
     k_rmsnorm_rows<<<grid_cap(rows, 1), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, rows, (int)D, eps,
                                                               (__nv_bfloat16*)y, rsqrt_out);
     PULSAR_LAUNCH_CHECK("k_rmsnorm_rows");
@@ -369,6 +480,16 @@ extern "C" int pulsar_op_rope(const void* qk, const float* cs, const float* sn, 
     if (rows == 0) return PULSAR_OK;
     PULSAR_CHECK_ARG(T > 0 && qk && cs && sn && y, "rope: invalid arguments (T=%lld)", (long long)T);
     const int64_t n = rows * (Dh / 2);
+    if ((Dh / 2) % 8 == 0 && aligned16(qk) && aligned16(cs) && aligned16(sn) && aligned16(y)) {
+        if (rows * Dh < (int64_t)1 << 31)
+            k_rope_v8<int><<<grid_cap(n / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)qk, cs, sn, (int)rows,
+                                                                         (int)T, (int)(Dh / 2), (__nv_bfloat16*)y);
+        else
+            k_rope_v8<int64_t><<<grid_cap(n / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)qk, cs, sn, rows, T,
+                                                                             (int)(Dh / 2), (__nv_bfloat16*)y);
+        PULSAR_LAUNCH_CHECK("k_rope_v8");
+        return PULSAR_OK;
+    }
     k_rope<<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)qk, cs, sn, rows, T, (int)(Dh / 2),
                                                     (__nv_bfloat16*)y);
     PULSAR_LAUNCH_CHECK("k_rope");
@@ -378,6 +499,16 @@ extern "C" int pulsar_op_rope(const void* qk, const float* cs, const float* sn, 
 extern "C" int pulsar_op_swiglu(const void* gu, int64_t rows, int64_t d_ff, void* out, void* stream) {
     PULSAR_CHECK_ARG(rows >= 0 && d_ff > 0, "swiglu: invalid shape");
     if (rows == 0) return PULSAR_OK;
+    if (d_ff % 8 == 0 && aligned16(gu) && aligned16(out)) {
+        if (rows * d_ff * 2 < (int64_t)1 << 31)
+            k_swiglu_v8<int><<<grid_cap(rows * d_ff / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)gu, (int)rows,
+                                                                                     (int)d_ff, (__nv_bfloat16*)out);
+        else
+            k_swiglu_v8<int64_t><<<grid_cap(rows * d_ff / 8, 256), 256, 0, S(stream)>>>(
+                (const __nv_bfloat16*)gu, rows, d_ff, (__nv_bfloat16*)out);
+        PULSAR_LAUNCH_CHECK("k_swiglu_v8");
+        return PULSAR_OK;
+    }
     k_swiglu<<<grid_cap(rows * d_ff, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)gu, rows, d_ff,
                                                                 (__nv_bfloat16*)out);
     PULSAR_LAUNCH_CHECK("k_swiglu");
@@ -403,7 +534,7 @@ extern "C" int pulsar_op_moe_router_topk(const void* logits, int logits_bf16, co
         PULSAR_LAUNCH_CHECK("k_router_topk");
     }
     if (z_loss || probs_mean) {
-        k_router_means<<<1, 256, 0, S(stream)>>>(ws, N, (int)E, zw, z_loss, probs_mean);
+        k_router_means<<<(int)E + 1, 256, 0, S(stream)>>>(ws, N, (int)E, zw, z_loss, probs_mean);
         PULSAR_LAUNCH_CHECK("k_router_means");
     }
     return PULSAR_OK;
@@ -427,8 +558,12 @@ extern "C" int pulsar_op_attn_gate(const void* attn, const float* gl, int64_t B,
     PULSAR_CHECK_ARG(B >= 0 && H >= 0 && T >= 0, "fused_attn_gate: invalid shape");
     const int64_t n = B * T * H * 8;
     if (n == 0) return PULSAR_OK;
-    k_attn_gate<<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)attn, gl, B, (int)H, T,
-                                                          (__nv_bfloat16*)out);
+    if (n < (int64_t)1 << 31)
+        k_attn_gate<int><<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)attn, gl, (int)B, (int)H,
+                                                                   (int)T, (__nv_bfloat16*)out);
+    else
+        k_attn_gate<int64_t><<<grid_cap(n, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)attn, gl, B, (int)H, T,
+                                                                       (__nv_bfloat16*)out);
     PULSAR_LAUNCH_CHECK("k_attn_gate");
     return PULSAR_OK;
 }
@@ -439,8 +574,12 @@ extern "C" int pulsar_op_conv1d_k4(const void* x, const float* w, int64_t B, int
     const int64_t n = B * T * D;
     if (n == 0) return PULSAR_OK;
     if (D % 8 == 0 && aligned16(x) && aligned16(w) && aligned16(y)) {
-        k_conv1d_k4_v8<<<grid_cap(n / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, B, T, D,
-                                                                     (__nv_bfloat16*)y);
+        if (n < (int64_t)1 << 31)
+            k_conv1d_k4_v8<int><<<grid_cap(n / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, (int)B, (int)T,
+                                                                               (int)D, (__nv_bfloat16*)y);
+        else
+            k_conv1d_k4_v8<int64_t><<<grid_cap(n / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, w, B, T, D,
+                                                                                   (__nv_bfloat16*)y);
         PULSAR_LAUNCH_CHECK("k_conv1d_k4_v8");
         return PULSAR_OK;
     }
@@ -593,7 +732,7 @@ extern "C" int pulsar_op_moe_router_topk_noalloc(const void* logits, int logits_
         PULSAR_LAUNCH_CHECK("k_router_topk");
     }
     if (z_loss || probs_mean) {
-        k_router_means<<<1, 256, 0, S(stream)>>>(ws, N, (int)E, zw, z_loss, probs_mean);
+        k_router_means<<<(int)E + 1, 256, 0, S(stream)>>>(ws, N, (int)E, zw, z_loss, probs_mean);
         PULSAR_LAUNCH_CHECK("k_router_means");
     }
     return PULSAR_OK;

@@ -158,7 +158,7 @@ template <typename KVT>
 __global__ void __launch_bounds__((H + HKV) * 32) k_qkv_post_prefill(
     int slot, int T, const float* __restrict__ qkv, const float* __restrict__ qn_w, const float* __restrict__ kn_w,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, float eps, int vres_mode, float lv,
-    float* __restrict__ vfirst, KVLayer L, int is_local, float* __restrict__ q_out) {
+    float* __restrict__ vfirst, KVLayer L, int is_local, float* __restrict__ q_out, int yarn_base) {
     const int t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* src = qkv + (int64_t)t * QKV;
@@ -168,8 +168,12 @@ __global__ void __launch_bounds__((H + HKV) * 32) k_qkv_post_prefill(
         const float inv = rsqrtf(warp_sum(x1 * x1 + x2 * x2) / (float)DH + eps);
         const float q1 = qn_w[warp * DH + lane] * (x1 * inv);
         const float q2 = qn_w[warp * DH + lane + 32] * (x2 * inv);
-        q_out[((int64_t)t * H + warp) * DH + lane] = q1 * c - q2 * s;
-        q_out[((int64_t)t * H + warp) * DH + lane + 32] = q2 * c + q1 * s;
+        // forward mode on global layers (yarn_base > 0): the query of position t scaled by
+        // 1 + 0.1 ln(max(t + 1, base) / base) (src/model.py:511-522, 871-879)
+        const float ys = yarn_base > 0 ? 1.f + 0.1f * logf(fmaxf((float)(t + 1), (float)yarn_base) / (float)yarn_base)
+                                       : 1.f;
+        q_out[((int64_t)t * H + warp) * DH + lane] = (q1 * c - q2 * s) * ys;
+        q_out[((int64_t)t * H + warp) * DH + lane + 32] = (q2 * c + q1 * s) * ys;
     } else {
         const int g = warp - H;
         const float k1 = src[H * DH + g * DH + lane], k2 = src[H * DH + g * DH + lane + 32];

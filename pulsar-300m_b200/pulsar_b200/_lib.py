@@ -60,6 +60,7 @@ PROTOTYPES = {
     "pulsar_engine_get_length": (c_int, [c_void_p, c_int, C.POINTER(C.c_int32)]),
     "pulsar_engine_set_length": (c_int, [c_void_p, c_int, c_int]),
     "pulsar_engine_read_kv": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "pulsar_engine_forward": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "pulsar_engine_prefill_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]),
     "pulsar_engine_generate_greedy": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                               C.POINTER(c_int64), c_void_p]),

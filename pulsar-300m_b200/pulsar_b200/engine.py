@@ -252,6 +252,15 @@ class DeviceEngine:
                                                      logits.data_ptr(), self.stream()), "prefill")
         return logits
 
+    def forward(self, slot: int, ids) -> torch.Tensor:
+        """pulsar_engine_forward: PulsarForCausalLM.forward's last-position softcapped logits [V]
+        for ids (the training-style full-sequence pass; the slot is scratch and left empty)."""
+        ids_t = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
+        logits = torch.empty(self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        _lib.check(_lib.load().pulsar_engine_forward(self._h, slot, ids_t.data_ptr(), ids_t.numel(),
+                                                     logits.data_ptr(), self.stream()), "forward")
+        return logits
+
     def pulse(self, pulse: int, rows, h_prev=None, h0n=None, want_logits: bool = True):
         """rows: list of (slot, pos, token). Returns (logits [R,V] or None, h_out [R,D], h0n [R,D])."""
         R = len(rows)
@@ -697,6 +706,62 @@ class PulsarInferenceEngine:
         self.last_stats = stats
         return torch.cat([ids.to(self.device, torch.int64), toks.to(torch.int64)], dim=1)
 
+    # ---- PulsarForCausalLM.generate (src/model.py:2246-2317) on the engine ----
+    @torch.no_grad()
+    def model_generate(self, input_ids: torch.Tensor, max_new_tokens: int = 64, temperature: float = 0.7,
+                       top_k: int = 50, top_p: float = 0.9, repetition_penalty: float = 1.15,
+                       num_pulses: int | None = None, eos_token_id: int | None = None,
+                       generator: torch.Generator | None = None) -> torch.Tensor:
+        """The reference model's generate: every step recomputes the whole context (its last
+        max_seq_len ids) with the training-style forward (DeviceEngine.forward, on the device),
+        then on the host: repetition penalty over the row's ids, greedy argmax (temperature 0) or
+        temperature, top-k, top-p and a multinomial draw (CPU generator: `generator`, else torch's
+        default, as the reference's torch.multinomial); finished rows emit eos and the loop
+        stops when every row has finished. Returns [B, T + n] int64 on this engine's device.
+        Each row runs its own forward: the reference's batched forward shares one MoE capacity
+        across a batch's rows, which couples them only when the capacity overflows."""
+        K = num_pulses if num_pulses is not None else self.cfg.default_pulses
+        if K != self.cfg.default_pulses:
+            raise ValueError(f"model_generate: the engine runs {self.cfg.default_pulses} pulses, got num_pulses={K}")
+        eos = eos_token_id if eos_token_id is not None else self.cfg.eos_token_id
+        ids = torch.as_tensor(input_ids)
+        if ids.dim() == 1:
+            ids = ids.view(1, -1)
+        rows = [r.tolist() for r in ids.cpu()]
+        finished = [False] * len(rows)
+        cache = self.new_cache()
+        try:
+            for _ in range(max_new_tokens):
+                for b, row in enumerate(rows):
+                    lg = self.dev.forward(cache.slot, row[-self.cfg.max_seq_len:]).float().cpu().clone()
+                    if repetition_penalty != 1.0:
+                        seen = torch.tensor(sorted(set(row)), dtype=torch.long)
+                        vals = lg[seen]
+                        lg[seen] = torch.where(vals > 0, vals / repetition_penalty, vals * repetition_penalty)
+                    if temperature > 0:
+                        lg = lg / temperature
+                        if top_k > 0:
+                            v, _ = torch.topk(lg, min(top_k, lg.numel()))
+                            lg[lg < v[-1]] = float("-inf")
+                        if top_p < 1.0:
+                            sl, si = torch.sort(lg, descending=True)
+                            cum = torch.cumsum(torch.softmax(sl, dim=-1), dim=-1)
+                            rm = cum > top_p
+                            rm[1:] = rm[:-1].clone()
+                            rm[0] = False
+                            lg[si[rm]] = float("-inf")
+                        tok = int(torch.multinomial(torch.softmax(lg, dim=-1), 1, generator=generator))
+                    else:
+                        tok = int(lg.argmax())
+                    if finished[b]:
+                        tok = eos
+                    row.append(tok)
+                    finished[b] = finished[b] or tok == eos
+                if all(finished):
+                    break
+        finally:
+            cache.release()
+        return torch.tensor(rows, dtype=torch.int64, device=self.device)
 
 def load_inference_model(checkpoint_path: str, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
                          tokenizer_path: str = "data/pulsar_tokenizer", **engine_kwargs):

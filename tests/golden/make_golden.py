@@ -21,6 +21,9 @@ Cases:
             max-probabilities over a range where the thresholds split exits across depths.
             early_exit_nolora also zeroes every loop-adapter lora_B (the reference's own
             initialisation of lora_B, src/model.py:710-714).
+  forward_* - PulsarForCausalLM.forward / generate (the training-style full recompute that
+            model.generate runs per token): last-position logits and greedy, penalised and
+            sampled streams.
 """
 
 from __future__ import annotations
@@ -180,6 +183,42 @@ def run_early_exit(name, cfg_dict, recipe, seed, prompt_seed, prompt_len, n_new,
     print(f"wrote {path}", flush=True)
 
 
+def run_forward(name, cfg_dict, recipe, seed, prompt_seed, prompt_len, n_new, out_dir, full_logits, sampled,
+                b_std=0.09):
+    """PulsarForCausalLM.forward (labels=None) and PulsarForCausalLM.generate
+    (src/model.py:1956-2125, 2246-2317): last-position softcapped logits of the prompt, the
+    greedy stream, the greedy stream with repetition penalty 1.15 and, when `sampled`, a
+    temperature 0.8 / top-k 50 / top-p 0.9 stream drawn after torch.manual_seed(11)."""
+    from src.model import PulsarConfig, PulsarForCausalLM
+    from pulsar_b200.config import PulsarConfig as MyCfg
+
+    cfg = PulsarConfig(**cfg_dict)
+    sd = make_state_dict(MyCfg(**cfg_dict), recipe=recipe, seed=seed, b_std=b_std)
+    torch.manual_seed(1234)
+    model = PulsarForCausalLM(cfg)
+    _, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected, unexpected
+    model.eval()
+    ids = random_prompts(1, prompt_len, cfg.vocab_size, seed=prompt_seed)[0].tolist()
+    probe_idx = torch.randperm(cfg.vocab_size, generator=torch.Generator().manual_seed(7))[:N_PROBE].clone()
+    rec = {"name": name, "cfg": cfg_dict, "recipe": recipe, "seed": seed, "b_std": b_std, "prompt": ids,
+           "n_new": n_new, "probe_idx": probe_idx}
+    x = torch.tensor([ids])
+    with torch.no_grad():
+        logits, _, _ = model(x, labels=None)
+    rec["forward"] = summarise(logits[0, -1], full_logits, probe_idx)
+    rec["greedy_ids"] = model.generate(x, max_new_tokens=n_new, temperature=0.0, repetition_penalty=1.0)[0, len(ids):].tolist()
+    rec["greedy_rep115_ids"] = model.generate(x, max_new_tokens=n_new, temperature=0.0,
+                                              repetition_penalty=1.15)[0, len(ids):].tolist()
+    if sampled:
+        torch.manual_seed(11)
+        rec["sampled_ids"] = model.generate(x, max_new_tokens=n_new, temperature=0.8, top_k=50, top_p=0.9,
+                                            repetition_penalty=1.15)[0, len(ids):].tolist()
+    path = os.path.join(out_dir, f"{name}.pt")
+    torch.save(rec, path)
+    print(f"wrote {path}: greedy={rec['greedy_ids']} rep={rec['greedy_rep115_ids']}", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("PULSAR_REFERENCE"),
@@ -216,6 +255,15 @@ def main():
         if args.only and c[0] != args.only:
             continue
         run_early_exit(*c[:11], args.out, *c[11:])
+    fwd_cases = [
+        # name, cfg, recipe, seed, prompt seed, prompt len, n_new, full logits, sampled, b_std
+        ("forward_tiny_B", tiny_cfg_dict(), "B", 0, 3, 40, 8, True, True, 0.35),   # T > window, > base
+        ("forward_full_A", full, "A", 0, 6, 1100, 2, False, False),                # YaRN on layers 3, 7
+    ]
+    for c in fwd_cases:
+        if args.only and c[0] != args.only:
+            continue
+        run_forward(*c[:7], args.out, *c[7:])
 
 
 if __name__ == "__main__":

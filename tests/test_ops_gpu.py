@@ -201,7 +201,8 @@ def _misaligned(t):
 @pytest.mark.parametrize("D", [1024, 1000])
 def test_vector_and_scalar_forms_agree(pc, D):
     """The 16-byte kernels (D % 8 == 0, aligned tensors) give bit-identical results to the
-    element-wise kernels (same summation order per element), for conv, combine and dispatch."""
+    element-wise kernels (same summation order per element), for conv, combine, dispatch,
+    swiglu and rope; rmsnorm's warp-per-row form agrees within bf16 rounding."""
     torch.manual_seed(5)
     B, T = 3, 40
     x = torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16)
@@ -220,6 +221,19 @@ def test_vector_and_scalar_forms_agree(pc, D):
     o3 = pc.moe_combine_forward(eo, idx, tw, slots, None)
     o4 = pc.moe_combine_forward(_misaligned(eo), idx, tw, slots, None)
     assert torch.equal(o1, o2) and torch.equal(o3, o4)
+    # swiglu and rope: element-wise, so the 16-byte and element-wise forms agree exactly
+    gu = _bf16(N, 2 * D, seed=24)
+    assert torch.equal(pc.fused_swiglu_forward(gu, D), pc.fused_swiglu_forward(_misaligned(gu), D))
+    q = _bf16(2, 4, 40, 64, seed=25)
+    cos, sin = _tables(40, 64)
+    assert torch.equal(pc.rope_forward(q, cos, sin), pc.rope_forward(_misaligned(q), cos, sin))
+    # rmsnorm: the warp-per-row form (D % 256 == 0) sums in another order; within bf16 rounding
+    x2 = _bf16(N, D, seed=26)
+    w2 = torch.rand(D, device="cuda") + 0.5
+    y1, r1 = pc.rmsnorm_forward(x2, w2, 1e-6)
+    y2, r2 = pc.rmsnorm_forward(_misaligned(x2), w2, 1e-6)
+    assert torch.allclose(r1, r2, rtol=1e-6, atol=0)
+    assert_close(y1, y2, atol=2e-2, msg="rmsnorm forms")
     if D % 8 == 0:   # dispatch requires D % 8 == 0 (the reference's check)
         xs = _bf16(N, D, seed=23)
         # distinct (expert, slot) pairs so the copy order does not matter

@@ -17,7 +17,7 @@ _MODELS = {}
 
 
 def _model(g):
-    key = (g["name"].split("_")[0], g["recipe"], g["seed"], g.get("b_std", 0.09))
+    key = (g["cfg"].get("d_model", 1024), g["cfg"].get("n_core", 8), g["recipe"], g["seed"], g.get("b_std", 0.09))
     if key not in _MODELS:
         cfg = PulsarConfig(**g["cfg"])
         sd = make_state_dict(cfg, recipe=g["recipe"], seed=g["seed"], b_std=g.get("b_std", 0.09))
@@ -133,6 +133,38 @@ def test_block_spec_penalised_matches_reference_stream_on_tiny(gamma):
     ref = g["greedy_rep115_ids"]
     assert O.block_spec_generate_ids(m, g["prompt"], len(ref), gamma=gamma, repetition_penalty=1.15) == ref
     assert O.block_spec_generate_ids(m, g["prompt"], len(ref), gamma=gamma) != ref
+
+
+def test_forward_and_model_generate_tiny():
+    """PulsarForCausalLM.forward / generate (src/model.py:1956-2125, 2246-2317) on the tiny
+    config with a 40-token prompt (T > window and > base_seq_len): the oracle's full-sequence
+    forward against the reference's softcapped logits, and its model_generate streams (greedy,
+    penalised, and sampled from the same seed) against the reference's."""
+    g = load_golden("forward_tiny_B")
+    m, _ = _model(g)
+    lg = O.forward_logits(m, g["prompt"])
+    _check_logits(lg, g["forward"], ORACLE_TOL, "forward")
+    n, T = g["n_new"], len(g["prompt"])
+    assert O.model_generate_ids(m, [g["prompt"]], n, temperature=0.0, repetition_penalty=1.0)[0][T:] == g["greedy_ids"]
+    assert O.model_generate_ids(m, [g["prompt"]], n, temperature=0.0, repetition_penalty=1.15)[0][T:] == \
+        g["greedy_rep115_ids"]
+    gen = torch.Generator().manual_seed(11)
+    assert O.model_generate_ids(m, [g["prompt"]], n, temperature=0.8, top_k=50, top_p=0.9, repetition_penalty=1.15,
+                                generator=gen)[0][T:] == g["sampled_ids"]
+    # the forward is not the inference prefill (value residual, masks, softcap)
+    assert (O.prefill(m, g["prompt"], O.OracleKV(m, 64)) - lg).abs().max().item() > 1e-2
+
+
+def test_forward_full_yarn():
+    """The production config at T = 1100 > 1024: YaRN on the global layers (3, 7) and causal
+    attention over all 1100 keys on the local layers (the reference's sliding window starts
+    beyond 4096 tokens)."""
+    g = load_golden("forward_full_A")
+    m, _ = _model(g)
+    g["forward"]["_probe_idx"] = g["probe_idx"]
+    lg = O.forward_logits(m, g["prompt"])
+    _check_logits(lg, g["forward"], ORACLE_TOL, "forward T=1100")
+    assert int(lg.argmax()) == g["greedy_ids"][0]
 
 
 def test_philox_known_answer():
