@@ -739,7 +739,7 @@ T* offs(T* p, int64_t n) { return p ? p + n : nullptr; }
 template <typename KVT, int NU>
 int launch_attn_flash_nu(pulsar_engine* e, dim3 grid, const int4* rows, int R, const float* q, const KVLayer& L,
                          int local, int nsplit, float* part, cudaStream_t st) {
-    constexpr int smem = (int)attn_flash_smem<KVT>();
+    constexpr int smem = (int)attn_flash_smem<KVT, NU>();
     PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_attn_flash<KVT, NU>), smem, "k_attn_flash shared memory"));
     k_attn_flash<KVT, NU><<<grid, ATT_FTHREADS, smem, st>>>(rows, R, e->attn_rpb, q, L, local, nsplit, part, e->max_pos(),
                                                             e->cfg.max_batch, e->m_err);

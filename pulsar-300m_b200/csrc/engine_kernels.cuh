@@ -297,7 +297,9 @@ __global__ void __launch_bounds__((H + HKV) * 32) k_qkv_post(
 constexpr int ATT_RPB_MAX = 8;
 constexpr int ATT_FCK = 64;          // keys per chunk
 constexpr int ATT_FTHREADS = 256;
-template <typename KVT>
+// KT: blocks of two or more rows keep an fp32 K^T copy of the chunk (kt[dim][key]) for their
+// scores, so that a warp reads one K^T row (consecutive keys) and broadcasts the queries.
+template <typename KVT, bool KT = false>
 struct AttnFlashSmem {
     uint64_t full[2];
     alignas(128) KVT k[2][ATT_FCK * DH];
@@ -305,11 +307,28 @@ struct AttnFlashSmem {
     alignas(16) float q[ATT_RPB_MAX * GQA][DH];
     alignas(16) float sc[ATT_RPB_MAX * GQA][ATT_FCK];
     float m[ATT_RPB_MAX * GQA], l[ATT_RPB_MAX * GQA], scale[ATT_RPB_MAX * GQA];
+    float kt[KT ? DH : 1][ATT_FCK + 1];
 };
 
+// 16 consecutive elements of a K row as fp32 (two 16-byte loads for bf16, four for fp32).
+__device__ __forceinline__ void attn_row16(const __nv_bfloat16* p, float* f) {
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(p)[0], f);
+    bf16x8_to_f32(reinterpret_cast<const uint4*>(p)[1], f + 8);
+}
+__device__ __forceinline__ void attn_row16(const float* p, float* f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 v = reinterpret_cast<const float4*>(p)[i];
+        f[4 * i] = v.x;
+        f[4 * i + 1] = v.y;
+        f[4 * i + 2] = v.z;
+        f[4 * i + 3] = v.w;
+    }
+}
+
 // Issue the bulk copies of chunk [k0, k0 + nk) of (slot, head g) into ring stage st (one thread).
-template <typename KVT>
-__device__ __forceinline__ void attn_issue(AttnFlashSmem<KVT>* s, int st, const KVLayer& L, int slot, int g, int k0,
+template <typename KVT, bool KT>
+__device__ __forceinline__ void attn_issue(AttnFlashSmem<KVT, KT>* s, int st, const KVLayer& L, int slot, int g, int k0,
                                            int nk) {
     constexpr uint32_t ROW = DH * sizeof(KVT);
     mbar_arrive_expect_tx(&s->full[st], 2u * nk * ROW);
@@ -341,8 +360,9 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                                                              const float* __restrict__ q, KVLayer L, int is_local,
                                                              int nsplit, float* __restrict__ part, int max_pos,
                                                              int n_slots, int* err) {
+    constexpr bool KT = NU >= 2;
     extern __shared__ __align__(128) unsigned char att_raw[];
-    auto* s = reinterpret_cast<AttnFlashSmem<KVT>*>(att_raw);
+    auto* s = reinterpret_cast<AttnFlashSmem<KVT, KT>*>(att_raw);
     const int sp = blockIdx.x, g = blockIdx.y;
     const int rb0 = blockIdx.z * rpb, rb1 = min(R, rb0 + rpb);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -379,7 +399,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
         auto chunk_k0 = [&](int i) { return lo0 + (sp + i * nsplit) * ATT_FCK; };
         auto chunk_nk = [&](int i) { return min(chunk_k0(i) + ATT_FCK, posL + 1) - chunk_k0(i); };
         if (tid == 0)
-            for (int i = 0; i < 2 && i < mine; ++i) attn_issue<KVT>(s, i, L, first.x, g, chunk_k0(i), chunk_nk(i));
+            for (int i = 0; i < 2 && i < mine; ++i) attn_issue<KVT, KT>(s, i, L, first.x, g, chunk_k0(i), chunk_nk(i));
         float o[NU];   // P.V accumulators of dimension `key` for units grp, grp + 4, ...
 #pragma unroll
         for (int j = 0; j < NU; ++j) o[j] = 0.f;
@@ -401,14 +421,40 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
             ++uses[st];
             const KVT* Kt = s->k[st];
             const KVT* Vt = s->v[st];
-            // scores: thread (key, unit group); the key's row is read in rotated pair order
-            // (pair (j + lane) mod 32 at step j: one bank per lane of the warp)
+            // scores: thread (key, unit group). Blocks of one row read the key's row in rotated
+            // pair order (pair (j + lane) mod 32 at step j: one bank per lane of the warp); blocks
+            // of several rows first transpose the chunk to fp32 K^T (thread: key t / 4, dims
+            // 16 (t % 4) ..), then read K^T rows by key and broadcast each unit's query.
+            if constexpr (KT) {
+                const int tk = tid >> 2, tq = tid & 3;
+                if (tk < nk) {
+                    float f[16];
+                    attn_row16(Kt + tk * DH + 16 * tq, f);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) s->kt[16 * tq + j][tk] = f[j];
+                }
+                __syncthreads();
+            }
             {
                 const int kk = key, kpos = k0 + kk;
                 float acc[NU];
 #pragma unroll
                 for (int j = 0; j < NU; ++j) acc[j] = 0.f;
-                if (kk < nk) {
+                if (KT && kk < nk) {
+#pragma unroll 4
+                    for (int d = 0; d < DH; d += 4) {
+                        const float c0 = s->kt[d][kk], c1 = s->kt[d + 1][kk], c2 = s->kt[d + 2][kk],
+                                    c3 = s->kt[d + 3][kk];
+#pragma unroll
+                        for (int uu = 0; uu < NU; ++uu) {
+                            const int u = grp + 4 * uu;
+                            if (u < nq) {
+                                const float4 qv = *reinterpret_cast<const float4*>(&s->q[u][d]);
+                                acc[uu] += qv.x * c0 + qv.y * c1 + qv.z * c2 + qv.w * c3;
+                            }
+                        }
+                    }
+                } else if (kk < nk) {
                     const KVT* kr = Kt + kk * DH;
 #pragma unroll 4
                     for (int j = 0; j < DH / 2; ++j) {
@@ -480,7 +526,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                     if (uu < nu) o[uu] += s->sc[grp + 4 * uu][kk] * v;
             }
             __syncthreads();   // stage st is free again
-            if (tid == 0 && i + 2 < mine) attn_issue<KVT>(s, st, L, first.x, g, chunk_k0(i + 2), chunk_nk(i + 2));
+            if (tid == 0 && i + 2 < mine) attn_issue<KVT, KT>(s, st, L, first.x, g, chunk_k0(i + 2), chunk_nk(i + 2));
         }
         // partial (m, l, o) of every unit at index sp
 #pragma unroll
@@ -500,9 +546,9 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
     }
 }
 
-template <typename KVT>
+template <typename KVT, int NU = 1>
 constexpr size_t attn_flash_smem() {
-    return sizeof(AttnFlashSmem<KVT>) + 128;
+    return sizeof(AttnFlashSmem<KVT, (NU >= 2)>) + 128;
 }
 
 // Splits of a flash-decoding launch: enough blocks to fill the GPU (about 6 per SM) when a pass
