@@ -628,31 +628,35 @@ def run_ops(args):
     flush = torch.empty(256 * 2 ** 20 // 4, device=dev)
     st = torch.cuda.current_stream()
 
-    def time_op(fn):
-        for _ in range(3):
-            fn()
-        ts = []
-        for _ in range(max(5, args.kernel_reps)):
-            flush.fill_(1.0)
-            # ~100 us of device-side spin after the flush: the host enqueues the op (its Python /
-            # binding overhead) before the GPU reaches the start event, so the events bracket
-            # device time only
-            torch.cuda._sleep(200_000)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(st)
-            fn()
-            b.record(st)
-            b.synchronize()
-            ts.append(a.elapsed_time(b) * 1e3)
-        return statistics.median(ts)
+    def time_once(fn):
+        flush.fill_(1.0)
+        # ~100 us of device-side spin after the flush: the host enqueues the op (its Python /
+        # binding overhead) before the GPU reaches the start event, so the events bracket
+        # device time only
+        torch.cuda._sleep(200_000)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        b.synchronize()
+        return a.elapsed_time(b) * 1e3
 
     out = {}
     for name, (call, nbytes) in cases.items():
+        arms = [("shim", pc)] + ([("reference", ref)] if ref is not None else [])
+        for _, mod in arms:
+            for _ in range(3):
+                call(mod)
+        ts = {k: [] for k, _ in arms}
+        for rep in range(max(5, args.kernel_reps)):   # the arms alternate which one runs first
+            order = arms if rep % 2 == 0 else arms[::-1]
+            for k, mod in order:
+                ts[k].append(time_once(lambda: call(mod)))
         row = {"bytes": nbytes}
-        us = time_op(lambda: call(pc))
+        us = statistics.median(ts["shim"])
         row["shim_us"], row["shim_gbs"] = round(us, 2), round(nbytes / us / 1e3, 1)
         if ref is not None:
-            ur = time_op(lambda: call(ref))
+            ur = statistics.median(ts["reference"])
             row["reference_us"], row["reference_gbs"] = round(ur, 2), round(nbytes / ur / 1e3, 1)
             row["speedup"] = round(ur / us, 2)
         out[name] = row

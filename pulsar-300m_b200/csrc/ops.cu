@@ -140,11 +140,14 @@ __global__ void k_swiglu(const __nv_bfloat16* __restrict__ gu, int64_t rows, int
 }
 
 // 16-byte form (d % 8 == 0, gu / out 16-byte aligned): a thread per 8 outputs.
+// sh >= 0: d / 8 is 2^sh, so the row and column come from a shift and a mask.
 template <typename IT>
-__global__ void k_swiglu_v8(const __nv_bfloat16* __restrict__ gu, IT rows, IT d, __nv_bfloat16* __restrict__ out) {
+__global__ void k_swiglu_v8(const __nv_bfloat16* __restrict__ gu, IT rows, IT d, int sh,
+                            __nv_bfloat16* __restrict__ out) {
     const IT d8 = d >> 3, n = rows * d8;
     for (IT i = blockIdx.x * (IT)blockDim.x + threadIdx.x; i < n; i += (IT)gridDim.x * blockDim.x) {
-        const IT r = i / d8, j = (i - r * d8) * 8;
+        const IT r = sh >= 0 ? (i >> sh) : i / d8;
+        const IT j = (i - r * d8) * 8;
         float g[8], u[8], o[8];
         bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(gu + r * 2 * d + j)), g);
         bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(gu + r * 2 * d + d + j)), u);
@@ -251,6 +254,55 @@ __global__ void k_qk_rmsnorm_rope(const __nv_bfloat16* __restrict__ x, int64_t s
     }
 }
 
+// Half-warp per vector form (every vector's base 8-byte aligned): lane j of the half holds
+// elements 4j..4j+3 (one 8-byte load); the rotation partner of element d (d +- 32) sits on lane
+// j ^ 8, one shuffle away. Each warp takes two vectors per step (the loop stays warp-uniform).
+template <typename IT>
+__global__ void k_qk_rmsnorm_rope_h(const __nv_bfloat16* __restrict__ x, IT sB, IT sH, IT sT, IT n_vec, int n_heads,
+                                    IT T, const float* __restrict__ w, const float* __restrict__ cs,
+                                    const float* __restrict__ sn, float eps, __nv_bfloat16* __restrict__ y,
+                                    float* __restrict__ rs) {
+    const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
+    const IT warps = (IT)gridDim.x * (blockDim.x >> 5);
+    for (IT vp = blockIdx.x * (IT)(blockDim.x >> 5) + (threadIdx.x >> 5); 2 * vp < n_vec; vp += warps) {
+        const IT v = 2 * vp + half;
+        const bool ok = v < n_vec;
+        const IT vv = ok ? v : 2 * vp;
+        const IT t = vv % T;
+        const IT ht = vv / T;
+        const int h = (int)(ht % n_heads);
+        const IT b = ht / n_heads;
+        const __nv_bfloat16* xv = x + b * sB + (IT)h * sH + t * sT + 4 * hl;
+        const uint2 u = *reinterpret_cast<const uint2*>(xv);
+        const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        const float f[4] = {p0.x, p0.y, p1.x, p1.y};
+        float ss = f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(ss / 64.f + eps);
+        if (ok && hl == 0 && rs) rs[v] = inv;
+        const float4 wv = *reinterpret_cast<const float4*>(w + h * 64 + 4 * hl);
+        const float q[4] = {wv.x * (f[0] * inv), wv.y * (f[1] * inv), wv.z * (f[2] * inv), wv.w * (f[3] * inv)};
+        float pq[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pq[i] = __shfl_xor_sync(0xffffffffu, q[i], 8);
+        const float4 c4 = *reinterpret_cast<const float4*>(cs + t * 32 + 4 * (hl & 7));
+        const float4 s4 = *reinterpret_cast<const float4*>(sn + t * 32 + 4 * (hl & 7));
+        const float c[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+        float o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = hl < 8 ? q[i] * c[i] - pq[i] * sv[i] : q[i] * c[i] + pq[i] * sv[i];
+        if (ok) {
+            const __nv_bfloat162 a0 = __floats2bfloat162_rn(o[0], o[1]), a1 = __floats2bfloat162_rn(o[2], o[3]);
+            uint2 st;
+            st.x = *reinterpret_cast<const uint32_t*>(&a0);
+            st.y = *reinterpret_cast<const uint32_t*>(&a1);
+            *reinterpret_cast<uint2*>(y + v * 64 + 4 * hl) = st;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- attention gate
 // IT: index type (32-bit when the element count allows: cheaper divisions).
 template <typename IT>
@@ -341,40 +393,44 @@ __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ eo, const int64_
 
 // 16-byte form of k_moe_combine (D % 8 == 0, every bf16 tensor 16-byte aligned): a thread per
 // 8 channels of one token, same summation order (shared output, then the routes in k order).
+// KC > 0: the route count K known at compile time (the model's top-4), the routes unrolled.
+template <int KC>
 __global__ void k_moe_combine_v8(const __nv_bfloat16* __restrict__ eo, const int64_t* __restrict__ idx,
                                  const __nv_bfloat16* __restrict__ tw, const int32_t* __restrict__ slot,
-                                 const __nv_bfloat16* __restrict__ sh, int64_t N, int K, int64_t E, int64_t C,
-                                 int64_t D, __nv_bfloat16* __restrict__ out) {
-    const int64_t D8 = D >> 3;
-    for (int64_t t = blockIdx.x; t < N; t += gridDim.x) {
-        for (int64_t c = threadIdx.x; c < D8; c += blockDim.x) {
+                                 const __nv_bfloat16* __restrict__ sh, int N, int Kr, int E, int C, int D,
+                                 __nv_bfloat16* __restrict__ out) {
+    const int K = KC > 0 ? KC : Kr;
+    const int D8 = D >> 3;
+    for (int t = blockIdx.x; t < N; t += gridDim.x) {
+        for (int c = threadIdx.x; c < D8; c += blockDim.x) {
             float acc[8];
             if (sh) {
-                bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(sh + t * D) + c), acc);
+                bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(sh + (int64_t)t * D) + c), acc);
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) acc[j] = 0.f;
             }
-            // up to 8 routes: every route's 16-byte load in flight before the accumulation (in k order)
-            int k0 = 0;
-            for (; k0 < K; k0 += 8) {
-                uint4 rv[8];
-                float wt[8];
-                bool ok[8];
+            // routes in groups of G: every route's 16-byte load in flight before the accumulation
+            // (in k order)
+            constexpr int G = KC > 0 ? KC : 8;
+            for (int k0 = 0; k0 < K; k0 += G) {
+                uint4 rv[G];
+                float wt[G];
+                bool ok[G];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < G; ++u) {
                     const int k = k0 + u;
                     ok[u] = false;
                     if (k < K) {
-                        const int64_t e = __ldg(idx + t * K + k);
-                        const int s = __ldg(slot + t * K + k);
+                        const int64_t e = __ldg(idx + (int64_t)t * K + k);
+                        const int s = __ldg(slot + (int64_t)t * K + k);
                         ok[u] = s >= 0 && s < C && e >= 0 && e < E;
-                        wt[u] = __bfloat162float(tw[t * K + k]);
-                        if (ok[u]) rv[u] = __ldg(reinterpret_cast<const uint4*>(eo + (e * C + s) * D) + c);
+                        wt[u] = __bfloat162float(tw[(int64_t)t * K + k]);
+                        if (ok[u]) rv[u] = __ldg(reinterpret_cast<const uint4*>(eo + (e * C + s) * (int64_t)D) + c);
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < G; ++u) {
                     if (ok[u]) {
                         float v[8];
                         bf16x8_to_f32(rv[u], v);
@@ -383,7 +439,7 @@ __global__ void k_moe_combine_v8(const __nv_bfloat16* __restrict__ eo, const int
                     }
                 }
             }
-            reinterpret_cast<uint4*>(out + t * D)[c] = f32_to_bf16x8(acc);
+            reinterpret_cast<uint4*>(out + (int64_t)t * D)[c] = f32_to_bf16x8(acc);
         }
     }
 }
@@ -500,12 +556,14 @@ extern "C" int pulsar_op_swiglu(const void* gu, int64_t rows, int64_t d_ff, void
     PULSAR_CHECK_ARG(rows >= 0 && d_ff > 0, "swiglu: invalid shape");
     if (rows == 0) return PULSAR_OK;
     if (d_ff % 8 == 0 && aligned16(gu) && aligned16(out)) {
+        const int64_t d8 = d_ff / 8;
+        const int sh = (d8 & (d8 - 1)) == 0 ? __builtin_ctzll((unsigned long long)d8) : -1;
         if (rows * d_ff * 2 < (int64_t)1 << 31)
             k_swiglu_v8<int><<<grid_cap(rows * d_ff / 8, 256), 256, 0, S(stream)>>>((const __nv_bfloat16*)gu, (int)rows,
-                                                                                     (int)d_ff, (__nv_bfloat16*)out);
+                                                                                     (int)d_ff, sh, (__nv_bfloat16*)out);
         else
             k_swiglu_v8<int64_t><<<grid_cap(rows * d_ff / 8, 256), 256, 0, S(stream)>>>(
-                (const __nv_bfloat16*)gu, rows, d_ff, (__nv_bfloat16*)out);
+                (const __nv_bfloat16*)gu, rows, d_ff, sh, (__nv_bfloat16*)out);
         PULSAR_LAUNCH_CHECK("k_swiglu_v8");
         return PULSAR_OK;
     }
@@ -546,6 +604,22 @@ extern "C" int pulsar_op_qk_rmsnorm_rope(const void* x, int64_t sB, int64_t sH, 
     PULSAR_CHECK_ARG(n_vec >= 0 && n_heads > 0, "qk_rmsnorm_rope: invalid shape");
     if (n_vec == 0) return PULSAR_OK;
     PULSAR_CHECK_ARG(T > 0 && x && w && cs && sn && y, "qk_rmsnorm_rope: invalid arguments");
+    const bool a8 = (reinterpret_cast<uintptr_t>(x) & 7) == 0 && sB % 4 == 0 && sH % 4 == 0 && sT % 4 == 0 &&
+                    aligned16(w) && aligned16(cs) && aligned16(sn) && (reinterpret_cast<uintptr_t>(y) & 7) == 0;
+    if (a8) {
+        // largest element offset read: (B - 1) sB + (heads - 1) sH + (T - 1) sT + 63
+        const int64_t nb = n_vec / (T * n_heads);
+        const int64_t span = (nb > 0 ? nb - 1 : 0) * sB + (n_heads - 1) * sH + (T - 1) * sT + 64;
+        if (n_vec * 64 < (int64_t)1 << 31 && span < (int64_t)1 << 31 && sB >= 0 && sH >= 0 && sT >= 0)
+            k_qk_rmsnorm_rope_h<int><<<grid_cap(n_vec, 16), 256, 0, S(stream)>>>(
+                (const __nv_bfloat16*)x, (int)sB, (int)sH, (int)sT, (int)n_vec, (int)n_heads, (int)T, w, cs, sn, eps,
+                (__nv_bfloat16*)y, rs);
+        else
+            k_qk_rmsnorm_rope_h<int64_t><<<grid_cap(n_vec, 16), 256, 0, S(stream)>>>(
+                (const __nv_bfloat16*)x, sB, sH, sT, n_vec, (int)n_heads, T, w, cs, sn, eps, (__nv_bfloat16*)y, rs);
+        PULSAR_LAUNCH_CHECK("k_qk_rmsnorm_rope_h");
+        return PULSAR_OK;
+    }
     k_qk_rmsnorm_rope<<<grid_cap(n_vec, 8), 256, 0, S(stream)>>>((const __nv_bfloat16*)x, sB, sH, sT, n_vec,
                                                                   (int)n_heads, T, w, cs, sn, eps,
                                                                   (__nv_bfloat16*)y, rs);
@@ -593,11 +667,17 @@ extern "C" int pulsar_op_moe_combine(const void* eo, const int64_t* idx, const v
                                      void* stream) {
     PULSAR_CHECK_ARG(N >= 0 && K >= 0 && E > 0 && C >= 0 && D > 0, "moe_combine: invalid shape");
     if (N == 0) return PULSAR_OK;
-    if (D % 8 == 0 && aligned16(eo) && aligned16(sh) && aligned16(out)) {
+    const bool fits32 = N < ((int64_t)1 << 31) && E * C < ((int64_t)1 << 31) && D < ((int64_t)1 << 31);
+    if (D % 8 == 0 && fits32 && aligned16(eo) && aligned16(sh) && aligned16(out)) {
         const int threads = D / 8 >= 128 ? 128 : (int)((D / 8 + 31) / 32 * 32);
-        k_moe_combine_v8<<<grid_cap(N, 1), threads, 0, S(stream)>>>(
-            (const __nv_bfloat16*)eo, idx, (const __nv_bfloat16*)tw, slot, (const __nv_bfloat16*)sh, N, (int)K, E, C, D,
-            (__nv_bfloat16*)out);
+        if (K == 4)
+            k_moe_combine_v8<4><<<grid_cap(N, 1), threads, 0, S(stream)>>>(
+                (const __nv_bfloat16*)eo, idx, (const __nv_bfloat16*)tw, slot, (const __nv_bfloat16*)sh, (int)N, 4,
+                (int)E, (int)C, (int)D, (__nv_bfloat16*)out);
+        else
+            k_moe_combine_v8<0><<<grid_cap(N, 1), threads, 0, S(stream)>>>(
+                (const __nv_bfloat16*)eo, idx, (const __nv_bfloat16*)tw, slot, (const __nv_bfloat16*)sh, (int)N, (int)K,
+                (int)E, (int)C, (int)D, (__nv_bfloat16*)out);
         PULSAR_LAUNCH_CHECK("k_moe_combine_v8");
         return PULSAR_OK;
     }

@@ -227,6 +227,15 @@ def test_vector_and_scalar_forms_agree(pc, D):
     q = _bf16(2, 4, 40, 64, seed=25)
     cos, sin = _tables(40, 64)
     assert torch.equal(pc.rope_forward(q, cos, sin), pc.rope_forward(_misaligned(q), cos, sin))
+    # qk rmsnorm + rope: the half-warp form (8-byte aligned vectors; an odd vector count leaves
+    # the last warp half idle) against the warp-per-vector form, within bf16 rounding
+    qh = _bf16(1, 3, 7, 64, seed=27)
+    wq = torch.rand(3, 64, device="cuda") + 0.5
+    c7, s7 = _tables(7, 64)
+    a1, ra = pc.qk_rmsnorm_rope_forward(qh, wq, c7, s7, 7, 1e-6)
+    a2, rb = pc.qk_rmsnorm_rope_forward(_misaligned(qh), wq, c7, s7, 7, 1e-6)
+    assert torch.allclose(ra, rb, rtol=1e-6, atol=0)
+    assert_close(a1, a2, atol=2e-2, msg="qk_rmsnorm_rope forms")
     # rmsnorm: the warp-per-row form (D % 256 == 0) sums in another order; within bf16 rounding
     x2 = _bf16(N, D, seed=26)
     w2 = torch.rand(D, device="cuda") + 0.5

@@ -70,12 +70,13 @@ def test_rmsnorm(mods):
 
 def test_router_topk(mods):
     pc, ref = mods
-    logits = torch.randn(N, E, device="cuda")
-    bias = torch.randn(E, device="cuda") * 0.1
+    g = torch.Generator(device="cpu").manual_seed(10)
+    logits = torch.randn(N, E, generator=g).cuda()
+    bias = (torch.randn(E, generator=g) * 0.1).cuda()
     i1, w1, z1, p1 = pc.moe_router_topk_forward(logits, bias, K, 1e-3)
     i2, w2, z2, p2 = ref.moe_router_topk_forward(logits, bias, K, 1e-3)
     assert torch.equal(i1.long(), i2.long()), "top-k ids differ"
-    assert torch.allclose(w1.float(), w2.float(), rtol=1e-4, atol=1e-6)
+    _close_bf16(w1, w2, "router weights (bf16)", atol=1e-3)
     assert torch.allclose(p1.float(), p2.float(), rtol=1e-4, atol=1e-7)
     assert torch.allclose(z1.float(), z2.float(), rtol=1e-4, atol=0)
 
