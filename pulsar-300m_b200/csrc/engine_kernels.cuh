@@ -299,14 +299,16 @@ constexpr int ATT_FCK = 64;          // keys per chunk
 constexpr int ATT_FTHREADS = 256;
 // KT: blocks of two or more rows keep an fp32 K^T copy of the chunk (kt[dim][key]) for their
 // scores, so that a warp reads one K^T row (consecutive keys) and broadcasts the queries.
-template <typename KVT, bool KT = false>
+// NQ: query units a block holds (its rows per block x GQA), which sizes the query and score
+// arrays (a one-row block needs 4 of the 32 an eight-row block needs, and fits more blocks per SM).
+template <typename KVT, bool KT = false, int NQ = ATT_RPB_MAX * GQA>
 struct AttnFlashSmem {
     uint64_t full[2];
     alignas(128) KVT k[2][ATT_FCK * DH];
     alignas(128) KVT v[2][ATT_FCK * DH];
-    alignas(16) float q[ATT_RPB_MAX * GQA][DH];
-    alignas(16) float sc[ATT_RPB_MAX * GQA][ATT_FCK];
-    float m[ATT_RPB_MAX * GQA], l[ATT_RPB_MAX * GQA], scale[ATT_RPB_MAX * GQA];
+    alignas(16) float q[NQ][DH];
+    alignas(16) float sc[NQ][ATT_FCK];
+    float m[NQ], l[NQ], scale[NQ];
     float kt[KT ? DH : 1][ATT_FCK + 1];
 };
 
@@ -327,8 +329,8 @@ __device__ __forceinline__ void attn_row16(const float* p, float* f) {
 }
 
 // Issue the bulk copies of chunk [k0, k0 + nk) of (slot, head g) into ring stage st (one thread).
-template <typename KVT, bool KT>
-__device__ __forceinline__ void attn_issue(AttnFlashSmem<KVT, KT>* s, int st, const KVLayer& L, int slot, int g, int k0,
+template <typename KVT, bool KT, int NQ>
+__device__ __forceinline__ void attn_issue(AttnFlashSmem<KVT, KT, NQ>* s, int st, const KVLayer& L, int slot, int g, int k0,
                                            int nk) {
     constexpr uint32_t ROW = DH * sizeof(KVT);
     mbar_arrive_expect_tx(&s->full[st], 2u * nk * ROW);
@@ -362,7 +364,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                                                              int n_slots, int* err) {
     constexpr bool KT = NU >= 2;
     extern __shared__ __align__(128) unsigned char att_raw[];
-    auto* s = reinterpret_cast<AttnFlashSmem<KVT, KT>*>(att_raw);
+    auto* s = reinterpret_cast<AttnFlashSmem<KVT, KT, NU * GQA>*>(att_raw);
     const int sp = blockIdx.x, g = blockIdx.y;
     const int rb0 = blockIdx.z * rpb, rb1 = min(R, rb0 + rpb);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
         auto chunk_k0 = [&](int i) { return lo0 + (sp + i * nsplit) * ATT_FCK; };
         auto chunk_nk = [&](int i) { return min(chunk_k0(i) + ATT_FCK, posL + 1) - chunk_k0(i); };
         if (tid == 0)
-            for (int i = 0; i < 2 && i < mine; ++i) attn_issue<KVT, KT>(s, i, L, first.x, g, chunk_k0(i), chunk_nk(i));
+            for (int i = 0; i < 2 && i < mine; ++i) attn_issue<KVT, KT, NU * GQA>(s, i, L, first.x, g, chunk_k0(i), chunk_nk(i));
         float o[NU];   // P.V accumulators of dimension `key` for units grp, grp + 4, ...
 #pragma unroll
         for (int j = 0; j < NU; ++j) o[j] = 0.f;
@@ -526,7 +528,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                     if (uu < nu) o[uu] += s->sc[grp + 4 * uu][kk] * v;
             }
             __syncthreads();   // stage st is free again
-            if (tid == 0 && i + 2 < mine) attn_issue<KVT, KT>(s, st, L, first.x, g, chunk_k0(i + 2), chunk_nk(i + 2));
+            if (tid == 0 && i + 2 < mine) attn_issue<KVT, KT, NU * GQA>(s, st, L, first.x, g, chunk_k0(i + 2), chunk_nk(i + 2));
         }
         // partial (m, l, o) of every unit at index sp
 #pragma unroll
@@ -548,7 +550,7 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
 
 template <typename KVT, int NU = 1>
 constexpr size_t attn_flash_smem() {
-    return sizeof(AttnFlashSmem<KVT, (NU >= 2)>) + 128;
+    return sizeof(AttnFlashSmem<KVT, (NU >= 2), NU * GQA>) + 128;
 }
 
 // Splits of a flash-decoding launch: enough blocks to fill the GPU (about 6 per SM) when a pass
