@@ -402,9 +402,13 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
         auto chunk_nk = [&](int i) { return min(chunk_k0(i) + ATT_FCK, posL + 1) - chunk_k0(i); };
         if (tid == 0)
             for (int i = 0; i < 2 && i < mine; ++i) attn_issue<KVT, KT, NU * GQA>(s, i, L, first.x, g, chunk_k0(i), chunk_nk(i));
-        float o[NU];   // P.V accumulators of dimension `key` for units grp, grp + 4, ...
+        // P.V accumulators of dimension `key`: one-row blocks, every unit over key quarter grp;
+        // wider blocks, units grp, grp + 4, ... over all keys
+        constexpr int NQ = NU * GQA;
+        constexpr int NO = NU == 1 ? NQ : NU;
+        float o[NO];
 #pragma unroll
-        for (int j = 0; j < NU; ++j) o[j] = 0.f;
+        for (int j = 0; j < NO; ++j) o[j] = 0.f;
         __syncthreads();
         for (int i = 0; i < mine; ++i) {
             const int st = i & 1;
@@ -503,43 +507,108 @@ __global__ void __launch_bounds__(ATT_FTHREADS) k_attn_flash(const int4* __restr
                 }
             }
             __syncthreads();
-            // P.V: thread (dimension `key`, unit group), keys in order; each V element is read
-            // once for all the group's units, the weights four keys at a time
-            const int nu = (nq - grp + 3) / 4;   // units of this group
+            // P.V. One-row blocks: thread (dimension `key`, key quarter grp), every unit of the
+            // block for its dimension over keys [16 grp, 16 grp + 16) of the chunk, each V element
+            // read once for all units, the weights as float4 broadcasts (a warp shares its quarter).
+            // Wider blocks: thread (dimension `key`, unit group grp), keys in order, each V element
+            // read once for the group's units, the weights four keys at a time.
+            if constexpr (NU == 1) {
 #pragma unroll
-            for (int uu = 0; uu < NU; ++uu)
-                if (uu < nu) o[uu] *= s->scale[grp + 4 * uu];
-            int kk = 0;
-            for (; kk + 4 <= nk; kk += 4) {
-                const float v0 = attn_elem(Vt + kk * DH, key), v1 = attn_elem(Vt + (kk + 1) * DH, key);
-                const float v2 = attn_elem(Vt + (kk + 2) * DH, key), v3 = attn_elem(Vt + (kk + 3) * DH, key);
+                for (int u = 0; u < NO; ++u)
+                    if (u < nq) o[u] *= s->scale[u];
+                const int ke = min(16 * grp + 16, nk);
+                int kk = 16 * grp;
+                for (; kk + 4 <= ke; kk += 4) {
+                    const float v0 = attn_elem(Vt + kk * DH, key), v1 = attn_elem(Vt + (kk + 1) * DH, key);
+                    const float v2 = attn_elem(Vt + (kk + 2) * DH, key), v3 = attn_elem(Vt + (kk + 3) * DH, key);
 #pragma unroll
-                for (int uu = 0; uu < NU; ++uu) {
-                    if (uu < nu) {
-                        const float4 pw = *reinterpret_cast<const float4*>(&s->sc[grp + 4 * uu][kk]);
-                        o[uu] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
+                    for (int u = 0; u < NQ; ++u) {
+                        if (u < nq) {
+                            const float4 pw = *reinterpret_cast<const float4*>(&s->sc[u][kk]);
+                            o[u] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
+                        }
                     }
                 }
-            }
-            for (; kk < nk; ++kk) {
-                const float v = attn_elem(Vt + kk * DH, key);
+                for (; kk < ke; ++kk) {
+                    const float v = attn_elem(Vt + kk * DH, key);
+#pragma unroll
+                    for (int u = 0; u < NQ; ++u)
+                        if (u < nq) o[u] += s->sc[u][kk] * v;
+                }
+            } else {
+                const int nu = (nq - grp + 3) / 4;   // units of this group
 #pragma unroll
                 for (int uu = 0; uu < NU; ++uu)
-                    if (uu < nu) o[uu] += s->sc[grp + 4 * uu][kk] * v;
+                    if (uu < nu) o[uu] *= s->scale[grp + 4 * uu];
+                int kk = 0;
+                for (; kk + 4 <= nk; kk += 4) {
+                    const float v0 = attn_elem(Vt + kk * DH, key), v1 = attn_elem(Vt + (kk + 1) * DH, key);
+                    const float v2 = attn_elem(Vt + (kk + 2) * DH, key), v3 = attn_elem(Vt + (kk + 3) * DH, key);
+#pragma unroll
+                    for (int uu = 0; uu < NU; ++uu) {
+                        if (uu < nu) {
+                            const float4 pw = *reinterpret_cast<const float4*>(&s->sc[grp + 4 * uu][kk]);
+                            o[uu] += pw.x * v0 + pw.y * v1 + pw.z * v2 + pw.w * v3;
+                        }
+                    }
+                }
+                for (; kk < nk; ++kk) {
+                    const float v = attn_elem(Vt + kk * DH, key);
+#pragma unroll
+                    for (int uu = 0; uu < NU; ++uu)
+                        if (uu < nu) o[uu] += s->sc[grp + 4 * uu][kk] * v;
+                }
             }
             __syncthreads();   // stage st is free again
             if (tid == 0 && i + 2 < mine) attn_issue<KVT, KT, NU * GQA>(s, st, L, first.x, g, chunk_k0(i + 2), chunk_nk(i + 2));
         }
-        // partial (m, l, o) of every unit at index sp
+        // one-row blocks: the four key quarters' sums, (q0 + q2) + (q1 + q3), through the query
+        // and score arrays (free now: red[2][NQ][64]); then the partial (m, l, o) of every unit
+        // at index sp
+        if constexpr (NU == 1) {
+            float* red = &s->q[0][0];
+            if (grp >= 2) {
 #pragma unroll
-        for (int uu = 0; uu < NU; ++uu) {
-            const int u = grp + 4 * uu;
-            if (u < nq) {
-                float* out = part + (((int64_t)(s0 + u / GQA) * H + g * GQA + u % GQA) * nsplit + sp) * PART;
-                out[2 + key] = o[uu];
-                if (key == 0) {
-                    out[0] = s->m[u];
-                    out[1] = s->m[u] == -INFINITY ? 0.f : s->l[u];
+                for (int u = 0; u < NQ; ++u)
+                    if (u < nq) red[((grp - 2) * NQ + u) * DH + key] = o[u];
+            }
+            __syncthreads();
+            if (grp < 2) {
+#pragma unroll
+                for (int u = 0; u < NQ; ++u)
+                    if (u < nq) o[u] += red[(grp * NQ + u) * DH + key];
+            }
+            __syncthreads();
+            if (grp == 1) {
+#pragma unroll
+                for (int u = 0; u < NQ; ++u)
+                    if (u < nq) red[u * DH + key] = o[u];
+            }
+            __syncthreads();
+            if (grp == 0) {
+#pragma unroll
+                for (int u = 0; u < NQ; ++u) {
+                    if (u < nq) {
+                        float* out = part + (((int64_t)(s0 + u / GQA) * H + g * GQA + u % GQA) * nsplit + sp) * PART;
+                        out[2 + key] = o[u] + red[u * DH + key];
+                        if (key == 0) {
+                            out[0] = s->m[u];
+                            out[1] = s->m[u] == -INFINITY ? 0.f : s->l[u];
+                        }
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int uu = 0; uu < NU; ++uu) {
+                const int u = grp + 4 * uu;
+                if (u < nq) {
+                    float* out = part + (((int64_t)(s0 + u / GQA) * H + g * GQA + u % GQA) * nsplit + sp) * PART;
+                    out[2 + key] = o[uu];
+                    if (key == 0) {
+                        out[0] = s->m[u];
+                        out[1] = s->m[u] == -INFINITY ? 0.f : s->l[u];
+                    }
                 }
             }
         }
