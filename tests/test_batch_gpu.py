@@ -7,7 +7,9 @@ Size-independent properties at (or near) the configs' sizes:
     alone (recipe A, whose top-1 margins are far above the 2e-2 tie tolerance);
   * config 3 (64 sequences, gamma 6, temperature 0.8, top-p 0.95): sequences of the batched
     sampled call match the oracle's block-verify loop on their own Philox stream (seq id =
-    batch index) up to the first decision inside the tie tolerances;
+    batch index) up to the first decision inside the tie tolerances (also at temperature 0.3,
+    where the decided prefix covers the stream);
+  * the largest batch (1024 sequences): batched decoding equals each sequence alone;
   * config 4 (4 sequences, 32768-token prompts, gamma 4): speculative greedy decoding emits
     the tokens of sequential greedy decoding (recipe A margins), exercising the sliding window
     and the YaRN global layers on a full-window cache.
@@ -62,10 +64,14 @@ def test_config5_batch256_greedy_matches_single():
     _batched_vs_single(256, 512, 64, 4, check=(0, 255))
 
 
-def test_config3_batch64_sampled_matches_oracle():
-    """Config 3 shape (reduced lengths): 64 sequences, gamma 6, T 0.8, top-p 0.95, Philox seed 0."""
-    B, T, n, gamma, temp, top_p, seed = 64, 24, 12, 6, 0.8, 0.95, 0
-    eng, sd, cfg = _engine("B", torch.float32, max_batch=B, max_seq_len=T + n + 16, max_prefill=T)
+@pytest.mark.parametrize("recipe,kv,temp,min_decided", [("B", torch.float32, 0.8, 0), ("A", torch.float32, 0.3, 8)])
+def test_config3_batch64_sampled_matches_oracle(recipe, kv, temp, min_decided):
+    """Config 3 shape (reduced lengths): 64 sequences, gamma 6, top-p 0.95, Philox seed 0. At the
+    config's temperature 0.8 the random-init distributions keep ~30k tokens, so few or no draws
+    are outside the tie tolerance (the statistics are still checked); at 0.3 (recipe A) the
+    decided prefix must cover 8+ tokens."""
+    B, T, n, gamma, top_p, seed = 64, 24, 12, 6, 0.95, 0
+    eng, sd, cfg = _engine(recipe, kv, max_batch=B, max_seq_len=T + n + 16, max_prefill=T)
     try:
         use_path(eng, 0)
         P = random_prompts(B, T, cfg.vocab_size, seed=0)
@@ -80,6 +86,7 @@ def test_config3_batch64_sampled_matches_oracle():
             ref = O.block_spec_generate_ids(m, ids, n, gamma=gamma, temperature=temp, top_p=top_p, seed=seed,
                                             seq_id=b, stats=st, trace=trace)
             k = min(n, sampled_safe_prefix(pre, trace, st, gamma, temp, top_p, seed, b))
+            assert k >= min_decided, f"sequence {b}: only {k} decided tokens"
             assert got[b].tolist()[:k] == ref[:k], f"sequence {b}: first {k} tokens differ from the oracle"
     finally:
         eng.close()
@@ -100,3 +107,8 @@ def test_config4_long_context_spec_equals_sequential():
         assert spec.tolist() == seq.tolist()
     finally:
         eng.close()
+
+
+def test_max_batch_1024_greedy_matches_single():
+    """The engine's largest batch: 1024 sequences in one call (verify passes of 5120 rows)."""
+    _batched_vs_single(1024, 16, 8, 4, check=(0, 511, 1023))
