@@ -212,6 +212,19 @@ int pulsar_engine_read_kv(pulsar_engine* eng, int32_t slot, int32_t layer, int32
 int pulsar_engine_prefill_attention(pulsar_engine* eng, int32_t slot, int32_t layer, int32_t T, const float* q_dev,
                                     float* out_dev, int32_t tensor_cores, void* stream);
 
+/* The decode attention of the per-op and many-row pulse passes for one layer (src/infer.py
+ * 290-306 per row: softmax(q k^T / 8) v, without the head gate), over the keys the slot holds
+ * at positions 0..pos (the last 1024 of them on a local layer). rows_dev: [R][4] int32 (slot,
+ * pos, unused, unused), 16-byte aligned, runs of consecutive positions of one slot forming
+ * verify blocks of up to rows_per_block (1..8) rows; q_dev: [R][16][64] fp32 normed and rotated
+ * queries (unscaled); out_dev: [R][16][64] fp32 (0 for a row with no visible key or an invalid
+ * slot or position). tensor_cores 1: k_attn_dec_tc (bf16 cache only; an fp32 cache takes the
+ * SIMT kernel either way), 0: the SIMT k_attn_flash. Device pointers; enqueued on `stream` and
+ * waited for (it allocates its partial buffer): a check, not for the token path. */
+int pulsar_engine_decode_attention(pulsar_engine* eng, int32_t layer, int32_t R, const int32_t* rows_dev,
+                                   int32_t rows_per_block, const float* q_dev, float* out_dev, int32_t tensor_cores,
+                                   void* stream);
+
 /* Greedy decode loop, reference semantics (stream_generate with temperature 0 and
  * repetition_penalty 1, src/infer.py:551-621): starting from the prefill logits already
  * in the slot's state, emit n_new tokens. gamma == 0: exact sequential decode (3 pulses
@@ -309,6 +322,10 @@ int pulsar_engine_early_exit_counts(pulsar_engine* eng, int64_t* counts_host);
  * bf16 A, bf16(bf16 B * bf16(loop_M[p] * alpha / q)), fp32 product sum in order plus the
  * base, one rounding) and run every pass on them, the persistent kernel included; 0 returns
  * to the exact fp32 adapter correction. Without a live adapter it stays 0. */
+/* "tc_dec_attn" (0/1, default 1): the decode attention of the per-op and many-row passes on
+ * the tensor cores (128-key chunks fed by tensor-map loads, Q and P split into bf16 hi + lo)
+ * for a bf16 cache; 0 selects the SIMT kernel. Reads back 1 only when the tensor-core kernel
+ * is in use (an fp32 cache always takes the SIMT kernel). */
 int pulsar_engine_set_option(pulsar_engine* eng, const char* name, int64_t value);
 int pulsar_engine_get_option(pulsar_engine* eng, const char* name, int64_t* value);
 

@@ -9,6 +9,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "capi_util.h"
@@ -19,6 +20,7 @@
 #include "tc_gemm.cuh"
 #include "prefill_attn_tc.cuh"
 #include "tma_gemm.cuh"
+#include "dec_attn_tc.cuh"
 
 using namespace pulsar;
 
@@ -533,6 +535,11 @@ struct pulsar_engine {
     int64_t kv_bytes = 0, arena_bytes = 0, work_bytes = 0;
     KVLayer kvl[NL];
     int nch[NL] = {};
+    // bf16 cache: one 2-D tensor map over the whole arena (rows of 64 elements, boxes of 128 rows)
+    // for the tensor-core decode attention, and each layer's first row in it
+    alignas(64) CUtensorMap kv_map{};
+    bool kv_map_ok = false;
+    int64_t kv_lrow[NL] = {};
     std::vector<int> len;
     // decode workspace (R <= MAX_ROWS)
     struct {
@@ -549,6 +556,7 @@ struct pulsar_engine {
     bool use_tc = true;        // option "tc_gemm": tensor-core GEMMs (prefill, wide path)
     bool tc_attn = true;       // option "tc_attn": prefill attention on the tensor cores
     bool use_tma = true;       // option "tma_gemm": TMA-fed warp-specialised GEMM where it applies
+    bool tc_dec = true;        // option "tc_dec_attn": decode attention on the tensor cores (bf16 cache)
     // bf16 hi / lo split of a GEMM's activations (tensor-core path), split_elems each
     __nv_bfloat16 *split_hi = nullptr, *split_lo = nullptr;
     int64_t split_elems = 0;
@@ -746,9 +754,44 @@ int launch_attn_flash_nu(pulsar_engine* e, dim3 grid, const int4* rows, int R, c
     return launch_status("k_attn_flash");
 }
 
+// Tensor-core decode attention (k_attn_dec_tc): a bf16 cache whose tensor map was encoded, unless
+// option "tc_dec_attn" is 0.
+template <typename KVT>
+bool dec_tc(const pulsar_engine* e) {
+    return std::is_same<KVT, __nv_bfloat16>::value && e->tc_dec && e->kv_map_ok;
+}
+// Keys per chunk of the decode attention that dec_tc selects (the split count's unit).
+template <typename KVT>
+int attn_chunk(const pulsar_engine* e) {
+    return dec_tc<KVT>(e) ? DT_CK : ATT_FCK;
+}
+
+template <int NU>
+int launch_attn_dec_tc_nu(pulsar_engine* e, dim3 grid, const int4* rows, int R, const float* q, const KVLayer& L,
+                          int local, int nsplit, float* part, cudaStream_t st) {
+    constexpr int smem = (int)dt_smem_bytes<NU>();
+    PULSAR_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k_attn_dec_tc<NU>), smem, "k_attn_dec_tc shared memory"));
+    const int64_t lrow = (static_cast<const char*>(L.base) - static_cast<const char*>(e->kv)) / (DH * 2);
+    k_attn_dec_tc<NU><<<grid, DtLayout<NU>::THREADS, smem, st>>>(e->kv_map, rows, R, e->attn_rpb, q, L, lrow, local, nsplit, part,
+                                                       e->max_pos(), e->cfg.max_batch, e->m_err);
+    return launch_status("k_attn_dec_tc");
+}
+
 template <typename KVT>
 int launch_attn_flash(pulsar_engine* e, dim3 grid, const int4* rows, int R, const float* q, const KVLayer& L, int local,
                       int nsplit, float* part, cudaStream_t st) {
+    if (dec_tc<KVT>(e)) {
+        switch (e->attn_rpb) {
+            case 1: return launch_attn_dec_tc_nu<1>(e, grid, rows, R, q, L, local, nsplit, part, st);
+            case 2: return launch_attn_dec_tc_nu<2>(e, grid, rows, R, q, L, local, nsplit, part, st);
+            case 3: return launch_attn_dec_tc_nu<3>(e, grid, rows, R, q, L, local, nsplit, part, st);
+            case 4: return launch_attn_dec_tc_nu<4>(e, grid, rows, R, q, L, local, nsplit, part, st);
+            case 5: return launch_attn_dec_tc_nu<5>(e, grid, rows, R, q, L, local, nsplit, part, st);
+            case 6: return launch_attn_dec_tc_nu<6>(e, grid, rows, R, q, L, local, nsplit, part, st);
+            case 7: return launch_attn_dec_tc_nu<7>(e, grid, rows, R, q, L, local, nsplit, part, st);
+            default: return launch_attn_dec_tc_nu<ATT_RPB_MAX>(e, grid, rows, R, q, L, local, nsplit, part, st);
+        }
+    }
     switch (e->attn_rpb) {
         case 1: return launch_attn_flash_nu<KVT, 1>(e, grid, rows, R, q, L, local, nsplit, part, st);
         case 2: return launch_attn_flash_nu<KVT, 2>(e, grid, rows, R, q, L, local, nsplit, part, st);
@@ -792,7 +835,8 @@ int enqueue_pulse(pulsar_engine* e, int p, int R, const int4* rows, const float*
             local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
         const int groups = (R + e->attn_rpb - 1) / e->attn_rpb;
-        const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l]);
+        const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l],
+                                       attn_chunk<KVT>(e));
         PULSAR_TRY(launch_attn_flash<KVT>(e, dim3(nsplit, HKV, groups), rows, R, w.q, e->kvl[l], local ? 1 : 0, nsplit,
                                           w.part, st));
         k_attn_combine<<<R, H * 32, 0, st>>>(w.part, nsplit, w.xn,
@@ -1206,7 +1250,8 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
             local ? e->sin_l : e->sin_g, eps, vres_mode, e->vres[p][l], w.vfirst, e->kvl[l], local ? 0 : 1,
             e->cfg.base_seq_len, w.q, e->max_pos(), e->cfg.max_batch);
         const int groups = (R + e->attn_rpb - 1) / e->attn_rpb;
-        const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l]);
+        const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[l],
+                                       attn_chunk<KVT>(e));
         PULSAR_TRY(launch_attn_flash<KVT>(e, dim3(nsplit, HKV, groups), rows, R, w.q, e->kvl[l], local ? 1 : 0, nsplit,
                                           w.part, st));
         k_attn_combine<<<R, H * 32, 0, st>>>(w.part, nsplit, w.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
@@ -1513,6 +1558,16 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
     for (int l = 0; l < NL; ++l) {
         e->kvl[l].base = static_cast<char*>(e->kv) + layer_off[l] * esz;
         e->kvl[l].slot_stride = slot_elems;
+        e->kv_lrow[l] = layer_off[l] / DH;
+    }
+    // Zeroed once: attention reads whole 128-key chunks and masks the keys past a row's position,
+    // so positions never written must hold finite values.
+    if ((st = cuda_status(cudaMemset(e->kv, 0, (size_t)slot_elems * cfg->max_batch * esz), "zero the KV cache")))
+        return fail(st);
+    {
+        const uint64_t kv_rows = (uint64_t)slot_elems * cfg->max_batch / DH;
+        e->kv_map_ok = !cfg->kv_fp32 && kv_rows + DT_CK <= (uint64_t)INT32_MAX &&
+                       encode_bf16_map(&e->kv_map, e->kv, kv_rows, DH, DT_CK);
     }
     e->len.assign(cfg->max_batch, 0);
     // decode workspace
@@ -1971,6 +2026,75 @@ extern "C" int pulsar_engine_prefill_attention(pulsar_engine* e, int32_t slot, i
                      : prefill_attention<__nv_bfloat16>(e, slot, layer, T, q_dev, out_dev, tensor_cores != 0, st);
 }
 
+// Merge of the split partials of decode_attention: per (row, head) o / l over the splits (0
+// when no key was visible), without the head gate.
+__global__ void __launch_bounds__(H * 32) k_attn_merge_plain(const float* __restrict__ part, int nsplit,
+                                                             float* __restrict__ out) {
+    const int r = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* pp = part + ((int64_t)r * H + h) * nsplit * PART;
+    float M = -INFINITY;
+    for (int c = 0; c < nsplit; ++c) M = fmaxf(M, pp[c * PART]);
+    float l = 0.f, o1 = 0.f, o2 = 0.f;
+    for (int c = 0; c < nsplit; ++c) {
+        const float m = pp[c * PART];
+        if (m == -INFINITY) continue;
+        const float w = expf(m - M);
+        l += w * pp[c * PART + 1];
+        o1 += w * pp[c * PART + 2 + lane];
+        o2 += w * pp[c * PART + 2 + lane + 32];
+    }
+    float* y = out + ((int64_t)r * H + h) * DH;
+    y[lane] = l > 0.f ? o1 / l : 0.f;
+    y[lane + 32] = l > 0.f ? o2 / l : 0.f;
+}
+
+template <typename KVT>
+int decode_attention(pulsar_engine* e, int layer, int R, const int4* rows, int rpb, const float* q, float* out,
+                     bool tc, cudaStream_t st) {
+    const bool local = is_local_layer(layer);
+    const int save_rpb = e->attn_rpb;
+    const bool save_tc = e->tc_dec;
+    e->attn_rpb = rpb;
+    e->tc_dec = tc;
+    const int groups = (R + rpb - 1) / rpb;
+    const int nsplit = attn_splits(groups, local ? WINDOW + ATT_RPB_MAX : e->max_pos(), e->mega_grid, e->nch[layer],
+                                   attn_chunk<KVT>(e));
+    float* part = nullptr;
+    int rc = cuda_status(cudaMalloc(&part, (size_t)R * H * nsplit * PART * sizeof(float)), "decode_attention: partials");
+    if (rc == PULSAR_OK)
+        rc = launch_attn_flash<KVT>(e, dim3(nsplit, HKV, groups), rows, R, q, e->kvl[layer], local ? 1 : 0, nsplit, part,
+                                    st);
+    if (rc == PULSAR_OK) {
+        k_attn_merge_plain<<<R, H * 32, 0, st>>>(part, nsplit, out);
+        rc = launch_status("k_attn_merge_plain");
+    }
+    if (rc == PULSAR_OK) rc = cuda_status(cudaStreamSynchronize(st), "decode_attention");
+    if (rc == PULSAR_OK) rc = check_kernel_err(e);
+    if (part) cudaFree(part);
+    e->attn_rpb = save_rpb;
+    e->tc_dec = save_tc;
+    return rc;
+}
+
+extern "C" int pulsar_engine_decode_attention(pulsar_engine* e, int32_t layer, int32_t R, const int32_t* rows_dev,
+                                              int32_t rows_per_block, const float* q_dev, float* out_dev,
+                                              int32_t tensor_cores, void* stream) {
+    PULSAR_TRY(check_engine(e, false));
+    PULSAR_CHECK_ARG(layer >= 0 && layer < NL, "decode_attention: layer %d out of range [0, %d)", layer, NL);
+    PULSAR_CHECK_ARG(R >= 1, "decode_attention: R = %d", R);
+    PULSAR_CHECK_ARG(rows_per_block >= 1 && rows_per_block <= ATT_RPB_MAX,
+                     "decode_attention: rows_per_block %d out of range [1, %d]", rows_per_block, ATT_RPB_MAX);
+    PULSAR_CHECK_ARG(rows_dev && q_dev && out_dev, "decode_attention: null pointer");
+    PULSAR_CHECK_ARG(((uintptr_t)rows_dev & 15) == 0 && ((uintptr_t)q_dev & 15) == 0,
+                     "decode_attention: rows and queries must be 16-byte aligned");
+    PULSAR_TRY(cuda_status(cudaSetDevice(e->cfg.device), "cudaSetDevice"));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int4* rows = reinterpret_cast<const int4*>(rows_dev);
+    return e->kv32() ? decode_attention<float>(e, layer, R, rows, rows_per_block, q_dev, out_dev, tensor_cores != 0, st)
+                     : decode_attention<__nv_bfloat16>(e, layer, R, rows, rows_per_block, q_dev, out_dev,
+                                                       tensor_cores != 0, st);
+}
+
 extern "C" int pulsar_engine_read_kv(pulsar_engine* e, int32_t slot, int32_t layer, int32_t pos0, int32_t n,
                                      float* k_host, float* v_host) {
     PULSAR_TRY(check_engine(e, false));
@@ -2204,6 +2328,14 @@ extern "C" int pulsar_engine_set_option(pulsar_engine* e, const char* name, int6
         e->tc_attn = value != 0;
         return PULSAR_OK;
     }
+    if (strcmp(name, "tc_dec_attn") == 0) {
+        if ((value != 0) != e->tc_dec) {
+            for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
+            e->graphs.clear();
+        }
+        e->tc_dec = value != 0;
+        return PULSAR_OK;
+    }
     if (strcmp(name, "tma_gemm") == 0) {
         if ((value != 0) != e->use_tma) {
             for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second.ex);
@@ -2284,6 +2416,8 @@ extern "C" int pulsar_engine_get_option(pulsar_engine* e, const char* name, int6
     if (strcmp(name, "tc_gemm") == 0) { *value = e->use_tc ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "tc_attn") == 0) { *value = e->tc_attn ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "tma_gemm") == 0) { *value = e->use_tma ? 1 : 0; return PULSAR_OK; }
+    // 1 when the decode attention runs on the tensor cores (bf16 cache, option on)
+    if (strcmp(name, "tc_dec_attn") == 0) { *value = (e->tc_dec && e->kv_map_ok) ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "merged_adapter") == 0) { *value = e->merge_adapter ? 1 : 0; return PULSAR_OK; }
     if (strcmp(name, "wide_rows") == 0) { *value = e->wide_rows; return PULSAR_OK; }
     if (strcmp(name, "loop_adapter") == 0) { *value = e->has_lora ? 1 : 0; return PULSAR_OK; }

@@ -623,12 +623,12 @@ constexpr size_t attn_flash_smem() {
 }
 
 // Splits of a flash-decoding launch: enough blocks to fill the GPU (about 6 per SM) when a pass
-// has few row groups, never more than the chunks of the longest span nor than `cap` (the
-// partial stride the buffers hold).
-inline int attn_splits(int groups, int max_span, int sms, int cap) {
+// has few row groups, never more than the chunks (of `chunk` keys, one more for an unaligned
+// start) of the longest span nor than `cap` (the partial stride the buffers hold).
+inline int attn_splits(int groups, int max_span, int sms, int cap, int chunk = ATT_FCK) {
     const int base = HKV * groups;
     int n = (6 * sms + base - 1) / base;
-    const int chunks = (max_span + ATT_FCK - 1) / ATT_FCK + 1;
+    const int chunks = (max_span + chunk - 1) / chunk + 1;
     if (n > chunks) n = chunks;
     if (n > cap) n = cap;
     return n < 1 ? 1 : n;

@@ -62,6 +62,8 @@ PROTOTYPES = {
     "pulsar_engine_read_kv": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "pulsar_engine_forward": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "pulsar_engine_prefill_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    "pulsar_engine_decode_attention": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                                               c_void_p]),
     "pulsar_engine_generate_greedy": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
                                               C.POINTER(c_int64), c_void_p]),
     "pulsar_engine_generate_sampled": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,

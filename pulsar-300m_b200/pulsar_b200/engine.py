@@ -222,6 +222,21 @@ class DeviceEngine:
                    "prefill_attention")
         return out
 
+    def decode_attention(self, layer: int, rows, q: torch.Tensor, tensor_cores: bool = True,
+                         rows_per_block: int = 1) -> torch.Tensor:
+        """The decode attention of one layer (pulsar_engine_decode_attention) for rows
+        [(slot, pos), ...] over the keys each slot holds at positions 0..pos: q [R, n_heads,
+        head_dim] fp32 (normed, rotated, unscaled) -> [R, n_heads, head_dim] fp32, without the
+        head gate. rows_per_block groups consecutive rows into verify blocks (1..8)."""
+        rt = torch.tensor([[s, p, 0, 0] for (s, p) in rows], dtype=torch.int32, device=self.device)
+        q = q.to(device=self.device, dtype=torch.float32).contiguous()
+        out = torch.empty_like(q)
+        _lib.check(_lib.load().pulsar_engine_decode_attention(self._h, layer, len(rows), rt.data_ptr(), rows_per_block,
+                                                               q.data_ptr(), out.data_ptr(), 1 if tensor_cores else 0,
+                                                               self.stream()),
+                   "decode_attention")
+        return out
+
     def set_option(self, name: str, value: int) -> None:
         """Engine options (see include/pulsar_b200.h): "megakernel" 0/1."""
         _lib.check(_lib.load().pulsar_engine_set_option(self._h, name.encode(), int(value)), f"set_option({name})")
