@@ -56,6 +56,14 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     return r;
 }
 
+// x as bf16 hi + lo halves at index i (|x - hi - lo| <= 2^-16 |x|): the activation operand of
+// the tensor-core GEMMs, written by the kernel that produces x.
+__device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo, int64_t i, float x) {
+    const __nv_bfloat16 h = __float2bfloat16(x);
+    hi[i] = h;
+    lo[i] = __float2bfloat16(x - __bfloat162float(h));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -6,12 +6,15 @@
 // of one slot at consecutive positions (a verify block); a run holds nq = rows x GQA query units
 // (<= 32). Its keys are walked in chunks of 128 aligned to absolute multiples of 128 (a chunk
 // never wraps a local layer's ring): chunks sp, sp + nsplit, ... Per chunk:
-//   S^T = K Q^T   tcgen05.mma M = 128 (keys), N = NQP (units, 16 or 32), K = 64 (dims):
-//                 A = the chunk's K rows as the cache stores them (K-major), B = the queries
+//   S^T = K Q^T   tcgen05.mma M = 128 (keys), N = 2 NQP (the units' Q hi rows, then their lo rows;
+//                 NQP = 16 or 32), K = 64 (dims): A = the chunk's K rows as the cache stores them
+//                 (K-major), B = the queries; a unit's score is the sum of its two columns
 //   softmax       thread = (key, group of units): TMEM lane = key, the group's columns = units
-//   O += P V      tcgen05.mma M = 128 (units; rows past nq unused), N = 64 (dims), K = 128 (keys):
-//                 A = P written by the softmax threads, B = the chunk's V rows (MN-major: the cache
-//                 stores V key-major, dims contiguous); O stays in TMEM over the run
+//   O += P V      tcgen05.mma M = 128 (rows: P hi of the units, then P lo of the units at row
+//                 8 RG + u; rows past them unused), N = 64 (dims), K = 128 (keys): A = P written
+//                 by the softmax threads, B = the chunk's V rows (MN-major: the cache stores V
+//                 key-major, dims contiguous); O stays in TMEM over the run, unit u's output is
+//                 the sum of its rows u and 8 RG + u
 //
 // Roles. Warp 4G (one lane) is the producer: it issues the 2-D tensor-map loads of K and V
 // (cp.async.bulk.tensor, box 64 x 128 rows, SWIZZLE_128B, this CTA only) into two 3-stage rings
@@ -63,9 +66,10 @@ struct DtLayout {
     static constexpr int UPG = (NQ + G - 1) / G;     // units per group (<= 8)
     static constexpr int THREADS = 128 * G + 32;     // softmax warps + the producer warp
     static constexpr int RG = (NQ + 7) / 8;          // 8-row groups of P that hold units
-    static constexpr uint32_t PKB = RG * 1024;       // one 64-key block of P (hi or lo)
-    static constexpr uint32_t PBUF = 4 * PKB;        // hi, lo x two 64-key blocks
-    static constexpr uint32_t P0 = 0;                // two P buffers
+    static constexpr int LO = 8 * RG;                // P's (and O's) row of unit u's lo half: LO + u
+    static constexpr uint32_t PKB = 2 * RG * 1024;   // one 64-key block of P: hi rows, then lo rows
+    static constexpr uint32_t PBUF = 2 * PKB;        // two 64-key blocks
+    static constexpr uint32_t P0 = 0;                // two P buffers (and, at a run's end, O's rows)
     static constexpr uint32_t Q_HI = 2 * PBUF, Q_LO = Q_HI + NQP * 128;
     static constexpr uint32_t KR = ((Q_LO + NQP * 128 + 1023) / 1024) * 1024;
     static constexpr uint32_t TILE = DT_CK * DH * 2;   // 128 rows of K or V: 16 KB
@@ -76,10 +80,12 @@ struct DtLayout {
     static constexpr uint32_t MISC = SCL + NQP * 4;           // abort flag, TMEM base
     static constexpr uint32_t BYTES = MISC + 16;
     // the P operand's MMA rows reach 16 KB past each 64-key block's start
-    static_assert(P0 + PBUF + 3 * PKB + 16 * 1024 <= BYTES, "P operand rows must stay inside the block's shared memory");
+    static_assert(P0 + PBUF + PKB + 16 * 1024 <= BYTES, "P operand rows must stay inside the block's shared memory");
     static_assert(UPG <= 8 && (G - 1) * UPG + 8 <= NQP, "a group's 8-column TMEM load stays inside the scores");
-    // TMEM columns: S^T double buffer at 0 and 32, O at 64
-    static constexpr uint32_t TM_S = 0, TM_O = 64, TM_COLS = 128;
+    static_assert(2 * LO * (DH + 1) * 4 <= 2 * PBUF, "O's rows fit the P buffers at a run's end");
+    // TMEM columns: S^T double buffer (hi products, then lo products: 2 NQP columns each), O
+    static constexpr uint32_t TM_S = 0, TM_SB = 2 * NQP, TM_O = 4 * NQP;
+    static constexpr uint32_t TM_COLS = NQP == 16 ? 128 : 256;
 };
 
 template <int NU>
@@ -197,7 +203,7 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
     KVLayer L, int64_t lrow, int is_local, int nsplit, float* __restrict__ part, int max_pos, int n_slots, int* err) {
     using Lay = DtLayout<NU>;
     constexpr int NQP = Lay::NQP, G = Lay::G, UPG = Lay::UPG, NSM = 128 * G;   // NSM: softmax threads
-    constexpr uint32_t idS = dt_idesc(NQP, false), idO = dt_idesc(DH, true);
+    constexpr uint32_t idS = dt_idesc(2 * NQP, false), idO = dt_idesc(DH, true);
     extern __shared__ __align__(1024) unsigned char dt_raw[];
     unsigned char* sm = dt_raw + ((1024 - (smem_u32(dt_raw) & 1023)) & 1023);
     const uint32_t sb = smem_u32(sm);
@@ -303,12 +309,9 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
                 auto mma_s = [&](int c) {   // S^T of chunk c (its K has landed)
                     const uint32_t kt = sb + Lay::KR + (uint32_t)(c % DT_STAGES) * Lay::TILE;
 #pragma unroll
-                    for (int ks = 0; ks < DH / 16; ++ks) {
-                        const uint64_t a = tc_desc_sw128(kt + ks * 32);
-                        tc_mma(tmem + Lay::TM_S + 32 * (c & 1), a, tc_desc_sw128(sb + Lay::Q_HI + ks * 32), idS,
-                               ks > 0 ? 1u : 0u);
-                        tc_mma(tmem + Lay::TM_S + 32 * (c & 1), a, tc_desc_sw128(sb + Lay::Q_LO + ks * 32), idS, 1u);
-                    }
+                    for (int ks = 0; ks < DH / 16; ++ks)   // B: the Q hi rows, then (contiguous) the lo rows
+                        tc_mma(tmem + Lay::TM_S + Lay::TM_SB * (c & 1), tc_desc_sw128(kt + ks * 32),
+                               tc_desc_sw128(sb + Lay::Q_HI + ks * 32), idS, ks > 0 ? 1u : 0u);
                     tc_commit(&sdone[c & 1]);
                 };
                 bool ok = dt_wait(&kfull[gbase % DT_STAGES], (gbase / DT_STAGES) & 1, abort);
@@ -333,12 +336,9 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
                     const uint32_t pa = sb + Lay::P0 + (uint32_t)(c & 1) * Lay::PBUF;
                     const uint32_t vt = sb + Lay::VR + (uint32_t)(c % DT_STAGES) * Lay::TILE;
 #pragma unroll
-                    for (int ks = 0; ks < DT_CK / 16; ++ks) {
-                        const uint32_t ka = pa + (uint32_t)(ks >> 2) * Lay::PKB + (ks & 3) * 32;
-                        const uint64_t bv = tc_desc_sw128(vt + ks * 2048);
-                        tc_mma(tmem + Lay::TM_O, tc_desc_sw128(ka), bv, idO, (j > 0 || ks > 0) ? 1u : 0u);
-                        tc_mma(tmem + Lay::TM_O, tc_desc_sw128(ka + 2 * Lay::PKB), bv, idO, 1u);
-                    }
+                    for (int ks = 0; ks < DT_CK / 16; ++ks)
+                        tc_mma(tmem + Lay::TM_O, tc_desc_sw128(pa + (uint32_t)(ks >> 2) * Lay::PKB + (ks & 3) * 32),
+                               tc_desc_sw128(vt + ks * 2048), idO, (j > 0 || ks > 0) ? 1u : 0u);
                     tc_commit(&odone[c & 1]);
                     // refills: chunk c's K stage (its scores were read before P was ready) takes
                     // chunk c + 3; chunk c - 1's V stage, once its P.V has completed, chunk c + 2
@@ -375,8 +375,10 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
                 bool bad = !dt_wait(&sdone[b], (c >> 1) & 1, abort);
                 __syncwarp();   // tcgen05.ld is warp-collective
                 tc_fence_after();
-                uint32_t sr[8];
-                dt_ld8(tmem + ((uint32_t)(qd * 32) << 16) + Lay::TM_S + 32 * b + u0, sr);
+                uint32_t sr[8], srl[8];
+                const uint32_t scol = tmem + ((uint32_t)(qd * 32) << 16) + Lay::TM_S + Lay::TM_SB * b + u0;
+                dt_ld8(scol, sr);
+                dt_ld8(scol + NQP, srl);
                 dt_ld_wait();
                 const int kpos = chunk_k0(j) + key;
                 float s[UPG];
@@ -389,7 +391,7 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
                         const int pos = posF + u / GQA;
                         const int lor = is_local ? max(0, pos - WINDOW + 1) : 0;
                         if (kpos <= pos && kpos >= lor) {
-                            s[k] = __uint_as_float(sr[k]);
+                            s[k] = __uint_as_float(sr[k]) + __uint_as_float(srl[k]);
                             need |= m_est[k] == -INFINITY || s[k] - m_est[k] > DT_TH;
                         }
                     }
@@ -420,20 +422,23 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
                         aborted = true;
                         break;
                     }
-                    if (warp == 0 && j > 0) {
-                        // O (lanes = units) after the previous chunk's P.V, times each unit's rescale
+                    if (warp < (2 * Lay::LO + 31) / 32 && j > 0) {
+                        // O's rows (TMEM lanes: unit u's hi half at u, lo half at LO + u) after the
+                        // previous chunk's P.V, times the unit's rescale; warps 0 and 1 own lanes 0-63
                         const bool ok = __all_sync(0xffffffffu, dt_wait(&odone[(c - 1) & 1], ((c - 1) >> 1) & 1, abort));
                         tc_fence_after();
                         if (ok) {
-                            const float f = lane < nq ? scl[lane] : 1.f;
+                            const int row = warp * 32 + lane, u = row < Lay::LO ? row : row - Lay::LO;
+                            const float f = (row < 2 * Lay::LO && u < nq) ? scl[u] : 1.f;
+                            const uint32_t orow = tmem + ((uint32_t)(warp * 32) << 16) + Lay::TM_O;
 #pragma unroll
                             for (int cc = 0; cc < DH / 16; ++cc) {
                                 uint32_t r[16];
-                                dt_ld16(tmem + Lay::TM_O + 16 * cc, r);
+                                dt_ld16(orow + 16 * cc, r);
                                 dt_ld_wait();
 #pragma unroll
                                 for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-                                dt_st16(tmem + Lay::TM_O + 16 * cc, r);
+                                dt_st16(orow + 16 * cc, r);
                             }
                             dt_st_wait();
                         }
@@ -450,17 +455,18 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
                         l_t[k] += p;
                         const __nv_bfloat16 ph = __float2bfloat16(p);
                         const __nv_bfloat16 pl = __float2bfloat16(p - __bfloat162float(ph));
-                        const uint32_t off = dt_sw_off(u, key & 63);
-                        dt_sts16(pb + off, ph);
-                        dt_sts16(pb + 2 * Lay::PKB + off, pl);
+                        dt_sts16(pb + dt_sw_off(u, key & 63), ph);
+                        dt_sts16(pb + dt_sw_off(Lay::LO + u, key & 63), pl);
                     }
                 }
                 tc_fence_proxy_async();   // P is read by the tensor cores
-                tc_fence_before();        // and warp 0's rescale of O is ordered before the next P.V
+                tc_fence_before();        // and the rescale of O is ordered before the next P.V
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&pready[b]);
             }
-            // the run's partials: l summed over the group's four warps, (m, l, o) of unit u by lane u of warp 0
+            // the run's partials: l summed over the group's four warps; O's rows (TMEM lanes
+            // 0 .. 2 LO - 1, owned by warps 0 and 1) staged as [row][65] floats in the P buffers
+            // (free once every P.V has completed); (m, l, o) of unit u by lane u of warp 0
 #pragma unroll
             for (int k = 0; k < UPG; ++k) {
                 const int u = u0 + k;
@@ -470,34 +476,38 @@ __global__ void __launch_bounds__(DtLayout<NU>::THREADS) k_attn_dec_tc(
                     if (qd == 0 && lane == 0) scl[u] = m_est[k];
                 }
             }
-            dt_bar_sync<NSM>();
-            if (warp == 0) {
+            float* ost = reinterpret_cast<float*>(sm + Lay::P0);
+            if (warp < (2 * Lay::LO + 31) / 32) {
                 const bool ok = __all_sync(0xffffffffu, mine > 0 && !aborted &&
                                                             dt_wait(&odone[(gbase + mine - 1) & 1],
                                                                     ((gbase + mine - 1) >> 1) & 1, abort));
                 tc_fence_after();
-                float* out = part + (((int64_t)(s0 + lane / GQA) * H + g * GQA + lane % GQA) * nsplit + sp) * PART;
-                if (lane < nq) {
-                    const float m = mine > 0 ? scl[lane] : -INFINITY;
-                    const float4 r4 = *reinterpret_cast<const float4*>(&red[lane * 4]);
-                    out[0] = m == -INFINITY ? -INFINITY : m * 0.69314718f;   // base 2 -> natural log
-                    out[1] = m == -INFINITY ? 0.f : (r4.x + r4.y) + (r4.z + r4.w);
-                }
+                const int row = warp * 32 + lane;
+                const uint32_t orow = tmem + ((uint32_t)(warp * 32) << 16) + Lay::TM_O;
 #pragma unroll
                 for (int cc = 0; cc < DH / 16; ++cc) {
                     uint32_t r[16];
                     if (ok) {
-                        dt_ld16(tmem + Lay::TM_O + 16 * cc, r);
+                        dt_ld16(orow + 16 * cc, r);
                         dt_ld_wait();
                     }
-                    if (lane < nq) {
-                        float2* o2 = reinterpret_cast<float2*>(out + 2 + 16 * cc);
+                    if (row < 2 * Lay::LO)
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            o2[i] = ok ? make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]))
-                                       : make_float2(0.f, 0.f);
-                    }
+                        for (int i = 0; i < 16; ++i) ost[row * (DH + 1) + 16 * cc + i] = ok ? __uint_as_float(r[i]) : 0.f;
                 }
+            }
+            dt_bar_sync<NSM>();
+            if (warp == 0 && lane < nq) {
+                float* out = part + (((int64_t)(s0 + lane / GQA) * H + g * GQA + lane % GQA) * nsplit + sp) * PART;
+                const float m = mine > 0 ? scl[lane] : -INFINITY;
+                const float4 r4 = *reinterpret_cast<const float4*>(&red[lane * 4]);
+                out[0] = m == -INFINITY ? -INFINITY : m * 0.69314718f;   // base 2 -> natural log
+                out[1] = m == -INFINITY ? 0.f : (r4.x + r4.y) + (r4.z + r4.w);
+                const float* oh = ost + lane * (DH + 1);
+                const float* ol = ost + (Lay::LO + lane) * (DH + 1);
+                float2* o2 = reinterpret_cast<float2*>(out + 2);
+#pragma unroll 8
+                for (int d = 0; d < DH / 2; ++d) o2[d] = make_float2(oh[2 * d] + ol[2 * d], oh[2 * d + 1] + ol[2 * d + 1]);
             }
         }
         // end of the run: every MMA of it has completed; red, scl and the queries are free

@@ -564,6 +564,9 @@ struct pulsar_engine {
         float *h, *h_in, *xn, *qkv, *q, *vfirst, *part, *att, *act_sh, *sh, *hn, *t_qkv, *t_wo, *wts, *act_e, *ye,
             *logits;
         int *idx, *lists, *cnt, *slot, *rows_e, *kept;
+        // bf16 hi / lo of the GEMM operands their producers split: the normed rows, the attention
+        // output and the final norm (xs, [rows][1024]), the shared expert's activation (ss)
+        __nv_bfloat16 *xs_hi, *xs_lo, *ss_hi, *ss_lo;
     } ww{};
     // prefill workspace
     struct {
@@ -572,6 +575,8 @@ struct pulsar_engine {
             *ye, *hn, *pmax;
         int *idx, *lists, *cnt, *slot, *rows_e, *kept, *pidx;
         int cap;
+        // bf16 hi / lo of the GEMM operands their producers split (as in the wide workspace)
+        __nv_bfloat16 *xs_hi, *xs_lo, *ss_hi, *ss_lo;
     } pf{};
     // decode-loop state
     SeqDev* seqs = nullptr;
@@ -1065,15 +1070,25 @@ int gemm(pulsar_engine* e, const GemmArgs& g, int batches, cudaStream_t st) {
                       (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 && g.ldc % 4 == 0 && g.c_stride % 4 == 0 &&
                       (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 4 == 0 && g.a_stride % 4 == 0 &&
                       (int64_t)batches * g.M * g.K <= e->split_elems;
+    // an operand its producer already split: [batch * M][K] rows, 16-byte aligned
+    const bool presplit = g.a_hi && g.a_lo && !g.a_rows && g.lda == g.K && (batches == 1 || g.a_stride == (int64_t)g.M * g.K) &&
+                          (reinterpret_cast<uintptr_t>(g.a_hi) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.a_lo) & 15) == 0;
     if (e->use_tc && fits) {
-        const int64_t per_batch = (int64_t)g.M * g.K / 8;
-        k_split_hilo<<<dim3((unsigned)((per_batch + 255) / 256), batches), 256, 0, st>>>(g, e->split_hi, e->split_lo);
-        PULSAR_TRY(launch_status("k_split_hilo"));
+        const __nv_bfloat16* ahi = e->split_hi;
+        const __nv_bfloat16* alo = e->split_lo;
+        if (presplit) {
+            ahi = g.a_hi;
+            alo = g.a_lo;
+        } else {
+            const int64_t per_batch = (int64_t)g.M * g.K / 8;
+            k_split_hilo<<<dim3((unsigned)((per_batch + 255) / 256), batches), 256, 0, st>>>(g, e->split_hi, e->split_lo);
+            PULSAR_TRY(launch_status("k_split_hilo"));
+        }
         // TMA-fed kernel: weights of every batch at a whole number of rows from the first
         CUtensorMap ma, mb;
         if (e->use_tma && (batches == 1 || g.w_stride % g.K == 0) &&
-            encode_bf16_map(&ma, e->split_hi, (uint64_t)batches * g.M, g.K, TC_BM) &&
-            encode_bf16_map(&mb, e->split_lo, (uint64_t)batches * g.M, g.K, TC_BM)) {
+            encode_bf16_map(&ma, ahi, (uint64_t)batches * g.M, g.K, TC_BM) &&
+            encode_bf16_map(&mb, alo, (uint64_t)batches * g.M, g.K, TC_BM)) {
             const int wpb = batches > 1 ? (int)(g.w_stride / g.K) : 0;
             // narrow grids (under one CTA per SM) take 64-column tiles: twice the CTAs
             const int tiles128 = ((EPI == GEPI_SWIGLU) ? (g.N / 2) / (BN / 2) : g.N / BN) *
@@ -1086,7 +1101,7 @@ int gemm(pulsar_engine* e, const GemmArgs& g, int batches, cudaStream_t st) {
                                     "k_tc_gemm shared memory"));
         const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2) / (BN / 2) : g.N / BN;
         dim3 grid(ntiles, (g.M + TC_BM - 1) / TC_BM, batches);
-        k_tc_gemm<EPI, BN><<<grid, TC_THREADS, tc_smem_bytes<BN>(), st>>>(g, e->split_hi, e->split_lo, e->m_err);
+        k_tc_gemm<EPI, BN><<<grid, TC_THREADS, tc_smem_bytes<BN>(), st>>>(g, ahi, alo, e->m_err);
         return launch_status("k_tc_gemm");
     }
     const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2 + 31) / 32 : (g.N + GB_N - 1) / GB_N;
@@ -1139,8 +1154,11 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             const bool lora = lora_live(e);
             const bool local = is_local_layer(l);
             k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, f.xn,
-                                              lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, f.t);
+                                              lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, f.t,
+                                              f.xs_hi, f.xs_lo);
             GemmArgs g = gargs(f.xn, D, T, w_qkv(e, p, l), QKV, D, f.qkv, QKV);
+            g.a_hi = f.xs_hi;
+            g.a_lo = f.xs_lo;
             if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = f.t; }
             PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
             const int vres_mode = fwd ? ((p == 0 && l == 0) ? 1 : 2) : ((p == 0) ? (l == 0 ? 1 : 2) : 0);
@@ -1162,19 +1180,30 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             }
             k_gate_rows<<<T, H * 32, 0, st>>>(f.o, f.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                               e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, f.att,
-                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, f.t);
+                                              lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, f.t,
+                                              f.xs_hi, f.xs_lo);
             PULSAR_LAUNCH_CHECK("prefill attention");
             g = gargs(f.att, D, T, w_o(e, p, l), D, D, f.h, D);
+            g.a_hi = f.xs_hi;
+            g.a_lo = f.xs_lo;
             if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = f.t; }
             PULSAR_TRY(gemm<GEPI_ADD>(e, g, 1, st));
             k_rmsnorm_lora<<<T, 256, 0, st>>>(f.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, f.xn,
-                                              nullptr, nullptr);
+                                              nullptr, nullptr, f.xs_hi, f.xs_lo);
             const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
             k_router<<<T, E * 32, 0, st>>>(f.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, f.idx,
                                            f.wts);
             PULSAR_LAUNCH_CHECK("prefill router");
-            PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gargs(f.xn, D, T, e->sh_gu[l], 2 * DS, D, f.act_sh, DS), 1, st));
-            PULSAR_TRY(gemm<GEPI_STORE>(e, gargs(f.act_sh, DS, T, e->sh_dn[l], D, DS, f.sh, D), 1, st));
+            GemmArgs gs = gargs(f.xn, D, T, e->sh_gu[l], 2 * DS, D, f.act_sh, DS);
+            gs.a_hi = f.xs_hi;
+            gs.a_lo = f.xs_lo;
+            gs.c_hi = f.ss_hi;
+            gs.c_lo = f.ss_lo;
+            PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gs, 1, st));
+            gs = gargs(f.act_sh, DS, T, e->sh_dn[l], D, DS, f.sh, D);
+            gs.a_hi = f.ss_hi;
+            gs.a_lo = f.ss_lo;
+            PULSAR_TRY(gemm<GEPI_STORE>(e, gs, 1, st));
             k_moe_bucket<<<E, 1024, 0, st>>>(f.idx, M4, f.lists, M4, f.cnt);
             k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(f.lists, M4, f.cnt, f.wts, cap, f.slot, f.rows_e,
                                                                   f.kept);
@@ -1239,8 +1268,11 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         const bool lora = lora_live(e);
         const bool local = is_local_layer(l);
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "attn_norm.weight")) + (int64_t)p * D, eps, w.xn,
-                                          lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv);
+                                          lora ? e->T_(e->L(l, "attn.wqkv_adapter.lora_A")) : nullptr, w.t_qkv,
+                                          w.xs_hi, w.xs_lo);
         GemmArgs g = gargs(w.xn, D, R, w_qkv(e, p, l), QKV, D, w.qkv, QKV);
+        g.a_hi = w.xs_hi;
+        g.a_lo = w.xs_lo;
         if (lora) { g.lora_b = e->lb_qkv[p][l]; g.lora_t = w.t_qkv; }
         PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
         const int vres_mode = (p == 0) ? (l == 0 ? 1 : 2) : 0;
@@ -1256,18 +1288,29 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
                                           w.part, st));
         k_attn_combine<<<R, H * 32, 0, st>>>(w.part, nsplit, w.xn, e->T_(e->L(l, "attn.attn_gate")) + (int64_t)p * H * D,
                                              e->T_(e->L(l, "attn.attn_gate_bias")) + (int64_t)p * H, w.att,
-                                             lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo);
+                                             lora ? e->T_(e->L(l, "attn.wo_adapter.lora_A")) : nullptr, w.t_wo,
+                                             w.xs_hi, w.xs_lo);
         PULSAR_LAUNCH_CHECK("wide attention");
         g = gargs(w.att, D, R, w_o(e, p, l), D, D, w.h, D);
+        g.a_hi = w.xs_hi;
+        g.a_lo = w.xs_lo;
         if (lora) { g.lora_b = e->lb_wo[p][l]; g.lora_t = w.t_wo; }
         PULSAR_TRY(gemm<GEPI_ADD>(e, g, 1, st));
         k_rmsnorm_lora<<<R, 256, 0, st>>>(w.h, e->T_(e->L(l, "mlp_norm.weight")) + (int64_t)p * D, eps, w.xn, nullptr,
-                                          nullptr);
+                                          nullptr, w.xs_hi, w.xs_lo);
         const float* eb = e->T_(e->L(l, "mlp.expert_bias")) + (e->cfg.per_pulse_bias ? (int64_t)p * E : 0);
         k_router<<<R, E * 32, 0, st>>>(w.xn, e->T_(e->L(l, "mlp.router_weight")) + (int64_t)p * E * D, eb, w.idx, w.wts);
         PULSAR_LAUNCH_CHECK("wide router");
-        PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gargs(w.xn, D, R, e->sh_gu[l], 2 * DS, D, w.act_sh, DS), 1, st));
-        PULSAR_TRY(gemm<GEPI_STORE>(e, gargs(w.act_sh, DS, R, e->sh_dn[l], D, DS, w.sh, D), 1, st));
+        GemmArgs gs = gargs(w.xn, D, R, e->sh_gu[l], 2 * DS, D, w.act_sh, DS);
+        gs.a_hi = w.xs_hi;
+        gs.a_lo = w.xs_lo;
+        gs.c_hi = w.ss_hi;
+        gs.c_lo = w.ss_lo;
+        PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gs, 1, st));
+        gs = gargs(w.act_sh, DS, R, e->sh_dn[l], D, DS, w.sh, D);
+        gs.a_hi = w.ss_hi;
+        gs.a_lo = w.ss_lo;
+        PULSAR_TRY(gemm<GEPI_STORE>(e, gs, 1, st));
         k_moe_bucket<<<E, 1024, 0, st>>>(w.idx, M4, w.lists, M4, w.cnt);
         k_moe_slots<<<dim3((M4 + 255) / 256, E), 256, 0, st>>>(w.lists, M4, w.cnt, w.wts, cap, w.slot, w.rows_e, w.kept);
         PULSAR_LAUNCH_CHECK("wide slots");
@@ -1289,13 +1332,15 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
     }
     const bool want = logits != nullptr || amax != nullptr;
     k_pulse_end<<<R, 256, 0, st>>>(w.h, w.h_in, e->T_("pulse_res_scale") + (int64_t)p * D, e->T_("final_norm.weight"),
-                                   eps, h_out, want ? w.hn : nullptr, hs);
+                                   eps, h_out, want ? w.hn : nullptr, hs, w.xs_hi, w.xs_lo);
     PULSAR_LAUNCH_CHECK("wide pulse end");
     if (want) {
         float* lg = logits ? logits : w.logits;
         const int ld = logits ? ld_logits : e->V;
         GemmArgs g = gargs(w.hn, D, R, e->emb, e->V, D, lg, ld);
         g.softcap = e->cfg.logit_softcap;
+        g.a_hi = w.xs_hi;
+        g.a_lo = w.xs_lo;
         PULSAR_TRY(gemm<GEPI_STORE>(e, g, 1, st));
         if (amax) {
             k_argmax_rows<<<R, 1024, 0, st>>>(lg, e->V, ld, amax);
@@ -1601,7 +1646,9 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&x.logits, (size_t)RW * cfg->vocab_size)) || (st = e->wmalloc(&x.idx, (size_t)RW * TOPK)) ||
         (st = e->wmalloc(&x.lists, (size_t)E * RW * TOPK)) || (st = e->wmalloc(&x.cnt, E)) ||
         (st = e->wmalloc(&x.slot, (size_t)RW * TOPK)) || (st = e->wmalloc(&x.rows_e, (size_t)E * RW)) ||
-        (st = e->wmalloc(&x.kept, E)))
+        (st = e->wmalloc(&x.kept, E)) || (st = e->wmalloc(&x.xs_hi, (size_t)RW * D)) ||
+        (st = e->wmalloc(&x.xs_lo, (size_t)RW * D)) || (st = e->wmalloc(&x.ss_hi, (size_t)RW * DS)) ||
+        (st = e->wmalloc(&x.ss_lo, (size_t)RW * DS)))
         return fail(st);
     {   // activation split for the tensor-core GEMMs: the largest A of prefill or a wide pass
         const int cap_pf = prefill_capacity(cfg->max_prefill);
@@ -1628,7 +1675,9 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&f.idx, (size_t)T * TOPK)) || (st = e->wmalloc(&f.lists, (size_t)E * T * TOPK)) ||
         (st = e->wmalloc(&f.cnt, E)) || (st = e->wmalloc(&f.slot, (size_t)T * TOPK)) ||
         (st = e->wmalloc(&f.rows_e, (size_t)E * cap)) || (st = e->wmalloc(&f.kept, E)) ||
-        (st = e->wmalloc(&f.pidx, (size_t)nblk)))
+        (st = e->wmalloc(&f.pidx, (size_t)nblk)) || (st = e->wmalloc(&f.xs_hi, TD)) ||
+        (st = e->wmalloc(&f.xs_lo, TD)) || (st = e->wmalloc(&f.ss_hi, (size_t)T * DS)) ||
+        (st = e->wmalloc(&f.ss_lo, (size_t)T * DS)))
         return fail(st);
     // decode-loop state
     const int NB = cfg->max_batch;

@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(256) k_reinject(int R, const float* __restrict
 // t = A xn (24 values) when `lora_a` is set. One block per row.
 __global__ void __launch_bounds__(256) k_rmsnorm_lora(const float* __restrict__ h, const float* __restrict__ w, float eps,
                                                       float* __restrict__ xn, const float* __restrict__ lora_a,
-                                                      float* __restrict__ lora_t) {
+                                                      float* __restrict__ lora_t, __nv_bfloat16* __restrict__ xh = nullptr,
+                                                      __nv_bfloat16* __restrict__ xl = nullptr) {
     __shared__ float red[32];
     const int r = blockIdx.x;
     float x[4];
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm_lora(const float* __restrict__ 
         const int d = threadIdx.x + i * 256;
         x[i] = w[d] * (x[i] * inv);
         xn[(int64_t)r * D + d] = x[i];
+        if (xh) split_store(xh, xl, (int64_t)r * D + d, x[i]);
     }
     if (lora_a) {
         for (int j = 0; j < LORA_R; ++j) {
@@ -639,7 +641,9 @@ inline int attn_splits(int groups, int max_span, int sms, int cap, int chunk = A
 __global__ void __launch_bounds__(H * 32) k_attn_combine(const float* __restrict__ part, int nchunk,
                                                          const float* __restrict__ xn, const float* __restrict__ gw,
                                                          const float* __restrict__ gb, float* __restrict__ att,
-                                                         const float* __restrict__ lora_a, float* __restrict__ lora_t) {
+                                                         const float* __restrict__ lora_a, float* __restrict__ lora_t,
+                                                         __nv_bfloat16* __restrict__ ah = nullptr,
+                                                         __nv_bfloat16* __restrict__ al = nullptr) {
     __shared__ float outs[H * DH];
     __shared__ float red[32];
     const int r = blockIdx.x;
@@ -666,6 +670,10 @@ __global__ void __launch_bounds__(H * 32) k_attn_combine(const float* __restrict
     const float y1 = (o1 * inv) * g, y2 = (o2 * inv) * g;
     att[(int64_t)r * D + h * DH + lane] = y1;
     att[(int64_t)r * D + h * DH + lane + 32] = y2;
+    if (ah) {
+        split_store(ah, al, (int64_t)r * D + h * DH + lane, y1);
+        split_store(ah, al, (int64_t)r * D + h * DH + lane + 32, y2);
+    }
     outs[h * DH + lane] = y1;
     outs[h * DH + lane + 32] = y2;
     if (lora_a) {
@@ -860,7 +868,9 @@ __global__ void __launch_bounds__(128) k_moe_down(int R, const float* __restrict
 // hn = final RMSNorm(h_out) for the LM head.
 __global__ void __launch_bounds__(256) k_pulse_end(const float* __restrict__ h, const float* __restrict__ h_in,
                                                    const float* __restrict__ res_scale, const float* __restrict__ fnorm,
-                                                   float eps, float* __restrict__ h_out, float* __restrict__ hn, int hs) {
+                                                   float eps, float* __restrict__ h_out, float* __restrict__ hn, int hs,
+                                                   __nv_bfloat16* __restrict__ hnh = nullptr,
+                                                   __nv_bfloat16* __restrict__ hnl = nullptr) {
     __shared__ float red[32];
     const int r = blockIdx.x;
     float y[4];
@@ -880,6 +890,7 @@ __global__ void __launch_bounds__(256) k_pulse_end(const float* __restrict__ h, 
     for (int i = 0; i < 4; ++i) {
         const int d = threadIdx.x + i * 256;
         hn[(int64_t)r * D + d] = fnorm[d] * (y[i] * inv);
+        if (hnh) split_store(hnh, hnl, (int64_t)r * D + d, hn[(int64_t)r * D + d]);
     }
 }
 

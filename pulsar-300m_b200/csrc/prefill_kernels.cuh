@@ -29,6 +29,14 @@ struct GemmArgs {
     const float* lora_b;     // [N][24] or null
     const float* lora_t;     // [M][24]
     float softcap;           // STORE epilogue: y = softcap * tanh(y / softcap) when > 0
+    // tensor-core GEMMs: A already split into bf16 hi / lo ([batch * M][K] rows, lda == K, no
+    // gather), or null (the GEMM splits it)
+    const __nv_bfloat16* a_hi;
+    const __nv_bfloat16* a_lo;
+    // tensor-core SWIGLU epilogue: also the bf16 hi / lo split of its output, laid out like C
+    // (the operand of the GEMM that reads C), or null
+    __nv_bfloat16* c_hi;
+    __nv_bfloat16* c_lo;
 };
 
 template <int EPI>
@@ -352,7 +360,8 @@ __global__ void __launch_bounds__(256) k_attn_prefill(int slot, int T, const flo
 __global__ void __launch_bounds__(H * 32) k_gate_rows(const float* __restrict__ o, const float* __restrict__ xn,
                                                       const float* __restrict__ gw, const float* __restrict__ gb,
                                                       float* __restrict__ att, const float* __restrict__ lora_a,
-                                                      float* __restrict__ lora_t) {
+                                                      float* __restrict__ lora_t, __nv_bfloat16* __restrict__ ah = nullptr,
+                                                      __nv_bfloat16* __restrict__ al = nullptr) {
     __shared__ float outs[H * DH];
     __shared__ float red[32];
     const int r = blockIdx.x;
@@ -366,6 +375,10 @@ __global__ void __launch_bounds__(H * 32) k_gate_rows(const float* __restrict__ 
     const float y2 = o[((int64_t)r * H + h) * DH + lane + 32] * gt;
     att[(int64_t)r * D + h * DH + lane] = y1;
     att[(int64_t)r * D + h * DH + lane + 32] = y2;
+    if (ah) {
+        split_store(ah, al, (int64_t)r * D + h * DH + lane, y1);
+        split_store(ah, al, (int64_t)r * D + h * DH + lane + 32, y2);
+    }
     outs[h * DH + lane] = y1;
     outs[h * DH + lane + 32] = y2;
     if (lora_a) {

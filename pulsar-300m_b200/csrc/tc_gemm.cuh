@@ -179,12 +179,27 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, int b, int m0, in
             float gt[16], up[16];
             tc_ld16(lane_addr + c, gt);
             tc_ld16(lane_addr + BN / 2 + c, up);
-            if (row_ok)
+            if (row_ok) {
 #pragma unroll
                 for (int i = 0; i < 16; i += 4)
                     *reinterpret_cast<float4*>(C + n0 + c + i) =
                         make_float4(siluf_(gt[i]) * up[i], siluf_(gt[i + 1]) * up[i + 1],
                                     siluf_(gt[i + 2]) * up[i + 2], siluf_(gt[i + 3]) * up[i + 3]);
+                if (g.c_hi) {   // the split operand of the GEMM that reads C: 16 bf16 hi and lo
+                    const int64_t o = (int64_t)b * g.c_stride + (int64_t)m * g.ldc + n0 + c;
+                    __nv_bfloat16 h[16], l[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float y = siluf_(gt[i]) * up[i];
+                        h[i] = __float2bfloat16(y);
+                        l[i] = __float2bfloat16(y - __bfloat162float(h[i]));
+                    }
+                    reinterpret_cast<uint4*>(g.c_hi + o)[0] = reinterpret_cast<const uint4*>(h)[0];
+                    reinterpret_cast<uint4*>(g.c_hi + o)[1] = reinterpret_cast<const uint4*>(h)[1];
+                    reinterpret_cast<uint4*>(g.c_lo + o)[0] = reinterpret_cast<const uint4*>(l)[0];
+                    reinterpret_cast<uint4*>(g.c_lo + o)[1] = reinterpret_cast<const uint4*>(l)[1];
+                }
+            }
         }
     } else {
         for (int c = 0; c < BN; c += 16) {
