@@ -565,8 +565,9 @@ struct pulsar_engine {
             *logits;
         int *idx, *lists, *cnt, *slot, *rows_e, *kept;
         // bf16 hi / lo of the GEMM operands their producers split: the normed rows, the attention
-        // output and the final norm (xs, [rows][1024]), the shared expert's activation (ss)
-        __nv_bfloat16 *xs_hi, *xs_lo, *ss_hi, *ss_lo;
+        // output and the final norm (xs, [rows][1024]), the shared expert's activation (ss), the
+        // routed experts' activations (es, laid out like act_e)
+        __nv_bfloat16 *xs_hi, *xs_lo, *ss_hi, *ss_lo, *es_hi, *es_lo;
     } ww{};
     // prefill workspace
     struct {
@@ -576,7 +577,7 @@ struct pulsar_engine {
         int *idx, *lists, *cnt, *slot, *rows_e, *kept, *pidx;
         int cap;
         // bf16 hi / lo of the GEMM operands their producers split (as in the wide workspace)
-        __nv_bfloat16 *xs_hi, *xs_lo, *ss_hi, *ss_lo;
+        __nv_bfloat16 *xs_hi, *xs_lo, *ss_hi, *ss_lo, *es_hi, *es_lo;
     } pf{};
     // decode-loop state
     SeqDev* seqs = nullptr;
@@ -1107,7 +1108,25 @@ int gemm(pulsar_engine* e, const GemmArgs& g, int batches, cudaStream_t st) {
     const int ntiles = (EPI == GEPI_SWIGLU) ? (g.N / 2 + 31) / 32 : (g.N + GB_N - 1) / GB_N;
     dim3 grid(ntiles, (g.M + GB_M - 1) / GB_M, batches);
     k_gemm<EPI><<<grid, 256, 0, st>>>(g);
-    return launch_status("k_gemm");
+    PULSAR_TRY(launch_status("k_gemm"));
+    if (g.c_hi) {
+        // the split the tensor-core epilogue would have written, for a consumer that reads it
+        GemmArgs c{};
+        c.A = g.C;
+        c.lda = g.ldc;
+        c.a_stride = g.c_stride;
+        c.m_count = g.m_count;
+        c.M = g.M;
+        c.K = (EPI == GEPI_SWIGLU) ? g.N / 2 : g.N;
+        if (g.ldc != c.K || (batches > 1 && g.c_stride != (int64_t)g.M * c.K) || c.K % 8) {
+            set_error("gemm: the split output needs C as [batch * M][N] rows");
+            return PULSAR_ERR_UNSUPPORTED;
+        }
+        const int64_t per_batch = (int64_t)c.M * c.K / 8;
+        k_split_hilo<<<dim3((unsigned)((per_batch + 255) / 256), batches), 256, 0, st>>>(c, g.c_hi, g.c_lo);
+        return launch_status("k_split_hilo");
+    }
+    return PULSAR_OK;
 }
 
 GemmArgs gargs(const float* A, int lda, int M, const __nv_bfloat16* W, int N, int K, float* C, int ldc) {
@@ -1213,8 +1232,12 @@ int enqueue_prefill(pulsar_engine* e, int slot, const int* ids, int T, float* lo
             gu.m_count = f.kept;
             gu.w_stride = (int64_t)2 * DE * D;
             gu.c_stride = (int64_t)cap * DE;
+            gu.c_hi = f.es_hi;
+            gu.c_lo = f.es_lo;
             PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gu, E, st));
             GemmArgs gd = gargs(f.act_e, DE, cap, e->r_dn[l], D, DE, f.ye, D);
+            gd.a_hi = f.es_hi;
+            gd.a_lo = f.es_lo;
             gd.a_stride = (int64_t)cap * DE;
             gd.m_count = f.kept;
             gd.w_stride = (int64_t)D * DE;
@@ -1319,8 +1342,12 @@ int enqueue_pulse_wide(pulsar_engine* e, int p, int R, const int4* rows, const f
         gu.m_count = w.kept;
         gu.w_stride = (int64_t)2 * DE * D;
         gu.c_stride = (int64_t)cap * DE;
+        gu.c_hi = w.es_hi;
+        gu.c_lo = w.es_lo;
         PULSAR_TRY(gemm<GEPI_SWIGLU>(e, gu, E, st));
         GemmArgs gd = gargs(w.act_e, DE, cap, e->r_dn[l], D, DE, w.ye, D);
+        gd.a_hi = w.es_hi;
+        gd.a_lo = w.es_lo;
         gd.a_stride = (int64_t)cap * DE;
         gd.m_count = w.kept;
         gd.w_stride = (int64_t)D * DE;
@@ -1648,7 +1675,8 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&x.slot, (size_t)RW * TOPK)) || (st = e->wmalloc(&x.rows_e, (size_t)E * RW)) ||
         (st = e->wmalloc(&x.kept, E)) || (st = e->wmalloc(&x.xs_hi, (size_t)RW * D)) ||
         (st = e->wmalloc(&x.xs_lo, (size_t)RW * D)) || (st = e->wmalloc(&x.ss_hi, (size_t)RW * DS)) ||
-        (st = e->wmalloc(&x.ss_lo, (size_t)RW * DS)))
+        (st = e->wmalloc(&x.ss_lo, (size_t)RW * DS)) || (st = e->wmalloc(&x.es_hi, (size_t)E * RW * DE)) ||
+        (st = e->wmalloc(&x.es_lo, (size_t)E * RW * DE)))
         return fail(st);
     {   // activation split for the tensor-core GEMMs: the largest A of prefill or a wide pass
         const int cap_pf = prefill_capacity(cfg->max_prefill);
@@ -1677,7 +1705,8 @@ extern "C" int pulsar_engine_create(const pulsar_engine_config* cfg, pulsar_engi
         (st = e->wmalloc(&f.rows_e, (size_t)E * cap)) || (st = e->wmalloc(&f.kept, E)) ||
         (st = e->wmalloc(&f.pidx, (size_t)nblk)) || (st = e->wmalloc(&f.xs_hi, TD)) ||
         (st = e->wmalloc(&f.xs_lo, TD)) || (st = e->wmalloc(&f.ss_hi, (size_t)T * DS)) ||
-        (st = e->wmalloc(&f.ss_lo, (size_t)T * DS)))
+        (st = e->wmalloc(&f.ss_lo, (size_t)T * DS)) || (st = e->wmalloc(&f.es_hi, (size_t)E * cap * DE)) ||
+        (st = e->wmalloc(&f.es_lo, (size_t)E * cap * DE)))
         return fail(st);
     // decode-loop state
     const int NB = cfg->max_batch;
