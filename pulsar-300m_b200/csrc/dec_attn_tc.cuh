@@ -25,7 +25,8 @@
 // Softmax in base 2 with a lazy running maximum: the queries are pre-scaled by log2(e) / 8, and
 // the weights of a chunk are p = 2^(s - m) for the unit's running maximum m. m is exchanged
 // among a group's four warps only on a run's first chunk, or when a score exceeds m by more than
-// 2^32 (then O, in TMEM, is rescaled in place by warp 0, which owns TMEM lanes 0-31 = the units);
+// 2^32 (then O, in TMEM, is rescaled in place by warps 0 and 1, which own TMEM lanes 0-63: the
+// units' hi and lo rows);
 // otherwise a chunk costs the softmax warps one barrier. The weights are exact for any m (they
 // are relative to the same m in l and O); the partial's m goes out in natural-log units.
 // Each thread keeps partial sums l; the block reduces them once per run.
@@ -61,7 +62,7 @@ constexpr float DT_TH = 32.f;   // lazy maximum: rescale when a score exceeds m 
 template <int NU>
 struct DtLayout {
     static constexpr int NQ = NU * GQA;              // query units of a full run
-    static constexpr int NQP = NQ <= 16 ? 16 : 32;   // N of the score MMA
+    static constexpr int NQP = NQ <= 16 ? 16 : 32;   // Q rows per half (the score MMA's N is 2 NQP)
     static constexpr int G = (NQ + 7) / 8;           // softmax groups
     static constexpr int UPG = (NQ + G - 1) / G;     // units per group (<= 8)
     static constexpr int THREADS = 128 * G + 32;     // softmax warps + the producer warp
@@ -83,6 +84,8 @@ struct DtLayout {
     static_assert(P0 + PBUF + PKB + 16 * 1024 <= BYTES, "P operand rows must stay inside the block's shared memory");
     static_assert(UPG <= 8 && (G - 1) * UPG + 8 <= NQP, "a group's 8-column TMEM load stays inside the scores");
     static_assert(2 * LO * (DH + 1) * 4 <= 2 * PBUF, "O's rows fit the P buffers at a run's end");
+    static_assert(8 * 13 <= RED - BARS && RED % 16 == 0 && KR % 1024 == 0 && VR % 1024 == 0 && Q_HI % 1024 == 0,
+                  "the 13 mbarriers fit; float4 reads of red, tensor-map and swizzled destinations are aligned");
     // TMEM columns: S^T double buffer (hi products, then lo products: 2 NQP columns each), O
     static constexpr uint32_t TM_S = 0, TM_SB = 2 * NQP, TM_O = 4 * NQP;
     static constexpr uint32_t TM_COLS = NQP == 16 ? 128 : 256;
