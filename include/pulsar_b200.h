@@ -322,6 +322,11 @@ int pulsar_engine_early_exit_counts(pulsar_engine* eng, int64_t* counts_host);
  * bf16 A, bf16(bf16 B * bf16(loop_M[p] * alpha / q)), fp32 product sum in order plus the
  * base, one rounding) and run every pass on them, the persistent kernel included; 0 returns
  * to the exact fp32 adapter correction. Without a live adapter it stays 0. */
+/* "tc_gemm" (0/1, default 1): the GEMMs of prefill and the many-row path on the tensor cores
+ * (activations split into bf16 hi + lo); 0 selects the fp32 SIMT GEMM. "tma_gemm" (0/1, default
+ * 1): the TMA-fed warp-specialised tensor-core GEMM where a tensor map describes the operands;
+ * 0 the cp.async-fed one (bit-identical results). "tc_attn" (0/1, default 1): prefill attention
+ * on the tensor cores; 0 the fp32 SIMT kernel. */
 /* "tc_dec_attn" (0/1, default 1): the decode attention of the per-op and many-row passes on
  * the tensor cores (128-key chunks fed by tensor-map loads, Q and P split into bf16 hi + lo)
  * for a bf16 cache; 0 selects the SIMT kernel. Reads back 1 only when the tensor-core kernel
